@@ -1,0 +1,213 @@
+/*
+ * memvanta_b200.h -- C ABI of the B200 (sm_100a) implementation of
+ * MemVanta's GGUF block-quantized matmul hot path.
+ *
+ * Conventions
+ *  - Every function returns an int status: MV_OK (0) or one of the MV_ERR_*
+ *    codes below; mv_last_error() then returns a thread-local message.  No
+ *    C++ exception ever crosses this boundary (the reference throws
+ *    std::runtime_error at the same points; a C++ caller re-throws).
+ *  - Pointers named *_dev are device (HBM) pointers; *_host are host
+ *    pointers.  `stream` is a cudaStream_t passed as void* (NULL = legacy
+ *    default stream).  Device-pointer calls are asynchronous on `stream`.
+ *  - Matrices follow GGML order: a weight has `cols` = ne0 (the contraction
+ *    dimension K) and `rows` = ne1.  Batched activations are x[b*cols + c],
+ *    outputs y[b*rows + r] (the reference's layout, src/gguf_kernels.cpp:257).
+ *  - GGML type ids: 0 F32, 1 F16, 2 Q4_0, 8 Q8_0, 14 Q6_K.
+ *
+ * Reference citations are path:line inside the MemVanta project.
+ */
+#ifndef MEMVANTA_B200_H
+#define MEMVANTA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MV_API __attribute__((visibility("default")))
+#else
+#define MV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MV_OK 0
+#define MV_ERR_INVALID 1      /* bad argument / shape (reference: runtime_error) */
+#define MV_ERR_UNSUPPORTED 2  /* unsupported tensor type for this operation     */
+#define MV_ERR_CUDA 3         /* a CUDA runtime error                            */
+#define MV_ERR_OOM 4          /* device allocation failed                        */
+#define MV_ERR_IO 5           /* GGUF file could not be read / parsed            */
+#define MV_ERR_TIMEOUT 6      /* a bounded device-side wait ran out              */
+#define MV_ERR_NOT_BUILT 7    /* feature not available in this build             */
+
+#define MV_TYPE_F32 0
+#define MV_TYPE_F16 1
+#define MV_TYPE_Q4_0 2
+#define MV_TYPE_Q8_0 8
+#define MV_TYPE_Q6_K 14
+
+/* activation modes for mv_gemm (tensor_matmul_batch_v06) */
+#define MV_ACT_F32 0  /* fp32 activations: the reference's default prefill (src/gguf_kernels.cpp:268)            */
+#define MV_ACT_Q8 1   /* per-row Q8 activations: MEMVANTA_FORCE_Q8_ACT=1 (src/gguf_kernels.cpp:265-266)           */
+
+/* KV cache element types (reference KVCacheType, include/memvanta/llama_model.hpp:28) */
+#define MV_KV_F32 0
+#define MV_KV_F16 1
+#define MV_KV_Q8 2    /* one fp32 scale per token over kv_dim (src/llama_model.cpp:22)                            */
+#define MV_KV_Q8_0 3  /* one fp32 scale per 32-element block (extension; no reference counterpart)               */
+
+typedef struct mv_weight_s* mv_weight_t;
+typedef struct mv_model_s* mv_model_t;
+
+/* ------------------------------------------------------------ runtime */
+
+/* Selects the CUDA device for this thread and checks it is an sm_100 part.
+ * Replaces nothing in the reference (CPU-only); called once by the host. */
+MV_API int mv_init(int device);
+MV_API const char* mv_last_error(void);
+MV_API int mv_version(void);
+
+/* ------------------------------------------------------------ weights */
+
+/* Uploads one GGUF tensor (raw GGML blocks as they sit in the mmap) to HBM
+ * and repacks it into the planar device layout.  Called once per tensor at
+ * load time; replaces the reference's per-call reads of block bytes through
+ * GgufFile::tensor_data (src/gguf.cpp:139) in tensor_matvec & co.
+ * nbytes must equal ggml_tensor_nbytes(type, rows*cols) (src/gguf.cpp:82-105). */
+MV_API int mv_weight_upload(const void* host_blocks, uint64_t nbytes, int ggml_type, uint64_t rows, uint64_t cols,
+                     void* stream, mv_weight_t* out);
+/* Same, from raw GGML blocks already in device memory. */
+MV_API int mv_weight_from_device(const void* dev_blocks, uint64_t nbytes, int ggml_type, uint64_t rows, uint64_t cols,
+                          void* stream, mv_weight_t* out);
+MV_API int mv_weight_free(mv_weight_t w);
+MV_API int mv_weight_info(mv_weight_t w, int* ggml_type, uint64_t* rows, uint64_t* cols, uint64_t* device_bytes);
+/* Writes the weight back out as raw GGML blocks (host) -- the inverse of the
+ * upload repack, used to prove the repack lossless. */
+MV_API int mv_weight_download(mv_weight_t w, void* host_blocks, uint64_t nbytes);
+
+/* --------------------------------------------------- matmuls (device ptrs) */
+
+/* y[rows] = W x.  Q4_0 quantises x to Q8 per 32-block and runs the integer
+ * path; Q8_0, Q6_K, F16, F32 use fp32 x.
+ * Replaces tensor_matvec (src/gguf_kernels.cpp:244-253, declared
+ * include/memvanta/gguf_kernels.hpp:26). */
+MV_API int mv_gemv(mv_weight_t w, const float* x_dev, float* y_dev, void* stream);
+
+/* Y[batch,rows] = X[batch,cols] W^T.  act_mode MV_ACT_Q8 is the reference's
+ * MEMVANTA_FORCE_Q8_ACT=1 path (Q4_0 rows with Q8 activations; Q8_0 keeps
+ * fp32 activations); MV_ACT_F32 is its default fp32-activation path.  Q6_K,
+ * F16 and F32 always take fp32 activations, as tensor_matmul_batch does.
+ * Replaces tensor_matmul_batch_v06 (src/gguf_kernels.cpp:261-271,
+ * include/memvanta/gguf_kernels.hpp:30) and tensor_matmul_batch (:255-259). */
+MV_API int mv_gemm(mv_weight_t w, const float* x_dev, uint64_t batch, float* y_dev, int act_mode, void* stream);
+
+/* Per-row Q8 activation quantisation: q[rows*cols] int8, d[rows*cols/32] fp32.
+ * Replaces quantize_q8 / quantize_activations_q8
+ * (src/gguf_kernels.cpp:161-178). */
+MV_API int mv_quantize_q8(const float* x_dev, uint64_t rows, uint64_t cols, int8_t* q_dev, float* d_dev, void* stream);
+
+/* Diagnostic: the int32 dot of every Q4_0 block of W with the Q8-quantised x,
+ * isum[rows*(cols/32)], computed by the same device code as mv_gemv.
+ * Counterpart of dot_q4_q8_block (src/gguf_kernels.cpp:180-188). */
+MV_API int mv_q4_0_block_dots(mv_weight_t w, const float* x_dev, int32_t* isum_dev, void* stream);
+
+/* Dequantised row (embedding lookup): out[cols] = W[row,:].
+ * Replaces tensor_read_row_f32 (src/gguf_kernels.cpp:226). */
+MV_API int mv_read_row(mv_weight_t w, uint64_t row, float* out_dev, void* stream);
+/* Same for `n` rows given by a device array of token ids (out[n*cols]). */
+MV_API int mv_read_rows(mv_weight_t w, const int32_t* rows_dev, uint64_t n, float* out_dev, void* stream);
+
+/* --------------------------------------------------- ops (device ptrs) */
+
+/* out = x * (1/sqrt(mean(x^2)+eps)) * w per row of n; sum of squares in
+ * double.  Replaces LlamaModel::rmsnorm / rms_batch (src/llama_model.cpp:237,
+ * :245). */
+MV_API int mv_rmsnorm(const float* x_dev, const float* w_dev, uint64_t rows, uint64_t n, float eps, float* out_dev,
+               void* stream);
+/* Half-split RoPE in place for `rows` tokens: q[rows, n_head*hd],
+ * k[rows, n_head_kv*hd]; token r rotates with row pos[r] of the host-built
+ * cos/sin tables [n_ctx, hd/2].  Replaces LlamaModel::rope_ptr
+ * (src/llama_model.cpp:238). */
+MV_API int mv_rope(float* q_dev, uint64_t n_head, float* k_dev, uint64_t n_head_kv, uint64_t head_dim, uint64_t rows,
+            const float* cos_dev, const float* sin_dev, const int32_t* pos_dev, void* stream);
+/* out = g/(1+exp(-g)) * u.  src/llama_model.cpp:249, :257. */
+MV_API int mv_silu_mul(const float* g_dev, const float* u_dev, float* out_dev, uint64_t n, void* stream);
+/* x += y.  src/llama_model.cpp:249, :257. */
+MV_API int mv_add_inplace(float* x_dev, const float* y_dev, uint64_t n, void* stream);
+/* h = fp32_to_fp16(x) with the reference's rounding (src/gguf_kernels.cpp:242). */
+MV_API int mv_fp32_to_fp16(const float* x_dev, uint16_t* h_dev, uint64_t n, void* stream);
+
+/* ------------------------------------------------ paged KV cache (device) */
+
+/* Bytes of one cached token row of kv_dim elements and fp32 scales per row. */
+MV_API uint64_t mv_kv_row_bytes(int kv_type, uint64_t kv_dim);
+MV_API uint64_t mv_kv_row_scales(int kv_type, uint64_t kv_dim);
+
+/* Writes `rows` tokens of k/v [rows, kv_dim] into the paged cache.  Token r
+ * goes to position pos[r] of sequence seq[r] (seq_dev may be NULL: all 0):
+ * page block_table[seq*max_pages + pos/page] slot pos%page.  k_pages /
+ * v_pages hold n_pages*page rows of mv_kv_row_bytes each; k_scales /
+ * v_scales (Q8 types only) n_pages*page*mv_kv_row_scales floats.
+ * Replaces PagedKVCache::write (src/llama_model.cpp:22). */
+MV_API int mv_kv_append(int kv_type, const float* k_dev, const float* v_dev, uint64_t rows, uint64_t kv_dim,
+                 const int32_t* seq_dev, const int32_t* pos_dev, const int32_t* block_table_dev,
+                 uint64_t max_pages, uint64_t page, void* k_pages_dev, void* v_pages_dev, float* k_scales_dev,
+                 float* v_scales_dev, void* stream);
+
+/* One-query attention for n_seq sequences over a paged cache:
+ * q[n_seq, n_head*hd] -> out[n_seq, n_head*hd]; sequence s attends to
+ * ctx_len[s] tokens whose pages are block_table[s*max_pages + i].  Per head:
+ * softmax(q.k/sqrt(hd)) . v, GQA kv head h/(n_head/n_head_kv).  Split over
+ * the context (split-K) with an exact max/sum merge.
+ * Replaces the decode attention loop over PagedKVCache::dot_key/add_value
+ * (src/llama_model.cpp:23-55, :256). */
+MV_API int mv_paged_attn_decode(int kv_type, const float* q_dev, uint64_t n_seq, uint64_t n_head, uint64_t n_head_kv,
+                         uint64_t head_dim, const void* k_pages_dev, const void* v_pages_dev,
+                         const float* k_scales_dev, const float* v_scales_dev, const int32_t* block_table_dev,
+                         uint64_t max_pages, uint64_t page, const int32_t* ctx_len_dev, uint64_t max_ctx,
+                         float* out_dev, void* stream);
+
+/* ---------------------------------- host-pointer calls (reference contract) */
+
+/* tensor_matvec with the reference's contract: x and y are HOST pointers,
+ * y fully overwritten, synchronous.  src/gguf_kernels.cpp:244-253. */
+MV_API int mv_tensor_matvec_host(mv_weight_t w, const float* x_host, float* y_host);
+/* tensor_matmul_batch_v06 with host pointers.  src/gguf_kernels.cpp:261-271. */
+MV_API int mv_tensor_matmul_batch_host(mv_weight_t w, const float* x_host, float* y_host, uint64_t batch, int act_mode);
+/* tensor_read_row_f32 with a host output.  src/gguf_kernels.cpp:226. */
+MV_API int mv_tensor_read_row_host(mv_weight_t w, uint64_t row, float* out_host);
+
+/* ------------------------------------------------------------- model */
+
+/* Device-resident LlamaModel backend: parses the GGUF (mmap), uploads every
+ * weight once, builds the RoPE tables on the host exactly as the reference
+ * does.  Replaces LlamaModel::LlamaModel / load_config
+ * (src/llama_model.cpp:222-235, include/memvanta/llama_model.hpp:102).
+ * ctx = 0 keeps the GGUF context length; page_tokens = 0 -> 128. */
+MV_API int mv_model_open(const char* gguf_path, uint64_t ctx, uint64_t page_tokens, int kv_type, mv_model_t* out);
+MV_API int mv_model_close(mv_model_t m);
+/* n_ctx, n_embd, n_ff, n_layer, n_head, n_head_kv, vocab (7 values). */
+MV_API int mv_model_config(mv_model_t m, uint64_t* out7);
+MV_API int mv_model_reset(mv_model_t m);                       /* LlamaModel::reset, :236 */
+MV_API uint64_t mv_model_position(mv_model_t m);               /* LlamaModel::position     */
+MV_API uint64_t mv_model_kv_bytes(mv_model_t m);               /* kv_bytes_allocated       */
+/* Decode one token; logits_host (vocab floats) may be NULL when
+ * compute_logits is 0.  LlamaModel::forward, src/llama_model.cpp:253-259. */
+MV_API int mv_model_forward(mv_model_t m, int32_t token, int compute_logits, float* logits_host);
+/* Prefill in chunks of `batch` tokens with Q8 activations (the reference's
+ * MEMVANTA_FORCE_Q8_ACT=1 numerics).  LlamaModel::prefill, :260. */
+MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens_host, uint64_t n, uint64_t batch, int compute_logits,
+                     float* logits_host);
+/* Greedy decode of n tokens starting from `token`, on the device: every step
+ * is one captured CUDA graph and the argmax stays in HBM; only the n token ids
+ * come back.  Matches forward()+Sampler::sample at temperature 0 (:60-61). */
+MV_API int mv_model_generate_greedy(mv_model_t m, int32_t token, uint64_t n, int32_t* out_tokens_host);
+/* The model's stream (cudaStream_t) -- for event timing by the caller. */
+MV_API void* mv_model_stream(mv_model_t m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MEMVANTA_B200_H */

@@ -1,0 +1,117 @@
+// common.cuh -- device helpers shared by every memvanta_b200 kernel.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace mvb {
+
+constexpr int kWarp = 32;
+
+// Raises a kernel's dynamic shared-memory limit once per device.
+template <class Kernel>
+inline void ensure_smem_attr(Kernel* k, int bytes) {
+    static unsigned done = 0;  // bit per device id
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 32 && (done >> dev) & 1u) return;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (dev < 32) done |= 1u << dev;
+}
+
+// ---------------------------------------------------------------- reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// --------------------------------------------------------------- loads
+// Weight bytes are read exactly once per launch: bypass L1 allocation and
+// go through the read-only path.
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint32_t ld_stream_u32(const void* p) {
+    uint32_t r;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ unsigned short ld_stream_u16(const void* p) {
+    unsigned short r;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float half_bits_to_float(unsigned short h) {
+    return __half2float(__ushort_as_half(h));
+}
+
+// ------------------------------------------------------ integer dot products
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// Exact float of a signed byte held in the low 8 bits: 2^23 + (b ^ 0x80)
+// as a float bit pattern, minus 2^23 + 128.
+__device__ __forceinline__ float s8_to_f32(uint32_t word, int byte) {
+    const uint32_t u = __byte_perm(word, 0x4B000000u, 0x7650u + byte) ^ 0x80u;
+    return __uint_as_float(u) - 8388736.0f;
+}
+// Exact float of an unsigned byte minus `bias` (bias < 2^22).
+__device__ __forceinline__ float u8_to_f32_minus(uint32_t word, int byte, float bias_plus_2p23) {
+    const uint32_t u = __byte_perm(word, 0x4B000000u, 0x7650u + byte);
+    return __uint_as_float(u) - bias_plus_2p23;
+}
+
+// --------------------------------------------------------- fp32 -> fp16
+// The reference's own conversion (src/gguf_kernels.cpp:242): add half an
+// output ulp to the magnitude and truncate (round-half-up on magnitude), carry
+// into the exponent, >= 2^16 (and NaN) -> inf, below 2^-25 -> signed zero.
+// Restated bit for bit so KV pages match the reference exactly; the
+// hardware's round-to-nearest-even conversion would differ on ties.
+__device__ __forceinline__ unsigned short f32_to_f16_ref(float f) {
+    const uint32_t x = __float_as_uint(f);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t mant = x & 0x7fffffu;
+    const int e = int((x >> 23) & 0xffu) - 112;
+    if (e >= 31) return (unsigned short)(sign | 0x7c00u);
+    if (e > 0) return (unsigned short)(sign | (uint32_t(e) << 10) | ((mant + 0x1000u) >> 13));
+    if (e < -10) return (unsigned short)sign;
+    mant = (mant | 0x800000u) >> (1 - e);
+    return (unsigned short)(sign + ((mant + 0x1000u) >> 13));
+}
+
+// ------------------------------------------------------ activation quant
+// One 32-element block of the reference's quantize_q8
+// (src/gguf_kernels.cpp:161-172), one element per lane: mx = max|x|,
+// d = mx>0 ? mx/127 : 1, q = clamp(round-half-away(x * (1/d)), -127, 127).
+// IEEE division and multiplication (no fast-math) keep it bit-identical.
+__device__ __forceinline__ int quant_q8_lane(float v, float& d_out) {
+    const float mx = warp_max(fabsf(v));
+    const float d = mx > 0.0f ? mx / 127.0f : 1.0f;
+    const float inv = 1.0f / d;
+    float r = roundf(v * inv);
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    d_out = d;
+    return int(r);
+}
+
+}  // namespace mvb

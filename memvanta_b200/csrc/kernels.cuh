@@ -1,0 +1,84 @@
+// kernels.cuh -- host-side launchers of every kernel, shared by the C ABI
+// (capi.cu) and the device-resident model (model.cu).  All launchers are
+// asynchronous on `s` and return cudaGetLastError() of the launch.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "weights.cuh"
+
+namespace mvb {
+
+int num_sms();
+
+// ---- weights.cu
+cudaError_t repack_from_ggml(mv_weight_s& w, const uint8_t* raw_dev, cudaStream_t s);
+cudaError_t unpack_to_ggml(const mv_weight_s& w, uint8_t* raw_dev, cudaStream_t s);
+cudaError_t read_rows(const mv_weight_s& w, const int32_t* rows, uint64_t n, float* out, cudaStream_t s);
+cudaError_t quantize_q8_rows(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* d, cudaStream_t s);
+
+// ---- gemv.cu : decode GEMV over Q4_0 with Q8 activations (integer path)
+enum class Q4Pro : int {
+    Plain = 0,    // activations = x
+    RmsNorm = 1,  // activations = rmsnorm(x) * norm_w (the reference's rmsnorm)
+};
+enum class Q4Epi : int {
+    Store = 0,     // y[r] = acc
+    AddTo = 1,     // y[r] += acc          (residual stream)
+    SiluGate = 2,  // rows come in (gate,up) pairs: y[r/2] = silu(g) * u
+};
+struct GemvQ4Args {
+    const mv_weight_s* w;
+    const float* x;
+    const float* norm_w;  // RmsNorm only
+    float eps;
+    float* y;
+    Q4Pro pro;
+    Q4Epi epi;
+};
+cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s);
+cudaError_t q4_block_dots(const mv_weight_s& w, const float* x, int32_t* isum, cudaStream_t s);
+
+// ---- gemv.cu : fp32-activation matmul for every type (T tokens per pass)
+cudaError_t matmul_f32act(const mv_weight_s& w, const float* x, uint64_t batch, float* y, cudaStream_t s);
+
+// ---- gemm.cu : batched Q4_0 x Q8 activations (prefill)
+// q/d: activations already quantised per row (quantize_q8_rows).
+cudaError_t gemm_q4_q8(const mv_weight_s& w, const int8_t* q, const float* d, uint64_t batch, float* y,
+                       cudaStream_t s);
+
+// ---- ops.cu
+cudaError_t rmsnorm_rows(const float* x, const float* w, uint64_t rows, uint64_t n, float eps, float* out,
+                         cudaStream_t s);
+cudaError_t rope_rows(float* q, uint64_t n_head, float* k, uint64_t n_head_kv, uint64_t hd, uint64_t rows,
+                      const float* cos_t, const float* sin_t, const int32_t* pos, cudaStream_t s);
+cudaError_t silu_mul(const float* g, const float* u, float* out, uint64_t n, cudaStream_t s);
+cudaError_t add_inplace(float* x, const float* y, uint64_t n, cudaStream_t s);
+cudaError_t f32_to_f16_ref(const float* x, uint16_t* h, uint64_t n, cudaStream_t s);
+cudaError_t argmax_f32(const float* x, uint64_t n, int32_t* out_idx, cudaStream_t s);
+
+// ---- attention.cu
+uint64_t kv_row_bytes(int kv_type, uint64_t kv_dim);
+uint64_t kv_row_scales(int kv_type, uint64_t kv_dim);
+cudaError_t kv_append(int kv_type, const float* k, const float* v, uint64_t rows, uint64_t kv_dim,
+                      const int32_t* seq, const int32_t* pos, const int32_t* block_table, uint64_t max_pages,
+                      uint64_t page, void* k_pages, void* v_pages, float* k_scales, float* v_scales,
+                      cudaStream_t s);
+struct AttnArgs {
+    int kv_type;
+    const float* q;
+    uint64_t n_seq, n_head, n_head_kv, hd;
+    const void* k_pages;
+    const void* v_pages;
+    const float* k_scales;
+    const float* v_scales;
+    const int32_t* block_table;
+    uint64_t max_pages, page;
+    const int32_t* ctx_len;  // per sequence
+    uint64_t max_ctx;        // upper bound of ctx_len (sizes the split grid)
+    float* out;
+    float* scratch;          // split partials; attn_scratch_floats() floats
+};
+uint64_t attn_scratch_floats(uint64_t n_seq, uint64_t n_head, uint64_t hd, uint64_t max_ctx);
+cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s);
+
+}  // namespace mvb

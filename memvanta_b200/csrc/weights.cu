@@ -1,0 +1,185 @@
+// weights.cu -- GGUF block repack / unpack, row dequantisation (embedding
+// lookup) and the per-row Q8 activation quantiser.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mvb {
+
+int num_sms() {
+    static thread_local int dev = -1, sms = 0;
+    int d = 0;
+    cudaGetDevice(&d);
+    if (d != dev) {
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d);
+        dev = d;
+    }
+    return sms;
+}
+
+// ------------------------------------------------------------- repack
+// One thread per block.  Raw GGUF bytes are read with byte loads (18/34/210
+// byte blocks are unaligned); the planes are written with wide stores.
+__global__ void repack_q4_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ qs, uint16_t* __restrict__ d,
+                                 uint64_t nblocks) {
+    for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblocks; b += (uint64_t)gridDim.x * blockDim.x) {
+        const uint8_t* p = raw + b * 18;
+        d[b] = (uint16_t)(p[0] | (p[1] << 8));
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            w[i] = p[2 + 4 * i] | (p[3 + 4 * i] << 8) | (p[4 + 4 * i] << 16) | ((uint32_t)p[5 + 4 * i] << 24);
+        reinterpret_cast<uint4*>(qs)[b] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+__global__ void unpack_q4_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ d, uint8_t* __restrict__ raw,
+                                 uint64_t nblocks) {
+    for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblocks; b += (uint64_t)gridDim.x * blockDim.x) {
+        uint8_t* p = raw + b * 18;
+        p[0] = d[b] & 0xff;
+        p[1] = d[b] >> 8;
+        for (int i = 0; i < 16; ++i) p[2 + i] = qs[b * 16 + i];
+    }
+}
+__global__ void repack_q8_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ qs, uint16_t* __restrict__ d,
+                                 uint64_t nblocks) {
+    for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblocks; b += (uint64_t)gridDim.x * blockDim.x) {
+        const uint8_t* p = raw + b * 34;
+        d[b] = (uint16_t)(p[0] | (p[1] << 8));
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            w[i] = p[2 + 4 * i] | (p[3 + 4 * i] << 8) | (p[4 + 4 * i] << 16) | ((uint32_t)p[5 + 4 * i] << 24);
+        uint4* o = reinterpret_cast<uint4*>(qs + b * 32);
+        o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+}
+__global__ void unpack_q8_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ d, uint8_t* __restrict__ raw,
+                                 uint64_t nblocks) {
+    for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblocks; b += (uint64_t)gridDim.x * blockDim.x) {
+        uint8_t* p = raw + b * 34;
+        p[0] = d[b] & 0xff;
+        p[1] = d[b] >> 8;
+        for (int i = 0; i < 32; ++i) p[2 + i] = qs[b * 32 + i];
+    }
+}
+// Q6_K: 210 B {ql[128], qh[64], scales[16], d} -> four planes.
+__global__ void repack_q6k_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ ql, uint8_t* __restrict__ qh,
+                                  int8_t* __restrict__ sc, uint16_t* __restrict__ d, uint64_t nblocks) {
+    for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblocks; b += (uint64_t)gridDim.x * blockDim.x) {
+        const uint8_t* p = raw + b * 210;
+        for (int i = 0; i < 128; ++i) ql[b * 128 + i] = p[i];
+        for (int i = 0; i < 64; ++i) qh[b * 64 + i] = p[128 + i];
+        for (int i = 0; i < 16; ++i) sc[b * 16 + i] = (int8_t)p[192 + i];
+        d[b] = (uint16_t)(p[208] | (p[209] << 8));
+    }
+}
+__global__ void unpack_q6k_kernel(const uint8_t* __restrict__ ql, const uint8_t* __restrict__ qh, const int8_t* __restrict__ sc,
+                                  const uint16_t* __restrict__ d, uint8_t* __restrict__ raw, uint64_t nblocks) {
+    for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblocks; b += (uint64_t)gridDim.x * blockDim.x) {
+        uint8_t* p = raw + b * 210;
+        for (int i = 0; i < 128; ++i) p[i] = ql[b * 128 + i];
+        for (int i = 0; i < 64; ++i) p[128 + i] = qh[b * 64 + i];
+        for (int i = 0; i < 16; ++i) p[192 + i] = (uint8_t)sc[b * 16 + i];
+        p[208] = d[b] & 0xff;
+        p[209] = d[b] >> 8;
+    }
+}
+
+static dim3 grid_for(uint64_t n, int threads) {
+    const uint64_t g = (n + threads - 1) / threads;
+    const uint64_t cap = (uint64_t)num_sms() * 16;
+    return dim3((unsigned)(g < cap ? (g ? g : 1) : cap));
+}
+
+cudaError_t repack_from_ggml(mv_weight_s& w, const uint8_t* raw, cudaStream_t s) {
+    const uint64_t nblocks = w.rows * w.nb;
+    switch (w.type) {
+        case 2: repack_q4_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(raw, w.qs, w.d, nblocks); break;
+        case 8: repack_q8_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(raw, w.qs, w.d, nblocks); break;
+        case 14: repack_q6k_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(raw, w.qs, w.qh, w.sc, w.d, nblocks); break;
+        default: return cudaMemcpyAsync(w.qs, raw, w.rows * w.cols * (w.type == 0 ? 4 : 2), cudaMemcpyDeviceToDevice, s);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t unpack_to_ggml(const mv_weight_s& w, uint8_t* raw, cudaStream_t s) {
+    const uint64_t nblocks = w.rows * w.nb;
+    switch (w.type) {
+        case 2: unpack_q4_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(w.qs, w.d, raw, nblocks); break;
+        case 8: unpack_q8_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(w.qs, w.d, raw, nblocks); break;
+        case 14: unpack_q6k_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(w.qs, w.qh, w.sc, w.d, raw, nblocks); break;
+        default: return cudaMemcpyAsync(raw, w.qs, w.rows * w.cols * (w.type == 0 ? 4 : 2), cudaMemcpyDeviceToDevice, s);
+    }
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ read rows
+// out[i, :] = dequantised row rows[i], as tensor_read_row_f32
+// (src/gguf_kernels.cpp:226): Q4_0 d*(q-8), Q8_0 d*q, Q6_K d*scale*q6
+// (float products in that order), F16 exact, F32 copy.  One CTA per row.
+__global__ void read_rows_kernel(mv_weight_s w, const int32_t* __restrict__ rows, float* __restrict__ out) {
+    const uint64_t r = (uint64_t)rows[blockIdx.x];
+    float* o = out + (uint64_t)blockIdx.x * w.cols;
+    if (r >= w.rows) {  // out-of-range ids give a NaN row instead of a wild read
+        for (uint64_t c = threadIdx.x; c < w.cols; c += blockDim.x) o[c] = __int_as_float(0x7fc00000);
+        return;
+    }
+    for (uint64_t c = threadIdx.x; c < w.cols; c += blockDim.x) {
+        float v;
+        if (w.type == 2) {
+            const uint64_t b = r * w.nb + c / 32;
+            const int e = c % 32;
+            const uint8_t byte = w.qs[b * 16 + (e & 15)];
+            const int q = (e < 16 ? (byte & 15) : (byte >> 4)) - 8;
+            v = half_bits_to_float(w.d[b]) * (float)q;
+        } else if (w.type == 8) {
+            const uint64_t b = r * w.nb + c / 32;
+            v = half_bits_to_float(w.d[b]) * (float)(int8_t)w.qs[b * 32 + c % 32];
+        } else if (w.type == 14) {
+            const uint64_t b = r * w.nb + c / 256;
+            const int i = c % 256, r32 = i / 32, j = i % 32, g = r32 / 4, slot = r32 % 4;
+            const int lo = (w.qs[b * 128 + g * 64 + (slot & 1) * 32 + j] >> (slot < 2 ? 0 : 4)) & 15;
+            const int hi = (w.qh[b * 64 + g * 32 + j] >> (2 * slot)) & 3;
+            const int q6 = (lo | (hi << 4)) - 32;
+            v = half_bits_to_float(w.d[b]) * (float)w.sc[b * 16 + i / 16] * (float)q6;
+        } else if (w.type == 1) {
+            v = half_bits_to_float(reinterpret_cast<const uint16_t*>(w.qs)[r * w.cols + c]);
+        } else {
+            v = reinterpret_cast<const float*>(w.qs)[r * w.cols + c];
+        }
+        o[c] = v;
+    }
+}
+
+cudaError_t read_rows(const mv_weight_s& w, const int32_t* rows, uint64_t n, float* out, cudaStream_t s) {
+    if (!n) return cudaSuccess;
+    read_rows_kernel<<<(unsigned)n, 256, 0, s>>>(w, rows, out);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------ activation quant
+// Per row, per 32-element block: the reference's quantize_q8.  One warp per
+// block, one element per lane.
+__global__ void quantize_q8_kernel(const float* __restrict__ x, uint64_t nblocks, int8_t* __restrict__ q,
+                                   float* __restrict__ d) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
+    for (uint64_t b = blockIdx.x * (uint64_t)(blockDim.x / 32) + threadIdx.x / 32; b < nblocks; b += warps) {
+        float dd;
+        const int v = quant_q8_lane(x[b * 32 + lane], dd);
+        q[b * 32 + lane] = (int8_t)v;
+        if (lane == 0) d[b] = dd;
+    }
+}
+
+cudaError_t quantize_q8_rows(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* d, cudaStream_t s) {
+    const uint64_t nblocks = rows * (cols / 32);
+    if (!nblocks) return cudaSuccess;
+    const uint64_t ctas = (nblocks + 7) / 8;
+    const uint64_t cap = (uint64_t)num_sms() * 8;
+    quantize_q8_kernel<<<(unsigned)(ctas < cap ? ctas : cap), 256, 0, s>>>(x, nblocks, q, d);
+    return cudaGetLastError();
+}
+
+}  // namespace mvb

@@ -1,0 +1,96 @@
+"""LlamaModel: the device-resident decoder behind the C ABI (mv_model_*).
+
+Mirrors the reference's public class (include/memvanta/llama_model.hpp:100-113):
+``LlamaModel(path, threads, ctx, page_tokens, kv_type)``, ``forward``,
+``prefill``, ``generate``, ``reset``, ``position``, ``kv_bytes_allocated``.
+``threads`` is accepted for signature compatibility and ignored (the GPU
+parallelises internally).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from ._lib import KV_F16, check, load
+
+
+class LlamaModel:
+    def __init__(self, gguf_path: str | os.PathLike, threads: int = 1, ctx_override: int = 0,
+                 kv_page_tokens: int = 128, kv_type: int = KV_F16):
+        self._m = None
+        h = C.c_void_p()
+        check(load().mv_model_open(os.fspath(gguf_path).encode(), ctx_override, kv_page_tokens, kv_type,
+                                   C.byref(h)))
+        self._m = h
+        cfg = (C.c_uint64 * 7)()
+        check(load().mv_model_config(self._m, cfg))
+        self.n_ctx, self.n_embd, self.n_ff, self.n_layer, self.n_head, self.n_head_kv, self.vocab = list(cfg)
+        self._logits = np.empty(self.vocab, np.float32)
+
+    def config(self) -> dict:
+        return {"n_ctx": self.n_ctx, "n_embd": self.n_embd, "n_ff": self.n_ff, "n_layer": self.n_layer,
+                "n_head": self.n_head, "n_head_kv": self.n_head_kv, "vocab": self.vocab}
+
+    def reset(self) -> None:
+        check(load().mv_model_reset(self._m))
+
+    def position(self) -> int:
+        return load().mv_model_position(self._m)
+
+    def kv_bytes_allocated(self) -> int:
+        return load().mv_model_kv_bytes(self._m)
+
+    @property
+    def stream(self) -> int:
+        return load().mv_model_stream(self._m) or 0
+
+    def forward(self, token: int, compute_logits: bool = True, out: np.ndarray | None = None) -> np.ndarray:
+        """One decode step (src/llama_model.cpp:253-259); returns host logits."""
+        out = self._logits if out is None else out
+        check(load().mv_model_forward(self._m, int(token), int(compute_logits),
+                                      out.ctypes.data_as(C.c_void_p) if compute_logits else None))
+        return out
+
+    def prefill(self, tokens, batch_size: int = 64, compute_logits_last: bool = True) -> np.ndarray:
+        """Chunked prefill (src/llama_model.cpp:260) with Q8 activations."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        check(load().mv_model_prefill(self._m, t.ctypes.data_as(C.c_void_p), t.size, batch_size,
+                                      int(compute_logits_last),
+                                      self._logits.ctypes.data_as(C.c_void_p) if compute_logits_last else None))
+        return self._logits
+
+    def generate_greedy(self, token: int, n: int) -> np.ndarray:
+        """n greedy steps from `token`, argmax on the device."""
+        out = np.empty(n, np.int32)
+        check(load().mv_model_generate_greedy(self._m, int(token), n, out.ctypes.data_as(C.c_void_p)))
+        return out
+
+    def generate(self, prompt, n: int, eos_id: int | None = None) -> list:
+        """LlamaModel::generate at temperature 0 (src/llama_model.cpp:261)."""
+        prompt = list(prompt)
+        if not prompt:
+            raise ValueError("prompt cannot be empty")
+        self.reset()
+        if len(prompt) > 1:
+            self.prefill(prompt[:-1], 64, False)
+        cur, out = prompt[-1], []
+        for _ in range(n):
+            nxt = int(np.argmax(self.forward(cur, True)))
+            out.append(nxt)
+            cur = nxt
+            if eos_id is not None and nxt == eos_id:
+                break
+        return out
+
+    def close(self) -> None:
+        if self._m:
+            load().mv_model_close(self._m)
+            self._m = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,194 @@
+"""Parity of the CUDA ops around the matmuls and of the paged KV attention
+(through the C ABI) with the oracle and the reference's golden outputs."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import memvanta_b200 as mv
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a, cuda):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+def host(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def test_fp32_to_fp16_golden(cuda, golden):
+    g = golden("fp16_cases.npz")
+    h = host(mv.fp32_to_fp16(dev(g["x"], cuda))).view(np.uint16)
+    assert np.array_equal(h, g["h"])
+
+
+def test_rmsnorm(cuda, oracle):
+    rng = np.random.default_rng(31)
+    x = (rng.standard_normal((5, 4096)) * 3).astype(np.float32)
+    w = (1 + rng.uniform(-0.02, 0.02, 4096)).astype(np.float32)
+    got = host(mv.rmsnorm(dev(x, cuda), dev(w, cuda), 1e-6))
+    want = np.stack([oracle.rmsnorm(x[i], w, 1e-6) for i in range(5)])
+    # double sum of squares: only the summation order differs -> equal to 1 ulp
+    np.testing.assert_allclose(got, want, rtol=2.5e-7, atol=0)
+
+
+def test_rope_bit_exact(cuda, oracle):
+    rng = np.random.default_rng(32)
+    n_head, n_head_kv, hd, n_ctx = 32, 8, 128, 64
+    cos_t, sin_t = oracle.rope_tables(n_ctx, hd, 10000.0)
+    q = rng.standard_normal((3, n_head * hd)).astype(np.float32)
+    k = rng.standard_normal((3, n_head_kv * hd)).astype(np.float32)
+    pos = np.array([0, 17, 63], np.int32)
+    qd, kd = dev(q, cuda), dev(k, cuda)
+    mv.rope(qd, n_head, kd, n_head_kv, hd, dev(cos_t, cuda), dev(sin_t, cuda), dev(pos, cuda))
+    for i in range(3):
+        qo, ko = oracle.rope(q[i], n_head, k[i], n_head_kv, hd, cos_t[pos[i]], sin_t[pos[i]])
+        assert np.array_equal(host(qd)[i].view(np.uint32), qo.view(np.uint32))
+        assert np.array_equal(host(kd)[i].view(np.uint32), ko.view(np.uint32))
+
+
+def test_silu_mul(cuda, oracle):
+    rng = np.random.default_rng(33)
+    g = (rng.standard_normal(11008) * 4).astype(np.float32)
+    u = rng.standard_normal(11008).astype(np.float32)
+    got = host(mv.silu_mul(dev(g, cuda), dev(u, cuda)))
+    np.testing.assert_allclose(got, oracle.silu_mul(g, u), rtol=1e-6, atol=1e-7)
+
+
+# ---------------------------------------------------------------- KV cache
+
+def _alloc_cache(cuda, kv_type, kv_dim, n_slots):
+    import torch
+    rb = mv.kv_row_bytes(kv_type, kv_dim)
+    ns = mv.kv_row_scales(kv_type, kv_dim)
+    kp = torch.zeros((n_slots, rb), dtype=torch.uint8, device=cuda)
+    vp = torch.zeros_like(kp)
+    ks = torch.zeros((n_slots, max(ns, 1)), dtype=torch.float32, device=cuda) if ns else None
+    vs = torch.zeros_like(ks) if ns else None
+    return kp, vp, ks, vs, ns
+
+
+@pytest.mark.parametrize("kv_type", [mv.KV_F32, mv.KV_F16, mv.KV_Q8, mv.KV_Q8_0])
+def test_kv_append_bit_exact(cuda, oracle, kv_type):
+    rng = np.random.default_rng(34 + kv_type)
+    kv_dim, page, rows = 4096, 16, 7
+    k = rng.standard_normal((rows, kv_dim)).astype(np.float32)
+    v = (rng.standard_normal((rows, kv_dim)) * 5).astype(np.float32)
+    k[2] = 0.0                                             # all-zero row -> scale 1
+    table = np.array([3, 0, 5, 1], np.int32)
+    pos = np.array([0, 1, 15, 16, 17, 40, 63], np.int32)
+    kp, vp, ks, vs, ns = _alloc_cache(cuda, kv_type, kv_dim, 6 * page)
+    mv.kv_append(kv_type, dev(k, cuda), dev(v, cuda), dev(pos, cuda), dev(table, cuda), 4, page, kp, vp, ks, vs)
+    kp_h, vp_h = host(kp), host(vp)
+    for r in range(rows):
+        slot = table[pos[r] // page] * page + pos[r] % page
+        raw_k, sk = oracle.kv_store(kv_type, k[r])
+        raw_v, sv = oracle.kv_store(kv_type, v[r])
+        assert np.array_equal(kp_h[slot], raw_k) and np.array_equal(vp_h[slot], raw_v), r
+        if ns:
+            assert np.array_equal(host(ks)[slot, :ns], sk) and np.array_equal(host(vs)[slot, :ns], sv)
+
+
+def _oracle_cache(oracle, kv_type, K, V, table, page, n_slots):
+    kv_dim = K.shape[1]
+    rb, ns = oracle.kv_row_bytes(kv_type, kv_dim), oracle.kv_row_scales(kv_type, kv_dim)
+    kp = np.zeros((n_slots, rb), np.uint8)
+    vp = np.zeros_like(kp)
+    ks = np.zeros((n_slots, max(ns, 1)), np.float32)
+    vs = np.zeros_like(ks)
+    for t in range(K.shape[0]):
+        slot = table[t // page] * page + t % page
+        kp[slot], s1 = oracle.kv_store(kv_type, K[t])
+        vp[slot], s2 = oracle.kv_store(kv_type, V[t])
+        ks[slot, :ns], vs[slot, :ns] = s1, s2
+    return kp, vp, (ks if ns else None), (vs if ns else None)
+
+
+def test_attention_golden(cuda, golden):
+    """The reference's PagedKVCache dot_key/add_value loop, F32/F16/Q8 pages."""
+    import torch
+    g = golden("kv_attention.npz")
+    n_head, n_head_kv, hd, page, n_ctx = (int(v) for v in g["meta"])
+    kv_dim = n_head_kv * hd
+    n_pages = (n_ctx + page - 1) // page
+    table = dev(np.arange(n_pages, dtype=np.int32), cuda)
+    pos = dev(np.arange(n_ctx, dtype=np.int32), cuda)
+    for kvt, tag in [(mv.KV_F32, "f32"), (mv.KV_F16, "f16"), (mv.KV_Q8, "q8")]:
+        kp, vp, ks, vs, _ = _alloc_cache(cuda, kvt, kv_dim, n_pages * page)
+        mv.kv_append(kvt, dev(g["K"], cuda), dev(g["V"], cuda), pos, table, n_pages, page, kp, vp, ks, vs)
+        out = mv.paged_attn_decode(kvt, dev(g["q"][None], cuda), n_head, n_head_kv, hd, kp, vp, table, n_pages, page,
+                                   dev(np.array([n_ctx], np.int32), cuda), n_ctx, ks, vs)
+        assert rel_err(host(out)[0], g[f"{tag}_att"]) <= 1e-4, tag
+
+
+@pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_Q8, mv.KV_Q8_0, mv.KV_F32])
+def test_config4_ragged_paged_attention(cuda, oracle, kv_type):
+    """Config 4: 64 sequences, ctx ~ U(64..768), 16-token pages scattered by a
+    random permutation block table, 32 heads x 128, Q/K/V ~ N(0,1)."""
+    import torch
+    rng = np.random.default_rng(40 + kv_type)
+    n_seq, n_head, hd, page = 64, 32, 128, 16
+    n_head_kv = n_head
+    kv_dim = n_head_kv * hd
+    ctx = rng.integers(64, 769, n_seq).astype(np.int32)
+    max_pages = int((ctx.max() + page - 1) // page)
+    total_pages = int(sum((c + page - 1) // page for c in ctx))
+    perm = rng.permutation(total_pages).astype(np.int32)
+    table = np.zeros((n_seq, max_pages), np.int32)
+    o = 0
+    for s in range(n_seq):
+        npg = (ctx[s] + page - 1) // page
+        table[s, :npg] = perm[o:o + npg]
+        o += npg
+    kp, vp, ks, vs, ns = _alloc_cache(cuda, kv_type, kv_dim, total_pages * page)
+    q = rng.standard_normal((n_seq, n_head * hd)).astype(np.float32)
+    seqs_k, seqs_v = [], []
+    for s in range(n_seq):
+        K = rng.standard_normal((ctx[s], kv_dim)).astype(np.float32)
+        V = rng.standard_normal((ctx[s], kv_dim)).astype(np.float32)
+        seqs_k.append(K)
+        seqs_v.append(V)
+        seq = dev(np.full(ctx[s], s, np.int32), cuda)
+        mv.kv_append(kv_type, dev(K, cuda), dev(V, cuda), dev(np.arange(ctx[s], dtype=np.int32), cuda),
+                     dev(table, cuda), max_pages, page, kp, vp, ks, vs, seq=seq)
+    out = host(mv.paged_attn_decode(kv_type, dev(q, cuda), n_head, n_head_kv, hd, kp, vp, dev(table, cuda), max_pages,
+                                    page, dev(ctx, cuda), int(ctx.max()), ks, vs))
+    # the oracle on a sample of sequences (it runs the reference loop per head)
+    for s in [0, 1, int(np.argmax(ctx)), int(np.argmin(ctx)), 37]:
+        okp, ovp, oks, ovs = _oracle_cache(oracle, kv_type, seqs_k[s], seqs_v[s], table[s], page, total_pages * page)
+        want = oracle.attn_decode(kv_type, q[s], n_head, n_head_kv, hd, okp, ovp, oks, ovs, table[s], page, int(ctx[s]))
+        assert rel_err(out[s], want) <= 1e-4, (s, rel_err(out[s], want))
+
+
+def test_gqa_and_head_dims(cuda, oracle):
+    rng = np.random.default_rng(44)
+    for n_head, n_head_kv, hd in [(8, 2, 128), (4, 4, 64), (8, 1, 256), (16, 2, 64)]:
+        kv_dim, page, n_ctx = n_head_kv * hd, 16, 133
+        n_pages = (n_ctx + page - 1) // page
+        table = rng.permutation(n_pages).astype(np.int32)
+        K = rng.standard_normal((n_ctx, kv_dim)).astype(np.float32)
+        V = rng.standard_normal((n_ctx, kv_dim)).astype(np.float32)
+        q = rng.standard_normal(n_head * hd).astype(np.float32)
+        kp, vp, ks, vs, _ = _alloc_cache(cuda, mv.KV_F16, kv_dim, n_pages * page)
+        mv.kv_append(mv.KV_F16, dev(K, cuda), dev(V, cuda), dev(np.arange(n_ctx, dtype=np.int32), cuda),
+                     dev(table, cuda), n_pages, page, kp, vp, ks, vs)
+        out = host(mv.paged_attn_decode(mv.KV_F16, dev(q[None], cuda), n_head, n_head_kv, hd, kp, vp, dev(table, cuda),
+                                        n_pages, page, dev(np.array([n_ctx], np.int32), cuda), n_ctx))
+        okp, ovp, _, _ = _oracle_cache(oracle, mv.KV_F16, K, V, table, page, n_pages * page)
+        want = oracle.attn_decode(mv.KV_F16, q, n_head, n_head_kv, hd, okp, ovp, None, None, table, page, n_ctx)
+        assert rel_err(out[0], want) <= 1e-4, (n_head, n_head_kv, hd)
+
+
+def test_attention_rejects_bad_shapes(cuda):
+    import torch
+    z = torch.zeros(1024, device=cuda)
+    with pytest.raises(mv.MemVantaError, match="head_dim"):
+        mv.paged_attn_decode(mv.KV_F16, z[None], 8, 8, 96, z, z, z.int(), 1, 16, z.int(), 1)
+    with pytest.raises(mv.MemVantaError, match="multiple"):
+        mv.paged_attn_decode(mv.KV_F16, z[None], 6, 4, 128, z, z, z.int(), 1, 16, z.int(), 1)

@@ -4,8 +4,13 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
 Workloads:
-  q4_gemv   config 0 -- one step = one Q4_0 x Q8 GEMV over a 4096x4096 weight
-            (16 rotated copies, 151 MB > 126 MB L2), metric HBM GB/s.
+  q4_gemv   config 0 -- one step = 16 Q4_0 x Q8 GEMVs, one over each of 16
+            copies of a 4096x4096 weight (151 MB > 126 MB L2, so every launch
+            streams its weight from HBM), metric HBM GB/s.
+
+--clock-window S keeps the same CUDA graph running for S seconds right
+before the timed region so nvidia-smi has samples under load (the timed
+region itself is unchanged).
 
 Multi-GPU: one process per GPU under torchrun; every rank runs its own
 replica of the workload (the GEMV does not shard), timing is the max over
@@ -179,20 +184,20 @@ def run_q4_gemv_ours(args, world, rank, local):
                     mv.gemv(W[i % Q4_COPIES], xd, ys[i % Q4_COPIES], stream)
         return g
 
-    g_warm, g_timed = capture(max(args.warmup, 1) * Q4_COPIES), capture(args.steps)
+    launches = args.steps * Q4_COPIES
+    g_warm, g_timed = capture(args.warmup * Q4_COPIES), capture(launches)
     g_warm.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        # the clock sampler needs a few hundred ms of load: replay the timed
-        # graph a number of times and keep the last replay's events
-        reps = max(1, int(0.6 / max(1e-6, 2e-6 * args.steps)))
-        for _ in range(reps - 1):
-            g_timed.replay()
-        torch.cuda.synchronize()
+        t_end = time.perf_counter() + args.clock_window
+        while time.perf_counter() < t_end:
+            g_warm.replay()
+            torch.cuda.synchronize()
         barrier(world)
+        torch.cuda.synchronize()
         e0.record(stream)
         g_timed.replay()
         e1.record(stream)
@@ -204,7 +209,7 @@ def run_q4_gemv_ours(args, world, rank, local):
     mv.gemv(W[0], xd, y_ref, stream)
     torch.cuda.synchronize()
     assert torch.equal(y_ref, ys[0])
-    per_launch_s = ms / 1e3 / args.steps
+    per_launch_s = ms / 1e3 / launches
     gbs = Q4_ALG_BYTES / per_launch_s / 1e9
     # e2e: the reference-facing host-pointer call (tensor_matvec contract)
     y_host = np.empty(Q4_ROWS, np.float32)
@@ -218,7 +223,7 @@ def run_q4_gemv_ours(args, world, rank, local):
     e2e_s = (time.perf_counter() - t0) / n_e2e
     e2e_s = all_max(e2e_s, world)
     return {"ms_total": ms, "per_launch_s": per_launch_s, "gbs": gbs, "e2e_gbs": Q4_ALG_BYTES / e2e_s / 1e9,
-            "clocks": clk.summary(), "gpu_launches": args.steps}
+            "clocks": clk.summary(), "gpu_launches": launches}
 
 
 def run_q4_gemv_cpu(seconds=8.0):
@@ -252,10 +257,11 @@ def run_q4_gemv_cpu(seconds=8.0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="q4_gemv", choices=["q4_gemv"])
+    ap.add_argument("--clock-window", type=float, default=0.5)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -293,7 +299,8 @@ def main():
     value = r["gbs"] * world
     line = {
         "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": r["ms_total"] / args.steps, "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": r["ms_total"] / args.steps, "launches_per_step": Q4_COPIES,
+        "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic", "config": config,
         "roofline": {"bound": "hbm", "achieved": round(r["gbs"], 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(r["gbs"] / peaks["hbm_gbs"], 4), "traffic": traffic_from_profiles("gemv_q4"),

@@ -4,9 +4,9 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
 Workloads:
-  q4_gemv   config 0 -- one step = 16 Q4_0 x Q8 GEMVs, one over each of 16
-            copies of a 4096x4096 weight (151 MB > 126 MB L2, so every launch
-            streams its weight from HBM), metric HBM GB/s.
+  q4_gemv   config 0 -- one step = 32 Q4_0 x Q8 GEMVs, one over each of 32
+            copies of a 4096x4096 weight (303 MB, 2.4x the 126 MB L2, so every
+            launch streams its weight from HBM), metric HBM GB/s.
 
 --clock-window S keeps the same CUDA graph running for S seconds right
 before the timed region so nvidia-smi has samples under load (the timed
@@ -151,7 +151,7 @@ def traffic_from_profiles(kernel_key: str):
 Q4_ROWS = Q4_COLS = 4096
 Q4_W_BYTES = Q4_ROWS * (Q4_COLS // 32) * 18
 Q4_ALG_BYTES = Q4_W_BYTES + Q4_COLS * 4 + Q4_ROWS * 4   # weights once + x in + y out
-Q4_COPIES = 16                                           # 16 x 9.4 MB = 151 MB > L2
+Q4_COPIES = 32                                           # 32 x 9.47 MB = 303 MB, 2.4x the L2
 
 
 def q4_inputs(seed=1234):
@@ -267,8 +267,8 @@ def main():
         args.warmup = 3
     world, rank, local = dist_setup()
     metric, unit = "Q4_0 GEMV achieved HBM GB/s (config 0, 4096x4096)", "GB/s"
-    config = {"workload": "config0: Q4_0xQ8 GEMV 4096x4096, x~N(0,1), 16 rotated weight copies (151 MB > 126 MB L2)",
-              "rows": Q4_ROWS, "cols": Q4_COLS, "l2": "inputs rotated across 16 weight copies larger than L2",
+    config = {"workload": "config0: Q4_0xQ8 GEMV 4096x4096, x~N(0,1), 32 rotated weight copies (303 MB > 126 MB L2)",
+              "rows": Q4_ROWS, "cols": Q4_COLS, "l2": "inputs rotated across 32 weight copies (303 MB, 2.4x L2)",
               "parallelism": f"replicas x{world}"}
 
     if args.impl == "reference":

@@ -56,6 +56,51 @@ cudaStream_t host_stream() {
     return s;
 }
 
+// Device buffers reused by the host-pointer calls of one thread (grown on
+// demand, never shrunk), so a tensor_matvec-style call costs two copies and a
+// launch rather than two allocations as well.
+struct HostCallBuffers {
+    void* x = nullptr;
+    void* y = nullptr;
+    size_t nx = 0, ny = 0;
+    ~HostCallBuffers() {
+        if (x) cudaFree(x);
+        if (y) cudaFree(y);
+    }
+    cudaError_t reserve(size_t bx, size_t by) {
+        if (bx > nx) {
+            if (x) cudaFree(x);
+            x = nullptr;
+            nx = 0;
+            if (cudaError_t e = cudaMalloc(&x, bx)) return e;
+            nx = bx;
+        }
+        if (by > ny) {
+            if (y) cudaFree(y);
+            y = nullptr;
+            ny = 0;
+            if (cudaError_t e = cudaMalloc(&y, by)) return e;
+            ny = by;
+        }
+        return cudaSuccess;
+    }
+};
+HostCallBuffers& host_buffers() {
+    static thread_local HostCallBuffers b;
+    return b;
+}
+
+// Stream-ordered scratch (cudaMallocAsync) comes from the device's default
+// pool; keep freed blocks in the pool instead of returning them to the driver
+// at every synchronisation.
+void keep_pool_memory(int device) {
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+        uint64_t threshold = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+    }
+}
+
 int check_weight(const mv_weight_s* w) {
     if (!w) return fail(MV_ERR_INVALID, "null weight handle");
     return MV_OK;
@@ -163,6 +208,7 @@ MV_API int mv_init(int device) {
     if (major != 10)
         return fail(MV_ERR_UNSUPPORTED, "memvanta_b200 is built for sm_100a; device has compute capability " +
                                             std::to_string(major) + ".x");
+    keep_pool_memory(device);
     return MV_OK;
 }
 
@@ -350,20 +396,14 @@ MV_API int mv_tensor_matvec_host(mv_weight_t w, const float* x_host, float* y_ho
     if (int rc = check_weight(w)) return rc;
     if (!x_host || !y_host) return fail(MV_ERR_INVALID, "null x or y");
     cudaStream_t s = host_stream();
-    float *x = nullptr, *y = nullptr;
-    CK(cudaMallocAsync(reinterpret_cast<void**>(&x), w->cols * sizeof(float), s));
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&y), w->rows * sizeof(float), s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(x, x_host, w->cols * sizeof(float), cudaMemcpyHostToDevice, s);
-    int rc = MV_OK;
-    if (e == cudaSuccess) rc = mv_gemv(w, x, y, s);
-    if (e == cudaSuccess && rc == MV_OK)
-        e = cudaMemcpyAsync(y_host, y, w->rows * sizeof(float), cudaMemcpyDeviceToHost, s);
-    cudaFreeAsync(x, s);
-    if (y) cudaFreeAsync(y, s);
-    cudaError_t e2 = cudaStreamSynchronize(s);
-    if (rc) return rc;
-    if (e != cudaSuccess) return cuda_fail(e, "tensor_matvec_host");
-    if (e2 != cudaSuccess) return cuda_fail(e2, "tensor_matvec_host sync");
+    HostCallBuffers& hb = host_buffers();
+    CK(hb.reserve(w->cols * sizeof(float), w->rows * sizeof(float)));
+    float* x = static_cast<float*>(hb.x);
+    float* y = static_cast<float*>(hb.y);
+    CK(cudaMemcpyAsync(x, x_host, w->cols * sizeof(float), cudaMemcpyHostToDevice, s));
+    if (int rc = mv_gemv(w, x, y, s)) return rc;
+    CK(cudaMemcpyAsync(y_host, y, w->rows * sizeof(float), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
     return MV_OK;
 }
 
@@ -373,20 +413,14 @@ MV_API int mv_tensor_matmul_batch_host(mv_weight_t w, const float* x_host, float
     if (batch == 0) return MV_OK;
     if (!x_host || !y_host) return fail(MV_ERR_INVALID, "null x or y");
     cudaStream_t s = host_stream();
-    float *x = nullptr, *y = nullptr;
-    CK(cudaMallocAsync(reinterpret_cast<void**>(&x), batch * w->cols * sizeof(float), s));
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&y), batch * w->rows * sizeof(float), s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(x, x_host, batch * w->cols * sizeof(float), cudaMemcpyHostToDevice, s);
-    int rc = MV_OK;
-    if (e == cudaSuccess) rc = mv_gemm(w, x, batch, y, act_mode, s);
-    if (e == cudaSuccess && rc == MV_OK)
-        e = cudaMemcpyAsync(y_host, y, batch * w->rows * sizeof(float), cudaMemcpyDeviceToHost, s);
-    cudaFreeAsync(x, s);
-    if (y) cudaFreeAsync(y, s);
-    cudaError_t e2 = cudaStreamSynchronize(s);
-    if (rc) return rc;
-    if (e != cudaSuccess) return cuda_fail(e, "tensor_matmul_batch_host");
-    if (e2 != cudaSuccess) return cuda_fail(e2, "tensor_matmul_batch_host sync");
+    HostCallBuffers& hb = host_buffers();
+    CK(hb.reserve(batch * w->cols * sizeof(float), batch * w->rows * sizeof(float)));
+    float* x = static_cast<float*>(hb.x);
+    float* y = static_cast<float*>(hb.y);
+    CK(cudaMemcpyAsync(x, x_host, batch * w->cols * sizeof(float), cudaMemcpyHostToDevice, s));
+    if (int rc = mv_gemm(w, x, batch, y, act_mode, s)) return rc;
+    CK(cudaMemcpyAsync(y_host, y, batch * w->rows * sizeof(float), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
     return MV_OK;
 }
 
@@ -394,16 +428,11 @@ MV_API int mv_tensor_read_row_host(mv_weight_t w, uint64_t row, float* out_host)
     if (int rc = check_weight(w)) return rc;
     if (!out_host) return fail(MV_ERR_INVALID, "null output");
     cudaStream_t s = host_stream();
-    float* out = nullptr;
-    CK(cudaMallocAsync(reinterpret_cast<void**>(&out), w->cols * sizeof(float), s));
-    int rc = mv_read_row(w, row, out, s);
-    cudaError_t e = cudaSuccess;
-    if (rc == MV_OK) e = cudaMemcpyAsync(out_host, out, w->cols * sizeof(float), cudaMemcpyDeviceToHost, s);
-    cudaFreeAsync(out, s);
-    cudaError_t e2 = cudaStreamSynchronize(s);
-    if (rc) return rc;
-    if (e != cudaSuccess) return cuda_fail(e, "tensor_read_row_host");
-    if (e2 != cudaSuccess) return cuda_fail(e2, "tensor_read_row_host sync");
+    HostCallBuffers& hb = host_buffers();
+    CK(hb.reserve(sizeof(int32_t), w->cols * sizeof(float)));
+    if (int rc = mv_read_row(w, row, static_cast<float*>(hb.y), s)) return rc;
+    CK(cudaMemcpyAsync(out_host, hb.y, w->cols * sizeof(float), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
     return MV_OK;
 }
 

@@ -3,20 +3,26 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <mutex>
+#include <set>
+#include <utility>
 
 namespace mvb {
 
 constexpr int kWarp = 32;
 
-// Raises a kernel's dynamic shared-memory limit once per device.
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device).
 template <class Kernel>
 inline void ensure_smem_attr(Kernel* k, int bytes) {
-    static unsigned done = 0;  // bit per device id
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 32 && (done >> dev) & 1u) return;
+    const std::pair<const void*, int> key{reinterpret_cast<const void*>(k), dev};
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count(key)) return;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (dev < 32) done |= 1u << dev;
+    done.insert(key);
 }
 
 // ---------------------------------------------------------------- reductions

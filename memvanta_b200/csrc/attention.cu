@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(AttnArgs a,
     float qv[G][E];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        const float* qh = a.q + (size_t)s * a.n_head * hd + (size_t)(kh * G + g) * hd + lane * E;
+        const float* qh = a.q + (size_t)s * a.q_stride + (size_t)(kh * G + g) * hd + lane * E;
 #pragma unroll
         for (int i = 0; i < E; ++i) qv[g][i] = qh[i];
     }
@@ -283,7 +283,8 @@ static cudaError_t launch_attn_e(uint64_t hd, int G, dim3 grid, size_t smem, cud
     return cudaErrorInvalidValue;
 }
 
-static void split_plan(uint64_t n_seq, uint64_t n_head_kv, uint64_t max_ctx, int& split_len, int& n_split) {
+static void split_plan(uint64_t n_seq, uint64_t n_head_kv, uint64_t G, uint64_t hd, uint64_t max_ctx, int& split_len,
+                       int& n_split) {
     const uint64_t units = n_seq * n_head_kv;
     const uint64_t target = (uint64_t)num_sms() * 4;
     uint64_t ns = units >= target ? 1 : (target + units - 1) / units;
@@ -292,6 +293,9 @@ static void split_plan(uint64_t n_seq, uint64_t n_head_kv, uint64_t max_ctx, int
     uint64_t len = (max_ctx + ns - 1) / ns;
     len = (len + 15) / 16 * 16;
     if (len == 0) len = 16;
+    // the slice's scores and the per-warp partial outputs must fit in shared memory
+    const uint64_t cap = ((200 * 1024 / 4) - (uint64_t)kAttnWarps * G * hd) / G / 16 * 16;
+    if (len > cap) len = cap;
     split_len = (int)len;
     n_split = (int)((max_ctx + len - 1) / len);
     if (n_split < 1) n_split = 1;
@@ -299,16 +303,17 @@ static void split_plan(uint64_t n_seq, uint64_t n_head_kv, uint64_t max_ctx, int
 
 uint64_t attn_scratch_floats(uint64_t n_seq, uint64_t n_head, uint64_t hd, uint64_t max_ctx) {
     // upper bound over every plan split_plan can choose for this shape
+    // (slices are at least 16 tokens long)
     const uint64_t max_ns = max_ctx / 16 + 1;
     return n_seq * n_head * max_ns * (hd + 2);
 }
 
 cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s) {
     if (!a.n_seq) return cudaSuccess;
-    int split_len, n_split;
-    split_plan(a.n_seq, a.n_head_kv, a.max_ctx ? a.max_ctx : 1, split_len, n_split);
     const int G = (int)(a.n_head / a.n_head_kv);
     if (G > kAttnMaxG || a.n_head % a.n_head_kv) return cudaErrorInvalidValue;
+    int split_len, n_split;
+    split_plan(a.n_seq, a.n_head_kv, (uint64_t)G, a.hd, a.max_ctx ? a.max_ctx : 1, split_len, n_split);
     const size_t smem = ((size_t)G * split_len + (size_t)kAttnWarps * G * a.hd) * sizeof(float);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     dim3 grid((unsigned)a.n_seq, (unsigned)a.n_head_kv, (unsigned)n_split);

@@ -193,6 +193,10 @@ int upload_common(const void* src, bool src_on_device, uint64_t nbytes, int type
 
 }  // namespace
 
+namespace mvb {
+void set_last_error(const std::string& msg) { g_err = msg; }
+}  // namespace mvb
+
 extern "C" {
 
 MV_API const char* mv_last_error(void) { return g_err.c_str(); }
@@ -383,7 +387,8 @@ MV_API int mv_paged_attn_decode(int kv_type, const float* q, uint64_t n_seq, uin
     float* scratch = nullptr;
     const uint64_t nf = mvb::attn_scratch_floats(n_seq, n_head, hd, max_ctx ? max_ctx : 1);
     CK(cudaMallocAsync(reinterpret_cast<void**>(&scratch), nf * sizeof(float), s));
-    mvb::AttnArgs a{kv_type, q, n_seq, n_head, n_head_kv, hd, k_pages, v_pages, k_scales, v_scales, block_table,
+    mvb::AttnArgs a{kv_type, q, n_head * hd, n_seq, n_head, n_head_kv, hd, k_pages, v_pages, k_scales, v_scales,
+                    block_table,
                     max_pages, page, ctx_len, max_ctx ? max_ctx : 1, out, scratch};
     cudaError_t e = mvb::paged_attn_decode(a, s);
     cudaFreeAsync(scratch, s);

@@ -20,7 +20,7 @@ __global__ void __launch_bounds__(kGWarps * 32) gemm_q4_q8_kernel(const uint4* _
                                                                   const unsigned short* __restrict__ dsc, int rows,
                                                                   int nb, const int8_t* __restrict__ q,
                                                                   const float* __restrict__ d, int batch,
-                                                                  float* __restrict__ y) {
+                                                                  float* __restrict__ y, int accumulate) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     int4* lo = reinterpret_cast<int4*>(smem_raw);           // [T][nb]
     int4* hi = lo + kGTok * nb;                              // [T][nb]
@@ -81,13 +81,16 @@ __global__ void __launch_bounds__(kGWarps * 32) gemm_q4_q8_kernel(const uint4* _
 #pragma unroll
         for (int t = 0; t < kGTok; ++t) {
             const float v = warp_sum(acc[t]);
-            if (lane == 0 && t < nt) y[(size_t)(t0 + t) * rows + r] = v;
+            if (lane == 0 && t < nt) {
+                float* dst = y + (size_t)(t0 + t) * rows + r;
+                *dst = accumulate ? *dst + v : v;
+            }
         }
     }
 }
 
 cudaError_t gemm_q4_q8(const mv_weight_s& w, const int8_t* q, const float* d, uint64_t batch, float* y,
-                       cudaStream_t s) {
+                       cudaStream_t s, bool accumulate) {
     if (!batch) return cudaSuccess;
     const size_t smem = (size_t)kGTok * w.nb * (16 + 16 + 4 + 4);
     ensure_smem_attr(gemm_q4_q8_kernel, 220 * 1024);
@@ -95,7 +98,7 @@ cudaError_t gemm_q4_q8(const mv_weight_s& w, const int8_t* q, const float* d, ui
     const uint64_t cap = (uint64_t)num_sms() * 2;
     dim3 grid((unsigned)(ctas < cap ? ctas : cap), (unsigned)((batch + kGTok - 1) / kGTok));
     gemm_q4_q8_kernel<<<grid, kGWarps * 32, smem, s>>>(reinterpret_cast<const uint4*>(w.qs), w.d, (int)w.rows,
-                                                       (int)w.nb, q, d, (int)batch, y);
+                                                       (int)w.nb, q, d, (int)batch, y, accumulate ? 1 : 0);
     return cudaGetLastError();
 }
 

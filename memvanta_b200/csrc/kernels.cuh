@@ -6,9 +6,12 @@
 #include <cstdint>
 #include "weights.cuh"
 
+#include <string>
+
 namespace mvb {
 
 int num_sms();
+void set_last_error(const std::string& msg);  // capi.cu: the message mv_last_error() returns
 
 // ---- weights.cu
 cudaError_t repack_from_ggml(mv_weight_s& w, const uint8_t* raw_dev, cudaStream_t s);
@@ -43,8 +46,9 @@ cudaError_t matmul_f32act(const mv_weight_s& w, const float* x, uint64_t batch, 
 
 // ---- gemm.cu : batched Q4_0 x Q8 activations (prefill)
 // q/d: activations already quantised per row (quantize_q8_rows).
+// accumulate: y += result (residual stream) instead of y = result.
 cudaError_t gemm_q4_q8(const mv_weight_s& w, const int8_t* q, const float* d, uint64_t batch, float* y,
-                       cudaStream_t s);
+                       cudaStream_t s, bool accumulate = false);
 
 // ---- ops.cu
 cudaError_t rmsnorm_rows(const float* x, const float* w, uint64_t rows, uint64_t n, float eps, float* out,
@@ -65,7 +69,8 @@ cudaError_t kv_append(int kv_type, const float* k, const float* v, uint64_t rows
                       cudaStream_t s);
 struct AttnArgs {
     int kv_type;
-    const float* q;
+    const float* q;          // query row s at q + s * q_stride
+    uint64_t q_stride;
     uint64_t n_seq, n_head, n_head_kv, hd;
     const void* k_pages;
     const void* v_pages;

@@ -1,19 +1,763 @@
-// model.cu -- device-resident LlamaModel backend (placeholder until the
-// model lands; every entry point reports MV_ERR_NOT_BUILT).
+// model.cu -- device-resident LlamaModel backend (mv_model_*).
+//
+// Mirrors the reference's LlamaModel (src/llama_model.cpp:222-263,
+// include/memvanta/llama_model.hpp:100-138) with the weights, KV cache and
+// activations resident in HBM:
+//
+//  * load: the GGUF is mmapped (gguf_loader.cpp); every tensor's blocks are
+//    uploaded once.  Per layer, q|k|v are concatenated into one weight (rows
+//    q, then k, then v) and gate/up are interleaved row by row (gate_i, up_i),
+//    so one GEMV launch serves three (two) of the reference's tensor_matvec
+//    calls.  The RoPE tables are built on the host with the reference's own
+//    float expressions (:233) and uploaded.
+//  * decode (forward): one CUDA graph per step --
+//      embed(token) ; per layer { qkv GEMV with RMSNorm+Q8 prologue ;
+//      RoPE + KV append ; split-K paged attention ; o GEMV (+= x) ;
+//      gate/up GEMV with RMSNorm+Q8 prologue and SiLU-gate epilogue ;
+//      down GEMV (+= x) } ; output RMSNorm ; head matvec ; greedy argmax.
+//    The token id and position live in device memory, so the same graph
+//    replays for every position and greedy decoding never leaves the GPU.
+//  * prefill: per chunk of B tokens the reference's MEMVANTA_FORCE_Q8_ACT=1
+//    numerics -- RMSNorm, per-row Q8 activations, Q4_0 x Q8 GEMM, RoPE + KV
+//    append, causal attention (token b sees positions <= start+b), SiLU gate,
+//    residuals; a 1-token chunk takes the reference's fp32-activation path
+//    (tensor_matmul_batch_v06 routes batch < 2 to tensor_matmul_batch, :263).
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
 #include "../../include/memvanta_b200.h"
+#include "common.cuh"
+#include "gguf_loader.hpp"
+#include "kernels.cuh"
+#include "weights.cuh"
+
+namespace mvb {
+
+// ------------------------------------------------------------- kernels
+
+// RoPE (half-split, the reference's GCC roundings) on the q and k parts of
+// one qkv row, then the k and v parts into the paged cache.  One CTA per row.
+// ctx_out (optional) receives pos+1 for the attention that follows.
+__global__ void rope_append_kernel(float* __restrict__ qkv, int ld, int n_head, int n_head_kv, int hd,
+                                   const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                   const int32_t* __restrict__ pos, int kv_type, const int32_t* __restrict__ table,
+                                   int page, uint8_t* __restrict__ k_pages, uint8_t* __restrict__ v_pages,
+                                   float* __restrict__ k_scales, float* __restrict__ v_scales,
+                                   int32_t* __restrict__ ctx_out) {
+    const int r = blockIdx.x, half = hd / 2, D = n_head * hd, KV = n_head_kv * hd;
+    float* row = qkv + (size_t)r * ld;
+    const int p = pos[r];
+    const float* co = cos_t + (size_t)p * half;
+    const float* si = sin_t + (size_t)p * half;
+    for (int i = threadIdx.x; i < (n_head + n_head_kv) * half; i += blockDim.x) {
+        const int h = i / half, j = i % half;
+        float* b = row + h * hd;  // k heads directly follow the q heads in the row
+        const float x0 = b[j], x1 = b[j + half], c = co[j], s = si[j];
+        b[j] = __fmaf_rn(x0, c, -__fmul_rn(x1, s));
+        b[j + half] = __fmaf_rn(x0, s, __fmul_rn(x1, c));
+    }
+    __syncthreads();
+    const size_t slot = (size_t)table[p / page] * page + p % page;
+    for (int which = 0; which < 2; ++which) {
+        const float* src = row + D + which * KV;
+        uint8_t* pages = which ? v_pages : k_pages;
+        float* scales = which ? v_scales : k_scales;
+        if (kv_type == 0) {
+            float* dst = reinterpret_cast<float*>(pages) + slot * KV;
+            for (int i = threadIdx.x; i < KV; i += blockDim.x) dst[i] = src[i];
+        } else if (kv_type == 1) {
+            uint16_t* dst = reinterpret_cast<uint16_t*>(pages) + slot * KV;
+            for (int i = threadIdx.x; i < KV; i += blockDim.x) dst[i] = f32_to_f16_ref(src[i]);
+        } else if (kv_type == 2) {
+            __shared__ float red[32];
+            float m = 0.0f;
+            for (int i = threadIdx.x; i < KV; i += blockDim.x) m = fmaxf(m, fabsf(src[i]));
+            m = warp_max(m);
+            const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+            if (lane == 0) red[warp] = m;
+            __syncthreads();
+            if (warp == 0) {
+                float t = lane < nw ? red[lane] : 0.0f;
+                t = warp_max(t);
+                if (lane == 0) red[0] = t;
+            }
+            __syncthreads();
+            const float sc = red[0] > 0.0f ? red[0] / 127.0f : 1.0f;
+            int8_t* dst = reinterpret_cast<int8_t*>(pages) + slot * KV;
+            for (int i = threadIdx.x; i < KV; i += blockDim.x) {
+                float q = roundf(src[i] / sc);
+                dst[i] = (int8_t)(int)fminf(fmaxf(q, -127.0f), 127.0f);
+            }
+            if (threadIdx.x == 0) scales[slot] = sc;
+            __syncthreads();  // red[] is reused by the V pass
+        } else {
+            int8_t* dst = reinterpret_cast<int8_t*>(pages) + slot * KV;
+            const int lane = threadIdx.x & 31;
+            for (int b = threadIdx.x >> 5; b < KV / 32; b += blockDim.x >> 5) {
+                float dd;
+                dst[b * 32 + lane] = (int8_t)quant_q8_lane(src[b * 32 + lane], dd);
+                if (lane == 0) scales[slot * (KV / 32) + b] = dd;
+            }
+        }
+    }
+    if (ctx_out && threadIdx.x == 0) ctx_out[r] = p + 1;
+}
+
+// Prefill: gate/up rows come interleaved (g_i, u_i); ff = g/(1+exp(-g)) * u.
+__global__ void silu_pairs_kernel(const float* __restrict__ gu, float* __restrict__ ff, uint64_t n) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const float g = gu[2 * i], u = gu[2 * i + 1];
+        ff[i] = (g / (1.0f + expf(-g))) * u;
+    }
+}
+
+// Greedy step tail: argmax (first index of the max, as std::max_element in
+// Sampler::sample, src/llama_model.cpp:60) -> next token, token history at
+// the current position, position + 1.
+__global__ void greedy_step_kernel(const float* __restrict__ logits, int n, int32_t* __restrict__ token,
+                                   int32_t* __restrict__ pos, int32_t* __restrict__ history) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float v = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float x = logits[i];
+        if (x > v || (x == v && i < idx)) {
+            v = x;
+            idx = i;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (v2 > v || (v2 == v && i2 < idx)) {
+            v = v2;
+            idx = i2;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) {
+        sv[warp] = v;
+        si[warp] = idx;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < nw ? sv[lane] : -INFINITY;
+        idx = lane < nw ? si[lane] : 0x7fffffff;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+            const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+            if (v2 > v || (v2 == v && i2 < idx)) {
+                v = v2;
+                idx = i2;
+            }
+        }
+        if (lane == 0) {
+            const int t = idx == 0x7fffffff ? 0 : idx;
+            const int p = *pos;
+            *token = t;
+            history[p] = t;
+            *pos = p + 1;
+        }
+    }
+}
+
+// Decode without logits still advances the device position.
+__global__ void advance_pos_kernel(int32_t* __restrict__ pos) { *pos += 1; }
+
+unsigned ew_grid(uint64_t n) {
+    const uint64_t g = (n + 255) / 256, cap = (uint64_t)num_sms() * 8;
+    return (unsigned)(g < cap ? (g ? g : 1) : cap);
+}
+
+// --------------------------------------------------------------- model
+
+struct DevBuf {
+    void* p = nullptr;
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+    template <class T>
+    T* as() const { return static_cast<T*>(p); }
+};
+
+struct Layer {
+    mv_weight_s* qkv = nullptr;
+    mv_weight_s* o = nullptr;
+    mv_weight_s* gu = nullptr;
+    mv_weight_s* down = nullptr;
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    uint8_t* k_pages = nullptr;
+    uint8_t* v_pages = nullptr;
+    float* k_scales = nullptr;
+    float* v_scales = nullptr;
+};
+
+}  // namespace mvb
+
+struct mv_model_s {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    // config (LlamaConfig, include/memvanta/llama_model.hpp:14-26)
+    uint64_t n_ctx = 0, n_embd = 0, n_ff = 0, n_layer = 0, n_head = 0, n_head_kv = 0, vocab = 0;
+    float eps = 1e-5f, theta = 10000.0f;
+    uint64_t hd = 0, kv_dim = 0, page = 128, n_pages = 0;
+    int kv_type = MV_KV_F16;
+    uint64_t pos = 0;
+
+    std::vector<mv_weight_s*> owned;  // every uploaded weight
+    mv_weight_s* tok_embd = nullptr;
+    mv_weight_s* output = nullptr;
+    float* output_norm = nullptr;
+    std::vector<mvb::Layer> layers;
+
+    std::vector<void*> allocs;             // every other device allocation
+    float* rope_cos = nullptr;
+    float* rope_sin = nullptr;
+    int32_t* table = nullptr;              // [max_q][n_pages] identity rows
+    uint64_t table_rows = 0;
+
+    // decode state (device)
+    float *x = nullptr, *qkv = nullptr, *att = nullptr, *ff = nullptr, *gu = nullptr, *nrm = nullptr;
+    float* logits = nullptr;
+    float* attn_scratch = nullptr;
+    uint64_t attn_scratch_n = 0;
+    int32_t *token_dev = nullptr, *pos_dev = nullptr, *ctx_dev = nullptr, *history = nullptr;
+    int32_t* host_io = nullptr;            // pinned: [token, pos]
+    float* logits_host = nullptr;          // pinned
+    cudaGraphExec_t graph_logits = nullptr, graph_nologits = nullptr;
+
+    // prefill buffers (grown on demand)
+    uint64_t pf_cap = 0;
+    float *X = nullptr, *N = nullptr, *QKV = nullptr, *ATT = nullptr, *GU = nullptr, *FF = nullptr, *PROJ = nullptr;
+    int8_t* XQ = nullptr;
+    float* XD = nullptr;
+    int32_t *pf_tok = nullptr, *pf_pos = nullptr, *pf_ctx = nullptr;
+    int32_t* pf_host = nullptr;            // pinned staging for tokens/pos/ctx
+};
+
+namespace {
+
+thread_local std::string g_model_err;
+
+struct ModelError : std::runtime_error {
+    int code;
+    ModelError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+void ck(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        throw ModelError(e == cudaErrorMemoryAllocation ? MV_ERR_OOM : MV_ERR_CUDA,
+                         std::string(what) + ": " + cudaGetErrorString(e));
+    }
+}
+
+template <class T>
+T* dalloc(mv_model_s* m, uint64_t count) {
+    void* p = nullptr;
+    ck(cudaMalloc(&p, count * sizeof(T) + 16), "cudaMalloc(model)");
+    m->allocs.push_back(p);
+    return static_cast<T*>(p);
+}
+
+mv_weight_s* upload_raw(mv_model_s* m, const uint8_t* raw, uint64_t nbytes, int type, uint64_t rows,
+                             uint64_t cols) {
+    mv_weight_t w = nullptr;
+    if (int rc = mv_weight_upload(raw, nbytes, type, rows, cols, m->stream, &w))
+        throw ModelError(rc, std::string("weight upload: ") + mv_last_error());
+    m->owned.push_back(w);
+    return w;
+}
+
+mv_weight_s* upload_tensor(mv_model_s* m, const mvb::GgufReader& f, const mvb::GgufTensorInfo& t) {
+    if (t.dims.size() < 2) throw ModelError(MV_ERR_INVALID, "matrix tensor needs rank 2: " + t.name);
+    return upload_raw(m, f.data(t), t.nbytes, (int)t.type, t.ne(1), t.ne(0));
+}
+
+float* upload_vector(mv_model_s* m, const mvb::GgufReader& f, const mvb::GgufTensorInfo& t, uint64_t n) {
+    // tensor_vector_to_f32 (src/gguf_kernels.cpp:224): F32 copied, F16 widened
+    if (t.elements() != n) throw ModelError(MV_ERR_INVALID, "tensor vector size mismatch: " + t.name);
+    std::vector<float> v(n);
+    if (t.type == 0) {
+        std::memcpy(v.data(), f.data(t), n * 4);
+    } else if (t.type == 1) {
+        const uint16_t* h = reinterpret_cast<const uint16_t*>(f.data(t));
+        for (uint64_t i = 0; i < n; ++i) {
+            const uint32_t s = (h[i] >> 15) & 1u, e = (h[i] >> 10) & 31u, mm = h[i] & 1023u;
+            float val;
+            if (e == 0) val = std::ldexp((float)mm, -24);
+            else if (e == 31) val = mm ? NAN : INFINITY;
+            else val = std::ldexp((float)(mm | 1024u), (int)e - 25);
+            v[i] = s ? -val : val;
+        }
+    } else {
+        throw ModelError(MV_ERR_UNSUPPORTED, "unsupported vector tensor type: " + t.name);
+    }
+    float* d = dalloc<float>(m, n);
+    ck(cudaMemcpy(d, v.data(), n * 4, cudaMemcpyHostToDevice), "upload vector");
+    return d;
+}
+
+// Concatenates whole rows of same-typed, same-width tensors (raw GGML bytes).
+mv_weight_s* upload_concat(mv_model_s* m, const mvb::GgufReader& f,
+                                const std::vector<const mvb::GgufTensorInfo*>& ts, bool interleave) {
+    const uint32_t type = ts[0]->type;
+    const uint64_t cols = ts[0]->ne(0);
+    for (auto* t : ts)
+        if (t->type != type || t->ne(0) != cols || t->dims.size() < 2)
+            throw ModelError(MV_ERR_UNSUPPORTED, "layer tensors to fuse differ in type or width: " + t->name);
+    const uint64_t row_bytes = ts[0]->nbytes / ts[0]->ne(1);
+    uint64_t rows = 0;
+    for (auto* t : ts) rows += t->ne(1);
+    std::vector<uint8_t> buf(rows * row_bytes);
+    if (interleave) {  // gate/up: row 2i = gate_i, row 2i+1 = up_i
+        if (ts.size() != 2 || ts[0]->ne(1) != ts[1]->ne(1))
+            throw ModelError(MV_ERR_INVALID, "gate/up shapes differ: " + ts[0]->name);
+        const uint8_t* g = f.data(*ts[0]);
+        const uint8_t* u = f.data(*ts[1]);
+        for (uint64_t i = 0; i < ts[0]->ne(1); ++i) {
+            std::memcpy(buf.data() + (2 * i) * row_bytes, g + i * row_bytes, row_bytes);
+            std::memcpy(buf.data() + (2 * i + 1) * row_bytes, u + i * row_bytes, row_bytes);
+        }
+    } else {
+        uint64_t off = 0;
+        for (auto* t : ts) {
+            std::memcpy(buf.data() + off, f.data(*t), t->nbytes);
+            off += t->nbytes;
+        }
+    }
+    return upload_raw(m, buf.data(), buf.size(), (int)type, rows, cols);
+}
+
+void ensure_prefill(mv_model_s* m, uint64_t B) {
+    if (B <= m->pf_cap) return;
+    const uint64_t D = m->n_embd, F = m->n_ff, QKVW = D + 2 * m->kv_dim;
+    const uint64_t K = std::max(D, F);
+    m->X = dalloc<float>(m, B * D);
+    m->N = dalloc<float>(m, B * D);
+    m->QKV = dalloc<float>(m, B * QKVW);
+    m->ATT = dalloc<float>(m, B * D);
+    m->GU = dalloc<float>(m, B * 2 * F);
+    m->FF = dalloc<float>(m, B * F);
+    m->PROJ = dalloc<float>(m, B * D);
+    m->XQ = dalloc<int8_t>(m, B * K);
+    m->XD = dalloc<float>(m, B * K / 32);
+    m->pf_tok = dalloc<int32_t>(m, B);
+    m->pf_pos = dalloc<int32_t>(m, B);
+    m->pf_ctx = dalloc<int32_t>(m, B);
+    if (m->pf_host) cudaFreeHost(m->pf_host);
+    ck(cudaMallocHost(reinterpret_cast<void**>(&m->pf_host), 3 * B * sizeof(int32_t)), "cudaMallocHost");
+    if (B > m->table_rows) {
+        std::vector<int32_t> t(B * m->n_pages);
+        for (uint64_t r = 0; r < B; ++r)
+            for (uint64_t p = 0; p < m->n_pages; ++p) t[r * m->n_pages + p] = (int32_t)p;
+        m->table = dalloc<int32_t>(m, t.size());
+        ck(cudaMemcpy(m->table, t.data(), t.size() * 4, cudaMemcpyHostToDevice), "table upload");
+        m->table_rows = B;
+    }
+    const uint64_t need = mvb::attn_scratch_floats(B, m->n_head, m->hd, m->n_ctx);
+    if (need > m->attn_scratch_n) {
+        m->attn_scratch = dalloc<float>(m, need);
+        m->attn_scratch_n = need;
+    }
+    m->pf_cap = B;
+}
+
+// x_out = W x_in for one weight of any type, with the decode path's fused
+// prologue/epilogue where the weight is Q4_0.
+void project_decode(mv_model_s* m, mv_weight_s* w, const float* x, const float* norm_w, float* y, mvb::Q4Epi epi) {
+    cudaStream_t s = m->stream;
+    if (w->type == 2) {
+        mvb::GemvQ4Args a{w, x, norm_w, m->eps, y, norm_w ? mvb::Q4Pro::RmsNorm : mvb::Q4Pro::Plain, epi};
+        ck(mvb::gemv_q4(a, s), "gemv_q4");
+        return;
+    }
+    const float* in = x;
+    if (norm_w) {
+        ck(mvb::rmsnorm_rows(x, norm_w, 1, w->cols, m->eps, m->nrm, s), "rmsnorm");
+        in = m->nrm;
+    }
+    if (epi == mvb::Q4Epi::Store) {
+        ck(mvb::matmul_f32act(*w, in, 1, y, s), "matmul");
+    } else if (epi == mvb::Q4Epi::AddTo) {
+        ck(mvb::matmul_f32act(*w, in, 1, m->logits, s), "matmul");  // logits buffer as scratch
+        ck(mvb::add_inplace(y, m->logits, w->rows, s), "add");
+    } else {
+        ck(mvb::matmul_f32act(*w, in, 1, m->gu, s), "matmul");
+        mvb::silu_pairs_kernel<<<mvb::ew_grid(w->rows / 2), 256, 0, s>>>(m->gu, y, w->rows / 2);
+        ck(cudaGetLastError(), "silu_pairs");
+    }
+}
+
+mvb::AttnArgs attn_args(mv_model_s* m, const mvb::Layer& L, const float* q, uint64_t q_stride, uint64_t n_q,
+                        const int32_t* ctx, uint64_t max_ctx, float* out) {
+    return mvb::AttnArgs{m->kv_type, q, q_stride, n_q, m->n_head, m->n_head_kv, m->hd, L.k_pages, L.v_pages,
+                         L.k_scales, L.v_scales, m->table, m->n_pages, m->page, ctx, max_ctx, out, m->attn_scratch};
+}
+
+// Every kernel of one decode step, in order, on m->stream.
+void launch_decode(mv_model_s* m, bool with_logits) {
+    cudaStream_t s = m->stream;
+    const uint64_t D = m->n_embd, QKVW = D + 2 * m->kv_dim;
+    ck(mvb::read_rows(*m->tok_embd, m->token_dev, 1, m->x, s), "embed");
+    for (auto& L : m->layers) {
+        project_decode(m, L.qkv, m->x, L.attn_norm, m->qkv, mvb::Q4Epi::Store);
+        mvb::rope_append_kernel<<<1, 256, 0, s>>>(m->qkv, (int)QKVW, (int)m->n_head, (int)m->n_head_kv, (int)m->hd,
+                                                  m->rope_cos, m->rope_sin, m->pos_dev, m->kv_type, m->table,
+                                                  (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales,
+                                                  m->ctx_dev);
+        ck(cudaGetLastError(), "rope_append");
+        ck(mvb::paged_attn_decode(attn_args(m, L, m->qkv, QKVW, 1, m->ctx_dev, m->n_ctx, m->att), s), "attention");
+        project_decode(m, L.o, m->att, nullptr, m->x, mvb::Q4Epi::AddTo);
+        project_decode(m, L.gu, m->x, L.ffn_norm, m->ff, mvb::Q4Epi::SiluGate);
+        project_decode(m, L.down, m->ff, nullptr, m->x, mvb::Q4Epi::AddTo);
+    }
+    if (with_logits) {
+        project_decode(m, m->output, m->x, m->output_norm, m->logits, mvb::Q4Epi::Store);
+        mvb::greedy_step_kernel<<<1, 1024, 0, s>>>(m->logits, (int)m->vocab, m->token_dev, m->pos_dev, m->history);
+        ck(cudaGetLastError(), "greedy_step");
+    } else {
+        mvb::advance_pos_kernel<<<1, 1, 0, s>>>(m->pos_dev);
+        ck(cudaGetLastError(), "advance_pos");
+    }
+}
+
+cudaGraphExec_t capture_decode(mv_model_s* m, bool with_logits) {
+    cudaGraph_t g = nullptr;
+    ck(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+        launch_decode(m, with_logits);
+    } catch (...) {
+        cudaStreamEndCapture(m->stream, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    ck(cudaStreamEndCapture(m->stream, &g), "end capture");
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    ck(e, "graph instantiate");
+    return exec;
+}
+
+void set_decode_inputs(mv_model_s* m, int32_t token) {
+    m->host_io[0] = token;
+    m->host_io[1] = (int32_t)m->pos;
+    ck(cudaMemcpyAsync(m->token_dev, &m->host_io[0], 4, cudaMemcpyHostToDevice, m->stream), "token H2D");
+    ck(cudaMemcpyAsync(m->pos_dev, &m->host_io[1], 4, cudaMemcpyHostToDevice, m->stream), "pos H2D");
+}
+
+void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, int kv_type) {
+    mvb::GgufReader f(path);
+    std::string arch;
+    f.get_string("general.architecture", arch);
+    if (arch != "llama")
+        throw ModelError(MV_ERR_UNSUPPORTED, "MemVanta real-model path currently supports GGUF architecture=llama, got: " + arch);
+    auto req = [&](const char* k) {
+        uint64_t v;
+        if (!f.get_u64(k, v)) throw ModelError(MV_ERR_IO, std::string("missing GGUF metadata: ") + k);
+        return v;
+    };
+    m->n_ctx = req("llama.context_length");
+    m->n_embd = req("llama.embedding_length");
+    m->n_ff = req("llama.feed_forward_length");
+    m->n_layer = req("llama.block_count");
+    m->n_head = req("llama.attention.head_count");
+    uint64_t kvh;
+    m->n_head_kv = f.get_u64("llama.attention.head_count_kv", kvh) ? kvh : m->n_head;
+    double dv;
+    m->eps = f.get_f64("llama.attention.layer_norm_rms_epsilon", dv) ? (float)dv : 1e-5f;
+    m->theta = f.get_f64("llama.rope.freq_base", dv) ? (float)dv : 10000.0f;
+    const auto& te = f.tensor("token_embd.weight");
+    m->vocab = te.ne(1);
+    if (te.ne(0) != m->n_embd) throw ModelError(MV_ERR_INVALID, "token embedding shape mismatch");
+    if (ctx) m->n_ctx = std::min(m->n_ctx, ctx);
+    if (m->n_embd % m->n_head || !m->n_head_kv || m->n_head % m->n_head_kv)
+        throw ModelError(MV_ERR_INVALID, "invalid Llama head configuration");
+    m->hd = m->n_embd / m->n_head;
+    m->kv_dim = m->n_head_kv * m->hd;
+    if (m->hd != 64 && m->hd != 128 && m->hd != 256)
+        throw ModelError(MV_ERR_UNSUPPORTED, "device attention supports head_dim 64, 128, 256");
+    if (m->n_head / m->n_head_kv > 8) throw ModelError(MV_ERR_UNSUPPORTED, "GQA group above 8");
+    if (kv_type < 0 || kv_type > 3) throw ModelError(MV_ERR_UNSUPPORTED, "unknown KV cache type");
+    if (kv_type == MV_KV_Q8_0 && m->kv_dim % 32) throw ModelError(MV_ERR_INVALID, "Q8_0 KV needs kv_dim % 32 == 0");
+    m->kv_type = kv_type;
+    m->page = page ? page : 128;
+    m->n_pages = (m->n_ctx + m->page - 1) / m->page;
+    f.advise_sequential();
+
+    m->tok_embd = upload_tensor(m, f, te);
+    const auto& on = f.tensor("output_norm.weight");
+    m->output_norm = upload_vector(m, f, on, m->n_embd);
+    const mvb::GgufTensorInfo* out = f.find("output.weight");
+    m->output = out ? upload_tensor(m, f, *out) : m->tok_embd;  // tied output (:226)
+
+    const uint64_t rows = m->n_pages * m->page;
+    const uint64_t rb = mvb::kv_row_bytes(kv_type, m->kv_dim), ns = mvb::kv_row_scales(kv_type, m->kv_dim);
+    m->layers.resize(m->n_layer);
+    for (uint64_t i = 0; i < m->n_layer; ++i) {
+        auto name = [&](const char* s) { return "blk." + std::to_string(i) + s; };
+        auto& L = m->layers[i];
+        L.attn_norm = upload_vector(m, f, f.tensor(name(".attn_norm.weight")), m->n_embd);
+        L.ffn_norm = upload_vector(m, f, f.tensor(name(".ffn_norm.weight")), m->n_embd);
+        L.qkv = upload_concat(m, f, {&f.tensor(name(".attn_q.weight")), &f.tensor(name(".attn_k.weight")),
+                                     &f.tensor(name(".attn_v.weight"))}, false);
+        if (L.qkv->rows != m->n_embd + 2 * m->kv_dim) throw ModelError(MV_ERR_INVALID, "q/k/v shape mismatch");
+        L.o = upload_tensor(m, f, f.tensor(name(".attn_output.weight")));
+        L.gu = upload_concat(m, f, {&f.tensor(name(".ffn_gate.weight")), &f.tensor(name(".ffn_up.weight"))}, true);
+        L.down = upload_tensor(m, f, f.tensor(name(".ffn_down.weight")));
+        L.k_pages = dalloc<uint8_t>(m, rows * rb);
+        L.v_pages = dalloc<uint8_t>(m, rows * rb);
+        L.k_scales = ns ? dalloc<float>(m, rows * ns) : nullptr;
+        L.v_scales = ns ? dalloc<float>(m, rows * ns) : nullptr;
+    }
+    // RoPE tables exactly as the reference builds them (src/llama_model.cpp:233)
+    const uint64_t half = m->hd / 2;
+    std::vector<float> co(m->n_ctx * half), si(m->n_ctx * half);
+    for (uint64_t p = 0; p < m->n_ctx; ++p)
+        for (uint64_t i = 0; i < half; ++i) {
+            const float inv = std::pow(m->theta, -2.0f * float(i) / float(m->hd));
+            const float a = float(p) * inv;
+            co[p * half + i] = std::cos(a);
+            si[p * half + i] = std::sin(a);
+        }
+    m->rope_cos = dalloc<float>(m, co.size());
+    m->rope_sin = dalloc<float>(m, si.size());
+    ck(cudaMemcpy(m->rope_cos, co.data(), co.size() * 4, cudaMemcpyHostToDevice), "rope cos");
+    ck(cudaMemcpy(m->rope_sin, si.data(), si.size() * 4, cudaMemcpyHostToDevice), "rope sin");
+
+    const uint64_t D = m->n_embd, F = m->n_ff;
+    m->x = dalloc<float>(m, D);
+    m->qkv = dalloc<float>(m, D + 2 * m->kv_dim);
+    m->att = dalloc<float>(m, D);
+    m->ff = dalloc<float>(m, F);
+    m->gu = dalloc<float>(m, 2 * F);
+    m->nrm = dalloc<float>(m, D);
+    m->logits = dalloc<float>(m, std::max(m->vocab, std::max(2 * F, D)));
+    m->token_dev = dalloc<int32_t>(m, 1);
+    m->pos_dev = dalloc<int32_t>(m, 1);
+    m->ctx_dev = dalloc<int32_t>(m, 1);
+    m->history = dalloc<int32_t>(m, m->n_ctx + 1);
+    ck(cudaMallocHost(reinterpret_cast<void**>(&m->host_io), 4 * sizeof(int32_t)), "cudaMallocHost");
+    ck(cudaMallocHost(reinterpret_cast<void**>(&m->logits_host), m->vocab * sizeof(float)), "cudaMallocHost");
+    ensure_prefill(m, 1);  // identity block table + attention scratch
+
+    // One eager step (pos 0, token 0) makes every kernel's attributes and the
+    // library's lazy state ready before the decode graphs are captured; the
+    // KV row it writes at position 0 is overwritten by the first real token.
+    m->pos = 0;
+    set_decode_inputs(m, 0);
+    launch_decode(m, true);
+    ck(cudaStreamSynchronize(m->stream), "warm-up step");
+    m->graph_logits = capture_decode(m, true);
+    m->graph_nologits = capture_decode(m, false);
+    m->pos = 0;
+}
+
+void free_model(mv_model_s* m) {
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->graph_logits) cudaGraphExecDestroy(m->graph_logits);
+    if (m->graph_nologits) cudaGraphExecDestroy(m->graph_nologits);
+    for (auto* w : m->owned) mv_weight_free(w);
+    for (void* p : m->allocs) cudaFree(p);
+    if (m->host_io) cudaFreeHost(m->host_io);
+    if (m->logits_host) cudaFreeHost(m->logits_host);
+    if (m->pf_host) cudaFreeHost(m->pf_host);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+template <class Fn>
+int guarded(Fn&& fn) {
+    try {
+        fn();
+        return MV_OK;
+    } catch (const ModelError& e) {
+        g_model_err = e.what();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_model_err = e.what();
+        return MV_ERR_IO;
+    }
+}
+
+int model_fail(int rc) {
+    mvb::set_last_error(g_model_err);  // surfaces through mv_last_error()
+    return rc;
+}
+
+void prefill_chunk(mv_model_s* m, const int32_t* tokens, uint64_t B, bool logits_last) {
+    cudaStream_t s = m->stream;
+    const uint64_t D = m->n_embd, F = m->n_ff, QKVW = D + 2 * m->kv_dim;
+    const uint64_t start = m->pos;
+    for (uint64_t b = 0; b < B; ++b) {
+        m->pf_host[b] = tokens[b];
+        m->pf_host[B + b] = (int32_t)(start + b);
+        m->pf_host[2 * B + b] = (int32_t)(start + b + 1);
+    }
+    ck(cudaMemcpyAsync(m->pf_tok, m->pf_host, B * 4, cudaMemcpyHostToDevice, s), "tokens H2D");
+    ck(cudaMemcpyAsync(m->pf_pos, m->pf_host + B, B * 4, cudaMemcpyHostToDevice, s), "pos H2D");
+    ck(cudaMemcpyAsync(m->pf_ctx, m->pf_host + 2 * B, B * 4, cudaMemcpyHostToDevice, s), "ctx H2D");
+    ck(mvb::read_rows(*m->tok_embd, m->pf_tok, B, m->X, s), "embed");
+    // Q8 activations when B >= 2 and the weight is Q4_0 (FORCE_Q8 path);
+    // fp32 activations otherwise, as tensor_matmul_batch_v06 dispatches.
+    auto project = [&](mv_weight_s* w, const float* in, uint64_t K, float* out, bool accumulate) {
+        if (B >= 2 && w->type == 2) {
+            ck(mvb::quantize_q8_rows(in, B, K, m->XQ, m->XD, s), "quantize");
+            ck(mvb::gemm_q4_q8(*w, m->XQ, m->XD, B, out, s, accumulate), "gemm");
+        } else if (accumulate) {
+            ck(mvb::matmul_f32act(*w, in, B, m->PROJ, s), "matmul");
+            ck(mvb::add_inplace(out, m->PROJ, B * w->rows, s), "add");
+        } else {
+            ck(mvb::matmul_f32act(*w, in, B, out, s), "matmul");
+        }
+    };
+    for (auto& L : m->layers) {
+        ck(mvb::rmsnorm_rows(m->X, L.attn_norm, B, D, m->eps, m->N, s), "rmsnorm");
+        project(L.qkv, m->N, D, m->QKV, false);
+        mvb::rope_append_kernel<<<(unsigned)B, 256, 0, s>>>(m->QKV, (int)QKVW, (int)m->n_head, (int)m->n_head_kv,
+                                                            (int)m->hd, m->rope_cos, m->rope_sin, m->pf_pos,
+                                                            m->kv_type, m->table, (int)m->page, L.k_pages, L.v_pages,
+                                                            L.k_scales, L.v_scales, nullptr);
+        ck(cudaGetLastError(), "rope_append");
+        ck(mvb::paged_attn_decode(attn_args(m, L, m->QKV, QKVW, B, m->pf_ctx, start + B, m->ATT), s), "attention");
+        project(L.o, m->ATT, D, m->X, true);
+        ck(mvb::rmsnorm_rows(m->X, L.ffn_norm, B, D, m->eps, m->N, s), "rmsnorm");
+        project(L.gu, m->N, D, m->GU, false);
+        mvb::silu_pairs_kernel<<<mvb::ew_grid(B * F), 256, 0, s>>>(m->GU, m->FF, B * F);
+        ck(cudaGetLastError(), "silu_pairs");
+        project(L.down, m->FF, F, m->X, true);
+    }
+    m->pos += B;
+    if (logits_last) {
+        const float* last = m->X + (B - 1) * D;
+        project_decode(m, m->output, last, m->output_norm, m->logits, mvb::Q4Epi::Store);
+    }
+}
+
+}  // namespace
 
 extern "C" {
-MV_API int mv_model_open(const char*, uint64_t, uint64_t, int, mv_model_t* out) {
-    if (out) *out = nullptr;
-    return MV_ERR_NOT_BUILT;
+
+MV_API int mv_model_open(const char* path, uint64_t ctx, uint64_t page_tokens, int kv_type, mv_model_t* out) {
+    if (!out || !path) return MV_ERR_INVALID;
+    *out = nullptr;
+    auto* m = new mv_model_s();
+    int rc = guarded([&] {
+        ck(cudaGetDevice(&m->device), "cudaGetDevice");
+        ck(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        load_model(m, path, ctx, page_tokens, kv_type);
+    });
+    if (rc) {
+        free_model(m);
+        return model_fail(rc);
+    }
+    *out = m;
+    return MV_OK;
 }
-MV_API int mv_model_close(mv_model_t) { return MV_OK; }
-MV_API int mv_model_config(mv_model_t, uint64_t*) { return MV_ERR_NOT_BUILT; }
-MV_API int mv_model_reset(mv_model_t) { return MV_ERR_NOT_BUILT; }
-MV_API uint64_t mv_model_position(mv_model_t) { return 0; }
-MV_API uint64_t mv_model_kv_bytes(mv_model_t) { return 0; }
-MV_API int mv_model_forward(mv_model_t, int32_t, int, float*) { return MV_ERR_NOT_BUILT; }
-MV_API int mv_model_prefill(mv_model_t, const int32_t*, uint64_t, uint64_t, int, float*) { return MV_ERR_NOT_BUILT; }
-MV_API int mv_model_generate_greedy(mv_model_t, int32_t, uint64_t, int32_t*) { return MV_ERR_NOT_BUILT; }
-MV_API void* mv_model_stream(mv_model_t) { return nullptr; }
+
+MV_API int mv_model_close(mv_model_t m) {
+    if (m) free_model(m);
+    return MV_OK;
 }
+
+MV_API int mv_model_config(mv_model_t m, uint64_t* o) {
+    if (!m || !o) return MV_ERR_INVALID;
+    o[0] = m->n_ctx;
+    o[1] = m->n_embd;
+    o[2] = m->n_ff;
+    o[3] = m->n_layer;
+    o[4] = m->n_head;
+    o[5] = m->n_head_kv;
+    o[6] = m->vocab;
+    return MV_OK;
+}
+
+MV_API int mv_model_reset(mv_model_t m) {
+    if (!m) return MV_ERR_INVALID;
+    m->pos = 0;
+    return MV_OK;
+}
+
+MV_API uint64_t mv_model_position(mv_model_t m) { return m ? m->pos : 0; }
+
+MV_API uint64_t mv_model_kv_bytes(mv_model_t m) {
+    // pages the current position has touched, as PagedKVCache allocates them
+    if (!m) return 0;
+    const uint64_t pages = (m->pos + m->page - 1) / m->page;
+    const uint64_t per_row = mvb::kv_row_bytes(m->kv_type, m->kv_dim) +
+                             4 * mvb::kv_row_scales(m->kv_type, m->kv_dim);
+    return 2 * m->n_layer * pages * m->page * per_row;
+}
+
+MV_API void* mv_model_stream(mv_model_t m) { return m ? m->stream : nullptr; }
+
+MV_API int mv_model_forward(mv_model_t m, int32_t token, int compute_logits, float* logits_host) {
+    if (!m) return MV_ERR_INVALID;
+    int rc = guarded([&] {
+        if (token < 0 || (uint64_t)token >= m->vocab) throw ModelError(MV_ERR_INVALID, "token id out of range");
+        if (m->pos >= m->n_ctx) throw ModelError(MV_ERR_INVALID, "context exhausted");
+        set_decode_inputs(m, token);
+        ck(cudaGraphLaunch(compute_logits ? m->graph_logits : m->graph_nologits, m->stream), "graph launch");
+        m->pos += 1;
+        if (compute_logits) {
+            ck(cudaMemcpyAsync(m->logits_host, m->logits, m->vocab * 4, cudaMemcpyDeviceToHost, m->stream), "logits D2H");
+            ck(cudaStreamSynchronize(m->stream), "sync");
+            if (logits_host) std::memcpy(logits_host, m->logits_host, m->vocab * 4);
+        }
+    });
+    return rc ? model_fail(rc) : MV_OK;
+}
+
+MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uint64_t batch, int compute_logits,
+                            float* logits_host) {
+    if (!m) return MV_ERR_INVALID;
+    if (n == 0) return MV_OK;
+    int rc = guarded([&] {
+        if (!tokens) throw ModelError(MV_ERR_INVALID, "null tokens");
+        if (m->pos + n > m->n_ctx) throw ModelError(MV_ERR_INVALID, "context exhausted");
+        for (uint64_t i = 0; i < n; ++i)
+            if (tokens[i] < 0 || (uint64_t)tokens[i] >= m->vocab) throw ModelError(MV_ERR_INVALID, "token id out of range");
+        const uint64_t B = std::max<uint64_t>(1, batch);
+        ensure_prefill(m, std::min(B, n));
+        for (uint64_t i = 0; i < n; i += B) {
+            const uint64_t nb = std::min(B, n - i);
+            prefill_chunk(m, tokens + i, nb, compute_logits && i + nb == n);
+        }
+        if (compute_logits) {
+            ck(cudaMemcpyAsync(m->logits_host, m->logits, m->vocab * 4, cudaMemcpyDeviceToHost, m->stream), "logits D2H");
+            ck(cudaStreamSynchronize(m->stream), "sync");
+            if (logits_host) std::memcpy(logits_host, m->logits_host, m->vocab * 4);
+        } else {
+            ck(cudaStreamSynchronize(m->stream), "sync");
+        }
+    });
+    return rc ? model_fail(rc) : MV_OK;
+}
+
+MV_API int mv_model_generate_greedy(mv_model_t m, int32_t token, uint64_t n, int32_t* out_tokens) {
+    if (!m) return MV_ERR_INVALID;
+    if (n == 0) return MV_OK;
+    int rc = guarded([&] {
+        if (!out_tokens) throw ModelError(MV_ERR_INVALID, "null output");
+        if (token < 0 || (uint64_t)token >= m->vocab) throw ModelError(MV_ERR_INVALID, "token id out of range");
+        if (m->pos + n > m->n_ctx) throw ModelError(MV_ERR_INVALID, "context exhausted");
+        const uint64_t start = m->pos;
+        set_decode_inputs(m, token);
+        for (uint64_t i = 0; i < n; ++i) ck(cudaGraphLaunch(m->graph_logits, m->stream), "graph launch");
+        ck(cudaMemcpyAsync(out_tokens, m->history + start, n * 4, cudaMemcpyDeviceToHost, m->stream), "tokens D2H");
+        ck(cudaStreamSynchronize(m->stream), "sync");
+        m->pos += n;
+    });
+    return rc ? model_fail(rc) : MV_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,146 @@
+"""End-to-end parity of the device LlamaModel with the reference's LlamaModel.
+
+Bar: logits within 2e-2 max-abs; the first 32
+greedy tokens identical.  Prefill is compared with the reference running
+MEMVANTA_FORCE_Q8_ACT=1 (the numerics of the int8 prefill GEMM); decode needs
+no switch (tensor_matvec always quantises Q4_0 activations).
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import tempfile
+
+import numpy as np
+import pytest
+
+import memvanta_b200 as mv
+from memvanta_b200 import gguf
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+TINY = gguf.LlamaShape(n_layer=2, n_embd=256, n_head=2, n_head_kv=1, n_ff=512, vocab=256, n_ctx=256,
+                       rms_eps=1e-6, rope_theta=10000.0)
+MID = gguf.LlamaShape(n_layer=4, n_embd=1024, n_head=8, n_head_kv=4, n_ff=2816, vocab=4096, n_ctx=512,
+                      rms_eps=1e-6, rope_theta=10000.0)
+
+
+@pytest.fixture(scope="module")
+def tmp():
+    with tempfile.TemporaryDirectory() as d:
+        yield d
+
+
+def sha256(path):
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for chunk in iter(lambda: f.read(1 << 20), b""):
+            h.update(chunk)
+    return h.hexdigest()
+
+
+def test_tiny_model_golden(cuda, golden, tmp):
+    g = golden("tiny_model.npz")
+    path = os.path.join(tmp, "tiny.gguf")
+    gguf.write_random_llama(path, TINY, seed=77)
+    assert sha256(path) == str(g["sha256"]), "fixture generator drifted"
+    m = mv.LlamaModel(path, ctx_override=128, kv_page_tokens=16, kv_type=mv.KV_F16)
+    logits = m.prefill(g["prompt"], batch_size=8).copy()
+    assert np.max(np.abs(logits - g["prefill_logits_q1"])) <= LOGIT_TOL
+    assert m.position() == len(g["prompt"])
+    cur = int(np.argmax(logits))
+    toks = []
+    for i in range(12):
+        l = m.forward(cur)
+        assert np.max(np.abs(l - g["decode_logits_q1"][i])) <= LOGIT_TOL, i
+        cur = int(np.argmax(l))
+        toks.append(cur)
+    assert toks == list(g["decode_tokens_q1"])
+    # device-side greedy decoding gives the same tokens
+    m.reset()
+    logits = m.prefill(g["prompt"], batch_size=8)
+    dev_toks = m.generate_greedy(int(np.argmax(logits)), 12)
+    assert list(dev_toks) == list(g["decode_tokens_q1"])
+    m.close()
+
+
+def _run_reference(reference, path, prompt, n_gen, batch, kv_type, ctx):
+    r = reference.model_open(path, threads=8, ctx=ctx, page=16, kv_type=kv_type)
+    try:
+        pl = reference.model_prefill(r, prompt, batch=batch, compute_logits=True, force_q8=True)
+        cur, toks, logits = int(np.argmax(pl)), [], []
+        for _ in range(n_gen):
+            l = reference.model_forward(r, cur, True)
+            logits.append(l)
+            cur = int(np.argmax(l))
+            toks.append(cur)
+        return pl, np.stack(logits), toks
+    finally:
+        reference.model_free(r)
+
+
+@pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_F32, mv.KV_Q8])
+def test_mid_model_vs_reference(cuda, reference, tmp, kv_type):
+    path = os.path.join(tmp, "mid.gguf")
+    if not os.path.exists(path):
+        gguf.write_random_llama(path, MID, seed=5)
+    rng = np.random.default_rng(8)
+    prompt = rng.integers(0, MID.vocab, size=57).astype(np.int32)
+    pl_ref, lg_ref, tok_ref = _run_reference(reference, path, prompt, 32, 16, kv_type, 256)
+    m = mv.LlamaModel(path, ctx_override=256, kv_page_tokens=16, kv_type=kv_type)
+    pl = m.prefill(prompt, batch_size=16).copy()
+    assert np.max(np.abs(pl - pl_ref)) <= LOGIT_TOL
+    cur, toks = int(np.argmax(pl)), []
+    for i in range(32):
+        l = m.forward(cur)
+        assert np.max(np.abs(l - lg_ref[i])) <= LOGIT_TOL, (i, float(np.max(np.abs(l - lg_ref[i]))))
+        cur = int(np.argmax(l))
+        toks.append(cur)
+    assert toks == tok_ref
+    m.close()
+
+
+def test_prefill_chunking_and_one_token_chunk(cuda, reference, tmp):
+    """Chunks of 7 leave a 1-token tail: the reference runs that chunk with
+    fp32 activations (batch < 2), and so does the device model."""
+    path = os.path.join(tmp, "mid.gguf")
+    if not os.path.exists(path):
+        gguf.write_random_llama(path, MID, seed=5)
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, MID.vocab, size=22).astype(np.int32)   # 7+7+7+1
+    r = reference.model_open(path, threads=8, ctx=256, page=16, kv_type=mv.KV_F16)
+    try:
+        want = reference.model_prefill(r, prompt, batch=7, compute_logits=True, force_q8=True)
+    finally:
+        reference.model_free(r)
+    m = mv.LlamaModel(path, ctx_override=256, kv_page_tokens=16, kv_type=mv.KV_F16)
+    got = m.prefill(prompt, batch_size=7)
+    assert np.max(np.abs(got - want)) <= LOGIT_TOL
+    m.close()
+
+
+def test_model_errors(cuda, tmp):
+    path = os.path.join(tmp, "tiny.gguf")
+    if not os.path.exists(path):
+        gguf.write_random_llama(path, TINY, seed=77)
+    m = mv.LlamaModel(path, ctx_override=8, kv_page_tokens=16)
+    with pytest.raises(mv.MemVantaError, match="token id out of range"):
+        m.forward(TINY.vocab)
+    with pytest.raises(mv.MemVantaError, match="context exhausted"):
+        m.prefill(list(range(9)), 4)
+    m.prefill(list(range(8)), 4)
+    with pytest.raises(mv.MemVantaError, match="context exhausted"):
+        m.forward(1)
+    m.reset()
+    assert m.position() == 0
+    m.forward(1)
+    assert m.position() == 1
+    m.close()
+    with pytest.raises(mv.MemVantaError):
+        mv.LlamaModel(os.path.join(tmp, "missing.gguf"))
+    bad = os.path.join(tmp, "bad.gguf")
+    with open(bad, "wb") as f:
+        f.write(b"GGUF" + bytes(20))
+    with pytest.raises(mv.MemVantaError):
+        mv.LlamaModel(bad)

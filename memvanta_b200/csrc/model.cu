@@ -171,6 +171,14 @@ __global__ void greedy_step_kernel(const float* __restrict__ logits, int n, int3
 // Decode without logits still advances the device position.
 __global__ void advance_pos_kernel(int32_t* __restrict__ pos) { *pos += 1; }
 
+// Token id and position of the next decode step, passed by value so no host
+// staging buffer has to outlive the launch.
+__global__ void set_inputs_kernel(int32_t* __restrict__ token_dev, int32_t* __restrict__ pos_dev, int32_t token,
+                                  int32_t pos) {
+    *token_dev = token;
+    *pos_dev = pos;
+}
+
 unsigned ew_grid(uint64_t n) {
     const uint64_t g = (n + 255) / 256, cap = (uint64_t)num_sms() * 8;
     return (unsigned)(g < cap ? (g ? g : 1) : cap);
@@ -230,7 +238,6 @@ struct mv_model_s {
     float* attn_scratch = nullptr;
     uint64_t attn_scratch_n = 0;
     int32_t *token_dev = nullptr, *pos_dev = nullptr, *ctx_dev = nullptr, *history = nullptr;
-    int32_t* host_io = nullptr;            // pinned: [token, pos]
     float* logits_host = nullptr;          // pinned
     cudaGraphExec_t graph_logits = nullptr, graph_nologits = nullptr;
 
@@ -239,8 +246,10 @@ struct mv_model_s {
     float *X = nullptr, *N = nullptr, *QKV = nullptr, *ATT = nullptr, *GU = nullptr, *FF = nullptr, *PROJ = nullptr;
     int8_t* XQ = nullptr;
     float* XD = nullptr;
+    // token ids / positions / context lengths of a whole prefill call
+    uint64_t in_cap = 0;
     int32_t *pf_tok = nullptr, *pf_pos = nullptr, *pf_ctx = nullptr;
-    int32_t* pf_host = nullptr;            // pinned staging for tokens/pos/ctx
+    int32_t* pf_host = nullptr;            // pinned staging, 3 * in_cap
 };
 
 namespace {
@@ -350,11 +359,6 @@ void ensure_prefill(mv_model_s* m, uint64_t B) {
     m->PROJ = dalloc<float>(m, B * D);
     m->XQ = dalloc<int8_t>(m, B * K);
     m->XD = dalloc<float>(m, B * K / 32);
-    m->pf_tok = dalloc<int32_t>(m, B);
-    m->pf_pos = dalloc<int32_t>(m, B);
-    m->pf_ctx = dalloc<int32_t>(m, B);
-    if (m->pf_host) cudaFreeHost(m->pf_host);
-    ck(cudaMallocHost(reinterpret_cast<void**>(&m->pf_host), 3 * B * sizeof(int32_t)), "cudaMallocHost");
     if (B > m->table_rows) {
         std::vector<int32_t> t(B * m->n_pages);
         for (uint64_t r = 0; r < B; ++r)
@@ -449,10 +453,31 @@ cudaGraphExec_t capture_decode(mv_model_s* m, bool with_logits) {
 }
 
 void set_decode_inputs(mv_model_s* m, int32_t token) {
-    m->host_io[0] = token;
-    m->host_io[1] = (int32_t)m->pos;
-    ck(cudaMemcpyAsync(m->token_dev, &m->host_io[0], 4, cudaMemcpyHostToDevice, m->stream), "token H2D");
-    ck(cudaMemcpyAsync(m->pos_dev, &m->host_io[1], 4, cudaMemcpyHostToDevice, m->stream), "pos H2D");
+    mvb::set_inputs_kernel<<<1, 1, 0, m->stream>>>(m->token_dev, m->pos_dev, token, (int32_t)m->pos);
+    ck(cudaGetLastError(), "set_inputs");
+}
+
+// Stages the token ids, positions and context lengths of a whole prefill
+// call with one copy each.  The caller has synchronised the stream, so the
+// pinned staging buffer is free to overwrite.
+void stage_prefill_inputs(mv_model_s* m, const int32_t* tokens, uint64_t n) {
+    if (n > m->in_cap) {
+        m->pf_tok = dalloc<int32_t>(m, n);
+        m->pf_pos = dalloc<int32_t>(m, n);
+        m->pf_ctx = dalloc<int32_t>(m, n);
+        if (m->pf_host) cudaFreeHost(m->pf_host);
+        m->pf_host = nullptr;
+        ck(cudaMallocHost(reinterpret_cast<void**>(&m->pf_host), 3 * n * sizeof(int32_t)), "cudaMallocHost");
+        m->in_cap = n;
+    }
+    for (uint64_t i = 0; i < n; ++i) {
+        m->pf_host[i] = tokens[i];
+        m->pf_host[n + i] = (int32_t)(m->pos + i);
+        m->pf_host[2 * n + i] = (int32_t)(m->pos + i + 1);
+    }
+    ck(cudaMemcpyAsync(m->pf_tok, m->pf_host, n * 4, cudaMemcpyHostToDevice, m->stream), "tokens H2D");
+    ck(cudaMemcpyAsync(m->pf_pos, m->pf_host + n, n * 4, cudaMemcpyHostToDevice, m->stream), "pos H2D");
+    ck(cudaMemcpyAsync(m->pf_ctx, m->pf_host + 2 * n, n * 4, cudaMemcpyHostToDevice, m->stream), "ctx H2D");
 }
 
 void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, int kv_type) {
@@ -546,7 +571,6 @@ void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, in
     m->pos_dev = dalloc<int32_t>(m, 1);
     m->ctx_dev = dalloc<int32_t>(m, 1);
     m->history = dalloc<int32_t>(m, m->n_ctx + 1);
-    ck(cudaMallocHost(reinterpret_cast<void**>(&m->host_io), 4 * sizeof(int32_t)), "cudaMallocHost");
     ck(cudaMallocHost(reinterpret_cast<void**>(&m->logits_host), m->vocab * sizeof(float)), "cudaMallocHost");
     ensure_prefill(m, 1);  // identity block table + attention scratch
 
@@ -568,7 +592,6 @@ void free_model(mv_model_s* m) {
     if (m->graph_nologits) cudaGraphExecDestroy(m->graph_nologits);
     for (auto* w : m->owned) mv_weight_free(w);
     for (void* p : m->allocs) cudaFree(p);
-    if (m->host_io) cudaFreeHost(m->host_io);
     if (m->logits_host) cudaFreeHost(m->logits_host);
     if (m->pf_host) cudaFreeHost(m->pf_host);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -594,19 +617,15 @@ int model_fail(int rc) {
     return rc;
 }
 
-void prefill_chunk(mv_model_s* m, const int32_t* tokens, uint64_t B, bool logits_last) {
+// One chunk of B tokens; `off` indexes the call's staged inputs.
+void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     cudaStream_t s = m->stream;
     const uint64_t D = m->n_embd, F = m->n_ff, QKVW = D + 2 * m->kv_dim;
     const uint64_t start = m->pos;
-    for (uint64_t b = 0; b < B; ++b) {
-        m->pf_host[b] = tokens[b];
-        m->pf_host[B + b] = (int32_t)(start + b);
-        m->pf_host[2 * B + b] = (int32_t)(start + b + 1);
-    }
-    ck(cudaMemcpyAsync(m->pf_tok, m->pf_host, B * 4, cudaMemcpyHostToDevice, s), "tokens H2D");
-    ck(cudaMemcpyAsync(m->pf_pos, m->pf_host + B, B * 4, cudaMemcpyHostToDevice, s), "pos H2D");
-    ck(cudaMemcpyAsync(m->pf_ctx, m->pf_host + 2 * B, B * 4, cudaMemcpyHostToDevice, s), "ctx H2D");
-    ck(mvb::read_rows(*m->tok_embd, m->pf_tok, B, m->X, s), "embed");
+    const int32_t* tok = m->pf_tok + off;
+    const int32_t* pos = m->pf_pos + off;
+    const int32_t* ctx = m->pf_ctx + off;
+    ck(mvb::read_rows(*m->tok_embd, tok, B, m->X, s), "embed");
     // Q8 activations when B >= 2 and the weight is Q4_0 (FORCE_Q8 path);
     // fp32 activations otherwise, as tensor_matmul_batch_v06 dispatches.
     auto project = [&](mv_weight_s* w, const float* in, uint64_t K, float* out, bool accumulate) {
@@ -624,11 +643,11 @@ void prefill_chunk(mv_model_s* m, const int32_t* tokens, uint64_t B, bool logits
         ck(mvb::rmsnorm_rows(m->X, L.attn_norm, B, D, m->eps, m->N, s), "rmsnorm");
         project(L.qkv, m->N, D, m->QKV, false);
         mvb::rope_append_kernel<<<(unsigned)B, 256, 0, s>>>(m->QKV, (int)QKVW, (int)m->n_head, (int)m->n_head_kv,
-                                                            (int)m->hd, m->rope_cos, m->rope_sin, m->pf_pos,
+                                                            (int)m->hd, m->rope_cos, m->rope_sin, pos,
                                                             m->kv_type, m->table, (int)m->page, L.k_pages, L.v_pages,
                                                             L.k_scales, L.v_scales, nullptr);
         ck(cudaGetLastError(), "rope_append");
-        ck(mvb::paged_attn_decode(attn_args(m, L, m->QKV, QKVW, B, m->pf_ctx, start + B, m->ATT), s), "attention");
+        ck(mvb::paged_attn_decode(attn_args(m, L, m->QKV, QKVW, B, ctx, start + B, m->ATT), s), "attention");
         project(L.o, m->ATT, D, m->X, true);
         ck(mvb::rmsnorm_rows(m->X, L.ffn_norm, B, D, m->eps, m->N, s), "rmsnorm");
         project(L.gu, m->N, D, m->GU, false);
@@ -727,10 +746,12 @@ MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uin
         for (uint64_t i = 0; i < n; ++i)
             if (tokens[i] < 0 || (uint64_t)tokens[i] >= m->vocab) throw ModelError(MV_ERR_INVALID, "token id out of range");
         const uint64_t B = std::max<uint64_t>(1, batch);
+        ck(cudaStreamSynchronize(m->stream), "sync");
         ensure_prefill(m, std::min(B, n));
+        stage_prefill_inputs(m, tokens, n);
         for (uint64_t i = 0; i < n; i += B) {
             const uint64_t nb = std::min(B, n - i);
-            prefill_chunk(m, tokens + i, nb, compute_logits && i + nb == n);
+            prefill_chunk(m, i, nb, compute_logits && i + nb == n);
         }
         if (compute_logits) {
             ck(cudaMemcpyAsync(m->logits_host, m->logits, m->vocab * 4, cudaMemcpyDeviceToHost, m->stream), "logits D2H");

@@ -186,22 +186,24 @@ def run_q4_gemv_ours(args, world, rank, local):
 
     launches = args.steps * Q4_COPIES
     g_warm, g_timed = capture(args.warmup * Q4_COPIES), capture(launches)
-    g_warm.replay()
-    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        t_end = time.perf_counter() + args.clock_window
-        while time.perf_counter() < t_end:
-            g_warm.replay()
-            torch.cuda.synchronize()
+    # graphs replay on the current stream: keep it the stream the events use
+    with torch.cuda.stream(stream):
+        g_warm.replay()
+        torch.cuda.synchronize()
         barrier(world)
         torch.cuda.synchronize()
-        e0.record(stream)
-        g_timed.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
+        with ClockSampler(local) as clk:
+            t_end = time.perf_counter() + args.clock_window
+            while time.perf_counter() < t_end:
+                g_warm.replay()
+                torch.cuda.synchronize()
+            barrier(world)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            g_timed.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     ms = all_max(ms, world)
     # correctness spot check of the timed path

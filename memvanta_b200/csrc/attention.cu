@@ -88,240 +88,174 @@ cudaError_t kv_append(int kv_type, const float* k, const float* v, uint64_t rows
 }
 
 // ------------------------------------------------------- decode attention
-// Grid (n_seq, n_head_kv, n_split).  A CTA owns one kv head of one sequence
-// and one contiguous slice of its context, and serves all G = n_head /
-// n_head_kv query heads that share that kv head.  Lane l owns head
-// dimensions [l*E, l*E+E) (E = hd/32), so every K or V row is one coalesced
-// warp-wide read.
+// One CTA per (query row, query head), hd threads.  The reference's own
+// evaluation order, so the output matches it bit for bit up to the host
+// libm's expf (here a correctly rounded exp):
 //
-//  1. scores s_t = (q . k_t) / sqrt(hd) for the slice's tokens (warps stride
-//     over tokens), kept in shared memory;
-//  2. per query head: m = max s_t, e_t = exp(s_t - m), l = sum e_t;
-//  3. o = sum_t e_t v_t (warps stride over tokens, then a cross-warp sum);
-//  4. (m, l, o) of the slice go to scratch; attn_merge combines the slices:
-//     M = max m_j, L = sum l_j e^(m_j - M), out = sum o_j e^(m_j - M) / L.
-// For one slice this is the reference's softmax(q k / sqrt(hd)) v with its
-// exact max subtraction; the reference sums the denominator in double and
-// scales each weight by float(1/den) before accumulating v, which changes
-// only the rounding.
-constexpr int kAttnWarps = 4;
-constexpr int kAttnMaxG = 8;
+//  1. s_t = dot(q, k_t) / sqrt(hd) for every cached token, one thread per
+//     token, with the reference's 8 FMA lanes (lane l takes dimensions
+//     l, l+8, ...) summed t0+t1+...+t7 (src/llama_model.cpp:23-39;
+//     Q8: times the token's K scale);
+//  2. m = max s_t; e_t = exp(s_t - m); den = sum of e_t in double;
+//     alpha_t = e_t * float(1/den) (src/llama_model.cpp:256);
+//  3. thread d owns output dimension d: out_d = fma(alpha_t, v_t[d], out_d)
+//     sequentially over t (Q8: alpha_t * v_scale first) -- the FMA chain of
+//     PagedKVCache::add_value (src/llama_model.cpp:40-55).
+// GQA: query head h reads kv head h / (n_head / n_head_kv).
+constexpr int kAttnUnroll = 8;
 
-template <int E>
-__device__ __forceinline__ void load_row(int kv_type, const uint8_t* pages, const float* scales, size_t slot,
-                                         int kv_dim, int off, float out[E]) {
-    if (kv_type == 1) {
-        const uint16_t* r = reinterpret_cast<const uint16_t*>(pages) + slot * kv_dim + off;
-        if constexpr (E == 4) {
-            const uint2 h = *reinterpret_cast<const uint2*>(r);
-            out[0] = half_bits_to_float(h.x & 0xffff);
-            out[1] = half_bits_to_float(h.x >> 16);
-            out[2] = half_bits_to_float(h.y & 0xffff);
-            out[3] = half_bits_to_float(h.y >> 16);
-        } else {
-#pragma unroll
-            for (int i = 0; i < E; ++i) out[i] = half_bits_to_float(r[i]);
-        }
-    } else if (kv_type == 0) {
-        const float* r = reinterpret_cast<const float*>(pages) + slot * kv_dim + off;
-#pragma unroll
-        for (int i = 0; i < E; ++i) out[i] = r[i];
-    } else {
-        const int8_t* r = reinterpret_cast<const int8_t*>(pages) + slot * kv_dim + off;
-        float sc;
-        if (kv_type == 2) sc = 1.0f;  // per-token scale applied by the caller
-        else sc = scales[slot * (kv_dim / 32) + off / 32];
-#pragma unroll
-        for (int i = 0; i < E; ++i) out[i] = (float)r[i] * sc;
-    }
+__device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
+
+__device__ __forceinline__ size_t slot_of(const AttnArgs& a, int s, int t) {
+    return (size_t)a.block_table[(size_t)s * a.max_pages + t / (int)a.page] * a.page + t % (int)a.page;
 }
 
-template <int E, int G>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(AttnArgs a, int split_len, int n_split) {
-    extern __shared__ float sm[];  // [G][split_len] scores, then [kAttnWarps][G][hd] partial o
-    const int s = blockIdx.x, kh = blockIdx.y, j = blockIdx.z;
-    const int hd = (int)a.hd, kv_dim = (int)(a.n_head_kv * a.hd);
+template <int HD>
+__global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
+    extern __shared__ float sm[];  // [HD] q, then [ctx] scores / weights
+    __shared__ float redf[HD / 32];
+    __shared__ double redd[HD / 32];
+    const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int G = (int)(a.n_head / a.n_head_kv), kh = h / G;
+    const int kv_dim = (int)(a.n_head_kv * HD);
     const int ctx = a.ctx_len[s];
-    const int t0 = j * split_len, t1 = min(ctx, t0 + split_len);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const size_t n_splits = (size_t)n_split;
-    // scratch layout: per (s, head, split): [hd] o, then m, l
-    auto slot_of = [&](int t) -> size_t {
-        return (size_t)a.block_table[(size_t)s * a.max_pages + t / (int)a.page] * a.page + t % (int)a.page;
-    };
+    float* qs = sm;
+    float* sc = sm + HD;
+    qs[tid] = a.q[(size_t)s * a.q_stride + (size_t)h * HD + tid];
+    __syncthreads();
+    const float root = sqrtf((float)HD);
     const uint8_t* kp = static_cast<const uint8_t*>(a.k_pages);
     const uint8_t* vp = static_cast<const uint8_t*>(a.v_pages);
-    const int off = kh * hd + lane * E;
-    float qv[G][E];
+
+    // 1. scores
+    for (int t = tid; t < ctx; t += HD) {
+        const size_t slot = slot_of(a, s, t);
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (a.kv_type == 1) {
+            const uint4* k = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(kp) + slot * kv_dim +
+                                                            (size_t)kh * HD);
+#pragma unroll 4
+            for (int d = 0; d < HD; d += 8) {
+                const uint4 w = k[d / 8];
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const float* qh = a.q + (size_t)s * a.q_stride + (size_t)(kh * G + g) * hd + lane * E;
+                for (int l = 0; l < 8; ++l)
+                    acc[l] = fmaf(qs[d + l], half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1)))), acc[l]);
+            }
+        } else if (a.kv_type == 0) {
+            const float4* k = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kp) + slot * kv_dim +
+                                                              (size_t)kh * HD);
+#pragma unroll 4
+            for (int d = 0; d < HD; d += 8) {
+                const float4 u = k[d / 4], v = k[d / 4 + 1];
+                const float ks[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int i = 0; i < E; ++i) qv[g][i] = qh[i];
-    }
-    const float root = sqrtf((float)hd);
-    float* sc = sm;
-    if (t0 < t1) {
-        // 1. scores
-        for (int t = t0 + warp; t < t1; t += kAttnWarps) {
-            const size_t sl = slot_of(t);
-            float kvv[E];
-            load_row<E>(a.kv_type, kp, a.k_scales, sl, kv_dim, off, kvv);
-            const float ks = a.kv_type == 2 ? a.k_scales[sl] : 1.0f;
+                for (int l = 0; l < 8; ++l) acc[l] = fmaf(qs[d + l], ks[l], acc[l]);
+            }
+        } else {
+            const uint2* k = reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(kp) + slot * kv_dim +
+                                                            (size_t)kh * HD);
+#pragma unroll 4
+            for (int d = 0; d < HD; d += 8) {
+                const uint2 w = k[d / 8];
+                float sc8 = 1.0f;
+                if (a.kv_type == 3) sc8 = a.k_scales[slot * (kv_dim / 32) + (kh * HD + d) / 32];
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float p = 0.0f;
-#pragma unroll
-                for (int i = 0; i < E; ++i) p = fmaf(qv[g][i], kvv[i], p);
-                p = warp_sum(p);
-                if (lane == 0) sc[g * split_len + (t - t0)] = (p * ks) / root;
+                for (int l = 0; l < 8; ++l) acc[l] = fmaf(qs[d + l], s8_to_f32(l < 4 ? w.x : w.y, l & 3) * sc8, acc[l]);
             }
         }
+        float dot = acc[0];
+#pragma unroll
+        for (int l = 1; l < 8; ++l) dot += acc[l];
+        if (a.kv_type == 2) dot = dot * a.k_scales[slot];
+        sc[t] = dot / root;
     }
     __syncthreads();
-    // 2. per-head max / exp / sum over the slice (warp g handles head g, ...)
-    __shared__ float mh[kAttnMaxG], lh[kAttnMaxG];
-    for (int g = warp; g < G; g += kAttnWarps) {
-        float m = -INFINITY;
-        for (int t = lane; t < t1 - t0; t += 32) m = fmaxf(m, sc[g * split_len + t]);
-        m = warp_max(m);
-        float l = 0.0f;
-        for (int t = lane; t < t1 - t0; t += 32) {
-            const float e = expf(sc[g * split_len + t] - m);
-            sc[g * split_len + t] = e;
-            l += e;
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            mh[g] = m;
-            lh[g] = l;
-        }
-    }
+
+    // 2. max, exp, double denominator, weights
+    float m = -INFINITY;
+    for (int t = tid; t < ctx; t += HD) m = fmaxf(m, sc[t]);
+    m = warp_max(m);
+    if (lane == 0) redf[warp] = m;
     __syncthreads();
-    // 3. o = sum e_t v_t
-    float acc[G][E];
+    m = redf[0];
 #pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int i = 0; i < E; ++i) acc[g][i] = 0.0f;
-    for (int t = t0 + warp; t < t1; t += kAttnWarps) {
-        const size_t sl = slot_of(t);
-        float vv[E];
-        load_row<E>(a.kv_type, vp, a.v_scales, sl, kv_dim, off, vv);
-        const float vs = a.kv_type == 2 ? a.v_scales[sl] : 1.0f;
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float p = sc[g * split_len + (t - t0)] * vs;
-#pragma unroll
-            for (int i = 0; i < E; ++i) acc[g][i] = fmaf(p, vv[i], acc[g][i]);
-        }
+    for (int w = 1; w < HD / 32; ++w) m = fmaxf(m, redf[w]);
+    double den = 0.0;
+    for (int t = tid; t < ctx; t += HD) {
+        const float e = expf_cr(sc[t] - m);
+        sc[t] = e;
+        den += (double)e;
     }
-    float* po = sm + (size_t)G * split_len;  // [kAttnWarps][G][hd]
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int i = 0; i < E; ++i) po[((size_t)warp * G + g) * hd + lane * E + i] = acc[g][i];
+    den = warp_sum_d(den);
+    if (lane == 0) redd[warp] = den;
     __syncthreads();
-    for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
-        const int g = idx / hd, dcol = idx % hd;
-        float o = 0.0f;
-        for (int w = 0; w < kAttnWarps; ++w) o += po[((size_t)w * G + g) * hd + dcol];
-        float* dst = a.scratch + (((size_t)s * a.n_head + (size_t)kh * G + g) * n_splits + j) * (hd + 2);
-        dst[dcol] = o;
-        if (dcol == 0) {
-            dst[hd] = t0 < t1 ? mh[g] : -INFINITY;
-            dst[hd + 1] = t0 < t1 ? lh[g] : 0.0f;
+    den = 0.0;
+#pragma unroll
+    for (int w = 0; w < HD / 32; ++w) den += redd[w];
+    const float inv = (float)(1.0 / den);
+    for (int t = tid; t < ctx; t += HD) sc[t] = sc[t] * inv;
+    __syncthreads();
+
+    // 3. out_d: sequential FMA chain over the tokens
+    float out = 0.0f;
+    const size_t off = (size_t)kh * HD + tid;
+    int t = 0;
+    for (; t + kAttnUnroll <= ctx; t += kAttnUnroll) {
+        float v[kAttnUnroll], al[kAttnUnroll];
+#pragma unroll
+        for (int u = 0; u < kAttnUnroll; ++u) {
+            const size_t slot = slot_of(a, s, t + u);
+            al[u] = sc[t + u];
+            if (a.kv_type == 1) v[u] = half_bits_to_float(reinterpret_cast<const uint16_t*>(vp)[slot * kv_dim + off]);
+            else if (a.kv_type == 0) v[u] = reinterpret_cast<const float*>(vp)[slot * kv_dim + off];
+            else {
+                v[u] = (float)reinterpret_cast<const int8_t*>(vp)[slot * kv_dim + off];
+                al[u] = al[u] * (a.kv_type == 2 ? a.v_scales[slot] : a.v_scales[slot * (kv_dim / 32) + off / 32]);
+            }
         }
+#pragma unroll
+        for (int u = 0; u < kAttnUnroll; ++u) out = fmaf(al[u], v[u], out);
     }
-}
-
-__global__ void attn_merge_kernel(AttnArgs a, int n_split) {
-    const int s = blockIdx.x, h = blockIdx.y, hd = (int)a.hd;
-    const float* base = a.scratch + ((size_t)s * a.n_head + h) * n_split * (hd + 2);
-    float M = -INFINITY;
-    for (int j = 0; j < n_split; ++j) M = fmaxf(M, base[(size_t)j * (hd + 2) + hd]);
-    float L = 0.0f;
-    for (int j = 0; j < n_split; ++j) {
-        const float m = base[(size_t)j * (hd + 2) + hd];
-        if (m != -INFINITY) L += base[(size_t)j * (hd + 2) + hd + 1] * expf(m - M);
-    }
-    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-    for (int dcol = threadIdx.x; dcol < hd; dcol += blockDim.x) {
-        float o = 0.0f;
-        for (int j = 0; j < n_split; ++j) {
-            const float m = base[(size_t)j * (hd + 2) + hd];
-            if (m != -INFINITY) o = fmaf(base[(size_t)j * (hd + 2) + dcol], expf(m - M), o);
+    for (; t < ctx; ++t) {
+        const size_t slot = slot_of(a, s, t);
+        float al = sc[t], v;
+        if (a.kv_type == 1) v = half_bits_to_float(reinterpret_cast<const uint16_t*>(vp)[slot * kv_dim + off]);
+        else if (a.kv_type == 0) v = reinterpret_cast<const float*>(vp)[slot * kv_dim + off];
+        else {
+            v = (float)reinterpret_cast<const int8_t*>(vp)[slot * kv_dim + off];
+            al = al * (a.kv_type == 2 ? a.v_scales[slot] : a.v_scales[slot * (kv_dim / 32) + off / 32]);
         }
-        a.out[((size_t)s * a.n_head + h) * hd + dcol] = o * inv;
+        out = fmaf(al, v, out);
     }
+    a.out[((size_t)s * a.n_head + h) * HD + tid] = out;
 }
 
-template <int E, int G>
-static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t s, const AttnArgs& a, int split_len, int n_split) {
-    ensure_smem_attr(attn_split_kernel<E, G>, 200 * 1024);
-    attn_split_kernel<E, G><<<grid, kAttnWarps * 32, smem, s>>>(a, split_len, n_split);
-    return cudaSuccess;
-}
-template <int E>
-static cudaError_t launch_attn_g(int G, dim3 grid, size_t smem, cudaStream_t s, const AttnArgs& a, int split_len,
-                                 int n_split) {
-    switch (G) {
-        case 1: return launch_attn<E, 1>(grid, smem, s, a, split_len, n_split);
-        case 2: return launch_attn<E, 2>(grid, smem, s, a, split_len, n_split);
-        case 4: return launch_attn<E, 4>(grid, smem, s, a, split_len, n_split);
-        case 8: return launch_attn<E, 8>(grid, smem, s, a, split_len, n_split);
-    }
-    return cudaErrorInvalidValue;
-}
-static cudaError_t launch_attn_e(uint64_t hd, int G, dim3 grid, size_t smem, cudaStream_t s, const AttnArgs& a,
-                                 int split_len, int n_split) {
-    switch (hd) {
-        case 64: return launch_attn_g<2>(G, grid, smem, s, a, split_len, n_split);
-        case 128: return launch_attn_g<4>(G, grid, smem, s, a, split_len, n_split);
-        case 256: return launch_attn_g<8>(G, grid, smem, s, a, split_len, n_split);
-    }
-    return cudaErrorInvalidValue;
-}
-
-static void split_plan(uint64_t n_seq, uint64_t n_head_kv, uint64_t G, uint64_t hd, uint64_t max_ctx, int& split_len,
-                       int& n_split) {
-    const uint64_t units = n_seq * n_head_kv;
-    const uint64_t target = (uint64_t)num_sms() * 4;
-    uint64_t ns = units >= target ? 1 : (target + units - 1) / units;
-    const uint64_t max_ns = (max_ctx + 31) / 32;  // keep >= 32 tokens per slice
-    if (ns > max_ns) ns = max_ns ? max_ns : 1;
-    uint64_t len = (max_ctx + ns - 1) / ns;
-    len = (len + 15) / 16 * 16;
-    if (len == 0) len = 16;
-    // the slice's scores and the per-warp partial outputs must fit in shared memory
-    const uint64_t cap = ((200 * 1024 / 4) - (uint64_t)kAttnWarps * G * hd) / G / 16 * 16;
-    if (len > cap) len = cap;
-    split_len = (int)len;
-    n_split = (int)((max_ctx + len - 1) / len);
-    if (n_split < 1) n_split = 1;
-}
-
-uint64_t attn_scratch_floats(uint64_t n_seq, uint64_t n_head, uint64_t hd, uint64_t max_ctx) {
-    // upper bound over every plan split_plan can choose for this shape
-    // (slices are at least 16 tokens long)
-    const uint64_t max_ns = max_ctx / 16 + 1;
-    return n_seq * n_head * max_ns * (hd + 2);
-}
+uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx) { return (hd + max_ctx) * sizeof(float); }
 
 cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s) {
     if (!a.n_seq) return cudaSuccess;
-    const int G = (int)(a.n_head / a.n_head_kv);
-    if (G > kAttnMaxG || a.n_head % a.n_head_kv) return cudaErrorInvalidValue;
-    int split_len, n_split;
-    split_plan(a.n_seq, a.n_head_kv, (uint64_t)G, a.hd, a.max_ctx ? a.max_ctx : 1, split_len, n_split);
-    const size_t smem = ((size_t)G * split_len + (size_t)kAttnWarps * G * a.hd) * sizeof(float);
+    if (a.n_head % a.n_head_kv) return cudaErrorInvalidValue;
+    const size_t smem = attn_smem_bytes(a.hd, a.max_ctx ? a.max_ctx : 1);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    dim3 grid((unsigned)a.n_seq, (unsigned)a.n_head_kv, (unsigned)n_split);
-    cudaError_t e = launch_attn_e(a.hd, G, grid, smem, s, a, split_len, n_split);
-    if (e != cudaSuccess) return e;
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    attn_merge_kernel<<<dim3((unsigned)a.n_seq, (unsigned)a.n_head), 128, 0, s>>>(a, n_split);
+    dim3 grid((unsigned)a.n_seq, (unsigned)a.n_head);
+    switch (a.hd) {
+        case 64:
+            ensure_smem_attr(attn_exact_kernel<64>, 200 * 1024);
+            attn_exact_kernel<64><<<grid, 64, smem, s>>>(a);
+            break;
+        case 128:
+            ensure_smem_attr(attn_exact_kernel<128>, 200 * 1024);
+            attn_exact_kernel<128><<<grid, 128, smem, s>>>(a);
+            break;
+        case 256:
+            ensure_smem_attr(attn_exact_kernel<256>, 200 * 1024);
+            attn_exact_kernel<256><<<grid, 256, smem, s>>>(a);
+            break;
+        default:
+            return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
 }
 

@@ -261,8 +261,11 @@ MV_API int mv_gemv(mv_weight_t w, const float* x, float* y, void* stream) {
     if (!x || !y) return fail(MV_ERR_INVALID, "null x or y");
     cudaStream_t s = as_stream(stream);
     if (w->type == 2) {
+        if (reinterpret_cast<uintptr_t>(x) % 16) return fail(MV_ERR_INVALID, "x must be 16-byte aligned");
         mvb::GemvQ4Args a{w, x, nullptr, 0.0f, y, mvb::Q4Pro::Plain, mvb::Q4Epi::Store};
         CK(mvb::gemv_q4(a, s));
+    } else if (w->type == 14 && w->cols * 4 <= 200 * 1024) {
+        CK(mvb::gemv_q6k(*w, x, y, s));
     } else {
         CK(mvb::matmul_f32act(*w, x, 1, y, s));
     }
@@ -383,16 +386,10 @@ MV_API int mv_paged_attn_decode(int kv_type, const float* q, uint64_t n_seq, uin
     if (hd != 64 && hd != 128 && hd != 256) return fail(MV_ERR_UNSUPPORTED, "head_dim must be 64, 128 or 256");
     if (!page) return fail(MV_ERR_INVALID, "page must be > 0");
     if (n_seq == 0) return MV_OK;
-    cudaStream_t s = as_stream(stream);
-    float* scratch = nullptr;
-    const uint64_t nf = mvb::attn_scratch_floats(n_seq, n_head, hd, max_ctx ? max_ctx : 1);
-    CK(cudaMallocAsync(reinterpret_cast<void**>(&scratch), nf * sizeof(float), s));
+    if (mvb::attn_smem_bytes(hd, max_ctx) > 200 * 1024) return fail(MV_ERR_INVALID, "max_ctx too large");
     mvb::AttnArgs a{kv_type, q, n_head * hd, n_seq, n_head, n_head_kv, hd, k_pages, v_pages, k_scales, v_scales,
-                    block_table,
-                    max_pages, page, ctx_len, max_ctx ? max_ctx : 1, out, scratch};
-    cudaError_t e = mvb::paged_attn_decode(a, s);
-    cudaFreeAsync(scratch, s);
-    if (e != cudaSuccess) return cuda_fail(e, "paged_attn_decode");
+                    block_table, max_pages, page, ctx_len, max_ctx ? max_ctx : 1, out};
+    CK(mvb::paged_attn_decode(a, as_stream(stream)));
     return MV_OK;
 }
 

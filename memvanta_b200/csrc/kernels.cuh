@@ -19,7 +19,7 @@ cudaError_t unpack_to_ggml(const mv_weight_s& w, uint8_t* raw_dev, cudaStream_t 
 cudaError_t read_rows(const mv_weight_s& w, const int32_t* rows, uint64_t n, float* out, cudaStream_t s);
 cudaError_t quantize_q8_rows(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* d, cudaStream_t s);
 
-// ---- gemv.cu : decode GEMV over Q4_0 with Q8 activations (integer path)
+// ---- gemv_q4.cu : decode GEMV over Q4_0 with Q8 activations (integer path)
 enum class Q4Pro : int {
     Plain = 0,    // activations = x
     RmsNorm = 1,  // activations = rmsnorm(x) * norm_w (the reference's rmsnorm)
@@ -41,7 +41,10 @@ struct GemvQ4Args {
 cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s);
 cudaError_t q4_block_dots(const mv_weight_s& w, const float* x, int32_t* isum, cudaStream_t s);
 
-// ---- gemv.cu : fp32-activation matmul for every type (T tokens per pass)
+// ---- gemv_q6k.cu : decode GEMV for the Q6_K output head (fp32 x)
+cudaError_t gemv_q6k(const mv_weight_s& w, const float* x, float* y, cudaStream_t s);
+
+// ---- matmul_f32.cu : fp32-activation matmul for every type (T tokens per pass)
 cudaError_t matmul_f32act(const mv_weight_s& w, const float* x, uint64_t batch, float* y, cudaStream_t s);
 
 // ---- gemm.cu : batched Q4_0 x Q8 activations (prefill)
@@ -78,12 +81,11 @@ struct AttnArgs {
     const float* v_scales;
     const int32_t* block_table;
     uint64_t max_pages, page;
-    const int32_t* ctx_len;  // per sequence
-    uint64_t max_ctx;        // upper bound of ctx_len (sizes the split grid)
-    float* out;
-    float* scratch;          // split partials; attn_scratch_floats() floats
+    const int32_t* ctx_len;  // per query row
+    uint64_t max_ctx;        // upper bound of ctx_len (sizes shared memory)
+    float* out;              // [n_seq][n_head*hd]
 };
-uint64_t attn_scratch_floats(uint64_t n_seq, uint64_t n_head, uint64_t hd, uint64_t max_ctx);
+uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx);
 cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s);
 
 }  // namespace mvb

@@ -12,7 +12,7 @@
 //    float expressions (:233) and uploaded.
 //  * decode (forward): one CUDA graph per step --
 //      embed(token) ; per layer { qkv GEMV with RMSNorm+Q8 prologue ;
-//      RoPE + KV append ; split-K paged attention ; o GEMV (+= x) ;
+//      RoPE + KV append ; paged attention in the reference's order ; o GEMV (+= x) ;
 //      gate/up GEMV with RMSNorm+Q8 prologue and SiLU-gate epilogue ;
 //      down GEMV (+= x) } ; output RMSNorm ; head matvec ; greedy argmax.
 //    The token id and position live in device memory, so the same graph
@@ -41,10 +41,64 @@ namespace mvb {
 
 // ------------------------------------------------------------- kernels
 
+// RoPE (half-split, the reference's GCC roundings: fma(x0,c,-(x1*s)) and
+// fma(x0,s,x1*c)) on the q and k parts of each qkv row, and the k and v parts
+// into the paged cache (F32 copy / F16 with the reference rounding / Q8_0 per
+// 32-element block).  Grid (rows, n_head + 2*n_head_kv): one CTA per q head
+// (rotate), k head (rotate + store) and v head (store).  ctx_out (optional)
+// receives pos+1 for the attention that follows.
+__global__ void rope_append_heads_kernel(float* __restrict__ qkv, int ld, int n_head, int n_head_kv, int hd,
+                                         const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                         const int32_t* __restrict__ pos, int kv_type, const int32_t* __restrict__ table,
+                                         int page, uint8_t* __restrict__ k_pages, uint8_t* __restrict__ v_pages,
+                                         float* __restrict__ k_scales, float* __restrict__ v_scales,
+                                         int32_t* __restrict__ ctx_out) {
+    const int r = blockIdx.x, unit = blockIdx.y, half = hd / 2, KV = n_head_kv * hd;
+    float* row = qkv + (size_t)r * ld;
+    const int p = pos[r];
+    float* b = row + (size_t)unit * hd;  // q heads, then k heads, then v heads
+    if (unit < n_head + n_head_kv) {
+        const float* co = cos_t + (size_t)p * half;
+        const float* si = sin_t + (size_t)p * half;
+        for (int j = threadIdx.x; j < half; j += blockDim.x) {
+            const float x0 = b[j], x1 = b[j + half], c = co[j], s = si[j];
+            b[j] = __fmaf_rn(x0, c, -__fmul_rn(x1, s));
+            b[j + half] = __fmaf_rn(x0, s, __fmul_rn(x1, c));
+        }
+    }
+    if (unit >= n_head) {
+        __syncthreads();
+        const bool is_v = unit >= n_head + n_head_kv;
+        const int head = unit - n_head - (is_v ? n_head_kv : 0);
+        const size_t slot = (size_t)table[p / page] * page + p % page;
+        uint8_t* pages = is_v ? v_pages : k_pages;
+        const size_t base = slot * KV + (size_t)head * hd;
+        if (kv_type == 0) {
+            float* dst = reinterpret_cast<float*>(pages) + base;
+            for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = b[i];
+        } else if (kv_type == 1) {
+            uint16_t* dst = reinterpret_cast<uint16_t*>(pages) + base;
+            for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = f32_to_f16_ref(b[i]);
+        } else {  // Q8_0: warp per 32-element block
+            float* scales = is_v ? v_scales : k_scales;
+            int8_t* dst = reinterpret_cast<int8_t*>(pages) + base;
+            const int lane = threadIdx.x & 31;
+            for (int blk = threadIdx.x >> 5; blk < hd / 32; blk += blockDim.x >> 5) {
+                float dd;
+                dst[blk * 32 + lane] = (int8_t)quant_q8_lane(b[blk * 32 + lane], dd);
+                if (lane == 0) scales[slot * (KV / 32) + (size_t)head * (hd / 32) + blk] = dd;
+            }
+        }
+    }
+    if (ctx_out && unit == 0 && threadIdx.x == 0) ctx_out[r] = p + 1;
+}
+
+// The MV_KV_Q8 cache keeps one scale per token over all kv_dim elements, so
+// its store needs the whole row: RoPE and store in one CTA per row.
 // RoPE (half-split, the reference's GCC roundings) on the q and k parts of
 // one qkv row, then the k and v parts into the paged cache.  One CTA per row.
 // ctx_out (optional) receives pos+1 for the attention that follows.
-__global__ void rope_append_kernel(float* __restrict__ qkv, int ld, int n_head, int n_head_kv, int hd,
+__global__ void rope_append_row_kernel(float* __restrict__ qkv, int ld, int n_head, int n_head_kv, int hd,
                                    const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                    const int32_t* __restrict__ pos, int kv_type, const int32_t* __restrict__ table,
                                    int page, uint8_t* __restrict__ k_pages, uint8_t* __restrict__ v_pages,
@@ -235,8 +289,6 @@ struct mv_model_s {
     // decode state (device)
     float *x = nullptr, *qkv = nullptr, *att = nullptr, *ff = nullptr, *gu = nullptr, *nrm = nullptr;
     float* logits = nullptr;
-    float* attn_scratch = nullptr;
-    uint64_t attn_scratch_n = 0;
     int32_t *token_dev = nullptr, *pos_dev = nullptr, *ctx_dev = nullptr, *history = nullptr;
     float* logits_host = nullptr;          // pinned
     cudaGraphExec_t graph_logits = nullptr, graph_nologits = nullptr;
@@ -367,11 +419,6 @@ void ensure_prefill(mv_model_s* m, uint64_t B) {
         ck(cudaMemcpy(m->table, t.data(), t.size() * 4, cudaMemcpyHostToDevice), "table upload");
         m->table_rows = B;
     }
-    const uint64_t need = mvb::attn_scratch_floats(B, m->n_head, m->hd, m->n_ctx);
-    if (need > m->attn_scratch_n) {
-        m->attn_scratch = dalloc<float>(m, need);
-        m->attn_scratch_n = need;
-    }
     m->pf_cap = B;
 }
 
@@ -390,7 +437,8 @@ void project_decode(mv_model_s* m, mv_weight_s* w, const float* x, const float* 
         in = m->nrm;
     }
     if (epi == mvb::Q4Epi::Store) {
-        ck(mvb::matmul_f32act(*w, in, 1, y, s), "matmul");
+        if (w->type == 14 && w->cols * 4 <= 200 * 1024) ck(mvb::gemv_q6k(*w, in, y, s), "gemv_q6k");
+        else ck(mvb::matmul_f32act(*w, in, 1, y, s), "matmul");
     } else if (epi == mvb::Q4Epi::AddTo) {
         ck(mvb::matmul_f32act(*w, in, 1, m->logits, s), "matmul");  // logits buffer as scratch
         ck(mvb::add_inplace(y, m->logits, w->rows, s), "add");
@@ -401,10 +449,26 @@ void project_decode(mv_model_s* m, mv_weight_s* w, const float* x, const float* 
     }
 }
 
+void rope_append(mv_model_s* m, const mvb::Layer& L, float* qkv, uint64_t rows, const int32_t* pos, int32_t* ctx_out) {
+    const uint64_t QKVW = m->n_embd + 2 * m->kv_dim;
+    if (m->kv_type == MV_KV_Q8) {
+        mvb::rope_append_row_kernel<<<(unsigned)rows, 256, 0, m->stream>>>(
+            qkv, (int)QKVW, (int)m->n_head, (int)m->n_head_kv, (int)m->hd, m->rope_cos, m->rope_sin, pos, m->kv_type,
+            m->table, (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales, ctx_out);
+    } else {
+        const int threads = m->kv_type == MV_KV_Q8_0 ? (int)std::max<uint64_t>(64, m->hd) : (int)(m->hd / 2);
+        mvb::rope_append_heads_kernel<<<dim3((unsigned)rows, (unsigned)(m->n_head + 2 * m->n_head_kv)), threads, 0,
+                                        m->stream>>>(
+            qkv, (int)QKVW, (int)m->n_head, (int)m->n_head_kv, (int)m->hd, m->rope_cos, m->rope_sin, pos, m->kv_type,
+            m->table, (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales, ctx_out);
+    }
+    ck(cudaGetLastError(), "rope_append");
+}
+
 mvb::AttnArgs attn_args(mv_model_s* m, const mvb::Layer& L, const float* q, uint64_t q_stride, uint64_t n_q,
                         const int32_t* ctx, uint64_t max_ctx, float* out) {
     return mvb::AttnArgs{m->kv_type, q, q_stride, n_q, m->n_head, m->n_head_kv, m->hd, L.k_pages, L.v_pages,
-                         L.k_scales, L.v_scales, m->table, m->n_pages, m->page, ctx, max_ctx, out, m->attn_scratch};
+                         L.k_scales, L.v_scales, m->table, m->n_pages, m->page, ctx, max_ctx, out};
 }
 
 // Every kernel of one decode step, in order, on m->stream.
@@ -414,11 +478,7 @@ void launch_decode(mv_model_s* m, bool with_logits) {
     ck(mvb::read_rows(*m->tok_embd, m->token_dev, 1, m->x, s), "embed");
     for (auto& L : m->layers) {
         project_decode(m, L.qkv, m->x, L.attn_norm, m->qkv, mvb::Q4Epi::Store);
-        mvb::rope_append_kernel<<<1, 256, 0, s>>>(m->qkv, (int)QKVW, (int)m->n_head, (int)m->n_head_kv, (int)m->hd,
-                                                  m->rope_cos, m->rope_sin, m->pos_dev, m->kv_type, m->table,
-                                                  (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales,
-                                                  m->ctx_dev);
-        ck(cudaGetLastError(), "rope_append");
+        rope_append(m, L, m->qkv, 1, m->pos_dev, m->ctx_dev);
         ck(mvb::paged_attn_decode(attn_args(m, L, m->qkv, QKVW, 1, m->ctx_dev, m->n_ctx, m->att), s), "attention");
         project_decode(m, L.o, m->att, nullptr, m->x, mvb::Q4Epi::AddTo);
         project_decode(m, L.gu, m->x, L.ffn_norm, m->ff, mvb::Q4Epi::SiluGate);
@@ -572,7 +632,7 @@ void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, in
     m->ctx_dev = dalloc<int32_t>(m, 1);
     m->history = dalloc<int32_t>(m, m->n_ctx + 1);
     ck(cudaMallocHost(reinterpret_cast<void**>(&m->logits_host), m->vocab * sizeof(float)), "cudaMallocHost");
-    ensure_prefill(m, 1);  // identity block table + attention scratch
+    ensure_prefill(m, 1);  // identity block table
 
     // One eager step (pos 0, token 0) makes every kernel's attributes and the
     // library's lazy state ready before the decode graphs are captured; the
@@ -642,11 +702,7 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     for (auto& L : m->layers) {
         ck(mvb::rmsnorm_rows(m->X, L.attn_norm, B, D, m->eps, m->N, s), "rmsnorm");
         project(L.qkv, m->N, D, m->QKV, false);
-        mvb::rope_append_kernel<<<(unsigned)B, 256, 0, s>>>(m->QKV, (int)QKVW, (int)m->n_head, (int)m->n_head_kv,
-                                                            (int)m->hd, m->rope_cos, m->rope_sin, pos,
-                                                            m->kv_type, m->table, (int)m->page, L.k_pages, L.v_pages,
-                                                            L.k_scales, L.v_scales, nullptr);
-        ck(cudaGetLastError(), "rope_append");
+        rope_append(m, L, m->QKV, B, pos, nullptr);
         ck(mvb::paged_attn_decode(attn_args(m, L, m->QKV, QKVW, B, ctx, start + B, m->ATT), s), "attention");
         project(L.o, m->ATT, D, m->X, true);
         ck(mvb::rmsnorm_rows(m->X, L.ffn_norm, B, D, m->eps, m->N, s), "rmsnorm");

@@ -119,6 +119,8 @@ __global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
     const int lane = tid & 31, warp = tid >> 5;
     const int G = (int)(a.n_head / a.n_head_kv), kh = h / G;
     const int kv_dim = (int)(a.n_head_kv * HD);
+    pdl_trigger();
+    pdl_wait();
     const int ctx = a.ctx_len[s];
     float* qs = sm;
     float* sc = sm + HD;
@@ -243,20 +245,16 @@ cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s) {
     switch (a.hd) {
         case 64:
             ensure_smem_attr(attn_exact_kernel<64>, 200 * 1024);
-            attn_exact_kernel<64><<<grid, 64, smem, s>>>(a);
-            break;
+            return launch_pdl(attn_exact_kernel<64>, grid, dim3(64), smem, s, a);
         case 128:
             ensure_smem_attr(attn_exact_kernel<128>, 200 * 1024);
-            attn_exact_kernel<128><<<grid, 128, smem, s>>>(a);
-            break;
+            return launch_pdl(attn_exact_kernel<128>, grid, dim3(128), smem, s, a);
         case 256:
             ensure_smem_attr(attn_exact_kernel<256>, 200 * 1024);
-            attn_exact_kernel<256><<<grid, 256, smem, s>>>(a);
-            break;
+            return launch_pdl(attn_exact_kernel<256>, grid, dim3(256), smem, s, a);
         default:
             return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 }  // namespace mvb

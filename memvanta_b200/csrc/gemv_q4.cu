@@ -98,12 +98,21 @@ __device__ __forceinline__ void prologue(const float* __restrict__ x, const floa
                                          bool rms, int nb, const Act& a) {
     const int G = nb * 4;  // groups of 8 elements
     const int iters = (G + (int)blockDim.x - 1) / (int)blockDim.x;
+    // the first kKeep groups of each thread stay in registers between the
+    // RMS pass and the quantisation pass
+    constexpr int kKeep = 2;
+    float4 keep[kKeep][2];
     float inv = 1.0f;
     if (rms) {
         double ss = 0.0;
-        for (int g = threadIdx.x; g < G; g += blockDim.x) {
+        int it = 0;
+        for (int g = threadIdx.x; g < G; g += blockDim.x, ++it) {
             const float4 u = reinterpret_cast<const float4*>(x)[2 * g];
             const float4 v = reinterpret_cast<const float4*>(x)[2 * g + 1];
+            if (it < kKeep) {
+                keep[it][0] = u;
+                keep[it][1] = v;
+            }
             ss += (double)u.x * u.x + (double)u.y * u.y + (double)u.z * u.z + (double)u.w * u.w;
             ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
         }
@@ -115,8 +124,14 @@ __device__ __forceinline__ void prologue(const float* __restrict__ x, const floa
         const bool active = g < G;  // uniform over the 4 lanes of a block
         float v[8];
         if (active) {
-            const float4 u = reinterpret_cast<const float4*>(x)[2 * g];
-            const float4 w = reinterpret_cast<const float4*>(x)[2 * g + 1];
+            float4 u, w;
+            if (rms && it < kKeep) {
+                u = keep[it][0];
+                w = keep[it][1];
+            } else {
+                u = reinterpret_cast<const float4*>(x)[2 * g];
+                w = reinterpret_cast<const float4*>(x)[2 * g + 1];
+            }
             v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; v[4] = w.x; v[5] = w.y; v[6] = w.z; v[7] = w.w;
             if (rms) {
                 const float4 n0 = reinterpret_cast<const float4*>(norm_w)[2 * g];
@@ -255,41 +270,50 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __res
     const int nbatch = (nb + 32 * PF - 1) / (32 * PF);
     const int gw = blockIdx.x * kWarps + warp, GW = gridDim.x * kWarps;
 
-    // Work items are (row group, batch) in row-group-major order.
-    int rg = gw, bt = 0;
-    Batch<RPW> A, Bb;
-    if (rg < row_groups) load_batch<RPW>(A, qs, dsc, rows, nb, rg, 0, lane);
-    prologue(x, norm_w, eps, pro == (int)Q4Pro::RmsNorm, nb, a);
-
-    float sum = 0.0f;
+    // Work items are (row group, batch) in row-group-major order.  The first
+    // two items' weights are requested before waiting on the previous kernel
+    // (weights are immutable), so their fetch overlaps its tail and the
+    // activation prologue.
     auto advance = [&](int& g, int& b) {
         if (++b == nbatch) {
             b = 0;
             g += GW;
         }
     };
+    pdl_trigger();
+    int rg = gw, bt = 0;
+    int rg1 = rg, bt1 = bt;
+    advance(rg1, bt1);
+    Batch<RPW> A, Bb;
+    if (rg < row_groups) load_batch<RPW>(A, qs, dsc, rows, nb, rg, bt, lane);
+    if (rg1 < row_groups) load_batch<RPW>(Bb, qs, dsc, rows, nb, rg1, bt1, lane);
+    pdl_wait();
+    prologue(x, norm_w, eps, pro == (int)Q4Pro::RmsNorm, nb, a);
+
+    float sum = 0.0f;
     while (rg < row_groups) {
-        int rg1 = rg, bt1 = bt;
-        advance(rg1, bt1);
-        if (rg1 < row_groups) load_batch<RPW>(Bb, qs, dsc, rows, nb, rg1, bt1, lane);
+        // A holds item (rg, bt), Bb holds item (rg1, bt1)
         consume_batch<RPW>(A, a, cb, nb, bt, lane, sum);
         if (bt == nbatch - 1) {
             epilogue<RPW>(epi, rg, rows, lane, sum, y);
             sum = 0.0f;
         }
-        rg = rg1;
-        bt = bt1;
-        if (rg >= row_groups) break;
-        int rg2 = rg, bt2 = bt;
+        int rg2 = rg1, bt2 = bt1;
         advance(rg2, bt2);
         if (rg2 < row_groups) load_batch<RPW>(A, qs, dsc, rows, nb, rg2, bt2, lane);
-        consume_batch<RPW>(Bb, a, cb, nb, bt, lane, sum);
-        if (bt == nbatch - 1) {
-            epilogue<RPW>(epi, rg, rows, lane, sum, y);
+        if (rg1 >= row_groups) break;
+        consume_batch<RPW>(Bb, a, cb, nb, bt1, lane, sum);
+        if (bt1 == nbatch - 1) {
+            epilogue<RPW>(epi, rg1, rows, lane, sum, y);
             sum = 0.0f;
         }
+        int rg3 = rg2, bt3 = bt2;
+        advance(rg3, bt3);
+        if (rg3 < row_groups) load_batch<RPW>(Bb, qs, dsc, rows, nb, rg3, bt3, lane);
         rg = rg2;
         bt = bt2;
+        rg1 = rg3;
+        bt1 = bt3;
     }
 }
 
@@ -314,10 +338,9 @@ cudaError_t launch(const GemvQ4Args& g, cudaStream_t s) {
     const uint64_t groups = (w.rows + RPW - 1) / RPW;
     const uint64_t ctas = (groups + kWarps - 1) / kWarps;
     const uint64_t cap = (uint64_t)num_sms() * 2;
-    gemv_q4_kernel<RPW><<<(unsigned)(ctas < cap ? ctas : cap), kThreads, smem, s>>>(
-        reinterpret_cast<const uint4*>(w.qs), w.d, (int)w.rows, (int)w.nb, g.x, g.norm_w, g.eps, (int)g.pro,
-        (int)g.epi, g.y);
-    return cudaGetLastError();
+    return launch_pdl(gemv_q4_kernel<RPW>, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(kThreads), smem, s,
+                      reinterpret_cast<const uint4*>(w.qs), (const unsigned short*)w.d, (int)w.rows, (int)w.nb,
+                      g.x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y);
 }
 
 }  // namespace

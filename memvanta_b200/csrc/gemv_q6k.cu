@@ -95,19 +95,21 @@ __global__ void __launch_bounds__(kThreads) gemv_q6k_kernel(mv_weight_s w, const
                                                             float* __restrict__ y) {
     extern __shared__ __align__(16) float xs[];
     const int K = (int)w.cols, regions = K / 128;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        const int r = i / 128, k = i % 128;
-        xs[r * 128 + ((k + 4 * r) & 127)] = x[i];
-    }
-    __syncthreads();
     const int lane = threadIdx.x & 31;
     const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5), GW = gridDim.x * kWarps;
     const int rows = (int)w.rows;
     // regions == number of 128-element groups in a row; lane l takes group l
     // (prefetched one row ahead) and, for K > 4096, groups l+32, l+64, ...
+    pdl_trigger();
     Group cur, nxt;
     int r = gw;
-    if (r < rows) load_group(cur, w, r, lane, lane < regions);
+    if (r < rows) load_group(cur, w, r, lane, lane < regions);  // weights: before the dependency wait
+    pdl_wait();
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        const int rr = i / 128, k = i % 128;
+        xs[rr * 128 + ((k + 4 * rr) & 127)] = x[i];
+    }
+    __syncthreads();
     for (; r < rows; r += GW) {
         const int rn = r + GW;
         if (rn < rows) load_group(nxt, w, rn, lane, lane < regions);
@@ -132,8 +134,7 @@ cudaError_t gemv_q6k(const mv_weight_s& w, const float* x, float* y, cudaStream_
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     ensure_smem_attr(gemv_q6k_kernel, 200 * 1024);
     const uint64_t ctas = (w.rows + kWarps - 1) / kWarps, cap = (uint64_t)num_sms() * 4;
-    gemv_q6k_kernel<<<(unsigned)(ctas < cap ? ctas : cap), kThreads, smem, s>>>(w, x, y);
-    return cudaGetLastError();
+    return launch_pdl(gemv_q6k_kernel, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(kThreads), smem, s, w, x, y);
 }
 
 }  // namespace mvb

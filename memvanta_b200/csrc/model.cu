@@ -54,6 +54,8 @@ __global__ void rope_append_heads_kernel(float* __restrict__ qkv, int ld, int n_
                                          float* __restrict__ k_scales, float* __restrict__ v_scales,
                                          int32_t* __restrict__ ctx_out) {
     const int r = blockIdx.x, unit = blockIdx.y, half = hd / 2, KV = n_head_kv * hd;
+    pdl_trigger();
+    pdl_wait();
     float* row = qkv + (size_t)r * ld;
     const int p = pos[r];
     float* b = row + (size_t)unit * hd;  // q heads, then k heads, then v heads
@@ -105,6 +107,8 @@ __global__ void rope_append_row_kernel(float* __restrict__ qkv, int ld, int n_he
                                    float* __restrict__ k_scales, float* __restrict__ v_scales,
                                    int32_t* __restrict__ ctx_out) {
     const int r = blockIdx.x, half = hd / 2, D = n_head * hd, KV = n_head_kv * hd;
+    pdl_trigger();
+    pdl_wait();
     float* row = qkv + (size_t)r * ld;
     const int p = pos[r];
     const float* co = cos_t + (size_t)p * half;
@@ -178,6 +182,8 @@ __global__ void greedy_step_kernel(const float* __restrict__ logits, int n, int3
                                    int32_t* __restrict__ pos, int32_t* __restrict__ history) {
     __shared__ float sv[32];
     __shared__ int si[32];
+    pdl_trigger();
+    pdl_wait();
     float v = -INFINITY;
     int idx = 0x7fffffff;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -223,7 +229,10 @@ __global__ void greedy_step_kernel(const float* __restrict__ logits, int n, int3
 }
 
 // Decode without logits still advances the device position.
-__global__ void advance_pos_kernel(int32_t* __restrict__ pos) { *pos += 1; }
+__global__ void advance_pos_kernel(int32_t* __restrict__ pos) {
+    pdl_wait();
+    *pos += 1;
+}
 
 // Token id and position of the next decode step, passed by value so no host
 // staging buffer has to outlive the launch.
@@ -451,18 +460,22 @@ void project_decode(mv_model_s* m, mv_weight_s* w, const float* x, const float* 
 
 void rope_append(mv_model_s* m, const mvb::Layer& L, float* qkv, uint64_t rows, const int32_t* pos, int32_t* ctx_out) {
     const uint64_t QKVW = m->n_embd + 2 * m->kv_dim;
+    cudaError_t e;
     if (m->kv_type == MV_KV_Q8) {
-        mvb::rope_append_row_kernel<<<(unsigned)rows, 256, 0, m->stream>>>(
-            qkv, (int)QKVW, (int)m->n_head, (int)m->n_head_kv, (int)m->hd, m->rope_cos, m->rope_sin, pos, m->kv_type,
-            m->table, (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales, ctx_out);
+        e = mvb::launch_pdl(mvb::rope_append_row_kernel, dim3((unsigned)rows), dim3(256), 0, m->stream, qkv, (int)QKVW,
+                            (int)m->n_head, (int)m->n_head_kv, (int)m->hd, (const float*)m->rope_cos,
+                            (const float*)m->rope_sin, pos, m->kv_type, (const int32_t*)m->table, (int)m->page,
+                            L.k_pages, L.v_pages, L.k_scales, L.v_scales, ctx_out);
     } else {
         const int threads = m->kv_type == MV_KV_Q8_0 ? (int)std::max<uint64_t>(64, m->hd) : (int)(m->hd / 2);
-        mvb::rope_append_heads_kernel<<<dim3((unsigned)rows, (unsigned)(m->n_head + 2 * m->n_head_kv)), threads, 0,
-                                        m->stream>>>(
-            qkv, (int)QKVW, (int)m->n_head, (int)m->n_head_kv, (int)m->hd, m->rope_cos, m->rope_sin, pos, m->kv_type,
-            m->table, (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales, ctx_out);
+        e = mvb::launch_pdl(mvb::rope_append_heads_kernel,
+                            dim3((unsigned)rows, (unsigned)(m->n_head + 2 * m->n_head_kv)), dim3(threads), 0,
+                            m->stream, qkv, (int)QKVW, (int)m->n_head, (int)m->n_head_kv, (int)m->hd,
+                            (const float*)m->rope_cos, (const float*)m->rope_sin, pos, m->kv_type,
+                            (const int32_t*)m->table, (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales,
+                            ctx_out);
     }
-    ck(cudaGetLastError(), "rope_append");
+    ck(e, "rope_append");
 }
 
 mvb::AttnArgs attn_args(mv_model_s* m, const mvb::Layer& L, const float* q, uint64_t q_stride, uint64_t n_q,
@@ -486,8 +499,9 @@ void launch_decode(mv_model_s* m, bool with_logits) {
     }
     if (with_logits) {
         project_decode(m, m->output, m->x, m->output_norm, m->logits, mvb::Q4Epi::Store);
-        mvb::greedy_step_kernel<<<1, 1024, 0, s>>>(m->logits, (int)m->vocab, m->token_dev, m->pos_dev, m->history);
-        ck(cudaGetLastError(), "greedy_step");
+        ck(mvb::launch_pdl(mvb::greedy_step_kernel, dim3(1), dim3(1024), 0, s, (const float*)m->logits,
+                           (int)m->vocab, m->token_dev, m->pos_dev, m->history),
+           "greedy_step");
     } else {
         mvb::advance_pos_kernel<<<1, 1, 0, s>>>(m->pos_dev);
         ck(cudaGetLastError(), "advance_pos");

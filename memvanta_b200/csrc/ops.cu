@@ -13,6 +13,8 @@ namespace mvb {
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, int n, float eps,
                                float* __restrict__ out) {
     __shared__ double red[32];
+    pdl_trigger();
+    pdl_wait();
     const float* xr = x + (size_t)blockIdx.x * n;
     float* o = out + (size_t)blockIdx.x * n;
     double ss = 0.0;
@@ -37,8 +39,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
 cudaError_t rmsnorm_rows(const float* x, const float* w, uint64_t rows, uint64_t n, float eps, float* out,
                          cudaStream_t s) {
     if (!rows) return cudaSuccess;
-    rmsnorm_kernel<<<(unsigned)rows, 512, 0, s>>>(x, w, (int)n, eps, out);
-    return cudaGetLastError();
+    return launch_pdl(rmsnorm_kernel, dim3((unsigned)rows), dim3(512), 0, s, x, w, (int)n, eps, out);
 }
 
 // Half-split RoPE: pairs (i, i+hd/2) of every head rotate by row pos of the

@@ -119,6 +119,8 @@ cudaError_t unpack_to_ggml(const mv_weight_s& w, uint8_t* raw, cudaStream_t s) {
 // (src/gguf_kernels.cpp:226): Q4_0 d*(q-8), Q8_0 d*q, Q6_K d*scale*q6
 // (float products in that order), F16 exact, F32 copy.  One CTA per row.
 __global__ void read_rows_kernel(mv_weight_s w, const int32_t* __restrict__ rows, float* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     const uint64_t r = (uint64_t)rows[blockIdx.x];
     float* o = out + (uint64_t)blockIdx.x * w.cols;
     if (r >= w.rows) {  // out-of-range ids give a NaN row instead of a wild read
@@ -154,8 +156,7 @@ __global__ void read_rows_kernel(mv_weight_s w, const int32_t* __restrict__ rows
 
 cudaError_t read_rows(const mv_weight_s& w, const int32_t* rows, uint64_t n, float* out, cudaStream_t s) {
     if (!n) return cudaSuccess;
-    read_rows_kernel<<<(unsigned)n, 256, 0, s>>>(w, rows, out);
-    return cudaGetLastError();
+    return launch_pdl(read_rows_kernel, dim3((unsigned)n), dim3(256), 0, s, w, rows, out);
 }
 
 // ------------------------------------------------------ activation quant

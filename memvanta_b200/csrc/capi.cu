@@ -111,7 +111,7 @@ int alloc_planes(mv_weight_s* w) {
     const uint64_t nbl = w->rows * w->nb;
     uint64_t q = 0, h = 0, sc = 0, d = 0;
     switch (w->type) {
-        case 2: q = nbl * 16; d = nbl * 2; break;
+        case 2: q = nbl * 16; d = w->rows * w->dstride * 2; break;
         case 8: q = nbl * 32; d = nbl * 2; break;
         case 14: q = nbl * 128; h = nbl * 64; sc = nbl * 16; d = nbl * 2; break;
         case 1: q = w->rows * w->cols * 2; break;
@@ -128,6 +128,10 @@ int alloc_planes(mv_weight_s* w) {
     w->qh = h ? b + oh : nullptr;
     w->sc = sc ? reinterpret_cast<int8_t*>(b + osc) : nullptr;
     w->d = d ? reinterpret_cast<uint16_t*>(b + od) : nullptr;
+    if (w->d && w->dstride != w->nb) {
+        e = cudaMemset(w->d, 0, d);  // padding scales stay zero
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(scales)");
+    }
     return MV_OK;
 }
 
@@ -150,6 +154,7 @@ int make_weight(uint64_t nbytes, int type, uint64_t rows, uint64_t cols, mv_weig
     w->rows = rows;
     w->cols = cols;
     w->nb = cols / per;
+    w->dstride = type == 2 ? (w->nb + 7) / 8 * 8 : w->nb;
     cudaGetDevice(&w->device);
     if (int rc = alloc_planes(w)) {
         delete w;

@@ -26,7 +26,7 @@ constexpr uint32_t kNib = 0x0F0F0F0Fu;
 
 __global__ void __launch_bounds__(kGWarps * 32) gemm_q4_q8_kernel(const uint4* __restrict__ qs,
                                                                   const unsigned short* __restrict__ dsc, int rows,
-                                                                  int nb, const int8_t* __restrict__ q,
+                                                                  int nb, int dstride, const int8_t* __restrict__ q,
                                                                   const float* __restrict__ d, int batch,
                                                                   float* __restrict__ y, int accumulate) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(kGWarps * 32) gemm_q4_q8_kernel(const uint4* _
             if (b < nb) {
                 const size_t bi = (size_t)r * nb + b;
                 const uint4 w = ld_stream_u4(qs + bi);
-                const float dw = half_bits_to_float(ld_stream_u16(dsc + bi));
+                const float dw = half_bits_to_float(ld_stream_u16(dsc + (size_t)r * dstride + b));
                 const int wl[4] = {(int)(w.x & kNib), (int)(w.y & kNib), (int)(w.z & kNib), (int)(w.w & kNib)};
                 const int wh[4] = {(int)((w.x >> 4) & kNib), (int)((w.y >> 4) & kNib), (int)((w.z >> 4) & kNib),
                                    (int)((w.w >> 4) & kNib)};
@@ -112,7 +112,8 @@ cudaError_t gemm_q4_q8(const mv_weight_s& w, const int8_t* q, const float* d, ui
     const uint64_t cap = (uint64_t)num_sms() * 2;
     dim3 grid((unsigned)(ctas < cap ? ctas : cap), (unsigned)((batch + kGTok - 1) / kGTok));
     gemm_q4_q8_kernel<<<grid, kGWarps * 32, smem, s>>>(reinterpret_cast<const uint4*>(w.qs), w.d, (int)w.rows,
-                                                       (int)w.nb, q, d, (int)batch, y, accumulate ? 1 : 0);
+                                                       (int)w.nb, (int)w.dstride, q, d, (int)batch, y,
+                                                       accumulate ? 1 : 0);
     return cudaGetLastError();
 }
 

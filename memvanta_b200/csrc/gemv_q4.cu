@@ -13,11 +13,12 @@
 // out identical to the reference's to the last bit, so the Q8 quantisation of
 // the next layer's input sees exactly the reference's values.
 //
-// Bandwidth.  HBM-bound: each weight byte is read once with 128-bit loads
-// (one 16-byte nibble payload per lane per block, plus its fp16 scale).  A
-// warp owns RPW rows; its loads are double-buffered in registers in batches
-// of 4 payloads per lane, and the first batch is issued before the activation
-// prologue so the prologue's latency hides under the weight fetch.
+// Bandwidth.  HBM-bound: each weight byte is read once, staged through a
+// per-warp shared-memory ring by 16-byte cp.async copies (one nibble payload
+// per lane per block; the fp16 scales 8 per copy), several items deep so
+// about 110 KB per SM are in flight.  A warp owns RPW rows at a time; the
+// ring's first items are requested before the activation prologue (and
+// before waiting on the previous kernel), hiding both under the weight fetch.
 //
 // Prologue (every CTA): optional RMSNorm (double sum of squares,
 // src/llama_model.cpp:237) and the per-32 Q8 quantisation of x into shared
@@ -38,7 +39,6 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kLoads = 4;        // payloads per lane per batch
 constexpr int kCbStride = 34;    // float2 per chain-buffer row (16-byte aligned, conflict-free)
 constexpr uint32_t kLoNib = 0x0F0F0F0Fu;
 
@@ -93,80 +93,97 @@ __device__ __forceinline__ double block_sum_d(double v) {
     return r;
 }
 
-// Quantised activations of (optionally RMS-normalised) x into shared memory.
+// One 8-element group of the quantisation: 4 neighbouring lanes hold one
+// 32-element block.  All 32 lanes of the warp must call it (shuffles).
+__device__ __forceinline__ void quant_group(int g, bool active, float4 u, float4 w, const float* __restrict__ norm_w,
+                                            bool rms, float inv, const Act& a) {
+    float v[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+    if (active && rms) {
+        const float4 n0 = reinterpret_cast<const float4*>(norm_w)[2 * g];
+        const float4 n1 = reinterpret_cast<const float4*>(norm_w)[2 * g + 1];
+        const float nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * nw[i];  // (x*inv)*w as the reference
+    }
+    if (!active) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    const float d = m > 0.0f ? m / 127.0f : 1.0f;  // quantize_q8: d = mx/127, inv = 1/d
+    const float id = 1.0f / d;
+    uint32_t pk[2] = {0u, 0u};
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int q = (int)fminf(fmaxf(roundf(v[i] * id), -127.0f), 127.0f);  // lround: half away from 0
+        sum += q;
+        pk[i >> 2] |= (uint32_t)(q & 0xff) << (8 * (i & 3));
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (active) {
+        const int b = g >> 2, sub = g & 3;
+        uint2* dst = reinterpret_cast<uint2*>(sub < 2 ? &a.lo[b] : &a.hi[b]) + (sub & 1);
+        *dst = make_uint2(pk[0], pk[1]);
+        if (sub == 0) a.dc[b] = make_float2(d, __int_as_float(8 * sum));
+    }
+}
+
+// Quantised activations of (optionally RMS-normalised) x into shared memory:
+// a thread owns groups g = tid, tid + blockDim, ...; with RMSNorm the first
+// kKeep groups stay in registers between the sum-of-squares pass and the
+// quantisation pass.
 __device__ __forceinline__ void prologue(const float* __restrict__ x, const float* __restrict__ norm_w, float eps,
                                          bool rms, int nb, const Act& a) {
-    const int G = nb * 4;  // groups of 8 elements
-    const int iters = (G + (int)blockDim.x - 1) / (int)blockDim.x;
-    // the first kKeep groups of each thread stay in registers between the
-    // RMS pass and the quantisation pass
     constexpr int kKeep = 2;
+    const int G = nb * 4;  // groups of 8 elements
+    const int bd = (int)blockDim.x, tid = (int)threadIdx.x;
+    const int iters = (G + bd - 1) / bd;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
     float4 keep[kKeep][2];
+#pragma unroll
+    for (int it = 0; it < kKeep; ++it) {
+        const int g = tid + it * bd;
+        keep[it][0] = keep[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (g < G) {
+            keep[it][0] = x4[2 * g];
+            keep[it][1] = x4[2 * g + 1];
+        }
+    }
     float inv = 1.0f;
     if (rms) {
         double ss = 0.0;
-        int it = 0;
-        for (int g = threadIdx.x; g < G; g += blockDim.x, ++it) {
-            const float4 u = reinterpret_cast<const float4*>(x)[2 * g];
-            const float4 v = reinterpret_cast<const float4*>(x)[2 * g + 1];
-            if (it < kKeep) {
-                keep[it][0] = u;
-                keep[it][1] = v;
-            }
+        auto acc = [&](float4 u, float4 v) {
             ss += (double)u.x * u.x + (double)u.y * u.y + (double)u.z * u.z + (double)u.w * u.w;
             ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
-        }
+        };
+#pragma unroll
+        for (int it = 0; it < kKeep; ++it) acc(keep[it][0], keep[it][1]);
+        for (int g = tid + kKeep * bd; g < G; g += bd) acc(x4[2 * g], x4[2 * g + 1]);
         const double tot = block_sum_d(ss);
         inv = 1.0f / sqrtf((float)(tot / (double)(nb * 32)) + eps);
     }
-    for (int it = 0; it < iters; ++it) {
-        const int g = threadIdx.x + it * (int)blockDim.x;
+#pragma unroll
+    for (int it = 0; it < kKeep; ++it) {
+        if (it < iters) {  // uniform across the CTA
+            const int g = tid + it * bd;
+            quant_group(g, g < G, keep[it][0], keep[it][1], norm_w, rms, inv, a);
+        }
+    }
+    for (int it = kKeep; it < iters; ++it) {
+        const int g = tid + it * bd;
         const bool active = g < G;  // uniform over the 4 lanes of a block
-        float v[8];
+        float4 u = make_float4(0.f, 0.f, 0.f, 0.f), w = u;
         if (active) {
-            float4 u, w;
-            if (rms && it < kKeep) {
-                u = keep[it][0];
-                w = keep[it][1];
-            } else {
-                u = reinterpret_cast<const float4*>(x)[2 * g];
-                w = reinterpret_cast<const float4*>(x)[2 * g + 1];
-            }
-            v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; v[4] = w.x; v[5] = w.y; v[6] = w.z; v[7] = w.w;
-            if (rms) {
-                const float4 n0 = reinterpret_cast<const float4*>(norm_w)[2 * g];
-                const float4 n1 = reinterpret_cast<const float4*>(norm_w)[2 * g + 1];
-                const float nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * nw[i];  // (x*inv)*w as the reference
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+            u = x4[2 * g];
+            w = x4[2 * g + 1];
         }
-        float m = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-        const float d = m > 0.0f ? m / 127.0f : 1.0f;  // quantize_q8: d = mx/127, inv = 1/d
-        const float id = 1.0f / d;
-        uint32_t pk[2] = {0u, 0u};
-        int sum = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int q = (int)fminf(fmaxf(roundf(v[i] * id), -127.0f), 127.0f);  // lround: half away from 0
-            sum += q;
-            pk[i >> 2] |= (uint32_t)(q & 0xff) << (8 * (i & 3));
-        }
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        if (active) {
-            const int b = g >> 2, sub = g & 3;
-            uint2* dst = reinterpret_cast<uint2*>(sub < 2 ? &a.lo[b] : &a.hi[b]) + (sub & 1);
-            *dst = make_uint2(pk[0], pk[1]);
-            if (sub == 0) a.dc[b] = make_float2(d, __int_as_float(8 * sum));
-        }
+        quant_group(g, active, u, w, norm_w, rms, inv, a);
     }
     __syncthreads();
 }
@@ -175,69 +192,84 @@ __device__ __forceinline__ void prologue(const float* __restrict__ x, const floa
 // match to the host libm's expf the reference calls.
 __device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
 
+// ---------------------------------------------------------- staging ring
+// Each warp streams its rows through a ring of S shared-memory stages filled
+// by cp.async (16-byte asynchronous copies, completion tracked per thread by
+// commit/wait groups -- no software spin).  One stage holds one work item:
+// RPW rows x 32 blocks of payload (16 B per block, lane-contiguous) followed
+// by the same blocks' fp16 scales.  S-1 items are in flight while one is
+// consumed: about 7 KB per warp, 110 KB per SM with 16 warps.
 template <int RPW>
-struct Batch {
-    uint4 w[RPW][kLoads / RPW];
-    unsigned short d[RPW][kLoads / RPW];
+struct Ring {
+    static constexpr int S = 16 / RPW;
+    static constexpr int PAY = RPW * 32 * 16;
+    static constexpr int STAGE = PAY + RPW * 64;
+    static constexpr int BYTES = S * STAGE;  // 9216 per warp
 };
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Copies work item (row group rg, chunk c) into a stage.  Lane l copies block
+// c*32+l of every row; lanes 0..3 copy the chunk's 32 scales (8 per copy --
+// the d plane's rows are padded to a multiple of 8, so these are aligned and
+// stay inside the row).
 template <int RPW>
-__device__ __forceinline__ void load_batch(Batch<RPW>& B, const uint4* __restrict__ qs,
-                                           const unsigned short* __restrict__ dsc, int rows, int nb, int rg, int batch,
-                                           int lane) {
-    constexpr int PF = kLoads / RPW;  // chunks of 32 blocks per batch
+__device__ __forceinline__ void issue_item(uint8_t* st, const uint4* __restrict__ qs,
+                                           const unsigned short* __restrict__ dsc, int rows, int nb, int dstride,
+                                           int rg, int c, int lane) {
+    const int b = c * 32 + lane;
 #pragma unroll
-    for (int p = 0; p < PF; ++p) {
-        const int b = (batch * PF + p) * 32 + lane;
-#pragma unroll
-        for (int j = 0; j < RPW; ++j) {
-            const int r = rg * RPW + j;
-            if (b < nb && r < rows) {
-                const size_t bi = (size_t)r * nb + b;
-                B.w[j][p] = ld_stream_u4(qs + bi);
-                B.d[j][p] = ld_stream_u16(dsc + bi);
-            }
+    for (int j = 0; j < RPW; ++j) {
+        const int r = rg * RPW + j;
+        if (r < rows) {
+            if (b < nb) cp_async16(st + (j * 32 + lane) * 16, qs + (size_t)r * nb + b);
+            if (lane < 4 && c * 32 + lane * 8 < nb)
+                cp_async16(st + Ring<RPW>::PAY + j * 64 + lane * 16, dsc + (size_t)r * dstride + c * 32 + lane * 8);
         }
     }
 }
 
-// Per-block terms of one batch, then each row's FMA chain over them in
-// block order.  `sum` is live in lanes 0..RPW-1 (lane j = row j).
+// Per-block terms of one item, then each row's FMA chain over them in block
+// order.  `sum` is live in lanes 0..RPW-1 (lane j = row j of the group).
 template <int RPW>
-__device__ __forceinline__ void consume_batch(const Batch<RPW>& B, const Act& a, float2* cb, int nb, int batch,
-                                              int lane, float& sum) {
-    constexpr int PF = kLoads / RPW;
+__device__ __forceinline__ void consume_item(const uint8_t* st, const Act& a, float2* cb, int nb, int c, int lane,
+                                             float& sum) {
+    const int b = c * 32 + lane;
+    if (b < nb) {
+        const int4 alo = a.lo[b], ahi = a.hi[b];
+        const float2 dc = a.dc[b];
+        const uint4* pay = reinterpret_cast<const uint4*>(st);
+        const unsigned short* dw = reinterpret_cast<const unsigned short*>(st + Ring<RPW>::PAY);
 #pragma unroll
-    for (int p = 0; p < PF; ++p) {
-        const int c = batch * PF + p;
-        const int b = c * 32 + lane;
-        if (c * 32 >= nb) break;  // uniform: past the last chunk
-        if (b < nb) {
-            const int4 alo = a.lo[b], ahi = a.hi[b];
-            const float2 dc = a.dc[b];
-#pragma unroll
-            for (int j = 0; j < RPW; ++j) {
-                const int isum = block_isum(B.w[j][p], alo, ahi, __float_as_int(dc.y));
-                cb[j * kCbStride + lane] = make_float2(half_bits_to_float(B.d[j][p]) * dc.x, (float)isum);
-            }
+        for (int j = 0; j < RPW; ++j) {
+            const int isum = block_isum(pay[j * 32 + lane], alo, ahi, __float_as_int(dc.y));
+            cb[j * kCbStride + lane] = make_float2(half_bits_to_float(dw[j * 32 + lane]) * dc.x, (float)isum);
         }
-        __syncwarp();
-        if (lane < RPW) {
-            const float2* row = cb + lane * kCbStride;
-            const int n = min(32, nb - c * 32);
-            if (n == 32) {
-#pragma unroll
-                for (int k = 0; k < 32; k += 2) {
-                    const float4 t = *reinterpret_cast<const float4*>(row + k);
-                    sum = fmaf(t.x, t.y, sum);
-                    sum = fmaf(t.z, t.w, sum);
-                }
-            } else {
-                for (int k = 0; k < n; ++k) sum = fmaf(row[k].x, row[k].y, sum);
-            }
-        }
-        __syncwarp();
     }
+    __syncwarp();
+    if (lane < RPW) {
+        const float2* row = cb + lane * kCbStride;
+        const int n = min(32, nb - c * 32);
+        if (n == 32) {
+#pragma unroll
+            for (int k = 0; k < 32; k += 2) {
+                const float4 t = *reinterpret_cast<const float4*>(row + k);
+                sum = fmaf(t.x, t.y, sum);
+                sum = fmaf(t.z, t.w, sum);
+            }
+        } else {
+            for (int k = 0; k < n; ++k) sum = fmaf(row[k].x, row[k].y, sum);
+        }
+    }
+    __syncwarp();
 }
 
 template <int RPW>
@@ -259,62 +291,55 @@ __device__ __forceinline__ void epilogue(int epi, int rg, int rows, int lane, fl
 template <int RPW>
 __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __restrict__ qs,
                                                               const unsigned short* __restrict__ dsc, int rows,
-                                                              int nb, const float* __restrict__ x,
+                                                              int nb, int dstride, const float* __restrict__ x,
                                                               const float* __restrict__ norm_w, float eps, int pro,
                                                               int epi, float* __restrict__ y) {
-    constexpr int PF = kLoads / RPW;
+    using R = Ring<RPW>;
     const Act a = act_smem(nb);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float2* cb = a.cb + (size_t)warp * RPW * kCbStride;
+    uint8_t* ring = reinterpret_cast<uint8_t*>(a.cb + (size_t)kWarps * RPW * kCbStride) + (size_t)warp * R::BYTES;
     const int row_groups = (rows + RPW - 1) / RPW;
-    const int nbatch = (nb + 32 * PF - 1) / (32 * PF);
+    const int nchunk = (nb + 31) / 32;
     const int gw = blockIdx.x * kWarps + warp, GW = gridDim.x * kWarps;
 
-    // Work items are (row group, batch) in row-group-major order.  The first
-    // two items' weights are requested before waiting on the previous kernel
-    // (weights are immutable), so their fetch overlaps its tail and the
-    // activation prologue.
-    auto advance = [&](int& g, int& b) {
-        if (++b == nbatch) {
-            b = 0;
+    // Work items (row group, chunk), row-group-major; weights are immutable, so
+    // the first S-1 items are requested before waiting on the previous kernel.
+    pdl_trigger();
+    int irg = gw, ic = 0;  // next item to issue
+    auto step = [&](int& g, int& c) {
+        if (++c == nchunk) {
+            c = 0;
             g += GW;
         }
     };
-    pdl_trigger();
-    int rg = gw, bt = 0;
-    int rg1 = rg, bt1 = bt;
-    advance(rg1, bt1);
-    Batch<RPW> A, Bb;
-    if (rg < row_groups) load_batch<RPW>(A, qs, dsc, rows, nb, rg, bt, lane);
-    if (rg1 < row_groups) load_batch<RPW>(Bb, qs, dsc, rows, nb, rg1, bt1, lane);
+#pragma unroll
+    for (int k = 0; k < R::S - 1; ++k) {
+        if (irg < row_groups) issue_item<RPW>(ring + k * R::STAGE, qs, dsc, rows, nb, dstride, irg, ic, lane);
+        cp_async_commit();
+        step(irg, ic);
+    }
     pdl_wait();
     prologue(x, norm_w, eps, pro == (int)Q4Pro::RmsNorm, nb, a);
 
     float sum = 0.0f;
+    int rg = gw, c = 0, slot = 0, islot = R::S - 1;
     while (rg < row_groups) {
-        // A holds item (rg, bt), Bb holds item (rg1, bt1)
-        consume_batch<RPW>(A, a, cb, nb, bt, lane, sum);
-        if (bt == nbatch - 1) {
+        cp_async_wait<R::S - 2>();  // this item's copies have landed (per thread)
+        __syncwarp();               // ... and every lane's (the scales come from lanes 0..3)
+        consume_item<RPW>(ring + slot * R::STAGE, a, cb, nb, c, lane, sum);
+        if (irg < row_groups) issue_item<RPW>(ring + islot * R::STAGE, qs, dsc, rows, nb, dstride, irg, ic, lane);
+        cp_async_commit();
+        step(irg, ic);
+        if (++islot == R::S) islot = 0;
+        if (c == nchunk - 1) {
             epilogue<RPW>(epi, rg, rows, lane, sum, y);
             sum = 0.0f;
         }
-        int rg2 = rg1, bt2 = bt1;
-        advance(rg2, bt2);
-        if (rg2 < row_groups) load_batch<RPW>(A, qs, dsc, rows, nb, rg2, bt2, lane);
-        if (rg1 >= row_groups) break;
-        consume_batch<RPW>(Bb, a, cb, nb, bt1, lane, sum);
-        if (bt1 == nbatch - 1) {
-            epilogue<RPW>(epi, rg1, rows, lane, sum, y);
-            sum = 0.0f;
-        }
-        int rg3 = rg2, bt3 = bt2;
-        advance(rg3, bt3);
-        if (rg3 < row_groups) load_batch<RPW>(Bb, qs, dsc, rows, nb, rg3, bt3, lane);
-        rg = rg2;
-        bt = bt2;
-        rg1 = rg3;
-        bt1 = bt3;
+        step(rg, c);
+        if (++slot == R::S) slot = 0;
     }
+    cp_async_wait<0>();
 }
 
 // Diagnostic twin: the per-block int32 dots of the same device code.
@@ -333,14 +358,15 @@ __global__ void __launch_bounds__(kThreads) q4_block_dots_kernel(const uint4* __
 template <int RPW>
 cudaError_t launch(const GemvQ4Args& g, cudaStream_t s) {
     const mv_weight_s& w = *g.w;
-    const size_t smem = act_smem_bytes(w.nb, RPW);
+    const size_t smem = act_smem_bytes(w.nb, RPW) + (size_t)kWarps * Ring<RPW>::BYTES;
+    if (smem > 110 * 1024) return cudaErrorInvalidValue;  // two CTAs per SM
     ensure_smem_attr(gemv_q4_kernel<RPW>, 200 * 1024);
     const uint64_t groups = (w.rows + RPW - 1) / RPW;
     const uint64_t ctas = (groups + kWarps - 1) / kWarps;
     const uint64_t cap = (uint64_t)num_sms() * 2;
     return launch_pdl(gemv_q4_kernel<RPW>, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(kThreads), smem, s,
                       reinterpret_cast<const uint4*>(w.qs), (const unsigned short*)w.d, (int)w.rows, (int)w.nb,
-                      g.x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y);
+                      (int)w.dstride, g.x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y);
 }
 
 }  // namespace

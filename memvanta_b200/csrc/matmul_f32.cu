@@ -32,7 +32,7 @@ __device__ __forceinline__ void deq4(const mv_weight_s& w, uint64_t r, uint64_t 
         const int e = (int)(e0 % 32);
         const uint32_t word = ld_stream_u32(w.qs + b * 16 + (e & 15));
         const uint32_t nib = e < 16 ? (word & kLoNib) : ((word >> 4) & kLoNib);
-        const float d = half_bits_to_float(ld_stream_u16(w.d + b));
+        const float d = half_bits_to_float(ld_stream_u16(w.d + r * w.dstride + e0 / 32));
 #pragma unroll
         for (int i = 0; i < 4; ++i) out[i] = u8_to_f32_minus(nib, i, 8388616.0f) * d;
     } else if constexpr (TYPE == 8) {  // Q8_0

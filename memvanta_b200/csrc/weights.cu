@@ -20,10 +20,10 @@ int num_sms() {
 // One thread per block.  Raw GGUF bytes are read with byte loads (18/34/210
 // byte blocks are unaligned); the planes are written with wide stores.
 __global__ void repack_q4_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ qs, uint16_t* __restrict__ d,
-                                 uint64_t nblocks) {
+                                 uint64_t nblocks, uint64_t nb, uint64_t dstride) {
     for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblocks; b += (uint64_t)gridDim.x * blockDim.x) {
         const uint8_t* p = raw + b * 18;
-        d[b] = (uint16_t)(p[0] | (p[1] << 8));
+        d[(b / nb) * dstride + b % nb] = (uint16_t)(p[0] | (p[1] << 8));
         uint32_t w[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
@@ -32,11 +32,12 @@ __global__ void repack_q4_kernel(const uint8_t* __restrict__ raw, uint8_t* __res
     }
 }
 __global__ void unpack_q4_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ d, uint8_t* __restrict__ raw,
-                                 uint64_t nblocks) {
+                                 uint64_t nblocks, uint64_t nb, uint64_t dstride) {
     for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblocks; b += (uint64_t)gridDim.x * blockDim.x) {
         uint8_t* p = raw + b * 18;
-        p[0] = d[b] & 0xff;
-        p[1] = d[b] >> 8;
+        const uint16_t dv = d[(b / nb) * dstride + b % nb];
+        p[0] = dv & 0xff;
+        p[1] = dv >> 8;
         for (int i = 0; i < 16; ++i) p[2 + i] = qs[b * 16 + i];
     }
 }
@@ -95,7 +96,7 @@ static dim3 grid_for(uint64_t n, int threads) {
 cudaError_t repack_from_ggml(mv_weight_s& w, const uint8_t* raw, cudaStream_t s) {
     const uint64_t nblocks = w.rows * w.nb;
     switch (w.type) {
-        case 2: repack_q4_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(raw, w.qs, w.d, nblocks); break;
+        case 2: repack_q4_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(raw, w.qs, w.d, nblocks, w.nb, w.dstride); break;
         case 8: repack_q8_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(raw, w.qs, w.d, nblocks); break;
         case 14: repack_q6k_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(raw, w.qs, w.qh, w.sc, w.d, nblocks); break;
         default: return cudaMemcpyAsync(w.qs, raw, w.rows * w.cols * (w.type == 0 ? 4 : 2), cudaMemcpyDeviceToDevice, s);
@@ -106,7 +107,7 @@ cudaError_t repack_from_ggml(mv_weight_s& w, const uint8_t* raw, cudaStream_t s)
 cudaError_t unpack_to_ggml(const mv_weight_s& w, uint8_t* raw, cudaStream_t s) {
     const uint64_t nblocks = w.rows * w.nb;
     switch (w.type) {
-        case 2: unpack_q4_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(w.qs, w.d, raw, nblocks); break;
+        case 2: unpack_q4_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(w.qs, w.d, raw, nblocks, w.nb, w.dstride); break;
         case 8: unpack_q8_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(w.qs, w.d, raw, nblocks); break;
         case 14: unpack_q6k_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(w.qs, w.qh, w.sc, w.d, raw, nblocks); break;
         default: return cudaMemcpyAsync(raw, w.qs, w.rows * w.cols * (w.type == 0 ? 4 : 2), cudaMemcpyDeviceToDevice, s);
@@ -134,7 +135,7 @@ __global__ void read_rows_kernel(mv_weight_s w, const int32_t* __restrict__ rows
             const int e = c % 32;
             const uint8_t byte = w.qs[b * 16 + (e & 15)];
             const int q = (e < 16 ? (byte & 15) : (byte >> 4)) - 8;
-            v = half_bits_to_float(w.d[b]) * (float)q;
+            v = half_bits_to_float(w.d[r * w.dstride + c / 32]) * (float)q;
         } else if (w.type == 8) {
             const uint64_t b = r * w.nb + c / 32;
             v = half_bits_to_float(w.d[b]) * (float)(int8_t)w.qs[b * 32 + c % 32];

@@ -5,7 +5,8 @@
 // once into planes ("structure of arrays"), row-major [rows][blocks]:
 //
 //   Q4_0  qs  u8  [rows][nb][16]   the 16 nibble bytes of each block, as in GGUF
-//         d   f16 [rows][nb]
+//         d   f16 [rows][dstride]  dstride = nb rounded up to 8, so every row's
+//                                  scales start 16-byte aligned (zero padding)
 //   Q8_0  qs  i8  [rows][nb][32]
 //         d   f16 [rows][nb]
 //   Q6_K  qs  u8  [rows][nsb][128] ql
@@ -24,6 +25,7 @@ struct mv_weight_s {
     int type = 0;
     uint64_t rows = 0, cols = 0;
     uint64_t nb = 0;          // blocks per row (32-element; 256 for Q6_K)
+    uint64_t dstride = 0;     // fp16 scales per row in the d plane (>= nb)
     void* base = nullptr;     // single device allocation holding all planes
     uint64_t bytes = 0;
     uint8_t* qs = nullptr;    // payload plane (Q4_0/Q8_0 qs, Q6_K ql, F16/F32 data)

@@ -102,78 +102,159 @@ cudaError_t kv_append(int kv_type, const float* k, const float* v, uint64_t rows
 //     sequentially over t (Q8: alpha_t * v_scale first) -- the FMA chain of
 //     PagedKVCache::add_value (src/llama_model.cpp:40-55).
 // GQA: query head h reads kv head h / (n_head / n_head_kv).
-constexpr int kAttnUnroll = 8;
+constexpr int kVTile = 32;    // tokens per V tile
+constexpr int kVStages = 4;
 
 __device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
 
-__device__ __forceinline__ size_t slot_of(const AttnArgs& a, int s, int t) {
-    return (size_t)a.block_table[(size_t)s * a.max_pages + t / (int)a.page] * a.page + t % (int)a.page;
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Tokens per K tile: one per thread, at most 128, and two tiles of padded
+// rows within 128 KB.
+__host__ __device__ inline int attn_ktile(uint64_t hd, int kv_type) {
+    const uint64_t esize = kv_type == 0 ? 4 : kv_type == 1 ? 2 : 1;
+    uint64_t kt = 65536 / (hd * esize + 16);
+    if (kt > hd) kt = hd;
+    if (kt > 128) kt = 128;
+    return (int)(kt / 32 * 32);
+}
+
+// Shared-memory plan of one CTA (all offsets 16-byte aligned).
+struct AttnSmem {
+    uint64_t q, table, sc, vsc, ring, total;
+};
+__host__ __device__ inline AttnSmem attn_plan(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type) {
+    auto up = [](uint64_t n) { return (n + 15) / 16 * 16; };
+    const uint64_t esize = kv_type == 0 ? 4 : kv_type == 1 ? 2 : 1;
+    const uint64_t krow = hd * esize + 16;                          // padded K row
+    const uint64_t kring = 2 * (uint64_t)attn_ktile(hd, kv_type) * krow;  // double-buffered K tiles
+    const uint64_t vring = (uint64_t)kVStages * kVTile * hd * esize; // V stages
+    const uint64_t nsc = kv_type == 2 ? 1 : kv_type == 3 ? hd / 32 : 0;  // V scales per token
+    AttnSmem p;
+    p.q = 0;
+    p.table = up(hd * 4);
+    p.sc = p.table + up(max_pages * 4);
+    p.vsc = p.sc + up(max_ctx * 4);
+    p.ring = p.vsc + up(max_ctx * nsc * 4);
+    p.total = p.ring + (kring > vring ? kring : vring);
+    return p;
 }
 
 template <int HD>
 __global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
-    extern __shared__ float sm[];  // [HD] q, then [ctx] scores / weights
+    extern __shared__ __align__(16) unsigned char smem[];
     __shared__ float redf[HD / 32];
     __shared__ double redd[HD / 32];
     const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int G = (int)(a.n_head / a.n_head_kv), kh = h / G;
     const int kv_dim = (int)(a.n_head_kv * HD);
+    const int kvt = a.kv_type;
+    const int esize = kvt == 0 ? 4 : kvt == 1 ? 2 : 1;
+    const int page = (int)a.page;
+    const AttnSmem P = attn_plan(HD, a.max_ctx, a.max_pages, kvt);
+    float* qs = reinterpret_cast<float*>(smem + P.q);
+    int* tbl = reinterpret_cast<int*>(smem + P.table);
+    float* sc = reinterpret_cast<float*>(smem + P.sc);
+    float* vsc = reinterpret_cast<float*>(smem + P.vsc);
+    uint8_t* ring = smem + P.ring;
+    const uint8_t* kp = static_cast<const uint8_t*>(a.k_pages);
+    const uint8_t* vp = static_cast<const uint8_t*>(a.v_pages);
+    const size_t row_bytes = (size_t)kv_dim * esize;
+    const size_t head_off = (size_t)kh * HD * esize;
+    const int slice = HD * esize;  // bytes of one token's head slice
+
     pdl_trigger();
     pdl_wait();
     const int ctx = a.ctx_len[s];
-    float* qs = sm;
-    float* sc = sm + HD;
+    const int npg = (ctx + page - 1) / page;
+    for (int i = tid; i < npg; i += HD) tbl[i] = a.block_table[(size_t)s * a.max_pages + i];
     qs[tid] = a.q[(size_t)s * a.q_stride + (size_t)h * HD + tid];
     __syncthreads();
-    const float root = sqrtf((float)HD);
-    const uint8_t* kp = static_cast<const uint8_t*>(a.k_pages);
-    const uint8_t* vp = static_cast<const uint8_t*>(a.v_pages);
+    auto slot_of = [&](int t) -> size_t { return (size_t)tbl[t / page] * page + t % page; };
 
-    // 1. scores
-    for (int t = tid; t < ctx; t += HD) {
-        const size_t slot = slot_of(a, s, t);
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (a.kv_type == 1) {
-            const uint4* k = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(kp) + slot * kv_dim +
-                                                            (size_t)kh * HD);
-#pragma unroll 4
-            for (int d = 0; d < HD; d += 8) {
-                const uint4 w = k[d / 8];
-                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int l = 0; l < 8; ++l)
-                    acc[l] = fmaf(qs[d + l], half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1)))), acc[l]);
+    // 1. scores: thread t of a K tile owns one token; its head slice is staged
+    //    by cp.async into its own (padded) shared row, two tiles in flight.
+    {
+        const int krow = slice + 16;
+        const int KT = attn_ktile(HD, kvt);  // threads tid < KT own one token of each tile
+        auto issue_k = [&](int tile, int buf) {
+            const int t = tile * KT + tid;
+            if (tid < KT && t < ctx) {
+                const uint8_t* src = kp + slot_of(t) * row_bytes + head_off;
+                uint8_t* dst = ring + ((size_t)buf * KT + tid) * krow;
+                for (int c = 0; c < slice; c += 16) cp_async16(dst + c, src + c);
             }
-        } else if (a.kv_type == 0) {
-            const float4* k = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kp) + slot * kv_dim +
-                                                              (size_t)kh * HD);
+            cp_async_commit();
+        };
+        const int ntile = (ctx + KT - 1) / KT;
+        issue_k(0, 0);
+        for (int tile = 0; tile < ntile; ++tile) {
+            if (tile + 1 < ntile) issue_k(tile + 1, (tile + 1) & 1);
+            else cp_async_commit();
+            cp_async_wait<1>();  // own row of this tile has landed
+            const int t = tile * KT + tid;
+            if (tid < KT && t < ctx) {
+                const uint8_t* row = ring + ((size_t)(tile & 1) * KT + tid) * krow;
+                float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                if (kvt == 1) {
 #pragma unroll 4
-            for (int d = 0; d < HD; d += 8) {
-                const float4 u = k[d / 4], v = k[d / 4 + 1];
-                const float ks[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+                    for (int d = 0; d < HD; d += 8) {
+                        const uint4 w = *reinterpret_cast<const uint4*>(row + d * 2);
+                        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                for (int l = 0; l < 8; ++l) acc[l] = fmaf(qs[d + l], ks[l], acc[l]);
-            }
-        } else {
-            const uint2* k = reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(kp) + slot * kv_dim +
-                                                            (size_t)kh * HD);
+                        for (int l = 0; l < 8; ++l)
+                            acc[l] = fmaf(qs[d + l], half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1)))),
+                                          acc[l]);
+                    }
+                } else if (kvt == 0) {
 #pragma unroll 4
-            for (int d = 0; d < HD; d += 8) {
-                const uint2 w = k[d / 8];
-                float sc8 = 1.0f;
-                if (a.kv_type == 3) sc8 = a.k_scales[slot * (kv_dim / 32) + (kh * HD + d) / 32];
+                    for (int d = 0; d < HD; d += 8) {
+                        const float4 u = *reinterpret_cast<const float4*>(row + d * 4);
+                        const float4 v = *reinterpret_cast<const float4*>(row + d * 4 + 16);
+                        const float ks[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
 #pragma unroll
-                for (int l = 0; l < 8; ++l) acc[l] = fmaf(qs[d + l], s8_to_f32(l < 4 ? w.x : w.y, l & 3) * sc8, acc[l]);
+                        for (int l = 0; l < 8; ++l) acc[l] = fmaf(qs[d + l], ks[l], acc[l]);
+                    }
+                } else {
+                    const size_t slot = slot_of(t);
+#pragma unroll 4
+                    for (int d = 0; d < HD; d += 8) {
+                        const uint2 w = *reinterpret_cast<const uint2*>(row + d);
+                        float sc8 = 1.0f;
+                        if (kvt == 3) sc8 = a.k_scales[slot * (kv_dim / 32) + (kh * HD + d) / 32];
+#pragma unroll
+                        for (int l = 0; l < 8; ++l)
+                            acc[l] = fmaf(qs[d + l], s8_to_f32(l < 4 ? w.x : w.y, l & 3) * sc8, acc[l]);
+                    }
+                }
+                float dot = acc[0];
+#pragma unroll
+                for (int l = 1; l < 8; ++l) dot += acc[l];
+                if (kvt == 2) dot = dot * a.k_scales[slot_of(t)];
+                sc[t] = dot / sqrtf((float)HD);
             }
         }
-        float dot = acc[0];
-#pragma unroll
-        for (int l = 1; l < 8; ++l) dot += acc[l];
-        if (a.kv_type == 2) dot = dot * a.k_scales[slot];
-        sc[t] = dot / root;
+        cp_async_wait<0>();
     }
-    __syncthreads();
+    // per-token V scales (Q8 types), gathered while the softmax runs
+    if (kvt == 2) {
+        for (int t = tid; t < ctx; t += HD) vsc[t] = a.v_scales[slot_of(t)];
+    } else if (kvt == 3) {
+        for (int i = tid; i < ctx * (HD / 32); i += HD) {
+            const int t = i / (HD / 32), b = i % (HD / 32);
+            vsc[i] = a.v_scales[slot_of(t) * (kv_dim / 32) + kh * (HD / 32) + b];
+        }
+    }
+    __syncthreads();  // every K tile is consumed: the ring is free for V
 
     // 2. max, exp, double denominator, weights
     float m = -INFINITY;
@@ -197,49 +278,56 @@ __global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
 #pragma unroll
     for (int w = 0; w < HD / 32; ++w) den += redd[w];
     const float inv = (float)(1.0 / den);
-    for (int t = tid; t < ctx; t += HD) sc[t] = sc[t] * inv;
-    __syncthreads();
 
-    // 3. out_d: sequential FMA chain over the tokens
-    float out = 0.0f;
-    const size_t off = (size_t)kh * HD + tid;
-    int t = 0;
-    for (; t + kAttnUnroll <= ctx; t += kAttnUnroll) {
-        float v[kAttnUnroll], al[kAttnUnroll];
-#pragma unroll
-        for (int u = 0; u < kAttnUnroll; ++u) {
-            const size_t slot = slot_of(a, s, t + u);
-            al[u] = sc[t + u];
-            if (a.kv_type == 1) v[u] = half_bits_to_float(reinterpret_cast<const uint16_t*>(vp)[slot * kv_dim + off]);
-            else if (a.kv_type == 0) v[u] = reinterpret_cast<const float*>(vp)[slot * kv_dim + off];
-            else {
-                v[u] = (float)reinterpret_cast<const int8_t*>(vp)[slot * kv_dim + off];
-                al[u] = al[u] * (a.kv_type == 2 ? a.v_scales[slot] : a.v_scales[slot * (kv_dim / 32) + off / 32]);
+    // 3. thread d: out_d = fma(alpha_t, v_t[d], out_d) over t in order; V
+    //    tiles of kVTile tokens staged by all threads through a kVStages ring.
+    const int chunks = kVTile * slice / 16;  // 16-byte copies per tile
+    const int ntile = (ctx + kVTile - 1) / kVTile;
+    auto issue_v = [&](int tile) {
+        if (tile < ntile) {
+            uint8_t* dst = ring + (size_t)(tile % kVStages) * kVTile * slice;
+            for (int c = tid; c < chunks; c += HD) {
+                const int tt = c / (slice / 16), off = (c % (slice / 16)) * 16;
+                const int t = tile * kVTile + tt;
+                if (t < ctx) cp_async16(dst + tt * slice + off, vp + slot_of(t) * row_bytes + head_off + off);
             }
         }
-#pragma unroll
-        for (int u = 0; u < kAttnUnroll; ++u) out = fmaf(al[u], v[u], out);
-    }
-    for (; t < ctx; ++t) {
-        const size_t slot = slot_of(a, s, t);
-        float al = sc[t], v;
-        if (a.kv_type == 1) v = half_bits_to_float(reinterpret_cast<const uint16_t*>(vp)[slot * kv_dim + off]);
-        else if (a.kv_type == 0) v = reinterpret_cast<const float*>(vp)[slot * kv_dim + off];
-        else {
-            v = (float)reinterpret_cast<const int8_t*>(vp)[slot * kv_dim + off];
-            al = al * (a.kv_type == 2 ? a.v_scales[slot] : a.v_scales[slot * (kv_dim / 32) + off / 32]);
+        cp_async_commit();
+    };
+    for (int k = 0; k < kVStages - 1; ++k) issue_v(k);
+    float out = 0.0f;
+    for (int tile = 0; tile < ntile; ++tile) {
+        cp_async_wait<kVStages - 2>();
+        __syncthreads();  // the tile is visible to every thread
+        const uint8_t* vt = ring + (size_t)(tile % kVStages) * kVTile * slice;
+        const int n = min(kVTile, ctx - tile * kVTile);
+        for (int tt = 0; tt < n; ++tt) {
+            const int t = tile * kVTile + tt;
+            float al = sc[t] * inv;  // alpha_t = e_t * float(1/den)
+            float v;
+            if (kvt == 1) v = half_bits_to_float(reinterpret_cast<const uint16_t*>(vt + tt * slice)[tid]);
+            else if (kvt == 0) v = reinterpret_cast<const float*>(vt + tt * slice)[tid];
+            else {
+                v = (float)reinterpret_cast<const int8_t*>(vt + tt * slice)[tid];
+                al = al * (kvt == 2 ? vsc[t] : vsc[t * (HD / 32) + tid / 32]);
+            }
+            out = fmaf(al, v, out);
         }
-        out = fmaf(al, v, out);
+        __syncthreads();  // everyone is done with this stage before it is refilled
+        issue_v(tile + kVStages - 1);
     }
+    cp_async_wait<0>();
     a.out[((size_t)s * a.n_head + h) * HD + tid] = out;
 }
 
-uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx) { return (hd + max_ctx) * sizeof(float); }
+uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type) {
+    return attn_plan(hd, max_ctx, max_pages, kv_type).total;
+}
 
 cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s) {
     if (!a.n_seq) return cudaSuccess;
     if (a.n_head % a.n_head_kv) return cudaErrorInvalidValue;
-    const size_t smem = attn_smem_bytes(a.hd, a.max_ctx ? a.max_ctx : 1);
+    const size_t smem = attn_smem_bytes(a.hd, a.max_ctx ? a.max_ctx : 1, a.max_pages, a.kv_type);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     dim3 grid((unsigned)a.n_seq, (unsigned)a.n_head);
     switch (a.hd) {

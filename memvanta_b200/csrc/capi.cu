@@ -391,7 +391,8 @@ MV_API int mv_paged_attn_decode(int kv_type, const float* q, uint64_t n_seq, uin
     if (hd != 64 && hd != 128 && hd != 256) return fail(MV_ERR_UNSUPPORTED, "head_dim must be 64, 128 or 256");
     if (!page) return fail(MV_ERR_INVALID, "page must be > 0");
     if (n_seq == 0) return MV_OK;
-    if (mvb::attn_smem_bytes(hd, max_ctx) > 200 * 1024) return fail(MV_ERR_INVALID, "max_ctx too large");
+    if (mvb::attn_smem_bytes(hd, max_ctx ? max_ctx : 1, max_pages, kv_type) > 200 * 1024)
+        return fail(MV_ERR_INVALID, "max_ctx too large for one attention CTA");
     mvb::AttnArgs a{kv_type, q, n_head * hd, n_seq, n_head, n_head_kv, hd, k_pages, v_pages, k_scales, v_scales,
                     block_table, max_pages, page, ctx_len, max_ctx ? max_ctx : 1, out};
     CK(mvb::paged_attn_decode(a, as_stream(stream)));

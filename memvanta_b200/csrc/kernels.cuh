@@ -85,7 +85,7 @@ struct AttnArgs {
     uint64_t max_ctx;        // upper bound of ctx_len (sizes shared memory)
     float* out;              // [n_seq][n_head*hd]
 };
-uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx);
+uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type);
 cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s);
 
 }  // namespace mvb

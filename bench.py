@@ -4,6 +4,11 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
 Workloads:
+  llama7b   config 3 (default) -- random-init OpenLLaMA-7B-shaped Q4_0 Llama
+            (Q6_K head), F16 paged KV, ctx 768.  One step = one greedy decode
+            token; the K timed steps run from position 128 after a 128-token
+            seed prefill, so K = 128 is the reference's tg128.  pp512 (prefill
+            batch 32) is timed in the same run and reported beside it.
   q4_gemv   config 0 -- one step = 32 Q4_0 x Q8 GEMVs, one over each of 32
             copies of a 4096x4096 weight (303 MB, 2.4x the 126 MB L2, so every
             launch streams its weight from HBM), metric HBM GB/s.
@@ -254,20 +259,176 @@ def run_q4_gemv_cpu(seconds=8.0):
             "sample": f"{n} tensor_matvec calls on one 4096x4096 Q4_0 weight (oracle/_ref, {threads} threads)"}
 
 
+# ------------------------------------------------------ llama7b (config 3)
+
+L7_PATH = os.environ.get("MV_BENCH_GGUF", "/tmp/memvanta_b200_rand7b_seed1234.gguf")
+L7_CTX, L7_SEED_TOKENS, L7_PP, L7_BATCH = 768, 128, 512, 32
+# bytes one decode token reads: every Q4_0 layer weight and the Q6_K head once
+L7_LAYER_W = 4 * 4096 * 4096 // 32 * 18 + 3 * 11008 * 4096 // 32 * 18
+L7_HEAD_W = 32000 * 4096 // 256 * 210
+
+
+def fixed_tokens(n, vocab=32000, offset=0):
+    """The reference bench's prompt ids, (i*1543+17) % vocab
+    (benchmarks/real_model_bench.cpp:18)."""
+    return ((np.arange(offset, offset + n) * 1543 + 17) % vocab).astype(np.int32)
+
+
+def ensure_llama7b():
+    from memvanta_b200 import gguf
+    if not os.path.exists(L7_PATH):
+        tmp = L7_PATH + f".tmp{os.getpid()}"
+        gguf.write_random_llama(tmp, gguf.LLAMA_7B, seed=1234)
+        os.replace(tmp, L7_PATH)
+    return L7_PATH
+
+
+def gemv_roofline(dev, stream):
+    """Live timing of the decode GEMV (the dominant kernel) on the four decode
+    shapes, weighted as one token uses them: per layer q|k|v 12288x4096,
+    o 4096x4096, gate|up 22016x4096 (SiLU pairs), down 4096x11008."""
+    import torch
+    import memvanta_b200 as mv
+    from memvanta_b200 import gguf
+    rng = np.random.default_rng(7)
+    total_bytes, total_s, detail = 0, 0.0, {}
+    for name, rows, cols in [("qkv", 12288, 4096), ("o", 4096, 4096), ("gate_up", 22016, 4096), ("down", 4096, 11008)]:
+        copies = max(2, int(np.ceil(3 * 126e6 / (rows * cols / 32 * 18))))  # > L2 in total
+        ws = [mv.Weight.upload(gguf.gen_q4_0(rows, cols, rng), mv.Q4_0, rows, cols) for _ in range(copies)]
+        x = torch.randn(cols, device=dev)
+        y = torch.empty(rows, device=dev)
+        n = 8 * copies
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            mv.gemv(ws[0], x, y, stream)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(n):
+                    mv.gemv(ws[i % copies], x, y, stream)
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        per = e0.elapsed_time(e1) / 1e3 / n
+        alg = rows * cols // 32 * 18 + cols * 4 + rows * 4
+        detail[name] = {"rows": rows, "cols": cols, "us_per_launch": round(per * 1e6, 2),
+                        "gbs": round(alg / per / 1e9, 1)}
+        total_bytes += alg
+        total_s += per
+        for w in ws:
+            w.free()
+        del g
+    return total_bytes / total_s / 1e9, total_bytes, total_s, detail
+
+
+def run_llama7b_ours(args, world, rank, local):
+    import torch
+    import memvanta_b200 as mv
+    mv.init(local)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    path = ensure_llama7b()
+    m = mv.LlamaModel(path, ctx_override=L7_CTX, kv_page_tokens=16, kv_type=mv.KV_F16)
+    ms = torch.cuda.ExternalStream(m.stream)
+    K, W = args.steps, args.warmup
+    if L7_SEED_TOKENS + max(K, W) > L7_CTX:
+        raise SystemExit(f"--steps/--warmup above {L7_CTX - L7_SEED_TOKENS} exceed the ctx {L7_CTX} run")
+    seed = fixed_tokens(L7_SEED_TOKENS)
+    # warm-up: a full sequence of W decode steps (graphs, clocks, caches)
+    m.reset()
+    m.prefill(seed, L7_BATCH, False)
+    m.generate_greedy(17, W)
+    # timed: K greedy decode steps from position 128 (tg128 when K = 128)
+    m.reset()
+    m.prefill(seed, L7_BATCH, False)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0.record(ms)
+        toks = m.generate_greedy(17, K)
+        e1.record(ms)
+        torch.cuda.synchronize()
+    tg_ms = e0.elapsed_time(e1)
+    tg_ms = all_max(tg_ms, world)
+    # pp512: prefill of the 512-token prompt in batches of 32, one timed call
+    prompt = fixed_tokens(L7_PP)
+    m.reset()
+    m.prefill(prompt[:L7_BATCH], L7_BATCH, True)
+    m.reset()
+    torch.cuda.synchronize()
+    barrier(world)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(ms)
+    m.prefill(prompt, L7_BATCH, True)
+    p1.record(ms)
+    torch.cuda.synchronize()
+    pp_ms = all_max(p0.elapsed_time(p1), world)
+    # e2e: the reference contract -- forward(token) returns host logits, the
+    # caller samples greedily on the host (real_model_bench tg loop)
+    m.reset()
+    m.prefill(seed, L7_BATCH, False)
+    for _ in range(3):
+        m.forward(17)
+    m.reset()
+    m.prefill(seed, L7_BATCH, False)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    cur = 17
+    for _ in range(K):
+        cur = int(np.argmax(m.forward(cur)))
+    e2e_s = all_max(time.perf_counter() - t0, world)
+    kernels_per_step = 1 + 6 * m.n_layer + 2
+    m.close()
+    gbs, alg_bytes, gemv_s, detail = gemv_roofline(dev, torch.cuda.Stream(device=dev))
+    return {"tg_ms": tg_ms, "pp_ms": pp_ms, "e2e_s": e2e_s, "clocks": clk.summary(),
+            "gpu_launches": K * kernels_per_step + 1, "first_tokens": [int(t) for t in toks[:8]],
+            "gemv_gbs": gbs, "gemv_detail": detail}
+
+
+def run_llama7b_cpu(threads=None, prompt=32, gen=8):
+    """The reference's own memvanta_real_bench (oracle/_ref, built from the
+    unmodified sources) on this host's cores: pp<prompt> and tg<gen> tok/s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import REF_REAL_BENCH
+    path = ensure_llama7b()
+    threads = threads or cpu_threads()
+    cmd = [REF_REAL_BENCH, "--model", path, "--threads", str(threads), "--ctx", str(L7_CTX), "--prompt", str(prompt),
+           "--gen", str(gen), "--batch", str(L7_BATCH), "--kv", "f16", "--warmup", "0", "--reps", "1", "--no-client"]
+    out = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+    if out.returncode != 0:
+        raise RuntimeError(f"reference bench failed: {out.stderr.strip()[-300:]}")
+    vals = {}
+    for line in out.stdout.splitlines():
+        parts = [p.strip() for p in line.split("|")]
+        if len(parts) > 7 and (parts[6].startswith("pp") or parts[6].startswith("tg")):
+            vals[parts[6][:2]] = float(parts[7].split()[0])
+    return {"tg": vals.get("tg"), "pp": vals.get("pp"), "threads": threads,
+            "sample": f"memvanta_real_bench --prompt {prompt} --gen {gen} --batch {L7_BATCH} --ctx {L7_CTX} --kv f16 "
+                      f"--threads {threads} on the same random 7B GGUF (tg after a 128-token seed prefill)"}
+
+
 # -------------------------------------------------------------------- main
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="q4_gemv", choices=["q4_gemv"])
+    ap.add_argument("--workload", default="llama7b", choices=["llama7b", "q4_gemv"])
     ap.add_argument("--clock-window", type=float, default=0.5)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup()
+    if args.workload == "llama7b":
+        return main_llama7b(args, world, rank, local)
     metric, unit = "Q4_0 GEMV achieved HBM GB/s (config 0, 4096x4096)", "GB/s"
     config = {"workload": "config0: Q4_0xQ8 GEMV 4096x4096, x~N(0,1), 32 rotated weight copies (303 MB > 126 MB L2)",
               "rows": Q4_ROWS, "cols": Q4_COLS, "l2": "inputs rotated across 32 weight copies (303 MB, 2.4x L2)",
@@ -312,6 +473,68 @@ def main():
                 "d2h_bytes_per_step": Q4_ROWS * 4,
                 "path": "mv_tensor_matvec_host (host x/y, H2D + GEMV + D2H + sync per call)"},
         "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["gpu_launches"],
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main_llama7b(args, world, rank, local):
+    metric, unit = "7B Q4_0 tg128 tok/s", "tok/s"
+    config = {"workload": f"config3: random-init OpenLLaMA-7B-shaped Llama, Q4_0 layers + Q6_K head, F16 paged KV "
+                          f"(16-token pages), ctx {L7_CTX}; {args.steps} greedy decode tokens from position "
+                          f"{L7_SEED_TOKENS}; pp512 = 512-token prompt prefilled in batches of {L7_BATCH}",
+              "model": "llama-7b-shape (32L, d4096, 32h x 128, ffn 11008, vocab 32000)",
+              "global_batch": 1, "seq_len": L7_CTX, "parallelism": f"replicas x{world}",
+              "l2": "decode reads 3.75 GB of weights per token (30x the 126 MB L2)"}
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cpu = run_llama7b_cpu()
+        line = {"impl": "reference", "metric": metric, "value": cpu["tg"], "unit": unit, "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "q4_0/q8",
+                "data": "synthetic", "config": config, "pp_tok_s": cpu["pp"],
+                "cpu_baseline": {"value": cpu["tg"], "unit": unit, "cores": cpu["threads"], "kind": "reference",
+                                 "sample": cpu["sample"]},
+                "e2e": {"value": cpu["tg"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    import torch
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    r = run_llama7b_ours(args, world, rank, local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peaks = measured_peaks()
+    cpu = None
+    if world == 1:
+        c = run_llama7b_cpu()
+        cpu = {"value": c["tg"], "unit": unit, "cores": c["threads"], "kind": "reference", "sample": c["sample"],
+               "pp_tok_s": c["pp"]}
+    tg = args.steps / (r["tg_ms"] / 1e3)
+    pp = L7_PP / (r["pp_ms"] / 1e3)
+    bytes_per_token = 32 * L7_LAYER_W + L7_HEAD_W
+    line = {
+        "metric": metric, "value": round(tg * world, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["tg_ms"] / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x q8 (int8 dot, fp32 accumulate)",
+        "data": "synthetic (random-init weights, seeded)", "config": config,
+        "pp512_tok_s": round(pp * world, 2), "pp512_ms": round(r["pp_ms"], 2),
+        "decode_weight_bw_gbs": round(bytes_per_token * tg / 1e9, 1),
+        "roofline": {"bound": "hbm", "kernel": "mvb::gemv_q4_kernel (Q4_0 x Q8 decode GEMV)",
+                     "achieved": round(r["gemv_gbs"], 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(r["gemv_gbs"] / peaks["hbm_gbs"], 4), "traffic": traffic_from_profiles("gemv_q4"),
+                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, burst)",
+                     "shapes": r["gemv_detail"]},
+        "e2e": {"value": round(args.steps / r["e2e_s"] * world, 2), "unit": unit, "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 32000 * 4,
+                "path": "LlamaModel.forward (mv_model_forward): token in, host logits out, host argmax per token"},
+        "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["gpu_launches"],
+        "first_tokens": r["first_tokens"],
     }
     print(json.dumps(line), flush=True)
 

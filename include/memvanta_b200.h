@@ -103,6 +103,18 @@ MV_API int mv_gemv(mv_weight_t w, const float* x_dev, float* y_dev, void* stream
  * include/memvanta/gguf_kernels.hpp:30) and tensor_matmul_batch (:255-259). */
 MV_API int mv_gemm(mv_weight_t w, const float* x_dev, uint64_t batch, float* y_dev, int act_mode, void* stream);
 
+/* mv_gemm(w, x, batch, y, MV_ACT_Q8, stream) for a Q4_0 weight, with the
+ * same result, for callers that must not allocate device memory while they
+ * run (a framework whose own pool owns all GPU memory, a fixed memory budget,
+ * a latency-critical loop).  No counterpart in the reference.  The quantised
+ * activations go to one 8 MiB array compiled into the library, held on every
+ * GPU that loads it until the process exits, so batch * cols * 1.125 bytes
+ * must fit in 8 MiB (larger calls return MV_ERR_INVALID).  The first call on a
+ * device looks the array's address up (cudaGetSymbolAddress): make it before
+ * any stream capture.  Calls that overlap on the GPU share the array and race;
+ * the caller serialises them.  Allocates nothing, frees nothing. */
+MV_API int mv_gemm_q8_noalloc(mv_weight_t w, const float* x_dev, uint64_t batch, float* y_dev, void* stream);
+
 /* Per-row Q8 activation quantisation: q[rows*cols] int8, d[rows*cols/32] fp32.
  * Replaces quantize_q8 / quantize_activations_q8
  * (src/gguf_kernels.cpp:161-178). */

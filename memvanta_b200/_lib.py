@@ -37,6 +37,7 @@ SIGNATURES = {
     "mv_weight_download": (_i, [_p, _p, _u64]),
     "mv_gemv": (_i, [_p, _p, _p, _p]),
     "mv_gemm": (_i, [_p, _p, _u64, _p, _i, _p]),
+    "mv_gemm_q8_noalloc": (_i, [_p, _p, _u64, _p, _p]),
     "mv_quantize_q8": (_i, [_p, _u64, _u64, _p, _p, _p]),
     "mv_q4_0_block_dots": (_i, [_p, _p, _p, _p]),
     "mv_read_row": (_i, [_p, _u64, _p, _p]),

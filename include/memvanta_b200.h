@@ -68,6 +68,11 @@ typedef struct mv_model_s* mv_model_t;
 MV_API int mv_init(int device);
 MV_API const char* mv_last_error(void);
 MV_API int mv_version(void);
+/* Synchronises `stream` and reports MV_ERR_TIMEOUT if a tensor-core kernel
+ * (mv_gemm with MV_ACT_Q8, model prefill) gave up a bounded device-side wait
+ * since the last check -- its outputs are then invalid.  Host-pointer calls
+ * and the model check this themselves.  No counterpart in the reference. */
+MV_API int mv_stream_status(void* stream);
 
 /* ------------------------------------------------------------ weights */
 
@@ -96,9 +101,10 @@ MV_API int mv_weight_download(mv_weight_t w, void* host_blocks, uint64_t nbytes)
 MV_API int mv_gemv(mv_weight_t w, const float* x_dev, float* y_dev, void* stream);
 
 /* Y[batch,rows] = X[batch,cols] W^T.  act_mode MV_ACT_Q8 is the reference's
- * MEMVANTA_FORCE_Q8_ACT=1 path (Q4_0 rows with Q8 activations; Q8_0 keeps
- * fp32 activations); MV_ACT_F32 is its default fp32-activation path.  Q6_K,
- * F16 and F32 always take fp32 activations, as tensor_matmul_batch does.
+ * MEMVANTA_FORCE_Q8_ACT=1 path (Q4_0 rows with Q8 activations, batch >= 2, on
+ * the tensor cores, bit-exact with the reference; Q8_0 keeps fp32
+ * activations); MV_ACT_F32 is its default fp32-activation path.  Q6_K, F16
+ * and F32 always take fp32 activations, as tensor_matmul_batch does.
  * Replaces tensor_matmul_batch_v06 (src/gguf_kernels.cpp:261-271,
  * include/memvanta/gguf_kernels.hpp:30) and tensor_matmul_batch (:255-259). */
 MV_API int mv_gemm(mv_weight_t w, const float* x_dev, uint64_t batch, float* y_dev, int act_mode, void* stream);
@@ -108,8 +114,9 @@ MV_API int mv_gemm(mv_weight_t w, const float* x_dev, uint64_t batch, float* y_d
  * run (a framework whose own pool owns all GPU memory, a fixed memory budget,
  * a latency-critical loop).  No counterpart in the reference.  The quantised
  * activations go to one 8 MiB array compiled into the library, held on every
- * GPU that loads it until the process exits, so batch * cols * 1.125 bytes
- * must fit in 8 MiB (larger calls return MV_ERR_INVALID).  The first call on a
+ * GPU that loads it until the process exits, so batch * cols bytes of int8
+ * values plus (cols / 32) * round_up(batch, 64) * 8 bytes of scales must fit
+ * in 8 MiB (larger calls return MV_ERR_INVALID).  The first call on a
  * device looks the array's address up (cudaGetSymbolAddress): make it before
  * any stream capture.  Calls that overlap on the GPU share the array and race;
  * the caller serialises them.  Allocates nothing, frees nothing. */

@@ -143,6 +143,12 @@ def gemm(w: Weight, x, y, act_mode: int = ACT_Q8, stream=None) -> None:
                          _stream(stream)))
 
 
+def stream_status(stream=None) -> None:
+    """Synchronise the stream; raise MV_ERR_TIMEOUT if a tensor-core kernel
+    gave up a bounded device-side wait since the last check."""
+    check(load().mv_stream_status(_stream(stream)))
+
+
 def quantize_q8(x, stream=None):
     import torch
     rows, cols = (1, x.numel()) if x.dim() == 1 else tuple(x.shape)

@@ -290,16 +290,26 @@ MV_API int mv_gemm(mv_weight_t w, const float* x, uint64_t batch, float* y, int 
         CK(mvb::matmul_f32act(*w, x, batch, y, s));
         return MV_OK;
     }
-    // Q4_0 with Q8 activations: per-row quantisation into stream-ordered scratch.
+    // Q4_0 with Q8 activations: per-row quantisation into stream-ordered
+    // scratch (scales block-major), then the tensor-core GEMM.
+    const uint64_t ldb = mvb::gemm_tc_ldb(batch);
     int8_t* q = nullptr;
     float* d = nullptr;
     CK(cudaMallocAsync(reinterpret_cast<void**>(&q), batch * w->cols, s));
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&d), batch * (w->cols / 32) * sizeof(float), s);
-    if (e == cudaSuccess) e = mvb::quantize_q8_rows(x, batch, w->cols, q, d, s);
-    if (e == cudaSuccess) e = mvb::gemm_q4_q8(*w, q, d, batch, y, s);
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&d), 2 * (w->cols / 32) * ldb * sizeof(float), s);
+    if (e == cudaSuccess) e = mvb::quantize_q8_rows_t(x, batch, w->cols, q, d, ldb, s);
+    if (e == cudaSuccess) e = mvb::gemm_q4_q8_tc(*w, q, d, ldb, batch, y, s);
     cudaFreeAsync(q, s);
     if (d) cudaFreeAsync(d, s);
-    if (e != cudaSuccess) return cuda_fail(e, "gemm_q4_q8");
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_q4_q8_tc");
+    return MV_OK;
+}
+
+MV_API int mv_stream_status(void* stream) {
+    int status = 0;
+    CK(mvb::tc_status(as_stream(stream), &status));
+    if (status) return fail(MV_ERR_TIMEOUT, "a tensor-core kernel gave up a bounded wait (site " +
+                                                std::to_string(status) + "); its outputs are invalid");
     return MV_OK;
 }
 
@@ -428,8 +438,7 @@ MV_API int mv_tensor_matmul_batch_host(mv_weight_t w, const float* x_host, float
     CK(cudaMemcpyAsync(x, x_host, batch * w->cols * sizeof(float), cudaMemcpyHostToDevice, s));
     if (int rc = mv_gemm(w, x, batch, y, act_mode, s)) return rc;
     CK(cudaMemcpyAsync(y_host, y, batch * w->rows * sizeof(float), cudaMemcpyDeviceToHost, s));
-    CK(cudaStreamSynchronize(s));
-    return MV_OK;
+    return mv_stream_status(s);
 }
 
 MV_API int mv_tensor_read_row_host(mv_weight_t w, uint64_t row, float* out_host) {

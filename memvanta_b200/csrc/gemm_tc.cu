@@ -1,0 +1,522 @@
+// gemm_tc.cu -- batched Q4_0 x Q8-activation matmul (prefill) on the
+// 5th-generation tensor cores: tcgen05 int8 MMA into TMEM, fed by TMA, with
+// the per-block fp16 weight scales and fp32 activation scales applied in the
+// epilogue.
+//
+// Numerics are the reference's MEMVANTA_FORCE_Q8_ACT=1 prefill
+// (tensor_matmul_batch_v06, src/gguf_kernels.cpp:265-266): every activation
+// row is quantised per 32-element block (quantize_activations_q8, :174-178)
+// and every (token t, row r) output is the decode dot dot_q4_q8 (:189), a
+// sequential chain over the blocks b
+//     sum = fma(d_w[r,b] * d_a[t,b], float(isum[r,t,b]), sum),  sum = 0 first,
+// isum = sum_k (nib_k - 8) * q_k.  The integer block dots come from the
+// tensor cores: each block is ONE tcgen05.mma (M = 128 rows, N tokens, K = 32
+// = one block) into a TMEM slot of its own, so every slot holds the exact dot
+// of one block, and epilogue warps run the chain over the slots in block
+// order on the CUDA cores: every output equals the reference's bit for bit.
+//
+// Exact int -> float without integer instructions:
+//   * A is the raw nibble (u8, 0..15), B the Q8 value (s8), so the MMA yields
+//     D = isum + 8 * sum_k q_k.
+//   * Every slot is preset to the bit pattern 0x4B400000 (= 1.5 * 2^23 as a
+//     float) and the MMA accumulates onto it; |D| < 2^16, so the slot's bits
+//     read as a float are exactly 1.5 * 2^23 + D.
+//   * The quantiser stores c[t,b] = 1.5 * 2^23 + 8 * sum_k q_k (exact), and
+//     (1.5 * 2^23 + D) - c[t,b] = isum exactly (both in [2^23, 2^24)).
+//   So the epilogue spends one FADD, one FMUL and one FFMA per (row, token,
+//   block), and a tcgen05.st puts the preset back after reading a slot.
+//
+// Layouts (per pipeline stage of G = 4 blocks, 128 rows, N tokens; all
+// 16-byte chunks XOR-swizzled by their row as TMA lays them out):
+//   raw  [128 rows][64 B]    the Q4_0 nibble bytes of 4 blocks, one 2-D TMA
+//                            box over the [rows][nb*16 B] payload plane,
+//                            64-byte swizzle (chunk j of row i at j^((i>>1)&3))
+//   A8   [128 rows][128 B]   the nibbles one per byte, K-major, 128-byte
+//                            swizzle (chunk j at j^(i&7)), 8-row groups 1024 B
+//                            apart; block g is the 32-byte K slice at +32 g
+//   B    [N][128 B]          the Q8 activations of the 4 blocks in the same
+//                            form, landed directly by one 2-D TMA box
+// Epilogue data, per group of 16 blocks, in a ring of 4 slots the producer
+// fills well ahead of use:
+//   dw   [128 rows][32 B]    the fp16 weight scales, 2-D TMA box over the
+//                            [rows][dstride] plane, 32-byte swizzle
+//   sc   [2][16][N]          the activation scales and the constants c
+//                            (block-major [nb][ldb] each, tokens padded to 64)
+//
+// Warp roles (one CTA per SM, persistent over 128-row x N-token tiles):
+//   warp 0       TMA producer (one lane): stages and epilogue data
+//   warps 1-2    MMA issuers (one lane each, alternate stages); warp 1 also
+//                allocates TMEM (whole warp)
+//   warps 3-6    converters: nibble bytes -> one nibble per byte, one row per thread
+//   warps 7-14   epilogue: TMEM -> registers -> chain -> y; warp w reads TMEM
+//                lanes 32*(w%4).. (its row quadrant), token half (w-7)/4
+// Rings: S smem stages (full: TMA bytes landed; conv: A8 written; empty: MMAs
+// done reading), 512/(G*N) TMEM stage groups (tfull: MMAs done; tempty:
+// epilogue read them and restored the preset) and 4 epilogue-data slots
+// (efull: TMA bytes landed; eempty: epilogue done).  Every wait is bounded
+// (tc.cuh).
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "tc.cuh"
+
+namespace mvb {
+
+__device__ int g_tc_status = 0;
+
+cudaError_t tc_status(cudaStream_t s, int* status) {
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return e;
+    int v = 0;
+    e = cudaMemcpyFromSymbol(&v, g_tc_status, sizeof(int));
+    if (e == cudaSuccess && v != 0) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_tc_status, &zero, sizeof(int));
+    }
+    *status = v;
+    return e;
+}
+
+uint64_t gemm_tc_ldb(uint64_t batch) { return (batch + 63) / 64 * 64; }
+
+namespace {
+
+constexpr int kM = 128;  // weight rows per tile = TMEM lanes
+constexpr int kG = 4;    // Q4_0 blocks per pipeline stage
+constexpr int kMmaWarps = 2;  // MMA issuers, alternating stages
+constexpr int kConvWarps = 4;
+constexpr int kConvWarp0 = 1 + kMmaWarps;
+constexpr int kEpiWarp0 = kConvWarp0 + kConvWarps;
+constexpr uint32_t kPreset = 0x4B400000u;  // 1.5 * 2^23 as a float
+constexpr int kEB = 16;                    // blocks per epilogue-data slot
+constexpr int kES = 4;                     // epilogue-data slots
+
+template <int N>
+struct Cfg {
+    static constexpr int kEW = 2;       // epilogue warps per TMEM lane quadrant
+    static constexpr int kTT = N / kEW;  // tokens per epilogue thread
+    static constexpr int kEpiWarps = 4 * kEW;
+    static constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
+    static constexpr int kRaw = kM * kG * 16;  // [128][64 B]
+    static constexpr int kA8 = kM * kG * 32;   // [128][128 B]
+    static constexpr int kB = N * kG * 32;     // [N][128 B]
+    static constexpr int kStage = kRaw + kA8 + kB;
+    static constexpr int kS = (224 * 1024 - kES * (kM * kEB * 2 + 2 * kEB * N * 4)) / kStage < 8
+                                  ? (224 * 1024 - kES * (kM * kEB * 2 + 2 * kEB * N * 4)) / kStage
+                                  : 8;
+    static constexpr int kTG = 512 / (kG * N);
+    static constexpr int kDw = kM * kEB * 2;                // weight scales [128][16] fp16
+    static constexpr int kEpi = kDw + 2 * kEB * N * 4;      // + [2][16][N] fp32: scales, constants c
+    static constexpr int kEpiOff = kS * kStage;
+    static constexpr int kBarOff = kEpiOff + kES * kEpi;
+    static constexpr int kBars = 3 * kS + 2 * kTG + 2 * kES + 1;
+    static constexpr int kSmem = kBarOff + kBars * 8 + 16 + 1024;  // + alignment slack
+    static constexpr int kLdBlocks = 32 / kTT;                     // blocks per TMEM load batch
+    static_assert(kG % kLdBlocks == 0, "load batches must tile a stage");
+    static_assert(kTG >= 2, "two TMEM stage groups at least");
+    static_assert(kStage % 1024 == 0 && kEpi % 1024 == 0, "swizzled TMA tiles need 1024-byte alignment");
+    static_assert(kEB % kG == 0, "a data slot covers whole stages");
+};
+
+struct TcArgs {
+    float* y;  // [batch][rows]
+    int rows, nb, batch, n_ttiles, n_tiles, accumulate;
+};
+
+template <int TT>
+__device__ __forceinline__ void tmem_load(uint32_t taddr, uint32_t (&v)[TT]) {
+    if constexpr (TT == 8) {
+        tc::tmem_ld8(taddr, v);
+    } else if constexpr (TT == 16) {
+        tc::tmem_ld16(taddr, v);
+    } else {
+        tc::tmem_ld32(taddr, v);
+    }
+}
+template <int TT>
+__device__ __forceinline__ void tmem_preset(uint32_t taddr) {
+    if constexpr (TT == 8) {
+        tc::tmem_fill8(taddr, kPreset);
+    } else if constexpr (TT == 16) {
+        tc::tmem_fill16(taddr, kPreset);
+    } else {
+        tc::tmem_fill32(taddr, kPreset);
+    }
+}
+
+template <int N>
+__global__ void __launch_bounds__(Cfg<N>::kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                   const __grid_constant__ CUtensorMap dmap, const __grid_constant__ CUtensorMap smap,
+                   const TcArgs a) {
+    using C = Cfg<N>;
+    constexpr int TT = C::kTT, LB = C::kLdBlocks;
+    extern __shared__ unsigned char smem_dyn[];
+    const uint32_t s0 = tc::smem_u32(smem_dyn);
+    const uint32_t pad = ((s0 + 1023u) & ~1023u) - s0;
+    unsigned char* const sm = smem_dyn + pad;
+    const uint32_t sbase = s0 + pad;
+    const uint32_t bars = sbase + C::kBarOff;
+    const auto full_bar = [&](int s) { return bars + 8u * s; };
+    const auto conv_bar = [&](int s) { return bars + 8u * (C::kS + s); };
+    const auto empty_bar = [&](int s) { return bars + 8u * (2 * C::kS + s); };
+    const auto tfull_bar = [&](int g) { return bars + 8u * (3 * C::kS + g); };
+    const auto tempty_bar = [&](int g) { return bars + 8u * (3 * C::kS + C::kTG + g); };
+    const auto efull_bar = [&](int e) { return bars + 8u * (3 * C::kS + 2 * C::kTG + e); };
+    const auto eempty_bar = [&](int e) { return bars + 8u * (3 * C::kS + 2 * C::kTG + kES + e); };
+    const uint32_t done_bar = bars + 8u * (3 * C::kS + 2 * C::kTG + 2 * kES);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kBarOff + C::kBars * 8);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + C::kBarOff + C::kBars * 8 + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool epi = warp >= kEpiWarp0;
+    const int quad = warp & 3;                  // epilogue: TMEM lanes 32*quad .. +31
+    const int slice = (warp - kEpiWarp0) >> 2;  // epilogue: tokens slice*TT .. +TT-1 of a tile
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kS; ++s) {
+            tc::mbar_init(full_bar(s), 1);
+            tc::mbar_init(conv_bar(s), kConvWarps);
+            tc::mbar_init(empty_bar(s), 1);
+        }
+        for (int g = 0; g < C::kTG; ++g) {
+            tc::mbar_init(tfull_bar(g), 1);
+            tc::mbar_init(tempty_bar(g), C::kEpiWarps);
+        }
+        for (int e = 0; e < kES; ++e) {
+            tc::mbar_init(efull_bar(e), 1);
+            tc::mbar_init(eempty_bar(e), C::kEpiWarps);
+        }
+        tc::mbar_init(done_bar, kMmaWarps);
+        *abort_flag = 0;
+        tc::mbar_fence_init();
+        tc::tma_prefetch_map(&wmap);
+        tc::tma_prefetch_map(&xmap);
+        tc::tma_prefetch_map(&dmap);
+        tc::tma_prefetch_map(&smap);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tc::smem_u32(tmem_slot), 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + slice * TT;  // epilogue's TMEM corner
+    if (epi) {
+        // preset every slot this warp reads (its lanes x its token columns)
+        for (int col = 0; col < 512; col += N) tmem_preset<TT>(tl + col);
+        tc::tmem_wait_st();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+
+    if (warp == 0) {
+        // ---------------------------------------------------- TMA producer
+        if (lane == 0) {
+            uint32_t k = 0, j = 0;  // stages, epilogue-data groups issued
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+                const int row0 = (tile / a.n_ttiles) * kM, t0 = (tile % a.n_ttiles) * N;
+                for (int b0 = 0; b0 < a.nb; b0 += kG) {
+                    if (b0 % kEB == 0) {
+                        const int e = j % kES;
+                        if (!tc::mbar_wait(eempty_bar(e), ((j / kES) & 1u) ^ 1u, abort_flag, &g_tc_status, 10)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t ed = sbase + C::kEpiOff + e * C::kEpi;
+                        tc::mbar_expect_tx(efull_bar(e), C::kEpi);
+                        tc::tma_load_2d(ed, &smap, b0, row0, efull_bar(e));
+                        tc::tma_load_3d(ed + C::kDw, &dmap, t0, b0, 0, efull_bar(e));
+                        ++j;
+                    }
+                    const int s = k % C::kS;
+                    if (!tc::mbar_wait(empty_bar(s), ((k / C::kS) & 1u) ^ 1u, abort_flag, &g_tc_status, 1)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t st = sbase + s * C::kStage;
+                    tc::mbar_expect_tx(full_bar(s), C::kRaw + C::kB);
+                    tc::tma_load_2d(st, &wmap, b0 * 16, row0, full_bar(s));
+                    tc::tma_load_2d(st + C::kRaw + C::kA8, &xmap, b0 * 32, t0, full_bar(s));
+                    ++k;
+                }
+            }
+            // drain: the latest load of every slot has landed before the CTA exits
+            for (uint32_t i = k > (uint32_t)C::kS ? k - C::kS : 0; i < k; ++i)
+                tc::mbar_wait(full_bar(i % C::kS), (i / C::kS) & 1u, abort_flag, &g_tc_status, 2, false);
+            for (uint32_t i = j > (uint32_t)kES ? j - kES : 0; i < j; ++i)
+                tc::mbar_wait(efull_bar(i % kES), (i / kES) & 1u, abort_flag, &g_tc_status, 11, false);
+        }
+    } else if (warp <= kMmaWarps) {
+        // ---------------------------------------------------- MMA issuers
+        // Issuer i takes the stages k with k % kMmaWarps == i: the latency an
+        // issuing thread spends around its commits and waits overlaps.
+        const uint32_t mine = warp - 1;
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_u8s8(kM, N);
+            // descriptor of stage 0's A8 tile; B follows A8 by kA8 bytes in every stage
+            const uint64_t adesc0 = tc::sdesc_kmajor_sw128(sbase + C::kRaw);
+            uint32_t k = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+                for (int b0 = 0; b0 < a.nb; b0 += kG) {
+                    if (k % kMmaWarps != mine) {
+                        ++k;
+                        continue;
+                    }
+                    const int s = k % C::kS, tg = k % C::kTG;
+                    const uint32_t ph = (k / C::kS) & 1u;
+                    if (!tc::mbar_wait(full_bar(s), ph, abort_flag, &g_tc_status, 3) ||
+                        !tc::mbar_wait(conv_bar(s), ph, abort_flag, &g_tc_status, 4) ||
+                        !tc::mbar_wait(tempty_bar(tg), ((k / C::kTG) & 1u) ^ 1u, abort_flag, &g_tc_status, 5)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    // block g = the 32-byte K slice at +32 g: +2 in the descriptors' address field
+                    const uint64_t ad = adesc0 + (uint64_t)(s * (C::kStage >> 4));
+                    const uint32_t d0 = tmem + tg * (kG * N);
+                    if (b0 + kG <= a.nb) {
+#pragma unroll
+                        for (int g = 0; g < kG; ++g)
+                            tc::mma_i8(d0 + g * N, ad + 2 * g, ad + (C::kA8 >> 4) + 2 * g, idesc, 1u);
+                    } else {
+                        for (int g = 0; g < a.nb - b0; ++g)
+                            tc::mma_i8(d0 + g * N, ad + 2 * g, ad + (C::kA8 >> 4) + 2 * g, idesc, 1u);
+                    }
+                    tc::mma_commit(empty_bar(s));
+                    tc::mma_commit(tfull_bar(tg));
+                    ++k;
+                }
+            }
+            // every MMA issued has completed before TMEM is released
+            tc::mma_commit(done_bar);
+            tc::mbar_wait(done_bar, 0, abort_flag, &g_tc_status, 6, false);
+        }
+    } else if (!epi) {
+        // ------------------------------------------------------ converters
+        const int c = threadIdx.x - kConvWarp0 * 32;  // row of the tile
+        const int rsw = (c >> 1) & 3;    // 64-byte swizzle phase of raw row c
+        const int asw = c & 7;           // 128-byte swizzle phase of A8 row c
+        uint32_t k = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+            for (int b0 = 0; b0 < a.nb; b0 += kG) {
+                const int s = k % C::kS;
+                if (!__all_sync(0xffffffffu,
+                                tc::mbar_wait(full_bar(s), (k / C::kS) & 1u, abort_flag, &g_tc_status, 7))) {
+                    ok = false;
+                    break;
+                }
+                const unsigned char* raw = sm + s * C::kStage + c * 64;
+                unsigned char* a8 = sm + s * C::kStage + C::kRaw + c * 128;
+#pragma unroll
+                for (int g = 0; g < kG; ++g) {
+                    // GGUF order: byte i holds element i (low nibble) and 16 + i (high)
+                    const uint4 w = *reinterpret_cast<const uint4*>(raw + ((g ^ rsw) << 4));
+                    *reinterpret_cast<uint4*>(a8 + (((2 * g) ^ asw) << 4)) =
+                        make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
+                    *reinterpret_cast<uint4*>(a8 + (((2 * g + 1) ^ asw) << 4)) =
+                        make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
+                                   (w.w >> 4) & 0x0F0F0F0Fu);
+                }
+                tc::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(conv_bar(s));
+                ++k;
+            }
+        }
+    } else {
+        // -------------------------------------------------------- epilogue
+        const int rr = quad * 32 + lane;
+        const int dsw = (rr >> 2) & 1;  // 32-byte swizzle phase of this row's weight scales
+        uint32_t k = 0, j = 0;          // stages, epilogue-data groups consumed
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+            const int r = (tile / a.n_ttiles) * kM + rr;
+            const int tb = (tile % a.n_ttiles) * N + slice * TT;
+            float acc[TT];
+#pragma unroll
+            for (int t = 0; t < TT; ++t) acc[t] = 0.0f;
+            for (int b16 = 0; b16 < a.nb; b16 += kEB) {
+                const int e = j % kES;
+                if (!__all_sync(0xffffffffu,
+                                tc::mbar_wait(efull_bar(e), (j / kES) & 1u, abort_flag, &g_tc_status, 12))) {
+                    ok = false;
+                    break;
+                }
+                const unsigned char* ed = sm + C::kEpiOff + e * C::kEpi;
+                const uint4 w0 = *reinterpret_cast<const uint4*>(ed + rr * 32 + ((0 ^ dsw) << 4));
+                const uint4 w1 = *reinterpret_cast<const uint4*>(ed + rr * 32 + ((1 ^ dsw) << 4));
+                const uint32_t dwp[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                const float* da = reinterpret_cast<const float*>(ed + C::kDw);  // [16][N]
+                const float* cb = da + kEB * N;                                 // [16][N]
+#pragma unroll
+                for (int h = 0; h < kEB / kG; ++h) {  // the stages of this group
+                    const int b0 = b16 + h * kG;
+                    if (b0 >= a.nb) break;
+                    const int nblk = a.nb - b0;
+                    const int tg = k % C::kTG;
+                    // warp-uniform outcome: the TMEM accesses below are .sync.aligned
+                    if (!__all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(tg), (k / C::kTG) & 1u, abort_flag,
+                                                               &g_tc_status, 8))) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+#pragma unroll
+                    for (int gb = 0; gb < kG; gb += LB) {
+                        uint32_t v[LB][TT];
+#pragma unroll
+                        for (int i = 0; i < LB; ++i) tmem_load<TT>(tl + tg * (kG * N) + (gb + i) * N, v[i]);
+                        tc::tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < LB; ++i) tmem_preset<TT>(tl + tg * (kG * N) + (gb + i) * N);
+#pragma unroll
+                        for (int i = 0; i < LB; ++i) {
+                            const int g = gb + i;
+                            if (g < nblk) {
+                                const int eb = h * kG + g;  // block index in the group of 16
+                                const uint32_t word = dwp[eb >> 1];
+                                const float dw = half_bits_to_float((unsigned short)((eb & 1) ? word >> 16 : word));
+                                const float4* d4p = reinterpret_cast<const float4*>(da + eb * N + slice * TT);
+                                const float4* c4p = reinterpret_cast<const float4*>(cb + eb * N + slice * TT);
+#pragma unroll
+                                for (int t4 = 0; t4 < TT / 4; ++t4) {
+                                    const float4 d4 = d4p[t4], c4 = c4p[t4];
+                                    const uint32_t* vv = &v[i][4 * t4];
+                                    acc[4 * t4 + 0] = fmaf(dw * d4.x, __uint_as_float(vv[0]) - c4.x, acc[4 * t4 + 0]);
+                                    acc[4 * t4 + 1] = fmaf(dw * d4.y, __uint_as_float(vv[1]) - c4.y, acc[4 * t4 + 1]);
+                                    acc[4 * t4 + 2] = fmaf(dw * d4.z, __uint_as_float(vv[2]) - c4.z, acc[4 * t4 + 2]);
+                                    acc[4 * t4 + 3] = fmaf(dw * d4.w, __uint_as_float(vv[3]) - c4.w, acc[4 * t4 + 3]);
+                                }
+                            }
+                        }
+                    }
+                    tc::tmem_wait_st();
+                    tc::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(tempty_bar(tg));
+                    ++k;
+                }
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(eempty_bar(e));
+                ++j;
+            }
+            if (!ok) break;
+            if (r < a.rows) {
+#pragma unroll
+                for (int t = 0; t < TT; ++t) {
+                    if (tb + t < a.batch) {
+                        float* p = a.y + (size_t)(tb + t) * a.rows + r;
+                        *p = a.accumulate ? *p + acc[t] : acc[t];
+                    }
+                }
+            }
+        }
+    }
+
+    // teardown: every role is out of its loop, copies and MMAs have drained
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeFn encode_fn() {
+    static const EncodeFn fn = []() -> EncodeFn {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<EncodeFn>(p);
+    }();
+    return fn;
+}
+
+bool encode(EncodeFn enc, CUtensorMap* map, CUtensorMapDataType type, int rank, void* base, const cuuint64_t* dims,
+            const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swizzle) {
+    const cuuint32_t es[3] = {1, 1, 1};
+    return enc(map, type, rank, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int N>
+cudaError_t launch_tc(const mv_weight_s& w, const int8_t* q, const float* dT, uint64_t ldb, uint64_t batch, float* y,
+                      cudaStream_t s, bool accumulate) {
+    using C = Cfg<N>;
+    const EncodeFn enc = encode_fn();
+    if (!enc) {
+        set_last_error("cuTensorMapEncodeTiled is unavailable in this driver");
+        return cudaErrorNotSupported;
+    }
+    CUtensorMap wmap, xmap, dmap, smap;
+    // payload plane [rows][nb*16 B] -> raw [128][64 B], 64-byte swizzle
+    const cuuint64_t wdims[2] = {w.nb * 16, w.rows}, wstr[1] = {w.nb * 16};
+    const cuuint32_t wbox[2] = {(cuuint32_t)(kG * 16), (cuuint32_t)kM};
+    // activations [batch][K] -> B [N][128 B], 128-byte swizzle
+    const cuuint64_t xdims[2] = {w.nb * 32, batch}, xstr[1] = {w.nb * 32};
+    const cuuint32_t xbox[2] = {(cuuint32_t)(kG * 32), (cuuint32_t)N};
+    // scales and constants [2][nb][ldb] fp32 -> [2][16][N]
+    const cuuint64_t ddims[3] = {ldb, w.nb, 2}, dstr[2] = {ldb * 4, w.nb * ldb * 4};
+    const cuuint32_t dbox[3] = {(cuuint32_t)N, (cuuint32_t)kEB, 2};
+    // weight scales [rows][dstride] fp16 -> [128][16], 32-byte swizzle
+    const cuuint64_t sdims[2] = {w.dstride, w.rows}, sstr[1] = {w.dstride * 2};
+    const cuuint32_t sbox[2] = {(cuuint32_t)kEB, (cuuint32_t)kM};
+    if (!encode(enc, &wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w.qs, wdims, wstr, wbox, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !encode(enc, &xmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), xdims, xstr, xbox,
+                CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode(enc, &dmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(dT), ddims, dstr, dbox,
+                CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode(enc, &smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, w.d, sdims, sstr, sbox, CU_TENSOR_MAP_SWIZZLE_32B)) {
+        set_last_error("cuTensorMapEncodeTiled rejected a tensor map of the tensor-core GEMM");
+        return cudaErrorInvalidValue;
+    }
+    const int n_ttiles = (int)((batch + N - 1) / N);
+    const int n_tiles = (int)((w.rows + kM - 1) / kM) * n_ttiles;
+    const TcArgs args{y, (int)w.rows, (int)w.nb, (int)batch, n_ttiles, n_tiles, accumulate ? 1 : 0};
+    ensure_smem_attr(gemm_tc_kernel<N>, C::kSmem);
+    const int grid = n_tiles < num_sms() ? n_tiles : num_sms();
+    gemm_tc_kernel<N><<<grid, C::kThreads, C::kSmem, s>>>(wmap, xmap, dmap, smap, args);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t gemm_q4_q8_tc(const mv_weight_s& w, const int8_t* q, const float* dT, uint64_t ldb, uint64_t batch,
+                          float* y, cudaStream_t s, bool accumulate) {
+    if (!batch) return cudaSuccess;
+    if (w.type != 2 || ldb < gemm_tc_ldb(batch) || ldb % 4 || w.rows >= (1ull << 31) || batch >= (1ull << 31))
+        return cudaErrorInvalidValue;
+    // Tile width N: a tile's time is dominated by a per-stage cost (barrier
+    // round trips, MMA issue) that hardly depends on N, plus ~1 cycle per
+    // token; pick the N with the fewest waves x cost.
+    const uint64_t row_tiles = (w.rows + kM - 1) / kM, sms = (uint64_t)num_sms();
+    int best = 16;
+    double best_cost = 1e300;
+    for (int n : {16, 32, 64}) {
+        const uint64_t tiles = row_tiles * ((batch + n - 1) / n);
+        const double cost = (double)((tiles + sms - 1) / sms) * (200.0 + 1.0 * n);
+        if (cost < best_cost * 0.999) {
+            best = n;
+            best_cost = cost;
+        }
+    }
+    switch (best) {
+        case 16: return launch_tc<16>(w, q, dT, ldb, batch, y, s, accumulate);
+        case 32: return launch_tc<32>(w, q, dT, ldb, batch, y, s, accumulate);
+        default: return launch_tc<64>(w, q, dT, ldb, batch, y, s, accumulate);
+    }
+}
+
+}  // namespace mvb

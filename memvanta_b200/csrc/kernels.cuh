@@ -18,6 +18,11 @@ cudaError_t repack_from_ggml(mv_weight_s& w, const uint8_t* raw_dev, cudaStream_
 cudaError_t unpack_to_ggml(const mv_weight_s& w, uint8_t* raw_dev, cudaStream_t s);
 cudaError_t read_rows(const mv_weight_s& w, const int32_t* rows, uint64_t n, float* out, cudaStream_t s);
 cudaError_t quantize_q8_rows(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* d, cudaStream_t s);
+// for the tensor-core GEMM: scales block-major, dT[b * ldb + row], then at
+// dT + nb * ldb the GEMM's per-block constants; 2 * nb * ldb floats in all,
+// rows..ldb-1 zero-filled (ldb >= rows)
+cudaError_t quantize_q8_rows_t(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* dT, uint64_t ldb,
+                               cudaStream_t s);
 
 // ---- gemv_q4.cu : decode GEMV over Q4_0 with Q8 activations (integer path)
 enum class Q4Pro : int {
@@ -47,11 +52,16 @@ cudaError_t gemv_q6k(const mv_weight_s& w, const float* x, float* y, cudaStream_
 // ---- matmul_f32.cu : fp32-activation matmul for every type (T tokens per pass)
 cudaError_t matmul_f32act(const mv_weight_s& w, const float* x, uint64_t batch, float* y, cudaStream_t s);
 
-// ---- gemm.cu : batched Q4_0 x Q8 activations (prefill)
-// q/d: activations already quantised per row (quantize_q8_rows).
-// accumulate: y += result (residual stream) instead of y = result.
-cudaError_t gemm_q4_q8(const mv_weight_s& w, const int8_t* q, const float* d, uint64_t batch, float* y,
-                       cudaStream_t s, bool accumulate = false);
+// ---- gemm_tc.cu : batched Q4_0 x Q8 activations (prefill) on the tensor cores
+// (tcgen05 int8 MMA, TMEM, TMA); y += result instead of y = result when accumulate
+// q: [batch][cols] int8, dT: the 2 * nb * ldb floats of quantize_q8_rows_t
+// with ldb = gemm_tc_ldb(batch).  Exactly the reference's FORCE_Q8 chain per
+// output.
+uint64_t gemm_tc_ldb(uint64_t batch);
+cudaError_t gemm_q4_q8_tc(const mv_weight_s& w, const int8_t* q, const float* dT, uint64_t ldb, uint64_t batch,
+                          float* y, cudaStream_t s, bool accumulate = false);
+// synchronise s; *status = site code of an expired bounded wait (0 = none), cleared
+cudaError_t tc_status(cudaStream_t s, int* status);
 
 // ---- ops.cu
 cudaError_t rmsnorm_rows(const float* x, const float* w, uint64_t rows, uint64_t n, float eps, float* out,

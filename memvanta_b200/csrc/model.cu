@@ -419,7 +419,7 @@ void ensure_prefill(mv_model_s* m, uint64_t B) {
     m->FF = dalloc<float>(m, B * F);
     m->PROJ = dalloc<float>(m, B * D);
     m->XQ = dalloc<int8_t>(m, B * K);
-    m->XD = dalloc<float>(m, B * K / 32);
+    m->XD = dalloc<float>(m, 2 * mvb::gemm_tc_ldb(B) * K / 32);  // block-major scales + constants
     if (B > m->table_rows) {
         std::vector<int32_t> t(B * m->n_pages);
         for (uint64_t r = 0; r < B; ++r)
@@ -704,8 +704,9 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     // fp32 activations otherwise, as tensor_matmul_batch_v06 dispatches.
     auto project = [&](mv_weight_s* w, const float* in, uint64_t K, float* out, bool accumulate) {
         if (B >= 2 && w->type == 2) {
-            ck(mvb::quantize_q8_rows(in, B, K, m->XQ, m->XD, s), "quantize");
-            ck(mvb::gemm_q4_q8(*w, m->XQ, m->XD, B, out, s, accumulate), "gemm");
+            const uint64_t ldb = mvb::gemm_tc_ldb(B);
+            ck(mvb::quantize_q8_rows_t(in, B, K, m->XQ, m->XD, ldb, s), "quantize");
+            ck(mvb::gemm_q4_q8_tc(*w, m->XQ, m->XD, ldb, B, out, s, accumulate), "gemm");
         } else if (accumulate) {
             ck(mvb::matmul_f32act(*w, in, B, m->PROJ, s), "matmul");
             ck(mvb::add_inplace(out, m->PROJ, B * w->rows, s), "add");
@@ -830,6 +831,10 @@ MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uin
         } else {
             ck(cudaStreamSynchronize(m->stream), "sync");
         }
+        int status = 0;
+        ck(mvb::tc_status(m->stream, &status), "status");
+        if (status)
+            throw ModelError(MV_ERR_TIMEOUT, "prefill GEMM gave up a bounded wait (site " + std::to_string(status) + ")");
     });
     return rc ? model_fail(rc) : MV_OK;
 }

@@ -74,8 +74,9 @@ extern "C" MV_API int mv_gemm_q8_noalloc(mv_weight_t w, const float* x, uint64_t
         // as mv_gemm: one token takes the fp32-activation path, which needs no scratch
         e = mvb::matmul_f32act(*w, x, batch, y, s);
     } else {
+        const uint64_t ldb = mvb::gemm_tc_ldb(batch);
         const uint64_t q_bytes = (batch * w->cols + 255) / 256 * 256;
-        const uint64_t d_bytes = batch * (w->cols / 32) * sizeof(float);
+        const uint64_t d_bytes = 2 * ldb * (w->cols / 32) * sizeof(float);
         if (q_bytes + d_bytes > kScratchBytes)
             return fail(MV_ERR_INVALID, "batch x cols needs " + std::to_string(q_bytes + d_bytes) +
                                             " bytes of scratch; mv_gemm_q8_noalloc has " +
@@ -85,8 +86,8 @@ extern "C" MV_API int mv_gemm_q8_noalloc(mv_weight_t w, const float* x, uint64_t
         if (e == cudaSuccess) {
             int8_t* q = static_cast<int8_t*>(base);
             float* d = reinterpret_cast<float*>(static_cast<unsigned char*>(base) + q_bytes);
-            e = mvb::quantize_q8_rows(x, batch, w->cols, q, d, s);
-            if (e == cudaSuccess) e = mvb::gemm_q4_q8(*w, q, d, batch, y, s);
+            e = mvb::quantize_q8_rows_t(x, batch, w->cols, q, d, ldb, s);
+            if (e == cudaSuccess) e = mvb::gemm_q4_q8_tc(*w, q, d, ldb, batch, y, s);
         }
     }
     if (e != cudaSuccess) {

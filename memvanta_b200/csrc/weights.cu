@@ -175,6 +175,46 @@ __global__ void quantize_q8_kernel(const float* __restrict__ x, uint64_t nblocks
     }
 }
 
+// The same quantisation laid out for the tensor-core GEMM: scales
+// block-major, dT[b * ldb + row], and right after them (at dT + nb * ldb) the
+// exact constants c[b * ldb + row] = 1.5 * 2^23 + 8 * sum(q of the block) that
+// turn the GEMM's biased unsigned-nibble dot back into the reference's int32
+// block dot (gemm_tc.cu).  Rows rows..ldb-1 of both are zero.
+__global__ void quantize_q8_t_kernel(const float* __restrict__ x, uint64_t rows, uint64_t nb, int8_t* __restrict__ q,
+                                     float* __restrict__ dT, uint64_t ldb) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
+    const uint64_t first = blockIdx.x * (uint64_t)(blockDim.x / 32) + threadIdx.x / 32;
+    float* cT = dT + nb * ldb;
+    for (uint64_t b = first; b < rows * nb; b += warps) {
+        float dd;
+        const int v = quant_q8_lane(x[b * 32 + lane], dd);
+        q[b * 32 + lane] = (int8_t)v;
+        const int sum = warp_sum_i(v);
+        if (lane == 0) {
+            const uint64_t at = (b % nb) * ldb + b / nb;
+            dT[at] = dd;
+            cT[at] = 12582912.0f + (float)(8 * sum);
+        }
+    }
+    const uint64_t padw = ldb - rows, padn = nb * padw;
+    for (uint64_t i = first * 32 + lane; i < padn; i += warps * 32) {
+        const uint64_t at = (i / padw) * ldb + rows + i % padw;
+        dT[at] = 0.0f;
+        cT[at] = 0.0f;
+    }
+}
+
+cudaError_t quantize_q8_rows_t(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* dT, uint64_t ldb,
+                               cudaStream_t s) {
+    const uint64_t nblocks = rows * (cols / 32);
+    if (!nblocks || ldb < rows) return nblocks ? cudaErrorInvalidValue : cudaSuccess;
+    const uint64_t ctas = (nblocks + 7) / 8;
+    const uint64_t cap = (uint64_t)num_sms() * 8;
+    quantize_q8_t_kernel<<<(unsigned)(ctas < cap ? ctas : cap), 256, 0, s>>>(x, rows, cols / 32, q, dT, ldb);
+    return cudaGetLastError();
+}
+
 cudaError_t quantize_q8_rows(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* d, cudaStream_t s) {
     const uint64_t nblocks = rows * (cols / 32);
     if (!nblocks) return cudaSuccess;

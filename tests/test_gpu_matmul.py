@@ -171,7 +171,67 @@ def test_config1_q4_gemm_q8act(cuda, oracle, rows, cols, batch):
     X = rng.standard_normal((batch, cols)).astype(np.float32)
     W = upload(w, gguf.Q4_0, rows, cols)
     want = oracle.matmul_batch_v06(gguf.Q4_0, w, rows, cols, X, force_q8=True)
-    assert rel_err(run_gemm(W, X, cuda, mv.ACT_Q8), want) <= 1e-3
+    got = run_gemm(W, X, cuda, mv.ACT_Q8)
+    assert rel_err(got, want) <= 1e-3
+    # the tensor-core GEMM keeps the reference's per-output FMA chain: bit-exact
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def _sms():
+    import torch
+    return torch.cuda.get_device_properties(0).multi_processor_count
+
+
+@pytest.mark.parametrize("tile,cols", [("n16", 160), ("n16", 672), ("n32", 4096), ("n64", 672), ("n64", 1056)])
+def test_tc_gemm_tile_widths_bit_exact(cuda, oracle, tile, cols):
+    """Every tile width of the tensor-core GEMM (16 / 32 / 64 tokens), with
+    block counts that end in a partial pipeline stage (nb = 5, 21, 33) and
+    partial row and token tiles; bit-exact against the FORCE_Q8 chain.  The
+    shapes make the launcher's wave model pick the width: one 128-row tile
+    per SM with 16 tokens (n16, rows not a multiple of 128), 32 tokens (n32)
+    and 128 tokens (n64)."""
+    sms = _sms()
+    rows, batch = {"n16": (300, 70), "n32": (128 * sms, 32), "n64": (128 * sms - 5, 128)}[tile]
+    rng = np.random.default_rng(cols + batch)
+    w = gguf.gen_q4_0(rows, cols, rng)
+    X = rng.standard_normal((batch, cols)).astype(np.float32)
+    W = upload(w, gguf.Q4_0, rows, cols)
+    got = run_gemm(W, X, cuda, mv.ACT_Q8)
+    mv.stream_status()
+    want = oracle.matmul_batch_v06(gguf.Q4_0, w, rows, cols, X, force_q8=True)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_tc_gemm_edge_values(cuda, oracle):
+    """Extreme blocks: nibbles all 0 or all 15, activations of one sign at the
+    Q8 clamp, zero rows/tokens, a negative fp16 scale -- bit-exact."""
+    rng = np.random.default_rng(77)
+    rows, cols, batch = 136, 256, 20
+    w = gguf.gen_q4_0(rows, cols, rng).reshape(rows, cols // 32, 18).copy()
+    w[0, :, 2:] = 0x00                       # every nibble 0  -> q - 8 = -8
+    w[1, :, 2:] = 0xFF                       # every nibble 15 -> q - 8 = 7
+    w[2, :, :2] = 0                          # zero scales
+    w[3, :, :2] = np.frombuffer(np.float16(-0.03).tobytes(), np.uint8)
+    w = w.reshape(-1)
+    X = rng.standard_normal((batch, cols)).astype(np.float32)
+    X[0] = 1e4
+    X[1] = -1e-4
+    X[2] = 0.0
+    X[3, ::2] = 3.0
+    X[3, 1::2] = -3.0
+    W = upload(w, gguf.Q4_0, rows, cols)
+    got = run_gemm(W, X, cuda, mv.ACT_Q8)
+    want = oracle.matmul_batch_v06(gguf.Q4_0, w, rows, cols, X, force_q8=True)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_stream_status_clean(cuda):
+    """After normal tensor-core work the bounded-wait status word is clear."""
+    rng = np.random.default_rng(5)
+    w = gguf.gen_q4_0(256, 512, rng)
+    W = upload(w, gguf.Q4_0, 256, 512)
+    run_gemm(W, rng.standard_normal((40, 512)).astype(np.float32), cuda, mv.ACT_Q8)
+    mv.stream_status()
 
 
 def test_config2_q8_0_and_q6_k(cuda, oracle):

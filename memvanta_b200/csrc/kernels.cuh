@@ -23,6 +23,9 @@ cudaError_t quantize_q8_rows(const float* x, uint64_t rows, uint64_t cols, int8_
 // rows..ldb-1 zero-filled (ldb >= rows)
 cudaError_t quantize_q8_rows_t(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* dT, uint64_t ldb,
                                cudaStream_t s);
+// the same on rmsnorm(x) * w (the reference's rmsnorm), without materialising it
+cudaError_t rmsnorm_quantize_q8_rows_t(const float* x, const float* w, uint64_t rows, uint64_t cols, float eps,
+                                       int8_t* q, float* dT, uint64_t ldb, cudaStream_t s);
 
 // ---- gemv_q4.cu : decode GEMV over Q4_0 with Q8 activations (integer path)
 enum class Q4Pro : int {

@@ -714,14 +714,24 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
             ck(mvb::matmul_f32act(*w, in, B, out, s), "matmul");
         }
     };
+    // rmsnorm(X) as the input of a projection: fused into the quantisation on
+    // the tensor-core path, materialised otherwise
+    auto project_normed = [&](mv_weight_s* w, const float* norm_w, float* out) {
+        if (B >= 2 && w->type == 2) {
+            const uint64_t ldb = mvb::gemm_tc_ldb(B);
+            ck(mvb::rmsnorm_quantize_q8_rows_t(m->X, norm_w, B, D, m->eps, m->XQ, m->XD, ldb, s), "rmsnorm+quantize");
+            ck(mvb::gemm_q4_q8_tc(*w, m->XQ, m->XD, ldb, B, out, s, false), "gemm");
+        } else {
+            ck(mvb::rmsnorm_rows(m->X, norm_w, B, D, m->eps, m->N, s), "rmsnorm");
+            project(w, m->N, D, out, false);
+        }
+    };
     for (auto& L : m->layers) {
-        ck(mvb::rmsnorm_rows(m->X, L.attn_norm, B, D, m->eps, m->N, s), "rmsnorm");
-        project(L.qkv, m->N, D, m->QKV, false);
+        project_normed(L.qkv, L.attn_norm, m->QKV);
         rope_append(m, L, m->QKV, B, pos, nullptr);
         ck(mvb::paged_attn_decode(attn_args(m, L, m->QKV, QKVW, B, ctx, start + B, m->ATT), s), "attention");
         project(L.o, m->ATT, D, m->X, true);
-        ck(mvb::rmsnorm_rows(m->X, L.ffn_norm, B, D, m->eps, m->N, s), "rmsnorm");
-        project(L.gu, m->N, D, m->GU, false);
+        project_normed(L.gu, L.ffn_norm, m->GU);
         mvb::silu_pairs_kernel<<<mvb::ew_grid(B * F), 256, 0, s>>>(m->GU, m->FF, B * F);
         ck(cudaGetLastError(), "silu_pairs");
         project(L.down, m->FF, F, m->X, true);

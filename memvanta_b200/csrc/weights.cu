@@ -205,6 +205,92 @@ __global__ void quantize_q8_t_kernel(const float* __restrict__ x, uint64_t rows,
     }
 }
 
+// RMSNorm of every row (ops.cu rmsnorm_kernel: sum of squares in double,
+// x * inv * w with two roundings) fused with the quantisation above, for the
+// prefill GEMMs whose input is a normalised row (q|k|v, gate|up).  One CTA per
+// row; each thread owns 4 consecutive elements per step, so a 32-element
+// block is 8 consecutive lanes and its max / sum are 3 shuffle steps.
+__global__ void rmsnorm_quantize_t_kernel(const float* __restrict__ x, const float* __restrict__ w, int n, float eps,
+                                          uint64_t rows, int8_t* __restrict__ q, float* __restrict__ dT,
+                                          uint64_t ldb) {
+    __shared__ double red[32];
+    const uint64_t row = blockIdx.x;
+    const int nc = n / 4, nb = n / 32;
+    const int steps = (nc + blockDim.x - 1) / blockDim.x;
+    const float4* xr = reinterpret_cast<const float4*>(x + row * n);
+    double ss = 0.0;
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+        const float4 v = xr[c];
+        ss += (double)v.x * v.x;
+        ss += (double)v.y * v.y;
+        ss += (double)v.z * v.z;
+        ss += (double)v.w * v.w;
+    }
+    ss = warp_sum_d(ss);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (warp == 0) {
+        double t = lane < nw ? red[lane] : 0.0;
+        t = warp_sum_d(t);
+        if (lane == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = 1.0f / sqrtf((float)(red[0] / (double)n) + eps);
+    float* cT = dT + (uint64_t)nb * ldb;
+    for (int st = 0; st < steps; ++st) {  // every lane takes part in the shuffles
+        const int c = st * blockDim.x + threadIdx.x;
+        const bool live = c < nc;       // whole 8-lane groups live or not (nc % 8 == 0)
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (live) {
+            const float4 v = xr[c], g = reinterpret_cast<const float4*>(w)[c];
+            o = make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
+        }
+        float mx = fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w)));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        const float d = mx > 0.0f ? mx / 127.0f : 1.0f;
+        const float id = 1.0f / d;
+        const int q0 = (int)fminf(fmaxf(roundf(o.x * id), -127.0f), 127.0f);
+        const int q1 = (int)fminf(fmaxf(roundf(o.y * id), -127.0f), 127.0f);
+        const int q2 = (int)fminf(fmaxf(roundf(o.z * id), -127.0f), 127.0f);
+        const int q3 = (int)fminf(fmaxf(roundf(o.w * id), -127.0f), 127.0f);
+        int sum = q0 + q1 + q2 + q3;
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        if (live) {
+            reinterpret_cast<uint32_t*>(q + row * n)[c] =
+                (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8) | ((uint32_t)(q2 & 0xFF) << 16) |
+                ((uint32_t)(q3 & 0xFF) << 24);
+            if ((c & 7) == 0) {
+                const uint64_t at = (uint64_t)(c / 8) * ldb + row;
+                dT[at] = d;
+                cT[at] = 12582912.0f + (float)(8 * sum);
+            }
+        }
+    }
+    if (blockIdx.x == 0) {  // tokens rows..ldb-1 of every block: zero
+        const uint64_t padw = ldb - rows, padn = (uint64_t)nb * padw;
+        for (uint64_t i = threadIdx.x; i < padn; i += blockDim.x) {
+            const uint64_t at = (i / padw) * ldb + rows + i % padw;
+            dT[at] = 0.0f;
+            cT[at] = 0.0f;
+        }
+    }
+}
+
+cudaError_t rmsnorm_quantize_q8_rows_t(const float* x, const float* w, uint64_t rows, uint64_t cols, float eps,
+                                       int8_t* q, float* dT, uint64_t ldb, cudaStream_t s) {
+    if (!rows) return cudaSuccess;
+    if (cols % 32 || ldb < rows) return cudaErrorInvalidValue;
+    const uint64_t nc = cols / 4;
+    const unsigned threads = (unsigned)(nc >= 1024 ? 1024 : (nc + 31) / 32 * 32);
+    rmsnorm_quantize_t_kernel<<<(unsigned)rows, threads, 0, s>>>(x, w, (int)cols, eps, rows, q, dT, ldb);
+    return cudaGetLastError();
+}
+
 cudaError_t quantize_q8_rows_t(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* dT, uint64_t ldb,
                                cudaStream_t s) {
     const uint64_t nblocks = rows * (cols / 32);

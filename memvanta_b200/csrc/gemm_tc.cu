@@ -1,7 +1,7 @@
 // gemm_tc.cu -- batched Q4_0 x Q8-activation matmul (prefill) on the
-// 5th-generation tensor cores: tcgen05 int8 MMA into TMEM, fed by TMA, with
-// the per-block fp16 weight scales and fp32 activation scales applied in the
-// epilogue.
+// 5th-generation tensor cores: tcgen05 int8 MMA with the weights in tensor
+// memory, activations fed by TMA, the per-block fp16 weight scales and fp32
+// activation scales applied in the epilogue.
 //
 // Numerics are the reference's MEMVANTA_FORCE_Q8_ACT=1 prefill
 // (tensor_matmul_batch_v06, src/gguf_kernels.cpp:265-266): every activation
@@ -18,43 +18,48 @@
 // Exact int -> float without integer instructions:
 //   * A is the raw nibble (u8, 0..15), B the Q8 value (s8), so the MMA yields
 //     D = isum + 8 * sum_k q_k.
-//   * Every slot is preset to the bit pattern 0x4B400000 (= 1.5 * 2^23 as a
-//     float) and the MMA accumulates onto it; |D| < 2^16, so the slot's bits
+//   * Every D slot is preset to the bit pattern 0x4B400000 (= 1.5 * 2^23 as
+//     a float) and the MMA accumulates onto it; |D| < 2^16, so the slot's bits
 //     read as a float are exactly 1.5 * 2^23 + D.
 //   * The quantiser stores c[t,b] = 1.5 * 2^23 + 8 * sum_k q_k (exact), and
 //     (1.5 * 2^23 + D) - c[t,b] = isum exactly (both in [2^23, 2^24)).
-//   So the epilogue spends one FADD, one FMUL and one FFMA per (row, token,
-//   block), and a tcgen05.st puts the preset back after reading a slot.
+//   So the epilogue spends one subtract, one multiply and one FMA per (row,
+//   token, block) -- packed two tokens per instruction (f32x2) -- and a
+//   tcgen05.st puts the preset back after reading a slot.
 //
-// Layouts (per pipeline stage of G = 4 blocks, 128 rows, N tokens; all
-// 16-byte chunks XOR-swizzled by their row as TMA lays them out):
-//   raw  [128 rows][64 B]    the Q4_0 nibble bytes of 4 blocks, one 2-D TMA
-//                            box over the [rows][nb*16 B] payload plane,
-//                            64-byte swizzle (chunk j of row i at j^((i>>1)&3))
-//   A8   [128 rows][128 B]   the nibbles one per byte, K-major, 128-byte
-//                            swizzle (chunk j at j^(i&7)), 8-row groups 1024 B
-//                            apart; block g is the 32-byte K slice at +32 g
-//   B    [N][128 B]          the Q8 activations of the 4 blocks in the same
-//                            form, landed directly by one 2-D TMA box
+// Data path, per pipeline stage of G = 4 blocks of a 128-row x N-token tile:
+//   raw  smem [128 rows][64 B]  the Q4_0 nibble bytes of the 4 blocks: one 2-D
+//                               TMA box over the [rows][nb*16 B] payload plane,
+//                               64-byte swizzle (chunk j of row i at j^((i>>1)&3))
+//   B    smem [N][128 B]        the Q8 activations of the 4 blocks, K-major,
+//                               128-byte swizzle (one TMA box); block g is the
+//                               32-byte K slice at +32 g of every row
+//   A    TMEM 128 lanes x 32 cols  the nibbles one per byte (lane = row, 4 per
+//                               32-bit column), written by the converter warps
+//                               with tcgen05.st and read by the MMA from TMEM
+//   D    TMEM 128 lanes x 4N cols  one N-column slot per block
 // Epilogue data, per group of 16 blocks, in a ring of 4 slots the producer
 // fills well ahead of use:
-//   dw   [128 rows][32 B]    the fp16 weight scales, 2-D TMA box over the
-//                            [rows][dstride] plane, 32-byte swizzle
-//   sc   [2][16][N]          the activation scales and the constants c
-//                            (block-major [nb][ldb] each, tokens padded to 64)
+//   dw   [128 rows][32 B]       the fp16 weight scales, 2-D TMA box over the
+//                               [rows][dstride] plane, 32-byte swizzle
+//   sc   [2][16][N]             the activation scales and the constants c
+//                               (block-major [nb][ldb] each, tokens padded to 64)
 //
 // Warp roles (one CTA per SM, persistent over 128-row x N-token tiles):
 //   warp 0       TMA producer (one lane): stages and epilogue data
-//   warps 1-2    MMA issuers (one lane each, alternate stages); warp 1 also
-//                allocates TMEM (whole warp)
-//   warps 3-6    converters: nibble bytes -> one nibble per byte, one row per thread
-//   warps 7-14   epilogue: TMEM -> registers -> chain -> y; warp w reads TMEM
-//                lanes 32*(w%4).. (its row quadrant), token half (w-7)/4
-// Rings: S smem stages (full: TMA bytes landed; conv: A8 written; empty: MMAs
-// done reading), 512/(G*N) TMEM stage groups (tfull: MMAs done; tempty:
-// epilogue read them and restored the preset) and 4 epilogue-data slots
-// (efull: TMA bytes landed; eempty: epilogue done).  Every wait is bounded
-// (tc.cuh).
+//   warps 1-3    MMA issuers (one lane each, stages round-robin: an issuing
+//                thread spends ~60 cycles per MMA and more on its waits and
+//                commits, so three overlap); warp 1 also allocates TMEM
+//   warps 4-7    converters: warp w writes TMEM lanes 32*(w%4).. (its rows)
+//   warps 8-23   epilogue: TMEM -> registers -> chain -> y; warp w reads TMEM
+//                lanes 32*(w%4).. (its row quadrant), token quarter (w-8)/4:
+//                four warps per quadrant hide one another's TMEM and barrier
+//                latencies
+// Rings: S smem stages (full: TMA bytes landed; empty: converters read the
+// nibbles and the MMAs read B), 4 TMEM A stages (aready: converters wrote;
+// aempty: MMAs read), the TMEM D groups (tfull: MMAs done; tempty: epilogue
+// read them and restored the preset) and 4 epilogue-data slots (efull: TMA
+// bytes landed; eempty: epilogue done).  Every wait is bounded (tc.cuh).
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -84,39 +89,38 @@ namespace {
 
 constexpr int kM = 128;  // weight rows per tile = TMEM lanes
 constexpr int kG = 4;    // Q4_0 blocks per pipeline stage
-constexpr int kMmaWarps = 2;  // MMA issuers, alternating stages
-constexpr int kConvWarps = 4;
+constexpr int kMmaWarps = 3;
 constexpr int kConvWarp0 = 1 + kMmaWarps;
+constexpr int kConvWarps = 4;
 constexpr int kEpiWarp0 = kConvWarp0 + kConvWarps;
-constexpr uint32_t kPreset = 0x4B400000u;  // 1.5 * 2^23 as a float
-constexpr int kEB = 16;                    // blocks per epilogue-data slot
-constexpr int kES = 4;                     // epilogue-data slots
+constexpr int kEW = 4;  // epilogue warps per TMEM lane quadrant
+constexpr int kEpiWarps = 4 * kEW;
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
+constexpr uint32_t kPreset = 0x4B400000u;   // 1.5 * 2^23 as a float
+constexpr int kEB = 16;                     // blocks per epilogue-data slot
+constexpr int kES = 4;                      // epilogue-data slots
+constexpr int kSA = 4;                      // TMEM A stages
+constexpr int kACols = kG * 8;              // TMEM columns of one A stage
+constexpr int kDCols = 512 - kSA * kACols;  // TMEM columns of the D ring
 
 template <int N>
 struct Cfg {
-    static constexpr int kEW = 2;       // epilogue warps per TMEM lane quadrant
-    static constexpr int kTT = N / kEW;  // tokens per epilogue thread
-    static constexpr int kEpiWarps = 4 * kEW;
-    static constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
+    static constexpr int kTT = N / kEW;        // tokens per epilogue thread
     static constexpr int kRaw = kM * kG * 16;  // [128][64 B]
-    static constexpr int kA8 = kM * kG * 32;   // [128][128 B]
     static constexpr int kB = N * kG * 32;     // [N][128 B]
-    static constexpr int kStage = kRaw + kA8 + kB;
-    static constexpr int kS = (224 * 1024 - kES * (kM * kEB * 2 + 2 * kEB * N * 4)) / kStage < 8
-                                  ? (224 * 1024 - kES * (kM * kEB * 2 + 2 * kEB * N * 4)) / kStage
-                                  : 8;
-    static constexpr int kTG = 512 / (kG * N);
-    static constexpr int kDw = kM * kEB * 2;                // weight scales [128][16] fp16
-    static constexpr int kEpi = kDw + 2 * kEB * N * 4;      // + [2][16][N] fp32: scales, constants c
+    static constexpr int kStage = kRaw + kB;
+    static constexpr int kDw = kM * kEB * 2;            // weight scales [128][16] fp16
+    static constexpr int kEpi = kDw + 2 * kEB * N * 4;  // + [2][16][N] fp32: scales, constants c
+    static constexpr int kS = 12;
+    static constexpr int kTG = kDCols / (kG * N);  // TMEM D groups
     static constexpr int kEpiOff = kS * kStage;
     static constexpr int kBarOff = kEpiOff + kES * kEpi;
-    static constexpr int kBars = 3 * kS + 2 * kTG + 2 * kES + 1;
+    static constexpr int kBars = 2 * kS + 2 * kSA + 2 * kTG + 2 * kES + 1;
     static constexpr int kSmem = kBarOff + kBars * 8 + 16 + 1024;  // + alignment slack
-    static constexpr int kLdBlocks = 32 / kTT;                     // blocks per TMEM load batch
-    static_assert(kG % kLdBlocks == 0, "load batches must tile a stage");
-    static_assert(kTG >= 2, "two TMEM stage groups at least");
+    static_assert(kTG >= 2, "two TMEM D groups at least");
     static_assert(kStage % 1024 == 0 && kEpi % 1024 == 0, "swizzled TMA tiles need 1024-byte alignment");
-    static_assert(kEB % kG == 0, "a data slot covers whole stages");
+    static_assert(kEB % kG == 0 && kTT % 4 == 0, "tile shape");
+    static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 struct TcArgs {
@@ -126,66 +130,74 @@ struct TcArgs {
 
 template <int TT>
 __device__ __forceinline__ void tmem_load(uint32_t taddr, uint32_t (&v)[TT]) {
-    if constexpr (TT == 8) {
+    if constexpr (TT == 4) {
+        tc::tmem_ld4(taddr, v);
+    } else if constexpr (TT == 8) {
         tc::tmem_ld8(taddr, v);
-    } else if constexpr (TT == 16) {
-        tc::tmem_ld16(taddr, v);
     } else {
-        tc::tmem_ld32(taddr, v);
+        tc::tmem_ld16(taddr, v);
     }
 }
 template <int TT>
 __device__ __forceinline__ void tmem_preset(uint32_t taddr) {
-    if constexpr (TT == 8) {
+    if constexpr (TT == 4) {
+        tc::tmem_fill4(taddr, kPreset);
+    } else if constexpr (TT == 8) {
         tc::tmem_fill8(taddr, kPreset);
-    } else if constexpr (TT == 16) {
-        tc::tmem_fill16(taddr, kPreset);
     } else {
-        tc::tmem_fill32(taddr, kPreset);
+        tc::tmem_fill16(taddr, kPreset);
     }
 }
 
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+    return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+
 template <int N>
-__global__ void __launch_bounds__(Cfg<N>::kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                    const __grid_constant__ CUtensorMap dmap, const __grid_constant__ CUtensorMap smap,
                    const TcArgs a) {
     using C = Cfg<N>;
-    constexpr int TT = C::kTT, LB = C::kLdBlocks;
+    constexpr int TT = C::kTT, LB = 32 / TT < kG ? 32 / TT : kG;  // blocks per TMEM load batch
     extern __shared__ unsigned char smem_dyn[];
     const uint32_t s0 = tc::smem_u32(smem_dyn);
     const uint32_t pad = ((s0 + 1023u) & ~1023u) - s0;
     unsigned char* const sm = smem_dyn + pad;
     const uint32_t sbase = s0 + pad;
     const uint32_t bars = sbase + C::kBarOff;
-    const auto full_bar = [&](int s) { return bars + 8u * s; };
-    const auto conv_bar = [&](int s) { return bars + 8u * (C::kS + s); };
-    const auto empty_bar = [&](int s) { return bars + 8u * (2 * C::kS + s); };
-    const auto tfull_bar = [&](int g) { return bars + 8u * (3 * C::kS + g); };
-    const auto tempty_bar = [&](int g) { return bars + 8u * (3 * C::kS + C::kTG + g); };
-    const auto efull_bar = [&](int e) { return bars + 8u * (3 * C::kS + 2 * C::kTG + e); };
-    const auto eempty_bar = [&](int e) { return bars + 8u * (3 * C::kS + 2 * C::kTG + kES + e); };
-    const uint32_t done_bar = bars + 8u * (3 * C::kS + 2 * C::kTG + 2 * kES);
+    const uint32_t full0 = bars;
+    const uint32_t empty0 = full0 + 8u * C::kS;
+    const uint32_t aready0 = empty0 + 8u * C::kS;
+    const uint32_t aempty0 = aready0 + 8u * kSA;
+    const uint32_t tfull0 = aempty0 + 8u * kSA;
+    const uint32_t tempty0 = tfull0 + 8u * C::kTG;
+    const uint32_t efull0 = tempty0 + 8u * C::kTG;
+    const uint32_t eempty0 = efull0 + 8u * kES;
+    const uint32_t done_bar = eempty0 + 8u * kES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kBarOff + C::kBars * 8);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + C::kBarOff + C::kBars * 8 + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool epi = warp >= kEpiWarp0;
-    const int quad = warp & 3;                  // epilogue: TMEM lanes 32*quad .. +31
+    const int quad = warp & 3;                  // converter/epilogue: TMEM lanes 32*quad .. +31
     const int slice = (warp - kEpiWarp0) >> 2;  // epilogue: tokens slice*TT .. +TT-1 of a tile
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kS; ++s) {
-            tc::mbar_init(full_bar(s), 1);
-            tc::mbar_init(conv_bar(s), kConvWarps);
-            tc::mbar_init(empty_bar(s), 1);
+            tc::mbar_init(full0 + 8 * s, 1);
+            tc::mbar_init(empty0 + 8 * s, kConvWarps + 1);  // nibbles read + the MMAs' commit
+        }
+        for (int i = 0; i < kSA; ++i) {
+            tc::mbar_init(aready0 + 8 * i, kConvWarps);
+            tc::mbar_init(aempty0 + 8 * i, 1);
         }
         for (int g = 0; g < C::kTG; ++g) {
-            tc::mbar_init(tfull_bar(g), 1);
-            tc::mbar_init(tempty_bar(g), C::kEpiWarps);
+            tc::mbar_init(tfull0 + 8 * g, 1);
+            tc::mbar_init(tempty0 + 8 * g, kEpiWarps);
         }
         for (int e = 0; e < kES; ++e) {
-            tc::mbar_init(efull_bar(e), 1);
-            tc::mbar_init(eempty_bar(e), C::kEpiWarps);
+            tc::mbar_init(efull0 + 8 * e, 1);
+            tc::mbar_init(eempty0 + 8 * e, kEpiWarps);
         }
         tc::mbar_init(done_bar, kMmaWarps);
         *abort_flag = 0;
@@ -203,10 +215,11 @@ __global__ void __launch_bounds__(Cfg<N>::kThreads, 1)
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + slice * TT;  // epilogue's TMEM corner
+    const uint32_t lanes = (uint32_t)(quad * 32) << 16;  // this warp's TMEM lane quadrant
+    const uint32_t tl = tmem + lanes + slice * TT;         // epilogue's TMEM corner
     if (epi) {
-        // preset every slot this warp reads (its lanes x its token columns)
-        for (int col = 0; col < 512; col += N) tmem_preset<TT>(tl + col);
+        // preset every D slot this warp reads (its lanes x its token columns)
+        for (int col = 0; col < C::kTG * kG * N; col += N) tmem_preset<TT>(tl + col);
         tc::tmem_wait_st();
     }
     tc::tc_fence_before();
@@ -223,74 +236,62 @@ __global__ void __launch_bounds__(Cfg<N>::kThreads, 1)
                 for (int b0 = 0; b0 < a.nb; b0 += kG) {
                     if (b0 % kEB == 0) {
                         const int e = j % kES;
-                        if (!tc::mbar_wait(eempty_bar(e), ((j / kES) & 1u) ^ 1u, abort_flag, &g_tc_status, 10)) {
+                        if (!tc::mbar_wait(eempty0 + 8 * e, ((j / kES) & 1u) ^ 1u, abort_flag, &g_tc_status, 10)) {
                             ok = false;
                             break;
                         }
                         const uint32_t ed = sbase + C::kEpiOff + e * C::kEpi;
-                        tc::mbar_expect_tx(efull_bar(e), C::kEpi);
-                        tc::tma_load_2d(ed, &smap, b0, row0, efull_bar(e));
-                        tc::tma_load_3d(ed + C::kDw, &dmap, t0, b0, 0, efull_bar(e));
+                        tc::mbar_expect_tx(efull0 + 8 * e, C::kEpi);
+                        tc::tma_load_2d(ed, &smap, b0, row0, efull0 + 8 * e);
+                        tc::tma_load_3d(ed + C::kDw, &dmap, t0, b0, 0, efull0 + 8 * e);
                         ++j;
                     }
                     const int s = k % C::kS;
-                    if (!tc::mbar_wait(empty_bar(s), ((k / C::kS) & 1u) ^ 1u, abort_flag, &g_tc_status, 1)) {
+                    if (!tc::mbar_wait(empty0 + 8 * s, ((k / C::kS) & 1u) ^ 1u, abort_flag, &g_tc_status, 1)) {
                         ok = false;
                         break;
                     }
                     const uint32_t st = sbase + s * C::kStage;
-                    tc::mbar_expect_tx(full_bar(s), C::kRaw + C::kB);
-                    tc::tma_load_2d(st, &wmap, b0 * 16, row0, full_bar(s));
-                    tc::tma_load_2d(st + C::kRaw + C::kA8, &xmap, b0 * 32, t0, full_bar(s));
+                    tc::mbar_expect_tx(full0 + 8 * s, C::kStage);
+                    tc::tma_load_2d(st, &wmap, b0 * 16, row0, full0 + 8 * s);
+                    tc::tma_load_2d(st + C::kRaw, &xmap, b0 * 32, t0, full0 + 8 * s);
                     ++k;
                 }
             }
             // drain: the latest load of every slot has landed before the CTA exits
             for (uint32_t i = k > (uint32_t)C::kS ? k - C::kS : 0; i < k; ++i)
-                tc::mbar_wait(full_bar(i % C::kS), (i / C::kS) & 1u, abort_flag, &g_tc_status, 2, false);
+                tc::mbar_wait(full0 + 8 * (i % C::kS), (i / C::kS) & 1u, abort_flag, &g_tc_status, 2, false);
             for (uint32_t i = j > (uint32_t)kES ? j - kES : 0; i < j; ++i)
-                tc::mbar_wait(efull_bar(i % kES), (i / kES) & 1u, abort_flag, &g_tc_status, 11, false);
+                tc::mbar_wait(efull0 + 8 * (i % kES), (i / kES) & 1u, abort_flag, &g_tc_status, 11, false);
         }
     } else if (warp <= kMmaWarps) {
         // ---------------------------------------------------- MMA issuers
-        // Issuer i takes the stages k with k % kMmaWarps == i: the latency an
-        // issuing thread spends around its commits and waits overlaps.
         const uint32_t mine = warp - 1;
         if (lane == 0) {
             constexpr uint32_t idesc = tc::idesc_u8s8(kM, N);
-            // descriptor of stage 0's A8 tile; B follows A8 by kA8 bytes in every stage
-            const uint64_t adesc0 = tc::sdesc_kmajor_sw128(sbase + C::kRaw);
+            const uint64_t bdesc0 = tc::sdesc_kmajor_sw128(sbase + C::kRaw);  // stage 0's B tile
             uint32_t k = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
-                for (int b0 = 0; b0 < a.nb; b0 += kG) {
-                    if (k % kMmaWarps != mine) {
-                        ++k;
-                        continue;
-                    }
-                    const int s = k % C::kS, tg = k % C::kTG;
-                    const uint32_t ph = (k / C::kS) & 1u;
-                    if (!tc::mbar_wait(full_bar(s), ph, abort_flag, &g_tc_status, 3) ||
-                        !tc::mbar_wait(conv_bar(s), ph, abort_flag, &g_tc_status, 4) ||
-                        !tc::mbar_wait(tempty_bar(tg), ((k / C::kTG) & 1u) ^ 1u, abort_flag, &g_tc_status, 5)) {
+                for (int b0 = 0; b0 < a.nb; b0 += kG, ++k) {
+                    if (k % kMmaWarps != mine) continue;
+                    const int s = k % C::kS, ai = k % kSA, tg = k % C::kTG;
+                    if (!tc::mbar_wait(full0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_tc_status, 3) ||
+                        !tc::mbar_wait(aready0 + 8 * ai, (k / kSA) & 1u, abort_flag, &g_tc_status, 4) ||
+                        !tc::mbar_wait(tempty0 + 8 * tg, ((k / C::kTG) & 1u) ^ 1u, abort_flag, &g_tc_status, 5)) {
                         ok = false;
                         break;
                     }
                     tc::tc_fence_after();
-                    // block g = the 32-byte K slice at +32 g: +2 in the descriptors' address field
-                    const uint64_t ad = adesc0 + (uint64_t)(s * (C::kStage >> 4));
+                    // block g: A at +8 g columns, B = the 32-byte K slice at +32 g (+2 in the address field)
+                    const uint64_t bd = bdesc0 + (uint64_t)(s * (C::kStage >> 4));
+                    const uint32_t ad = tmem + kDCols + ai * kACols;
                     const uint32_t d0 = tmem + tg * (kG * N);
-                    if (b0 + kG <= a.nb) {
-#pragma unroll
-                        for (int g = 0; g < kG; ++g)
-                            tc::mma_i8(d0 + g * N, ad + 2 * g, ad + (C::kA8 >> 4) + 2 * g, idesc, 1u);
-                    } else {
-                        for (int g = 0; g < a.nb - b0; ++g)
-                            tc::mma_i8(d0 + g * N, ad + 2 * g, ad + (C::kA8 >> 4) + 2 * g, idesc, 1u);
-                    }
-                    tc::mma_commit(empty_bar(s));
-                    tc::mma_commit(tfull_bar(tg));
-                    ++k;
+                    const int nblk = a.nb - b0 < kG ? a.nb - b0 : kG;
+                    for (int g = 0; g < nblk; ++g) tc::mma_i8_ts(d0 + g * N, ad + 8 * g, bd + 2 * g, idesc, 1u);
+                    tc::mma_commit(empty0 + 8 * s);
+                    tc::mma_commit(aempty0 + 8 * ai);
+                    tc::mma_commit(tfull0 + 8 * tg);
                 }
             }
             // every MMA issued has completed before TMEM is released
@@ -299,35 +300,45 @@ __global__ void __launch_bounds__(Cfg<N>::kThreads, 1)
         }
     } else if (!epi) {
         // ------------------------------------------------------ converters
-        const int c = threadIdx.x - kConvWarp0 * 32;  // row of the tile
+        const int c = quad * 32 + lane;  // row of the tile = this thread's TMEM lane
         const int rsw = (c >> 1) & 3;    // 64-byte swizzle phase of raw row c
-        const int asw = c & 7;           // 128-byte swizzle phase of A8 row c
         uint32_t k = 0;
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
-            for (int b0 = 0; b0 < a.nb; b0 += kG) {
-                const int s = k % C::kS;
-                if (!__all_sync(0xffffffffu,
-                                tc::mbar_wait(full_bar(s), (k / C::kS) & 1u, abort_flag, &g_tc_status, 7))) {
+            for (int b0 = 0; b0 < a.nb; b0 += kG, ++k) {
+                const int s = k % C::kS, ai = k % kSA;
+                const bool got =
+                    tc::mbar_wait(full0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_tc_status, 7) &&
+                    tc::mbar_wait(aempty0 + 8 * ai, ((k / kSA) & 1u) ^ 1u, abort_flag, &g_tc_status, 12);
+                // warp-uniform outcome: the TMEM store below is .sync.aligned
+                if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
                 }
+                tc::tc_fence_after();
                 const unsigned char* raw = sm + s * C::kStage + c * 64;
-                unsigned char* a8 = sm + s * C::kStage + C::kRaw + c * 128;
+                uint32_t v[32];
 #pragma unroll
                 for (int g = 0; g < kG; ++g) {
                     // GGUF order: byte i holds element i (low nibble) and 16 + i (high)
                     const uint4 w = *reinterpret_cast<const uint4*>(raw + ((g ^ rsw) << 4));
-                    *reinterpret_cast<uint4*>(a8 + (((2 * g) ^ asw) << 4)) =
-                        make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
-                    *reinterpret_cast<uint4*>(a8 + (((2 * g + 1) ^ asw) << 4)) =
-                        make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
-                                   (w.w >> 4) & 0x0F0F0F0Fu);
+                    v[8 * g + 0] = w.x & 0x0F0F0F0Fu;
+                    v[8 * g + 1] = w.y & 0x0F0F0F0Fu;
+                    v[8 * g + 2] = w.z & 0x0F0F0F0Fu;
+                    v[8 * g + 3] = w.w & 0x0F0F0F0Fu;
+                    v[8 * g + 4] = (w.x >> 4) & 0x0F0F0F0Fu;
+                    v[8 * g + 5] = (w.y >> 4) & 0x0F0F0F0Fu;
+                    v[8 * g + 6] = (w.z >> 4) & 0x0F0F0F0Fu;
+                    v[8 * g + 7] = (w.w >> 4) & 0x0F0F0F0Fu;
                 }
-                tc::fence_proxy_async_smem();
+                tc::tmem_st32(tmem + lanes + kDCols + ai * kACols, v);
+                tc::tmem_wait_st();
+                tc::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(conv_bar(s));
-                ++k;
+                if (lane == 0) {
+                    tc::mbar_arrive(aready0 + 8 * ai);
+                    tc::mbar_arrive(empty0 + 8 * s);
+                }
             }
         }
     } else {
@@ -339,13 +350,13 @@ __global__ void __launch_bounds__(Cfg<N>::kThreads, 1)
         for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
             const int r = (tile / a.n_ttiles) * kM + rr;
             const int tb = (tile % a.n_ttiles) * N + slice * TT;
-            float acc[TT];
+            uint64_t acc[TT / 2];  // token pairs, (+0, +0) first
 #pragma unroll
-            for (int t = 0; t < TT; ++t) acc[t] = 0.0f;
+            for (int t = 0; t < TT / 2; ++t) acc[t] = 0ull;
             for (int b16 = 0; b16 < a.nb; b16 += kEB) {
                 const int e = j % kES;
                 if (!__all_sync(0xffffffffu,
-                                tc::mbar_wait(efull_bar(e), (j / kES) & 1u, abort_flag, &g_tc_status, 12))) {
+                                tc::mbar_wait(efull0 + 8 * e, (j / kES) & 1u, abort_flag, &g_tc_status, 13))) {
                     ok = false;
                     break;
                 }
@@ -362,49 +373,51 @@ __global__ void __launch_bounds__(Cfg<N>::kThreads, 1)
                     const int nblk = a.nb - b0;
                     const int tg = k % C::kTG;
                     // warp-uniform outcome: the TMEM accesses below are .sync.aligned
-                    if (!__all_sync(0xffffffffu, tc::mbar_wait(tfull_bar(tg), (k / C::kTG) & 1u, abort_flag,
+                    if (!__all_sync(0xffffffffu, tc::mbar_wait(tfull0 + 8 * tg, (k / C::kTG) & 1u, abort_flag,
                                                                &g_tc_status, 8))) {
                         ok = false;
                         break;
                     }
                     tc::tc_fence_after();
+                    // LB slots in flight at once (32 registers), one wait, then the presets back
 #pragma unroll
                     for (int gb = 0; gb < kG; gb += LB) {
-                        uint32_t v[LB][TT];
+                    uint32_t v[LB][TT];
 #pragma unroll
-                        for (int i = 0; i < LB; ++i) tmem_load<TT>(tl + tg * (kG * N) + (gb + i) * N, v[i]);
-                        tc::tmem_wait_ld();
+                    for (int i = 0; i < LB; ++i) tmem_load<TT>(tl + tg * (kG * N) + (gb + i) * N, v[i]);
+                    tc::tmem_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < LB; ++i) tmem_preset<TT>(tl + tg * (kG * N) + (gb + i) * N);
+                    for (int i = 0; i < LB; ++i) tmem_preset<TT>(tl + tg * (kG * N) + (gb + i) * N);
 #pragma unroll
-                        for (int i = 0; i < LB; ++i) {
-                            const int g = gb + i;
-                            if (g < nblk) {
-                                const int eb = h * kG + g;  // block index in the group of 16
-                                const uint32_t word = dwp[eb >> 1];
-                                const float dw = half_bits_to_float((unsigned short)((eb & 1) ? word >> 16 : word));
-                                const float4* d4p = reinterpret_cast<const float4*>(da + eb * N + slice * TT);
-                                const float4* c4p = reinterpret_cast<const float4*>(cb + eb * N + slice * TT);
+                    for (int i = 0; i < LB; ++i) {
+                        const int g = gb + i;
+                        if (g < nblk) {
+                            const int eb = h * kG + g;  // block index in the group of 16
+                            const uint32_t word = dwp[eb >> 1];
+                            const float dw = half_bits_to_float((unsigned short)((eb & 1) ? word >> 16 : word));
+                            const uint64_t dw2 = pack2(dw, dw);
+                            const ulonglong2* d4p = reinterpret_cast<const ulonglong2*>(da + eb * N + slice * TT);
+                            const ulonglong2* c4p = reinterpret_cast<const ulonglong2*>(cb + eb * N + slice * TT);
 #pragma unroll
-                                for (int t4 = 0; t4 < TT / 4; ++t4) {
-                                    const float4 d4 = d4p[t4], c4 = c4p[t4];
-                                    const uint32_t* vv = &v[i][4 * t4];
-                                    acc[4 * t4 + 0] = fmaf(dw * d4.x, __uint_as_float(vv[0]) - c4.x, acc[4 * t4 + 0]);
-                                    acc[4 * t4 + 1] = fmaf(dw * d4.y, __uint_as_float(vv[1]) - c4.y, acc[4 * t4 + 1]);
-                                    acc[4 * t4 + 2] = fmaf(dw * d4.z, __uint_as_float(vv[2]) - c4.z, acc[4 * t4 + 2]);
-                                    acc[4 * t4 + 3] = fmaf(dw * d4.w, __uint_as_float(vv[3]) - c4.w, acc[4 * t4 + 3]);
-                                }
+                            for (int t4 = 0; t4 < TT / 4; ++t4) {
+                                const ulonglong2 d4 = d4p[t4], c4 = c4p[t4];
+                                const uint64_t v0 = (uint64_t)v[i][4 * t4] | ((uint64_t)v[i][4 * t4 + 1] << 32);
+                                const uint64_t v1 = (uint64_t)v[i][4 * t4 + 2] | ((uint64_t)v[i][4 * t4 + 3] << 32);
+                                acc[2 * t4] = tc::f2_fma(tc::f2_mul(dw2, d4.x), tc::f2_sub(v0, c4.x), acc[2 * t4]);
+                                acc[2 * t4 + 1] =
+                                    tc::f2_fma(tc::f2_mul(dw2, d4.y), tc::f2_sub(v1, c4.y), acc[2 * t4 + 1]);
                             }
                         }
+                    }
                     }
                     tc::tmem_wait_st();
                     tc::tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(tempty_bar(tg));
+                    if (lane == 0) tc::mbar_arrive(tempty0 + 8 * tg);
                     ++k;
                 }
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(eempty_bar(e));
+                if (lane == 0) tc::mbar_arrive(eempty0 + 8 * e);
                 ++j;
             }
             if (!ok) break;
@@ -412,8 +425,9 @@ __global__ void __launch_bounds__(Cfg<N>::kThreads, 1)
 #pragma unroll
                 for (int t = 0; t < TT; ++t) {
                     if (tb + t < a.batch) {
+                        const float v = __uint_as_float((uint32_t)(acc[t / 2] >> (32 * (t & 1))));
                         float* p = a.y + (size_t)(tb + t) * a.rows + r;
-                        *p = a.accumulate ? *p + acc[t] : acc[t];
+                        *p = a.accumulate ? *p + v : v;
                     }
                 }
             }
@@ -487,7 +501,7 @@ cudaError_t launch_tc(const mv_weight_s& w, const int8_t* q, const float* dT, ui
     const TcArgs args{y, (int)w.rows, (int)w.nb, (int)batch, n_ttiles, n_tiles, accumulate ? 1 : 0};
     ensure_smem_attr(gemm_tc_kernel<N>, C::kSmem);
     const int grid = n_tiles < num_sms() ? n_tiles : num_sms();
-    gemm_tc_kernel<N><<<grid, C::kThreads, C::kSmem, s>>>(wmap, xmap, dmap, smap, args);
+    gemm_tc_kernel<N><<<grid, kThreads, C::kSmem, s>>>(wmap, xmap, dmap, smap, args);
     return cudaGetLastError();
 }
 
@@ -498,25 +512,14 @@ cudaError_t gemm_q4_q8_tc(const mv_weight_s& w, const int8_t* q, const float* dT
     if (!batch) return cudaSuccess;
     if (w.type != 2 || ldb < gemm_tc_ldb(batch) || ldb % 4 || w.rows >= (1ull << 31) || batch >= (1ull << 31))
         return cudaErrorInvalidValue;
-    // Tile width N: a tile's time is dominated by a per-stage cost (barrier
-    // round trips, MMA issue) that hardly depends on N, plus ~1 cycle per
-    // token; pick the N with the fewest waves x cost.
+    // Tile width N: the epilogue's share grows with N, the per-block MMA,
+    // conversion and synchronisation share does not; pick the N with the
+    // fewest waves x cost.
     const uint64_t row_tiles = (w.rows + kM - 1) / kM, sms = (uint64_t)num_sms();
-    int best = 16;
-    double best_cost = 1e300;
-    for (int n : {16, 32, 64}) {
-        const uint64_t tiles = row_tiles * ((batch + n - 1) / n);
-        const double cost = (double)((tiles + sms - 1) / sms) * (200.0 + 1.0 * n);
-        if (cost < best_cost * 0.999) {
-            best = n;
-            best_cost = cost;
-        }
-    }
-    switch (best) {
-        case 16: return launch_tc<16>(w, q, dT, ldb, batch, y, s, accumulate);
-        case 32: return launch_tc<32>(w, q, dT, ldb, batch, y, s, accumulate);
-        default: return launch_tc<64>(w, q, dT, ldb, batch, y, s, accumulate);
-    }
+    const uint64_t w16 = (row_tiles * ((batch + 15) / 16) + sms - 1) / sms;
+    const uint64_t w32 = (row_tiles * ((batch + 31) / 32) + sms - 1) / sms;
+    return (double)w16 * 60.0 <= (double)w32 * 100.0 ? launch_tc<16>(w, q, dT, ldb, batch, y, s, accumulate)
+                                                     : launch_tc<32>(w, q, dT, ldb, batch, y, s, accumulate);
 }
 
 }  // namespace mvb

@@ -42,16 +42,26 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kCbStride = 34;    // float2 per chain-buffer row (16-byte aligned, conflict-free)
 constexpr uint32_t kLoNib = 0x0F0F0F0Fu;
 
+// dp4a with unsigned bytes in a, signed bytes in b
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// sum_k (nib_k - 8) * a_k of one block: low nibbles against elements 0..15,
+// the high nibbles kept in place (16 x nib, bytes up to 240, an unsigned dot)
+// against elements 16..31 and shifted back, minus c8 = 8 * sum(a).
 __device__ __forceinline__ int block_isum(const uint4 w, const int4 alo, const int4 ahi, int c8) {
     int s = dp4a((int)(w.x & kLoNib), alo.x, 0);
     s = dp4a((int)(w.y & kLoNib), alo.y, s);
     s = dp4a((int)(w.z & kLoNib), alo.z, s);
     s = dp4a((int)(w.w & kLoNib), alo.w, s);
-    s = dp4a((int)((w.x >> 4) & kLoNib), ahi.x, s);
-    s = dp4a((int)((w.y >> 4) & kLoNib), ahi.y, s);
-    s = dp4a((int)((w.z >> 4) & kLoNib), ahi.z, s);
-    s = dp4a((int)((w.w >> 4) & kLoNib), ahi.w, s);
-    return s - c8;
+    int h = dp4a_us(w.x & ~kLoNib, ahi.x, 0);
+    h = dp4a_us(w.y & ~kLoNib, ahi.y, h);
+    h = dp4a_us(w.z & ~kLoNib, ahi.z, h);
+    h = dp4a_us(w.w & ~kLoNib, ahi.w, h);
+    return s + (h >> 4) - c8;
 }
 
 struct Act {

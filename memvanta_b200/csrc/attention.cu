@@ -320,6 +320,252 @@ __global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
     a.out[((size_t)s * a.n_head + h) * HD + tid] = out;
 }
 
+// ------------------------------------------- fused decode step (F16/F32 KV)
+// One decode token: RoPE of the query and key heads, the append of this
+// token's K and V to the paged cache and the attention above, in one kernel
+// (grid n_head, hd threads).  The math is that of rope_append_heads_kernel
+// followed by attn_exact_kernel:
+//   * q and k rotate by the reference's half-split RoPE (fma(x0,c,-(x1*s)),
+//     fma(x0,s,x1*c)); the cache stores k and v as the reference's KV cache
+//     does (fp32, or fp16 rounded half-up), and this token's score and value
+//     use those stored values;
+//   * the cached tokens 0..p-1 are scored tile by tile as before, this token
+//     (t = p, last in order) after them; its value is the last FMA of every
+//     output chain -- the reference's order.
+// Before waiting on the previous kernel (the q|k|v GEMV) it only reads what
+// earlier decode steps wrote -- the position, the block table, the cached
+// K/V rows of tokens 0..p-1 -- so the first K tile and the first V tiles are
+// in flight while the GEMV finishes.  One CTA per kv head (h % group == 0)
+// writes the cache rows of this token.
+struct FusedSmem {
+    uint64_t q, table, sc, knew, vnew, kring, vring, total;
+};
+__host__ __device__ inline FusedSmem fused_plan(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type) {
+    auto up = [](uint64_t n) { return (n + 15) / 16 * 16; };
+    const uint64_t esize = kv_type == 0 ? 4 : 2;
+    const uint64_t krow = hd * esize + 16;
+    FusedSmem p;
+    p.q = 0;
+    p.table = up(hd * 4);
+    p.sc = p.table + up(max_pages * 4);
+    p.knew = p.sc + up(max_ctx * 4);
+    p.vnew = p.knew + up(hd * esize);
+    p.kring = p.vnew + up(hd * esize);
+    p.vring = p.kring + 2 * (uint64_t)attn_ktile(hd, kv_type) * krow;
+    p.total = p.vring + (uint64_t)kVStages * kVTile * hd * esize;
+    return p;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ float redf[HD / 32];
+    __shared__ double redd[HD / 32];
+    const int h = blockIdx.x, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int G = (int)(a.n_head / a.n_head_kv), kh = h / G;
+    const int D = (int)(a.n_head * HD), kv_dim = (int)(a.n_head_kv * HD);
+    const int kvt = a.kv_type, esize = kvt == 0 ? 4 : 2;
+    const int page = (int)a.page, half = HD / 2;
+    const FusedSmem P = fused_plan(HD, a.max_ctx, a.max_pages, kvt);
+    float* qs = reinterpret_cast<float*>(smem + P.q);
+    int* tbl = reinterpret_cast<int*>(smem + P.table);
+    float* sc = reinterpret_cast<float*>(smem + P.sc);
+    uint8_t* knew = smem + P.knew;
+    uint8_t* vnew = smem + P.vnew;
+    uint8_t* kring = smem + P.kring;
+    uint8_t* vring = smem + P.vring;
+    const uint8_t* kp = static_cast<const uint8_t*>(a.k_pages);
+    const uint8_t* vp = static_cast<const uint8_t*>(a.v_pages);
+    const size_t row_bytes = (size_t)kv_dim * esize;
+    const size_t head_off = (size_t)kh * HD * esize;
+    const int slice = HD * esize;  // bytes of one token's head slice
+
+    pdl_trigger();
+    const int p = a.pos[0];  // this token; tokens 0..p-1 are cached
+    const int npg = (p + page) / page;
+    for (int i = tid; i < npg; i += HD) tbl[i] = a.block_table[i];
+    __syncthreads();
+    auto slot_of = [&](int t) -> size_t { return (size_t)tbl[t / page] * page + t % page; };
+
+    const int krow = slice + 16;
+    const int KT = attn_ktile(HD, kvt);
+    const int nkt = (p + KT - 1) / KT;
+    auto issue_k = [&](int tile, int buf) {
+        const int t = tile * KT + tid;
+        if (tid < KT && t < p) {
+            const uint8_t* src = kp + slot_of(t) * row_bytes + head_off;
+            uint8_t* dst = kring + ((size_t)buf * KT + tid) * krow;
+            for (int c = 0; c < slice; c += 16) cp_async16(dst + c, src + c);
+        }
+        cp_async_commit();
+    };
+    const int chunks = kVTile * slice / 16;
+    const int nvt = (p + kVTile - 1) / kVTile;
+    auto issue_v = [&](int tile) {
+        if (tile < nvt) {
+            uint8_t* dst = vring + (size_t)(tile % kVStages) * kVTile * slice;
+            for (int c = tid; c < chunks; c += HD) {
+                const int tt = c / (slice / 16), off = (c % (slice / 16)) * 16;
+                const int t = tile * kVTile + tt;
+                if (t < p) cp_async16(dst + tt * slice + off, vp + slot_of(t) * row_bytes + head_off + off);
+            }
+        }
+        cp_async_commit();
+    };
+    // groups in flight: V tiles 0..kVStages-2, then K tile 0
+    for (int k = 0; k < kVStages - 1; ++k) issue_v(k);
+    issue_k(0, 0);
+
+    pdl_wait();
+    // this token: RoPE of q (head h) and k (kv head kh), k and v in cache form
+    {
+        const float* co = a.cos_t + (size_t)p * half;
+        const float* si = a.sin_t + (size_t)p * half;
+        const float* row = a.qkv;
+        if (tid < half) {
+            const float c = co[tid], sn = si[tid];
+            const float q0 = row[h * HD + tid], q1 = row[h * HD + tid + half];
+            qs[tid] = __fmaf_rn(q0, c, -__fmul_rn(q1, sn));
+            qs[tid + half] = __fmaf_rn(q0, sn, __fmul_rn(q1, c));
+            const float k0 = row[D + kh * HD + tid], k1 = row[D + kh * HD + tid + half];
+            const float r0 = __fmaf_rn(k0, c, -__fmul_rn(k1, sn)), r1 = __fmaf_rn(k0, sn, __fmul_rn(k1, c));
+            if (kvt == 1) {
+                reinterpret_cast<uint16_t*>(knew)[tid] = f32_to_f16_ref(r0);
+                reinterpret_cast<uint16_t*>(knew)[tid + half] = f32_to_f16_ref(r1);
+            } else {
+                reinterpret_cast<float*>(knew)[tid] = r0;
+                reinterpret_cast<float*>(knew)[tid + half] = r1;
+            }
+        }
+        const float v = row[D + kv_dim + kh * HD + tid];
+        if (kvt == 1) reinterpret_cast<uint16_t*>(vnew)[tid] = f32_to_f16_ref(v);
+        else reinterpret_cast<float*>(vnew)[tid] = v;
+    }
+    __syncthreads();
+    if (h % G == 0) {  // the cache rows of this token, once per kv head
+        const size_t at = slot_of(p) * row_bytes + head_off;
+        uint8_t* kd = static_cast<uint8_t*>(a.k_pages) + at;
+        uint8_t* vd = static_cast<uint8_t*>(a.v_pages) + at;
+        for (int i = tid; i < slice / 4; i += HD) {
+            reinterpret_cast<uint32_t*>(kd)[i] = reinterpret_cast<const uint32_t*>(knew)[i];
+            reinterpret_cast<uint32_t*>(vd)[i] = reinterpret_cast<const uint32_t*>(vnew)[i];
+        }
+    }
+    if (h == 0 && tid == 0 && a.ctx_out) a.ctx_out[0] = p + 1;
+
+    // 1. scores of the cached tokens, then this token's
+    auto dot_row = [&](const uint8_t* krw) -> float {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (kvt == 1) {
+#pragma unroll 4
+            for (int d = 0; d < HD; d += 8) {
+                const uint4 w = *reinterpret_cast<const uint4*>(krw + d * 2);
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int l = 0; l < 8; ++l)
+                    acc[l] = fmaf(qs[d + l], half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1)))), acc[l]);
+            }
+        } else {
+#pragma unroll 4
+            for (int d = 0; d < HD; d += 8) {
+                const float4 u = *reinterpret_cast<const float4*>(krw + d * 4);
+                const float4 v = *reinterpret_cast<const float4*>(krw + d * 4 + 16);
+                const float ks[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int l = 0; l < 8; ++l) acc[l] = fmaf(qs[d + l], ks[l], acc[l]);
+            }
+        }
+        float dot = acc[0];
+#pragma unroll
+        for (int l = 1; l < 8; ++l) dot += acc[l];
+        return dot / sqrtf((float)HD);
+    };
+    for (int tile = 0; tile < nkt; ++tile) {
+        if (tile + 1 < nkt) issue_k(tile + 1, (tile + 1) & 1);
+        else cp_async_commit();
+        cp_async_wait<1>();  // own row of this tile has landed (and, before it, the V tiles)
+        const int t = tile * KT + tid;
+        if (tid < KT && t < p) sc[t] = dot_row(kring + ((size_t)(tile & 1) * KT + tid) * krow);
+    }
+    if (tid == 0) sc[p] = dot_row(knew);
+    __syncthreads();
+
+    // 2. max, exp, double denominator, weights (all p + 1 tokens)
+    const int ctx = p + 1;
+    float m = -INFINITY;
+    for (int t = tid; t < ctx; t += HD) m = fmaxf(m, sc[t]);
+    m = warp_max(m);
+    if (lane == 0) redf[warp] = m;
+    __syncthreads();
+    m = redf[0];
+#pragma unroll
+    for (int w = 1; w < HD / 32; ++w) m = fmaxf(m, redf[w]);
+    double den = 0.0;
+    for (int t = tid; t < ctx; t += HD) {
+        const float e = expf_cr(sc[t] - m);
+        sc[t] = e;
+        den += (double)e;
+    }
+    den = warp_sum_d(den);
+    if (lane == 0) redd[warp] = den;
+    __syncthreads();
+    den = 0.0;
+#pragma unroll
+    for (int w = 0; w < HD / 32; ++w) den += redd[w];
+    const float inv = (float)(1.0 / den);
+
+    // 3. out_d = fma(alpha_t, v_t[d], out_d) over the cached tokens in order, then this token
+    float out = 0.0f;
+    for (int tile = 0; tile < nvt; ++tile) {
+        cp_async_wait<kVStages - 2>();
+        __syncthreads();  // the tile is visible to every thread
+        const uint8_t* vt = vring + (size_t)(tile % kVStages) * kVTile * slice;
+        const int n = min(kVTile, p - tile * kVTile);
+        for (int tt = 0; tt < n; ++tt) {
+            const float al = sc[tile * kVTile + tt] * inv;  // alpha_t = e_t * float(1/den)
+            const float v = kvt == 1 ? half_bits_to_float(reinterpret_cast<const uint16_t*>(vt + tt * slice)[tid])
+                                     : reinterpret_cast<const float*>(vt + tt * slice)[tid];
+            out = fmaf(al, v, out);
+        }
+        __syncthreads();  // everyone is done with this stage before it is refilled
+        issue_v(tile + kVStages - 1);
+    }
+    cp_async_wait<0>();
+    {
+        const float al = sc[p] * inv;
+        const float v = kvt == 1 ? half_bits_to_float(reinterpret_cast<const uint16_t*>(vnew)[tid])
+                                 : reinterpret_cast<const float*>(vnew)[tid];
+        out = fmaf(al, v, out);
+    }
+    a.out[(size_t)h * HD + tid] = out;
+}
+
+uint64_t attn_fused_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type) {
+    return fused_plan(hd, max_ctx, max_pages, kv_type).total;
+}
+
+cudaError_t attn_decode_fused(const AttnFusedArgs& a, cudaStream_t s) {
+    if (a.kv_type != 0 && a.kv_type != 1) return cudaErrorInvalidValue;
+    if (a.n_head % a.n_head_kv || a.hd % 32) return cudaErrorInvalidValue;
+    const size_t smem = attn_fused_smem_bytes(a.hd, a.max_ctx ? a.max_ctx : 1, a.max_pages, a.kv_type);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    const dim3 grid((unsigned)a.n_head);
+    switch (a.hd) {
+        case 64:
+            ensure_smem_attr(attn_decode_fused_kernel<64>, 200 * 1024);
+            return launch_pdl(attn_decode_fused_kernel<64>, grid, dim3(64), smem, s, a);
+        case 128:
+            ensure_smem_attr(attn_decode_fused_kernel<128>, 200 * 1024);
+            return launch_pdl(attn_decode_fused_kernel<128>, grid, dim3(128), smem, s, a);
+        case 256:
+            ensure_smem_attr(attn_decode_fused_kernel<256>, 200 * 1024);
+            return launch_pdl(attn_decode_fused_kernel<256>, grid, dim3(256), smem, s, a);
+        default:
+            return cudaErrorInvalidValue;
+    }
+}
+
 uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type) {
     return attn_plan(hd, max_ctx, max_pages, kv_type).total;
 }

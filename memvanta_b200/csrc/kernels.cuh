@@ -101,4 +101,22 @@ struct AttnArgs {
 uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type);
 cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s);
 
+// One decode token (F32 or F16 KV): RoPE + KV append + attention in one kernel.
+struct AttnFusedArgs {
+    int kv_type;                     // 0 F32, 1 F16
+    const float* qkv;                // this token's q heads | k heads | v heads (fp32, before RoPE)
+    uint64_t n_head, n_head_kv, hd;
+    const float* cos_t;              // [n_ctx][hd/2]
+    const float* sin_t;
+    const int32_t* pos;              // device: this token's position (tokens 0..pos-1 are cached)
+    const int32_t* block_table;      // [max_pages] page of every logical page
+    uint64_t max_pages, page, max_ctx;
+    void* k_pages;
+    void* v_pages;
+    int32_t* ctx_out;                // optional: receives pos + 1
+    float* out;                      // [n_head][hd]
+};
+uint64_t attn_fused_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type);
+cudaError_t attn_decode_fused(const AttnFusedArgs& a, cudaStream_t s);
+
 }  // namespace mvb

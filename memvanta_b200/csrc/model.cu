@@ -489,10 +489,21 @@ void launch_decode(mv_model_s* m, bool with_logits) {
     cudaStream_t s = m->stream;
     const uint64_t D = m->n_embd, QKVW = D + 2 * m->kv_dim;
     ck(mvb::read_rows(*m->tok_embd, m->token_dev, 1, m->x, s), "embed");
+    // F16/F32 KV: RoPE, the KV append and the attention are one kernel
+    const bool fused = m->kv_type == MV_KV_F32 || m->kv_type == MV_KV_F16;
     for (auto& L : m->layers) {
         project_decode(m, L.qkv, m->x, L.attn_norm, m->qkv, mvb::Q4Epi::Store);
-        rope_append(m, L, m->qkv, 1, m->pos_dev, m->ctx_dev);
-        ck(mvb::paged_attn_decode(attn_args(m, L, m->qkv, QKVW, 1, m->ctx_dev, m->n_ctx, m->att), s), "attention");
+        if (fused) {
+            const mvb::AttnFusedArgs fa{m->kv_type, m->qkv, m->n_head, m->n_head_kv, m->hd,
+                                        (const float*)m->rope_cos, (const float*)m->rope_sin, m->pos_dev,
+                                        (const int32_t*)m->table, m->n_pages, m->page, m->n_ctx,
+                                        L.k_pages, L.v_pages, m->ctx_dev, m->att};
+            ck(mvb::attn_decode_fused(fa, s), "attention (fused)");
+        } else {
+            rope_append(m, L, m->qkv, 1, m->pos_dev, m->ctx_dev);
+            ck(mvb::paged_attn_decode(attn_args(m, L, m->qkv, QKVW, 1, m->ctx_dev, m->n_ctx, m->att), s),
+               "attention");
+        }
         project_decode(m, L.o, m->att, nullptr, m->x, mvb::Q4Epi::AddTo);
         project_decode(m, L.gu, m->x, L.ffn_norm, m->ff, mvb::Q4Epi::SiluGate);
         project_decode(m, L.down, m->ff, nullptr, m->x, mvb::Q4Epi::AddTo);

@@ -383,7 +383,9 @@ def run_llama7b_ours(args, world, rank, local):
     for _ in range(K):
         cur = int(np.argmax(m.forward(cur)))
     e2e_s = all_max(time.perf_counter() - t0, world)
-    kernels_per_step = 1 + 6 * m.n_layer + 2
+    # embed; per layer q|k|v GEMV, fused RoPE+append+attention, o, gate|up, down;
+    # output RMSNorm + Q6_K head GEMV + greedy step
+    kernels_per_step = 1 + 5 * m.n_layer + 3
     m.close()
     gbs, alg_bytes, gemv_s, detail = gemv_roofline(dev, torch.cuda.Stream(device=dev))
     return {"tg_ms": tg_ms, "pp_ms": pp_ms, "e2e_s": e2e_s, "clocks": clk.summary(),
@@ -421,12 +423,19 @@ def main():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="llama7b", choices=["llama7b", "q4_gemv"])
+    ap.add_argument("--workload", default="llama7b", choices=["llama7b", "q4_gemv", "gemv", "gemm", "decode"],
+                    help="llama7b: the headline (config 3); q4_gemv: config 0; gemv / gemm / decode: one kernel "
+                         "or the 7B decode steps alone, for profiling")
+    ap.add_argument("--rows", type=int, default=12288, help="gemv/gemm: weight rows")
+    ap.add_argument("--cols", type=int, default=4096, help="gemv/gemm: weight cols (K)")
+    ap.add_argument("--batch", type=int, default=32, help="gemm: tokens")
     ap.add_argument("--clock-window", type=float, default=0.5)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup()
+    if args.workload in ("gemv", "gemm", "decode"):
+        return main_micro(args)
     if args.workload == "llama7b":
         return main_llama7b(args, world, rank, local)
     metric, unit = "Q4_0 GEMV achieved HBM GB/s (config 0, 4096x4096)", "GB/s"
@@ -474,6 +483,78 @@ def main():
                 "path": "mv_tensor_matvec_host (host x/y, H2D + GEMV + D2H + sync per call)"},
         "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["gpu_launches"],
     }
+    print(json.dumps(line), flush=True)
+
+
+def main_micro(args):
+    """One kernel (or the 7B decode steps alone) on one GPU, for profiling:
+    gemv = the decode GEMV on a rows x cols Q4_0 weight (activations
+    quantised per call), gemm = Q8 quantisation + the tensor-core GEMM for
+    `batch` tokens, decode = `steps` greedy decode steps of the 7B model after
+    its 128-token seed prefill.  Weights rotate through copies larger than L2;
+    launches are replayed from a CUDA graph and timed with events."""
+    import torch
+    import memvanta_b200 as mv
+    from memvanta_b200 import gguf
+    mv.init(0)
+    dev = torch.device("cuda", 0)
+    if args.workload == "decode":
+        m = mv.LlamaModel(ensure_llama7b(), ctx_override=L7_CTX, kv_page_tokens=16, kv_type=mv.KV_F16)
+        ms = torch.cuda.ExternalStream(m.stream)
+        seed = fixed_tokens(L7_SEED_TOKENS)
+        m.prefill(seed, L7_BATCH, False)
+        m.generate_greedy(17, args.warmup)
+        m.reset()
+        m.prefill(seed, L7_BATCH, False)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(ms)
+        m.generate_greedy(17, args.steps)
+        e1.record(ms)
+        torch.cuda.synchronize()
+        ms_step = e0.elapsed_time(e1) / args.steps
+        m.close()
+        print(json.dumps({"workload": "decode", "metric": "7B Q4_0 decode tok/s", "value": round(1e3 / ms_step, 2),
+                          "unit": "tok/s", "ms_per_step": round(ms_step, 4), "steps": args.steps}), flush=True)
+        return
+    rows, cols, B = args.rows, args.cols, args.batch
+    rng = np.random.default_rng(7)
+    wbytes = rows * cols // 32 * 18
+    copies = max(2, int(np.ceil(3 * 126e6 / wbytes)))
+    ws = [mv.Weight.upload(gguf.gen_q4_0(rows, cols, rng), mv.Q4_0, rows, cols) for _ in range(copies)]
+    n = max(args.steps, copies)
+    stream = torch.cuda.Stream(device=dev)
+    if args.workload == "gemv":
+        x, y = torch.randn(cols, device=dev), torch.empty(rows, device=dev)
+        launch = lambda w: mv.gemv(w, x, y, stream)  # noqa: E731
+    else:
+        x, y = torch.randn(B, cols, device=dev), torch.empty(B, rows, device=dev)
+        launch = lambda w: mv.gemm(w, x, y, mv.ACT_Q8, stream)  # noqa: E731
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 1)):
+            launch(ws[i % copies])
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                launch(ws[i % copies])
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    mv.stream_status(stream)
+    us = e0.elapsed_time(e1) * 1e3 / n
+    line = {"workload": args.workload, "rows": rows, "cols": cols, "us_per_launch": round(us, 3), "launches": n}
+    if args.workload == "gemv":
+        alg = wbytes + cols * 4 + rows * 4
+        line.update({"metric": "Q4_0 GEMV achieved GB/s", "value": round(alg / us / 1e3, 1), "unit": "GB/s",
+                     "algorithmic_bytes_per_launch": alg})
+    else:
+        line.update({"batch": B, "metric": "Q4_0 x Q8 GEMM TOPS (2*rows*cols*batch / time, quantisation included)",
+                     "value": round(2 * rows * cols * B / us / 1e6, 2), "unit": "TOPS"})
     print(json.dumps(line), flush=True)
 
 
@@ -525,11 +606,15 @@ def main_llama7b(args, world, rank, local):
         "data": "synthetic (random-init weights, seeded)", "config": config,
         "pp512_tok_s": round(pp * world, 2), "pp512_ms": round(r["pp_ms"], 2),
         "decode_weight_bw_gbs": round(bytes_per_token * tg / 1e9, 1),
-        "roofline": {"bound": "hbm", "kernel": "mvb::gemv_q4_kernel (Q4_0 x Q8 decode GEMV)",
-                     "achieved": round(r["gemv_gbs"], 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(r["gemv_gbs"] / peaks["hbm_gbs"], 4), "traffic": traffic_from_profiles("gemv_q4"),
+        # the dominant decode kernel, one launch of its q|k|v shape: live
+        # algorithmic bytes / live time; traffic = ncu DRAM bytes of the same launch
+        "roofline": {"bound": "hbm", "kernel": "mvb::gemv_q4_kernel (Q4_0 x Q8 decode GEMV), q|k|v 12288x4096 launch",
+                     "achieved": r["gemv_detail"]["qkv"]["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(r["gemv_detail"]["qkv"]["gbs"] / peaks["hbm_gbs"], 4),
+                     "traffic": traffic_from_profiles("gemv_q4_qkv"),
+                     "algorithmic_bytes_per_launch": 12288 * 4096 // 32 * 18 + 4096 * 4 + 12288 * 4,
                      "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, burst)",
-                     "shapes": r["gemv_detail"]},
+                     "all_shapes_weighted_gbs": round(r["gemv_gbs"], 1), "shapes": r["gemv_detail"]},
         "e2e": {"value": round(args.steps / r["e2e_s"] * world, 2), "unit": unit, "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 32000 * 4,
                 "path": "LlamaModel.forward (mv_model_forward): token in, host logits out, host argmax per token"},

@@ -17,9 +17,13 @@ Workloads:
 before the timed region so nvidia-smi has samples under load (the timed
 region itself is unchanged).
 
-Multi-GPU: one process per GPU under torchrun; every rank runs its own
-replica of the workload (the GEMV does not shard), timing is the max over
-ranks and `value` sums the work of all ranks.
+Multi-GPU: one process per GPU under torchrun.  llama7b runs ONE model
+split over the N GPUs by tensor parallelism (LlamaModel.tensor_parallel:
+q/k/v heads, o / gate / up / down / head rows sharded, activations
+all-gathered over NVLink peer memory inside the kernels), so the work is
+fixed as N grows ("scaling": "strong") and `value` is the one sequence's
+tok/s.  q4_gemv runs a replica per rank ("weak"; `value` sums the ranks).
+Timing is the max over ranks in both.
 
 `--impl reference` times the reference's own CPU code (oracle/_ref, built
 from the unmodified reference sources) on this host's cores, same metric.
@@ -283,16 +287,18 @@ def ensure_llama7b():
     return L7_PATH
 
 
-def gemv_roofline(dev, stream):
+def gemv_roofline(dev, stream, world=1):
     """Live timing of the decode GEMV (the dominant kernel) on the four decode
     shapes, weighted as one token uses them: per layer q|k|v 12288x4096,
-    o 4096x4096, gate|up 22016x4096 (SiLU pairs), down 4096x11008."""
+    o 4096x4096, gate|up 22016x4096 (SiLU pairs), down 4096x11008 -- each
+    rank's share of the rows under tensor parallelism over `world` GPUs."""
     import torch
     import memvanta_b200 as mv
     from memvanta_b200 import gguf
     rng = np.random.default_rng(7)
     total_bytes, total_s, detail = 0, 0.0, {}
-    for name, rows, cols in [("qkv", 12288, 4096), ("o", 4096, 4096), ("gate_up", 22016, 4096), ("down", 4096, 11008)]:
+    shapes = [("qkv", 12288, 4096), ("o", 4096, 4096), ("gate_up", 22016, 4096), ("down", 4096, 11008)]
+    for name, rows, cols in [(n, r // world, c) for n, r, c in shapes]:
         copies = max(2, int(np.ceil(3 * 126e6 / (rows * cols / 32 * 18))))  # > L2 in total
         ws = [mv.Weight.upload(gguf.gen_q4_0(rows, cols, rng), mv.Q4_0, rows, cols) for _ in range(copies)]
         x = torch.randn(cols, device=dev)
@@ -331,7 +337,11 @@ def run_llama7b_ours(args, world, rank, local):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     path = ensure_llama7b()
-    m = mv.LlamaModel(path, ctx_override=L7_CTX, kv_page_tokens=16, kv_type=mv.KV_F16)
+    if world > 1:  # one model over all ranks (tensor parallel, exact)
+        m = mv.LlamaModel.tensor_parallel(path, device=local, ctx_override=L7_CTX, kv_page_tokens=16,
+                                          kv_type=mv.KV_F16, prefill_batch=L7_BATCH)
+    else:
+        m = mv.LlamaModel(path, ctx_override=L7_CTX, kv_page_tokens=16, kv_type=mv.KV_F16)
     ms = torch.cuda.ExternalStream(m.stream)
     K, W = args.steps, args.warmup
     if L7_SEED_TOKENS + max(K, W) > L7_CTX:
@@ -384,10 +394,11 @@ def run_llama7b_ours(args, world, rank, local):
         cur = int(np.argmax(m.forward(cur)))
     e2e_s = all_max(time.perf_counter() - t0, world)
     # embed; per layer q|k|v GEMV, fused RoPE+append+attention, o, gate|up, down;
-    # output RMSNorm + Q6_K head GEMV + greedy step
-    kernels_per_step = 1 + 5 * m.n_layer + 3
+    # output RMSNorm + Q6_K head GEMV + greedy step; tensor parallel adds the
+    # wait before the head, the logits scatter, its wait and the step counter
+    kernels_per_step = 1 + 5 * m.n_layer + 3 + (4 if world > 1 else 0)
     m.close()
-    gbs, alg_bytes, gemv_s, detail = gemv_roofline(dev, torch.cuda.Stream(device=dev))
+    gbs, alg_bytes, gemv_s, detail = gemv_roofline(dev, torch.cuda.Stream(device=dev), world)
     return {"tg_ms": tg_ms, "pp_ms": pp_ms, "e2e_s": e2e_s, "clocks": clk.summary(),
             "gpu_launches": K * kernels_per_step + 1, "first_tokens": [int(t) for t in toks[:8]],
             "gemv_gbs": gbs, "gemv_detail": detail}
@@ -564,7 +575,8 @@ def main_llama7b(args, world, rank, local):
                           f"(16-token pages), ctx {L7_CTX}; {args.steps} greedy decode tokens from position "
                           f"{L7_SEED_TOKENS}; pp512 = 512-token prompt prefilled in batches of {L7_BATCH}",
               "model": "llama-7b-shape (32L, d4096, 32h x 128, ffn 11008, vocab 32000)",
-              "global_batch": 1, "seq_len": L7_CTX, "parallelism": f"replicas x{world}",
+              "global_batch": 1, "seq_len": L7_CTX,
+              "parallelism": f"tp{world} (exact all-gather tensor parallel)" if world > 1 else "single GPU",
               "l2": "decode reads 3.75 GB of weights per token (30x the 126 MB L2)"}
     if args.impl == "reference":
         if rank != 0:
@@ -599,23 +611,27 @@ def main_llama7b(args, world, rank, local):
     tg = args.steps / (r["tg_ms"] / 1e3)
     pp = L7_PP / (r["pp_ms"] / 1e3)
     bytes_per_token = 32 * L7_LAYER_W + L7_HEAD_W
+    qkv = r["gemv_detail"]["qkv"]
+    qkv_alg = qkv["rows"] * qkv["cols"] // 32 * 18 + qkv["cols"] * 4 + qkv["rows"] * 4
     line = {
-        "metric": metric, "value": round(tg * world, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
+        "metric": metric, "value": round(tg, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": r["tg_ms"] / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x q8 (int8 dot, fp32 accumulate)",
+        "scaling": "strong", "vs_baseline": None, "dtype": "q4_0 x q8 (int8 dot, fp32 accumulate)",
         "data": "synthetic (random-init weights, seeded)", "config": config,
-        "pp512_tok_s": round(pp * world, 2), "pp512_ms": round(r["pp_ms"], 2),
+        "pp512_tok_s": round(pp, 2), "pp512_ms": round(r["pp_ms"], 2),
         "decode_weight_bw_gbs": round(bytes_per_token * tg / 1e9, 1),
         # the dominant decode kernel, one launch of its q|k|v shape: live
         # algorithmic bytes / live time; traffic = ncu DRAM bytes of the same launch
-        "roofline": {"bound": "hbm", "kernel": "mvb::gemv_q4_kernel (Q4_0 x Q8 decode GEMV), q|k|v 12288x4096 launch",
-                     "achieved": r["gemv_detail"]["qkv"]["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(r["gemv_detail"]["qkv"]["gbs"] / peaks["hbm_gbs"], 4),
-                     "traffic": traffic_from_profiles("gemv_q4_qkv"),
-                     "algorithmic_bytes_per_launch": 12288 * 4096 // 32 * 18 + 4096 * 4 + 12288 * 4,
+        "roofline": {"bound": "hbm",
+                     "kernel": f"mvb::gemv_q4_kernel (Q4_0 x Q8 decode GEMV), q|k|v {qkv['rows']}x{qkv['cols']} "
+                               f"launch (one rank's share)",
+                     "achieved": qkv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(qkv["gbs"] / peaks["hbm_gbs"], 4),
+                     "traffic": traffic_from_profiles("gemv_q4_qkv") if world == 1 else None,
+                     "algorithmic_bytes_per_launch": qkv_alg,
                      "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, burst)",
                      "all_shapes_weighted_gbs": round(r["gemv_gbs"], 1), "shapes": r["gemv_detail"]},
-        "e2e": {"value": round(args.steps / r["e2e_s"] * world, 2), "unit": unit, "h2d_bytes_per_step": 4,
+        "e2e": {"value": round(args.steps / r["e2e_s"], 2), "unit": unit, "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 32000 * 4,
                 "path": "LlamaModel.forward (mv_model_forward): token in, host logits out, host argmax per token"},
         "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["gpu_launches"],

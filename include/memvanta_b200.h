@@ -226,6 +226,37 @@ MV_API int mv_model_generate_greedy(mv_model_t m, int32_t token, uint64_t n, int
 /* The model's stream (cudaStream_t) -- for event timing by the caller. */
 MV_API void* mv_model_stream(mv_model_t m);
 
+/* ---------------------------------------------- tensor parallel model */
+
+/* One process per GPU, `world` ranks of one node (2..8).  The reference runs
+ * on one host and has no counterpart; these three calls split the same
+ * LlamaModel over NVLink so that every call above returns the results of
+ * mv_model_open bit for bit.  Rank r holds q heads [r*H/world, ...), the same
+ * share of kv heads and their KV cache, and 1/world of the rows of every
+ * other matrix (o, gate, up, down, output); activations stay replicated and
+ * each kernel stores its slice into every rank's copy over peer memory.
+ * Needs Q4_0 layer weights, heads / kv heads / n_embd / n_ff / vocab divisible
+ * by world, and a KV type other than MV_KV_Q8.  prefill_batch bounds the
+ * `batch` of mv_model_prefill (0 -> 64).  Protocol:
+ *   mv_model_open_tp on every rank; mv_model_tp_handle on every rank; gather
+ *   the world handles (MV_TP_HANDLE_BYTES each, rank order) on every rank by
+ *   any host channel; mv_model_tp_connect on every rank at the same time.
+ * Afterwards every rank makes the same calls in the same order, each within
+ * the wait bound of the others (default 5 s, mv_model_tp_set_timeout).  A
+ * rank that stops answering makes the others' calls fail with MV_ERR_TIMEOUT
+ * once the bound runs out; the ranks are then out of step and every model is
+ * closed. */
+#define MV_TP_HANDLE_BYTES 64
+MV_API int mv_model_open_tp(const char* gguf_path, uint64_t ctx, uint64_t page_tokens, int kv_type, int rank,
+                            int world, uint64_t prefill_batch, mv_model_t* out);
+MV_API int mv_model_tp_handle(mv_model_t m, void* handle_out);
+MV_API int mv_model_tp_connect(mv_model_t m, const void* handles);
+/* Unmaps the other ranks' blocks (the model is unusable afterwards).  To
+ * close: barrier, mv_model_tp_disconnect, barrier, mv_model_close. */
+MV_API int mv_model_tp_disconnect(mv_model_t m);
+/* Bound, in milliseconds, of every wait for the other ranks (default 5000). */
+MV_API int mv_model_tp_set_timeout(mv_model_t m, uint64_t ms);
+
 #ifdef __cplusplus
 }
 #endif

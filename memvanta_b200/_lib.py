@@ -66,6 +66,11 @@ SIGNATURES = {
     "mv_model_prefill": (_i, [_p, _p, _u64, _u64, _i, _p]),
     "mv_model_generate_greedy": (_i, [_p, C.c_int32, _u64, _p]),
     "mv_model_stream": (_p, [_p]),
+    "mv_model_open_tp": (_i, [C.c_char_p, _u64, _u64, _i, _i, _i, _u64, C.POINTER(_p)]),
+    "mv_model_tp_handle": (_i, [_p, _p]),
+    "mv_model_tp_connect": (_i, [_p, _p]),
+    "mv_model_tp_set_timeout": (_i, [_p, _u64]),
+    "mv_model_tp_disconnect": (_i, [_p]),
 }
 
 

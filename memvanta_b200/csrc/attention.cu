@@ -12,6 +12,7 @@
 // generalises it to many sequences with scattered pages.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tp.cuh"
 
 namespace mvb {
 
@@ -538,7 +539,14 @@ __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) 
                                  : reinterpret_cast<const float*>(vnew)[tid];
         out = fmaf(al, v, out);
     }
-    a.out[(size_t)h * HD + tid] = out;
+    if (a.tp.world > 1) {
+        tp_for_each(a.tp, [&](int, char* base) {
+            reinterpret_cast<float*>(base + a.out_shared)[(size_t)(a.head_off + h) * HD + tid] = out;
+        });
+        if (a.signal_point >= 0) tp_signal_cta(a.tp, a.signal_point, a.slot);
+    } else {
+        a.out[(size_t)h * HD + tid] = out;
+    }
 }
 
 uint64_t attn_fused_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type) {

@@ -32,6 +32,7 @@
 // (nibbles 0..15 are non-negative bytes for the signed dp4a).
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tp.cuh"
 
 namespace mvb {
 
@@ -161,8 +162,8 @@ __device__ __forceinline__ void prologue(const float* __restrict__ x, const floa
         const int g = tid + it * bd;
         keep[it][0] = keep[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (g < G) {
-            keep[it][0] = x4[2 * g];
-            keep[it][1] = x4[2 * g + 1];
+            keep[it][0] = __ldcg(x4 + 2 * g);  // L2: other GPUs write x while kernels run
+            keep[it][1] = __ldcg(x4 + 2 * g + 1);
         }
     }
     float inv = 1.0f;
@@ -174,7 +175,7 @@ __device__ __forceinline__ void prologue(const float* __restrict__ x, const floa
         };
 #pragma unroll
         for (int it = 0; it < kKeep; ++it) acc(keep[it][0], keep[it][1]);
-        for (int g = tid + kKeep * bd; g < G; g += bd) acc(x4[2 * g], x4[2 * g + 1]);
+        for (int g = tid + kKeep * bd; g < G; g += bd) acc(__ldcg(x4 + 2 * g), __ldcg(x4 + 2 * g + 1));
         const double tot = block_sum_d(ss);
         inv = 1.0f / sqrtf((float)(tot / (double)(nb * 32)) + eps);
     }
@@ -190,8 +191,8 @@ __device__ __forceinline__ void prologue(const float* __restrict__ x, const floa
         const bool active = g < G;  // uniform over the 4 lanes of a block
         float4 u = make_float4(0.f, 0.f, 0.f, 0.f), w = u;
         if (active) {
-            u = x4[2 * g];
-            w = x4[2 * g + 1];
+            u = __ldcg(x4 + 2 * g);
+            w = __ldcg(x4 + 2 * g + 1);
         }
         quant_group(g, active, u, w, norm_w, rms, inv, a);
     }
@@ -282,19 +283,37 @@ __device__ __forceinline__ void consume_item(const uint8_t* st, const Act& a, fl
     __syncwarp();
 }
 
+// Output placement: y[idx] locally (y != nullptr), or, tensor parallel with
+// y == nullptr, y_row_off + idx in every rank's copy of the replicated buffer.
+struct YOut {
+    float* y;
+    const TpCtx& tp;
+    uint64_t shared;
+    int row_off;
+    bool replicated;
+    __device__ __forceinline__ float local(int idx) const {
+        return replicated ? __ldcg(reinterpret_cast<const float*>(tp_base(tp, tp.rank) + shared) + row_off + idx)
+                          : y[idx];
+    }
+    __device__ __forceinline__ void put(int idx, float v) const {
+        if (replicated) {
+            tp_for_each(tp, [&](int, char* base) { (reinterpret_cast<float*>(base + shared) + row_off)[idx] = v; });
+        } else {
+            y[idx] = v;
+        }
+    }
+};
+
 template <int RPW>
-__device__ __forceinline__ void epilogue(int epi, int rg, int rows, int lane, float sum, float* __restrict__ y) {
+__device__ __forceinline__ void epilogue(int epi, int rg, int rows, int lane, float sum, const YOut& yo) {
     if (epi == (int)Q4Epi::SiluGate) {
         // rows come in (gate_i, up_i) pairs: ff_i = g/(1+exp(-g)) * u
         const float u = __shfl_down_sync(0xffffffffu, sum, 1);
         const int r = rg * RPW + lane;
-        if (lane < RPW && (lane & 1) == 0 && r + 1 < rows) y[r / 2] = (sum / (1.0f + expf_cr(-sum))) * u;
+        if (lane < RPW && (lane & 1) == 0 && r + 1 < rows) yo.put(r / 2, (sum / (1.0f + expf_cr(-sum))) * u);
     } else {
         const int r = rg * RPW + lane;
-        if (lane < RPW && r < rows) {
-            if (epi == (int)Q4Epi::AddTo) y[r] += sum;
-            else y[r] = sum;
-        }
+        if (lane < RPW && r < rows) yo.put(r, epi == (int)Q4Epi::AddTo ? yo.local(r) + sum : sum);
     }
 }
 
@@ -303,7 +322,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __res
                                                               const unsigned short* __restrict__ dsc, int rows,
                                                               int nb, int dstride, const float* __restrict__ x,
                                                               const float* __restrict__ norm_w, float eps, int pro,
-                                                              int epi, float* __restrict__ y) {
+                                                              int epi, float* __restrict__ y, const TpCtx tp,
+                                                              uint64_t y_shared, int y_row_off, int wait_point,
+                                                              int signal_point, int slot_id) {
     using R = Ring<RPW>;
     const Act a = act_smem(nb);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -330,7 +351,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __res
         step(irg, ic);
     }
     pdl_wait();
+    if (tp.world > 1 && wait_point >= 0) tp_wait_cta(tp, wait_point, 100 + wait_point);
     prologue(x, norm_w, eps, pro == (int)Q4Pro::RmsNorm, nb, a);
+    const YOut yo{y, tp, y_shared, y_row_off, tp.world > 1 && y == nullptr};
 
     float sum = 0.0f;
     int rg = gw, c = 0, slot = 0, islot = R::S - 1;
@@ -343,13 +366,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __res
         step(irg, ic);
         if (++islot == R::S) islot = 0;
         if (c == nchunk - 1) {
-            epilogue<RPW>(epi, rg, rows, lane, sum, y);
+            epilogue<RPW>(epi, rg, rows, lane, sum, yo);
             sum = 0.0f;
         }
         step(rg, c);
         if (++slot == R::S) slot = 0;
     }
     cp_async_wait<0>();
+    if (tp.world > 1 && signal_point >= 0) tp_signal_cta(tp, signal_point, slot_id);
 }
 
 // Diagnostic twin: the per-block int32 dots of the same device code.
@@ -376,7 +400,8 @@ cudaError_t launch(const GemvQ4Args& g, cudaStream_t s) {
     const uint64_t cap = (uint64_t)num_sms() * 2;
     return launch_pdl(gemv_q4_kernel<RPW>, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(kThreads), smem, s,
                       reinterpret_cast<const uint4*>(w.qs), (const unsigned short*)w.d, (int)w.rows, (int)w.nb,
-                      (int)w.dstride, g.x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y);
+                      (int)w.dstride, g.x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y, g.tp ? *g.tp : TpCtx{},
+                      g.y_shared, g.y_row_off, g.wait_point, g.signal_point, g.slot);
 }
 
 }  // namespace
@@ -384,6 +409,7 @@ cudaError_t launch(const GemvQ4Args& g, cudaStream_t s) {
 cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s) {
     // x and norm_w are read as float4: the width must keep 8-element groups
     if (a.w->cols % 32) return cudaErrorInvalidValue;
+    if (!a.y && !(a.tp && a.tp->world > 1)) return cudaErrorInvalidValue;
     // Four rows per warp where the matrix has rows to spare (the chain cost
     // is shared by more rows), two otherwise so every SM has warps in flight.
     if (a.w->rows >= 8192) return launch<4>(a, s);

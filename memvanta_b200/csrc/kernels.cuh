@@ -4,6 +4,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <cstdint>
+#include "tp.cuh"
 #include "weights.cuh"
 
 #include <string>
@@ -45,6 +46,16 @@ struct GemvQ4Args {
     float* y;
     Q4Pro pro;
     Q4Epi epi;
+    // tensor parallel (tp.cuh), y == nullptr: the output is the replicated
+    // buffer at byte offset y_shared of every rank's shared block, this
+    // rank's rows land at y_row_off + row (SiluGate: y_row_off + row/2) in
+    // every copy.  With y set, tp only supplies the wait / signal points.
+    const TpCtx* tp = nullptr;
+    uint64_t y_shared = 0;
+    int y_row_off = 0;
+    int wait_point = -1;    // wait for this point's epoch before reading x
+    int signal_point = -1;  // publish this point's epoch when y is complete
+    int slot = 0;           // arrival counter
 };
 cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s);
 cudaError_t q4_block_dots(const mv_weight_s& w, const float* x, int32_t* isum, cudaStream_t s);
@@ -115,7 +126,21 @@ struct AttnFusedArgs {
     void* v_pages;
     int32_t* ctx_out;                // optional: receives pos + 1
     float* out;                      // [n_head][hd]
+    // tensor parallel: out is the replicated buffer at byte offset out_shared of
+    // every rank's shared block; this rank's heads start at head head_off
+    TpCtx tp;
+    uint64_t out_shared = 0;
+    int head_off = 0;
+    int signal_point = -1;
+    int slot = 0;
 };
+// ---- tp.cu (tensor parallel, protocol in tp.cuh)
+cudaError_t tp_wait(const TpCtx& tp, int point, cudaStream_t s);
+cudaError_t tp_scatter(const TpCtx& tp, const float* src, uint64_t rows, uint64_t w, uint64_t src_ld,
+                       uint64_t dst_shared, uint64_t dst_ld, uint64_t col_off, bool add, int point, int slot,
+                       cudaStream_t s);
+cudaError_t tp_step(int* step, cudaStream_t s);
+
 uint64_t attn_fused_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type);
 cudaError_t attn_decode_fused(const AttnFusedArgs& a, cudaStream_t s);
 

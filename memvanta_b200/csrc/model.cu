@@ -187,7 +187,7 @@ __global__ void greedy_step_kernel(const float* __restrict__ logits, int n, int3
     float v = -INFINITY;
     int idx = 0x7fffffff;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float x = logits[i];
+        const float x = __ldcg(logits + i);  // L2: other GPUs write their vocab slices
         if (x > v || (x == v && i < idx)) {
             v = x;
             idx = i;
@@ -311,6 +311,27 @@ struct mv_model_s {
     uint64_t in_cap = 0;
     int32_t *pf_tok = nullptr, *pf_pos = nullptr, *pf_ctx = nullptr;
     int32_t* pf_host = nullptr;            // pinned staging, 3 * in_cap
+
+    // Tensor parallelism (tp.cuh).  This rank holds q heads [rank*nh, +nh), kv
+    // heads [rank*nkv, +nkv) with their KV cache, o/down rows [rank*Dl, +Dl),
+    // ff rows [rank*Fl, +Fl) of gate and up, head rows [rank*Vl, +Vl); every
+    // GEMV keeps its full contraction, so the outputs equal one GPU's bit for
+    // bit.  One rank: the local sizes equal the global ones.
+    int tp_rank = 0, tp_world = 1;
+    uint64_t nh = 0, nkv = 0, kvd = 0, qkvw = 0, Dl = 0, Fl = 0, Vl = 0;
+    char* tp_block = nullptr;               // this rank's shared block (IPC-exported)
+    uint64_t tp_bytes = 0, tp_bmax = 0;     // size; prefill rows it holds
+    uint64_t off_x = 0, off_att = 0, off_ff = 0, off_logits = 0, off_X = 0, off_ATT = 0, off_FF = 0;
+    std::vector<void*> tp_opened;           // peers' blocks mapped into this process
+    mvb::TpCtx tp;
+    int* tp_step = nullptr;
+    unsigned* tp_counters = nullptr;
+    int* tp_status = nullptr;
+    long long* tp_limit = nullptr;          // wait bound in ns (device)
+    float* logits_l = nullptr;              // this rank's vocab slice
+    float *ATT_l = nullptr, *FF_l = nullptr, *PROJ_l = nullptr;  // prefill slices
+    bool tp_ready = false;                  // peers connected, graphs captured
+    int* tp_status_host = nullptr;          // pinned copy of tp_status
 };
 
 namespace {
@@ -376,6 +397,42 @@ float* upload_vector(mv_model_s* m, const mvb::GgufReader& f, const mvb::GgufTen
     return d;
 }
 
+// Rows [r0, r0 + n) of a matrix tensor (whole rows are contiguous bytes).
+struct RowRange {
+    const mvb::GgufTensorInfo* t;
+    uint64_t r0, n;
+};
+
+mv_weight_s* upload_rows(mv_model_s* m, const mvb::GgufReader& f, const std::vector<RowRange>& parts,
+                         bool interleave) {
+    const uint32_t type = parts[0].t->type;
+    const uint64_t cols = parts[0].t->ne(0);
+    for (auto& pr : parts)
+        if (pr.t->type != type || pr.t->ne(0) != cols || pr.t->dims.size() < 2 || pr.r0 + pr.n > pr.t->ne(1))
+            throw ModelError(MV_ERR_UNSUPPORTED, "row slices to fuse differ in type or width: " + pr.t->name);
+    const uint64_t row_bytes = parts[0].t->nbytes / parts[0].t->ne(1);
+    uint64_t rows = 0;
+    for (auto& pr : parts) rows += pr.n;
+    std::vector<uint8_t> buf(rows * row_bytes);
+    if (interleave) {  // gate/up: row 2i = gate_i, row 2i+1 = up_i
+        if (parts.size() != 2 || parts[0].n != parts[1].n)
+            throw ModelError(MV_ERR_INVALID, "gate/up shapes differ: " + parts[0].t->name);
+        const uint8_t* g = f.data(*parts[0].t) + parts[0].r0 * row_bytes;
+        const uint8_t* u = f.data(*parts[1].t) + parts[1].r0 * row_bytes;
+        for (uint64_t i = 0; i < parts[0].n; ++i) {
+            std::memcpy(buf.data() + (2 * i) * row_bytes, g + i * row_bytes, row_bytes);
+            std::memcpy(buf.data() + (2 * i + 1) * row_bytes, u + i * row_bytes, row_bytes);
+        }
+    } else {
+        uint64_t off = 0;
+        for (auto& pr : parts) {
+            std::memcpy(buf.data() + off, f.data(*pr.t) + pr.r0 * row_bytes, pr.n * row_bytes);
+            off += pr.n * row_bytes;
+        }
+    }
+    return upload_raw(m, buf.data(), buf.size(), (int)type, rows, cols);
+}
+
 // Concatenates whole rows of same-typed, same-width tensors (raw GGML bytes).
 mv_weight_s* upload_concat(mv_model_s* m, const mvb::GgufReader& f,
                                 const std::vector<const mvb::GgufTensorInfo*>& ts, bool interleave) {
@@ -409,15 +466,25 @@ mv_weight_s* upload_concat(mv_model_s* m, const mvb::GgufReader& f,
 
 void ensure_prefill(mv_model_s* m, uint64_t B) {
     if (B <= m->pf_cap) return;
-    const uint64_t D = m->n_embd, F = m->n_ff, QKVW = D + 2 * m->kv_dim;
+    const uint64_t D = m->n_embd, F = m->n_ff;
     const uint64_t K = std::max(D, F);
-    m->X = dalloc<float>(m, B * D);
+    const bool tp = m->tp_world > 1;
+    if (tp && B > m->tp_bmax)
+        throw ModelError(MV_ERR_INVALID, "prefill batch above the tensor-parallel prefill buffers (" +
+                                             std::to_string(m->tp_bmax) + " tokens)");
+    // replicated X / ATT / FF live in the shared block under tensor parallelism
+    m->X = tp ? reinterpret_cast<float*>(m->tp_block + m->off_X) : dalloc<float>(m, B * D);
     m->N = dalloc<float>(m, B * D);
-    m->QKV = dalloc<float>(m, B * QKVW);
-    m->ATT = dalloc<float>(m, B * D);
-    m->GU = dalloc<float>(m, B * 2 * F);
-    m->FF = dalloc<float>(m, B * F);
+    m->QKV = dalloc<float>(m, B * m->qkvw);
+    m->ATT = tp ? reinterpret_cast<float*>(m->tp_block + m->off_ATT) : dalloc<float>(m, B * D);
+    m->GU = dalloc<float>(m, B * 2 * m->Fl);
+    m->FF = tp ? reinterpret_cast<float*>(m->tp_block + m->off_FF) : dalloc<float>(m, B * F);
     m->PROJ = dalloc<float>(m, B * D);
+    if (tp) {
+        m->ATT_l = dalloc<float>(m, B * m->Dl);
+        m->FF_l = dalloc<float>(m, B * m->Fl);
+        m->PROJ_l = dalloc<float>(m, B * m->Dl);
+    }
     m->XQ = dalloc<int8_t>(m, B * K);
     m->XD = dalloc<float>(m, 2 * mvb::gemm_tc_ldb(B) * K / 32);  // block-major scales + constants
     if (B > m->table_rows) {
@@ -459,18 +526,18 @@ void project_decode(mv_model_s* m, mv_weight_s* w, const float* x, const float* 
 }
 
 void rope_append(mv_model_s* m, const mvb::Layer& L, float* qkv, uint64_t rows, const int32_t* pos, int32_t* ctx_out) {
-    const uint64_t QKVW = m->n_embd + 2 * m->kv_dim;
+    const uint64_t QKVW = m->qkvw;  // this rank's heads
     cudaError_t e;
     if (m->kv_type == MV_KV_Q8) {
         e = mvb::launch_pdl(mvb::rope_append_row_kernel, dim3((unsigned)rows), dim3(256), 0, m->stream, qkv, (int)QKVW,
-                            (int)m->n_head, (int)m->n_head_kv, (int)m->hd, (const float*)m->rope_cos,
+                            (int)m->nh, (int)m->nkv, (int)m->hd, (const float*)m->rope_cos,
                             (const float*)m->rope_sin, pos, m->kv_type, (const int32_t*)m->table, (int)m->page,
                             L.k_pages, L.v_pages, L.k_scales, L.v_scales, ctx_out);
     } else {
         const int threads = m->kv_type == MV_KV_Q8_0 ? (int)std::max<uint64_t>(64, m->hd) : (int)(m->hd / 2);
         e = mvb::launch_pdl(mvb::rope_append_heads_kernel,
-                            dim3((unsigned)rows, (unsigned)(m->n_head + 2 * m->n_head_kv)), dim3(threads), 0,
-                            m->stream, qkv, (int)QKVW, (int)m->n_head, (int)m->n_head_kv, (int)m->hd,
+                            dim3((unsigned)rows, (unsigned)(m->nh + 2 * m->nkv)), dim3(threads), 0,
+                            m->stream, qkv, (int)QKVW, (int)m->nh, (int)m->nkv, (int)m->hd,
                             (const float*)m->rope_cos, (const float*)m->rope_sin, pos, m->kv_type,
                             (const int32_t*)m->table, (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales,
                             ctx_out);
@@ -480,36 +547,95 @@ void rope_append(mv_model_s* m, const mvb::Layer& L, float* qkv, uint64_t rows, 
 
 mvb::AttnArgs attn_args(mv_model_s* m, const mvb::Layer& L, const float* q, uint64_t q_stride, uint64_t n_q,
                         const int32_t* ctx, uint64_t max_ctx, float* out) {
-    return mvb::AttnArgs{m->kv_type, q, q_stride, n_q, m->n_head, m->n_head_kv, m->hd, L.k_pages, L.v_pages,
+    return mvb::AttnArgs{m->kv_type, q, q_stride, n_q, m->nh, m->nkv, m->hd, L.k_pages, L.v_pages,
                          L.k_scales, L.v_scales, m->table, m->n_pages, m->page, ctx, max_ctx, out};
+}
+
+// Sync points of one step under tensor parallelism (tp.cuh): per layer the
+// attention heads, the o rows, the ff rows and the down rows, then the logits.
+int pt_att(uint64_t l) { return (int)(4 * l); }
+int pt_o(uint64_t l) { return (int)(4 * l + 1); }
+int pt_gu(uint64_t l) { return (int)(4 * l + 2); }
+int pt_down(uint64_t l) { return (int)(4 * l + 3); }
+int pt_head(const mv_model_s* m) { return (int)(4 * m->n_layer); }
+
+// One Q4_0 GEMV of a tensor-parallel decode step: reads the whole replicated
+// input once `wait` is published, writes this rank's rows at `row_off` of the
+// replicated output (every rank's copy) and publishes `signal`.
+void gemv_tp(mv_model_s* m, mv_weight_s* w, const float* x, const float* norm_w, mvb::Q4Epi epi, uint64_t y_off,
+             uint64_t row_off, int wait, int signal) {
+    mvb::GemvQ4Args a{w, x, norm_w, m->eps, nullptr, norm_w ? mvb::Q4Pro::RmsNorm : mvb::Q4Pro::Plain, epi};
+    a.tp = &m->tp;
+    a.y_shared = y_off;
+    a.y_row_off = (int)row_off;
+    a.wait_point = wait;
+    a.signal_point = signal;
+    a.slot = signal & 3;
+    ck(mvb::gemv_q4(a, m->stream), "gemv_q4 (tensor parallel)");
 }
 
 // Every kernel of one decode step, in order, on m->stream.
 void launch_decode(mv_model_s* m, bool with_logits) {
     cudaStream_t s = m->stream;
-    const uint64_t D = m->n_embd, QKVW = D + 2 * m->kv_dim;
+    const bool tp = m->tp_world > 1;
     ck(mvb::read_rows(*m->tok_embd, m->token_dev, 1, m->x, s), "embed");
     // F16/F32 KV: RoPE, the KV append and the attention are one kernel
     const bool fused = m->kv_type == MV_KV_F32 || m->kv_type == MV_KV_F16;
-    for (auto& L : m->layers) {
-        project_decode(m, L.qkv, m->x, L.attn_norm, m->qkv, mvb::Q4Epi::Store);
+    for (uint64_t l = 0; l < m->n_layer; ++l) {
+        auto& L = m->layers[l];
+        if (tp) {
+            mvb::GemvQ4Args a{L.qkv, m->x, L.attn_norm, m->eps, m->qkv, mvb::Q4Pro::RmsNorm, mvb::Q4Epi::Store};
+            a.tp = &m->tp;
+            a.wait_point = l ? pt_down(l - 1) : -1;
+            ck(mvb::gemv_q4(a, s), "gemv_q4 (tensor parallel)");
+        } else {
+            project_decode(m, L.qkv, m->x, L.attn_norm, m->qkv, mvb::Q4Epi::Store);
+        }
         if (fused) {
-            const mvb::AttnFusedArgs fa{m->kv_type, m->qkv, m->n_head, m->n_head_kv, m->hd,
-                                        (const float*)m->rope_cos, (const float*)m->rope_sin, m->pos_dev,
-                                        (const int32_t*)m->table, m->n_pages, m->page, m->n_ctx,
-                                        L.k_pages, L.v_pages, m->ctx_dev, m->att};
+            mvb::AttnFusedArgs fa{m->kv_type, m->qkv, m->nh, m->nkv, m->hd,
+                                  (const float*)m->rope_cos, (const float*)m->rope_sin, m->pos_dev,
+                                  (const int32_t*)m->table, m->n_pages, m->page, m->n_ctx,
+                                  L.k_pages, L.v_pages, m->ctx_dev, m->att};
+            if (tp) {
+                fa.tp = m->tp;
+                fa.out_shared = m->off_att;
+                fa.head_off = (int)(m->tp_rank * m->nh);
+                fa.signal_point = pt_att(l);
+                fa.slot = pt_att(l) & 3;
+            }
             ck(mvb::attn_decode_fused(fa, s), "attention (fused)");
         } else {
             rope_append(m, L, m->qkv, 1, m->pos_dev, m->ctx_dev);
-            ck(mvb::paged_attn_decode(attn_args(m, L, m->qkv, QKVW, 1, m->ctx_dev, m->n_ctx, m->att), s),
-               "attention");
+            float* out = tp ? m->ATT_l : m->att;
+            ck(mvb::paged_attn_decode(attn_args(m, L, m->qkv, m->qkvw, 1, m->ctx_dev, m->n_ctx, out), s), "attention");
+            if (tp)
+                ck(mvb::tp_scatter(m->tp, out, 1, m->Dl, m->Dl, m->off_att, m->n_embd, m->tp_rank * m->Dl, false,
+                                   pt_att(l), pt_att(l) & 3, s),
+                   "scatter");
         }
-        project_decode(m, L.o, m->att, nullptr, m->x, mvb::Q4Epi::AddTo);
-        project_decode(m, L.gu, m->x, L.ffn_norm, m->ff, mvb::Q4Epi::SiluGate);
-        project_decode(m, L.down, m->ff, nullptr, m->x, mvb::Q4Epi::AddTo);
+        if (tp) {
+            gemv_tp(m, L.o, m->att, nullptr, mvb::Q4Epi::AddTo, m->off_x, m->tp_rank * m->Dl, pt_att(l), pt_o(l));
+            gemv_tp(m, L.gu, m->x, L.ffn_norm, mvb::Q4Epi::SiluGate, m->off_ff, m->tp_rank * m->Fl, pt_o(l), pt_gu(l));
+            gemv_tp(m, L.down, m->ff, nullptr, mvb::Q4Epi::AddTo, m->off_x, m->tp_rank * m->Dl, pt_gu(l), pt_down(l));
+        } else {
+            project_decode(m, L.o, m->att, nullptr, m->x, mvb::Q4Epi::AddTo);
+            project_decode(m, L.gu, m->x, L.ffn_norm, m->ff, mvb::Q4Epi::SiluGate);
+            project_decode(m, L.down, m->ff, nullptr, m->x, mvb::Q4Epi::AddTo);
+        }
     }
+    // every rank's down rows are in x before the logits (and before the next
+    // step's embedding overwrites x)
+    if (tp) ck(mvb::tp_wait(m->tp, pt_down(m->n_layer - 1), s), "tp wait");
     if (with_logits) {
-        project_decode(m, m->output, m->x, m->output_norm, m->logits, mvb::Q4Epi::Store);
+        if (tp) {
+            project_decode(m, m->output, m->x, m->output_norm, m->logits_l, mvb::Q4Epi::Store);
+            ck(mvb::tp_scatter(m->tp, m->logits_l, 1, m->Vl, m->Vl, m->off_logits, m->vocab, m->tp_rank * m->Vl, false,
+                               pt_head(m), pt_head(m) & 3, s),
+               "scatter logits");
+            ck(mvb::tp_wait(m->tp, pt_head(m), s), "tp wait");
+        } else {
+            project_decode(m, m->output, m->x, m->output_norm, m->logits, mvb::Q4Epi::Store);
+        }
         ck(mvb::launch_pdl(mvb::greedy_step_kernel, dim3(1), dim3(1024), 0, s, (const float*)m->logits,
                            (int)m->vocab, m->token_dev, m->pos_dev, m->history),
            "greedy_step");
@@ -517,6 +643,7 @@ void launch_decode(mv_model_s* m, bool with_logits) {
         mvb::advance_pos_kernel<<<1, 1, 0, s>>>(m->pos_dev);
         ck(cudaGetLastError(), "advance_pos");
     }
+    if (tp) ck(mvb::tp_step(m->tp_step, s), "tp step");
 }
 
 cudaGraphExec_t capture_decode(mv_model_s* m, bool with_logits) {
@@ -565,7 +692,23 @@ void stage_prefill_inputs(mv_model_s* m, const int32_t* tokens, uint64_t n) {
     ck(cudaMemcpyAsync(m->pf_ctx, m->pf_host + 2 * n, n * 4, cudaMemcpyHostToDevice, m->stream), "ctx H2D");
 }
 
-void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, int kv_type) {
+// One eager step (pos 0, token 0) makes every kernel's attributes and the
+// library's lazy state ready before the decode graphs are captured; the KV
+// row it writes at position 0 is overwritten by the first real token.  With
+// tensor parallelism every rank runs it together (it synchronises).
+void ready_decode(mv_model_s* m) {
+    m->pos = 0;
+    set_decode_inputs(m, 0);
+    launch_decode(m, true);
+    ck(cudaStreamSynchronize(m->stream), "warm-up step");
+    m->graph_logits = capture_decode(m, true);
+    m->graph_nologits = capture_decode(m, false);
+    m->pos = 0;
+    m->tp_ready = true;
+}
+
+void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, int kv_type, int rank = 0,
+                int world = 1, uint64_t tp_bmax = 0) {
     mvb::GgufReader f(path);
     std::string arch;
     f.get_string("general.architecture", arch);
@@ -599,31 +742,63 @@ void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, in
     if (m->n_head / m->n_head_kv > 8) throw ModelError(MV_ERR_UNSUPPORTED, "GQA group above 8");
     if (kv_type < 0 || kv_type > 3) throw ModelError(MV_ERR_UNSUPPORTED, "unknown KV cache type");
     if (kv_type == MV_KV_Q8_0 && m->kv_dim % 32) throw ModelError(MV_ERR_INVALID, "Q8_0 KV needs kv_dim % 32 == 0");
+    if (world > 1 && kv_type == MV_KV_Q8)
+        throw ModelError(MV_ERR_UNSUPPORTED, "tensor parallelism splits the kv heads; the Q8 cache's per-token scale "
+                                             "spans all of them (use F16, F32 or Q8_0)");
     m->kv_type = kv_type;
     m->page = page ? page : 128;
     m->n_pages = (m->n_ctx + m->page - 1) / m->page;
+    // this rank's share (tensor parallel); the whole model on one rank
+    if (world < 1 || world > mvb::kTpMaxWorld || rank < 0 || rank >= world)
+        throw ModelError(MV_ERR_INVALID, "tensor-parallel rank/world out of range");
+    if (m->n_head % world || m->n_head_kv % world || m->n_embd % world || m->n_ff % world || m->vocab % world)
+        throw ModelError(MV_ERR_UNSUPPORTED, "tensor parallelism needs heads, kv heads, n_embd, n_ff and the vocab "
+                                             "divisible by the number of GPUs");
+    m->tp_rank = rank;
+    m->tp_world = world;
+    m->nh = m->n_head / world;
+    m->nkv = m->n_head_kv / world;
+    m->kvd = m->nkv * m->hd;
+    m->qkvw = m->nh * m->hd + 2 * m->kvd;
+    m->Dl = m->n_embd / world;
+    m->Fl = m->n_ff / world;
+    m->Vl = m->vocab / world;
     f.advise_sequential();
 
     m->tok_embd = upload_tensor(m, f, te);
     const auto& on = f.tensor("output_norm.weight");
     m->output_norm = upload_vector(m, f, on, m->n_embd);
     const mvb::GgufTensorInfo* out = f.find("output.weight");
-    m->output = out ? upload_tensor(m, f, *out) : m->tok_embd;  // tied output (:226)
+    if (world == 1) m->output = out ? upload_tensor(m, f, *out) : m->tok_embd;  // tied output (:226)
+    else m->output = upload_rows(m, f, {{out ? out : &te, rank * m->Vl, m->Vl}}, false);
 
     const uint64_t rows = m->n_pages * m->page;
-    const uint64_t rb = mvb::kv_row_bytes(kv_type, m->kv_dim), ns = mvb::kv_row_scales(kv_type, m->kv_dim);
+    const uint64_t rb = mvb::kv_row_bytes(kv_type, m->kvd), ns = mvb::kv_row_scales(kv_type, m->kvd);
     m->layers.resize(m->n_layer);
     for (uint64_t i = 0; i < m->n_layer; ++i) {
         auto name = [&](const char* s) { return "blk." + std::to_string(i) + s; };
         auto& L = m->layers[i];
         L.attn_norm = upload_vector(m, f, f.tensor(name(".attn_norm.weight")), m->n_embd);
         L.ffn_norm = upload_vector(m, f, f.tensor(name(".ffn_norm.weight")), m->n_embd);
-        L.qkv = upload_concat(m, f, {&f.tensor(name(".attn_q.weight")), &f.tensor(name(".attn_k.weight")),
-                                     &f.tensor(name(".attn_v.weight"))}, false);
-        if (L.qkv->rows != m->n_embd + 2 * m->kv_dim) throw ModelError(MV_ERR_INVALID, "q/k/v shape mismatch");
-        L.o = upload_tensor(m, f, f.tensor(name(".attn_output.weight")));
-        L.gu = upload_concat(m, f, {&f.tensor(name(".ffn_gate.weight")), &f.tensor(name(".ffn_up.weight"))}, true);
-        L.down = upload_tensor(m, f, f.tensor(name(".ffn_down.weight")));
+        const auto &tq = f.tensor(name(".attn_q.weight")), &tk = f.tensor(name(".attn_k.weight")),
+                   &tv = f.tensor(name(".attn_v.weight"));
+        const auto &to = f.tensor(name(".attn_output.weight")), &tg = f.tensor(name(".ffn_gate.weight")),
+                   &tu = f.tensor(name(".ffn_up.weight")), &td = f.tensor(name(".ffn_down.weight"));
+        if (world == 1) {
+            L.qkv = upload_concat(m, f, {&tq, &tk, &tv}, false);
+            L.o = upload_tensor(m, f, to);
+            L.gu = upload_concat(m, f, {&tg, &tu}, true);
+            L.down = upload_tensor(m, f, td);
+        } else {
+            const uint64_t q0 = rank * m->nh * m->hd, k0 = rank * m->kvd;
+            L.qkv = upload_rows(m, f, {{&tq, q0, m->nh * m->hd}, {&tk, k0, m->kvd}, {&tv, k0, m->kvd}}, false);
+            L.o = upload_rows(m, f, {{&to, rank * m->Dl, m->Dl}}, false);
+            L.gu = upload_rows(m, f, {{&tg, rank * m->Fl, m->Fl}, {&tu, rank * m->Fl, m->Fl}}, true);
+            L.down = upload_rows(m, f, {{&td, rank * m->Dl, m->Dl}}, false);
+            if (L.qkv->type != 2 || L.o->type != 2 || L.gu->type != 2 || L.down->type != 2)
+                throw ModelError(MV_ERR_UNSUPPORTED, "tensor parallelism needs Q4_0 layer weights");
+        }
+        if (L.qkv->rows != m->qkvw) throw ModelError(MV_ERR_INVALID, "q/k/v shape mismatch");
         L.k_pages = dalloc<uint8_t>(m, rows * rb);
         L.v_pages = dalloc<uint8_t>(m, rows * rb);
         L.k_scales = ns ? dalloc<float>(m, rows * ns) : nullptr;
@@ -645,36 +820,60 @@ void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, in
     ck(cudaMemcpy(m->rope_sin, si.data(), si.size() * 4, cudaMemcpyHostToDevice), "rope sin");
 
     const uint64_t D = m->n_embd, F = m->n_ff;
-    m->x = dalloc<float>(m, D);
-    m->qkv = dalloc<float>(m, D + 2 * m->kv_dim);
-    m->att = dalloc<float>(m, D);
-    m->ff = dalloc<float>(m, F);
-    m->gu = dalloc<float>(m, 2 * F);
+    if (world > 1) {
+        // the shared block every rank maps: flags, then the replicated buffers
+        auto up = [](uint64_t b) { return (b + 255) / 256 * 256; };
+        m->tp_bmax = tp_bmax ? tp_bmax : 64;
+        uint64_t off = mvb::kTpFlagsBytes;
+        m->off_x = off, off += up(D * 4);
+        m->off_att = off, off += up(D * 4);
+        m->off_ff = off, off += up(F * 4);
+        m->off_logits = off, off += up(m->vocab * 4);
+        m->off_X = off, off += up(m->tp_bmax * D * 4);
+        m->off_ATT = off, off += up(m->tp_bmax * D * 4);
+        m->off_FF = off, off += up(m->tp_bmax * F * 4);
+        m->tp_bytes = off;
+        ck(cudaMalloc(reinterpret_cast<void**>(&m->tp_block), m->tp_bytes), "cudaMalloc(shared block)");
+        ck(cudaMemset(m->tp_block, 0, m->tp_bytes), "clear shared block");
+        m->x = reinterpret_cast<float*>(m->tp_block + m->off_x);
+        m->att = reinterpret_cast<float*>(m->tp_block + m->off_att);
+        m->ff = reinterpret_cast<float*>(m->tp_block + m->off_ff);
+        m->logits = reinterpret_cast<float*>(m->tp_block + m->off_logits);
+        m->logits_l = dalloc<float>(m, std::max(m->Vl, std::max(2 * m->Fl, D)));
+        m->tp_step = dalloc<int>(m, 1);
+        m->tp_counters = dalloc<unsigned>(m, 8);
+        m->tp_status = dalloc<int>(m, 1);
+        ck(cudaMemset(m->tp_step, 0, 4), "clear step");
+        ck(cudaMemset(m->tp_counters, 0, 32), "clear counters");
+        ck(cudaMemset(m->tp_status, 0, 4), "clear status");
+        m->tp_limit = dalloc<long long>(m, 1);
+        const long long lim = mvb::kTpDefaultLimitNs;
+        ck(cudaMemcpy(m->tp_limit, &lim, 8, cudaMemcpyHostToDevice), "wait limit");
+    } else {
+        m->x = dalloc<float>(m, D);
+        m->att = dalloc<float>(m, D);
+        m->ff = dalloc<float>(m, F);
+        m->logits = dalloc<float>(m, std::max(m->vocab, std::max(2 * F, D)));
+    }
+    m->qkv = dalloc<float>(m, m->qkvw);
+    m->gu = dalloc<float>(m, 2 * m->Fl);
     m->nrm = dalloc<float>(m, D);
-    m->logits = dalloc<float>(m, std::max(m->vocab, std::max(2 * F, D)));
     m->token_dev = dalloc<int32_t>(m, 1);
     m->pos_dev = dalloc<int32_t>(m, 1);
     m->ctx_dev = dalloc<int32_t>(m, 1);
     m->history = dalloc<int32_t>(m, m->n_ctx + 1);
     ck(cudaMallocHost(reinterpret_cast<void**>(&m->logits_host), m->vocab * sizeof(float)), "cudaMallocHost");
     ensure_prefill(m, 1);  // identity block table
-
-    // One eager step (pos 0, token 0) makes every kernel's attributes and the
-    // library's lazy state ready before the decode graphs are captured; the
-    // KV row it writes at position 0 is overwritten by the first real token.
-    m->pos = 0;
-    set_decode_inputs(m, 0);
-    launch_decode(m, true);
-    ck(cudaStreamSynchronize(m->stream), "warm-up step");
-    m->graph_logits = capture_decode(m, true);
-    m->graph_nologits = capture_decode(m, false);
-    m->pos = 0;
+    if (world == 1) ready_decode(m);  // tensor parallel: once the peers are connected
 }
 
 void free_model(mv_model_s* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->graph_logits) cudaGraphExecDestroy(m->graph_logits);
     if (m->graph_nologits) cudaGraphExecDestroy(m->graph_nologits);
+    for (void* p : m->tp_opened) cudaIpcCloseMemHandle(p);
+    if (m->tp_block) cudaFree(m->tp_block);
+    if (m->tp_status_host) cudaFreeHost(m->tp_status_host);
     for (auto* w : m->owned) mv_weight_free(w);
     for (void* p : m->allocs) cudaFree(p);
     if (m->logits_host) cudaFreeHost(m->logits_host);
@@ -702,10 +901,27 @@ int model_fail(int rc) {
     return rc;
 }
 
+// Tensor parallel: calls need every rank connected; the status word a bounded
+// wait sets is copied back with the call's results and checked after its sync.
+void require_ready(const mv_model_s* m) {
+    if (m->tp_world > 1 && !m->tp_ready)
+        throw ModelError(MV_ERR_INVALID, "tensor-parallel model used before mv_model_tp_connect");
+}
+void enqueue_tp_status(mv_model_s* m) {
+    if (m->tp_world > 1)
+        ck(cudaMemcpyAsync(m->tp_status_host, m->tp_status, 4, cudaMemcpyDeviceToHost, m->stream), "status D2H");
+}
+void check_tp_status(const mv_model_s* m) {
+    if (m->tp_world > 1 && *m->tp_status_host)
+        throw ModelError(MV_ERR_TIMEOUT, "tensor-parallel wait for the other ranks gave up (site " +
+                                             std::to_string(*m->tp_status_host) + ")");
+}
+
 // One chunk of B tokens; `off` indexes the call's staged inputs.
 void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     cudaStream_t s = m->stream;
-    const uint64_t D = m->n_embd, F = m->n_ff, QKVW = D + 2 * m->kv_dim;
+    const uint64_t D = m->n_embd, F = m->n_ff;
+    const bool tp = m->tp_world > 1;
     const uint64_t start = m->pos;
     const int32_t* tok = m->pf_tok + off;
     const int32_t* pos = m->pf_pos + off;
@@ -737,21 +953,52 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
             project(w, m->N, D, out, false);
         }
     };
-    for (auto& L : m->layers) {
+    // tensor parallel: this rank's columns [col, col + w) of every row into
+    // every rank's replicated buffer, then wait for the other ranks' columns
+    auto exchange = [&](const float* src, uint64_t w, uint64_t dst_off, uint64_t dst_ld, uint64_t col, bool add,
+                        int point) {
+        ck(mvb::tp_scatter(m->tp, src, B, w, w, dst_off, dst_ld, col, add, point, point & 3, s), "scatter");
+        ck(mvb::tp_wait(m->tp, point, s), "tp wait");
+    };
+    for (uint64_t l = 0; l < m->n_layer; ++l) {
+        auto& L = m->layers[l];
         project_normed(L.qkv, L.attn_norm, m->QKV);
         rope_append(m, L, m->QKV, B, pos, nullptr);
-        ck(mvb::paged_attn_decode(attn_args(m, L, m->QKV, QKVW, B, ctx, start + B, m->ATT), s), "attention");
-        project(L.o, m->ATT, D, m->X, true);
+        ck(mvb::paged_attn_decode(attn_args(m, L, m->QKV, m->qkvw, B, ctx, start + B, tp ? m->ATT_l : m->ATT), s),
+           "attention");
+        if (tp) {
+            exchange(m->ATT_l, m->Dl, m->off_ATT, D, m->tp_rank * m->Dl, false, pt_att(l));
+            project(L.o, m->ATT, D, m->PROJ_l, false);
+            exchange(m->PROJ_l, m->Dl, m->off_X, D, m->tp_rank * m->Dl, true, pt_o(l));
+        } else {
+            project(L.o, m->ATT, D, m->X, true);
+        }
         project_normed(L.gu, L.ffn_norm, m->GU);
-        mvb::silu_pairs_kernel<<<mvb::ew_grid(B * F), 256, 0, s>>>(m->GU, m->FF, B * F);
+        float* ff = tp ? m->FF_l : m->FF;
+        mvb::silu_pairs_kernel<<<mvb::ew_grid(B * m->Fl), 256, 0, s>>>(m->GU, ff, B * m->Fl);
         ck(cudaGetLastError(), "silu_pairs");
-        project(L.down, m->FF, F, m->X, true);
+        if (tp) {
+            exchange(m->FF_l, m->Fl, m->off_FF, F, m->tp_rank * m->Fl, false, pt_gu(l));
+            project(L.down, m->FF, F, m->PROJ_l, false);
+            exchange(m->PROJ_l, m->Dl, m->off_X, D, m->tp_rank * m->Dl, true, pt_down(l));
+        } else {
+            project(L.down, m->FF, F, m->X, true);
+        }
     }
     m->pos += B;
     if (logits_last) {
         const float* last = m->X + (B - 1) * D;
-        project_decode(m, m->output, last, m->output_norm, m->logits, mvb::Q4Epi::Store);
+        if (tp) {
+            project_decode(m, m->output, last, m->output_norm, m->logits_l, mvb::Q4Epi::Store);
+            ck(mvb::tp_scatter(m->tp, m->logits_l, 1, m->Vl, m->Vl, m->off_logits, m->vocab, m->tp_rank * m->Vl,
+                               false, pt_head(m), pt_head(m) & 3, s),
+               "scatter logits");
+            ck(mvb::tp_wait(m->tp, pt_head(m), s), "tp wait");
+        } else {
+            project_decode(m, m->output, last, m->output_norm, m->logits, mvb::Q4Epi::Store);
+        }
     }
+    if (tp) ck(mvb::tp_step(m->tp_step, s), "tp step");
 }
 
 }  // namespace
@@ -773,6 +1020,90 @@ MV_API int mv_model_open(const char* path, uint64_t ctx, uint64_t page_tokens, i
     }
     *out = m;
     return MV_OK;
+}
+
+MV_API int mv_model_open_tp(const char* path, uint64_t ctx, uint64_t page_tokens, int kv_type, int rank, int world,
+                            uint64_t prefill_batch, mv_model_t* out) {
+    if (!out || !path) return MV_ERR_INVALID;
+    *out = nullptr;
+    auto* m = new mv_model_s();
+    int rc = guarded([&] {
+        ck(cudaGetDevice(&m->device), "cudaGetDevice");
+        ck(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        load_model(m, path, ctx, page_tokens, kv_type, rank, world, prefill_batch);
+        if (world > 1)
+            ck(cudaMallocHost(reinterpret_cast<void**>(&m->tp_status_host), sizeof(int)), "cudaMallocHost");
+    });
+    if (rc) {
+        free_model(m);
+        return model_fail(rc);
+    }
+    *out = m;
+    return MV_OK;
+}
+
+MV_API int mv_model_tp_handle(mv_model_t m, void* handle_out) {
+    if (!m || !handle_out || m->tp_world < 2) return MV_ERR_INVALID;
+    int rc = guarded([&] {
+        cudaIpcMemHandle_t h;
+        ck(cudaIpcGetMemHandle(&h, m->tp_block), "cudaIpcGetMemHandle");
+        std::memcpy(handle_out, &h, sizeof(h));
+    });
+    return rc ? model_fail(rc) : MV_OK;
+}
+
+MV_API int mv_model_tp_connect(mv_model_t m, const void* handles) {
+    if (!m || !handles || m->tp_world < 2 || m->tp_ready) return MV_ERR_INVALID;
+    int rc = guarded([&] {
+        static_assert(sizeof(cudaIpcMemHandle_t) == MV_TP_HANDLE_BYTES, "IPC handle size");
+        mvb::TpCtx t;
+        t.world = m->tp_world;
+        t.rank = m->tp_rank;
+        for (int d = 0; d < m->tp_world; ++d) {
+            if (d == m->tp_rank) {
+                t.base[d] = m->tp_block;
+                continue;
+            }
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, static_cast<const char*>(handles) + d * sizeof(h), sizeof(h));
+            void* p = nullptr;
+            ck(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+            m->tp_opened.push_back(p);
+            t.base[d] = static_cast<char*>(p);
+        }
+        t.step = m->tp_step;
+        t.pps = (int)(4 * m->n_layer + 1);
+        t.counters = m->tp_counters;
+        t.status = m->tp_status;
+        t.limit_ns = m->tp_limit;
+        m->tp = t;
+        ready_decode(m);  // every rank together: the warm-up step exchanges
+        enqueue_tp_status(m);
+        ck(cudaStreamSynchronize(m->stream), "sync");
+        check_tp_status(m);
+    });
+    return rc ? model_fail(rc) : MV_OK;
+}
+
+MV_API int mv_model_tp_disconnect(mv_model_t m) {
+    if (!m || m->tp_world < 2) return MV_ERR_INVALID;
+    int rc = guarded([&] {
+        ck(cudaStreamSynchronize(m->stream), "sync");
+        for (void* p : m->tp_opened) ck(cudaIpcCloseMemHandle(p), "cudaIpcCloseMemHandle");
+        m->tp_opened.clear();
+        m->tp_ready = false;
+    });
+    return rc ? model_fail(rc) : MV_OK;
+}
+
+MV_API int mv_model_tp_set_timeout(mv_model_t m, uint64_t ms) {
+    if (!m || m->tp_world < 2 || ms == 0) return MV_ERR_INVALID;
+    int rc = guarded([&] {
+        const long long ns = (long long)std::min<uint64_t>(ms, 3600000) * 1000000ll;
+        ck(cudaMemcpyAsync(m->tp_limit, &ns, 8, cudaMemcpyHostToDevice, m->stream), "wait limit");
+        ck(cudaStreamSynchronize(m->stream), "sync");
+    });
+    return rc ? model_fail(rc) : MV_OK;
 }
 
 MV_API int mv_model_close(mv_model_t m) {
@@ -804,8 +1135,8 @@ MV_API uint64_t mv_model_kv_bytes(mv_model_t m) {
     // pages the current position has touched, as PagedKVCache allocates them
     if (!m) return 0;
     const uint64_t pages = (m->pos + m->page - 1) / m->page;
-    const uint64_t per_row = mvb::kv_row_bytes(m->kv_type, m->kv_dim) +
-                             4 * mvb::kv_row_scales(m->kv_type, m->kv_dim);
+    const uint64_t per_row = mvb::kv_row_bytes(m->kv_type, m->kvd) +  // this rank's kv heads
+                             4 * mvb::kv_row_scales(m->kv_type, m->kvd);
     return 2 * m->n_layer * pages * m->page * per_row;
 }
 
@@ -816,12 +1147,15 @@ MV_API int mv_model_forward(mv_model_t m, int32_t token, int compute_logits, flo
     int rc = guarded([&] {
         if (token < 0 || (uint64_t)token >= m->vocab) throw ModelError(MV_ERR_INVALID, "token id out of range");
         if (m->pos >= m->n_ctx) throw ModelError(MV_ERR_INVALID, "context exhausted");
+        require_ready(m);
         set_decode_inputs(m, token);
         ck(cudaGraphLaunch(compute_logits ? m->graph_logits : m->graph_nologits, m->stream), "graph launch");
         m->pos += 1;
         if (compute_logits) {
             ck(cudaMemcpyAsync(m->logits_host, m->logits, m->vocab * 4, cudaMemcpyDeviceToHost, m->stream), "logits D2H");
+            enqueue_tp_status(m);
             ck(cudaStreamSynchronize(m->stream), "sync");
+            check_tp_status(m);
             if (logits_host) std::memcpy(logits_host, m->logits_host, m->vocab * 4);
         }
     });
@@ -837,6 +1171,7 @@ MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uin
         if (m->pos + n > m->n_ctx) throw ModelError(MV_ERR_INVALID, "context exhausted");
         for (uint64_t i = 0; i < n; ++i)
             if (tokens[i] < 0 || (uint64_t)tokens[i] >= m->vocab) throw ModelError(MV_ERR_INVALID, "token id out of range");
+        require_ready(m);
         const uint64_t B = std::max<uint64_t>(1, batch);
         ck(cudaStreamSynchronize(m->stream), "sync");
         ensure_prefill(m, std::min(B, n));
@@ -845,13 +1180,12 @@ MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uin
             const uint64_t nb = std::min(B, n - i);
             prefill_chunk(m, i, nb, compute_logits && i + nb == n);
         }
-        if (compute_logits) {
+        if (compute_logits)
             ck(cudaMemcpyAsync(m->logits_host, m->logits, m->vocab * 4, cudaMemcpyDeviceToHost, m->stream), "logits D2H");
-            ck(cudaStreamSynchronize(m->stream), "sync");
-            if (logits_host) std::memcpy(logits_host, m->logits_host, m->vocab * 4);
-        } else {
-            ck(cudaStreamSynchronize(m->stream), "sync");
-        }
+        enqueue_tp_status(m);
+        ck(cudaStreamSynchronize(m->stream), "sync");
+        check_tp_status(m);
+        if (compute_logits && logits_host) std::memcpy(logits_host, m->logits_host, m->vocab * 4);
         int status = 0;
         ck(mvb::tc_status(m->stream, &status), "status");
         if (status)
@@ -867,12 +1201,15 @@ MV_API int mv_model_generate_greedy(mv_model_t m, int32_t token, uint64_t n, int
         if (!out_tokens) throw ModelError(MV_ERR_INVALID, "null output");
         if (token < 0 || (uint64_t)token >= m->vocab) throw ModelError(MV_ERR_INVALID, "token id out of range");
         if (m->pos + n > m->n_ctx) throw ModelError(MV_ERR_INVALID, "context exhausted");
+        require_ready(m);
         const uint64_t start = m->pos;
         set_decode_inputs(m, token);
         for (uint64_t i = 0; i < n; ++i) ck(cudaGraphLaunch(m->graph_logits, m->stream), "graph launch");
         ck(cudaMemcpyAsync(out_tokens, m->history + start, n * 4, cudaMemcpyDeviceToHost, m->stream), "tokens D2H");
+        enqueue_tp_status(m);
         ck(cudaStreamSynchronize(m->stream), "sync");
         m->pos += n;
+        check_tp_status(m);
     });
     return rc ? model_fail(rc) : MV_OK;
 }

@@ -188,7 +188,7 @@ __global__ void quantize_q8_t_kernel(const float* __restrict__ x, uint64_t rows,
     float* cT = dT + nb * ldb;
     for (uint64_t b = first; b < rows * nb; b += warps) {
         float dd;
-        const int v = quant_q8_lane(x[b * 32 + lane], dd);
+        const int v = quant_q8_lane(__ldcg(x + b * 32 + lane), dd);  // L2: x may come from other GPUs
         q[b * 32 + lane] = (int8_t)v;
         const int sum = warp_sum_i(v);
         if (lane == 0) {
@@ -220,7 +220,7 @@ __global__ void rmsnorm_quantize_t_kernel(const float* __restrict__ x, const flo
     const float4* xr = reinterpret_cast<const float4*>(x + row * n);
     double ss = 0.0;
     for (int c = threadIdx.x; c < nc; c += blockDim.x) {
-        const float4 v = xr[c];
+        const float4 v = __ldcg(xr + c);  // L2: x may come from other GPUs
         ss += (double)v.x * v.x;
         ss += (double)v.y * v.y;
         ss += (double)v.z * v.z;
@@ -243,7 +243,7 @@ __global__ void rmsnorm_quantize_t_kernel(const float* __restrict__ x, const flo
         const bool live = c < nc;       // whole 8-lane groups live or not (nc % 8 == 0)
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
         if (live) {
-            const float4 v = xr[c], g = reinterpret_cast<const float4*>(w)[c];
+            const float4 v = __ldcg(xr + c), g = reinterpret_cast<const float4*>(w)[c];
             o = make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
         }
         float mx = fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w)));

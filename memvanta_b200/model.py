@@ -15,8 +15,12 @@ import numpy as np
 
 from ._lib import KV_F16, check, load
 
+HANDLE_BYTES = 64  # MV_TP_HANDLE_BYTES
+
 
 class LlamaModel:
+    tp_rank, tp_world, _group = 0, 1, None
+
     def __init__(self, gguf_path: str | os.PathLike, threads: int = 1, ctx_override: int = 0,
                  kv_page_tokens: int = 128, kv_type: int = KV_F16):
         self._m = None
@@ -24,10 +28,60 @@ class LlamaModel:
         check(load().mv_model_open(os.fspath(gguf_path).encode(), ctx_override, kv_page_tokens, kv_type,
                                    C.byref(h)))
         self._m = h
+        self._read_config()
+
+    def _read_config(self) -> None:
         cfg = (C.c_uint64 * 7)()
         check(load().mv_model_config(self._m, cfg))
         self.n_ctx, self.n_embd, self.n_ff, self.n_layer, self.n_head, self.n_head_kv, self.vocab = list(cfg)
         self._logits = np.empty(self.vocab, np.float32)
+
+    @classmethod
+    def tensor_parallel(cls, gguf_path: str | os.PathLike, group=None, device: int | None = None,
+                        ctx_override: int = 0, kv_page_tokens: int = 128, kv_type: int = KV_F16,
+                        prefill_batch: int = 512, timeout_ms: int | None = None) -> "LlamaModel":
+        """The same model split over the ranks of a torch.distributed group,
+        one process per GPU of one node (mv_model_open_tp).  Every rank calls
+        this, then makes the same calls in the same order; every call returns
+        what the single-GPU model returns, bit for bit.  The group only
+        carries the peer-memory handles (any backend); the data path is the
+        library's own kernels over NVLink."""
+        import torch.distributed as dist
+
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        if device is None:
+            device = int(os.environ.get("LOCAL_RANK", rank))
+        lib = load()
+        self = cls.__new__(cls)
+        self._m = None
+        h = C.c_void_p()
+        rc = lib.mv_init(device)
+        if rc == 0:
+            rc = lib.mv_model_open_tp(os.fspath(gguf_path).encode(), ctx_override, kv_page_tokens, kv_type,
+                                      rank, world, prefill_batch, C.byref(h))
+        handle = (C.c_char * HANDLE_BYTES)()
+        if rc == 0:
+            self._m = h
+            rc = lib.mv_model_tp_handle(h, handle)
+        msg = lib.mv_last_error().decode() if rc else ""
+        # every rank learns whether every other rank opened its share
+        got = [None] * world
+        dist.all_gather_object(got, (rc, msg, bytes(handle)), group=group)
+        bad = [(r, g[0], g[1]) for r, g in enumerate(got) if g[0]]
+        if bad:
+            self.close(barrier=False)
+            raise RuntimeError(f"tensor-parallel open failed on rank(s) {bad}")
+        self.tp_rank, self.tp_world, self._group = rank, world, group
+        if timeout_ms is not None:
+            check(lib.mv_model_tp_set_timeout(h, int(timeout_ms)))
+        buf = b"".join(g[2] for g in got)
+        check(lib.mv_model_tp_connect(h, buf))
+        self._read_config()
+        return self
+
+    def set_timeout(self, ms: int) -> None:
+        """Bound of every wait for the other ranks (tensor parallel only)."""
+        check(load().mv_model_tp_set_timeout(self._m, int(ms)))
 
     def config(self) -> dict:
         return {"n_ctx": self.n_ctx, "n_embd": self.n_embd, "n_ff": self.n_ff, "n_layer": self.n_layer,
@@ -84,13 +138,22 @@ class LlamaModel:
                 break
         return out
 
-    def close(self) -> None:
+    def close(self, barrier: bool = True) -> None:
+        """Frees the model.  Tensor parallel: every rank's block is mapped by
+        the others, so the ranks first wait for one another."""
         if self._m:
+            if barrier and self.tp_world > 1:
+                import torch.distributed as dist
+
+                if dist.is_initialized():
+                    dist.barrier(group=self._group)  # every rank idle
+                    load().mv_model_tp_disconnect(self._m)
+                    dist.barrier(group=self._group)  # nobody maps a block any more
             load().mv_model_close(self._m)
             self._m = None
 
     def __del__(self):
         try:
-            self.close()
+            self.close(barrier=False)
         except Exception:
             pass

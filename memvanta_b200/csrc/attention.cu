@@ -540,10 +540,7 @@ __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) 
         out = fmaf(al, v, out);
     }
     if (a.tp.world > 1) {
-        tp_for_each(a.tp, [&](int, char* base) {
-            reinterpret_cast<float*>(base + a.out_shared)[(size_t)(a.head_off + h) * HD + tid] = out;
-        });
-        if (a.signal_point >= 0) tp_signal_cta(a.tp, a.signal_point, a.slot);
+        ll_put_all(a.tp, a.out_shared, (uint64_t)(a.head_off + h) * HD + tid, out, tp_uepoch(a.tp, a.out_point));
     } else {
         a.out[(size_t)h * HD + tid] = out;
     }

@@ -149,22 +149,38 @@ __device__ __forceinline__ void quant_group(int g, bool active, float4 u, float4
 // a thread owns groups g = tid, tid + blockDim, ...; with RMSNorm the first
 // kKeep groups stay in registers between the sum-of-squares pass and the
 // quantisation pass.
-__device__ __forceinline__ void prologue(const float* __restrict__ x, const float* __restrict__ norm_w, float eps,
-                                         bool rms, int nb, const Act& a) {
+// Group loaders: 8 consecutive elements of x, from a float vector or (tensor
+// parallel decode) from an LL buffer once they carry the expected epoch.
+struct XFloat {
+    const float4* x4;
+    __device__ __forceinline__ void operator()(int g, float4& lo, float4& hi) const {
+        lo = __ldcg(x4 + 2 * g);
+        hi = __ldcg(x4 + 2 * g + 1);
+    }
+};
+struct XLL {
+    const TpCtx& tp;
+    const uint2* x;
+    unsigned ep;
+    int site;
+    __device__ __forceinline__ void operator()(int g, float4& lo, float4& hi) const {
+        ll_load8(tp, x + 8 * g, ep, site, lo, hi);
+    }
+};
+
+template <class Ld>
+__device__ __forceinline__ void prologue(const Ld& ld, const float* __restrict__ norm_w, float eps, bool rms, int nb,
+                                         const Act& a) {
     constexpr int kKeep = 2;
     const int G = nb * 4;  // groups of 8 elements
     const int bd = (int)blockDim.x, tid = (int)threadIdx.x;
     const int iters = (G + bd - 1) / bd;
-    const float4* x4 = reinterpret_cast<const float4*>(x);
     float4 keep[kKeep][2];
 #pragma unroll
     for (int it = 0; it < kKeep; ++it) {
         const int g = tid + it * bd;
         keep[it][0] = keep[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (g < G) {
-            keep[it][0] = __ldcg(x4 + 2 * g);  // L2: other GPUs write x while kernels run
-            keep[it][1] = __ldcg(x4 + 2 * g + 1);
-        }
+        if (g < G) ld(g, keep[it][0], keep[it][1]);
     }
     float inv = 1.0f;
     if (rms) {
@@ -175,7 +191,11 @@ __device__ __forceinline__ void prologue(const float* __restrict__ x, const floa
         };
 #pragma unroll
         for (int it = 0; it < kKeep; ++it) acc(keep[it][0], keep[it][1]);
-        for (int g = tid + kKeep * bd; g < G; g += bd) acc(__ldcg(x4 + 2 * g), __ldcg(x4 + 2 * g + 1));
+        for (int g = tid + kKeep * bd; g < G; g += bd) {
+            float4 u, v;
+            ld(g, u, v);
+            acc(u, v);
+        }
         const double tot = block_sum_d(ss);
         inv = 1.0f / sqrtf((float)(tot / (double)(nb * 32)) + eps);
     }
@@ -190,10 +210,7 @@ __device__ __forceinline__ void prologue(const float* __restrict__ x, const floa
         const int g = tid + it * bd;
         const bool active = g < G;  // uniform over the 4 lanes of a block
         float4 u = make_float4(0.f, 0.f, 0.f, 0.f), w = u;
-        if (active) {
-            u = __ldcg(x4 + 2 * g);
-            w = __ldcg(x4 + 2 * g + 1);
-        }
+        if (active) ld(g, u, w);
         quant_group(g, active, u, w, norm_w, rms, inv, a);
     }
     __syncthreads();
@@ -284,23 +301,25 @@ __device__ __forceinline__ void consume_item(const uint8_t* st, const Act& a, fl
 }
 
 // Output placement: y[idx] locally (y != nullptr), or, tensor parallel with
-// y == nullptr, y_row_off + idx in every rank's copy of the replicated buffer.
+// y == nullptr, element y_row_off + idx of the replicated LL buffer at byte
+// offset `shared` of every rank's block, tagged with epoch ep.  AddTo reads
+// the residual from this rank's own copy (its own rows: written by this rank).
 struct YOut {
     float* y;
     const TpCtx& tp;
     uint64_t shared;
     int row_off;
+    unsigned ep;      // epoch the outputs carry
+    unsigned res_ep;  // AddTo: epoch the residual (this rank's rows) must carry
     bool replicated;
     __device__ __forceinline__ float local(int idx) const {
-        return replicated ? __ldcg(reinterpret_cast<const float*>(tp_base(tp, tp.rank) + shared) + row_off + idx)
-                          : y[idx];
+        if (!replicated) return y[idx];
+        const uint2* own = reinterpret_cast<const uint2*>(tp_base(tp, tp.rank) + shared);
+        return ll_load1(tp, own + row_off + idx, res_ep, 200);
     }
     __device__ __forceinline__ void put(int idx, float v) const {
-        if (replicated) {
-            tp_for_each(tp, [&](int, char* base) { (reinterpret_cast<float*>(base + shared) + row_off)[idx] = v; });
-        } else {
-            y[idx] = v;
-        }
+        if (replicated) ll_put_all(tp, shared, (uint64_t)(row_off + idx), v, ep);
+        else y[idx] = v;
     }
 };
 
@@ -317,14 +336,20 @@ __device__ __forceinline__ void epilogue(int epi, int rg, int rows, int lane, fl
     }
 }
 
-template <int RPW>
+// LL: x is this rank's copy of a replicated LL buffer, read once its
+// elements carry point x_point's epoch (tensor-parallel decode).  The kernel
+// still waits for the previous one first (all of this rank's part of x is
+// then there, only the other ranks' parts may still be in flight): polling
+// from the moment the CTAs are resident measured slower, every CTA hammering
+// the same few kilobytes of L2 while the producers run.
+template <int RPW, bool LL>
 __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __restrict__ qs,
                                                               const unsigned short* __restrict__ dsc, int rows,
-                                                              int nb, int dstride, const float* __restrict__ x,
+                                                              int nb, int dstride, const void* __restrict__ x,
                                                               const float* __restrict__ norm_w, float eps, int pro,
                                                               int epi, float* __restrict__ y, const TpCtx tp,
-                                                              uint64_t y_shared, int y_row_off, int wait_point,
-                                                              int signal_point, int slot_id) {
+                                                              int x_point, uint64_t y_shared, int y_row_off,
+                                                              int y_point, int res_point) {
     using R = Ring<RPW>;
     const Act a = act_smem(nb);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -351,9 +376,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __res
         step(irg, ic);
     }
     pdl_wait();
-    if (tp.world > 1 && wait_point >= 0) tp_wait_cta(tp, wait_point, 100 + wait_point);
-    prologue(x, norm_w, eps, pro == (int)Q4Pro::RmsNorm, nb, a);
-    const YOut yo{y, tp, y_shared, y_row_off, tp.world > 1 && y == nullptr};
+    const bool rms = pro == (int)Q4Pro::RmsNorm;
+    if constexpr (LL) prologue(XLL{tp, static_cast<const uint2*>(x), tp_uepoch(tp, x_point), 100 + x_point},
+                               norm_w, eps, rms, nb, a);
+    else prologue(XFloat{static_cast<const float4*>(x)}, norm_w, eps, rms, nb, a);
+    const bool rep = tp.world > 1 && y == nullptr;
+    const YOut yo{y, tp, y_shared, y_row_off, rep ? tp_uepoch(tp, y_point) : 0u, rep ? tp_uepoch(tp, res_point) : 0u,
+                  rep};
 
     float sum = 0.0f;
     int rg = gw, c = 0, slot = 0, islot = R::S - 1;
@@ -373,7 +402,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __res
         if (++slot == R::S) slot = 0;
     }
     cp_async_wait<0>();
-    if (tp.world > 1 && signal_point >= 0) tp_signal_cta(tp, signal_point, slot_id);
 }
 
 // Diagnostic twin: the per-block int32 dots of the same device code.
@@ -381,7 +409,7 @@ __global__ void __launch_bounds__(kThreads) q4_block_dots_kernel(const uint4* __
                                                                  const float* __restrict__ x,
                                                                  int32_t* __restrict__ isum) {
     const Act a = act_smem(nb);
-    prologue(x, nullptr, 0.0f, false, nb, a);
+    prologue(XFloat{reinterpret_cast<const float4*>(x)}, nullptr, 0.0f, false, nb, a);
     const uint64_t total = (uint64_t)rows * nb;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
         const int b = (int)(i % nb);
@@ -389,19 +417,20 @@ __global__ void __launch_bounds__(kThreads) q4_block_dots_kernel(const uint4* __
     }
 }
 
-template <int RPW>
+template <int RPW, bool LL>
 cudaError_t launch(const GemvQ4Args& g, cudaStream_t s) {
     const mv_weight_s& w = *g.w;
     const size_t smem = act_smem_bytes(w.nb, RPW) + (size_t)kWarps * Ring<RPW>::BYTES;
     if (smem > 110 * 1024) return cudaErrorInvalidValue;  // two CTAs per SM
-    ensure_smem_attr(gemv_q4_kernel<RPW>, 200 * 1024);
+    ensure_smem_attr(gemv_q4_kernel<RPW, LL>, 200 * 1024);
     const uint64_t groups = (w.rows + RPW - 1) / RPW;
     const uint64_t ctas = (groups + kWarps - 1) / kWarps;
     const uint64_t cap = (uint64_t)num_sms() * 2;
-    return launch_pdl(gemv_q4_kernel<RPW>, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(kThreads), smem, s,
+    const void* x = LL ? g.x_ll : static_cast<const void*>(g.x);
+    return launch_pdl(gemv_q4_kernel<RPW, LL>, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(kThreads), smem, s,
                       reinterpret_cast<const uint4*>(w.qs), (const unsigned short*)w.d, (int)w.rows, (int)w.nb,
-                      (int)w.dstride, g.x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y, g.tp ? *g.tp : TpCtx{},
-                      g.y_shared, g.y_row_off, g.wait_point, g.signal_point, g.slot);
+                      (int)w.dstride, x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y, g.tp ? *g.tp : TpCtx{},
+                      g.x_point, g.y_shared, g.y_row_off, g.y_point, g.res_point);
 }
 
 }  // namespace
@@ -409,11 +438,12 @@ cudaError_t launch(const GemvQ4Args& g, cudaStream_t s) {
 cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s) {
     // x and norm_w are read as float4: the width must keep 8-element groups
     if (a.w->cols % 32) return cudaErrorInvalidValue;
-    if (!a.y && !(a.tp && a.tp->world > 1)) return cudaErrorInvalidValue;
+    const bool tp = a.tp && a.tp->world > 1;
+    if ((!a.y && !tp) || (a.x_ll && !tp) || (!a.x_ll && !a.x)) return cudaErrorInvalidValue;
     // Four rows per warp where the matrix has rows to spare (the chain cost
     // is shared by more rows), two otherwise so every SM has warps in flight.
-    if (a.w->rows >= 8192) return launch<4>(a, s);
-    return launch<2>(a, s);
+    if (a.x_ll) return a.w->rows >= 8192 ? launch<4, true>(a, s) : launch<2, true>(a, s);
+    return a.w->rows >= 8192 ? launch<4, false>(a, s) : launch<2, false>(a, s);
 }
 
 cudaError_t q4_block_dots(const mv_weight_s& w, const float* x, int32_t* isum, cudaStream_t s) {

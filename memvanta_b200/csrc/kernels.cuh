@@ -46,16 +46,20 @@ struct GemvQ4Args {
     float* y;
     Q4Pro pro;
     Q4Epi epi;
-    // tensor parallel (tp.cuh), y == nullptr: the output is the replicated
-    // buffer at byte offset y_shared of every rank's shared block, this
-    // rank's rows land at y_row_off + row (SiluGate: y_row_off + row/2) in
-    // every copy.  With y set, tp only supplies the wait / signal points.
+    // Tensor-parallel decode (tp.cuh, LL buffers).  x_ll set: the input is
+    // this rank's copy of a replicated LL buffer, read once its elements carry
+    // point x_point's epoch (x is ignored).  y == nullptr: the output is the
+    // replicated LL buffer at byte offset y_shared of every rank's block; this
+    // rank's rows land at y_row_off + row (SiluGate: y_row_off + row/2),
+    // tagged with point y_point's epoch; AddTo reads the residual (this
+    // rank's rows of the same buffer) once it carries res_point's epoch.
     const TpCtx* tp = nullptr;
+    const void* x_ll = nullptr;
+    int x_point = 0;
     uint64_t y_shared = 0;
     int y_row_off = 0;
-    int wait_point = -1;    // wait for this point's epoch before reading x
-    int signal_point = -1;  // publish this point's epoch when y is complete
-    int slot = 0;           // arrival counter
+    int y_point = 0;
+    int res_point = 0;
 };
 cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s);
 cudaError_t q4_block_dots(const mv_weight_s& w, const float* x, int32_t* isum, cudaStream_t s);
@@ -126,13 +130,13 @@ struct AttnFusedArgs {
     void* v_pages;
     int32_t* ctx_out;                // optional: receives pos + 1
     float* out;                      // [n_head][hd]
-    // tensor parallel: out is the replicated buffer at byte offset out_shared of
-    // every rank's shared block; this rank's heads start at head head_off
+    // tensor parallel: out is the replicated LL buffer at byte offset
+    // out_shared of every rank's block; this rank's heads start at head
+    // head_off; elements are tagged with point out_point's epoch
     TpCtx tp;
     uint64_t out_shared = 0;
     int head_off = 0;
-    int signal_point = -1;
-    int slot = 0;
+    int out_point = 0;
 };
 // ---- tp.cu (tensor parallel, protocol in tp.cuh)
 cudaError_t tp_wait(const TpCtx& tp, int point, cudaStream_t s);
@@ -140,6 +144,13 @@ cudaError_t tp_scatter(const TpCtx& tp, const float* src, uint64_t rows, uint64_
                        uint64_t dst_shared, uint64_t dst_ld, uint64_t col_off, bool add, int point, int slot,
                        cudaStream_t s);
 cudaError_t tp_step(int* step, cudaStream_t s);
+// LL buffers (decode): this rank's float vector into its own copy; an own
+// copy into a float vector once every element carries the point's epoch;
+// a float slice into every rank's copy at element col_off.
+cudaError_t tp_pack(const TpCtx& tp, const float* src, uint64_t n, uint64_t dst_shared, int point, cudaStream_t s);
+cudaError_t tp_unpack(const TpCtx& tp, uint64_t src_shared, uint64_t n, float* dst, int point, cudaStream_t s);
+cudaError_t tp_scatter_ll(const TpCtx& tp, const float* src, uint64_t n, uint64_t dst_shared, uint64_t col_off,
+                          int point, cudaStream_t s);
 
 uint64_t attn_fused_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type);
 cudaError_t attn_decode_fused(const AttnFusedArgs& a, cudaStream_t s);

@@ -552,25 +552,30 @@ mvb::AttnArgs attn_args(mv_model_s* m, const mvb::Layer& L, const float* q, uint
 }
 
 // Sync points of one step under tensor parallelism (tp.cuh): per layer the
-// attention heads, the o rows, the ff rows and the down rows, then the logits.
+// attention heads, the o rows, the ff rows and the down rows, then the
+// logits and (decode) the embedding.
 int pt_att(uint64_t l) { return (int)(4 * l); }
 int pt_o(uint64_t l) { return (int)(4 * l + 1); }
 int pt_gu(uint64_t l) { return (int)(4 * l + 2); }
 int pt_down(uint64_t l) { return (int)(4 * l + 3); }
 int pt_head(const mv_model_s* m) { return (int)(4 * m->n_layer); }
+int pt_embed(const mv_model_s* m) { return (int)(4 * m->n_layer + 1); }
+int points_per_step(const mv_model_s* m) { return (int)(4 * m->n_layer + 2); }
 
-// One Q4_0 GEMV of a tensor-parallel decode step: reads the whole replicated
-// input once `wait` is published, writes this rank's rows at `row_off` of the
-// replicated output (every rank's copy) and publishes `signal`.
-void gemv_tp(mv_model_s* m, mv_weight_s* w, const float* x, const float* norm_w, mvb::Q4Epi epi, uint64_t y_off,
-             uint64_t row_off, int wait, int signal) {
-    mvb::GemvQ4Args a{w, x, norm_w, m->eps, nullptr, norm_w ? mvb::Q4Pro::RmsNorm : mvb::Q4Pro::Plain, epi};
+// One Q4_0 GEMV of a tensor-parallel decode step: reads this rank's copy of
+// the replicated LL input `x_off` once it carries point x_point; y == nullptr
+// stores this rank's rows at `row_off` of every rank's LL output `y_off`
+// (point y_point), otherwise y is a local float output.
+void gemv_tp(mv_model_s* m, mv_weight_s* w, uint64_t x_off, int x_point, const float* norm_w, mvb::Q4Epi epi,
+             float* y, uint64_t y_off, uint64_t row_off, int y_point, int res_point = 0) {
+    mvb::GemvQ4Args a{w, nullptr, norm_w, m->eps, y, norm_w ? mvb::Q4Pro::RmsNorm : mvb::Q4Pro::Plain, epi};
     a.tp = &m->tp;
+    a.x_ll = m->tp_block + x_off;
+    a.x_point = x_point;
     a.y_shared = y_off;
     a.y_row_off = (int)row_off;
-    a.wait_point = wait;
-    a.signal_point = signal;
-    a.slot = signal & 3;
+    a.y_point = y_point;
+    a.res_point = res_point;
     ck(mvb::gemv_q4(a, m->stream), "gemv_q4 (tensor parallel)");
 }
 
@@ -578,19 +583,16 @@ void gemv_tp(mv_model_s* m, mv_weight_s* w, const float* x, const float* norm_w,
 void launch_decode(mv_model_s* m, bool with_logits) {
     cudaStream_t s = m->stream;
     const bool tp = m->tp_world > 1;
+    const uint64_t r = m->tp_rank;
     ck(mvb::read_rows(*m->tok_embd, m->token_dev, 1, m->x, s), "embed");
+    if (tp) ck(mvb::tp_pack(m->tp, m->x, m->n_embd, m->off_x, pt_embed(m), s), "pack");
     // F16/F32 KV: RoPE, the KV append and the attention are one kernel
     const bool fused = m->kv_type == MV_KV_F32 || m->kv_type == MV_KV_F16;
     for (uint64_t l = 0; l < m->n_layer; ++l) {
         auto& L = m->layers[l];
-        if (tp) {
-            mvb::GemvQ4Args a{L.qkv, m->x, L.attn_norm, m->eps, m->qkv, mvb::Q4Pro::RmsNorm, mvb::Q4Epi::Store};
-            a.tp = &m->tp;
-            a.wait_point = l ? pt_down(l - 1) : -1;
-            ck(mvb::gemv_q4(a, s), "gemv_q4 (tensor parallel)");
-        } else {
-            project_decode(m, L.qkv, m->x, L.attn_norm, m->qkv, mvb::Q4Epi::Store);
-        }
+        if (tp) gemv_tp(m, L.qkv, m->off_x, l ? pt_down(l - 1) : pt_embed(m), L.attn_norm, mvb::Q4Epi::Store, m->qkv,
+                        0, 0, 0);
+        else project_decode(m, L.qkv, m->x, L.attn_norm, m->qkv, mvb::Q4Epi::Store);
         if (fused) {
             mvb::AttnFusedArgs fa{m->kv_type, m->qkv, m->nh, m->nkv, m->hd,
                                   (const float*)m->rope_cos, (const float*)m->rope_sin, m->pos_dev,
@@ -599,40 +601,37 @@ void launch_decode(mv_model_s* m, bool with_logits) {
             if (tp) {
                 fa.tp = m->tp;
                 fa.out_shared = m->off_att;
-                fa.head_off = (int)(m->tp_rank * m->nh);
-                fa.signal_point = pt_att(l);
-                fa.slot = pt_att(l) & 3;
+                fa.head_off = (int)(r * m->nh);
+                fa.out_point = pt_att(l);
             }
             ck(mvb::attn_decode_fused(fa, s), "attention (fused)");
         } else {
             rope_append(m, L, m->qkv, 1, m->pos_dev, m->ctx_dev);
             float* out = tp ? m->ATT_l : m->att;
             ck(mvb::paged_attn_decode(attn_args(m, L, m->qkv, m->qkvw, 1, m->ctx_dev, m->n_ctx, out), s), "attention");
-            if (tp)
-                ck(mvb::tp_scatter(m->tp, out, 1, m->Dl, m->Dl, m->off_att, m->n_embd, m->tp_rank * m->Dl, false,
-                                   pt_att(l), pt_att(l) & 3, s),
-                   "scatter");
+            if (tp) ck(mvb::tp_scatter_ll(m->tp, out, m->Dl, m->off_att, r * m->Dl, pt_att(l), s), "scatter");
         }
         if (tp) {
-            gemv_tp(m, L.o, m->att, nullptr, mvb::Q4Epi::AddTo, m->off_x, m->tp_rank * m->Dl, pt_att(l), pt_o(l));
-            gemv_tp(m, L.gu, m->x, L.ffn_norm, mvb::Q4Epi::SiluGate, m->off_ff, m->tp_rank * m->Fl, pt_o(l), pt_gu(l));
-            gemv_tp(m, L.down, m->ff, nullptr, mvb::Q4Epi::AddTo, m->off_x, m->tp_rank * m->Dl, pt_gu(l), pt_down(l));
+            gemv_tp(m, L.o, m->off_att, pt_att(l), nullptr, mvb::Q4Epi::AddTo, nullptr, m->off_x, r * m->Dl, pt_o(l),
+                    l ? pt_down(l - 1) : pt_embed(m));
+            gemv_tp(m, L.gu, m->off_x, pt_o(l), L.ffn_norm, mvb::Q4Epi::SiluGate, nullptr, m->off_ff, r * m->Fl,
+                    pt_gu(l));
+            gemv_tp(m, L.down, m->off_ff, pt_gu(l), nullptr, mvb::Q4Epi::AddTo, nullptr, m->off_x, r * m->Dl,
+                    pt_down(l), pt_o(l));
         } else {
             project_decode(m, L.o, m->att, nullptr, m->x, mvb::Q4Epi::AddTo);
             project_decode(m, L.gu, m->x, L.ffn_norm, m->ff, mvb::Q4Epi::SiluGate);
             project_decode(m, L.down, m->ff, nullptr, m->x, mvb::Q4Epi::AddTo);
         }
     }
-    // every rank's down rows are in x before the logits (and before the next
-    // step's embedding overwrites x)
-    if (tp) ck(mvb::tp_wait(m->tp, pt_down(m->n_layer - 1), s), "tp wait");
+    // every rank's down rows, as floats, before the head (and before the next
+    // step's embedding reuses the buffer)
+    if (tp) ck(mvb::tp_unpack(m->tp, m->off_x, m->n_embd, m->x, pt_down(m->n_layer - 1), s), "unpack");
     if (with_logits) {
         if (tp) {
             project_decode(m, m->output, m->x, m->output_norm, m->logits_l, mvb::Q4Epi::Store);
-            ck(mvb::tp_scatter(m->tp, m->logits_l, 1, m->Vl, m->Vl, m->off_logits, m->vocab, m->tp_rank * m->Vl, false,
-                               pt_head(m), pt_head(m) & 3, s),
-               "scatter logits");
-            ck(mvb::tp_wait(m->tp, pt_head(m), s), "tp wait");
+            ck(mvb::tp_scatter_ll(m->tp, m->logits_l, m->Vl, m->off_logits, r * m->Vl, pt_head(m), s), "scatter");
+            ck(mvb::tp_unpack(m->tp, m->off_logits, m->vocab, m->logits, pt_head(m), s), "unpack");
         } else {
             project_decode(m, m->output, m->x, m->output_norm, m->logits, mvb::Q4Epi::Store);
         }
@@ -825,20 +824,20 @@ void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, in
         auto up = [](uint64_t b) { return (b + 255) / 256 * 256; };
         m->tp_bmax = tp_bmax ? tp_bmax : 64;
         uint64_t off = mvb::kTpFlagsBytes;
-        m->off_x = off, off += up(D * 4);
-        m->off_att = off, off += up(D * 4);
-        m->off_ff = off, off += up(F * 4);
-        m->off_logits = off, off += up(m->vocab * 4);
+        m->off_x = off, off += up(D * 8);  // decode: LL buffers, 8 bytes per element
+        m->off_att = off, off += up(D * 8);
+        m->off_ff = off, off += up(F * 8);
+        m->off_logits = off, off += up(m->vocab * 8);
         m->off_X = off, off += up(m->tp_bmax * D * 4);
         m->off_ATT = off, off += up(m->tp_bmax * D * 4);
         m->off_FF = off, off += up(m->tp_bmax * F * 4);
         m->tp_bytes = off;
         ck(cudaMalloc(reinterpret_cast<void**>(&m->tp_block), m->tp_bytes), "cudaMalloc(shared block)");
         ck(cudaMemset(m->tp_block, 0, m->tp_bytes), "clear shared block");
-        m->x = reinterpret_cast<float*>(m->tp_block + m->off_x);
-        m->att = reinterpret_cast<float*>(m->tp_block + m->off_att);
-        m->ff = reinterpret_cast<float*>(m->tp_block + m->off_ff);
-        m->logits = reinterpret_cast<float*>(m->tp_block + m->off_logits);
+        m->x = dalloc<float>(m, D);  // the embedding, and the final x before the head
+        m->att = dalloc<float>(m, D);
+        m->ff = dalloc<float>(m, F);
+        m->logits = dalloc<float>(m, m->vocab);
         m->logits_l = dalloc<float>(m, std::max(m->Vl, std::max(2 * m->Fl, D)));
         m->tp_step = dalloc<int>(m, 1);
         m->tp_counters = dalloc<unsigned>(m, 8);
@@ -990,10 +989,9 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
         const float* last = m->X + (B - 1) * D;
         if (tp) {
             project_decode(m, m->output, last, m->output_norm, m->logits_l, mvb::Q4Epi::Store);
-            ck(mvb::tp_scatter(m->tp, m->logits_l, 1, m->Vl, m->Vl, m->off_logits, m->vocab, m->tp_rank * m->Vl,
-                               false, pt_head(m), pt_head(m) & 3, s),
+            ck(mvb::tp_scatter_ll(m->tp, m->logits_l, m->Vl, m->off_logits, m->tp_rank * m->Vl, pt_head(m), s),
                "scatter logits");
-            ck(mvb::tp_wait(m->tp, pt_head(m), s), "tp wait");
+            ck(mvb::tp_unpack(m->tp, m->off_logits, m->vocab, m->logits, pt_head(m), s), "unpack logits");
         } else {
             project_decode(m, m->output, last, m->output_norm, m->logits, mvb::Q4Epi::Store);
         }
@@ -1072,7 +1070,7 @@ MV_API int mv_model_tp_connect(mv_model_t m, const void* handles) {
             t.base[d] = static_cast<char*>(p);
         }
         t.step = m->tp_step;
-        t.pps = (int)(4 * m->n_layer + 1);
+        t.pps = points_per_step(m);
         t.counters = m->tp_counters;
         t.status = m->tp_status;
         t.limit_ns = m->tp_limit;

@@ -106,12 +106,11 @@ __device__ __forceinline__ double block_sum_d(double v) {
 
 // One 8-element group of the quantisation: 4 neighbouring lanes hold one
 // 32-element block.  All 32 lanes of the warp must call it (shuffles).
-__device__ __forceinline__ void quant_group(int g, bool active, float4 u, float4 w, const float* __restrict__ norm_w,
-                                            bool rms, float inv, const Act& a) {
+// n0/n1: the group's RMSNorm weights (used when rms).
+__device__ __forceinline__ void quant_group(int g, bool active, float4 u, float4 w, float4 n0, float4 n1, bool rms,
+                                            float inv, const Act& a) {
     float v[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
     if (active && rms) {
-        const float4 n0 = reinterpret_cast<const float4*>(norm_w)[2 * g];
-        const float4 n1 = reinterpret_cast<const float4*>(norm_w)[2 * g + 1];
         const float nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * nw[i];  // (x*inv)*w as the reference
@@ -145,10 +144,6 @@ __device__ __forceinline__ void quant_group(int g, bool active, float4 u, float4
     }
 }
 
-// Quantised activations of (optionally RMS-normalised) x into shared memory:
-// a thread owns groups g = tid, tid + blockDim, ...; with RMSNorm the first
-// kKeep groups stay in registers between the sum-of-squares pass and the
-// quantisation pass.
 // Group loaders: 8 consecutive elements of x, from a float vector or (tensor
 // parallel decode) from an LL buffer once they carry the expected epoch.
 struct XFloat {
@@ -168,20 +163,57 @@ struct XLL {
     }
 };
 
+// Quantised activations of (optionally RMS-normalised) x into shared memory.
+// A thread owns groups g = tid, tid + blockDim, ...  The prologue sits on the
+// critical path between two kernels, so every load is issued at once: the
+// first kKeep groups of x (K up to 12288 at 256 threads) go to registers
+// together, and the RMSNorm weights of the first kNormKeep groups are
+// fetched before the kernel waits on its predecessor (norm_preload).
+constexpr int kKeep = 6;
+constexpr int kNormKeep = 2;
+
+struct NormPre {
+    float4 w[kNormKeep][2];
+};
+
+__device__ __forceinline__ void norm_preload(NormPre& np, const float* __restrict__ norm_w, bool rms, int nb) {
+    const int G = nb * 4, tid = (int)threadIdx.x, bd = (int)blockDim.x;
+#pragma unroll
+    for (int it = 0; it < kNormKeep; ++it) {
+        const int g = tid + it * bd;
+        np.w[it][0] = np.w[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (rms && g < G) {
+            np.w[it][0] = reinterpret_cast<const float4*>(norm_w)[2 * g];
+            np.w[it][1] = reinterpret_cast<const float4*>(norm_w)[2 * g + 1];
+        }
+    }
+}
+
 template <class Ld>
-__device__ __forceinline__ void prologue(const Ld& ld, const float* __restrict__ norm_w, float eps, bool rms, int nb,
-                                         const Act& a) {
-    constexpr int kKeep = 2;
+__device__ __forceinline__ void prologue(const Ld& ld, const NormPre& np, const float* __restrict__ norm_w, float eps,
+                                         bool rms, int nb, const Act& a) {
     const int G = nb * 4;  // groups of 8 elements
     const int bd = (int)blockDim.x, tid = (int)threadIdx.x;
     const int iters = (G + bd - 1) / bd;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 keep[kKeep][2];
 #pragma unroll
     for (int it = 0; it < kKeep; ++it) {
         const int g = tid + it * bd;
-        keep[it][0] = keep[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        keep[it][0] = keep[it][1] = z;
         if (g < G) ld(g, keep[it][0], keep[it][1]);
     }
+    auto norm_of = [&](int it, int g, float4& n0, float4& n1) {
+        n0 = n1 = z;
+        if (!rms || g >= G) return;
+        if (it < kNormKeep) {
+            n0 = np.w[it < kNormKeep ? it : 0][0];
+            n1 = np.w[it < kNormKeep ? it : 0][1];
+        } else {
+            n0 = reinterpret_cast<const float4*>(norm_w)[2 * g];
+            n1 = reinterpret_cast<const float4*>(norm_w)[2 * g + 1];
+        }
+    };
     float inv = 1.0f;
     if (rms) {
         double ss = 0.0;
@@ -203,15 +235,18 @@ __device__ __forceinline__ void prologue(const Ld& ld, const float* __restrict__
     for (int it = 0; it < kKeep; ++it) {
         if (it < iters) {  // uniform across the CTA
             const int g = tid + it * bd;
-            quant_group(g, g < G, keep[it][0], keep[it][1], norm_w, rms, inv, a);
+            float4 n0, n1;
+            norm_of(it, g, n0, n1);
+            quant_group(g, g < G, keep[it][0], keep[it][1], n0, n1, rms, inv, a);
         }
     }
     for (int it = kKeep; it < iters; ++it) {
         const int g = tid + it * bd;
         const bool active = g < G;  // uniform over the 4 lanes of a block
-        float4 u = make_float4(0.f, 0.f, 0.f, 0.f), w = u;
+        float4 u = z, w = z, n0, n1;
         if (active) ld(g, u, w);
-        quant_group(g, active, u, w, norm_w, rms, inv, a);
+        norm_of(it, g, n0, n1);
+        quant_group(g, active, u, w, n0, n1, rms, inv, a);
     }
     __syncthreads();
 }
@@ -375,11 +410,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __res
         cp_async_commit();
         step(irg, ic);
     }
-    pdl_wait();
     const bool rms = pro == (int)Q4Pro::RmsNorm;
-    if constexpr (LL) prologue(XLL{tp, static_cast<const uint2*>(x), tp_uepoch(tp, x_point), 100 + x_point},
+    NormPre np;
+    norm_preload(np, norm_w, rms, nb);  // weights: before the dependency wait
+    pdl_wait();
+    if constexpr (LL) prologue(XLL{tp, static_cast<const uint2*>(x), tp_uepoch(tp, x_point), 100 + x_point}, np,
                                norm_w, eps, rms, nb, a);
-    else prologue(XFloat{static_cast<const float4*>(x)}, norm_w, eps, rms, nb, a);
+    else prologue(XFloat{static_cast<const float4*>(x)}, np, norm_w, eps, rms, nb, a);
     const bool rep = tp.world > 1 && y == nullptr;
     const YOut yo{y, tp, y_shared, y_row_off, rep ? tp_uepoch(tp, y_point) : 0u, rep ? tp_uepoch(tp, res_point) : 0u,
                   rep};
@@ -409,7 +446,9 @@ __global__ void __launch_bounds__(kThreads) q4_block_dots_kernel(const uint4* __
                                                                  const float* __restrict__ x,
                                                                  int32_t* __restrict__ isum) {
     const Act a = act_smem(nb);
-    prologue(XFloat{reinterpret_cast<const float4*>(x)}, nullptr, 0.0f, false, nb, a);
+    NormPre np;
+    norm_preload(np, nullptr, false, nb);
+    prologue(XFloat{reinterpret_cast<const float4*>(x)}, np, nullptr, 0.0f, false, nb, a);
     const uint64_t total = (uint64_t)rows * nb;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
         const int b = (int)(i % nb);

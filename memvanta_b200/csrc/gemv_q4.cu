@@ -149,8 +149,8 @@ __device__ __forceinline__ void quant_group(int g, bool active, float4 u, float4
 struct XFloat {
     const float4* x4;
     __device__ __forceinline__ void operator()(int g, float4& lo, float4& hi) const {
-        lo = __ldcg(x4 + 2 * g);
-        hi = __ldcg(x4 + 2 * g + 1);
+        lo = x4[2 * g];
+        hi = x4[2 * g + 1];
     }
 };
 struct XLL {
@@ -166,10 +166,10 @@ struct XLL {
 // Quantised activations of (optionally RMS-normalised) x into shared memory.
 // A thread owns groups g = tid, tid + blockDim, ...  The prologue sits on the
 // critical path between two kernels, so every load is issued at once: the
-// first kKeep groups of x (K up to 12288 at 256 threads) go to registers
-// together, and the RMSNorm weights of the first kNormKeep groups are
-// fetched before the kernel waits on its predecessor (norm_preload).
-constexpr int kKeep = 6;
+// first KEEP groups of x go to registers together (KEEP = 2 covers K = 4096,
+// 6 covers K up to 12288 at 256 threads), and the RMSNorm weights of the
+// first kNormKeep groups are fetched before the kernel waits on its
+// predecessor (norm_preload).
 constexpr int kNormKeep = 2;
 
 struct NormPre {
@@ -189,9 +189,10 @@ __device__ __forceinline__ void norm_preload(NormPre& np, const float* __restric
     }
 }
 
-template <class Ld>
+template <int KEEP, class Ld>
 __device__ __forceinline__ void prologue(const Ld& ld, const NormPre& np, const float* __restrict__ norm_w, float eps,
                                          bool rms, int nb, const Act& a) {
+    constexpr int kKeep = KEEP;
     const int G = nb * 4;  // groups of 8 elements
     const int bd = (int)blockDim.x, tid = (int)threadIdx.x;
     const int iters = (G + bd - 1) / bd;
@@ -336,9 +337,11 @@ __device__ __forceinline__ void consume_item(const uint8_t* st, const Act& a, fl
 }
 
 // Output placement: y[idx] locally (y != nullptr), or, tensor parallel with
-// y == nullptr, element y_row_off + idx of the replicated LL buffer at byte
-// offset `shared` of every rank's block, tagged with epoch ep.  AddTo reads
-// the residual from this rank's own copy (its own rows: written by this rank).
+// y == nullptr (LL kernels only), element y_row_off + idx of the replicated
+// LL buffer at byte offset `shared` of every rank's block, tagged with epoch
+// ep.  AddTo reads the residual from this rank's own copy (its own rows:
+// written by this rank).
+template <bool LL>
 struct YOut {
     float* y;
     const TpCtx& tp;
@@ -348,18 +351,27 @@ struct YOut {
     unsigned res_ep;  // AddTo: epoch the residual (this rank's rows) must carry
     bool replicated;
     __device__ __forceinline__ float local(int idx) const {
-        if (!replicated) return y[idx];
-        const uint2* own = reinterpret_cast<const uint2*>(tp_base(tp, tp.rank) + shared);
-        return ll_load1(tp, own + row_off + idx, res_ep, 200);
+        if constexpr (LL) {
+            if (replicated) {
+                const uint2* own = reinterpret_cast<const uint2*>(tp_base(tp, tp.rank) + shared);
+                return ll_load1(tp, own + row_off + idx, res_ep, 200);
+            }
+        }
+        return y[idx];
     }
     __device__ __forceinline__ void put(int idx, float v) const {
-        if (replicated) ll_put_all(tp, shared, (uint64_t)(row_off + idx), v, ep);
-        else y[idx] = v;
+        if constexpr (LL) {
+            if (replicated) {
+                ll_put_all(tp, shared, (uint64_t)(row_off + idx), v, ep);
+                return;
+            }
+        }
+        y[idx] = v;
     }
 };
 
-template <int RPW>
-__device__ __forceinline__ void epilogue(int epi, int rg, int rows, int lane, float sum, const YOut& yo) {
+template <int RPW, bool LL>
+__device__ __forceinline__ void epilogue(int epi, int rg, int rows, int lane, float sum, const YOut<LL>& yo) {
     if (epi == (int)Q4Epi::SiluGate) {
         // rows come in (gate_i, up_i) pairs: ff_i = g/(1+exp(-g)) * u
         const float u = __shfl_down_sync(0xffffffffu, sum, 1);
@@ -377,7 +389,7 @@ __device__ __forceinline__ void epilogue(int epi, int rg, int rows, int lane, fl
 // then there, only the other ranks' parts may still be in flight): polling
 // from the moment the CTAs are resident measured slower, every CTA hammering
 // the same few kilobytes of L2 while the producers run.
-template <int RPW, bool LL>
+template <int RPW, bool LL, int KEEP>
 __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __restrict__ qs,
                                                               const unsigned short* __restrict__ dsc, int rows,
                                                               int nb, int dstride, const void* __restrict__ x,
@@ -414,11 +426,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __res
     NormPre np;
     norm_preload(np, norm_w, rms, nb);  // weights: before the dependency wait
     pdl_wait();
-    if constexpr (LL) prologue(XLL{tp, static_cast<const uint2*>(x), tp_uepoch(tp, x_point), 100 + x_point}, np,
-                               norm_w, eps, rms, nb, a);
-    else prologue(XFloat{static_cast<const float4*>(x)}, np, norm_w, eps, rms, nb, a);
+    if constexpr (LL) prologue<KEEP>(XLL{tp, static_cast<const uint2*>(x), tp_uepoch(tp, x_point), 100 + x_point},
+                                     np, norm_w, eps, rms, nb, a);
+    else prologue<KEEP>(XFloat{static_cast<const float4*>(x)}, np, norm_w, eps, rms, nb, a);
     const bool rep = tp.world > 1 && y == nullptr;
-    const YOut yo{y, tp, y_shared, y_row_off, rep ? tp_uepoch(tp, y_point) : 0u, rep ? tp_uepoch(tp, res_point) : 0u,
+    const YOut<LL> yo{y, tp, y_shared, y_row_off, rep ? tp_uepoch(tp, y_point) : 0u, rep ? tp_uepoch(tp, res_point) : 0u,
                   rep};
 
     float sum = 0.0f;
@@ -432,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __res
         step(irg, ic);
         if (++islot == R::S) islot = 0;
         if (c == nchunk - 1) {
-            epilogue<RPW>(epi, rg, rows, lane, sum, yo);
+            epilogue<RPW, LL>(epi, rg, rows, lane, sum, yo);
             sum = 0.0f;
         }
         step(rg, c);
@@ -448,7 +460,7 @@ __global__ void __launch_bounds__(kThreads) q4_block_dots_kernel(const uint4* __
     const Act a = act_smem(nb);
     NormPre np;
     norm_preload(np, nullptr, false, nb);
-    prologue(XFloat{reinterpret_cast<const float4*>(x)}, np, nullptr, 0.0f, false, nb, a);
+    prologue<2>(XFloat{reinterpret_cast<const float4*>(x)}, np, nullptr, 0.0f, false, nb, a);
     const uint64_t total = (uint64_t)rows * nb;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
         const int b = (int)(i % nb);
@@ -456,17 +468,17 @@ __global__ void __launch_bounds__(kThreads) q4_block_dots_kernel(const uint4* __
     }
 }
 
-template <int RPW, bool LL>
+template <int RPW, bool LL, int KEEP>
 cudaError_t launch(const GemvQ4Args& g, cudaStream_t s) {
     const mv_weight_s& w = *g.w;
     const size_t smem = act_smem_bytes(w.nb, RPW) + (size_t)kWarps * Ring<RPW>::BYTES;
     if (smem > 110 * 1024) return cudaErrorInvalidValue;  // two CTAs per SM
-    ensure_smem_attr(gemv_q4_kernel<RPW, LL>, 200 * 1024);
+    ensure_smem_attr(gemv_q4_kernel<RPW, LL, KEEP>, 200 * 1024);
     const uint64_t groups = (w.rows + RPW - 1) / RPW;
     const uint64_t ctas = (groups + kWarps - 1) / kWarps;
     const uint64_t cap = (uint64_t)num_sms() * 2;
     const void* x = LL ? g.x_ll : static_cast<const void*>(g.x);
-    return launch_pdl(gemv_q4_kernel<RPW, LL>, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(kThreads), smem, s,
+    return launch_pdl(gemv_q4_kernel<RPW, LL, KEEP>, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(kThreads), smem, s,
                       reinterpret_cast<const uint4*>(w.qs), (const unsigned short*)w.d, (int)w.rows, (int)w.nb,
                       (int)w.dstride, x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y, g.tp ? *g.tp : TpCtx{},
                       g.x_point, g.y_shared, g.y_row_off, g.y_point, g.res_point);
@@ -478,11 +490,17 @@ cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s) {
     // x and norm_w are read as float4: the width must keep 8-element groups
     if (a.w->cols % 32) return cudaErrorInvalidValue;
     const bool tp = a.tp && a.tp->world > 1;
-    if ((!a.y && !tp) || (a.x_ll && !tp) || (!a.x_ll && !a.x)) return cudaErrorInvalidValue;
+    if ((!a.y && !a.x_ll) || (a.x_ll && !tp) || (!a.x_ll && !a.x)) return cudaErrorInvalidValue;
     // Four rows per warp where the matrix has rows to spare (the chain cost
-    // is shared by more rows), two otherwise so every SM has warps in flight.
-    if (a.x_ll) return a.w->rows >= 8192 ? launch<4, true>(a, s) : launch<2, true>(a, s);
-    return a.w->rows >= 8192 ? launch<4, false>(a, s) : launch<2, false>(a, s);
+    // is shared by more rows), two otherwise so every SM has warps in flight;
+    // the prologue holds 2 groups of x per thread up to K = 4096, else 6.
+    const bool r4 = a.w->rows >= 8192, k2 = a.w->nb * 4 <= 2 * kThreads;
+    if (a.x_ll) {
+        if (r4) return k2 ? launch<4, true, 2>(a, s) : launch<4, true, 6>(a, s);
+        return k2 ? launch<2, true, 2>(a, s) : launch<2, true, 6>(a, s);
+    }
+    if (r4) return k2 ? launch<4, false, 2>(a, s) : launch<4, false, 6>(a, s);
+    return k2 ? launch<2, false, 2>(a, s) : launch<2, false, 6>(a, s);
 }
 
 cudaError_t q4_block_dots(const mv_weight_s& w, const float* x, int32_t* isum, cudaStream_t s) {

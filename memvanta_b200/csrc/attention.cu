@@ -357,7 +357,9 @@ __host__ __device__ inline FusedSmem fused_plan(uint64_t hd, uint64_t max_ctx, u
     return p;
 }
 
-template <int HD>
+// TP: tensor parallel, the output goes to every rank's LL buffer (a separate
+// instantiation, so the one-GPU kernel carries none of it).
+template <int HD, bool TP>
 __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ float redf[HD / 32];
@@ -539,11 +541,9 @@ __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) 
                                  : reinterpret_cast<const float*>(vnew)[tid];
         out = fmaf(al, v, out);
     }
-    if (a.tp.world > 1) {
-        ll_put_all(a.tp, a.out_shared, (uint64_t)(a.head_off + h) * HD + tid, out, tp_uepoch(a.tp, a.out_point));
-    } else {
-        a.out[(size_t)h * HD + tid] = out;
-    }
+    if constexpr (TP) ll_put_all(a.tp, a.out_shared, (uint64_t)(a.head_off + h) * HD + tid, out,
+                                 tp_uepoch(a.tp, a.out_point));
+    else a.out[(size_t)h * HD + tid] = out;
 }
 
 uint64_t attn_fused_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type) {
@@ -556,16 +556,17 @@ cudaError_t attn_decode_fused(const AttnFusedArgs& a, cudaStream_t s) {
     const size_t smem = attn_fused_smem_bytes(a.hd, a.max_ctx ? a.max_ctx : 1, a.max_pages, a.kv_type);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     const dim3 grid((unsigned)a.n_head);
+    auto go = [&](auto kernel, int hd) {
+        ensure_smem_attr(kernel, 200 * 1024);
+        return launch_pdl(kernel, grid, dim3(hd), smem, s, a);
+    };
+    const bool tp = a.tp.world > 1;
     switch (a.hd) {
-        case 64:
-            ensure_smem_attr(attn_decode_fused_kernel<64>, 200 * 1024);
-            return launch_pdl(attn_decode_fused_kernel<64>, grid, dim3(64), smem, s, a);
+        case 64: return tp ? go(attn_decode_fused_kernel<64, true>, 64) : go(attn_decode_fused_kernel<64, false>, 64);
         case 128:
-            ensure_smem_attr(attn_decode_fused_kernel<128>, 200 * 1024);
-            return launch_pdl(attn_decode_fused_kernel<128>, grid, dim3(128), smem, s, a);
+            return tp ? go(attn_decode_fused_kernel<128, true>, 128) : go(attn_decode_fused_kernel<128, false>, 128);
         case 256:
-            ensure_smem_attr(attn_decode_fused_kernel<256>, 200 * 1024);
-            return launch_pdl(attn_decode_fused_kernel<256>, grid, dim3(256), smem, s, a);
+            return tp ? go(attn_decode_fused_kernel<256, true>, 256) : go(attn_decode_fused_kernel<256, false>, 256);
         default:
             return cudaErrorInvalidValue;
     }

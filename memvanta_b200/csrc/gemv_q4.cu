@@ -390,7 +390,7 @@ __device__ __forceinline__ void epilogue(int epi, int rg, int rows, int lane, fl
 // from the moment the CTAs are resident measured slower, every CTA hammering
 // the same few kilobytes of L2 while the producers run.
 template <int RPW, bool LL, int KEEP>
-__global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const uint4* __restrict__ qs,
+__global__ void __launch_bounds__(kThreads, 3) gemv_q4_kernel(const uint4* __restrict__ qs,
                                                               const unsigned short* __restrict__ dsc, int rows,
                                                               int nb, int dstride, const void* __restrict__ x,
                                                               const float* __restrict__ norm_w, float eps, int pro,
@@ -492,15 +492,10 @@ cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s) {
     const bool tp = a.tp && a.tp->world > 1;
     if ((!a.y && !a.x_ll) || (a.x_ll && !tp) || (!a.x_ll && !a.x)) return cudaErrorInvalidValue;
     // Four rows per warp where the matrix has rows to spare (the chain cost
-    // is shared by more rows), two otherwise so every SM has warps in flight;
-    // the prologue holds 2 groups of x per thread up to K = 4096, else 6.
-    const bool r4 = a.w->rows >= 8192, k2 = a.w->nb * 4 <= 2 * kThreads;
-    if (a.x_ll) {
-        if (r4) return k2 ? launch<4, true, 2>(a, s) : launch<4, true, 6>(a, s);
-        return k2 ? launch<2, true, 2>(a, s) : launch<2, true, 6>(a, s);
-    }
-    if (r4) return k2 ? launch<4, false, 2>(a, s) : launch<4, false, 6>(a, s);
-    return k2 ? launch<2, false, 2>(a, s) : launch<2, false, 6>(a, s);
+    // is shared by more rows), two otherwise so every SM has warps in flight.
+    const bool r4 = a.w->rows >= 8192;
+    if (a.x_ll) return r4 ? launch<4, true, 2>(a, s) : launch<2, true, 2>(a, s);
+    return r4 ? launch<4, false, 2>(a, s) : launch<2, false, 2>(a, s);
 }
 
 cudaError_t q4_block_dots(const mv_weight_s& w, const float* x, int32_t* isum, cudaStream_t s) {

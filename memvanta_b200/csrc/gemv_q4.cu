@@ -453,6 +453,202 @@ __global__ void __launch_bounds__(kThreads, 3) gemv_q4_kernel(const uint4* __res
     cp_async_wait<0>();
 }
 
+// ------------------------------------------------------- row-tile kernel
+// The same exact computation organised so that every lane does useful work.
+// A CTA owns tiles of kTR = 16 rows (grid-stride over tiles) and walks K in
+// chunks of 32 blocks through a kTS-stage cp.async ring shared by the CTA.
+// Eight compute warps turn a staged chunk into per-block terms (d_w*d_a,
+// float(isum)) for all 16 x 32 (row, block) pairs -- lane = row, so the
+// activation block is a shared-memory broadcast -- into one of two term
+// buffers; a ninth warp runs each row's FMA chain over the terms in block
+// order (lane = row) while the compute warps fill the other buffer, and
+// writes the outputs.  Instruction count per (row, block) is a quarter of
+// the warp-per-row-group kernel above, whose chain ran on RPW lanes.
+constexpr int kTR = 16;                    // rows per tile
+constexpr int kTC = 32;                    // blocks per chunk
+constexpr int kTS = 6;                     // ring stages (5 chunks in flight per CTA)
+constexpr int kTW = kTC * 16 + 16;         // staged payload bytes per row (padded: conflict-free lane = row)
+constexpr int kTSc = kTC * 2 + 16;         // staged scale bytes per row (padded)
+constexpr int kTStage = kTR * (kTW + kTSc);
+constexpr int kTT = kTC + 2;               // float2 per term row (padded)
+constexpr int kTComp = 8;                  // compute warps
+constexpr int kTThreads = (kTComp + 1) * 32;
+
+struct TileSmem {
+    int4* lo;
+    int4* hi;
+    float2* dc;
+    float2* terms;  // [2][kTR][kTT]
+    uint8_t* ring;  // [kTS][kTStage]
+};
+
+__device__ __forceinline__ TileSmem tile_smem(int nb) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    TileSmem t;
+    t.lo = reinterpret_cast<int4*>(smem_raw);
+    t.hi = t.lo + nb;
+    t.dc = reinterpret_cast<float2*>(t.hi + nb);
+    t.terms = t.dc + ((nb + 1) & ~1);
+    t.ring = reinterpret_cast<uint8_t*>(t.terms + 2 * kTR * kTT);
+    return t;
+}
+
+size_t tile_smem_bytes(uint64_t nb) {
+    return nb * 32 + ((nb + 1) & ~1ull) * 8 + (size_t)2 * kTR * kTT * 8 + (size_t)kTS * kTStage;
+}
+
+__device__ __forceinline__ void bar_named(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Staging of chunk c of tile t: 16 rows x 32 blocks of nibbles (two 16-byte
+// copies per compute thread: rows tid/32 and tid/32 + 8, block tid % 32) and
+// the chunk's 32 scales of every row (threads 0..63: row tid/4, 8 scales).
+struct TileIssuer {
+    const uint4* qs;
+    const unsigned short* dsc;
+    int rows, nb, dstride, tid;
+    __device__ __forceinline__ void operator()(uint8_t* st, int t, int c) const {
+        const int r0 = t * kTR, blk = tid & 31, b = c * kTC + blk;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int row = (tid >> 5) + 8 * k;
+            if (r0 + row < rows && b < nb)
+                cp_async16(st + row * kTW + blk * 16, qs + (size_t)(r0 + row) * nb + b);
+        }
+        if (tid < kTR * 4) {
+            const int row = tid >> 2, q = tid & 3, bs = c * kTC + q * 8;
+            if (r0 + row < rows && bs < nb)
+                cp_async16(st + kTR * kTW + row * kTSc + q * 16, dsc + (size_t)(r0 + row) * dstride + bs);
+        }
+    }
+};
+
+// (tile, chunk) of this CTA's items in order, advanced one item at a time.
+struct TileCursor {
+    int t, c;
+    __device__ __forceinline__ void next(int nchunk) {
+        if (++c == nchunk) {
+            c = 0;
+            t += gridDim.x;
+        }
+    }
+};
+
+// KEEP: groups of x each thread holds in the prologue (2 for K <= 4608, 5 up
+// to 11520 at 288 threads), so the whole activation is requested at once.
+template <bool LL, int KEEP>
+__global__ void __launch_bounds__(kTThreads, KEEP == 2 ? 3 : 2) gemv_q4_tile_kernel(const uint4* __restrict__ qs,
+                                                                    const unsigned short* __restrict__ dsc, int rows,
+                                                                    int nb, int dstride, const void* __restrict__ x,
+                                                                    const float* __restrict__ norm_w, float eps,
+                                                                    int pro, int epi, float* __restrict__ y,
+                                                                    const TpCtx tp, int x_point, uint64_t y_shared,
+                                                                    int y_row_off, int y_point, int res_point) {
+    const TileSmem sm = tile_smem(nb);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tiles = (rows + kTR - 1) / kTR, nchunk = (nb + kTC - 1) / kTC;
+    const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int items = my_tiles * nchunk;
+    const TileIssuer issue{qs, dsc, rows, nb, dstride, tid};
+    TileCursor nx{(int)blockIdx.x, 0};  // next item to stage
+    // weights are immutable: the first kTS-1 chunks are requested before
+    // waiting on the previous kernel
+    pdl_trigger();
+    if (warp < kTComp) {
+#pragma unroll
+        for (int k = 0; k < kTS - 1; ++k) {
+            if (k < items) {
+                issue(sm.ring + k * kTStage, nx.t, nx.c);
+                nx.next(nchunk);
+            }
+            cp_async_commit();
+        }
+    }
+    const bool rms = pro == (int)Q4Pro::RmsNorm;
+    NormPre np;
+    norm_preload(np, norm_w, rms, nb);
+    pdl_wait();
+    const Act a{sm.lo, sm.hi, sm.dc, nullptr};
+    if constexpr (LL) prologue<KEEP>(XLL{tp, static_cast<const uint2*>(x), tp_uepoch(tp, x_point), 100 + x_point},
+                                     np, norm_w, eps, rms, nb, a);
+    else prologue<KEEP>(XFloat{static_cast<const float4*>(x)}, np, norm_w, eps, rms, nb, a);
+
+    if (warp < kTComp) {
+        // compute warps: lane & 15 = row, warp and lane >> 4 pick 2 blocks
+        const int row = lane & 15, bq = warp * 4 + (lane >> 4) * 2;
+        int c = 0, slot = 0, nslot = kTS - 1;
+        for (int it = 0; it < items; ++it) {
+            cp_async_wait<kTS - 2>();
+            bar_named(1, kTComp * 32);  // chunk `it` landed for every thread; chunk it-1 fully read
+            if (it + kTS - 1 < items) {
+                issue(sm.ring + nslot * kTStage, nx.t, nx.c);
+                nx.next(nchunk);
+            }
+            cp_async_commit();
+            if (++nslot == kTS) nslot = 0;
+            const uint8_t* st = sm.ring + slot * kTStage;
+            if (++slot == kTS) slot = 0;
+            const uint32_t sc2 = *reinterpret_cast<const uint32_t*>(st + kTR * kTW + row * kTSc + bq * 2);
+            float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int b = c * kTC + bq + j;
+                if (b < nb) {
+                    const int4 alo = sm.lo[b], ahi = sm.hi[b];
+                    const float2 dc = sm.dc[b];
+                    const uint4 w = *reinterpret_cast<const uint4*>(st + row * kTW + (bq + j) * 16);
+                    const int isum = block_isum(w, alo, ahi, __float_as_int(dc.y));
+                    const float tw = half_bits_to_float((unsigned short)(sc2 >> (16 * j))) * dc.x;
+                    if (j == 0) out.x = tw, out.y = (float)isum;
+                    else out.z = tw, out.w = (float)isum;
+                }
+            }
+            *reinterpret_cast<float4*>(sm.terms + ((it & 1) * kTR + row) * kTT + bq) = out;
+            bar_named(2, kTThreads);  // terms of `it` complete; the chain of it-1 is done
+            if (++c == nchunk) c = 0;
+        }
+        cp_async_wait<0>();
+    } else {
+        // chain warp: lane = row of the tile
+        const bool rep = LL && tp.world > 1 && y == nullptr;
+        const YOut<LL> yo{y, tp, y_shared, y_row_off, rep ? tp_uepoch(tp, y_point) : 0u,
+                          rep ? tp_uepoch(tp, res_point) : 0u, rep};
+        float sum = 0.0f;
+        TileCursor cur{(int)blockIdx.x, 0};
+        for (int it = 0; it < items; ++it) {
+            bar_named(2, kTThreads);
+            const int t = cur.t, c = cur.c;
+            cur.next(nchunk);
+            if (lane < kTR) {
+                const float2* tr = sm.terms + ((it & 1) * kTR + lane) * kTT;
+                const int n = min(kTC, nb - c * kTC);
+                if (n == kTC) {
+#pragma unroll
+                    for (int k = 0; k < kTC; k += 2) {
+                        const float4 v = *reinterpret_cast<const float4*>(tr + k);
+                        sum = fmaf(v.x, v.y, sum);
+                        sum = fmaf(v.z, v.w, sum);
+                    }
+                } else {
+                    for (int k = 0; k < n; ++k) sum = fmaf(tr[k].x, tr[k].y, sum);
+                }
+            }
+            if (c == nchunk - 1) {
+                const int r = t * kTR + lane;
+                if (epi == (int)Q4Epi::SiluGate) {
+                    const float u = __shfl_down_sync(0xffffffffu, sum, 1);
+                    if (lane < kTR && (lane & 1) == 0 && r + 1 < rows)
+                        yo.put(r / 2, (sum / (1.0f + expf_cr(-sum))) * u);
+                } else if (lane < kTR && r < rows) {
+                    yo.put(r, epi == (int)Q4Epi::AddTo ? yo.local(r) + sum : sum);
+                }
+                sum = 0.0f;
+            }
+        }
+    }
+}
+
 // Diagnostic twin: the per-block int32 dots of the same device code.
 __global__ void __launch_bounds__(kThreads) q4_block_dots_kernel(const uint4* __restrict__ qs, int rows, int nb,
                                                                  const float* __restrict__ x,
@@ -484,6 +680,21 @@ cudaError_t launch(const GemvQ4Args& g, cudaStream_t s) {
                       g.x_point, g.y_shared, g.y_row_off, g.y_point, g.res_point);
 }
 
+template <bool LL, int KEEP>
+cudaError_t launch_tile(const GemvQ4Args& g, cudaStream_t s) {
+    const mv_weight_s& w = *g.w;
+    const size_t smem = tile_smem_bytes(w.nb);
+    if (smem > 110 * 1024) return cudaErrorInvalidValue;  // two CTAs per SM at least
+    ensure_smem_attr(gemv_q4_tile_kernel<LL, KEEP>, 200 * 1024);
+    const uint64_t tiles = (w.rows + kTR - 1) / kTR;
+    const uint64_t cap = (uint64_t)num_sms() * (KEEP == 2 && smem <= 74 * 1024 ? 3 : 2);
+    const void* x = LL ? g.x_ll : static_cast<const void*>(g.x);
+    return launch_pdl(gemv_q4_tile_kernel<LL, KEEP>, dim3((unsigned)(tiles < cap ? tiles : cap)), dim3(kTThreads), smem, s,
+                      reinterpret_cast<const uint4*>(w.qs), (const unsigned short*)w.d, (int)w.rows, (int)w.nb,
+                      (int)w.dstride, x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y, g.tp ? *g.tp : TpCtx{},
+                      g.x_point, g.y_shared, g.y_row_off, g.y_point, g.res_point);
+}
+
 }  // namespace
 
 cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s) {
@@ -491,6 +702,11 @@ cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s) {
     if (a.w->cols % 32) return cudaErrorInvalidValue;
     const bool tp = a.tp && a.tp->world > 1;
     if ((!a.y && !a.x_ll) || (a.x_ll && !tp) || (!a.x_ll && !a.x)) return cudaErrorInvalidValue;
+    if (tile_smem_bytes(a.w->nb) <= 110 * 1024 && a.w->nb * 4 <= 5 * kTThreads) {
+        const bool k2 = a.w->nb * 4 <= 2 * kTThreads;
+        if (a.x_ll) return k2 ? launch_tile<true, 2>(a, s) : launch_tile<true, 5>(a, s);
+        return k2 ? launch_tile<false, 2>(a, s) : launch_tile<false, 5>(a, s);
+    }
     // Four rows per warp where the matrix has rows to spare (the chain cost
     // is shared by more rows), two otherwise so every SM has warps in flight.
     const bool r4 = a.w->rows >= 8192;

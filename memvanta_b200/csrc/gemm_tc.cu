@@ -444,26 +444,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
-
-EncodeFn encode_fn() {
-    static const EncodeFn fn = []() -> EncodeFn {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return nullptr;
-        return reinterpret_cast<EncodeFn>(p);
-    }();
-    return fn;
-}
-
-bool encode(EncodeFn enc, CUtensorMap* map, CUtensorMapDataType type, int rank, void* base, const cuuint64_t* dims,
-            const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swizzle) {
-    const cuuint32_t es[3] = {1, 1, 1};
-    return enc(map, type, rank, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
+using tc::EncodeFn;
+using tc::encode;
+using tc::encode_fn;
 
 template <int N>
 cudaError_t launch_tc(const mv_weight_s& w, const int8_t* q, const float* dT, uint64_t ldb, uint64_t batch, float* y,

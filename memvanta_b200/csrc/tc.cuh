@@ -10,6 +10,7 @@
 // drained, TMEM freed) and returns.
 #pragma once
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -18,6 +19,30 @@ namespace mvb {
 namespace tc {
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s without progress = stuck
+
+// ------------------------------------------------- tensor maps (host)
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+// The driver's cuTensorMapEncodeTiled, looked up once (nullptr if absent).
+inline EncodeFn encode_fn() {
+    static const EncodeFn fn = []() -> EncodeFn {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<EncodeFn>(p);
+    }();
+    return fn;
+}
+
+inline bool encode(EncodeFn enc, CUtensorMap* map, CUtensorMapDataType type, int rank, void* base,
+                   const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                   CUtensorMapSwizzle swizzle) {
+    const cuuint32_t es[3] = {1, 1, 1};
+    return enc(map, type, rank, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

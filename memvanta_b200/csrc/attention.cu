@@ -341,6 +341,12 @@ __global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
 struct FusedSmem {
     uint64_t q, table, sc, knew, vnew, kring, vring, total;
 };
+// V ring depth: 8 tiles (256 tokens, all of a typical context in flight
+// before the PDL wait) where a token's head slice is at most 256 bytes, 4
+// otherwise (shared memory).
+__host__ __device__ inline int fused_vstages(uint64_t hd, int kv_type) {
+    return hd * (kv_type == 0 ? 4 : 2) <= 256 ? 8 : 4;
+}
 __host__ __device__ inline FusedSmem fused_plan(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type) {
     auto up = [](uint64_t n) { return (n + 15) / 16 * 16; };
     const uint64_t esize = kv_type == 0 ? 4 : 2;
@@ -353,13 +359,13 @@ __host__ __device__ inline FusedSmem fused_plan(uint64_t hd, uint64_t max_ctx, u
     p.vnew = p.knew + up(hd * esize);
     p.kring = p.vnew + up(hd * esize);
     p.vring = p.kring + 2 * (uint64_t)attn_ktile(hd, kv_type) * krow;
-    p.total = p.vring + (uint64_t)kVStages * kVTile * hd * esize;
+    p.total = p.vring + (uint64_t)fused_vstages(hd, kv_type) * kVTile * hd * esize;
     return p;
 }
 
 // TP: tensor parallel, the output goes to every rank's LL buffer (a separate
 // instantiation, so the one-GPU kernel carries none of it).
-template <int HD, bool TP>
+template <int HD, bool TP, int VS>
 __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ float redf[HD / 32];
@@ -407,7 +413,7 @@ __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) 
     const int nvt = (p + kVTile - 1) / kVTile;
     auto issue_v = [&](int tile) {
         if (tile < nvt) {
-            uint8_t* dst = vring + (size_t)(tile % kVStages) * kVTile * slice;
+            uint8_t* dst = vring + (size_t)(tile % VS) * kVTile * slice;
             for (int c = tid; c < chunks; c += HD) {
                 const int tt = c / (slice / 16), off = (c % (slice / 16)) * 16;
                 const int t = tile * kVTile + tt;
@@ -416,18 +422,22 @@ __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) 
         }
         cp_async_commit();
     };
-    // groups in flight: V tiles 0..kVStages-2, then K tile 0
-    for (int k = 0; k < kVStages - 1; ++k) issue_v(k);
+    // groups in flight: V tiles 0..VS-2, then K tiles 0 and 1
+    for (int k = 0; k < VS - 1; ++k) issue_v(k);
     issue_k(0, 0);
+    if (nkt > 1) issue_k(1, 1);
+    // this token's rotation (the tables are immutable)
+    float c = 0.0f, sn = 0.0f;
+    if (tid < half) {
+        c = a.cos_t[(size_t)p * half + tid];
+        sn = a.sin_t[(size_t)p * half + tid];
+    }
 
     pdl_wait();
     // this token: RoPE of q (head h) and k (kv head kh), k and v in cache form
     {
-        const float* co = a.cos_t + (size_t)p * half;
-        const float* si = a.sin_t + (size_t)p * half;
         const float* row = a.qkv;
         if (tid < half) {
-            const float c = co[tid], sn = si[tid];
             const float q0 = row[h * HD + tid], q1 = row[h * HD + tid + half];
             qs[tid] = __fmaf_rn(q0, c, -__fmul_rn(q1, sn));
             qs[tid + half] = __fmaf_rn(q0, sn, __fmul_rn(q1, c));
@@ -484,14 +494,19 @@ __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) 
         for (int l = 1; l < 8; ++l) dot += acc[l];
         return dot / sqrtf((float)HD);
     };
+    // K groups: tiles 0 and 1 before the wait, tile t+1 after tile t-1 (own
+    // rows: each thread reads only the rows it copied)
     for (int tile = 0; tile < nkt; ++tile) {
-        if (tile + 1 < nkt) issue_k(tile + 1, (tile + 1) & 1);
-        else cp_async_commit();
+        if (tile >= 1 || nkt == 1) {
+            if (tile >= 1 && tile + 1 < nkt) issue_k(tile + 1, (tile + 1) & 1);
+            else cp_async_commit();
+        }
         cp_async_wait<1>();  // own row of this tile has landed (and, before it, the V tiles)
         const int t = tile * KT + tid;
         if (tid < KT && t < p) sc[t] = dot_row(kring + ((size_t)(tile & 1) * KT + tid) * krow);
     }
-    if (tid == 0) sc[p] = dot_row(knew);
+    // this token's score: by a thread without a token in the last tile
+    if (tid == (p % KT ? KT - 1 : 0)) sc[p] = dot_row(knew);
     __syncthreads();
 
     // 2. max, exp, double denominator, weights (all p + 1 tokens)
@@ -521,9 +536,9 @@ __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) 
     // 3. out_d = fma(alpha_t, v_t[d], out_d) over the cached tokens in order, then this token
     float out = 0.0f;
     for (int tile = 0; tile < nvt; ++tile) {
-        cp_async_wait<kVStages - 2>();
+        cp_async_wait<VS - 2>();
         __syncthreads();  // the tile is visible to every thread
-        const uint8_t* vt = vring + (size_t)(tile % kVStages) * kVTile * slice;
+        const uint8_t* vt = vring + (size_t)(tile % VS) * kVTile * slice;
         const int n = min(kVTile, p - tile * kVTile);
         for (int tt = 0; tt < n; ++tt) {
             const float al = sc[tile * kVTile + tt] * inv;  // alpha_t = e_t * float(1/den)
@@ -532,7 +547,7 @@ __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) 
             out = fmaf(al, v, out);
         }
         __syncthreads();  // everyone is done with this stage before it is refilled
-        issue_v(tile + kVStages - 1);
+        issue_v(tile + VS - 1);
     }
     cp_async_wait<0>();
     {
@@ -560,16 +575,17 @@ cudaError_t attn_decode_fused(const AttnFusedArgs& a, cudaStream_t s) {
         ensure_smem_attr(kernel, 200 * 1024);
         return launch_pdl(kernel, grid, dim3(hd), smem, s, a);
     };
-    const bool tp = a.tp.world > 1;
+    const bool tp = a.tp.world > 1, v8 = fused_vstages(a.hd, a.kv_type) == 8;
+#define MV_FUSED(H)                                                                                  \
+    (tp ? (v8 ? go(attn_decode_fused_kernel<H, true, 8>, H) : go(attn_decode_fused_kernel<H, true, 4>, H)) \
+        : (v8 ? go(attn_decode_fused_kernel<H, false, 8>, H) : go(attn_decode_fused_kernel<H, false, 4>, H)))
     switch (a.hd) {
-        case 64: return tp ? go(attn_decode_fused_kernel<64, true>, 64) : go(attn_decode_fused_kernel<64, false>, 64);
-        case 128:
-            return tp ? go(attn_decode_fused_kernel<128, true>, 128) : go(attn_decode_fused_kernel<128, false>, 128);
-        case 256:
-            return tp ? go(attn_decode_fused_kernel<256, true>, 256) : go(attn_decode_fused_kernel<256, false>, 256);
-        default:
-            return cudaErrorInvalidValue;
+        case 64: return MV_FUSED(64);
+        case 128: return MV_FUSED(128);
+        case 256: return MV_FUSED(256);
+        default: return cudaErrorInvalidValue;
     }
+#undef MV_FUSED
 }
 
 uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type) {

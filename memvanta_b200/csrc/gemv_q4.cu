@@ -30,9 +30,16 @@
 //   sum (nib-8)*a = sum dp4a(w & 0x0F0F0F0F, a_lo) + dp4a((w>>4) & 0x0F0F0F0F, a_hi)
 //                   - 8*sum(a)
 // (nibbles 0..15 are non-negative bytes for the signed dp4a).
+#include <cooperative_groups.h>
+
+#include <map>
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "tp.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace mvb {
 
@@ -104,11 +111,21 @@ __device__ __forceinline__ double block_sum_d(double v) {
     return r;
 }
 
+// Where a quantised group goes: this CTA's shared memory.
+struct LocalSink {
+    const Act& a;
+    __device__ __forceinline__ void put(int b, int sub, uint2 pk, bool first, float2 dc) const {
+        *(reinterpret_cast<uint2*>(sub < 2 ? &a.lo[b] : &a.hi[b]) + (sub & 1)) = pk;
+        if (first) a.dc[b] = dc;
+    }
+};
+
 // One 8-element group of the quantisation: 4 neighbouring lanes hold one
 // 32-element block.  All 32 lanes of the warp must call it (shuffles).
 // n0/n1: the group's RMSNorm weights (used when rms).
+template <class Sink = LocalSink>
 __device__ __forceinline__ void quant_group(int g, bool active, float4 u, float4 w, float4 n0, float4 n1, bool rms,
-                                            float inv, const Act& a) {
+                                            float inv, const Sink& out) {
     float v[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
     if (active && rms) {
         const float nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
@@ -136,12 +153,7 @@ __device__ __forceinline__ void quant_group(int g, bool active, float4 u, float4
     }
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    if (active) {
-        const int b = g >> 2, sub = g & 3;
-        uint2* dst = reinterpret_cast<uint2*>(sub < 2 ? &a.lo[b] : &a.hi[b]) + (sub & 1);
-        *dst = make_uint2(pk[0], pk[1]);
-        if (sub == 0) a.dc[b] = make_float2(d, __int_as_float(8 * sum));
-    }
+    if (active) out.put(g >> 2, g & 3, make_uint2(pk[0], pk[1]), (g & 3) == 0, make_float2(d, __int_as_float(8 * sum)));
 }
 
 // Group loaders: 8 consecutive elements of x, from a float vector or (tensor
@@ -238,7 +250,7 @@ __device__ __forceinline__ void prologue(const Ld& ld, const NormPre& np, const 
             const int g = tid + it * bd;
             float4 n0, n1;
             norm_of(it, g, n0, n1);
-            quant_group(g, g < G, keep[it][0], keep[it][1], n0, n1, rms, inv, a);
+            quant_group(g, g < G, keep[it][0], keep[it][1], n0, n1, rms, inv, LocalSink{a});
         }
     }
     for (int it = kKeep; it < iters; ++it) {
@@ -247,7 +259,7 @@ __device__ __forceinline__ void prologue(const Ld& ld, const NormPre& np, const 
         float4 u = z, w = z, n0, n1;
         if (active) ld(g, u, w);
         norm_of(it, g, n0, n1);
-        quant_group(g, active, u, w, n0, n1, rms, inv, a);
+        quant_group(g, active, u, w, n0, n1, rms, inv, LocalSink{a});
     }
     __syncthreads();
 }
@@ -453,6 +465,109 @@ __global__ void __launch_bounds__(kThreads, 3) gemv_q4_kernel(const uint4* __res
     cp_async_wait<0>();
 }
 
+// ------------------------------------------------- cluster-shared prologue
+// The activation is the same for every CTA of a GEMV, and with three CTAs on
+// every SM its quantisation (and RMSNorm) is a real share of the kernel's
+// critical path.  A cluster of kCl CTAs splits it: CTA r of the cluster
+// loads, normalises and quantises blocks [r*nbr, (r+1)*nbr) only and stores
+// them into the shared memory of every CTA of the cluster (distributed shared
+// memory); the RMSNorm sum of squares is the fixed-order sum of the kCl
+// partial sums.
+constexpr int kCl = 2;
+
+struct ClusterSink {
+    const Act& a;
+    __device__ __forceinline__ void put(int b, int sub, uint2 pk, bool first, float2 dc) const {
+        cg::cluster_group cl = cg::this_cluster();
+        uint2* lp = reinterpret_cast<uint2*>(sub < 2 ? &a.lo[b] : &a.hi[b]) + (sub & 1);
+#pragma unroll
+        for (int r = 0; r < kCl; ++r) {
+            *cl.map_shared_rank(lp, r) = pk;
+            if (first) *cl.map_shared_rank(&a.dc[b], r) = dc;
+        }
+    }
+};
+
+// This CTA's slice of x in groups [g0, g1) (cluster rank r of kCl).
+__device__ __forceinline__ void cluster_slice(int nb, int& g0, int& g1) {
+    const int rank = (int)cg::this_cluster().block_rank(), nbr = (nb + kCl - 1) / kCl;
+    g0 = min(nb, rank * nbr) * 4;
+    g1 = min(nb, (rank + 1) * nbr) * 4;
+}
+
+// RMSNorm weights of this thread's first two groups of the slice (immutable:
+// fetched before the dependency wait).
+__device__ __forceinline__ void norm_preload_slice(NormPre& np, const float* __restrict__ norm_w, bool rms, int nb) {
+    int g0, g1;
+    cluster_slice(nb, g0, g1);
+    const int tid = (int)threadIdx.x, bd = (int)blockDim.x;
+#pragma unroll
+    for (int it = 0; it < kNormKeep; ++it) {
+        const int g = g0 + tid + it * bd;
+        np.w[it][0] = np.w[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (rms && g < g1) {
+            np.w[it][0] = reinterpret_cast<const float4*>(norm_w)[2 * g];
+            np.w[it][1] = reinterpret_cast<const float4*>(norm_w)[2 * g + 1];
+        }
+    }
+}
+
+template <class Ld>
+__device__ __forceinline__ void prologue_cluster(const Ld& ld, const NormPre& np, const float* __restrict__ norm_w,
+                                                 float eps, bool rms, int nb, const Act& a, double* part) {
+    static_assert(kNormKeep == 2, "two groups per thread are kept");
+    cg::cluster_group cl = cg::this_cluster();
+    const int rank = (int)cl.block_rank();
+    int g0, g1;
+    cluster_slice(nb, g0, g1);
+    const int bd = (int)blockDim.x, tid = (int)threadIdx.x;
+    const int iters = (((nb + kCl - 1) / kCl) * 4 + bd - 1) / bd;  // the same in every CTA
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int ga = g0 + tid, gb = g0 + tid + bd;
+    float4 a0 = z, a1 = z, b0 = z, b1 = z;
+    if (ga < g1) ld(ga, a0, a1);
+    if (gb < g1) ld(gb, b0, b1);
+    float inv = 1.0f;
+    if (rms) {
+        double ss = 0.0;
+        auto acc = [&](float4 u, float4 v) {
+            ss += (double)u.x * u.x + (double)u.y * u.y + (double)u.z * u.z + (double)u.w * u.w;
+            ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+        };
+        acc(a0, a1);
+        acc(b0, b1);
+        for (int g = g0 + tid + 2 * bd; g < g1; g += bd) {
+            float4 u, v;
+            ld(g, u, v);
+            acc(u, v);
+        }
+        const double mine = block_sum_d(ss);
+        if (tid == 0)
+            for (int r = 0; r < kCl; ++r) *cl.map_shared_rank(part + rank, r) = mine;
+        cl.sync();  // every CTA's partial sum is everywhere
+        double tot = 0.0;
+        for (int r = 0; r < kCl; ++r) tot += part[r];
+        inv = 1.0f / sqrtf((float)(tot / (double)(nb * 32)) + eps);
+    }
+    const ClusterSink sink{a};
+    if (iters > 0) quant_group(ga, ga < g1, a0, a1, np.w[0][0], np.w[0][1], rms, inv, sink);
+    if (iters > 1) quant_group(gb, gb < g1, b0, b1, np.w[1][0], np.w[1][1], rms, inv, sink);
+    for (int it = 2; it < iters; ++it) {
+        const int g = g0 + tid + it * bd;
+        const bool active = g < g1;  // uniform over the 4 lanes of a block
+        float4 u = z, w = z, n0 = z, n1 = z;
+        if (active) {
+            ld(g, u, w);
+            if (rms) {
+                n0 = reinterpret_cast<const float4*>(norm_w)[2 * g];
+                n1 = reinterpret_cast<const float4*>(norm_w)[2 * g + 1];
+            }
+        }
+        quant_group(g, active, u, w, n0, n1, rms, inv, sink);
+    }
+    cl.sync();  // every block of x is in every CTA's shared memory
+}
+
 // ------------------------------------------------------- row-tile kernel
 // The same exact computation organised so that every lane does useful work.
 // A CTA owns tiles of kTR = 16 rows (grid-stride over tiles) and walks K in
@@ -535,16 +650,17 @@ struct TileCursor {
     }
 };
 
-// KEEP: groups of x each thread holds in the prologue (2 for K <= 4608, 5 up
-// to 11520 at 288 threads), so the whole activation is requested at once.
-template <bool LL, int KEEP>
-__global__ void __launch_bounds__(kTThreads, KEEP == 2 ? 3 : 2) gemv_q4_tile_kernel(const uint4* __restrict__ qs,
+// Launched in clusters of kCl CTAs: the activation prologue is split across
+// the cluster (prologue_cluster).
+template <bool LL>
+__global__ void __launch_bounds__(kTThreads, 3) gemv_q4_tile_kernel(const uint4* __restrict__ qs,
                                                                     const unsigned short* __restrict__ dsc, int rows,
                                                                     int nb, int dstride, const void* __restrict__ x,
                                                                     const float* __restrict__ norm_w, float eps,
                                                                     int pro, int epi, float* __restrict__ y,
                                                                     const TpCtx tp, int x_point, uint64_t y_shared,
                                                                     int y_row_off, int y_point, int res_point) {
+    __shared__ double part[kCl];
     const TileSmem sm = tile_smem(nb);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int tiles = (rows + kTR - 1) / kTR, nchunk = (nb + kTC - 1) / kTC;
@@ -567,12 +683,14 @@ __global__ void __launch_bounds__(kTThreads, KEEP == 2 ? 3 : 2) gemv_q4_tile_ker
     }
     const bool rms = pro == (int)Q4Pro::RmsNorm;
     NormPre np;
-    norm_preload(np, norm_w, rms, nb);
+    norm_preload_slice(np, norm_w, rms, nb);
+    cg::this_cluster().sync();  // every CTA of the cluster runs before any writes into its shared memory
     pdl_wait();
     const Act a{sm.lo, sm.hi, sm.dc, nullptr};
-    if constexpr (LL) prologue<KEEP>(XLL{tp, static_cast<const uint2*>(x), tp_uepoch(tp, x_point), 100 + x_point},
-                                     np, norm_w, eps, rms, nb, a);
-    else prologue<KEEP>(XFloat{static_cast<const float4*>(x)}, np, norm_w, eps, rms, nb, a);
+    if constexpr (LL)
+        prologue_cluster(XLL{tp, static_cast<const uint2*>(x), tp_uepoch(tp, x_point), 100 + x_point}, np, norm_w,
+                         eps, rms, nb, a, part);
+    else prologue_cluster(XFloat{static_cast<const float4*>(x)}, np, norm_w, eps, rms, nb, a, part);
 
     if (warp < kTComp) {
         // compute warps: lane & 15 = row, warp and lane >> 4 pick 2 blocks
@@ -680,19 +798,51 @@ cudaError_t launch(const GemvQ4Args& g, cudaStream_t s) {
                       g.x_point, g.y_shared, g.y_row_off, g.y_point, g.res_point);
 }
 
-template <bool LL, int KEEP>
+template <bool LL>
 cudaError_t launch_tile(const GemvQ4Args& g, cudaStream_t s) {
     const mv_weight_s& w = *g.w;
     const size_t smem = tile_smem_bytes(w.nb);
     if (smem > 110 * 1024) return cudaErrorInvalidValue;  // two CTAs per SM at least
-    ensure_smem_attr(gemv_q4_tile_kernel<LL, KEEP>, 200 * 1024);
+    ensure_smem_attr(gemv_q4_tile_kernel<LL>, 200 * 1024);
+    // as many clusters as can be resident at once (clusters are placed
+    // within a GPC, so this can be below SMs x CTAs per SM / kCl)
+    static std::mutex mu;
+    static std::map<std::pair<size_t, int>, int> fit;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int clusters = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = fit.find({smem, dev});
+        if (it != fit.end()) {
+            clusters = it->second;
+        } else {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(kCl * 64);
+            cfg.blockDim = dim3(kTThreads);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = kCl;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&clusters, gemv_q4_tile_kernel<LL>, &cfg) != cudaSuccess || clusters < 1) {
+                cudaGetLastError();
+                clusters = num_sms() * 2 / kCl;
+            }
+            fit[{smem, dev}] = clusters;
+        }
+    }
     const uint64_t tiles = (w.rows + kTR - 1) / kTR;
-    const uint64_t cap = (uint64_t)num_sms() * (KEEP == 2 && smem <= 74 * 1024 ? 3 : 2);
+    const uint64_t cap = (uint64_t)clusters * kCl;
+    const uint64_t grid = ((tiles < cap ? tiles : cap) + kCl - 1) / kCl * kCl;
     const void* x = LL ? g.x_ll : static_cast<const void*>(g.x);
-    return launch_pdl(gemv_q4_tile_kernel<LL, KEEP>, dim3((unsigned)(tiles < cap ? tiles : cap)), dim3(kTThreads), smem, s,
-                      reinterpret_cast<const uint4*>(w.qs), (const unsigned short*)w.d, (int)w.rows, (int)w.nb,
-                      (int)w.dstride, x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y, g.tp ? *g.tp : TpCtx{},
-                      g.x_point, g.y_shared, g.y_row_off, g.y_point, g.res_point);
+    return launch_pdl_cluster(gemv_q4_tile_kernel<LL>, dim3((unsigned)grid), dim3(kTThreads), smem, s, kCl,
+                              reinterpret_cast<const uint4*>(w.qs), (const unsigned short*)w.d, (int)w.rows,
+                              (int)w.nb, (int)w.dstride, x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y,
+                              g.tp ? *g.tp : TpCtx{}, g.x_point, g.y_shared, g.y_row_off, g.y_point, g.res_point);
 }
 
 }  // namespace
@@ -702,11 +852,7 @@ cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s) {
     if (a.w->cols % 32) return cudaErrorInvalidValue;
     const bool tp = a.tp && a.tp->world > 1;
     if ((!a.y && !a.x_ll) || (a.x_ll && !tp) || (!a.x_ll && !a.x)) return cudaErrorInvalidValue;
-    if (tile_smem_bytes(a.w->nb) <= 110 * 1024 && a.w->nb * 4 <= 5 * kTThreads) {
-        const bool k2 = a.w->nb * 4 <= 2 * kTThreads;
-        if (a.x_ll) return k2 ? launch_tile<true, 2>(a, s) : launch_tile<true, 5>(a, s);
-        return k2 ? launch_tile<false, 2>(a, s) : launch_tile<false, 5>(a, s);
-    }
+    if (tile_smem_bytes(a.w->nb) <= 110 * 1024) return a.x_ll ? launch_tile<true>(a, s) : launch_tile<false>(a, s);
     // Four rows per warp where the matrix has rows to spare (the chain cost
     // is shared by more rows), two otherwise so every SM has warps in flight.
     const bool r4 = a.w->rows >= 8192;

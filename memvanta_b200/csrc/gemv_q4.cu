@@ -37,6 +37,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tc.cuh"
 #include "tp.cuh"
 
 namespace cg = cooperative_groups;
@@ -468,22 +469,74 @@ __global__ void __launch_bounds__(kThreads, 3) gemv_q4_kernel(const uint4* __res
 // ------------------------------------------------- cluster-shared prologue
 // The activation is the same for every CTA of a GEMV, and with three CTAs on
 // every SM its quantisation (and RMSNorm) is a real share of the kernel's
-// critical path.  A cluster of kCl CTAs splits it: CTA r of the cluster
-// loads, normalises and quantises blocks [r*nbr, (r+1)*nbr) only and stores
-// them into the shared memory of every CTA of the cluster (distributed shared
-// memory); the RMSNorm sum of squares is the fixed-order sum of the kCl
-// partial sums.
+// critical path.  A pair of CTAs (a cluster of kCl = 2) splits it: CTA r
+// loads, normalises and quantises blocks [r*nbr, (r+1)*nbr) only, keeps them
+// and sends them to the other CTA's shared memory with st.async, which
+// completes bytes on the receiver's mbarrier -- no fence, no cluster barrier
+// on the data path (a release barrier here would also wait for this
+// thread's weight prefetch).  The RMSNorm sum of squares is the fixed-order
+// sum of the two partial sums, exchanged the same way.
 constexpr int kCl = 2;
 
-struct ClusterSink {
+__device__ int g_gemv_status = 0;  // site of a GEMV wait that ran out (0: none)
+
+struct PairX {
+    uint64_t bar[2];  // [0]: the partner's partial sum (8 B), [1]: its quantised blocks
+    double part[kCl];
+    int abort;
+};
+
+__device__ __forceinline__ uint32_t mapa_peer(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_async_b64(uint32_t raddr, uint64_t v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b64 [%0], %1, [%2];" ::"r"(raddr), "l"(v),
+                 "r"(rbar)
+                 : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Bytes one CTA sends the other: 40 per block (lo 16, hi 16, d/sum 8).
+__device__ __forceinline__ uint32_t pair_bytes(int nb, int rank) {
+    const int nbr = (nb + kCl - 1) / kCl;
+    const int b0 = min(nb, rank * nbr), b1 = min(nb, (rank + 1) * nbr);
+    return (uint32_t)(b1 - b0) * 40u;
+}
+
+// Thread 0, first thing in the kernel: the two receive barriers, armed for
+// what the partner will send; then every CTA of the cluster has started and
+// sees them initialised (relaxed arrive: nothing else is published yet).
+__device__ __forceinline__ void pair_setup(PairX& px, int nb, bool rms) {
+    if (threadIdx.x == 0) {
+        const uint32_t b = tc::smem_u32(px.bar);
+        px.abort = 0;
+        tc::mbar_init(b, 1);
+        tc::mbar_init(b + 8, 1);
+        tc::mbar_fence_init();
+        if (rms) tc::mbar_expect_tx(b, 8);
+        tc::mbar_expect_tx(b + 8, pair_bytes(nb, (int)cluster_rank() ^ 1));
+    }
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+
+struct PairSink {
     const Act& a;
+    uint32_t peer, rbar;
     __device__ __forceinline__ void put(int b, int sub, uint2 pk, bool first, float2 dc) const {
-        cg::cluster_group cl = cg::this_cluster();
         uint2* lp = reinterpret_cast<uint2*>(sub < 2 ? &a.lo[b] : &a.hi[b]) + (sub & 1);
-#pragma unroll
-        for (int r = 0; r < kCl; ++r) {
-            *cl.map_shared_rank(lp, r) = pk;
-            if (first) *cl.map_shared_rank(&a.dc[b], r) = dc;
+        *lp = pk;
+        st_async_b64(mapa_peer(tc::smem_u32(lp), peer), (uint64_t)pk.x | ((uint64_t)pk.y << 32), rbar);
+        if (first) {
+            a.dc[b] = dc;
+            st_async_b64(mapa_peer(tc::smem_u32(&a.dc[b]), peer),
+                         (uint64_t)__float_as_uint(dc.x) | ((uint64_t)__float_as_uint(dc.y) << 32), rbar);
         }
     }
 };
@@ -514,14 +567,15 @@ __device__ __forceinline__ void norm_preload_slice(NormPre& np, const float* __r
 
 template <class Ld>
 __device__ __forceinline__ void prologue_cluster(const Ld& ld, const NormPre& np, const float* __restrict__ norm_w,
-                                                 float eps, bool rms, int nb, const Act& a, double* part) {
+                                                 float eps, bool rms, int nb, const Act& a, PairX& px) {
     static_assert(kNormKeep == 2, "two groups per thread are kept");
-    cg::cluster_group cl = cg::this_cluster();
-    const int rank = (int)cl.block_rank();
+    static_assert(kCl == 2, "pairs of CTAs");
+    const uint32_t rank = cluster_rank(), peer = rank ^ 1u;
+    const uint32_t bar0 = tc::smem_u32(px.bar), bar1 = bar0 + 8;
     int g0, g1;
     cluster_slice(nb, g0, g1);
     const int bd = (int)blockDim.x, tid = (int)threadIdx.x;
-    const int iters = (((nb + kCl - 1) / kCl) * 4 + bd - 1) / bd;  // the same in every CTA
+    const int iters = (((nb + kCl - 1) / kCl) * 4 + bd - 1) / bd;  // the same in both CTAs
     const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
     const int ga = g0 + tid, gb = g0 + tid + bd;
     float4 a0 = z, a1 = z, b0 = z, b1 = z;
@@ -541,15 +595,16 @@ __device__ __forceinline__ void prologue_cluster(const Ld& ld, const NormPre& np
             ld(g, u, v);
             acc(u, v);
         }
-        const double mine = block_sum_d(ss);
+        const double mine = block_sum_d(ss);  // ends with __syncthreads
         if (tid == 0)
-            for (int r = 0; r < kCl; ++r) *cl.map_shared_rank(part + rank, r) = mine;
-        cl.sync();  // every CTA's partial sum is everywhere
-        double tot = 0.0;
-        for (int r = 0; r < kCl; ++r) tot += part[r];
+            st_async_b64(mapa_peer(tc::smem_u32(&px.part[rank]), peer), (uint64_t)__double_as_longlong(mine),
+                         mapa_peer(bar0, peer));
+        tc::mbar_wait(bar0, 0, &px.abort, &g_gemv_status, 3);
+        // rank 0's partial first in both CTAs: the same sum, the same inv
+        const double tot = rank == 0 ? mine + px.part[1] : px.part[0] + mine;
         inv = 1.0f / sqrtf((float)(tot / (double)(nb * 32)) + eps);
     }
-    const ClusterSink sink{a};
+    const PairSink sink{a, peer, mapa_peer(bar1, peer)};
     if (iters > 0) quant_group(ga, ga < g1, a0, a1, np.w[0][0], np.w[0][1], rms, inv, sink);
     if (iters > 1) quant_group(gb, gb < g1, b0, b1, np.w[1][0], np.w[1][1], rms, inv, sink);
     for (int it = 2; it < iters; ++it) {
@@ -565,7 +620,8 @@ __device__ __forceinline__ void prologue_cluster(const Ld& ld, const NormPre& np
         }
         quant_group(g, active, u, w, n0, n1, rms, inv, sink);
     }
-    cl.sync();  // every block of x is in every CTA's shared memory
+    tc::mbar_wait(bar1, 0, &px.abort, &g_gemv_status, 4);  // the partner's half has landed
+    __syncthreads();                                        // ... and this CTA's own half
 }
 
 // ------------------------------------------------------- row-tile kernel
@@ -660,7 +716,9 @@ __global__ void __launch_bounds__(kTThreads, 3) gemv_q4_tile_kernel(const uint4*
                                                                     int pro, int epi, float* __restrict__ y,
                                                                     const TpCtx tp, int x_point, uint64_t y_shared,
                                                                     int y_row_off, int y_point, int res_point) {
-    __shared__ double part[kCl];
+    __shared__ PairX px;
+    const bool rms = pro == (int)Q4Pro::RmsNorm;
+    pair_setup(px, nb, rms);
     const TileSmem sm = tile_smem(nb);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int tiles = (rows + kTR - 1) / kTR, nchunk = (nb + kTC - 1) / kTC;
@@ -681,16 +739,14 @@ __global__ void __launch_bounds__(kTThreads, 3) gemv_q4_tile_kernel(const uint4*
             cp_async_commit();
         }
     }
-    const bool rms = pro == (int)Q4Pro::RmsNorm;
     NormPre np;
     norm_preload_slice(np, norm_w, rms, nb);
-    cg::this_cluster().sync();  // every CTA of the cluster runs before any writes into its shared memory
     pdl_wait();
     const Act a{sm.lo, sm.hi, sm.dc, nullptr};
     if constexpr (LL)
         prologue_cluster(XLL{tp, static_cast<const uint2*>(x), tp_uepoch(tp, x_point), 100 + x_point}, np, norm_w,
-                         eps, rms, nb, a, part);
-    else prologue_cluster(XFloat{static_cast<const float4*>(x)}, np, norm_w, eps, rms, nb, a, part);
+                         eps, rms, nb, a, px);
+    else prologue_cluster(XFloat{static_cast<const float4*>(x)}, np, norm_w, eps, rms, nb, a, px);
 
     if (warp < kTComp) {
         // compute warps: lane & 15 = row, warp and lane >> 4 pick 2 blocks

@@ -623,7 +623,7 @@ def main_llama7b(args, world, rank, local):
         # the dominant decode kernel, one launch of its q|k|v shape: live
         # algorithmic bytes / live time; traffic = ncu DRAM bytes of the same launch
         "roofline": {"bound": "hbm",
-                     "kernel": f"mvb::gemv_q4_kernel (Q4_0 x Q8 decode GEMV), q|k|v {qkv['rows']}x{qkv['cols']} "
+                     "kernel": f"mvb::gemv_q4_tile_kernel (Q4_0 x Q8 decode GEMV), q|k|v {qkv['rows']}x{qkv['cols']} "
                                f"launch (one rank's share)",
                      "achieved": qkv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(qkv["gbs"] / peaks["hbm_gbs"], 4),

@@ -341,11 +341,18 @@ __global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
 struct FusedSmem {
     uint64_t q, table, sc, knew, vnew, kring, vring, total;
 };
-// V ring depth: 8 tiles (256 tokens, all of a typical context in flight
-// before the PDL wait) where a token's head slice is at most 256 bytes, 4
-// otherwise (shared memory).
+// Sizes of the decode kernel's K and V staging.  The kernel follows the
+// q|k|v GEMV, whose CTAs fill the SMs: the GEMV leaves one CTA slot free on
+// some SMs (GemvQ4Args::reserve) and the attention is kept small enough to
+// start there early (K tiles of 64 tokens, a 5-tile V ring: ~78 KB for hd 128
+// F16) and issue its cached K/V loads while the GEMV still runs -- measured
+// faster than a deeper ring that has to wait for two GEMV CTAs to leave.
+__host__ __device__ inline int fused_ktile(uint64_t hd, int kv_type) {
+    const int kt = attn_ktile(hd, kv_type);
+    return kt < 64 ? kt : 64;
+}
 __host__ __device__ inline int fused_vstages(uint64_t hd, int kv_type) {
-    return hd * (kv_type == 0 ? 4 : 2) <= 256 ? 8 : 4;
+    return hd * (kv_type == 0 ? 4 : 2) <= 256 ? 5 : 4;
 }
 __host__ __device__ inline FusedSmem fused_plan(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type) {
     auto up = [](uint64_t n) { return (n + 15) / 16 * 16; };
@@ -358,7 +365,7 @@ __host__ __device__ inline FusedSmem fused_plan(uint64_t hd, uint64_t max_ctx, u
     p.knew = p.sc + up(max_ctx * 4);
     p.vnew = p.knew + up(hd * esize);
     p.kring = p.vnew + up(hd * esize);
-    p.vring = p.kring + 2 * (uint64_t)attn_ktile(hd, kv_type) * krow;
+    p.vring = p.kring + 2 * (uint64_t)fused_ktile(hd, kv_type) * krow;
     p.total = p.vring + (uint64_t)fused_vstages(hd, kv_type) * kVTile * hd * esize;
     return p;
 }
@@ -398,7 +405,7 @@ __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) 
     auto slot_of = [&](int t) -> size_t { return (size_t)tbl[t / page] * page + t % page; };
 
     const int krow = slice + 16;
-    const int KT = attn_ktile(HD, kvt);
+    const int KT = fused_ktile(HD, kvt);
     const int nkt = (p + KT - 1) / KT;
     auto issue_k = [&](int tile, int buf) {
         const int t = tile * KT + tid;
@@ -575,10 +582,10 @@ cudaError_t attn_decode_fused(const AttnFusedArgs& a, cudaStream_t s) {
         ensure_smem_attr(kernel, 200 * 1024);
         return launch_pdl(kernel, grid, dim3(hd), smem, s, a);
     };
-    const bool tp = a.tp.world > 1, v8 = fused_vstages(a.hd, a.kv_type) == 8;
+    const bool tp = a.tp.world > 1, v5 = fused_vstages(a.hd, a.kv_type) == 5;
 #define MV_FUSED(H)                                                                                  \
-    (tp ? (v8 ? go(attn_decode_fused_kernel<H, true, 8>, H) : go(attn_decode_fused_kernel<H, true, 4>, H)) \
-        : (v8 ? go(attn_decode_fused_kernel<H, false, 8>, H) : go(attn_decode_fused_kernel<H, false, 4>, H)))
+    (tp ? (v5 ? go(attn_decode_fused_kernel<H, true, 5>, H) : go(attn_decode_fused_kernel<H, true, 4>, H)) \
+        : (v5 ? go(attn_decode_fused_kernel<H, false, 5>, H) : go(attn_decode_fused_kernel<H, false, 4>, H)))
     switch (a.hd) {
         case 64: return MV_FUSED(64);
         case 128: return MV_FUSED(128);

@@ -892,7 +892,9 @@ cudaError_t launch_tile(const GemvQ4Args& g, cudaStream_t s) {
         }
     }
     const uint64_t tiles = (w.rows + kTR - 1) / kTR;
-    const uint64_t cap = (uint64_t)clusters * kCl;
+    uint64_t cap = (uint64_t)clusters * kCl;
+    const uint64_t keep = ((uint64_t)g.reserve + kCl - 1) / kCl * kCl;
+    if (keep && cap > 2 * keep) cap -= keep;
     const uint64_t grid = ((tiles < cap ? tiles : cap) + kCl - 1) / kCl * kCl;
     const void* x = LL ? g.x_ll : static_cast<const void*>(g.x);
     return launch_pdl_cluster(gemv_q4_tile_kernel<LL>, dim3((unsigned)grid), dim3(kTThreads), smem, s, kCl,

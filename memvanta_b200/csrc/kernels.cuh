@@ -60,6 +60,9 @@ struct GemvQ4Args {
     int y_row_off = 0;
     int y_point = 0;
     int res_point = 0;
+    // CTA slots the launch leaves free for the kernel after it (the decode
+    // attention after the q|k|v GEMV starts on them while this one runs)
+    int reserve = 0;
 };
 cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s);
 cudaError_t q4_block_dots(const mv_weight_s& w, const float* x, int32_t* isum, cudaStream_t s);

@@ -500,10 +500,12 @@ void ensure_prefill(mv_model_s* m, uint64_t B) {
 
 // x_out = W x_in for one weight of any type, with the decode path's fused
 // prologue/epilogue where the weight is Q4_0.
-void project_decode(mv_model_s* m, mv_weight_s* w, const float* x, const float* norm_w, float* y, mvb::Q4Epi epi) {
+void project_decode(mv_model_s* m, mv_weight_s* w, const float* x, const float* norm_w, float* y, mvb::Q4Epi epi,
+                    int reserve = 0) {
     cudaStream_t s = m->stream;
     if (w->type == 2) {
         mvb::GemvQ4Args a{w, x, norm_w, m->eps, y, norm_w ? mvb::Q4Pro::RmsNorm : mvb::Q4Pro::Plain, epi};
+        a.reserve = reserve;
         ck(mvb::gemv_q4(a, s), "gemv_q4");
         return;
     }
@@ -567,7 +569,7 @@ int points_per_step(const mv_model_s* m) { return (int)(4 * m->n_layer + 2); }
 // stores this rank's rows at `row_off` of every rank's LL output `y_off`
 // (point y_point), otherwise y is a local float output.
 void gemv_tp(mv_model_s* m, mv_weight_s* w, uint64_t x_off, int x_point, const float* norm_w, mvb::Q4Epi epi,
-             float* y, uint64_t y_off, uint64_t row_off, int y_point, int res_point = 0) {
+             float* y, uint64_t y_off, uint64_t row_off, int y_point, int res_point = 0, int reserve = 0) {
     mvb::GemvQ4Args a{w, nullptr, norm_w, m->eps, y, norm_w ? mvb::Q4Pro::RmsNorm : mvb::Q4Pro::Plain, epi};
     a.tp = &m->tp;
     a.x_ll = m->tp_block + x_off;
@@ -576,6 +578,7 @@ void gemv_tp(mv_model_s* m, mv_weight_s* w, uint64_t x_off, int x_point, const f
     a.y_row_off = (int)row_off;
     a.y_point = y_point;
     a.res_point = res_point;
+    a.reserve = reserve;
     ck(mvb::gemv_q4(a, m->stream), "gemv_q4 (tensor parallel)");
 }
 
@@ -590,9 +593,11 @@ void launch_decode(mv_model_s* m, bool with_logits) {
     const bool fused = m->kv_type == MV_KV_F32 || m->kv_type == MV_KV_F16;
     for (uint64_t l = 0; l < m->n_layer; ++l) {
         auto& L = m->layers[l];
+        // the q|k|v GEMV leaves two CTA slots per attention CTA free (fused path)
+        const int reserve = fused ? (int)(2 * m->nh) : 0;
         if (tp) gemv_tp(m, L.qkv, m->off_x, l ? pt_down(l - 1) : pt_embed(m), L.attn_norm, mvb::Q4Epi::Store, m->qkv,
-                        0, 0, 0);
-        else project_decode(m, L.qkv, m->x, L.attn_norm, m->qkv, mvb::Q4Epi::Store);
+                        0, 0, 0, 0, reserve);
+        else project_decode(m, L.qkv, m->x, L.attn_norm, m->qkv, mvb::Q4Epi::Store, reserve);
         if (fused) {
             mvb::AttnFusedArgs fa{m->kv_type, m->qkv, m->nh, m->nkv, m->hd,
                                   (const float*)m->rope_cos, (const float*)m->rope_sin, m->pos_dev,

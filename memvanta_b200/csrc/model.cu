@@ -359,18 +359,81 @@ T* dalloc(mv_model_s* m, uint64_t count) {
     return static_cast<T*>(p);
 }
 
-mv_weight_s* upload_raw(mv_model_s* m, const uint8_t* raw, uint64_t nbytes, int type, uint64_t rows,
-                             uint64_t cols) {
-    mv_weight_t w = nullptr;
-    if (int rc = mv_weight_upload(raw, nbytes, type, rows, cols, m->stream, &w))
-        throw ModelError(rc, std::string("weight upload: ") + mv_last_error());
-    m->owned.push_back(w);
-    return w;
-}
+// One contiguous run of a tensor's raw GGML bytes, in upload order.
+struct Seg {
+    const uint8_t* src;
+    uint64_t n;
+};
 
-mv_weight_s* upload_tensor(mv_model_s* m, const mvb::GgufReader& f, const mvb::GgufTensorInfo& t) {
+// GGUF -> HBM upload pipeline.  A tensor's raw blocks go from the mapped file
+// through two pinned chunks -- the CPU gathers the next chunk (page-faulting
+// the file in, interleaving gate/up rows, slicing a rank's share) while the
+// copy engine sends the previous one -- into a device staging buffer, and
+// the repack kernel turns them into the planar layout the kernels read
+// (mv_weight_from_device).  The staging buffer is reused for every tensor
+// and freed with the uploader.
+struct Uploader {
+    static constexpr uint64_t kChunk = 8ull << 20;
+    cudaStream_t s;
+    uint8_t* pin[2] = {nullptr, nullptr};
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    int cur = 0;
+    uint8_t* dstage = nullptr;
+    uint64_t dcap = 0;
+
+    explicit Uploader(cudaStream_t st) : s(st) {
+        for (int k = 0; k < 2; ++k) {
+            ck(cudaMallocHost(reinterpret_cast<void**>(&pin[k]), kChunk), "cudaMallocHost(upload)");
+            ck(cudaEventCreateWithFlags(&ev[k], cudaEventDisableTiming), "cudaEventCreate(upload)");
+        }
+    }
+    ~Uploader() {
+        cudaStreamSynchronize(s);
+        for (int k = 0; k < 2; ++k) {
+            if (pin[k]) cudaFreeHost(pin[k]);
+            if (ev[k]) cudaEventDestroy(ev[k]);
+        }
+        if (dstage) cudaFree(dstage);
+    }
+
+    mv_weight_s* upload(mv_model_s* m, const std::vector<Seg>& segs, int type, uint64_t rows, uint64_t cols) {
+        uint64_t total = 0;
+        for (const Seg& g : segs) total += g.n;
+        if (total > dcap) {
+            ck(cudaStreamSynchronize(s), "sync(upload)");
+            if (dstage) cudaFree(dstage);
+            dstage = nullptr;
+            ck(cudaMalloc(reinterpret_cast<void**>(&dstage), total), "cudaMalloc(upload staging)");
+            dcap = total;
+        }
+        size_t si = 0;
+        uint64_t so = 0;
+        for (uint64_t off = 0; off < total;) {
+            const uint64_t c = std::min(kChunk, total - off);
+            ck(cudaEventSynchronize(ev[cur]), "upload chunk free");  // its previous copy has finished
+            for (uint64_t filled = 0; filled < c;) {
+                const uint64_t take = std::min(c - filled, segs[si].n - so);
+                std::memcpy(pin[cur] + filled, segs[si].src + so, take);
+                filled += take;
+                so += take;
+                if (so == segs[si].n) ++si, so = 0;
+            }
+            ck(cudaMemcpyAsync(dstage + off, pin[cur], c, cudaMemcpyHostToDevice, s), "upload copy");
+            ck(cudaEventRecord(ev[cur], s), "upload event");
+            cur ^= 1;
+            off += c;
+        }
+        mv_weight_t w = nullptr;
+        if (int rc = mv_weight_from_device(dstage, total, type, rows, cols, s, &w))  // repack, then sync
+            throw ModelError(rc, std::string("weight upload: ") + mv_last_error());
+        m->owned.push_back(w);
+        return w;
+    }
+};
+
+mv_weight_s* upload_tensor(mv_model_s* m, Uploader& up, const mvb::GgufReader& f, const mvb::GgufTensorInfo& t) {
     if (t.dims.size() < 2) throw ModelError(MV_ERR_INVALID, "matrix tensor needs rank 2: " + t.name);
-    return upload_raw(m, f.data(t), t.nbytes, (int)t.type, t.ne(1), t.ne(0));
+    return up.upload(m, {{f.data(t), t.nbytes}}, (int)t.type, t.ne(1), t.ne(0));
 }
 
 float* upload_vector(mv_model_s* m, const mvb::GgufReader& f, const mvb::GgufTensorInfo& t, uint64_t n) {
@@ -403,7 +466,7 @@ struct RowRange {
     uint64_t r0, n;
 };
 
-mv_weight_s* upload_rows(mv_model_s* m, const mvb::GgufReader& f, const std::vector<RowRange>& parts,
+mv_weight_s* upload_rows(mv_model_s* m, Uploader& up, const mvb::GgufReader& f, const std::vector<RowRange>& parts,
                          bool interleave) {
     const uint32_t type = parts[0].t->type;
     const uint64_t cols = parts[0].t->ne(0);
@@ -413,29 +476,26 @@ mv_weight_s* upload_rows(mv_model_s* m, const mvb::GgufReader& f, const std::vec
     const uint64_t row_bytes = parts[0].t->nbytes / parts[0].t->ne(1);
     uint64_t rows = 0;
     for (auto& pr : parts) rows += pr.n;
-    std::vector<uint8_t> buf(rows * row_bytes);
+    std::vector<Seg> segs;
     if (interleave) {  // gate/up: row 2i = gate_i, row 2i+1 = up_i
         if (parts.size() != 2 || parts[0].n != parts[1].n)
             throw ModelError(MV_ERR_INVALID, "gate/up shapes differ: " + parts[0].t->name);
         const uint8_t* g = f.data(*parts[0].t) + parts[0].r0 * row_bytes;
         const uint8_t* u = f.data(*parts[1].t) + parts[1].r0 * row_bytes;
+        segs.reserve(2 * parts[0].n);
         for (uint64_t i = 0; i < parts[0].n; ++i) {
-            std::memcpy(buf.data() + (2 * i) * row_bytes, g + i * row_bytes, row_bytes);
-            std::memcpy(buf.data() + (2 * i + 1) * row_bytes, u + i * row_bytes, row_bytes);
+            segs.push_back({g + i * row_bytes, row_bytes});
+            segs.push_back({u + i * row_bytes, row_bytes});
         }
     } else {
-        uint64_t off = 0;
-        for (auto& pr : parts) {
-            std::memcpy(buf.data() + off, f.data(*pr.t) + pr.r0 * row_bytes, pr.n * row_bytes);
-            off += pr.n * row_bytes;
-        }
+        for (auto& pr : parts) segs.push_back({f.data(*pr.t) + pr.r0 * row_bytes, pr.n * row_bytes});
     }
-    return upload_raw(m, buf.data(), buf.size(), (int)type, rows, cols);
+    return up.upload(m, segs, (int)type, rows, cols);
 }
 
 // Concatenates whole rows of same-typed, same-width tensors (raw GGML bytes).
-mv_weight_s* upload_concat(mv_model_s* m, const mvb::GgufReader& f,
-                                const std::vector<const mvb::GgufTensorInfo*>& ts, bool interleave) {
+mv_weight_s* upload_concat(mv_model_s* m, Uploader& up, const mvb::GgufReader& f,
+                           const std::vector<const mvb::GgufTensorInfo*>& ts, bool interleave) {
     const uint32_t type = ts[0]->type;
     const uint64_t cols = ts[0]->ne(0);
     for (auto* t : ts)
@@ -444,24 +504,21 @@ mv_weight_s* upload_concat(mv_model_s* m, const mvb::GgufReader& f,
     const uint64_t row_bytes = ts[0]->nbytes / ts[0]->ne(1);
     uint64_t rows = 0;
     for (auto* t : ts) rows += t->ne(1);
-    std::vector<uint8_t> buf(rows * row_bytes);
+    std::vector<Seg> segs;
     if (interleave) {  // gate/up: row 2i = gate_i, row 2i+1 = up_i
         if (ts.size() != 2 || ts[0]->ne(1) != ts[1]->ne(1))
             throw ModelError(MV_ERR_INVALID, "gate/up shapes differ: " + ts[0]->name);
         const uint8_t* g = f.data(*ts[0]);
         const uint8_t* u = f.data(*ts[1]);
+        segs.reserve(2 * ts[0]->ne(1));
         for (uint64_t i = 0; i < ts[0]->ne(1); ++i) {
-            std::memcpy(buf.data() + (2 * i) * row_bytes, g + i * row_bytes, row_bytes);
-            std::memcpy(buf.data() + (2 * i + 1) * row_bytes, u + i * row_bytes, row_bytes);
+            segs.push_back({g + i * row_bytes, row_bytes});
+            segs.push_back({u + i * row_bytes, row_bytes});
         }
     } else {
-        uint64_t off = 0;
-        for (auto* t : ts) {
-            std::memcpy(buf.data() + off, f.data(*t), t->nbytes);
-            off += t->nbytes;
-        }
+        for (auto* t : ts) segs.push_back({f.data(*t), t->nbytes});
     }
-    return upload_raw(m, buf.data(), buf.size(), (int)type, rows, cols);
+    return up.upload(m, segs, (int)type, rows, cols);
 }
 
 void ensure_prefill(mv_model_s* m, uint64_t B) {
@@ -768,13 +825,14 @@ void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, in
     m->Fl = m->n_ff / world;
     m->Vl = m->vocab / world;
     f.advise_sequential();
+    Uploader up(m->stream);
 
-    m->tok_embd = upload_tensor(m, f, te);
+    m->tok_embd = upload_tensor(m, up, f, te);
     const auto& on = f.tensor("output_norm.weight");
     m->output_norm = upload_vector(m, f, on, m->n_embd);
     const mvb::GgufTensorInfo* out = f.find("output.weight");
-    if (world == 1) m->output = out ? upload_tensor(m, f, *out) : m->tok_embd;  // tied output (:226)
-    else m->output = upload_rows(m, f, {{out ? out : &te, rank * m->Vl, m->Vl}}, false);
+    if (world == 1) m->output = out ? upload_tensor(m, up, f, *out) : m->tok_embd;  // tied output (:226)
+    else m->output = upload_rows(m, up, f, {{out ? out : &te, rank * m->Vl, m->Vl}}, false);
 
     const uint64_t rows = m->n_pages * m->page;
     const uint64_t rb = mvb::kv_row_bytes(kv_type, m->kvd), ns = mvb::kv_row_scales(kv_type, m->kvd);
@@ -789,16 +847,16 @@ void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, in
         const auto &to = f.tensor(name(".attn_output.weight")), &tg = f.tensor(name(".ffn_gate.weight")),
                    &tu = f.tensor(name(".ffn_up.weight")), &td = f.tensor(name(".ffn_down.weight"));
         if (world == 1) {
-            L.qkv = upload_concat(m, f, {&tq, &tk, &tv}, false);
-            L.o = upload_tensor(m, f, to);
-            L.gu = upload_concat(m, f, {&tg, &tu}, true);
-            L.down = upload_tensor(m, f, td);
+            L.qkv = upload_concat(m, up, f, {&tq, &tk, &tv}, false);
+            L.o = upload_tensor(m, up, f, to);
+            L.gu = upload_concat(m, up, f, {&tg, &tu}, true);
+            L.down = upload_tensor(m, up, f, td);
         } else {
             const uint64_t q0 = rank * m->nh * m->hd, k0 = rank * m->kvd;
-            L.qkv = upload_rows(m, f, {{&tq, q0, m->nh * m->hd}, {&tk, k0, m->kvd}, {&tv, k0, m->kvd}}, false);
-            L.o = upload_rows(m, f, {{&to, rank * m->Dl, m->Dl}}, false);
-            L.gu = upload_rows(m, f, {{&tg, rank * m->Fl, m->Fl}, {&tu, rank * m->Fl, m->Fl}}, true);
-            L.down = upload_rows(m, f, {{&td, rank * m->Dl, m->Dl}}, false);
+            L.qkv = upload_rows(m, up, f, {{&tq, q0, m->nh * m->hd}, {&tk, k0, m->kvd}, {&tv, k0, m->kvd}}, false);
+            L.o = upload_rows(m, up, f, {{&to, rank * m->Dl, m->Dl}}, false);
+            L.gu = upload_rows(m, up, f, {{&tg, rank * m->Fl, m->Fl}, {&tu, rank * m->Fl, m->Fl}}, true);
+            L.down = upload_rows(m, up, f, {{&td, rank * m->Dl, m->Dl}}, false);
             if (L.qkv->type != 2 || L.o->type != 2 || L.gu->type != 2 || L.down->type != 2)
                 throw ModelError(MV_ERR_UNSUPPORTED, "tensor parallelism needs Q4_0 layer weights");
         }

@@ -198,6 +198,32 @@ MV_API int mv_tensor_matmul_batch_host(mv_weight_t w, const float* x_host, float
 /* tensor_read_row_f32 with a host output.  src/gguf_kernels.cpp:226. */
 MV_API int mv_tensor_read_row_host(mv_weight_t w, uint64_t row, float* out_host);
 
+/* ------------------------------------------------ internal block formats */
+
+/* Device twins of the reference's internal-format kernels (the non-GGUF blocks
+ * of include/memvanta/quant.hpp:8-13: BlockQ8_0 = 36 bytes {float d; int8
+ * qs[32]}, BlockQ4_0 = 20 bytes {float d; uint8 qs[16]} with interleaved
+ * nibbles), read in place from device memory with the reference's rounding
+ * order (bit-identical outputs).  All pointers are device pointers, 4-byte
+ * aligned (fp32 x 16-byte aligned); cols % 32 == 0; asynchronous on `stream`. */
+/* quantize_q8_0 / quantize_q4_0, src/quant.cpp:44-85 (n % 32 == 0). */
+MV_API int mv_int_quantize_q8_0(const float* x_dev, uint64_t n, void* out36_dev, void* stream);
+MV_API int mv_int_quantize_q4_0(const float* x_dev, uint64_t n, void* out20_dev, void* stream);
+/* matvec_q4_q8 (src/quant_kernels.cpp:68-80): y = A20 . x36. */
+MV_API int mv_int_matvec_q4_q8(const void* A20_dev, const void* x36_dev, float* y_dev, uint64_t rows, uint64_t cols,
+                               void* stream);
+/* matvec_q4_0 / matvec_q8_0 against fp32 x (src/quant.cpp:158-174). */
+MV_API int mv_int_matvec_q4_0(const void* A20_dev, const float* x_dev, float* y_dev, uint64_t rows, uint64_t cols,
+                              void* stream);
+MV_API int mv_int_matvec_q8_0(const void* A36_dev, const float* x_dev, float* y_dev, uint64_t rows, uint64_t cols,
+                              void* stream);
+/* matmul_q4_0_batch (src/quant_kernels.cpp:82-91): y[b*rows + r]. */
+MV_API int mv_int_matmul_q4_0_batch(const void* A20_dev, const float* x_dev, float* y_dev, uint64_t rows,
+                                    uint64_t cols, uint64_t batch, void* stream);
+/* matvec_f32, the sequential fp32 row dot of src/matmul.cpp:6-8 (row-major A). */
+MV_API int mv_matvec_f32(const float* A_dev, const float* x_dev, float* y_dev, uint64_t rows, uint64_t cols,
+                         void* stream);
+
 /* ------------------------------------------------------------- model */
 
 /* Device-resident LlamaModel backend: parses the GGUF (mmap), uploads every

@@ -158,6 +158,62 @@ def quantize_q8(x, stream=None):
     return q, d
 
 
+# ---- internal (non-GGUF) block formats: device twins of quant.hpp / matmul.hpp
+# Tensors are torch CUDA tensors; blocks are uint8 tensors of 20 (Q4_0) or 36
+# (Q8_0) bytes per 32 elements.
+
+def int_quantize_q8_0(x, stream=None):
+    """quantize_q8_0 (src/quant.cpp:44-62) -> uint8[n/32*36]."""
+    import torch
+    out = torch.empty(x.numel() // 32 * 36, dtype=torch.uint8, device=x.device)
+    check(load().mv_int_quantize_q8_0(_t_ptr(x), x.numel(), _t_ptr(out), _stream(stream)))
+    return out
+
+
+def int_quantize_q4_0(x, stream=None):
+    """quantize_q4_0 (src/quant.cpp:64-85) -> uint8[n/32*20]."""
+    import torch
+    out = torch.empty(x.numel() // 32 * 20, dtype=torch.uint8, device=x.device)
+    check(load().mv_int_quantize_q4_0(_t_ptr(x), x.numel(), _t_ptr(out), _stream(stream)))
+    return out
+
+
+def int_matvec_q4_q8(A20, x36, rows: int, cols: int, stream=None):
+    import torch
+    y = torch.empty(rows, dtype=torch.float32, device=A20.device)
+    check(load().mv_int_matvec_q4_q8(_t_ptr(A20), _t_ptr(x36), _t_ptr(y), rows, cols, _stream(stream)))
+    return y
+
+
+def int_matvec_q4_0(A20, x, rows: int, cols: int, stream=None):
+    import torch
+    y = torch.empty(rows, dtype=torch.float32, device=A20.device)
+    check(load().mv_int_matvec_q4_0(_t_ptr(A20), _t_ptr(x), _t_ptr(y), rows, cols, _stream(stream)))
+    return y
+
+
+def int_matvec_q8_0(A36, x, rows: int, cols: int, stream=None):
+    import torch
+    y = torch.empty(rows, dtype=torch.float32, device=A36.device)
+    check(load().mv_int_matvec_q8_0(_t_ptr(A36), _t_ptr(x), _t_ptr(y), rows, cols, _stream(stream)))
+    return y
+
+
+def int_matmul_q4_0_batch(A20, x, rows: int, cols: int, batch: int, stream=None):
+    import torch
+    y = torch.empty((batch, rows), dtype=torch.float32, device=A20.device)
+    check(load().mv_int_matmul_q4_0_batch(_t_ptr(A20), _t_ptr(x), _t_ptr(y), rows, cols, batch, _stream(stream)))
+    return y
+
+
+def matvec_f32(A, x, stream=None):
+    import torch
+    rows, cols = A.shape
+    y = torch.empty(rows, dtype=torch.float32, device=A.device)
+    check(load().mv_matvec_f32(_t_ptr(A), _t_ptr(x), _t_ptr(y), rows, cols, _stream(stream)))
+    return y
+
+
 def q4_0_block_dots(w: Weight, x, stream=None):
     import torch
     isum = torch.empty((w.rows, w.cols // 32), dtype=torch.int32, device=x.device)

@@ -66,6 +66,13 @@ SIGNATURES = {
     "mv_model_prefill": (_i, [_p, _p, _u64, _u64, _i, _p]),
     "mv_model_generate_greedy": (_i, [_p, C.c_int32, _u64, _p]),
     "mv_model_stream": (_p, [_p]),
+    "mv_int_quantize_q8_0": (_i, [_p, _u64, _p, _p]),
+    "mv_int_quantize_q4_0": (_i, [_p, _u64, _p, _p]),
+    "mv_int_matvec_q4_q8": (_i, [_p, _p, _p, _u64, _u64, _p]),
+    "mv_int_matvec_q4_0": (_i, [_p, _p, _p, _u64, _u64, _p]),
+    "mv_int_matvec_q8_0": (_i, [_p, _p, _p, _u64, _u64, _p]),
+    "mv_int_matmul_q4_0_batch": (_i, [_p, _p, _p, _u64, _u64, _u64, _p]),
+    "mv_matvec_f32": (_i, [_p, _p, _p, _u64, _u64, _p]),
     "mv_model_open_tp": (_i, [C.c_char_p, _u64, _u64, _i, _i, _i, _u64, C.POINTER(_p)]),
     "mv_model_tp_handle": (_i, [_p, _p]),
     "mv_model_tp_connect": (_i, [_p, _p]),

@@ -436,18 +436,20 @@ def main():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="llama7b", choices=["llama7b", "q4_gemv", "gemv", "gemm", "decode"],
+    ap.add_argument("--workload", default="llama7b",
+                    choices=["llama7b", "q4_gemv", "gemv", "gemm", "decode", "paged_attn"],
                     help="llama7b: the headline (config 3); q4_gemv: config 0; gemv / gemm / decode: one kernel "
                          "or the 7B decode steps alone, for profiling")
     ap.add_argument("--rows", type=int, default=12288, help="gemv/gemm: weight rows")
     ap.add_argument("--cols", type=int, default=4096, help="gemv/gemm: weight cols (K)")
     ap.add_argument("--batch", type=int, default=32, help="gemm: tokens")
+    ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"], help="paged_attn: cache type")
     ap.add_argument("--clock-window", type=float, default=0.5)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup()
-    if args.workload in ("gemv", "gemm", "decode"):
+    if args.workload in ("gemv", "gemm", "decode", "paged_attn"):
         return main_micro(args)
     if args.workload == "llama7b":
         return main_llama7b(args, world, rank, local)
@@ -530,6 +532,8 @@ def main_micro(args):
         print(json.dumps({"workload": "decode", "metric": "7B Q4_0 decode tok/s", "value": round(1e3 / ms_step, 2),
                           "unit": "tok/s", "ms_per_step": round(ms_step, 4), "steps": args.steps}), flush=True)
         return
+    if args.workload == "paged_attn":
+        return main_paged_attn(args, mv, dev)
     rows, cols, B = args.rows, args.cols, args.batch
     rng = np.random.default_rng(7)
     wbytes = rows * cols // 32 * 18
@@ -569,6 +573,69 @@ def main_micro(args):
         line.update({"batch": B, "metric": "Q4_0 x Q8 GEMM TOPS (2*rows*cols*batch / time, quantisation included)",
                      "value": round(2 * rows * cols * B / us / 1e6, 2), "unit": "TOPS"})
     print(json.dumps(line), flush=True)
+
+
+def main_paged_attn(args, mv, dev):
+    """Config 4: paged decode attention over 64 sequences, ctx ~ U(64..768),
+    16-token pages scattered by a random permutation block table, 32 heads x
+    128, Q/K/V ~ N(0,1) (random fp16 pages; Q8_0 pages with random int8 and
+    scales for --kv q8_0).  The cache (~436 MB F16) is larger than L2, so every
+    launch reads it from HBM.  One launch per step, replayed from a graph."""
+    import torch
+    kv_type = {"f16": mv.KV_F16, "q8_0": mv.KV_Q8_0}[args.kv]
+    rng = np.random.default_rng(4)
+    n_seq, n_head, hd, page = 64, 32, 128, 16
+    kv_dim = n_head * hd
+    ctx = rng.integers(64, 769, n_seq).astype(np.int32)
+    max_pages = int((ctx.max() + page - 1) // page)
+    npg = (ctx + page - 1) // page
+    total = int(npg.sum())
+    perm = rng.permutation(total).astype(np.int32)
+    table = np.zeros((n_seq, max_pages), np.int32)
+    o = 0
+    for s_ in range(n_seq):
+        table[s_, :npg[s_]] = perm[o:o + npg[s_]]
+        o += npg[s_]
+    slots = total * page
+    g = torch.Generator(device=dev).manual_seed(4)
+    if kv_type == mv.KV_F16:
+        kp = torch.randn((slots, kv_dim), generator=g, device=dev).half().view(torch.uint8)
+        vp = torch.randn((slots, kv_dim), generator=g, device=dev).half().view(torch.uint8)
+        ks = vs = None
+    else:
+        kp = torch.randint(-127, 128, (slots, kv_dim), generator=g, device=dev, dtype=torch.int8).view(torch.uint8)
+        vp = torch.randint(-127, 128, (slots, kv_dim), generator=g, device=dev, dtype=torch.int8).view(torch.uint8)
+        ks = torch.rand((slots, kv_dim // 32), generator=g, device=dev) * 0.02
+        vs = torch.rand((slots, kv_dim // 32), generator=g, device=dev) * 0.02
+    q = torch.randn((n_seq, kv_dim), generator=g, device=dev)
+    tab, ctx_t = torch.from_numpy(table).to(dev), torch.from_numpy(ctx).to(dev)
+    out = torch.empty((n_seq, kv_dim), device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    call = lambda: mv.paged_attn_decode(kv_type, q, n_head, n_head, hd, kp, vp, tab, max_pages, page, ctx_t,  # noqa: E731
+                                        int(ctx.max()), ks, vs, out, stream)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 1)):
+            call()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for _ in range(args.steps):
+                call()
+        gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        gr.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    row_bytes = mv.kv_row_bytes(kv_type, kv_dim) + 4 * mv.kv_row_scales(kv_type, kv_dim)
+    alg = int(ctx.sum()) * 2 * row_bytes + 2 * n_seq * kv_dim * 4  # K and V of every context token, Q in, O out
+    print(json.dumps({"workload": "paged_attn", "kv": args.kv, "config": "config4: 64 seqs, ctx U(64..768), 16-token "
+                      "pages, random permutation block table, 32 heads x 128", "sum_ctx": int(ctx.sum()),
+                      "us_per_launch": round(us, 2), "metric": "paged attention achieved GB/s",
+                      "value": round(alg / us / 1e3, 1), "unit": "GB/s", "algorithmic_bytes_per_launch": alg,
+                      "frac_of_measured_hbm": round(alg / us / 1e3 / measured_peaks()["hbm_gbs"], 3)}), flush=True)
 
 
 def main_llama7b(args, world, rank, local):

@@ -437,9 +437,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="llama7b",
-                    choices=["llama7b", "q4_gemv", "gemv", "gemm", "decode", "paged_attn"],
-                    help="llama7b: the headline (config 3); q4_gemv: config 0; gemv / gemm / decode: one kernel "
-                         "or the 7B decode steps alone, for profiling")
+                    choices=["llama7b", "q4_gemv", "gemv", "gemm", "decode", "prefill", "paged_attn"],
+                    help="llama7b: the headline (config 3); q4_gemv: config 0; gemv / gemm / decode / prefill: "
+                         "one kernel, or the 7B decode steps or pp512 prefill alone, for profiling")
     ap.add_argument("--rows", type=int, default=12288, help="gemv/gemm: weight rows")
     ap.add_argument("--cols", type=int, default=4096, help="gemv/gemm: weight cols (K)")
     ap.add_argument("--batch", type=int, default=32, help="gemm: tokens")
@@ -449,7 +449,7 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup()
-    if args.workload in ("gemv", "gemm", "decode", "paged_attn"):
+    if args.workload in ("gemv", "gemm", "decode", "prefill", "paged_attn"):
         return main_micro(args)
     if args.workload == "llama7b":
         return main_llama7b(args, world, rank, local)
@@ -531,6 +531,28 @@ def main_micro(args):
         m.close()
         print(json.dumps({"workload": "decode", "metric": "7B Q4_0 decode tok/s", "value": round(1e3 / ms_step, 2),
                           "unit": "tok/s", "ms_per_step": round(ms_step, 4), "steps": args.steps}), flush=True)
+        return
+    if args.workload == "prefill":
+        # pp512 alone: `steps` prefills of the 512-token prompt in batches of
+        # 32 after one warm-up prefill of the first batch
+        m = mv.LlamaModel(ensure_llama7b(), ctx_override=L7_CTX, kv_page_tokens=16, kv_type=mv.KV_F16)
+        ms = torch.cuda.ExternalStream(m.stream)
+        prompt = fixed_tokens(L7_PP)
+        m.prefill(prompt[:L7_BATCH], L7_BATCH, True)
+        total = 0.0
+        for _ in range(args.steps):
+            m.reset()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(ms)
+            m.prefill(prompt, L7_BATCH, True)
+            e1.record(ms)
+            torch.cuda.synchronize()
+            total += e0.elapsed_time(e1)
+        m.close()
+        ms_pp = total / args.steps
+        print(json.dumps({"workload": "prefill", "metric": "7B Q4_0 pp512 tok/s", "value": round(L7_PP / ms_pp * 1e3, 2),
+                          "unit": "tok/s", "ms_per_prefill": round(ms_pp, 3), "steps": args.steps}), flush=True)
         return
     if args.workload == "paged_attn":
         return main_paged_attn(args, mv, dev)

@@ -188,6 +188,19 @@ MV_API int mv_paged_attn_decode(int kv_type, const float* q_dev, uint64_t n_seq,
                          uint64_t max_pages, uint64_t page, const int32_t* ctx_len_dev, uint64_t max_ctx,
                          float* out_dev, void* stream);
 
+/* Attention for n_q query rows of ONE sequence (a prefill chunk): every row
+ * reads the pages of block_table[0 .. max_pages); row i attends to its first
+ * ctx_len[i] tokens (causal: ctx_len[i] = start + i + 1).  Outputs identical
+ * to mv_paged_attn_decode given a block table that repeats that row; groups
+ * of query rows share each staged K/V tile.
+ * Replaces the batched attention loop of LlamaModel::forward_batch_impl
+ * (src/llama_model.cpp:248) over PagedKVCache::dot_key/add_value (:23-55). */
+MV_API int mv_paged_attn_prefill(int kv_type, const float* q_dev, uint64_t n_q, uint64_t n_head, uint64_t n_head_kv,
+                          uint64_t head_dim, const void* k_pages_dev, const void* v_pages_dev,
+                          const float* k_scales_dev, const float* v_scales_dev, const int32_t* block_table_dev,
+                          uint64_t max_pages, uint64_t page, const int32_t* ctx_len_dev, uint64_t max_ctx,
+                          float* out_dev, void* stream);
+
 /* ---------------------------------- host-pointer calls (reference contract) */
 
 /* tensor_matvec with the reference's contract: x and y are HOST pointers,

@@ -27,7 +27,7 @@ from ._lib import (F32, F16, Q4_0, Q8_0, Q6_K, ACT_F32, ACT_Q8, KV_F32, KV_F16, 
 __all__ = [
     "init", "Weight", "tensor_matvec", "tensor_matmul_batch", "tensor_matmul_batch_v06", "tensor_read_row_f32",
     "gemv", "gemm", "quantize_q8", "q4_0_block_dots", "read_rows", "rmsnorm", "rope", "silu_mul", "add_inplace",
-    "fp32_to_fp16", "kv_row_bytes", "kv_row_scales", "kv_append", "paged_attn_decode", "LlamaModel",
+    "fp32_to_fp16", "kv_row_bytes", "kv_row_scales", "kv_append", "paged_attn_decode", "paged_attn_prefill", "LlamaModel",
     "MemVantaError",
 ]
 
@@ -285,6 +285,20 @@ def paged_attn_decode(kv_type, q, n_head, n_head_kv, head_dim, k_pages, v_pages,
     check(load().mv_paged_attn_decode(kv_type, _t_ptr(q), n_seq, n_head, n_head_kv, head_dim, _t_ptr(k_pages),
                                       _t_ptr(v_pages), _t_ptr(k_scales), _t_ptr(v_scales), _t_ptr(block_table),
                                       max_pages, page, _t_ptr(ctx_len), max_ctx, _t_ptr(out), _stream(stream)))
+    return out
+
+
+def paged_attn_prefill(kv_type, q, n_head, n_head_kv, head_dim, k_pages, v_pages, block_table, max_pages, page,
+                       ctx_len, max_ctx, k_scales=None, v_scales=None, out=None, stream=None):
+    """Attention of the query rows of one sequence (a prefill chunk): every
+    row reads block-table row 0; row i sees ctx_len[i] tokens."""
+    import torch
+    n_q = q.shape[0]
+    if out is None:
+        out = torch.empty((n_q, n_head * head_dim), dtype=torch.float32, device=q.device)
+    check(load().mv_paged_attn_prefill(kv_type, _t_ptr(q), n_q, n_head, n_head_kv, head_dim, _t_ptr(k_pages),
+                                       _t_ptr(v_pages), _t_ptr(k_scales), _t_ptr(v_scales), _t_ptr(block_table),
+                                       max_pages, page, _t_ptr(ctx_len), max_ctx, _t_ptr(out), _stream(stream)))
     return out
 
 

@@ -177,7 +177,8 @@ __global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
     pdl_wait();
     const int ctx = a.ctx_len[s];
     const int npg = (ctx + page - 1) / page;
-    for (int i = tid; i < npg; i += HD) tbl[i] = a.block_table[(size_t)s * a.max_pages + i];
+    const size_t trow = a.one_seq ? 0 : (size_t)s;
+    for (int i = tid; i < npg; i += HD) tbl[i] = a.block_table[trow * a.max_pages + i];
     qs[tid] = a.q[(size_t)s * a.q_stride + (size_t)h * HD + tid];
     __syncthreads();
     auto slot_of = [&](int t) -> size_t { return (size_t)tbl[t / page] * page + t % page; };
@@ -319,6 +320,274 @@ __global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
     }
     cp_async_wait<0>();
     a.out[((size_t)s * a.n_head + h) * HD + tid] = out;
+}
+
+// ------------------------------------------ prefill attention (query groups)
+// The prefill form of attn_exact_kernel: QG consecutive query rows of ONE
+// sequence (they share the block-table row of the group's first query) and one
+// query head per CTA, hd threads (with one_seq every row reads block-table
+// row 0).  Every K tile and V tile is staged once and
+// used by all QG queries (a prefill chunk's queries attend to the same cached
+// tokens), and the V loop carries QG independent FMA chains per thread.  Each
+// query keeps attn_exact_kernel's evaluation order exactly -- the same 8-lane
+// dot per token, the same per-thread strided max / double sums combined warp
+// by warp, alpha_t = e_t * float(1/den), the same per-dimension FMA chain over
+// its own tokens in order -- so the outputs are identical to it bit for bit.
+// Query q of the group sees tokens t < ctx_len[s0 + q] (causal prefill).
+struct AttnGroupSmem {
+    uint64_t q, table, sc, vsc, ring, total;
+};
+__host__ __device__ inline AttnGroupSmem attn_group_plan(uint64_t hd, uint64_t max_ctx, uint64_t max_pages,
+                                                         int kv_type, int qg) {
+    auto up = [](uint64_t n) { return (n + 15) / 16 * 16; };
+    const uint64_t esize = kv_type == 0 ? 4 : kv_type == 1 ? 2 : 1;
+    const uint64_t krow = hd * esize + 16;
+    const uint64_t kring = 2 * (uint64_t)attn_ktile(hd, kv_type) * krow;
+    const uint64_t vring = (uint64_t)kVStages * kVTile * hd * esize;
+    const uint64_t nsc = kv_type == 2 ? 1 : kv_type == 3 ? hd / 32 : 0;
+    AttnGroupSmem p;
+    p.q = 0;
+    p.table = up((uint64_t)qg * hd * 4);
+    p.sc = p.table + up(max_pages * 4);
+    p.vsc = p.sc + up((uint64_t)qg * max_ctx * 4);
+    p.ring = p.vsc + up(max_ctx * nsc * 4);
+    p.total = p.ring + (kring > vring ? kring : vring);
+    return p;
+}
+
+template <int HD, int QG>
+__global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ float redf[QG][HD / 32];
+    __shared__ double redd[QG][HD / 32];
+    const int s0 = blockIdx.x * QG, h = blockIdx.y, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int G = (int)(a.n_head / a.n_head_kv), kh = h / G;
+    const int kv_dim = (int)(a.n_head_kv * HD);
+    const int kvt = a.kv_type;
+    const int esize = kvt == 0 ? 4 : kvt == 1 ? 2 : 1;
+    const int page = (int)a.page;
+    const int mctx = (int)a.max_ctx;
+    const AttnGroupSmem P = attn_group_plan(HD, a.max_ctx, a.max_pages, kvt, QG);
+    float* qs = reinterpret_cast<float*>(smem + P.q);  // [QG][HD]
+    int* tbl = reinterpret_cast<int*>(smem + P.table);
+    float* sc = reinterpret_cast<float*>(smem + P.sc);  // [QG][max_ctx]
+    float* vsc = reinterpret_cast<float*>(smem + P.vsc);
+    uint8_t* ring = smem + P.ring;
+    const uint8_t* kp = static_cast<const uint8_t*>(a.k_pages);
+    const uint8_t* vp = static_cast<const uint8_t*>(a.v_pages);
+    const size_t row_bytes = (size_t)kv_dim * esize;
+    const size_t head_off = (size_t)kh * HD * esize;
+    const int slice = HD * esize;
+
+    pdl_trigger();
+    pdl_wait();
+    int cq[QG];
+    int cmax = 0;
+#pragma unroll
+    for (int i = 0; i < QG; ++i) {
+        cq[i] = s0 + i < (int)a.n_seq ? a.ctx_len[s0 + i] : 0;
+        cmax = max(cmax, cq[i]);
+    }
+    const int npg = (cmax + page - 1) / page;
+    const size_t trow = a.one_seq ? 0 : (size_t)s0;
+    for (int i = tid; i < npg; i += HD) tbl[i] = a.block_table[trow * a.max_pages + i];
+#pragma unroll
+    for (int i = 0; i < QG; ++i)
+        qs[i * HD + tid] = cq[i] > 0 ? a.q[(size_t)(s0 + i) * a.q_stride + (size_t)h * HD + tid] : 0.0f;
+    __syncthreads();
+    auto slot_of = [&](int t) -> size_t { return (size_t)tbl[t / page] * page + t % page; };
+
+    // 1. scores: thread t of a K tile owns one token for all QG queries
+    {
+        const int krow = slice + 16;
+        const int KT = attn_ktile(HD, kvt);
+        auto issue_k = [&](int tile, int buf) {
+            const int t = tile * KT + tid;
+            if (tid < KT && t < cmax) {
+                const uint8_t* src = kp + slot_of(t) * row_bytes + head_off;
+                uint8_t* dst = ring + ((size_t)buf * KT + tid) * krow;
+                for (int c = 0; c < slice; c += 16) cp_async16(dst + c, src + c);
+            }
+            cp_async_commit();
+        };
+        const int ntile = (cmax + KT - 1) / KT;
+        issue_k(0, 0);
+        for (int tile = 0; tile < ntile; ++tile) {
+            if (tile + 1 < ntile) issue_k(tile + 1, (tile + 1) & 1);
+            else cp_async_commit();
+            cp_async_wait<1>();
+            const int t = tile * KT + tid;
+            if (tid < KT && t < cmax) {
+                const uint8_t* row = ring + ((size_t)(tile & 1) * KT + tid) * krow;
+                float acc[QG][8];
+#pragma unroll
+                for (int i = 0; i < QG; ++i)
+#pragma unroll
+                    for (int l = 0; l < 8; ++l) acc[i][l] = 0.f;
+                const size_t slot = kvt >= 2 ? slot_of(t) : 0;
+#pragma unroll 2
+                for (int d = 0; d < HD; d += 8) {
+                    float kf[8];
+                    if (kvt == 1) {
+                        const uint4 w = *reinterpret_cast<const uint4*>(row + d * 2);
+                        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                        for (int l = 0; l < 8; ++l)
+                            kf[l] = half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1))));
+                    } else if (kvt == 0) {
+                        const float4 u = *reinterpret_cast<const float4*>(row + d * 4);
+                        const float4 v = *reinterpret_cast<const float4*>(row + d * 4 + 16);
+                        kf[0] = u.x, kf[1] = u.y, kf[2] = u.z, kf[3] = u.w;
+                        kf[4] = v.x, kf[5] = v.y, kf[6] = v.z, kf[7] = v.w;
+                    } else {
+                        const uint2 w = *reinterpret_cast<const uint2*>(row + d);
+                        const float sc8 = kvt == 3 ? a.k_scales[slot * (kv_dim / 32) + (kh * HD + d) / 32] : 1.0f;
+#pragma unroll
+                        for (int l = 0; l < 8; ++l) kf[l] = s8_to_f32(l < 4 ? w.x : w.y, l & 3) * sc8;
+                    }
+#pragma unroll
+                    for (int i = 0; i < QG; ++i) {
+                        const float4 qa = *reinterpret_cast<const float4*>(qs + i * HD + d);
+                        const float4 qb = *reinterpret_cast<const float4*>(qs + i * HD + d + 4);
+                        const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+                        for (int l = 0; l < 8; ++l) acc[i][l] = fmaf(qv[l], kf[l], acc[i][l]);
+                    }
+                }
+                const float ksc = kvt == 2 ? a.k_scales[slot] : 1.0f;
+#pragma unroll
+                for (int i = 0; i < QG; ++i) {
+                    if (t < cq[i]) {
+                        float dot = acc[i][0];
+#pragma unroll
+                        for (int l = 1; l < 8; ++l) dot += acc[i][l];
+                        if (kvt == 2) dot = dot * ksc;
+                        sc[i * mctx + t] = dot / sqrtf((float)HD);
+                    }
+                }
+            }
+        }
+        cp_async_wait<0>();
+    }
+    if (kvt == 2) {
+        for (int t = tid; t < cmax; t += HD) vsc[t] = a.v_scales[slot_of(t)];
+    } else if (kvt == 3) {
+        for (int i = tid; i < cmax * (HD / 32); i += HD) {
+            const int t = i / (HD / 32), b = i % (HD / 32);
+            vsc[i] = a.v_scales[slot_of(t) * (kv_dim / 32) + kh * (HD / 32) + b];
+        }
+    }
+    __syncthreads();  // every K tile is consumed: the ring is free for V
+
+    // 2. per query: max, exp, double denominator, alpha_t = e_t * float(1/den)
+    float m[QG];
+#pragma unroll
+    for (int i = 0; i < QG; ++i) {
+        float v = -INFINITY;
+        for (int t = tid; t < cq[i]; t += HD) v = fmaxf(v, sc[i * mctx + t]);
+        v = warp_max(v);
+        if (lane == 0) redf[i][warp] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < QG; ++i) {
+        m[i] = redf[i][0];
+#pragma unroll
+        for (int w = 1; w < HD / 32; ++w) m[i] = fmaxf(m[i], redf[i][w]);
+        double den = 0.0;
+        for (int t = tid; t < cq[i]; t += HD) {
+            const float e = expf_cr(sc[i * mctx + t] - m[i]);
+            sc[i * mctx + t] = e;
+            den += (double)e;
+        }
+        den = warp_sum_d(den);
+        if (lane == 0) redd[i][warp] = den;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < QG; ++i) {
+        double den = 0.0;
+#pragma unroll
+        for (int w = 0; w < HD / 32; ++w) den += redd[i][w];
+        const float inv = (float)(1.0 / den);
+        for (int t = tid; t < cq[i]; t += HD) sc[i * mctx + t] = sc[i * mctx + t] * inv;
+    }
+
+    // 3. thread d: out_q,d = fma(alpha_q,t, v_t[d], out_q,d) over t < ctx_q in order
+    const int chunks = kVTile * slice / 16;
+    const int ntile = (cmax + kVTile - 1) / kVTile;
+    auto issue_v = [&](int tile) {
+        if (tile < ntile) {
+            uint8_t* dst = ring + (size_t)(tile % kVStages) * kVTile * slice;
+            for (int c = tid; c < chunks; c += HD) {
+                const int tt = c / (slice / 16), off = (c % (slice / 16)) * 16;
+                const int t = tile * kVTile + tt;
+                if (t < cmax) cp_async16(dst + tt * slice + off, vp + slot_of(t) * row_bytes + head_off + off);
+            }
+        }
+        cp_async_commit();
+    };
+    for (int k = 0; k < kVStages - 1; ++k) issue_v(k);
+    float out[QG];
+#pragma unroll
+    for (int i = 0; i < QG; ++i) out[i] = 0.0f;
+    for (int tile = 0; tile < ntile; ++tile) {
+        cp_async_wait<kVStages - 2>();
+        __syncthreads();  // the tile (and, first time round, every alpha) is visible
+        const uint8_t* vt = ring + (size_t)(tile % kVStages) * kVTile * slice;
+        const int n = min(kVTile, cmax - tile * kVTile);
+        for (int tt = 0; tt < n; ++tt) {
+            const int t = tile * kVTile + tt;
+            float v, vs = 1.0f;
+            if (kvt == 1) v = half_bits_to_float(reinterpret_cast<const uint16_t*>(vt + tt * slice)[tid]);
+            else if (kvt == 0) v = reinterpret_cast<const float*>(vt + tt * slice)[tid];
+            else {
+                v = (float)reinterpret_cast<const int8_t*>(vt + tt * slice)[tid];
+                vs = kvt == 2 ? vsc[t] : vsc[t * (HD / 32) + tid / 32];
+            }
+#pragma unroll
+            for (int i = 0; i < QG; ++i) {
+                if (t < cq[i]) {
+                    float al = sc[i * mctx + t];
+                    if (kvt >= 2) al = al * vs;
+                    out[i] = fmaf(al, v, out[i]);
+                }
+            }
+        }
+        __syncthreads();
+        issue_v(tile + kVStages - 1);
+    }
+    cp_async_wait<0>();
+#pragma unroll
+    for (int i = 0; i < QG; ++i)
+        if (s0 + i < (int)a.n_seq) a.out[((size_t)(s0 + i) * a.n_head + h) * HD + tid] = out[i];
+    if (a.xq) {
+        // the o projection's Q8 input, as quantize_q8_t_kernel lays it out:
+        // warp w holds 32-element block (h*HD + 32w)/32 of every query row
+        const uint64_t D = a.n_head * HD, nb = D / 32, ldb = a.xq_ldb;
+        const uint64_t blk = ((uint64_t)h * HD + 32 * warp) / 32;
+        float* cT = a.xdT + nb * ldb;
+#pragma unroll
+        for (int i = 0; i < QG; ++i) {
+            if (s0 + i < (int)a.n_seq) {  // warp-uniform
+                float dd;
+                const int v = quant_q8_lane(out[i], dd);
+                a.xq[(size_t)(s0 + i) * D + (size_t)h * HD + tid] = (int8_t)v;
+                const int sum = warp_sum_i(v);
+                if (lane == 0) {
+                    a.xdT[blk * ldb + s0 + i] = dd;
+                    cT[blk * ldb + s0 + i] = 12582912.0f + (float)(8 * sum);
+                }
+            }
+        }
+        if (blockIdx.x == 0) {  // token rows n_seq..ldb-1 of this block: zero
+            for (uint64_t r = a.n_seq + lane; r < ldb; r += 32) {
+                a.xdT[blk * ldb + r] = 0.0f;
+                cT[blk * ldb + r] = 0.0f;
+            }
+        }
+    }
 }
 
 // ------------------------------------------- fused decode step (F16/F32 KV)
@@ -618,6 +887,39 @@ cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s) {
         default:
             return cudaErrorInvalidValue;
     }
+}
+
+namespace {
+template <int HD, int QG>
+cudaError_t launch_group(const AttnArgs& a, size_t smem, cudaStream_t s) {
+    dim3 grid((unsigned)((a.n_seq + QG - 1) / QG), (unsigned)a.n_head);
+    ensure_smem_attr(attn_group_kernel<HD, QG>, 200 * 1024);
+    return launch_pdl(attn_group_kernel<HD, QG>, grid, dim3(HD), smem, s, a);
+}
+template <int QG>
+cudaError_t launch_group_hd(const AttnArgs& a, size_t smem, cudaStream_t s) {
+    switch (a.hd) {
+        case 64: return launch_group<64, QG>(a, smem, s);
+        case 128: return launch_group<128, QG>(a, smem, s);
+        case 256: return launch_group<256, QG>(a, smem, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+}  // namespace
+
+cudaError_t paged_attn_prefill(const AttnArgs& a, cudaStream_t s) {
+    if (!a.n_seq) return cudaSuccess;
+    if (a.n_head % a.n_head_kv) return cudaErrorInvalidValue;
+    // groups of 4 when that still gives every SM a CTA, else pairs
+    const int qg = (a.n_seq + 3) / 4 * a.n_head >= (uint64_t)num_sms() ? 4 : a.n_seq >= 2 ? 2 : 1;
+    const size_t smem = qg > 1 ? attn_group_plan(a.hd, a.max_ctx ? a.max_ctx : 1, a.max_pages, a.kv_type, qg).total : 0;
+    if (qg == 1 || smem > 200 * 1024) {
+        cudaError_t e = paged_attn_decode(a, s);
+        if (e == cudaSuccess && a.xq) e = quantize_q8_rows_t(a.out, a.n_seq, a.n_head * a.hd, a.xq, a.xdT, a.xq_ldb, s);
+        return e;
+    }
+    if (a.xq && a.xq_ldb < a.n_seq) return cudaErrorInvalidValue;
+    return qg == 4 ? launch_group_hd<4>(a, smem, s) : launch_group_hd<2>(a, smem, s);
 }
 
 }  // namespace mvb

@@ -51,10 +51,11 @@
 //                thread spends ~60 cycles per MMA and more on its waits and
 //                commits, so three overlap); warp 1 also allocates TMEM
 //   warps 4-7    converters: warp w writes TMEM lanes 32*(w%4).. (its rows)
-//   warps 8-23   epilogue: TMEM -> registers -> chain -> y; warp w reads TMEM
-//                lanes 32*(w%4).. (its row quadrant), token quarter (w-8)/4:
-//                four warps per quadrant hide one another's TMEM and barrier
-//                latencies
+//   warps 8-15   epilogue: TMEM -> registers -> chain -> y; warp w reads TMEM
+//                lanes 32*(w%4).. (its row quadrant), token half (w-8)/4:
+//                two warps per quadrant hide one another's TMEM and barrier
+//                latencies (measured against one and four: two is 2-3%
+//                faster than four on every prefill shape, one 10-25% slower)
 // Rings: S smem stages (full: TMA bytes landed; empty: converters read the
 // nibbles and the MMAs read B), 4 TMEM A stages (aready: converters wrote;
 // aempty: MMAs read), the TMEM D groups (tfull: MMAs done; tempty: epilogue
@@ -93,7 +94,7 @@ constexpr int kMmaWarps = 3;
 constexpr int kConvWarp0 = 1 + kMmaWarps;
 constexpr int kConvWarps = 4;
 constexpr int kEpiWarp0 = kConvWarp0 + kConvWarps;
-constexpr int kEW = 4;  // epilogue warps per TMEM lane quadrant
+constexpr int kEW = 2;  // epilogue warps per TMEM lane quadrant
 constexpr int kEpiWarps = 4 * kEW;
 constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
 constexpr uint32_t kPreset = 0x4B400000u;   // 1.5 * 2^23 as a float
@@ -103,9 +104,12 @@ constexpr int kSA = 4;                      // TMEM A stages
 constexpr int kACols = kG * 8;              // TMEM columns of one A stage
 constexpr int kDCols = 512 - kSA * kACols;  // TMEM columns of the D ring
 
-template <int N>
+// N = MMA width (tokens per MMA), NE = tokens of the tile the epilogue
+// keeps (NE < N: the MMA's other columns are never read; tiles of NE = 8
+// tokens put twice as many CTAs on a narrow weight as N = 16 can)
+template <int N, int NE>
 struct Cfg {
-    static constexpr int kTT = N / kEW;        // tokens per epilogue thread
+    static constexpr int kTT = NE / kEW;       // tokens per epilogue thread
     static constexpr int kRaw = kM * kG * 16;  // [128][64 B]
     static constexpr int kB = N * kG * 32;     // [N][128 B]
     static constexpr int kStage = kRaw + kB;
@@ -119,7 +123,7 @@ struct Cfg {
     static constexpr int kSmem = kBarOff + kBars * 8 + 16 + 1024;  // + alignment slack
     static_assert(kTG >= 2, "two TMEM D groups at least");
     static_assert(kStage % 1024 == 0 && kEpi % 1024 == 0, "swizzled TMA tiles need 1024-byte alignment");
-    static_assert(kEB % kG == 0 && kTT % 4 == 0, "tile shape");
+    static_assert(kEB % kG == 0 && kTT % 4 == 0 && NE <= N, "tile shape");
     static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
@@ -134,8 +138,10 @@ __device__ __forceinline__ void tmem_load(uint32_t taddr, uint32_t (&v)[TT]) {
         tc::tmem_ld4(taddr, v);
     } else if constexpr (TT == 8) {
         tc::tmem_ld8(taddr, v);
-    } else {
+    } else if constexpr (TT == 16) {
         tc::tmem_ld16(taddr, v);
+    } else {
+        tc::tmem_ld32(taddr, v);
     }
 }
 template <int TT>
@@ -144,8 +150,10 @@ __device__ __forceinline__ void tmem_preset(uint32_t taddr) {
         tc::tmem_fill4(taddr, kPreset);
     } else if constexpr (TT == 8) {
         tc::tmem_fill8(taddr, kPreset);
-    } else {
+    } else if constexpr (TT == 16) {
         tc::tmem_fill16(taddr, kPreset);
+    } else {
+        tc::tmem_fill32(taddr, kPreset);
     }
 }
 
@@ -153,12 +161,12 @@ __device__ __forceinline__ uint64_t pack2(float a, float b) {
     return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
 }
 
-template <int N>
+template <int N, int NE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                    const __grid_constant__ CUtensorMap dmap, const __grid_constant__ CUtensorMap smap,
                    const TcArgs a) {
-    using C = Cfg<N>;
+    using C = Cfg<N, NE>;
     constexpr int TT = C::kTT, LB = 32 / TT < kG ? 32 / TT : kG;  // blocks per TMEM load batch
     extern __shared__ unsigned char smem_dyn[];
     const uint32_t s0 = tc::smem_u32(smem_dyn);
@@ -182,6 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool epi = warp >= kEpiWarp0;
     const int quad = warp & 3;                  // converter/epilogue: TMEM lanes 32*quad .. +31
     const int slice = (warp - kEpiWarp0) >> 2;  // epilogue: tokens slice*TT .. +TT-1 of a tile
+    pdl_trigger();
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kS; ++s) {
             tc::mbar_init(full0 + 8 * s, 1);
@@ -225,6 +234,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
+    // programmatic dependent launch: the set-up above overlaps the previous
+    // kernel; activations, scales and y are touched only after it completed
+    pdl_wait();
 
     if (warp == 0) {
         // ---------------------------------------------------- TMA producer
@@ -232,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t k = 0, j = 0;  // stages, epilogue-data groups issued
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
-                const int row0 = (tile / a.n_ttiles) * kM, t0 = (tile % a.n_ttiles) * N;
+                const int row0 = (tile / a.n_ttiles) * kM, t0 = (tile % a.n_ttiles) * NE;
                 for (int b0 = 0; b0 < a.nb; b0 += kG) {
                     if (b0 % kEB == 0) {
                         const int e = j % kES;
@@ -349,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
             const int r = (tile / a.n_ttiles) * kM + rr;
-            const int tb = (tile % a.n_ttiles) * N + slice * TT;
+            const int tb = (tile % a.n_ttiles) * NE + slice * TT;
             uint64_t acc[TT / 2];  // token pairs, (+0, +0) first
 #pragma unroll
             for (int t = 0; t < TT / 2; ++t) acc[t] = 0ull;
@@ -448,10 +460,10 @@ using tc::EncodeFn;
 using tc::encode;
 using tc::encode_fn;
 
-template <int N>
+template <int N, int NE>
 cudaError_t launch_tc(const mv_weight_s& w, const int8_t* q, const float* dT, uint64_t ldb, uint64_t batch, float* y,
                       cudaStream_t s, bool accumulate) {
-    using C = Cfg<N>;
+    using C = Cfg<N, NE>;
     const EncodeFn enc = encode_fn();
     if (!enc) {
         set_last_error("cuTensorMapEncodeTiled is unavailable in this driver");
@@ -479,13 +491,12 @@ cudaError_t launch_tc(const mv_weight_s& w, const int8_t* q, const float* dT, ui
         set_last_error("cuTensorMapEncodeTiled rejected a tensor map of the tensor-core GEMM");
         return cudaErrorInvalidValue;
     }
-    const int n_ttiles = (int)((batch + N - 1) / N);
+    const int n_ttiles = (int)((batch + NE - 1) / NE);
     const int n_tiles = (int)((w.rows + kM - 1) / kM) * n_ttiles;
     const TcArgs args{y, (int)w.rows, (int)w.nb, (int)batch, n_ttiles, n_tiles, accumulate ? 1 : 0};
-    ensure_smem_attr(gemm_tc_kernel<N>, C::kSmem);
+    ensure_smem_attr(gemm_tc_kernel<N, NE>, C::kSmem);
     const int grid = n_tiles < num_sms() ? n_tiles : num_sms();
-    gemm_tc_kernel<N><<<grid, kThreads, C::kSmem, s>>>(wmap, xmap, dmap, smap, args);
-    return cudaGetLastError();
+    return launch_pdl(gemm_tc_kernel<N, NE>, dim3(grid), dim3(kThreads), C::kSmem, s, wmap, xmap, dmap, smap, args);
 }
 
 }  // namespace
@@ -495,14 +506,19 @@ cudaError_t gemm_q4_q8_tc(const mv_weight_s& w, const int8_t* q, const float* dT
     if (!batch) return cudaSuccess;
     if (w.type != 2 || ldb < gemm_tc_ldb(batch) || ldb % 4 || w.rows >= (1ull << 31) || batch >= (1ull << 31))
         return cudaErrorInvalidValue;
-    // Tile width N: the epilogue's share grows with N, the per-block MMA,
-    // conversion and synchronisation share does not; pick the N with the
-    // fewest waves x cost.
+    // Tile width (tokens per tile): the epilogue's share grows with it, the
+    // per-block MMA, conversion and synchronisation share does not; pick the
+    // width with the fewest waves x relative cost of one tile (measured:
+    // 8 tokens ~0.42, 16 ~0.6 of a 32-token tile).
     const uint64_t row_tiles = (w.rows + kM - 1) / kM, sms = (uint64_t)num_sms();
-    const uint64_t w16 = (row_tiles * ((batch + 15) / 16) + sms - 1) / sms;
-    const uint64_t w32 = (row_tiles * ((batch + 31) / 32) + sms - 1) / sms;
-    return (double)w16 * 60.0 <= (double)w32 * 100.0 ? launch_tc<16>(w, q, dT, ldb, batch, y, s, accumulate)
-                                                     : launch_tc<32>(w, q, dT, ldb, batch, y, s, accumulate);
+    auto waves = [&](uint64_t ne) { return (row_tiles * ((batch + ne - 1) / ne) + sms - 1) / sms; };
+    int ne = 32;
+    double best = (double)waves(32) * 100.0;
+    if ((double)waves(16) * 60.0 <= best) ne = 16, best = (double)waves(16) * 60.0;
+    if ((double)waves(8) * 42.0 < best) ne = 8;
+    return ne == 8    ? launch_tc<16, 8>(w, q, dT, ldb, batch, y, s, accumulate)
+           : ne == 16 ? launch_tc<16, 16>(w, q, dT, ldb, batch, y, s, accumulate)
+                      : launch_tc<32, 32>(w, q, dT, ldb, batch, y, s, accumulate);
 }
 
 }  // namespace mvb

@@ -27,6 +27,10 @@ cudaError_t quantize_q8_rows_t(const float* x, uint64_t rows, uint64_t cols, int
 // the same on rmsnorm(x) * w (the reference's rmsnorm), without materialising it
 cudaError_t rmsnorm_quantize_q8_rows_t(const float* x, const float* w, uint64_t rows, uint64_t cols, float eps,
                                        int8_t* q, float* dT, uint64_t ldb, cudaStream_t s);
+// the same on ff = silu(g) * u of a gate|up output with interleaved (g, u)
+// rows: gu is [rows][2 * cols], the quantised ff [rows][cols]
+cudaError_t silu_quantize_q8_rows_t(const float* gu, uint64_t rows, uint64_t cols, int8_t* q, float* dT, uint64_t ldb,
+                                    cudaStream_t s);
 
 // ---- gemv_q4.cu : decode GEMV over Q4_0 with Q8 activations (integer path)
 enum class Q4Pro : int {
@@ -115,9 +119,19 @@ struct AttnArgs {
     const int32_t* ctx_len;  // per query row
     uint64_t max_ctx;        // upper bound of ctx_len (sizes shared memory)
     float* out;              // [n_seq][n_head*hd]
+    int one_seq = 0;         // 1: every query row reads block-table row 0 (rows of one sequence)
+    // paged_attn_prefill only: when xq is set, the output rows are also
+    // quantised for the tensor-core GEMM (quantize_q8_rows_t's layout, ldb)
+    int8_t* xq = nullptr;
+    float* xdT = nullptr;
+    uint64_t xq_ldb = 0;
 };
 uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type);
 cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s);
+// Prefill form: the query rows belong to ONE sequence (a.one_seq, or every
+// row's block-table row is the same), so groups of them share each staged K/V
+// tile; results identical to paged_attn_decode.
+cudaError_t paged_attn_prefill(const AttnArgs& a, cudaStream_t s);
 
 // One decode token (F32 or F16 KV): RoPE + KV append + attention in one kernel.
 struct AttnFusedArgs {

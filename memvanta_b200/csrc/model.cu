@@ -1026,16 +1026,34 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
         auto& L = m->layers[l];
         project_normed(L.qkv, L.attn_norm, m->QKV);
         rope_append(m, L, m->QKV, B, pos, nullptr);
-        ck(mvb::paged_attn_decode(attn_args(m, L, m->QKV, m->qkvw, B, ctx, start + B, tp ? m->ATT_l : m->ATT), s),
-           "attention");
+        mvb::AttnArgs aa = attn_args(m, L, m->QKV, m->qkvw, B, ctx, start + B, tp ? m->ATT_l : m->ATT);
+        aa.one_seq = 1;
+        // single GPU, tensor-core o projection: the attention kernel also
+        // writes the o GEMM's Q8 input (no separate quantisation launch)
+        const bool fuse_o = !tp && B >= 2 && L.o->type == 2;
+        if (fuse_o) {
+            aa.xq = m->XQ;
+            aa.xdT = m->XD;
+            aa.xq_ldb = mvb::gemm_tc_ldb(B);
+        }
+        ck(mvb::paged_attn_prefill(aa, s), "attention");
         if (tp) {
             exchange(m->ATT_l, m->Dl, m->off_ATT, D, m->tp_rank * m->Dl, false, pt_att(l));
             project(L.o, m->ATT, D, m->PROJ_l, false);
             exchange(m->PROJ_l, m->Dl, m->off_X, D, m->tp_rank * m->Dl, true, pt_o(l));
+        } else if (fuse_o) {
+            ck(mvb::gemm_q4_q8_tc(*L.o, m->XQ, m->XD, mvb::gemm_tc_ldb(B), B, m->X, s, true), "gemm");
         } else {
             project(L.o, m->ATT, D, m->X, true);
         }
         project_normed(L.gu, L.ffn_norm, m->GU);
+        if (!tp && B >= 2 && L.down->type == 2) {
+            // SiLU gate fused into the down GEMM's Q8 quantisation
+            const uint64_t ldb = mvb::gemm_tc_ldb(B);
+            ck(mvb::silu_quantize_q8_rows_t(m->GU, B, F, m->XQ, m->XD, ldb, s), "silu+quantize");
+            ck(mvb::gemm_q4_q8_tc(*L.down, m->XQ, m->XD, ldb, B, m->X, s, true), "gemm");
+            continue;
+        }
         float* ff = tp ? m->FF_l : m->FF;
         mvb::silu_pairs_kernel<<<mvb::ew_grid(B * m->Fl), 256, 0, s>>>(m->GU, ff, B * m->Fl);
         ck(cudaGetLastError(), "silu_pairs");

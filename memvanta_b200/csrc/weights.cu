@@ -186,9 +186,44 @@ __global__ void quantize_q8_t_kernel(const float* __restrict__ x, uint64_t rows,
     const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
     const uint64_t first = blockIdx.x * (uint64_t)(blockDim.x / 32) + threadIdx.x / 32;
     float* cT = dT + nb * ldb;
+    pdl_trigger();
+    pdl_wait();
     for (uint64_t b = first; b < rows * nb; b += warps) {
         float dd;
         const int v = quant_q8_lane(__ldcg(x + b * 32 + lane), dd);  // L2: x may come from other GPUs
+        q[b * 32 + lane] = (int8_t)v;
+        const int sum = warp_sum_i(v);
+        if (lane == 0) {
+            const uint64_t at = (b % nb) * ldb + b / nb;
+            dT[at] = dd;
+            cT[at] = 12582912.0f + (float)(8 * sum);
+        }
+    }
+    const uint64_t padw = ldb - rows, padn = nb * padw;
+    for (uint64_t i = first * 32 + lane; i < padn; i += warps * 32) {
+        const uint64_t at = (i / padw) * ldb + rows + i % padw;
+        dT[at] = 0.0f;
+        cT[at] = 0.0f;
+    }
+}
+
+// The same quantisation of ff = silu(g) * u computed on the fly from the
+// gate|up GEMM output, whose rows come interleaved (g_i, u_i): the down
+// projection's input without materialising ff.  ff is evaluated exactly as
+// silu_pairs_kernel evaluates it, (g / (1 + expf(-g))) * u.
+__global__ void silu_quantize_q8_t_kernel(const float* __restrict__ gu, uint64_t rows, uint64_t nb,
+                                          int8_t* __restrict__ q, float* __restrict__ dT, uint64_t ldb) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
+    const uint64_t first = blockIdx.x * (uint64_t)(blockDim.x / 32) + threadIdx.x / 32;
+    float* cT = dT + nb * ldb;
+    pdl_trigger();
+    pdl_wait();
+    for (uint64_t b = first; b < rows * nb; b += warps) {
+        const float2 p = reinterpret_cast<const float2*>(gu)[b * 32 + lane];  // (g, u) of element b*32+lane
+        const float ff = (p.x / (1.0f + expf(-p.x))) * p.y;
+        float dd;
+        const int v = quant_q8_lane(ff, dd);
         q[b * 32 + lane] = (int8_t)v;
         const int sum = warp_sum_i(v);
         if (lane == 0) {
@@ -218,6 +253,8 @@ __global__ void rmsnorm_quantize_t_kernel(const float* __restrict__ x, const flo
     const int nc = n / 4, nb = n / 32;
     const int steps = (nc + blockDim.x - 1) / blockDim.x;
     const float4* xr = reinterpret_cast<const float4*>(x + row * n);
+    pdl_trigger();
+    pdl_wait();
     double ss = 0.0;
     for (int c = threadIdx.x; c < nc; c += blockDim.x) {
         const float4 v = __ldcg(xr + c);  // L2: x may come from other GPUs
@@ -287,8 +324,8 @@ cudaError_t rmsnorm_quantize_q8_rows_t(const float* x, const float* w, uint64_t 
     if (cols % 32 || ldb < rows) return cudaErrorInvalidValue;
     const uint64_t nc = cols / 4;
     const unsigned threads = (unsigned)(nc >= 1024 ? 1024 : (nc + 31) / 32 * 32);
-    rmsnorm_quantize_t_kernel<<<(unsigned)rows, threads, 0, s>>>(x, w, (int)cols, eps, rows, q, dT, ldb);
-    return cudaGetLastError();
+    return launch_pdl(rmsnorm_quantize_t_kernel, dim3((unsigned)rows), dim3(threads), 0, s, x, w, (int)cols, eps, rows,
+                      q, dT, ldb);
 }
 
 cudaError_t quantize_q8_rows_t(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* dT, uint64_t ldb,
@@ -297,8 +334,18 @@ cudaError_t quantize_q8_rows_t(const float* x, uint64_t rows, uint64_t cols, int
     if (!nblocks || ldb < rows) return nblocks ? cudaErrorInvalidValue : cudaSuccess;
     const uint64_t ctas = (nblocks + 7) / 8;
     const uint64_t cap = (uint64_t)num_sms() * 8;
-    quantize_q8_t_kernel<<<(unsigned)(ctas < cap ? ctas : cap), 256, 0, s>>>(x, rows, cols / 32, q, dT, ldb);
-    return cudaGetLastError();
+    return launch_pdl(quantize_q8_t_kernel, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(256), 0, s, x, rows,
+                      cols / 32, q, dT, ldb);
+}
+
+cudaError_t silu_quantize_q8_rows_t(const float* gu, uint64_t rows, uint64_t cols, int8_t* q, float* dT, uint64_t ldb,
+                                    cudaStream_t s) {
+    const uint64_t nblocks = rows * (cols / 32);
+    if (!nblocks || ldb < rows || cols % 32) return nblocks ? cudaErrorInvalidValue : cudaSuccess;
+    const uint64_t ctas = (nblocks + 7) / 8;
+    const uint64_t cap = (uint64_t)num_sms() * 8;
+    return launch_pdl(silu_quantize_q8_t_kernel, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(256), 0, s, gu, rows,
+                      cols / 32, q, dT, ldb);
 }
 
 cudaError_t quantize_q8_rows(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* d, cudaStream_t s) {

@@ -166,6 +166,39 @@ def test_config4_ragged_paged_attention(cuda, oracle, kv_type):
         assert rel_err(out[s], want) <= 1e-4, (s, rel_err(out[s], want))
 
 
+@pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_Q8, mv.KV_Q8_0, mv.KV_F32])
+@pytest.mark.parametrize("n_q,n_head,n_head_kv,hd", [(32, 32, 32, 128), (30, 32, 8, 128), (64, 32, 4, 64),
+                                                     (16, 16, 2, 256)])
+def test_prefill_attention_groups(cuda, oracle, kv_type, n_q, n_head, n_head_kv, hd):
+    """A prefill chunk: n_q causal query rows of one sequence (row i sees
+    start + i + 1 tokens) over scattered 16-token pages.  The grouped kernel
+    (query rows sharing each staged K/V tile) must equal the one-query kernel
+    bit for bit, and the oracle's reference loop within 1e-4."""
+    rng = np.random.default_rng(50 + kv_type + n_q + hd)
+    page, start = 16, 437
+    kv_dim = n_head_kv * hd
+    n_ctx = start + n_q
+    max_pages = (n_ctx + page - 1) // page
+    table = rng.permutation(max_pages + 5)[:max_pages].astype(np.int32)
+    kp, vp, ks, vs, ns = _alloc_cache(cuda, kv_type, kv_dim, (max_pages + 5) * page)
+    K = rng.standard_normal((n_ctx, kv_dim)).astype(np.float32)
+    V = rng.standard_normal((n_ctx, kv_dim)).astype(np.float32)
+    mv.kv_append(kv_type, dev(K, cuda), dev(V, cuda), dev(np.arange(n_ctx, dtype=np.int32), cuda),
+                 dev(table, cuda), max_pages, page, kp, vp, ks, vs)
+    q = rng.standard_normal((n_q, n_head * hd)).astype(np.float32)
+    ctx = (start + 1 + np.arange(n_q)).astype(np.int32)
+    got = host(mv.paged_attn_prefill(kv_type, dev(q, cuda), n_head, n_head_kv, hd, kp, vp, dev(table, cuda),
+                                     max_pages, page, dev(ctx, cuda), n_ctx, ks, vs))
+    rep = np.tile(table, (n_q, 1))
+    one = host(mv.paged_attn_decode(kv_type, dev(q, cuda), n_head, n_head_kv, hd, kp, vp, dev(rep, cuda),
+                                    max_pages, page, dev(ctx, cuda), n_ctx, ks, vs))
+    assert np.array_equal(got, one)
+    okp, ovp, oks, ovs = _oracle_cache(oracle, kv_type, K, V, table, page, (max_pages + 5) * page)
+    for i in [0, 1, n_q // 2, n_q - 1]:
+        want = oracle.attn_decode(kv_type, q[i], n_head, n_head_kv, hd, okp, ovp, oks, ovs, table, page, int(ctx[i]))
+        assert rel_err(got[i], want) <= 1e-4, (i, rel_err(got[i], want))
+
+
 def test_gqa_and_head_dims(cuda, oracle):
     rng = np.random.default_rng(44)
     for n_head, n_head_kv, hd in [(8, 2, 128), (4, 4, 64), (8, 1, 256), (16, 2, 64)]:

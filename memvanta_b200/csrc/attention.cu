@@ -303,16 +303,29 @@ __global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
         __syncthreads();  // the tile is visible to every thread
         const uint8_t* vt = ring + (size_t)(tile % kVStages) * kVTile * slice;
         const int n = min(kVTile, ctx - tile * kVTile);
-        for (int tt = 0; tt < n; ++tt) {
+        // alpha_t = e_t * float(1/den) (times the V scale for Q8); the loads
+        // of 8 tokens go out before their 8 chain steps
+        auto step = [&](int tt, float& v, float& al) {
             const int t = tile * kVTile + tt;
-            float al = sc[t] * inv;  // alpha_t = e_t * float(1/den)
-            float v;
+            al = sc[t] * inv;
             if (kvt == 1) v = half_bits_to_float(reinterpret_cast<const uint16_t*>(vt + tt * slice)[tid]);
             else if (kvt == 0) v = reinterpret_cast<const float*>(vt + tt * slice)[tid];
             else {
                 v = (float)reinterpret_cast<const int8_t*>(vt + tt * slice)[tid];
                 al = al * (kvt == 2 ? vsc[t] : vsc[t * (HD / 32) + tid / 32]);
             }
+        };
+        int tt = 0;
+        for (; tt + 8 <= n; tt += 8) {
+            float v[8], al[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) step(tt + j, v[j], al[j]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) out = fmaf(al[j], v[j], out);
+        }
+        for (; tt < n; ++tt) {
+            float v, al;
+            step(tt, v, al);
             out = fmaf(al, v, out);
         }
         __syncthreads();  // everyone is done with this stage before it is refilled
@@ -383,11 +396,12 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
     pdl_trigger();
     pdl_wait();
     int cq[QG];
-    int cmax = 0;
+    int cmax = 0, cmin = INT_MAX;
 #pragma unroll
     for (int i = 0; i < QG; ++i) {
         cq[i] = s0 + i < (int)a.n_seq ? a.ctx_len[s0 + i] : 0;
         cmax = max(cmax, cq[i]);
+        cmin = min(cmin, cq[i]);
     }
     const int npg = (cmax + page - 1) / page;
     const size_t trow = a.one_seq ? 0 : (size_t)s0;
@@ -537,15 +551,18 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
         __syncthreads();  // the tile (and, first time round, every alpha) is visible
         const uint8_t* vt = ring + (size_t)(tile % kVStages) * kVTile * slice;
         const int n = min(kVTile, cmax - tile * kVTile);
-        for (int tt = 0; tt < n; ++tt) {
+        auto vload = [&](int tt, float& v, float& vs) {
             const int t = tile * kVTile + tt;
-            float v, vs = 1.0f;
+            vs = 1.0f;
             if (kvt == 1) v = half_bits_to_float(reinterpret_cast<const uint16_t*>(vt + tt * slice)[tid]);
             else if (kvt == 0) v = reinterpret_cast<const float*>(vt + tt * slice)[tid];
             else {
                 v = (float)reinterpret_cast<const int8_t*>(vt + tt * slice)[tid];
                 vs = kvt == 2 ? vsc[t] : vsc[t * (HD / 32) + tid / 32];
             }
+        };
+        auto vstep = [&](int tt, float v, float vs) {
+            const int t = tile * kVTile + tt;
 #pragma unroll
             for (int i = 0; i < QG; ++i) {
                 if (t < cq[i]) {
@@ -554,6 +571,31 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
                     out[i] = fmaf(al, v, out[i]);
                 }
             }
+        };
+        // tokens every query of the group sees, 8 at a time: all their loads
+        // go out before the chain steps (each query's steps stay in token order)
+        const int nall = max(0, min(n, cmin - tile * kVTile));
+        int tt = 0;
+        for (; tt + 8 <= nall; tt += 8) {
+            float v[8], vs[8], al[QG][8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) vload(tt + j, v[j], vs[j]);
+#pragma unroll
+            for (int i = 0; i < QG; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    al[i][j] = sc[i * mctx + tile * kVTile + tt + j];
+                    if (kvt >= 2) al[i][j] = al[i][j] * vs[j];
+                }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int i = 0; i < QG; ++i) out[i] = fmaf(al[i][j], v[j], out[i]);
+        }
+        for (; tt < n; ++tt) {
+            float v, vs;
+            vload(tt, v, vs);
+            vstep(tt, v, vs);
         }
         __syncthreads();
         issue_v(tile + kVStages - 1);
@@ -816,10 +858,23 @@ __global__ void __launch_bounds__(HD) attn_decode_fused_kernel(AttnFusedArgs a) 
         __syncthreads();  // the tile is visible to every thread
         const uint8_t* vt = vring + (size_t)(tile % VS) * kVTile * slice;
         const int n = min(kVTile, p - tile * kVTile);
-        for (int tt = 0; tt < n; ++tt) {
-            const float al = sc[tile * kVTile + tt] * inv;  // alpha_t = e_t * float(1/den)
-            const float v = kvt == 1 ? half_bits_to_float(reinterpret_cast<const uint16_t*>(vt + tt * slice)[tid])
-                                     : reinterpret_cast<const float*>(vt + tt * slice)[tid];
+        auto step = [&](int tt, float& v, float& al) {
+            al = sc[tile * kVTile + tt] * inv;  // alpha_t = e_t * float(1/den)
+            v = kvt == 1 ? half_bits_to_float(reinterpret_cast<const uint16_t*>(vt + tt * slice)[tid])
+                         : reinterpret_cast<const float*>(vt + tt * slice)[tid];
+        };
+        // the loads of 8 tokens go out before their 8 chain steps
+        int tt = 0;
+        for (; tt + 8 <= n; tt += 8) {
+            float v[8], al[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) step(tt + j, v[j], al[j]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) out = fmaf(al[j], v[j], out);
+        }
+        for (; tt < n; ++tt) {
+            float v, al;
+            step(tt, v, al);
             out = fmaf(al, v, out);
         }
         __syncthreads();  // everyone is done with this stage before it is refilled

@@ -443,6 +443,9 @@ def main():
     ap.add_argument("--rows", type=int, default=12288, help="gemv/gemm: weight rows")
     ap.add_argument("--cols", type=int, default=4096, help="gemv/gemm: weight cols (K)")
     ap.add_argument("--batch", type=int, default=32, help="gemm: tokens")
+    ap.add_argument("--wtype", default="q4_0", choices=["q4_0", "q8_0", "q6_k"],
+                    help="gemv/gemm: weight type (config 2: q8_0 4096x4096, q6_k 32000x4096; the gemm of q8_0 and "
+                         "q6_k runs the reference's fp32-activation path)")
     ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"], help="paged_attn: cache type")
     ap.add_argument("--clock-window", type=float, default=0.5)
     args = ap.parse_args()
@@ -558,9 +561,11 @@ def main_micro(args):
         return main_paged_attn(args, mv, dev)
     rows, cols, B = args.rows, args.cols, args.batch
     rng = np.random.default_rng(7)
-    wbytes = rows * cols // 32 * 18
+    wt = {"q4_0": gguf.Q4_0, "q8_0": gguf.Q8_0, "q6_k": gguf.Q6_K}[args.wtype]
+    wbytes = gguf.tensor_nbytes(wt, rows * cols)
     copies = max(2, int(np.ceil(3 * 126e6 / wbytes)))
-    ws = [mv.Weight.upload(gguf.gen_q4_0(rows, cols, rng), mv.Q4_0, rows, cols) for _ in range(copies)]
+    ws = [mv.Weight.upload(gguf.gen_blocks(wt, rows, cols, rng), wt, rows, cols) for _ in range(copies)]
+    act = mv.ACT_Q8 if wt == gguf.Q4_0 else mv.ACT_F32  # tensor_matmul_batch_v06's dispatch
     n = max(args.steps, copies)
     stream = torch.cuda.Stream(device=dev)
     if args.workload == "gemv":
@@ -568,7 +573,7 @@ def main_micro(args):
         launch = lambda w: mv.gemv(w, x, y, stream)  # noqa: E731
     else:
         x, y = torch.randn(B, cols, device=dev), torch.empty(B, rows, device=dev)
-        launch = lambda w: mv.gemm(w, x, y, mv.ACT_Q8, stream)  # noqa: E731
+        launch = lambda w: mv.gemm(w, x, y, act, stream)  # noqa: E731
     with torch.cuda.stream(stream):
         for i in range(max(args.warmup, 1)):
             launch(ws[i % copies])
@@ -586,14 +591,19 @@ def main_micro(args):
         torch.cuda.synchronize()
     mv.stream_status(stream)
     us = e0.elapsed_time(e1) * 1e3 / n
-    line = {"workload": args.workload, "rows": rows, "cols": cols, "us_per_launch": round(us, 3), "launches": n}
+    line = {"workload": args.workload, "wtype": args.wtype, "rows": rows, "cols": cols, "us_per_launch": round(us, 3),
+            "launches": n}
+    peak = measured_peaks()["hbm_gbs"]
     if args.workload == "gemv":
         alg = wbytes + cols * 4 + rows * 4
-        line.update({"metric": "Q4_0 GEMV achieved GB/s", "value": round(alg / us / 1e3, 1), "unit": "GB/s",
-                     "algorithmic_bytes_per_launch": alg})
+        line.update({"metric": f"{args.wtype} GEMV achieved GB/s", "value": round(alg / us / 1e3, 1), "unit": "GB/s",
+                     "algorithmic_bytes_per_launch": alg, "hbm_frac": round(alg / us / 1e3 / peak, 4)})
     else:
-        line.update({"batch": B, "metric": "Q4_0 x Q8 GEMM TOPS (2*rows*cols*batch / time, quantisation included)",
-                     "value": round(2 * rows * cols * B / us / 1e6, 2), "unit": "TOPS"})
+        alg = wbytes + B * cols * 4 + B * rows * 4
+        line.update({"batch": B, "metric": f"{args.wtype} GEMM TOPS (2*rows*cols*batch / time"
+                                           + (", Q8 quantisation included)" if wt == gguf.Q4_0 else ", fp32 x)"),
+                     "value": round(2 * rows * cols * B / us / 1e6, 2), "unit": "TOPS",
+                     "weight_stream_gbs": round(alg / us / 1e3, 1), "hbm_frac": round(alg / us / 1e3 / peak, 4)})
     print(json.dumps(line), flush=True)
 
 

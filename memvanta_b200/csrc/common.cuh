@@ -50,6 +50,22 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// launch_pdl when pdl is true, else a plain launch (full stream order: the
+// kernel starts after everything before it in the stream, event waits
+// included; its pdl_trigger / pdl_wait are then no-ops).
+template <class... KArgs, class... Args>
+inline cudaError_t launch_opt(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+    if (pdl) return launch_pdl(kernel, grid, block, smem, s, std::forward<Args>(args)...);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.numAttrs = 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // The same with thread-block clusters of `cluster` CTAs along x.
 template <class... KArgs, class... Args>
 inline cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,

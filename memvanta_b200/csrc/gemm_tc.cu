@@ -128,8 +128,8 @@ struct Cfg {
 };
 
 struct TcArgs {
-    float* y;  // [batch][rows]
-    int rows, nb, batch, n_ttiles, n_tiles, accumulate;
+    float* y;  // row r of token t at y[t * ldy + r]
+    int rows, nb, batch, n_ttiles, n_tiles, accumulate, ldy;
 };
 
 template <int TT>
@@ -438,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int t = 0; t < TT; ++t) {
                     if (tb + t < a.batch) {
                         const float v = __uint_as_float((uint32_t)(acc[t / 2] >> (32 * (t & 1))));
-                        float* p = a.y + (size_t)(tb + t) * a.rows + r;
+                        float* p = a.y + (size_t)(tb + t) * a.ldy + r;
                         *p = a.accumulate ? *p + v : v;
                     }
                 }
@@ -462,7 +462,7 @@ using tc::encode_fn;
 
 template <int N, int NE>
 cudaError_t launch_tc(const mv_weight_s& w, const int8_t* q, const float* dT, uint64_t ldb, uint64_t batch, float* y,
-                      cudaStream_t s, bool accumulate) {
+                      uint64_t ldy, cudaStream_t s, bool accumulate) {
     using C = Cfg<N, NE>;
     const EncodeFn enc = encode_fn();
     if (!enc) {
@@ -493,7 +493,7 @@ cudaError_t launch_tc(const mv_weight_s& w, const int8_t* q, const float* dT, ui
     }
     const int n_ttiles = (int)((batch + NE - 1) / NE);
     const int n_tiles = (int)((w.rows + kM - 1) / kM) * n_ttiles;
-    const TcArgs args{y, (int)w.rows, (int)w.nb, (int)batch, n_ttiles, n_tiles, accumulate ? 1 : 0};
+    const TcArgs args{y, (int)w.rows, (int)w.nb, (int)batch, n_ttiles, n_tiles, accumulate ? 1 : 0, (int)ldy};
     ensure_smem_attr(gemm_tc_kernel<N, NE>, C::kSmem);
     const int grid = n_tiles < num_sms() ? n_tiles : num_sms();
     return launch_pdl(gemm_tc_kernel<N, NE>, dim3(grid), dim3(kThreads), C::kSmem, s, wmap, xmap, dmap, smap, args);
@@ -508,17 +508,40 @@ cudaError_t gemm_q4_q8_tc(const mv_weight_s& w, const int8_t* q, const float* dT
         return cudaErrorInvalidValue;
     // Tile width (tokens per tile): the epilogue's share grows with it, the
     // per-block MMA, conversion and synchronisation share does not; pick the
-    // width with the fewest waves x relative cost of one tile (measured:
-    // 8 tokens ~0.42, 16 ~0.6 of a 32-token tile).
-    const uint64_t row_tiles = (w.rows + kM - 1) / kM, sms = (uint64_t)num_sms();
-    auto waves = [&](uint64_t ne) { return (row_tiles * ((batch + ne - 1) / ne) + sms - 1) / sms; };
-    int ne = 32;
-    double best = (double)waves(32) * 100.0;
-    if ((double)waves(16) * 60.0 <= best) ne = 16, best = (double)waves(16) * 60.0;
-    if ((double)waves(8) * 42.0 < best) ne = 8;
-    return ne == 8    ? launch_tc<16, 8>(w, q, dT, ldb, batch, y, s, accumulate)
-           : ne == 16 ? launch_tc<16, 16>(w, q, dT, ldb, batch, y, s, accumulate)
-                      : launch_tc<32, 32>(w, q, dT, ldb, batch, y, s, accumulate);
+    // width with the fewest waves x relative cost of one tile (8 tokens
+    // ~0.42, 16 ~0.6 of a 32-token tile).
+    const uint64_t sms = (uint64_t)num_sms();
+    auto plan = [&](uint64_t row_tiles, int& ne) {
+        auto waves = [&](uint64_t e) { return (double)((row_tiles * ((batch + e - 1) / e) + sms - 1) / sms); };
+        ne = 32;
+        double best = waves(32) * 100.0;
+        if (waves(16) * 60.0 <= best) ne = 16, best = waves(16) * 60.0;
+        if (waves(8) * 42.0 < best) ne = 8, best = waves(8) * 42.0;
+        return best;
+    };
+    auto run = [&](const mv_weight_s& v, float* yv, int ne) {
+        return ne == 8    ? launch_tc<16, 8>(v, q, dT, ldb, batch, yv, w.rows, s, accumulate)
+               : ne == 16 ? launch_tc<16, 16>(v, q, dT, ldb, batch, yv, w.rows, s, accumulate)
+                          : launch_tc<32, 32>(v, q, dT, ldb, batch, yv, w.rows, s, accumulate);
+    };
+    const uint64_t row_tiles = (w.rows + kM - 1) / kM;
+    int ne = 32, ne_rest = 32;
+    const double one = plan(row_tiles, ne);
+    // One token tile and more 128-row tiles than SMs: a launch of one
+    // 32-token tile per SM, then the remaining rows in narrower tiles (each
+    // CTA of the second launch starts as an SM frees up), instead of uneven
+    // rounds of one launch (gate|up at 32 tokens: 172 row tiles).
+    if (batch <= 32 && row_tiles > sms && 100.0 + plan(row_tiles - sms, ne_rest) < one) {
+        mv_weight_s head = w, tail = w;
+        const uint64_t r0 = sms * kM;
+        head.rows = r0;
+        tail.rows = w.rows - r0;
+        tail.qs = w.qs + r0 * w.nb * 16;  // 16-byte aligned: whole rows of 16-byte payloads
+        tail.d = w.d + r0 * w.dstride;    // dstride is a multiple of 8 fp16
+        const cudaError_t e = run(head, y, 32);
+        return e != cudaSuccess ? e : run(tail, y + r0, ne_rest);
+    }
+    return run(w, y, ne);
 }
 
 }  // namespace mvb

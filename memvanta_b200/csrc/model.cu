@@ -307,6 +307,22 @@ struct mv_model_s {
     float *X = nullptr, *N = nullptr, *QKV = nullptr, *ATT = nullptr, *GU = nullptr, *FF = nullptr, *PROJ = nullptr;
     int8_t* XQ = nullptr;
     float* XD = nullptr;
+    // Single GPU: consecutive chunks of a prefill call alternate between two
+    // buffer sets and two streams, so chunk c + 1 runs one layer behind chunk
+    // c and its kernels fill the SMs chunk c's kernels leave idle.  Chunk
+    // c + 1's layer-l attention reads chunk c's layer-l K/V: it waits for
+    // pf_ev[c % 2][l], recorded after chunk c's layer-l KV append.
+    struct PfSet {
+        float *X = nullptr, *N = nullptr, *QKV = nullptr, *ATT = nullptr, *GU = nullptr, *FF = nullptr,
+              *PROJ = nullptr;
+        int8_t* XQ = nullptr;
+        float* XD = nullptr;
+        cudaStream_t stream = nullptr;
+    } pf_alt;
+    std::vector<cudaEvent_t> pf_ev[2];
+    const std::vector<cudaEvent_t>* pf_wait = nullptr;  // the previous chunk's events (nullptr: first chunk)
+    const std::vector<cudaEvent_t>* pf_rec = nullptr;   // this chunk's events
+    cudaEvent_t pf_join = nullptr;                      // main stream <-> alternate stream
     // token ids / positions / context lengths of a whole prefill call
     uint64_t in_cap = 0;
     int32_t *pf_tok = nullptr, *pf_pos = nullptr, *pf_ctx = nullptr;
@@ -544,6 +560,26 @@ void ensure_prefill(mv_model_s* m, uint64_t B) {
     }
     m->XQ = dalloc<int8_t>(m, B * K);
     m->XD = dalloc<float>(m, 2 * mvb::gemm_tc_ldb(B) * K / 32);  // block-major scales + constants
+    if (!tp) {
+        auto& a = m->pf_alt;
+        a.X = dalloc<float>(m, B * D);
+        a.N = dalloc<float>(m, B * D);
+        a.QKV = dalloc<float>(m, B * m->qkvw);
+        a.ATT = dalloc<float>(m, B * D);
+        a.GU = dalloc<float>(m, B * 2 * m->Fl);
+        a.FF = dalloc<float>(m, B * F);
+        a.PROJ = dalloc<float>(m, B * D);
+        a.XQ = dalloc<int8_t>(m, B * K);
+        a.XD = dalloc<float>(m, 2 * mvb::gemm_tc_ldb(B) * K / 32);
+        if (!a.stream) ck(cudaStreamCreateWithFlags(&a.stream, cudaStreamNonBlocking), "cudaStreamCreate(prefill)");
+        if (!m->pf_join) ck(cudaEventCreateWithFlags(&m->pf_join, cudaEventDisableTiming), "cudaEventCreate(prefill)");
+        for (auto& v : m->pf_ev)
+            while (v.size() < m->n_layer) {
+                cudaEvent_t e;
+                ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate(prefill)");
+                v.push_back(e);
+            }
+    }
     if (B > m->table_rows) {
         std::vector<int32_t> t(B * m->n_pages);
         for (uint64_t r = 0; r < B; ++r)
@@ -584,17 +620,21 @@ void project_decode(mv_model_s* m, mv_weight_s* w, const float* x, const float* 
     }
 }
 
-void rope_append(mv_model_s* m, const mvb::Layer& L, float* qkv, uint64_t rows, const int32_t* pos, int32_t* ctx_out) {
+// plain = true: a full-order launch, for a launch right after an event wait
+// (the attention after it, a PDL launch, relies on this kernel's completion
+// implying the event's).
+void rope_append(mv_model_s* m, const mvb::Layer& L, float* qkv, uint64_t rows, const int32_t* pos, int32_t* ctx_out,
+                 bool plain = false) {
     const uint64_t QKVW = m->qkvw;  // this rank's heads
     cudaError_t e;
     if (m->kv_type == MV_KV_Q8) {
-        e = mvb::launch_pdl(mvb::rope_append_row_kernel, dim3((unsigned)rows), dim3(256), 0, m->stream, qkv, (int)QKVW,
+        e = mvb::launch_opt(!plain, mvb::rope_append_row_kernel, dim3((unsigned)rows), dim3(256), 0, m->stream, qkv, (int)QKVW,
                             (int)m->nh, (int)m->nkv, (int)m->hd, (const float*)m->rope_cos,
                             (const float*)m->rope_sin, pos, m->kv_type, (const int32_t*)m->table, (int)m->page,
                             L.k_pages, L.v_pages, L.k_scales, L.v_scales, ctx_out);
     } else {
         const int threads = m->kv_type == MV_KV_Q8_0 ? (int)std::max<uint64_t>(64, m->hd) : (int)(m->hd / 2);
-        e = mvb::launch_pdl(mvb::rope_append_heads_kernel,
+        e = mvb::launch_opt(!plain, mvb::rope_append_heads_kernel,
                             dim3((unsigned)rows, (unsigned)(m->nh + 2 * m->nkv)), dim3(threads), 0,
                             m->stream, qkv, (int)QKVW, (int)m->nh, (int)m->nkv, (int)m->hd,
                             (const float*)m->rope_cos, (const float*)m->rope_sin, pos, m->kv_type,
@@ -940,6 +980,13 @@ void free_model(mv_model_s* m) {
     for (void* p : m->allocs) cudaFree(p);
     if (m->logits_host) cudaFreeHost(m->logits_host);
     if (m->pf_host) cudaFreeHost(m->pf_host);
+    if (m->pf_alt.stream) {
+        cudaStreamSynchronize(m->pf_alt.stream);
+        cudaStreamDestroy(m->pf_alt.stream);
+    }
+    for (auto& v : m->pf_ev)
+        for (cudaEvent_t e : v) cudaEventDestroy(e);
+    if (m->pf_join) cudaEventDestroy(m->pf_join);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -980,6 +1027,29 @@ void check_tp_status(const mv_model_s* m) {
 }
 
 // One chunk of B tokens; `off` indexes the call's staged inputs.
+// Swaps the model's prefill buffers and stream with the alternate set (and
+// back, on leaving the scope), so prefill_chunk runs a chunk on the other set.
+struct AltSet {
+    mv_model_s* m;
+    bool on;
+    AltSet(mv_model_s* m_, bool on_) : m(m_), on(on_) { flip(); }
+    ~AltSet() { flip(); }
+    void flip() {
+        if (!on) return;
+        auto& a = m->pf_alt;
+        std::swap(m->X, a.X);
+        std::swap(m->N, a.N);
+        std::swap(m->QKV, a.QKV);
+        std::swap(m->ATT, a.ATT);
+        std::swap(m->GU, a.GU);
+        std::swap(m->FF, a.FF);
+        std::swap(m->PROJ, a.PROJ);
+        std::swap(m->XQ, a.XQ);
+        std::swap(m->XD, a.XD);
+        std::swap(m->stream, a.stream);
+    }
+};
+
 void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     cudaStream_t s = m->stream;
     const uint64_t D = m->n_embd, F = m->n_ff;
@@ -1025,7 +1095,9 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     for (uint64_t l = 0; l < m->n_layer; ++l) {
         auto& L = m->layers[l];
         project_normed(L.qkv, L.attn_norm, m->QKV);
-        rope_append(m, L, m->QKV, B, pos, nullptr);
+        if (m->pf_wait) ck(cudaStreamWaitEvent(s, (*m->pf_wait)[l], 0), "wait (previous chunk's KV)");
+        rope_append(m, L, m->QKV, B, pos, nullptr, m->pf_wait != nullptr);
+        if (m->pf_rec) ck(cudaEventRecord((*m->pf_rec)[l], s), "record (this chunk's KV)");
         mvb::AttnArgs aa = attn_args(m, L, m->QKV, m->qkvw, B, ctx, start + B, tp ? m->ATT_l : m->ATT);
         aa.one_seq = 1;
         // single GPU, tensor-core o projection: the attention kernel also
@@ -1255,9 +1327,24 @@ MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uin
         ck(cudaStreamSynchronize(m->stream), "sync");
         ensure_prefill(m, std::min(B, n));
         stage_prefill_inputs(m, tokens, n);
-        for (uint64_t i = 0; i < n; i += B) {
+        // single GPU, several chunks: odd chunks on the alternate buffers and
+        // stream, one layer behind the chunk before them
+        const bool wave = m->tp_world == 1 && m->pf_alt.stream && n > B;
+        if (wave) {
+            ck(cudaEventRecord(m->pf_join, m->stream), "record (prefill start)");
+            ck(cudaStreamWaitEvent(m->pf_alt.stream, m->pf_join, 0), "wait (prefill start)");
+        }
+        for (uint64_t i = 0, c = 0; i < n; i += B, ++c) {
             const uint64_t nb = std::min(B, n - i);
+            m->pf_wait = wave && c ? &m->pf_ev[(c - 1) & 1] : nullptr;
+            m->pf_rec = wave ? &m->pf_ev[c & 1] : nullptr;
+            AltSet alt(m, wave && (c & 1));
             prefill_chunk(m, i, nb, compute_logits && i + nb == n);
+        }
+        m->pf_wait = m->pf_rec = nullptr;
+        if (wave) {
+            ck(cudaEventRecord(m->pf_join, m->pf_alt.stream), "record (prefill end)");
+            ck(cudaStreamWaitEvent(m->stream, m->pf_join, 0), "wait (prefill end)");
         }
         if (compute_logits)
             ck(cudaMemcpyAsync(m->logits_host, m->logits, m->vocab * 4, cudaMemcpyDeviceToHost, m->stream), "logits D2H");

@@ -183,17 +183,19 @@ def _sms():
 
 
 @pytest.mark.parametrize("tile,cols", [("n8", 160), ("n8", 672), ("n16", 160), ("n16", 672), ("n32", 4096),
-                                       ("n32b", 672), ("n32b", 1056)])
+                                       ("n32b", 672), ("n32b", 1056), ("split", 672), ("split", 4096)])
 def test_tc_gemm_tile_widths_bit_exact(cuda, oracle, tile, cols):
     """Every tile width of the tensor-core GEMM (8 tokens on a 16-wide MMA,
     16 and 32 tokens), with block counts that end in a partial pipeline stage
     (nb = 5, 21, 33) and partial row and token tiles; bit-exact against the
     FORCE_Q8 chain.  The shapes make the launcher's wave model pick the width:
     8 tokens for few row tiles (n8), 16 for a little over one row tile per SM
-    (n16), 32 for one row tile per SM at 32 and 128 tokens (n32, n32b)."""
+    (n16), 32 for one row tile per SM at 32 and 128 tokens (n32, n32b), and
+    for a single token tile over more row tiles than SMs two launches: one
+    32-token tile per SM, then the remaining rows in 8-token tiles (split)."""
     sms = _sms()
     rows, batch = {"n8": (300, 70), "n16": (128 * sms + 200, 70), "n32": (128 * sms, 32),
-                   "n32b": (128 * sms - 5, 128)}[tile]
+                   "n32b": (128 * sms - 5, 128), "split": (128 * sms + 200, 20)}[tile]
     rng = np.random.default_rng(cols + batch)
     w = gguf.gen_q4_0(rows, cols, rng)
     X = rng.standard_normal((batch, cols)).astype(np.float32)

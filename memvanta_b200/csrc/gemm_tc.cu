@@ -45,7 +45,12 @@
 //   sc   [2][16][N]             the activation scales and the constants c
 //                               (block-major [nb][ldb] each, tokens padded to 64)
 //
-// Warp roles (one CTA per SM, persistent over 128-row x N-token tiles):
+// Tiles: 128 rows x NE tokens, NE <= N (the epilogue reads the first NE
+// columns of each N-wide slot; NE = 8 on N = 16 puts twice the CTAs on a
+// narrow weight).  The launcher picks NE per weight and batch, and splits a
+// weight with more row tiles than SMs into two launches (gemm_q4_q8_tc).
+//
+// Warp roles (one CTA per SM, persistent over its tiles):
 //   warp 0       TMA producer (one lane): stages and epilogue data
 //   warps 1-3    MMA issuers (one lane each, stages round-robin: an issuing
 //                thread spends ~60 cycles per MMA and more on its waits and

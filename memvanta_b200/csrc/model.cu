@@ -1334,12 +1334,21 @@ MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uin
             ck(cudaEventRecord(m->pf_join, m->stream), "record (prefill start)");
             ck(cudaStreamWaitEvent(m->pf_alt.stream, m->pf_join, 0), "wait (prefill start)");
         }
-        for (uint64_t i = 0, c = 0; i < n; i += B, ++c) {
-            const uint64_t nb = std::min(B, n - i);
-            m->pf_wait = wave && c ? &m->pf_ev[(c - 1) & 1] : nullptr;
-            m->pf_rec = wave ? &m->pf_ev[c & 1] : nullptr;
-            AltSet alt(m, wave && (c & 1));
-            prefill_chunk(m, i, nb, compute_logits && i + nb == n);
+        try {
+            for (uint64_t i = 0, c = 0; i < n; i += B, ++c) {
+                const uint64_t nb = std::min(B, n - i);
+                m->pf_wait = wave && c ? &m->pf_ev[(c - 1) & 1] : nullptr;
+                m->pf_rec = wave ? &m->pf_ev[c & 1] : nullptr;
+                AltSet alt(m, wave && (c & 1));
+                prefill_chunk(m, i, nb, compute_logits && i + nb == n);
+            }
+        } catch (...) {
+            // an error part-way: nothing of this call may still run on the
+            // alternate stream when the caller goes on (its next call restages
+            // the inputs this call's chunks read)
+            m->pf_wait = m->pf_rec = nullptr;
+            if (wave) cudaStreamSynchronize(m->pf_alt.stream);
+            throw;
         }
         m->pf_wait = m->pf_rec = nullptr;
         if (wave) {

@@ -144,3 +144,23 @@ def test_model_errors(cuda, tmp):
         f.write(b"GGUF" + bytes(20))
     with pytest.raises(mv.MemVantaError):
         mv.LlamaModel(bad)
+
+
+def test_cuda_llama_model_binding_matches_reference(cuda, tmp):
+    """memvanta::CudaLlamaModel -- the C++ binding with LlamaModel's public
+    interface (memvanta_b200/bindings/llama_model_cuda.cpp) -- against the
+    reference's own LlamaModel in one C++ process (oracle/_ref/binding_check,
+    built from the reference sources): prefill logits within the bar,
+    identical greedy tokens from generate(), equal position() and
+    kv_bytes_allocated()."""
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = os.path.join(root, "oracle", "_ref", "binding_check")
+    if not os.path.exists(exe):
+        pytest.skip("oracle/_ref/binding_check is built only where the reference sources are present")
+    shape = gguf.LlamaShape(n_layer=2, n_embd=256, n_head=4, n_head_kv=4, n_ff=512, vocab=512, n_ctx=256,
+                            rms_eps=1e-6, rope_theta=10000.0)
+    path = os.path.join(tmp, "binding.gguf")
+    gguf.write_random_llama(path, shape, seed=3)
+    r = subprocess.run([exe, path, str(shape.vocab)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "equal 1" in r.stdout, r.stdout + r.stderr

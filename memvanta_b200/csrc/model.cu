@@ -1026,7 +1026,6 @@ void check_tp_status(const mv_model_s* m) {
                                              std::to_string(*m->tp_status_host) + ")");
 }
 
-// One chunk of B tokens; `off` indexes the call's staged inputs.
 // Swaps the model's prefill buffers and stream with the alternate set (and
 // back, on leaving the scope), so prefill_chunk runs a chunk on the other set.
 struct AltSet {
@@ -1050,6 +1049,7 @@ struct AltSet {
     }
 };
 
+// One chunk of B tokens; `off` indexes the call's staged inputs.
 void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     cudaStream_t s = m->stream;
     const uint64_t D = m->n_embd, F = m->n_ff;

@@ -628,8 +628,8 @@ void rope_append(mv_model_s* m, const mvb::Layer& L, float* qkv, uint64_t rows, 
     const uint64_t QKVW = m->qkvw;  // this rank's heads
     cudaError_t e;
     if (m->kv_type == MV_KV_Q8) {
-        e = mvb::launch_opt(!plain, mvb::rope_append_row_kernel, dim3((unsigned)rows), dim3(256), 0, m->stream, qkv, (int)QKVW,
-                            (int)m->nh, (int)m->nkv, (int)m->hd, (const float*)m->rope_cos,
+        e = mvb::launch_opt(!plain, mvb::rope_append_row_kernel, dim3((unsigned)rows), dim3(256), 0, m->stream, qkv,
+                            (int)QKVW, (int)m->nh, (int)m->nkv, (int)m->hd, (const float*)m->rope_cos,
                             (const float*)m->rope_sin, pos, m->kv_type, (const int32_t*)m->table, (int)m->page,
                             L.k_pages, L.v_pages, L.k_scales, L.v_scales, ctx_out);
     } else {

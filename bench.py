@@ -391,10 +391,15 @@ def run_llama7b_ours(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     t0 = time.perf_counter()
-    cur = 17
+    cur, e2e_toks = 17, []
     for _ in range(K):
         cur = int(np.argmax(m.forward(cur)))
+        e2e_toks.append(cur)
     e2e_s = all_max(time.perf_counter() - t0, world)
+    # the timed device-side greedy loop and the host-argmax forward loop
+    # decode the same sequence from the same state: their tokens must agree
+    if [int(t) for t in toks] != e2e_toks:
+        raise RuntimeError(f"generate_greedy tokens {list(toks[:8])} differ from the forward loop's {e2e_toks[:8]}")
     # embed; per layer q|k|v GEMV, fused RoPE+append+attention, o, gate|up, down;
     # output RMSNorm + Q6_K head GEMV + greedy step; tensor parallel adds the
     # wait before the head, the logits scatter, its wait and the step counter
@@ -403,10 +408,43 @@ def run_llama7b_ours(args, world, rank, local):
     gbs, alg_bytes, gemv_s, detail = gemv_roofline(dev, torch.cuda.Stream(device=dev), world)
     return {"tg_ms": tg_ms, "pp_ms": pp_ms, "e2e_s": e2e_s, "clocks": clk.summary(), "load_s": load_s,
             "gpu_launches": K * kernels_per_step + 1, "first_tokens": [int(t) for t in toks[:8]],
-            "gemv_gbs": gbs, "gemv_detail": detail}
+            "distinct_tokens": len(set(int(t) for t in toks)), "gemv_gbs": gbs, "gemv_detail": detail}
 
 
-def run_llama7b_cpu(threads=None, prompt=32, gen=8):
+def other_configs():
+    """BASELINE.json configs 0, 1, 2 and 4 on this GPU, one live timing each
+    (time_matmul / time_paged_attn): the headline line carries them as
+    extra keys."""
+    out = {}
+    c0 = time_matmul("gemv", "q4_0", 4096, 4096)
+    out["config0_q4_0_gemv_4096x4096"] = {"us": c0["us_per_launch"], "gbs": c0["value"], "hbm_frac": c0["hbm_frac"]}
+    c1 = {}
+    for name, rows, cols in (("gate_11008x4096", 11008, 4096), ("down_4096x11008", 4096, 11008)):
+        for B in (32, 128, 512):
+            r = time_matmul("gemm", "q4_0", rows, cols, B)
+            c1[f"{name}_b{B}"] = {"us": r["us_per_launch"], "tops": r["value"],
+                                  "int8_frac_of_nominal": r["int8_frac_of_nominal"],
+                                  "weight_stream_gbs": r["weight_stream_gbs"], "hbm_frac": r["hbm_frac"]}
+    out["config1_q4_0_gemm"] = c1
+    out["config1_int8_peak_tops"] = {"value": INT8_NOMINAL_TOPS, "source": "nominal dense int8 (no measured figure)"}
+    c2 = {}
+    for name, wt, rows in (("q8_0_4096x4096", "q8_0", 4096), ("q6_k_32000x4096", "q6_k", 32000)):
+        r = time_matmul("gemv", wt, rows, 4096)
+        c2[f"{name}_b1"] = {"us": r["us_per_launch"], "gbs": r["value"], "hbm_frac": r["hbm_frac"]}
+        r = time_matmul("gemm", wt, rows, 4096, 32)
+        c2[f"{name}_b32"] = {"us": r["us_per_launch"], "weight_stream_gbs": r["weight_stream_gbs"],
+                             "hbm_frac": r["hbm_frac"]}
+    out["config2_mixed_quant"] = c2
+    c4 = {}
+    for kv in ("f16", "q8_0"):
+        r = time_paged_attn(kv)
+        c4[kv] = {"us": r["us_per_launch"], "gbs": r["value"], "hbm_frac": r["frac_of_measured_hbm"],
+                  "sum_ctx": r["sum_ctx"]}
+    out["config4_paged_attention"] = c4
+    return out
+
+
+def run_llama7b_cpu(threads=None, prompt=512, gen=16):
     """The reference's own memvanta_real_bench (oracle/_ref, built from the
     unmodified sources) on this host's cores: pp<prompt> and tg<gen> tok/s."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -559,23 +597,39 @@ def main_micro(args):
         return
     if args.workload == "paged_attn":
         return main_paged_attn(args, mv, dev)
-    rows, cols, B = args.rows, args.cols, args.batch
+    line = time_matmul(args.workload, args.wtype, args.rows, args.cols, args.batch, args.steps, args.warmup)
+    print(json.dumps(line), flush=True)
+
+
+INT8_NOMINAL_TOPS = 4500.0  # dense int8 tensor peak, nominal (NVIDIA's figure without sparsity)
+
+
+def time_matmul(kind, wtype, rows, cols, B=1, steps=32, warmup=3):
+    """Live time of one decode GEMV (kind "gemv") or batched matmul ("gemm":
+    Q8 quantisation of X included, tensor_matmul_batch_v06's dispatch) on a
+    rows x cols weight of `wtype`.  Weights rotate through copies larger than
+    3x L2; launches are replayed from a CUDA graph and timed with events on
+    the launching stream."""
+    import torch
+    import memvanta_b200 as mv
+    from memvanta_b200 import gguf
+    dev = torch.device("cuda", torch.cuda.current_device())
     rng = np.random.default_rng(7)
-    wt = {"q4_0": gguf.Q4_0, "q8_0": gguf.Q8_0, "q6_k": gguf.Q6_K}[args.wtype]
+    wt = {"q4_0": gguf.Q4_0, "q8_0": gguf.Q8_0, "q6_k": gguf.Q6_K}[wtype]
     wbytes = gguf.tensor_nbytes(wt, rows * cols)
     copies = max(2, int(np.ceil(3 * 126e6 / wbytes)))
     ws = [mv.Weight.upload(gguf.gen_blocks(wt, rows, cols, rng), wt, rows, cols) for _ in range(copies)]
     act = mv.ACT_Q8 if wt == gguf.Q4_0 else mv.ACT_F32  # tensor_matmul_batch_v06's dispatch
-    n = max(args.steps, copies)
+    n = max(steps, copies)
     stream = torch.cuda.Stream(device=dev)
-    if args.workload == "gemv":
+    if kind == "gemv":
         x, y = torch.randn(cols, device=dev), torch.empty(rows, device=dev)
         launch = lambda w: mv.gemv(w, x, y, stream)  # noqa: E731
     else:
         x, y = torch.randn(B, cols, device=dev), torch.empty(B, rows, device=dev)
         launch = lambda w: mv.gemm(w, x, y, act, stream)  # noqa: E731
     with torch.cuda.stream(stream):
-        for i in range(max(args.warmup, 1)):
+        for i in range(max(warmup, 1)):
             launch(ws[i % copies])
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
@@ -591,30 +645,42 @@ def main_micro(args):
         torch.cuda.synchronize()
     mv.stream_status(stream)
     us = e0.elapsed_time(e1) * 1e3 / n
-    line = {"workload": args.workload, "wtype": args.wtype, "rows": rows, "cols": cols, "us_per_launch": round(us, 3),
+    del g
+    for w in ws:
+        w.free()
+    line = {"workload": kind, "wtype": wtype, "rows": rows, "cols": cols, "us_per_launch": round(us, 3),
             "launches": n}
     peak = measured_peaks()["hbm_gbs"]
-    if args.workload == "gemv":
+    if kind == "gemv":
         alg = wbytes + cols * 4 + rows * 4
-        line.update({"metric": f"{args.wtype} GEMV achieved GB/s", "value": round(alg / us / 1e3, 1), "unit": "GB/s",
+        line.update({"metric": f"{wtype} GEMV achieved GB/s", "value": round(alg / us / 1e3, 1), "unit": "GB/s",
                      "algorithmic_bytes_per_launch": alg, "hbm_frac": round(alg / us / 1e3 / peak, 4)})
     else:
         alg = wbytes + B * cols * 4 + B * rows * 4
-        line.update({"batch": B, "metric": f"{args.wtype} GEMM TOPS (2*rows*cols*batch / time"
+        tops = 2 * rows * cols * B / us / 1e6
+        line.update({"batch": B, "metric": f"{wtype} GEMM TOPS (2*rows*cols*batch / time"
                                            + (", Q8 quantisation included)" if wt == gguf.Q4_0 else ", fp32 x)"),
-                     "value": round(2 * rows * cols * B / us / 1e6, 2), "unit": "TOPS",
+                     "value": round(tops, 2), "unit": "TOPS",
                      "weight_stream_gbs": round(alg / us / 1e3, 1), "hbm_frac": round(alg / us / 1e3 / peak, 4)})
-    print(json.dumps(line), flush=True)
+        if wt == gguf.Q4_0:
+            line["int8_frac_of_nominal"] = round(tops / INT8_NOMINAL_TOPS, 4)
+    return line
 
 
 def main_paged_attn(args, mv, dev):
+    print(json.dumps(time_paged_attn(args.kv, args.steps, args.warmup)), flush=True)
+
+
+def time_paged_attn(kv="f16", steps=32, warmup=3):
     """Config 4: paged decode attention over 64 sequences, ctx ~ U(64..768),
     16-token pages scattered by a random permutation block table, 32 heads x
     128, Q/K/V ~ N(0,1) (random fp16 pages; Q8_0 pages with random int8 and
     scales for --kv q8_0).  The cache (~436 MB F16) is larger than L2, so every
     launch reads it from HBM.  One launch per step, replayed from a graph."""
     import torch
-    kv_type = {"f16": mv.KV_F16, "q8_0": mv.KV_Q8_0}[args.kv]
+    import memvanta_b200 as mv
+    dev = torch.device("cuda", torch.cuda.current_device())
+    kv_type = {"f16": mv.KV_F16, "q8_0": mv.KV_Q8_0}[kv]
     rng = np.random.default_rng(4)
     n_seq, n_head, hd, page = 64, 32, 128, 16
     kv_dim = n_head * hd
@@ -646,12 +712,12 @@ def main_paged_attn(args, mv, dev):
     call = lambda: mv.paged_attn_decode(kv_type, q, n_head, n_head, hd, kp, vp, tab, max_pages, page, ctx_t,  # noqa: E731
                                         int(ctx.max()), ks, vs, out, stream)
     with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 1)):
+        for _ in range(max(warmup, 1)):
             call()
         torch.cuda.synchronize()
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr, stream=stream):
-            for _ in range(args.steps):
+            for _ in range(steps):
                 call()
         gr.replay()
         torch.cuda.synchronize()
@@ -660,14 +726,15 @@ def main_paged_attn(args, mv, dev):
         gr.replay()
         e1.record(stream)
         torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    del gr
     row_bytes = mv.kv_row_bytes(kv_type, kv_dim) + 4 * mv.kv_row_scales(kv_type, kv_dim)
     alg = int(ctx.sum()) * 2 * row_bytes + 2 * n_seq * kv_dim * 4  # K and V of every context token, Q in, O out
-    print(json.dumps({"workload": "paged_attn", "kv": args.kv, "config": "config4: 64 seqs, ctx U(64..768), 16-token "
-                      "pages, random permutation block table, 32 heads x 128", "sum_ctx": int(ctx.sum()),
-                      "us_per_launch": round(us, 2), "metric": "paged attention achieved GB/s",
-                      "value": round(alg / us / 1e3, 1), "unit": "GB/s", "algorithmic_bytes_per_launch": alg,
-                      "frac_of_measured_hbm": round(alg / us / 1e3 / measured_peaks()["hbm_gbs"], 3)}), flush=True)
+    return {"workload": "paged_attn", "kv": kv, "config": "config4: 64 seqs, ctx U(64..768), 16-token "
+            "pages, random permutation block table, 32 heads x 128", "sum_ctx": int(ctx.sum()),
+            "us_per_launch": round(us, 2), "metric": "paged attention achieved GB/s",
+            "value": round(alg / us / 1e3, 1), "unit": "GB/s", "algorithmic_bytes_per_launch": alg,
+            "frac_of_measured_hbm": round(alg / us / 1e3 / measured_peaks()["hbm_gbs"], 3)}
 
 
 def main_llama7b(args, world, rank, local):
@@ -682,7 +749,9 @@ def main_llama7b(args, world, rank, local):
     if args.impl == "reference":
         if rank != 0:
             return
-        cpu = run_llama7b_cpu()
+        # the same workload as our arm: pp512 in batches of 32, then K = --steps
+        # greedy decode tokens after the reference bench's 128-token seed prefill
+        cpu = run_llama7b_cpu(prompt=L7_PP, gen=args.steps)
         line = {"impl": "reference", "metric": metric, "value": cpu["tg"], "unit": unit, "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "q4_0/q8",
                 "data": "synthetic", "config": config, "pp_tok_s": cpu["pp"],
@@ -703,6 +772,7 @@ def main_llama7b(args, world, rank, local):
         dist.destroy_process_group()
     if rank != 0:
         return
+    extra = other_configs() if world == 1 else {}
     peaks = measured_peaks()
     cpu = None
     if world == 1:
@@ -736,8 +806,10 @@ def main_llama7b(args, world, rank, local):
                 "d2h_bytes_per_step": 32000 * 4,
                 "path": "LlamaModel.forward (mv_model_forward): token in, host logits out, host argmax per token"},
         "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["gpu_launches"],
-        "first_tokens": r["first_tokens"],
+        "first_tokens": r["first_tokens"], "distinct_tokens": r["distinct_tokens"],
+        "greedy_check": "generate_greedy tokens == forward-loop (host argmax) tokens",
     }
+    line.update(extra)
     print(json.dumps(line), flush=True)
 
 

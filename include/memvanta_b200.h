@@ -68,6 +68,10 @@ typedef struct mv_model_s* mv_model_t;
 MV_API int mv_init(int device);
 MV_API const char* mv_last_error(void);
 MV_API int mv_version(void);
+/* Architecture of the device code the library loaded on the current device,
+ * as cudaFuncGetAttributes' binaryVersion (100 = sm_100).  No counterpart in
+ * the reference; lets a caller or a test check the build at run time. */
+MV_API int mv_binary_arch(int* out);
 /* Synchronises `stream` and reports MV_ERR_TIMEOUT if a tensor-core kernel
  * (mv_gemm with MV_ACT_Q8, model prefill) gave up a bounded device-side wait
  * since the last check -- its outputs are then invalid.  Host-pointer calls
@@ -114,12 +118,14 @@ MV_API int mv_gemm(mv_weight_t w, const float* x_dev, uint64_t batch, float* y_d
  * run (a framework whose own pool owns all GPU memory, a fixed memory budget,
  * a latency-critical loop).  No counterpart in the reference.  The quantised
  * activations go to one 8 MiB array compiled into the library, held on every
- * GPU that loads it until the process exits, so batch * cols bytes of int8
- * values plus (cols / 32) * round_up(batch, 64) * 8 bytes of scales must fit
- * in 8 MiB (larger calls return MV_ERR_INVALID).  The first call on a
- * device looks the array's address up (cudaGetSymbolAddress): make it before
- * any stream capture.  Calls that overlap on the GPU share the array and race;
- * the caller serialises them.  Allocates nothing, frees nothing. */
+ * GPU that loads it until the process exits, so round_up(batch * cols, 256)
+ * bytes of int8 values plus (cols / 32) * round_up(batch, 64) * 8 bytes of
+ * scales and GEMM constants must fit in 8 MiB (larger calls return
+ * MV_ERR_INVALID).  The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress) and keeps it for the process: make that call before
+ * any stream capture, and do not reset the device (cudaDeviceReset) after it.
+ * Calls that overlap on the GPU share the array and race; the caller
+ * serialises them.  Allocates nothing, frees nothing. */
 MV_API int mv_gemm_q8_noalloc(mv_weight_t w, const float* x_dev, uint64_t batch, float* y_dev, void* stream);
 
 /* Per-row Q8 activation quantisation: q[rows*cols] int8, d[rows*cols/32] fp32.

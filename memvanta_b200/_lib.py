@@ -30,6 +30,7 @@ SIGNATURES = {
     "mv_init": (_i, [_i]),
     "mv_last_error": (C.c_char_p, []),
     "mv_version": (_i, []),
+    "mv_binary_arch": (_i, [C.POINTER(_i)]),
     "mv_stream_status": (_i, [_p]),
     "mv_weight_upload": (_i, [_p, _u64, _i, _u64, _u64, _p, C.POINTER(_p)]),
     "mv_weight_from_device": (_i, [_p, _u64, _i, _u64, _u64, _p, C.POINTER(_p)]),

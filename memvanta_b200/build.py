@@ -18,7 +18,13 @@ def build_lib(jobs: int = 8) -> str:
     return os.path.join(HERE, "libmemvanta_b200.so")
 
 
-def build_oracle(ref_root: str = "/root/reference", jobs: int = 8) -> None:
+# Checkout of the reference sources the oracle's reference build compiles
+# (test infrastructure only); MV_REFERENCE_DIR overrides the default.
+REF_ROOT = os.environ.get("MV_REFERENCE_DIR", "/root/reference")
+
+
+def build_oracle(ref_root: str | None = None, jobs: int = 8) -> None:
+    ref_root = ref_root or REF_ROOT
     args = ["make", "-s", f"-j{jobs}", "-C", os.path.join(ROOT, "oracle")]
     if os.path.isdir(ref_root):
         args.append(f"REF={ref_root}")

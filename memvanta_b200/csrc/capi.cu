@@ -207,6 +207,19 @@ extern "C" {
 MV_API const char* mv_last_error(void) { return g_err.c_str(); }
 MV_API int mv_version(void) { return 1; }
 
+namespace {
+// An empty kernel whose attributes stand for the library's device code.
+__global__ void arch_probe_kernel() {}
+}  // namespace
+
+MV_API int mv_binary_arch(int* out) {
+    if (!out) return fail(MV_ERR_INVALID, "null output");
+    cudaFuncAttributes a{};
+    CK(cudaFuncGetAttributes(&a, arch_probe_kernel));
+    *out = a.binaryVersion;
+    return MV_OK;
+}
+
 MV_API int mv_init(int device) {
     int n = 0;
     CK(cudaGetDeviceCount(&n));

@@ -194,7 +194,12 @@ GgufReader::GgufReader(const std::string& path) {
         if (get_u64("general.alignment", a)) align = a;
         if (!align || (align & (align - 1))) throw std::runtime_error("invalid GGUF alignment");
         const uint64_t data_start = (c.pos() + align - 1) & ~(align - 1);
+        // a huge alignment wraps the rounding
+        if (data_start < c.pos()) throw std::runtime_error("invalid GGUF alignment");
         for (auto& r : raw) {
+            // checked before the add: a relative offset near 2^64 would wrap
+            if (data_start > size_ || r.rel > size_ - data_start)
+                throw std::runtime_error("tensor out of file bounds: " + r.info.name);
             r.info.offset = data_start + r.rel;
             r.info.nbytes = ggml_nbytes(r.info.type, r.info.elements());
             if (r.info.offset > size_ || r.info.nbytes > size_ - r.info.offset)

@@ -15,7 +15,8 @@
 // its name is only a host-side stand-in, so its device address is looked up
 // with cudaGetSymbolAddress once per device, with that device current, on the
 // first call made on that device; make that first call before any stream
-// capture.  All calls share the one array: calls whose work overlaps on the
+// capture.  The address is kept for the life of the process, so the device
+// must not be reset (cudaDeviceReset) after that first call.  All calls share the one array: calls whose work overlaps on the
 // GPU (other streams, other threads) race on it and must be serialised by the
 // caller.  Nothing needs clearing between calls -- each call writes every
 // scratch byte it later reads.

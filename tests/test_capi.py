@@ -1,12 +1,14 @@
 """CPU-side checks of the C ABI and host logic (no device calls)."""
 from __future__ import annotations
 
+import ctypes as C
 import os
 import re
 import subprocess
 import tempfile
 
 import numpy as np
+import pytest
 
 from memvanta_b200 import _lib, gguf
 
@@ -40,10 +42,22 @@ def test_python_signatures_cover_header():
     assert set(declared_symbols()) == set(_lib.SIGNATURES)
 
 
-def test_library_is_sm100a_only():
-    out = subprocess.run(["cuobjdump", "--list-elf", _lib.LIB_PATH], capture_output=True, text=True).stdout
-    arches = set(re.findall(r"sm_(\d+a?)", out))
-    assert arches == {"100a"}, arches
+def test_library_is_built_for_sm100a_only():
+    """The build names one target, sm_100a, in every compile and the link."""
+    mk = open(os.path.join(os.path.dirname(_lib.LIB_PATH), "csrc", "Makefile")).read()
+    arch = re.search(r"^ARCH := (.*)$", mk, re.M).group(1).strip()
+    assert arch == "-gencode arch=compute_100a,code=sm_100a"
+    assert "-gencode" not in mk.replace(arch, "")
+    assert "$(NVCC) $(NVFLAGS) -c" in mk and "$(NVCC) $(ARCH) -shared" in mk
+
+
+@pytest.mark.gpu
+def test_loaded_device_code_is_sm100(cuda):
+    """At run time the kernels the driver loaded are sm_100 code
+    (cudaFuncGetAttributes' binaryVersion, through mv_binary_arch)."""
+    v = C.c_int(0)
+    assert _lib.load().mv_binary_arch(C.byref(v)) == 0
+    assert v.value == 100
 
 
 def test_pure_host_entry_points():

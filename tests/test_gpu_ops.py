@@ -159,11 +159,20 @@ def test_config4_ragged_paged_attention(cuda, oracle, kv_type):
                      dev(table, cuda), max_pages, page, kp, vp, ks, vs, seq=seq)
     out = host(mv.paged_attn_decode(kv_type, dev(q, cuda), n_head, n_head_kv, hd, kp, vp, dev(table, cuda), max_pages,
                                     page, dev(ctx, cuda), int(ctx.max()), ks, vs))
-    # the oracle on a sample of sequences (it runs the reference loop per head)
-    for s in [0, 1, int(np.argmax(ctx)), int(np.argmin(ctx)), 37]:
+    # every sequence against the oracle (the reference loop per head).  The
+    # kernel keeps the reference's evaluation order; its exp is correctly
+    # rounded where the host libm's expf is within 0.502 ulp, and its double
+    # denominator is summed in a tree, so a rare last-bit difference of one
+    # weight remains: nearly every output is identical, none is off by more
+    # than a few ulps.
+    same = total = 0
+    for s in range(n_seq):
         okp, ovp, oks, ovs = _oracle_cache(oracle, kv_type, seqs_k[s], seqs_v[s], table[s], page, total_pages * page)
         want = oracle.attn_decode(kv_type, q[s], n_head, n_head_kv, hd, okp, ovp, oks, ovs, table[s], page, int(ctx[s]))
-        assert rel_err(out[s], want) <= 1e-4, (s, rel_err(out[s], want))
+        assert rel_err(out[s], want) <= 2e-6, (s, rel_err(out[s], want))
+        same += int(np.sum(out[s] == want))
+        total += want.size
+    assert same >= 0.99 * total, (same, total)
 
 
 @pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_Q8, mv.KV_Q8_0, mv.KV_F32])

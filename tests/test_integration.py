@@ -10,7 +10,7 @@ import tempfile
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = "/root/reference"
+REF = os.environ.get("MV_REFERENCE_DIR", "/root/reference")
 BINDING = os.path.join(ROOT, "memvanta_b200", "bindings", "gguf_kernels_cuda.cpp")
 
 

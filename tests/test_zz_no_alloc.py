@@ -1,10 +1,12 @@
 """mv_gemm_q8_noalloc: the Q8-activation batched matmul for callers that may
 not allocate device memory (a framework whose own pool owns the GPU's memory,
-a fixed memory budget, a latency-critical loop).  Its output must equal the
-allocating entry point's, mv_gemm(..., MV_ACT_Q8), on two calls in a row --
-the second call reuses the library's fixed scratch array the first one left
-behind.  This file is collected last so a failure here leaves every other
-test already run."""
+a fixed memory budget, a latency-critical loop).  Both entry points run the
+same bit-exact tensor-core GEMM on the same quantised activations, so its
+output must equal the allocating entry point's, mv_gemm(..., MV_ACT_Q8), bit
+for bit, on two calls in a row -- the second call reuses the library's fixed
+scratch array the first one left behind -- and equal the oracle's
+MEMVANTA_FORCE_Q8_ACT=1 matmul (tensor_matmul_batch_v06).  This file is
+collected last so a failure here leaves every other test already run."""
 from __future__ import annotations
 
 import ctypes as C
@@ -14,7 +16,6 @@ import pytest
 
 import memvanta_b200 as mv
 from memvanta_b200 import gguf
-from conftest import rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -25,25 +26,48 @@ def _noalloc(W, X, Y, stream):
                                   C.c_void_p(stream.cuda_stream))
 
 
+def _pool_reserved(dev):
+    """Bytes the device's default memory pool (cudaMallocAsync) holds."""
+    from cuda.bindings import runtime as rt
+    err, pool = rt.cudaDeviceGetDefaultMemPool(dev)
+    assert err == rt.cudaError_t.cudaSuccess
+    err, v = rt.cudaMemPoolGetAttribute(pool, rt.cudaMemPoolAttr.cudaMemPoolAttrReservedMemCurrent)
+    assert err == rt.cudaError_t.cudaSuccess
+    return int(v)
+
+
 @pytest.mark.parametrize("rows,cols,batch", [(11008, 4096, 32), (4096, 11008, 96), (64, 128, 3)])
-def test_noalloc_matches_mv_gemm_on_two_calls(cuda, rows, cols, batch):
+def test_noalloc_matches_mv_gemm_on_two_calls(cuda, oracle, rows, cols, batch):
     import torch
     rng = np.random.default_rng(rows + cols + batch)
-    W = mv.Weight.upload(gguf.gen_q4_0(rows, cols, rng), mv.Q4_0, rows, cols)
+    w = gguf.gen_q4_0(rows, cols, rng)
+    W = mv.Weight.upload(w, mv.Q4_0, rows, cols)
     stream = torch.cuda.current_stream()
     for call in range(2):
-        X = torch.from_numpy(rng.standard_normal((batch, cols)).astype(np.float32)).to(cuda)
+        x = rng.standard_normal((batch, cols)).astype(np.float32)
+        X = torch.from_numpy(x).to(cuda)
         want = torch.empty((batch, rows), dtype=torch.float32, device=cuda)
         mv.gemm(W, X, want, mv.ACT_Q8, stream)
-        torch.cuda.synchronize()
-        free_before = torch.cuda.mem_get_info()[0]
         got = torch.full((batch, rows), float("nan"), dtype=torch.float32, device=cuda)
+        torch.cuda.synchronize()
+        # mv_gemm's stream-ordered scratch went back to the pool: nothing the
+        # no-allocation call could take from it is held outside the pool, and
+        # the pool itself must not grow across the call
+        pool_before = _pool_reserved(cuda.index)
+        free_before = torch.cuda.mem_get_info()[0]
         rc = _noalloc(W, X, got, stream)
         assert rc == 0, mv.load().mv_last_error().decode()
         torch.cuda.synchronize()
+        assert _pool_reserved(cuda.index) == pool_before, call
         if call == 1:  # the first call on a device may load the module holding the array
             assert torch.cuda.mem_get_info()[0] == free_before
-        assert rel_err(got.cpu().numpy(), want.cpu().numpy()) <= 1e-3, call
+        g, r = got.cpu().numpy(), want.cpu().numpy()
+        assert np.array_equal(g, r), (call, float(np.nanmax(np.abs(g - r))))
+        if call == 0 and rows * cols <= 11008 * 4096 and batch >= 2:
+            # and both are the reference's FORCE_Q8 prefill matmul
+            ref = oracle.matmul_batch_v06(gguf.Q4_0, w, rows, cols, x, force_q8=True)
+            assert np.array_equal(g, ref.reshape(g.shape))
+    W.free()
 
 
 def test_noalloc_rejects_oversize_and_wrong_type(cuda):

@@ -69,6 +69,7 @@ SIGNATURES = {
     "mv_model_prefill": (_i, [_p, _p, _u64, _u64, _i, _p]),
     "mv_model_generate_greedy": (_i, [_p, C.c_int32, _u64, _p]),
     "mv_model_stream": (_p, [_p]),
+    "mv_model_decode_persistent": (_i, [_p]),
     "mv_int_quantize_q8_0": (_i, [_p, _u64, _p, _p]),
     "mv_int_quantize_q4_0": (_i, [_p, _u64, _p, _p]),
     "mv_int_matvec_q4_q8": (_i, [_p, _p, _p, _u64, _u64, _p]),

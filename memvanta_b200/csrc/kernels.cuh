@@ -172,4 +172,40 @@ cudaError_t tp_scatter_ll(const TpCtx& tp, const float* src, uint64_t n, uint64_
 uint64_t attn_fused_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type);
 cudaError_t attn_decode_fused(const AttnFusedArgs& a, cudaStream_t s);
 
+// ---- decode_mk.cu : every layer of one decode step as one persistent
+// (cooperative) kernel, one CTA per SM; one GPU, Q4_0 layer weights, F32/F16 KV
+struct MkGemv {                 // one Q4_0 weight in the planar layout (weights.cuh)
+    const uint8_t* qs;
+    const uint16_t* d;
+    int rows, nb, dstride;
+};
+struct MkLayer {
+    MkGemv w[4];                // q|k|v, o, gate|up (rows interleaved), down
+    const float* attn_norm;
+    const float* ffn_norm;
+    uint8_t* k_pages;
+    uint8_t* v_pages;
+};
+struct MkArgs {
+    const MkLayer* layers;      // device array [n_layer]
+    int n_layer, n_head, n_head_kv, hd, kv_type, page, max_ctx, max_pages;
+    float eps;
+    float* x;                   // [n_embd] residual stream: the embedding in, the last layer's out
+    float* qkv;                 // [(n_head + 2 n_head_kv) hd]
+    float* att;                 // [n_embd]
+    float* ff;                  // [n_ff]
+    const float* cos_t;         // RoPE tables [n_ctx][hd/2]
+    const float* sin_t;
+    const int32_t* pos;         // device: this token's position
+    const int32_t* block_table; // [max_pages]
+    int32_t* ctx_out;           // optional: receives pos + 1
+    unsigned* bar;              // grid-barrier counter (device word, zeroed by the launcher)
+    int* status;                // [0] site of an expired bounded wait (0: none), [1] abort word
+    int stages;                 // weight ring stages (decode_mk_supported)
+};
+// Whether this shape runs on the persistent kernel; *stages = ring depth
+// that fits the device's shared memory.
+bool decode_mk_supported(int hd, int kv_type, int max_ctx, int max_pages, uint64_t max_nb, int* stages);
+cudaError_t decode_mk(const MkArgs& a, cudaStream_t s);
+
 }  // namespace mvb

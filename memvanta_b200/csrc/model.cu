@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <stdexcept>
@@ -301,6 +302,14 @@ struct mv_model_s {
     int32_t *token_dev = nullptr, *pos_dev = nullptr, *ctx_dev = nullptr, *history = nullptr;
     float* logits_host = nullptr;          // pinned
     cudaGraphExec_t graph_logits = nullptr, graph_nologits = nullptr;
+    // one GPU: every layer of a decode step in one persistent kernel
+    // (decode_mk.cu); off with MV_DECODE_PERSISTENT=0 or where unsupported
+    bool mk = false;
+    int mk_stages = 0;
+    mvb::MkLayer* mk_layers = nullptr;     // device [n_layer]
+    unsigned* mk_bar = nullptr;
+    int* mk_status = nullptr;              // device [2]: site, abort
+    int* mk_status_host = nullptr;         // pinned copy of mk_status[0]
 
     // prefill buffers (grown on demand)
     uint64_t pf_cap = 0;
@@ -688,7 +697,33 @@ void launch_decode(mv_model_s* m, bool with_logits) {
     if (tp) ck(mvb::tp_pack(m->tp, m->x, m->n_embd, m->off_x, pt_embed(m), s), "pack");
     // F16/F32 KV: RoPE, the KV append and the attention are one kernel
     const bool fused = m->kv_type == MV_KV_F32 || m->kv_type == MV_KV_F16;
-    for (uint64_t l = 0; l < m->n_layer; ++l) {
+    if (m->mk) {
+        mvb::MkArgs a{};
+        a.layers = m->mk_layers;
+        a.n_layer = (int)m->n_layer;
+        a.n_head = (int)m->n_head;
+        a.n_head_kv = (int)m->n_head_kv;
+        a.hd = (int)m->hd;
+        a.kv_type = m->kv_type;
+        a.page = (int)m->page;
+        a.max_ctx = (int)m->n_ctx;
+        a.max_pages = (int)m->n_pages;
+        a.eps = m->eps;
+        a.x = m->x;
+        a.qkv = m->qkv;
+        a.att = m->att;
+        a.ff = m->ff;
+        a.cos_t = m->rope_cos;
+        a.sin_t = m->rope_sin;
+        a.pos = m->pos_dev;
+        a.block_table = m->table;
+        a.ctx_out = m->ctx_dev;
+        a.bar = m->mk_bar;
+        a.status = m->mk_status;
+        a.stages = m->mk_stages;
+        ck(mvb::decode_mk(a, s), "decode layers (persistent kernel)");
+    }
+    for (uint64_t l = 0; !m->mk && l < m->n_layer; ++l) {
         auto& L = m->layers[l];
         // the q|k|v GEMV leaves two CTA slots per attention CTA free (fused path)
         const int reserve = fused ? (int)(2 * m->nh) : 0;
@@ -806,6 +841,42 @@ void ready_decode(mv_model_s* m) {
     m->graph_nologits = capture_decode(m, false);
     m->pos = 0;
     m->tp_ready = true;
+}
+
+// One GPU, Q4_0 layer weights, F16/F32 KV: the decode layers run as one
+// persistent kernel (decode_mk.cu) unless MV_DECODE_PERSISTENT=0.  Its
+// outputs are bit-identical to the per-kernel path.
+void setup_persistent_decode(mv_model_s* m) {
+    const char* env = std::getenv("MV_DECODE_PERSISTENT");
+    if (env && std::string(env) == "0") return;
+    if (m->tp_world != 1 || (m->kv_type != MV_KV_F32 && m->kv_type != MV_KV_F16)) return;
+    if (m->n_head > (uint64_t)mvb::num_sms() || m->n_embd % 32 || m->n_ff % 32) return;
+    std::vector<mvb::MkLayer> hl(m->n_layer);
+    uint64_t max_nb = 0;
+    for (uint64_t l = 0; l < m->n_layer; ++l) {
+        const auto& L = m->layers[l];
+        const mv_weight_s* ws[4] = {L.qkv, L.o, L.gu, L.down};
+        for (int i = 0; i < 4; ++i) {
+            if (ws[i]->type != 2) return;
+            max_nb = std::max(max_nb, ws[i]->nb);
+            hl[l].w[i] = mvb::MkGemv{ws[i]->qs, ws[i]->d, (int)ws[i]->rows, (int)ws[i]->nb, (int)ws[i]->dstride};
+        }
+        hl[l].attn_norm = L.attn_norm;
+        hl[l].ffn_norm = L.ffn_norm;
+        hl[l].k_pages = L.k_pages;
+        hl[l].v_pages = L.v_pages;
+    }
+    int stages = 0;
+    if (!mvb::decode_mk_supported((int)m->hd, m->kv_type, (int)m->n_ctx, (int)m->n_pages, max_nb, &stages)) return;
+    m->mk_layers = dalloc<mvb::MkLayer>(m, m->n_layer);
+    ck(cudaMemcpy(m->mk_layers, hl.data(), hl.size() * sizeof(mvb::MkLayer), cudaMemcpyHostToDevice), "layer table");
+    m->mk_bar = dalloc<unsigned>(m, 1);
+    m->mk_status = dalloc<int>(m, 2);
+    ck(cudaMemset(m->mk_status, 0, 8), "clear status");
+    ck(cudaMallocHost(reinterpret_cast<void**>(&m->mk_status_host), sizeof(int)), "cudaMallocHost");
+    *m->mk_status_host = 0;
+    m->mk_stages = stages;
+    m->mk = true;
 }
 
 void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, int kv_type, int rank = 0,
@@ -966,6 +1037,7 @@ void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, in
     m->history = dalloc<int32_t>(m, m->n_ctx + 1);
     ck(cudaMallocHost(reinterpret_cast<void**>(&m->logits_host), m->vocab * sizeof(float)), "cudaMallocHost");
     ensure_prefill(m, 1);  // identity block table
+    if (world == 1) setup_persistent_decode(m);
     if (world == 1) ready_decode(m);  // tensor parallel: once the peers are connected
 }
 
@@ -976,6 +1048,7 @@ void free_model(mv_model_s* m) {
     for (void* p : m->tp_opened) cudaIpcCloseMemHandle(p);
     if (m->tp_block) cudaFree(m->tp_block);
     if (m->tp_status_host) cudaFreeHost(m->tp_status_host);
+    if (m->mk_status_host) cudaFreeHost(m->mk_status_host);
     for (auto* w : m->owned) mv_weight_free(w);
     for (void* p : m->allocs) cudaFree(p);
     if (m->logits_host) cudaFreeHost(m->logits_host);
@@ -1019,11 +1092,20 @@ void require_ready(const mv_model_s* m) {
 void enqueue_tp_status(mv_model_s* m) {
     if (m->tp_world > 1)
         ck(cudaMemcpyAsync(m->tp_status_host, m->tp_status, 4, cudaMemcpyDeviceToHost, m->stream), "status D2H");
+    if (m->mk)
+        ck(cudaMemcpyAsync(m->mk_status_host, m->mk_status, 4, cudaMemcpyDeviceToHost, m->stream), "status D2H");
 }
 void check_tp_status(const mv_model_s* m) {
     if (m->tp_world > 1 && *m->tp_status_host)
         throw ModelError(MV_ERR_TIMEOUT, "tensor-parallel wait for the other ranks gave up (site " +
                                              std::to_string(*m->tp_status_host) + ")");
+    if (m->mk && *m->mk_status_host) {
+        const int site = *m->mk_status_host;
+        *m->mk_status_host = 0;
+        cudaMemset(m->mk_status, 0, 8);  // the next step starts clean
+        throw ModelError(MV_ERR_TIMEOUT, "persistent decode kernel gave up a bounded wait (site " +
+                                             std::to_string(site) + ")");
+    }
 }
 
 // Swaps the model's prefill buffers and stream with the alternate set (and
@@ -1292,6 +1374,8 @@ MV_API uint64_t mv_model_kv_bytes(mv_model_t m) {
 }
 
 MV_API void* mv_model_stream(mv_model_t m) { return m ? m->stream : nullptr; }
+
+MV_API int mv_model_decode_persistent(mv_model_t m) { return m && m->mk ? 1 : 0; }
 
 MV_API int mv_model_forward(mv_model_t m, int32_t token, int compute_logits, float* logits_host) {
     if (!m) return MV_ERR_INVALID;

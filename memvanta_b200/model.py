@@ -100,6 +100,11 @@ class LlamaModel:
     def stream(self) -> int:
         return load().mv_model_stream(self._m) or 0
 
+    @property
+    def decode_persistent(self) -> bool:
+        """Whether a decode step runs every layer in one persistent kernel."""
+        return bool(load().mv_model_decode_persistent(self._m))
+
     def forward(self, token: int, compute_logits: bool = True, out: np.ndarray | None = None) -> np.ndarray:
         """One decode step (src/llama_model.cpp:253-259); returns host logits."""
         out = self._logits if out is None else out

@@ -101,6 +101,40 @@ def test_mid_model_vs_reference(cuda, reference, tmp, kv_type):
     m.close()
 
 
+@pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_F32])
+def test_persistent_decode_matches_per_kernel_path(cuda, tmp, kv_type, monkeypatch):
+    """The persistent decode kernel (every layer of a step in one cooperative
+    launch) against the per-operation kernels: identical logits at every
+    step, bit for bit, over a context that crosses several K/V tiles, and the
+    same device-side greedy tokens."""
+    path = os.path.join(tmp, "mid.gguf")
+    if not os.path.exists(path):
+        gguf.write_random_llama(path, MID, seed=5)
+    rng = np.random.default_rng(11)
+    prompt = rng.integers(0, MID.vocab, size=70).astype(np.int32)
+    monkeypatch.delenv("MV_DECODE_PERSISTENT", raising=False)
+    a = mv.LlamaModel(path, ctx_override=256, kv_page_tokens=16, kv_type=kv_type)
+    monkeypatch.setenv("MV_DECODE_PERSISTENT", "0")
+    b = mv.LlamaModel(path, ctx_override=256, kv_page_tokens=16, kv_type=kv_type)
+    try:
+        assert a.decode_persistent and not b.decode_persistent
+        pa, pb = a.prefill(prompt, 16).copy(), b.prefill(prompt, 16).copy()
+        assert np.array_equal(pa, pb)
+        cur = int(np.argmax(pa))
+        for i in range(90):
+            la, lb = a.forward(cur).copy(), b.forward(cur).copy()
+            assert np.array_equal(la, lb), (i, float(np.max(np.abs(la - lb))))
+            cur = int(np.argmax(la))
+        a.reset()
+        b.reset()
+        pa, pb = a.prefill(prompt, 16), b.prefill(prompt, 16)
+        t0 = int(np.argmax(pa))
+        assert list(a.generate_greedy(t0, 64)) == list(b.generate_greedy(t0, 64))
+    finally:
+        a.close()
+        b.close()
+
+
 def test_prefill_chunking_and_one_token_chunk(cuda, reference, tmp):
     """Chunks of 7 leave a 1-token tail: the reference runs that chunk with
     fp32 activations (batch < 2), and so does the device model."""

@@ -43,6 +43,10 @@
 // remaining phases as no-ops, the producer drains the copies it has in
 // flight, and the kernel returns.  The host reads the status word after the
 // step and clears it.
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "tc.cuh"
@@ -675,24 +679,75 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
 
 }  // namespace
 
+namespace {
+using MkKernel = void (*)(const MkArgs);
+
+MkKernel mk_kernel(int hd, int kv_type) {
+    const bool v5 = mk_vstages(hd, kv_type) == 5;
+    switch (hd) {
+        case 64: return v5 ? decode_mk_kernel<64, 5> : decode_mk_kernel<64, 4>;
+        case 128: return v5 ? decode_mk_kernel<128, 5> : decode_mk_kernel<128, 4>;
+        case 256: return v5 ? decode_mk_kernel<256, 5> : decode_mk_kernel<256, 4>;
+        default: return nullptr;
+    }
+}
+
+// The kernel's shared-memory limit raised to the device maximum and the
+// carveout set to all-shared, once per (kernel, device).
+cudaError_t prepare(MkKernel k, int* smem_max) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    std::lock_guard<std::mutex> lock(mu);
+    const std::pair<const void*, int> key{reinterpret_cast<const void*>(k), dev};
+    if (done.count(key)) return cudaSuccess;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, *smem_max);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e == cudaSuccess) done.insert(key);
+    return e;
+}
+}  // namespace
+
 bool decode_mk_supported(int hd, int kv_type, int max_ctx, int max_pages, uint64_t max_nb, int* stages) {
-    if (hd != 64 && hd != 128 && hd != 256) return false;
     if (kv_type != 0 && kv_type != 1) return false;
     if (max_nb > (uint64_t)kMaxNb) return false;
-    int dev = 0, smem_max = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return false;
-    const int fixed = (int)mk_plan(hd, max_ctx, max_pages, kv_type, 0).total + 2048;  // + static shared memory
-    const int s = (smem_max - fixed) / (kStage + 16);
-    if (s < 4) return false;
-    *stages = s > 32 ? 32 : s;
-    return true;
+    const MkKernel k = mk_kernel(hd, kv_type);
+    int smem_max = 0;
+    if (!k || prepare(k, &smem_max) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    // the deepest ring with which one CTA still fits on an SM (the launch is
+    // cooperative: every CTA must be resident)
+    for (int st = 32; st >= 4; --st) {
+        const size_t smem = mk_plan(hd, max_ctx, max_pages, kv_type, st).total;
+        if (smem > (size_t)smem_max) continue;
+        int blocks = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k, kThreads, smem) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        if (blocks >= 1) {
+            *stages = st;
+            return true;
+        }
+    }
+    return false;
 }
 
 uint64_t decode_mk_smem(const MkArgs& a) { return mk_plan(a.hd, a.max_ctx, a.max_pages, a.kv_type, a.stages).total; }
 
 cudaError_t decode_mk(const MkArgs& a, cudaStream_t s) {
+    const MkKernel k = mk_kernel(a.hd, a.kv_type);
+    if (!k) return cudaErrorInvalidValue;
+    int smem_max = 0;
+    cudaError_t e = prepare(k, &smem_max);
+    if (e != cudaSuccess) return e;
     const size_t smem = decode_mk_smem(a);
+    if (smem > (size_t)smem_max) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)num_sms());
     cfg.blockDim = dim3(kThreads);
@@ -703,24 +758,9 @@ cudaError_t decode_mk(const MkArgs& a, cudaStream_t s) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaMemsetAsync(a.bar, 0, sizeof(unsigned), s);
+    e = cudaMemsetAsync(a.bar, 0, sizeof(unsigned), s);
     if (e != cudaSuccess) return e;
-    int dev = 0, smem_max = 0;
-    cudaGetDevice(&dev);
-    e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (e != cudaSuccess) return e;
-    if (smem > (size_t)smem_max) return cudaErrorInvalidValue;
-    auto go = [&](auto kernel) {
-        ensure_smem_attr(kernel, smem_max);
-        return cudaLaunchKernelEx(&cfg, kernel, a);
-    };
-    const bool v5 = mk_vstages(a.hd, a.kv_type) == 5;
-    switch (a.hd) {
-        case 64: return v5 ? go(decode_mk_kernel<64, 5>) : go(decode_mk_kernel<64, 4>);
-        case 128: return v5 ? go(decode_mk_kernel<128, 5>) : go(decode_mk_kernel<128, 4>);
-        case 256: return v5 ? go(decode_mk_kernel<256, 5>) : go(decode_mk_kernel<256, 4>);
-        default: return cudaErrorInvalidValue;
-    }
+    return cudaLaunchKernelEx(&cfg, k, a);
 }
 
 }  // namespace mvb

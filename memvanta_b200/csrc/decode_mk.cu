@@ -692,13 +692,18 @@ MkKernel mk_kernel(int hd, int kv_type) {
     }
 }
 
-// The kernel's shared-memory limit raised to the device maximum and the
-// carveout set to all-shared, once per (kernel, device).
+// The kernel's dynamic shared-memory limit raised to the device maximum
+// (less its static shared memory) and the carveout set to all-shared, once
+// per (kernel, device); *smem_max = that limit.
 cudaError_t prepare(MkKernel k, int* smem_max) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e != cudaSuccess) return e;
+    cudaFuncAttributes fa{};
+    e = cudaFuncGetAttributes(&fa, k);
+    if (e != cudaSuccess) return e;
+    *smem_max -= (int)fa.sharedSizeBytes;
     static std::mutex mu;
     static std::set<std::pair<const void*, int>> done;
     std::lock_guard<std::mutex> lock(mu);
@@ -711,14 +716,21 @@ cudaError_t prepare(MkKernel k, int* smem_max) {
 }
 }  // namespace
 
-bool decode_mk_supported(int hd, int kv_type, int max_ctx, int max_pages, uint64_t max_nb, int* stages) {
-    if (kv_type != 0 && kv_type != 1) return false;
-    if (max_nb > (uint64_t)kMaxNb) return false;
-    const MkKernel k = mk_kernel(hd, kv_type);
-    int smem_max = 0;
-    if (!k || prepare(k, &smem_max) != cudaSuccess) {
-        cudaGetLastError();
+bool decode_mk_supported(int hd, int kv_type, int max_ctx, int max_pages, uint64_t max_nb, int* stages,
+                         std::string* why) {
+    auto no = [&](const std::string& r) {
+        if (why) *why = r;
         return false;
+    };
+    if (kv_type != 0 && kv_type != 1) return no("KV cache type is not F32/F16");
+    if (max_nb > (uint64_t)kMaxNb) return no("a weight is wider than " + std::to_string(kMaxNb * 32));
+    const MkKernel k = mk_kernel(hd, kv_type);
+    if (!k) return no("head_dim not 64/128/256");
+    int smem_max = 0;
+    cudaError_t e = prepare(k, &smem_max);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return no(std::string("kernel attributes: ") + cudaGetErrorString(e));
     }
     // the deepest ring with which one CTA still fits on an SM (the launch is
     // cooperative: every CTA must be resident)
@@ -726,16 +738,18 @@ bool decode_mk_supported(int hd, int kv_type, int max_ctx, int max_pages, uint64
         const size_t smem = mk_plan(hd, max_ctx, max_pages, kv_type, st).total;
         if (smem > (size_t)smem_max) continue;
         int blocks = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k, kThreads, smem) != cudaSuccess) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k, kThreads, smem);
+        if (e != cudaSuccess) {
             cudaGetLastError();
-            return false;
+            return no(std::string("occupancy query: ") + cudaGetErrorString(e));
         }
         if (blocks >= 1) {
             *stages = st;
             return true;
         }
     }
-    return false;
+    return no("no ring depth fits one CTA per SM (shared memory " + std::to_string(smem_max) + ", fixed part " +
+              std::to_string(mk_plan(hd, max_ctx, max_pages, kv_type, 0).total) + ")");
 }
 
 uint64_t decode_mk_smem(const MkArgs& a) { return mk_plan(a.hd, a.max_ctx, a.max_pages, a.kv_type, a.stages).total; }

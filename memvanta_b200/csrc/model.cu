@@ -849,15 +849,22 @@ void ready_decode(mv_model_s* m) {
 void setup_persistent_decode(mv_model_s* m) {
     const char* env = std::getenv("MV_DECODE_PERSISTENT");
     if (env && std::string(env) == "0") return;
-    if (m->tp_world != 1 || (m->kv_type != MV_KV_F32 && m->kv_type != MV_KV_F16)) return;
-    if (m->n_head > (uint64_t)mvb::num_sms() || m->n_embd % 32 || m->n_ff % 32) return;
+    // MV_DECODE_PERSISTENT=1 demands it: a model it cannot serve fails to open
+    const bool forced = env && std::string(env) == "1";
+    auto skip = [&](const std::string& why) {
+        if (forced) throw ModelError(MV_ERR_UNSUPPORTED, "persistent decode kernel: " + why);
+    };
+    if (m->tp_world != 1) return skip("tensor parallel");
+    if (m->kv_type != MV_KV_F32 && m->kv_type != MV_KV_F16) return skip("KV cache type is not F32/F16");
+    if (m->n_head > (uint64_t)mvb::num_sms()) return skip("more heads than SMs");
+    if (m->n_embd % 32 || m->n_ff % 32) return skip("n_embd / n_ff not multiples of 32");
     std::vector<mvb::MkLayer> hl(m->n_layer);
     uint64_t max_nb = 0;
     for (uint64_t l = 0; l < m->n_layer; ++l) {
         const auto& L = m->layers[l];
         const mv_weight_s* ws[4] = {L.qkv, L.o, L.gu, L.down};
         for (int i = 0; i < 4; ++i) {
-            if (ws[i]->type != 2) return;
+            if (ws[i]->type != 2) return skip("layer weights are not Q4_0");
             max_nb = std::max(max_nb, ws[i]->nb);
             hl[l].w[i] = mvb::MkGemv{ws[i]->qs, ws[i]->d, (int)ws[i]->rows, (int)ws[i]->nb, (int)ws[i]->dstride};
         }
@@ -867,7 +874,9 @@ void setup_persistent_decode(mv_model_s* m) {
         hl[l].v_pages = L.v_pages;
     }
     int stages = 0;
-    if (!mvb::decode_mk_supported((int)m->hd, m->kv_type, (int)m->n_ctx, (int)m->n_pages, max_nb, &stages)) return;
+    std::string why;
+    if (!mvb::decode_mk_supported((int)m->hd, m->kv_type, (int)m->n_ctx, (int)m->n_pages, max_nb, &stages, &why))
+        return skip(why);
     m->mk_layers = dalloc<mvb::MkLayer>(m, m->n_layer);
     ck(cudaMemcpy(m->mk_layers, hl.data(), hl.size() * sizeof(mvb::MkLayer), cudaMemcpyHostToDevice), "layer table");
     m->mk_bar = dalloc<unsigned>(m, 1);

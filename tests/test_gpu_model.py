@@ -112,7 +112,7 @@ def test_persistent_decode_matches_per_kernel_path(cuda, tmp, kv_type, monkeypat
         gguf.write_random_llama(path, MID, seed=5)
     rng = np.random.default_rng(11)
     prompt = rng.integers(0, MID.vocab, size=70).astype(np.int32)
-    monkeypatch.delenv("MV_DECODE_PERSISTENT", raising=False)
+    monkeypatch.setenv("MV_DECODE_PERSISTENT", "1")  # fails to open if it cannot run
     a = mv.LlamaModel(path, ctx_override=256, kv_page_tokens=16, kv_type=kv_type)
     monkeypatch.setenv("MV_DECODE_PERSISTENT", "0")
     b = mv.LlamaModel(path, ctx_override=256, kv_page_tokens=16, kv_type=kv_type)

@@ -284,6 +284,8 @@ MV_API int mv_gemv(mv_weight_t w, const float* x, float* y, void* stream) {
         CK(mvb::gemv_q4(a, s));
     } else if (w->type == 14 && w->cols * 4 <= 200 * 1024) {
         CK(mvb::gemv_q6k(*w, x, y, s));
+    } else if (w->type == 8 && w->cols * 4 <= 200 * 1024 && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+        CK(mvb::gemv_q8_0(*w, x, y, s));
     } else {
         CK(mvb::matmul_f32act(*w, x, 1, y, s));
     }

@@ -71,6 +71,9 @@ struct GemvQ4Args {
 cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s);
 cudaError_t q4_block_dots(const mv_weight_s& w, const float* x, int32_t* isum, cudaStream_t s);
 
+// ---- gemv_q8.cu : decode GEMV for Q8_0 weights (fp32 x, 16-byte aligned)
+cudaError_t gemv_q8_0(const mv_weight_s& w, const float* x, float* y, cudaStream_t s);
+
 // ---- gemv_q6k.cu : decode GEMV for the Q6_K output head (fp32 x)
 cudaError_t gemv_q6k(const mv_weight_s& w, const float* x, float* y, cudaStream_t s);
 

@@ -618,6 +618,7 @@ void project_decode(mv_model_s* m, mv_weight_s* w, const float* x, const float* 
     }
     if (epi == mvb::Q4Epi::Store) {
         if (w->type == 14 && w->cols * 4 <= 200 * 1024) ck(mvb::gemv_q6k(*w, in, y, s), "gemv_q6k");
+        else if (w->type == 8 && w->cols * 4 <= 200 * 1024) ck(mvb::gemv_q8_0(*w, in, y, s), "gemv_q8_0");
         else ck(mvb::matmul_f32act(*w, in, 1, y, s), "matmul");
     } else if (epi == mvb::Q4Epi::AddTo) {
         ck(mvb::matmul_f32act(*w, in, 1, m->logits, s), "matmul");  // logits buffer as scratch

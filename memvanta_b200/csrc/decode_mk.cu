@@ -61,8 +61,8 @@ constexpr int kWork = (kComp + 1) * 32;      // compute + chain threads
 constexpr int kThreads = kWork + 32;         // + producer
 constexpr int kTR = 16;                      // rows per tile
 constexpr int kTC = 32;                      // blocks per chunk
-constexpr int kPayRow = kTC * 16 + 16;       // staged nibble bytes per row (padded: conflict-free lane = row)
-constexpr int kScRow = kTC * 2 + 16;         // staged scale bytes per row (padded)
+constexpr int kPayRow = kTC * 16;            // staged nibble bytes per row (one TMA box row)
+constexpr int kScRow = kTC * 2;              // staged scale bytes per row
 constexpr int kStage = kTR * (kPayRow + kScRow);
 constexpr int kTT = kTC + 2;                 // float2 per term row (padded)
 constexpr int kMaxNb = 512;                  // blocks of the widest input (K <= 16384)
@@ -74,12 +74,6 @@ constexpr int kBarAttn = 4;  // the HD attention threads
 
 __device__ __forceinline__ void bar_named(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
 }
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
@@ -534,21 +528,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
                         ok = tc::mbar_wait(empty0 + 8 * s, ((k / S) & 1u) ^ 1u, a.status + 1, a.status, 41);
                         ok = __all_sync(0xffffffffu, ok);
                         if (!ok) break;
-                        const int r0 = t * kTR, nblk = min(kTC, w.nb - c * kTC);
-                        const int nrow = min(kTR, w.rows - r0);
-                        const uint32_t pay = (uint32_t)nblk * 16u, scb = ((uint32_t)nblk * 2u + 15u) & ~15u;
-                        const uint32_t st = sbase + P.ring + (uint32_t)s * kStage;
-                        if (lane == 0) tc::mbar_expect_tx(full0 + 8 * s, (uint32_t)nrow * (pay + scb));
-                        __syncwarp();
-                        if (lane < kTR) {
-                            if (lane < nrow)
-                                bulk_g2s(st + lane * kPayRow, w.qs + ((size_t)(r0 + lane) * w.nb + (size_t)c * kTC) * 16,
-                                         pay, full0 + 8 * s);
-                        } else {
-                            const int r = lane - kTR;
-                            if (r < nrow)
-                                bulk_g2s(st + kTR * kPayRow + r * kScRow,
-                                         w.d + (size_t)(r0 + r) * w.dstride + (size_t)c * kTC, scb, full0 + 8 * s);
+                        // one box of nibbles (16 rows x 512 B) and one of scales (16 rows x
+                        // 64 B); columns past the row end arrive as zeros and count in full
+                        if (lane == 0) {
+                            const uint32_t st = sbase + P.ring + (uint32_t)s * kStage;
+                            const CUtensorMap* mp = a.maps + 2 * (l * 4 + ph);
+                            tc::mbar_expect_tx(full0 + 8 * s, kStage);
+                            tc::tma_load_2d(st, mp, c * (kPayRow / 4), t * kTR, full0 + 8 * s);
+                            tc::tma_load_2d(st + kTR * kPayRow, mp + 1, c * kTC, t * kTR, full0 + 8 * s);
                         }
                     }
                 }
@@ -576,28 +563,29 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
         off = (off + q.T) % G;
         int it = 0;
         if (warp < kComp) {
-            const int row = lane & 15, bq = warp * 4 + (lane >> 4) * 2;
+            // thread: row tid / 16, blocks bl and bl + 16 of the chunk (bl = tid % 16):
+            // the 8 lanes of a quarter-warp read 8 consecutive 16-byte blocks of
+            // one staged row -- no bank conflict on the dense TMA rows
+            const int row = (int)threadIdx.x >> 4, bl = (int)threadIdx.x & 15;
             for (int t = q.t0; t < q.T; t += G) {
                 for (int c = 0; c < q.nch; ++c, ++k, ++it) {
                     const int s = (int)(k % (uint32_t)S);
                     bool ok = !*cta_abort;
                     if (ok) ok = tc::mbar_wait(full0 + 8 * s, (k / S) & 1u, a.status + 1, a.status, 43);
                     ok = __all_sync(0xffffffffu, ok);
-                    float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                    float2 o2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
                     if (ok) {
                         const unsigned char* st = sm + P.ring + (size_t)s * kStage;
-                        const uint32_t sc2 = *reinterpret_cast<const uint32_t*>(st + kTR * kPayRow + row * kScRow + bq * 2);
+                        const unsigned short* sc = reinterpret_cast<const unsigned short*>(st + kTR * kPayRow + row * kScRow);
 #pragma unroll
                         for (int j = 0; j < 2; ++j) {
-                            const int b = c * kTC + bq + j;
+                            const int cb = bl + 16 * j, b = c * kTC + cb;
                             if (b < w.nb) {
                                 const int4 alo = act.lo[b], ahi = act.hi[b];
                                 const float2 dc = act.dc[b];
-                                const uint4 wv = *reinterpret_cast<const uint4*>(st + row * kPayRow + (bq + j) * 16);
+                                const uint4 wv = *reinterpret_cast<const uint4*>(st + row * kPayRow + cb * 16);
                                 const int isum = block_isum(wv, alo, ahi, __float_as_int(dc.y));
-                                const float tw = half_bits_to_float((unsigned short)(sc2 >> (16 * j))) * dc.x;
-                                if (j == 0) o4.x = tw, o4.y = (float)isum;
-                                else o4.z = tw, o4.w = (float)isum;
+                                o2[j] = make_float2(half_bits_to_float(sc[cb]) * dc.x, (float)isum);
                             }
                         }
                         __syncwarp();
@@ -605,7 +593,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
                     } else {
                         *cta_abort = 1;
                     }
-                    *reinterpret_cast<float4*>(terms + ((it & 1) * kTR + row) * kTT + bq) = o4;
+                    terms[((it & 1) * kTR + row) * kTT + bl] = o2[0];
+                    terms[((it & 1) * kTR + row) * kTT + bl + 16] = o2[1];
                     bar_named(kBarHand, kWork);  // terms of `it` complete; the chain of it-1 is done
                 }
             }

@@ -2,6 +2,7 @@
 // (capi.cu) and the device-resident model (model.cu).  All launchers are
 // asynchronous on `s` and return cudaGetLastError() of the launch.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include "tp.cuh"
@@ -191,6 +192,10 @@ struct MkLayer {
 };
 struct MkArgs {
     const MkLayer* layers;      // device array [n_layer]
+    // device array [n_layer][4][2]: per layer weight (q|k|v, o, gate|up, down)
+    // the TMA maps of its nibble plane (uint32 words, box 128 x 16 rows) and
+    // its scale plane (fp16, box 32 x 16 rows)
+    const CUtensorMap* maps;
     int n_layer, n_head, n_head_kv, hd, kv_type, page, max_ctx, max_pages;
     float eps;
     float* x;                   // [n_embd] residual stream: the embedding in, the last layer's out

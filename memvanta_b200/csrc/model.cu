@@ -36,6 +36,7 @@
 #include "common.cuh"
 #include "gguf_loader.hpp"
 #include "kernels.cuh"
+#include "tc.cuh"
 #include "weights.cuh"
 
 namespace mvb {
@@ -307,6 +308,7 @@ struct mv_model_s {
     bool mk = false;
     int mk_stages = 0;
     mvb::MkLayer* mk_layers = nullptr;     // device [n_layer]
+    CUtensorMap* mk_maps = nullptr;        // device [n_layer][4][2]
     unsigned* mk_bar = nullptr;
     int* mk_status = nullptr;              // device [2]: site, abort
     int* mk_status_host = nullptr;         // pinned copy of mk_status[0]
@@ -701,6 +703,7 @@ void launch_decode(mv_model_s* m, bool with_logits) {
     if (m->mk) {
         mvb::MkArgs a{};
         a.layers = m->mk_layers;
+        a.maps = m->mk_maps;
         a.n_layer = (int)m->n_layer;
         a.n_head = (int)m->n_head;
         a.n_head_kv = (int)m->n_head_kv;
@@ -874,12 +877,34 @@ void setup_persistent_decode(mv_model_s* m) {
         hl[l].k_pages = L.k_pages;
         hl[l].v_pages = L.v_pages;
     }
+    // the TMA maps of every layer weight's nibble and scale planes
+    const mvb::tc::EncodeFn enc = mvb::tc::encode_fn();
+    if (!enc) return skip("cuTensorMapEncodeTiled is unavailable");
+    std::vector<CUtensorMap> maps(m->n_layer * 8);
+    for (uint64_t l = 0; l < m->n_layer; ++l) {
+        const auto& L = m->layers[l];
+        const mv_weight_s* ws[4] = {L.qkv, L.o, L.gu, L.down};
+        for (int i = 0; i < 4; ++i) {
+            const mv_weight_s& w = *ws[i];
+            const cuuint64_t qd[2] = {w.nb * 4, w.rows}, qst[1] = {w.nb * 16};
+            const cuuint32_t qb[2] = {128, 16};
+            const cuuint64_t dd[2] = {w.dstride, w.rows}, dst[1] = {w.dstride * 2};
+            const cuuint32_t db[2] = {32, 16};
+            if (!mvb::tc::encode(enc, &maps[(l * 4 + i) * 2], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, w.qs, qd, qst, qb,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE) ||
+                !mvb::tc::encode(enc, &maps[(l * 4 + i) * 2 + 1], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, w.d, dd, dst, db,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE))
+                return skip("a weight's tensor map was rejected");
+        }
+    }
     int stages = 0;
     std::string why;
     if (!mvb::decode_mk_supported((int)m->hd, m->kv_type, (int)m->n_ctx, (int)m->n_pages, max_nb, &stages, &why))
         return skip(why);
     m->mk_layers = dalloc<mvb::MkLayer>(m, m->n_layer);
     ck(cudaMemcpy(m->mk_layers, hl.data(), hl.size() * sizeof(mvb::MkLayer), cudaMemcpyHostToDevice), "layer table");
+    m->mk_maps = dalloc<CUtensorMap>(m, maps.size());  // 256-byte aligned allocation (maps need 64)
+    ck(cudaMemcpy(m->mk_maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice), "tensor maps");
     m->mk_bar = dalloc<unsigned>(m, 1);
     m->mk_status = dalloc<int>(m, 2);
     ck(cudaMemset(m->mk_status, 0, 8), "clear status");

@@ -1166,6 +1166,9 @@ struct AltSet {
     }
 };
 
+// Tokens one merged prefill batch holds at most (single GPU).
+constexpr uint64_t kMergedPrefill = 512;
+
 // One chunk of B tokens; `off` indexes the call's staged inputs.
 void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     cudaStream_t s = m->stream;
@@ -1442,7 +1445,21 @@ MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uin
         for (uint64_t i = 0; i < n; ++i)
             if (tokens[i] < 0 || (uint64_t)tokens[i] >= m->vocab) throw ModelError(MV_ERR_INVALID, "token id out of range");
         require_ready(m);
-        const uint64_t B = std::max<uint64_t>(1, batch);
+        const uint64_t B0 = std::max<uint64_t>(1, batch);
+        // The reference prefills in chunks of `batch` (LlamaModel::prefill,
+        // src/llama_model.cpp:260), but every token's arithmetic is the same
+        // whatever chunk it is in -- per-token Q8 activations, per-(token, row)
+        // GEMM chains, the chunk's K/V appended before its causal attention --
+        // except that a 1-token chunk takes the fp32-activation path
+        // (tensor_matmul_batch_v06 routes batch < 2 to tensor_matmul_batch).
+        // So on one GPU the chunks of 2 or more tokens run together as one
+        // batch of up to kMergedPrefill tokens (every weight read once per
+        // layer, not once per chunk); a last chunk of 1 token (n % batch == 1)
+        // runs on its own.  Outputs are identical to chunk-by-chunk execution.
+        const char* env = std::getenv("MV_PREFILL_MERGE");
+        const bool merge = m->tp_world == 1 && B0 >= 2 && !(env && std::string(env) == "0");
+        const uint64_t tail1 = (B0 >= 2 && n % B0 == 1) ? 1 : 0;
+        const uint64_t B = merge ? std::min<uint64_t>(std::max(B0, kMergedPrefill), n - tail1 ? n - tail1 : 1) : B0;
         ck(cudaStreamSynchronize(m->stream), "sync");
         ensure_prefill(m, std::min(B, n));
         stage_prefill_inputs(m, tokens, n);
@@ -1454,8 +1471,14 @@ MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uin
             ck(cudaStreamWaitEvent(m->pf_alt.stream, m->pf_join, 0), "wait (prefill start)");
         }
         try {
-            for (uint64_t i = 0, c = 0; i < n; i += B, ++c) {
-                const uint64_t nb = std::min(B, n - i);
+            uint64_t nb = 0;
+            for (uint64_t i = 0, c = 0; i < n; i += nb, ++c) {
+                nb = std::min(B, n - i);
+                if (merge) {
+                    // the merged span stops before the 1-token tail, which runs alone
+                    const uint64_t q8_end = n - tail1;
+                    nb = i < q8_end ? std::min(B, q8_end - i) : n - i;
+                }
                 m->pf_wait = wave && c ? &m->pf_ev[(c - 1) & 1] : nullptr;
                 m->pf_rec = wave ? &m->pf_ev[c & 1] : nullptr;
                 AltSet alt(m, wave && (c & 1));

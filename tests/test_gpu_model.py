@@ -135,6 +135,34 @@ def test_persistent_decode_matches_per_kernel_path(cuda, tmp, kv_type, monkeypat
         b.close()
 
 
+@pytest.mark.parametrize("n,batch", [(70, 16), (22, 7), (33, 32), (1, 8), (150, 64)])
+def test_merged_prefill_matches_chunk_by_chunk(cuda, tmp, n, batch, monkeypatch):
+    """One GPU runs the chunks of a prefill together as one batch (weights
+    read once per layer); the per-token arithmetic is the chunked one, so the
+    logits, the position and the cache (seen through the decode steps after
+    it) equal chunk-by-chunk execution (MV_PREFILL_MERGE=0) bit for bit."""
+    path = os.path.join(tmp, "mid.gguf")
+    if not os.path.exists(path):
+        gguf.write_random_llama(path, MID, seed=5)
+    prompt = np.random.default_rng(n).integers(0, MID.vocab, size=n).astype(np.int32)
+    monkeypatch.delenv("MV_PREFILL_MERGE", raising=False)
+    a = mv.LlamaModel(path, ctx_override=256, kv_page_tokens=16, kv_type=mv.KV_F16)
+    monkeypatch.setenv("MV_PREFILL_MERGE", "0")
+    b = mv.LlamaModel(path, ctx_override=256, kv_page_tokens=16, kv_type=mv.KV_F16)
+    try:
+        la, lb = a.prefill(prompt, batch).copy(), b.prefill(prompt, batch).copy()
+        assert np.array_equal(la, lb)
+        assert a.position() == b.position() == n
+        cur = int(np.argmax(la))
+        for _ in range(4):
+            da, db = a.forward(cur).copy(), b.forward(cur).copy()
+            assert np.array_equal(da, db)
+            cur = int(np.argmax(da))
+    finally:
+        a.close()
+        b.close()
+
+
 def test_prefill_chunking_and_one_token_chunk(cuda, reference, tmp):
     """Chunks of 7 leave a 1-token tail: the reference runs that chunk with
     fp32 activations (batch < 2), and so does the device model."""

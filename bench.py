@@ -437,9 +437,11 @@ def other_configs():
     out["config2_mixed_quant"] = c2
     c4 = {}
     for kv in ("f16", "q8_0"):
-        r = time_paged_attn(kv)
-        c4[kv] = {"us": r["us_per_launch"], "gbs": r["value"], "hbm_frac": r["frac_of_measured_hbm"],
-                  "sum_ctx": r["sum_ctx"]}
+        for split in (True, False):
+            r = time_paged_attn(kv, split=split)
+            c4[kv + ("_split_k" if split else "_exact")] = {"us": r["us_per_launch"], "gbs": r["value"],
+                                                            "hbm_frac": r["frac_of_measured_hbm"],
+                                                            "sum_ctx": r["sum_ctx"]}
     out["config4_paged_attention"] = c4
     return out
 
@@ -485,6 +487,8 @@ def main():
                     help="gemv/gemm: weight type (config 2: q8_0 4096x4096, q6_k 32000x4096; the gemm of q8_0 and "
                          "q6_k runs the reference's fp32-activation path)")
     ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"], help="paged_attn: cache type")
+    ap.add_argument("--attn", default="split", choices=["split", "exact"],
+                    help="paged_attn: split-K kernel or the exact-order kernel")
     ap.add_argument("--clock-window", type=float, default=0.5)
     args = ap.parse_args()
     if args.warmup < 3:
@@ -668,10 +672,10 @@ def time_matmul(kind, wtype, rows, cols, B=1, steps=32, warmup=3):
 
 
 def main_paged_attn(args, mv, dev):
-    print(json.dumps(time_paged_attn(args.kv, args.steps, args.warmup)), flush=True)
+    print(json.dumps(time_paged_attn(args.kv, args.steps, args.warmup, args.attn == "split")), flush=True)
 
 
-def time_paged_attn(kv="f16", steps=32, warmup=3):
+def time_paged_attn(kv="f16", steps=32, warmup=3, split=True):
     """Config 4: paged decode attention over 64 sequences, ctx ~ U(64..768),
     16-token pages scattered by a random permutation block table, 32 heads x
     128, Q/K/V ~ N(0,1) (random fp16 pages; Q8_0 pages with random int8 and
@@ -709,8 +713,9 @@ def time_paged_attn(kv="f16", steps=32, warmup=3):
     tab, ctx_t = torch.from_numpy(table).to(dev), torch.from_numpy(ctx).to(dev)
     out = torch.empty((n_seq, kv_dim), device=dev)
     stream = torch.cuda.Stream(device=dev)
-    call = lambda: mv.paged_attn_decode(kv_type, q, n_head, n_head, hd, kp, vp, tab, max_pages, page, ctx_t,  # noqa: E731
-                                        int(ctx.max()), ks, vs, out, stream)
+    fn = mv.paged_attn_decode_split if split else mv.paged_attn_decode
+    call = lambda: fn(kv_type, q, n_head, n_head, hd, kp, vp, tab, max_pages, page, ctx_t,  # noqa: E731
+                      int(ctx.max()), ks, vs, out, stream)
     with torch.cuda.stream(stream):
         for _ in range(max(warmup, 1)):
             call()
@@ -730,7 +735,8 @@ def time_paged_attn(kv="f16", steps=32, warmup=3):
     del gr
     row_bytes = mv.kv_row_bytes(kv_type, kv_dim) + 4 * mv.kv_row_scales(kv_type, kv_dim)
     alg = int(ctx.sum()) * 2 * row_bytes + 2 * n_seq * kv_dim * 4  # K and V of every context token, Q in, O out
-    return {"workload": "paged_attn", "kv": kv, "config": "config4: 64 seqs, ctx U(64..768), 16-token "
+    return {"workload": "paged_attn", "kv": kv, "kernel": "split-K" if split else "exact order",
+            "config": "config4: 64 seqs, ctx U(64..768), 16-token "
             "pages, random permutation block table, 32 heads x 128", "sum_ctx": int(ctx.sum()),
             "us_per_launch": round(us, 2), "metric": "paged attention achieved GB/s",
             "value": round(alg / us / 1e3, 1), "unit": "GB/s", "algorithmic_bytes_per_launch": alg,

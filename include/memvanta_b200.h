@@ -185,7 +185,10 @@ MV_API int mv_kv_append(int kv_type, const float* k_dev, const float* v_dev, uin
  * q[n_seq, n_head*hd] -> out[n_seq, n_head*hd]; sequence s attends to
  * ctx_len[s] tokens whose pages are block_table[s*max_pages + i].  Per head:
  * softmax(q.k/sqrt(hd)) . v, GQA kv head h/(n_head/n_head_kv).  Split over
- * the context (split-K) with an exact max/sum merge.
+ * the context in the reference's order (the per-dimension FMA chain runs over
+ * the tokens in sequence): the scores are bit-identical, the output differs
+ * from the reference only where the device's correctly rounded exp and tree
+ * summed double denominator round differently from the host's expf.
  * Replaces the decode attention loop over PagedKVCache::dot_key/add_value
  * (src/llama_model.cpp:23-55, :256). */
 MV_API int mv_paged_attn_decode(int kv_type, const float* q_dev, uint64_t n_seq, uint64_t n_head, uint64_t n_head_kv,
@@ -193,6 +196,19 @@ MV_API int mv_paged_attn_decode(int kv_type, const float* q_dev, uint64_t n_seq,
                          const float* k_scales_dev, const float* v_scales_dev, const int32_t* block_table_dev,
                          uint64_t max_pages, uint64_t page, const int32_t* ctx_len_dev, uint64_t max_ctx,
                          float* out_dev, void* stream);
+
+/* mv_paged_attn_decode split over the context (split-K): each of four warps
+ * per (sequence, head) owns a quarter of the tokens with its own running max,
+ * double denominator and partial output, merged once in a fixed order.  Scores
+ * are the reference's; the output agrees with it to ~1e-6 of its scale (not
+ * bit for bit) at a fraction of the exact path's latency for long contexts.
+ * Same arguments; Q8 caches need k_scales/v_scales.  Replaces the same
+ * reference loop (src/llama_model.cpp:256). */
+MV_API int mv_paged_attn_decode_split(int kv_type, const float* q_dev, uint64_t n_seq, uint64_t n_head,
+                                      uint64_t n_head_kv, uint64_t head_dim, const void* k_pages_dev,
+                                      const void* v_pages_dev, const float* k_scales_dev, const float* v_scales_dev,
+                                      const int32_t* block_table_dev, uint64_t max_pages, uint64_t page,
+                                      const int32_t* ctx_len_dev, uint64_t max_ctx, float* out_dev, void* stream);
 
 /* Attention for n_q query rows of ONE sequence (a prefill chunk): every row
  * reads the pages of block_table[0 .. max_pages); row i attends to its first

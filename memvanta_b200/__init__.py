@@ -288,6 +288,20 @@ def paged_attn_decode(kv_type, q, n_head, n_head_kv, head_dim, k_pages, v_pages,
     return out
 
 
+def paged_attn_decode_split(kv_type, q, n_head, n_head_kv, head_dim, k_pages, v_pages, block_table, max_pages,
+                            page, ctx_len, max_ctx, k_scales=None, v_scales=None, out=None, stream=None):
+    """paged_attn_decode split over the context (not bit-exact: ~1e-6)."""
+    import torch
+    n_seq = q.shape[0]
+    if out is None:
+        out = torch.empty((n_seq, n_head * head_dim), dtype=torch.float32, device=q.device)
+    check(load().mv_paged_attn_decode_split(kv_type, _t_ptr(q), n_seq, n_head, n_head_kv, head_dim, _t_ptr(k_pages),
+                                            _t_ptr(v_pages), _t_ptr(k_scales), _t_ptr(v_scales),
+                                            _t_ptr(block_table), max_pages, page, _t_ptr(ctx_len), max_ctx,
+                                            _t_ptr(out), _stream(stream)))
+    return out
+
+
 def paged_attn_prefill(kv_type, q, n_head, n_head_kv, head_dim, k_pages, v_pages, block_table, max_pages, page,
                        ctx_len, max_ctx, k_scales=None, v_scales=None, out=None, stream=None):
     """Attention of the query rows of one sequence (a prefill chunk): every

@@ -54,6 +54,8 @@ SIGNATURES = {
     "mv_kv_append": (_i, [_i, _p, _p, _u64, _u64, _p, _p, _p, _u64, _u64, _p, _p, _p, _p, _p]),
     "mv_paged_attn_decode": (_i, [_i, _p, _u64, _u64, _u64, _u64, _p, _p, _p, _p, _p, _u64, _u64, _p, _u64, _p,
                                   _p]),
+    "mv_paged_attn_decode_split": (_i, [_i, _p, _u64, _u64, _u64, _u64, _p, _p, _p, _p, _p, _u64, _u64, _p, _u64,
+                                        _p, _p]),
     "mv_paged_attn_prefill": (_i, [_i, _p, _u64, _u64, _u64, _u64, _p, _p, _p, _p, _p, _u64, _u64, _p, _u64, _p,
                                    _p]),
     "mv_tensor_matvec_host": (_i, [_p, _p, _p]),

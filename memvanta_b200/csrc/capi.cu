@@ -424,6 +424,23 @@ MV_API int mv_paged_attn_decode(int kv_type, const float* q, uint64_t n_seq, uin
     return MV_OK;
 }
 
+MV_API int mv_paged_attn_decode_split(int kv_type, const float* q, uint64_t n_seq, uint64_t n_head,
+                                      uint64_t n_head_kv, uint64_t hd, const void* k_pages, const void* v_pages,
+                                      const float* k_scales, const float* v_scales, const int32_t* block_table,
+                                      uint64_t max_pages, uint64_t page, const int32_t* ctx_len, uint64_t max_ctx,
+                                      float* out, void* stream) {
+    if (kv_type < 0 || kv_type > 3) return fail(MV_ERR_UNSUPPORTED, "unknown KV cache type");
+    if (!n_head_kv || n_head % n_head_kv) return fail(MV_ERR_INVALID, "n_head must be a multiple of n_head_kv");
+    if (hd != 64 && hd != 128 && hd != 256) return fail(MV_ERR_UNSUPPORTED, "head_dim must be 64, 128 or 256");
+    if (!page) return fail(MV_ERR_INVALID, "page must be > 0");
+    if (kv_type >= 2 && !(k_scales && v_scales)) return fail(MV_ERR_INVALID, "Q8 caches need k_scales and v_scales");
+    if (n_seq == 0) return MV_OK;
+    mvb::AttnArgs a{kv_type, q, n_head * hd, n_seq, n_head, n_head_kv, hd, k_pages, v_pages, k_scales, v_scales,
+                    block_table, max_pages, page, ctx_len, max_ctx ? max_ctx : 1, out};
+    CK(mvb::paged_attn_decode_split(a, as_stream(stream)));
+    return MV_OK;
+}
+
 MV_API int mv_paged_attn_prefill(int kv_type, const float* q, uint64_t n_q, uint64_t n_head, uint64_t n_head_kv,
                                  uint64_t hd, const void* k_pages, const void* v_pages, const float* k_scales,
                                  const float* v_scales, const int32_t* block_table, uint64_t max_pages, uint64_t page,

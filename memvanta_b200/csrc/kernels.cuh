@@ -132,6 +132,9 @@ struct AttnArgs {
 };
 uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type);
 cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s);
+// attn_split.cu: the same, split over the context (warps merge their softmax
+// states); not bit-exact (~1e-6 of the output scale), for throughput
+cudaError_t paged_attn_decode_split(const AttnArgs& a, cudaStream_t s);
 // Prefill form: the query rows belong to ONE sequence (a.one_seq, or every
 // row's block-table row is the same), so groups of them share each staged K/V
 // tile; results identical to paged_attn_decode.

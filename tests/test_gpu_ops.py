@@ -125,6 +125,9 @@ def test_attention_golden(cuda, golden):
         out = mv.paged_attn_decode(kvt, dev(g["q"][None], cuda), n_head, n_head_kv, hd, kp, vp, table, n_pages, page,
                                    dev(np.array([n_ctx], np.int32), cuda), n_ctx, ks, vs)
         assert rel_err(host(out)[0], g[f"{tag}_att"]) <= 1e-4, tag
+        out2 = mv.paged_attn_decode_split(kvt, dev(g["q"][None], cuda), n_head, n_head_kv, hd, kp, vp, table, n_pages,
+                                          page, dev(np.array([n_ctx], np.int32), cuda), n_ctx, ks, vs)
+        assert rel_err(host(out2)[0], g[f"{tag}_att"]) <= 1e-4, tag
 
 
 @pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_Q8, mv.KV_Q8_0, mv.KV_F32])
@@ -159,6 +162,9 @@ def test_config4_ragged_paged_attention(cuda, oracle, kv_type):
                      dev(table, cuda), max_pages, page, kp, vp, ks, vs, seq=seq)
     out = host(mv.paged_attn_decode(kv_type, dev(q, cuda), n_head, n_head_kv, hd, kp, vp, dev(table, cuda), max_pages,
                                     page, dev(ctx, cuda), int(ctx.max()), ks, vs))
+    # split over the context (four warps per head merge their softmax states)
+    split = host(mv.paged_attn_decode_split(kv_type, dev(q, cuda), n_head, n_head_kv, hd, kp, vp, dev(table, cuda),
+                                            max_pages, page, dev(ctx, cuda), int(ctx.max()), ks, vs))
     # every sequence against the oracle (the reference loop per head).  The
     # kernel keeps the reference's evaluation order; its exp is correctly
     # rounded where the host libm's expf is within 0.502 ulp, and its double
@@ -171,6 +177,8 @@ def test_config4_ragged_paged_attention(cuda, oracle, kv_type):
         okp, ovp, oks, ovs = _oracle_cache(oracle, kv_type, seqs_k[s], seqs_v[s], table[s], page, total_pages * page)
         want = oracle.attn_decode(kv_type, q[s], n_head, n_head_kv, hd, okp, ovp, oks, ovs, table[s], page, int(ctx[s]))
         worst = max(worst, rel_err(out[s], want))
+        # split-K: not bit-exact; bar 1e-5 of the output scale
+        assert rel_err(split[s], want) <= 1e-5, (s, rel_err(split[s], want))
         same += int(np.sum(out[s] == want))
         total += want.size
     assert worst <= 1e-5 and same >= 0.9 * total, (worst, same, total)

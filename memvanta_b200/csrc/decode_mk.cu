@@ -32,10 +32,13 @@
 // took one tile more in one phase take one less later.  A tile is streamed
 // as chunks of 32 blocks (16 x 512 B of nibbles + 16 x 64 B of scales).
 //
-// Warps: 8 compute warps turn a staged chunk into per-block terms
-// (d_w * d_a, float(isum)); warp 8 runs the 16 rows' chains and writes the
-// outputs; warp 9 is the producer.  Warps 0-8 also run each phase's
-// prologue and, in CTAs 0..n_head-1, the attention.
+// Warps: 16 compute warps turn a staged chunk into per-block terms
+// (d_w * d_a, float(isum)), warp w for row w of the tile and lane b for
+// block b of the chunk; warp 16 runs the 16 rows' chains and writes the
+// outputs; warp 17 is the producer.  Warps 0-16 also run each phase's
+// prologue (one pass, x held in registers, the RMSNorm weights fetched
+// before the barrier) and, in CTAs 0..n_head-1, the attention, whose cached
+// K/V are requested at the start of the layer.
 //
 // Every wait is bounded (2 s without progress, tc::mbar_wait and the grid
 // barrier's spin): a wait that runs out raises the device-wide abort word
@@ -55,8 +58,8 @@ namespace mvb {
 
 namespace {
 
-constexpr int kComp = 8;                     // compute warps
-constexpr int kProdWarp = kComp + 1;         // warp 9
+constexpr int kComp = 16;                    // compute warps (warp w = row w of a tile)
+constexpr int kProdWarp = kComp + 1;         // warp 17
 constexpr int kWork = (kComp + 1) * 32;      // compute + chain threads
 constexpr int kThreads = kWork + 32;         // + producer
 constexpr int kTR = 16;                      // rows per tile
@@ -206,20 +209,54 @@ struct Act {
     float2* dc;
 };
 
-// Quantised activations of x (optionally RMS-normalised with w) into shared
-// memory, by the kWork threads.  x was written by other CTAs in this launch:
-// it is read from L2 (ld.cg), never from a possibly stale L1 line.
-__device__ void prologue(const float* x, const float* __restrict__ norm_w, float eps, int nb, const Act& a,
-                         double* red) {
+// Groups of 8 activations a work thread owns at most (kMaxNb * 4 groups).
+constexpr int kKeep = (kMaxNb * 4 + kWork - 1) / kWork;
+
+// RMSNorm weights of this thread's groups: immutable, so fetched before the
+// grid barrier that precedes the prologue.  The normalised input is n_embd
+// wide: at most kNormKeep groups per thread (n_embd <= kNormKeep * 8 * kWork).
+constexpr int kNormKeep = 2;
+struct NormPre {
+    float4 w[kNormKeep][2];
+};
+__device__ __forceinline__ void norm_fetch(NormPre& np, const float* __restrict__ norm_w, int nb) {
+    const int G = nb * 4, tid = threadIdx.x;
+#pragma unroll
+    for (int it = 0; it < kNormKeep; ++it) {
+        const int g = tid + it * kWork;
+        np.w[it][0] = np.w[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (g < G) {
+            np.w[it][0] = __ldg(reinterpret_cast<const float4*>(norm_w) + 2 * g);
+            np.w[it][1] = __ldg(reinterpret_cast<const float4*>(norm_w) + 2 * g + 1);
+        }
+    }
+}
+
+// Quantised activations of x (optionally RMS-normalised: np != nullptr) into
+// shared memory, by the kWork threads, in one pass: every thread's groups of
+// x are loaded at once and kept in registers through the sum of squares and
+// the quantisation.  x was written by other CTAs in this launch: it is read
+// from L2 (ld.cg), never from a possibly stale L1 line.
+__device__ void prologue(const float* x, const NormPre* np, float eps, int nb, const Act& a, double* red) {
     const int G = nb * 4, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int iters = (G + kWork - 1) / kWork;
+    const int iters = (G + kWork - 1) / kWork;  // uniform
     const float4* x4 = reinterpret_cast<const float4*>(x);
-    const bool rms = norm_w != nullptr;
+    float4 xv[kKeep][2];
+#pragma unroll
+    for (int it = 0; it < kKeep; ++it) {
+        const int g = tid + it * kWork;
+        xv[it][0] = xv[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (it < iters && g < G) {
+            xv[it][0] = __ldcg(x4 + 2 * g);
+            xv[it][1] = __ldcg(x4 + 2 * g + 1);
+        }
+    }
     float inv = 1.0f;
-    if (rms) {
+    if (np) {
         double ss = 0.0;
-        for (int g = tid; g < G; g += kWork) {
-            const float4 u = __ldcg(x4 + 2 * g), v = __ldcg(x4 + 2 * g + 1);
+#pragma unroll
+        for (int it = 0; it < kKeep; ++it) {
+            const float4 u = xv[it][0], v = xv[it][1];
             ss += (double)u.x * u.x + (double)u.y * u.y + (double)u.z * u.z + (double)u.w * u.w;
             ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
         }
@@ -231,20 +268,18 @@ __device__ void prologue(const float* x, const float* __restrict__ norm_w, float
         for (int w = 0; w < kWork / 32; ++w) tot += red[w];
         inv = 1.0f / sqrtf((float)(tot / (double)(nb * 32)) + eps);
     }
-    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int it = 0; it < kKeep; ++it) {
+        if (it >= iters) break;  // uniform across the CTA
         const int g = tid + it * kWork;
         const bool active = g < G;  // uniform over the 4 lanes of a block
-        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (active) {
-            const float4 u = __ldcg(x4 + 2 * g), w = __ldcg(x4 + 2 * g + 1);
-            v[0] = u.x, v[1] = u.y, v[2] = u.z, v[3] = u.w, v[4] = w.x, v[5] = w.y, v[6] = w.z, v[7] = w.w;
-            if (rms) {
-                const float4 n0 = __ldg(reinterpret_cast<const float4*>(norm_w) + 2 * g);
-                const float4 n1 = __ldg(reinterpret_cast<const float4*>(norm_w) + 2 * g + 1);
-                const float nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+        float v[8] = {xv[it][0].x, xv[it][0].y, xv[it][0].z, xv[it][0].w,
+                      xv[it][1].x, xv[it][1].y, xv[it][1].z, xv[it][1].w};
+        if (np && it < kNormKeep) {
+            const float nw[8] = {np->w[it][0].x, np->w[it][0].y, np->w[it][0].z, np->w[it][0].w,
+                                 np->w[it][1].x, np->w[it][1].y, np->w[it][1].z, np->w[it][1].w};
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * nw[i];  // (x*inv)*w as the reference
-            }
+            for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * nw[i];  // (x*inv)*w as the reference
         }
         // quantize_q8 (src/gguf_kernels.cpp:161-172): 4 neighbouring lanes hold one block
         float m = 0.0f;
@@ -488,7 +523,7 @@ struct Attn {
 
 // ------------------------------------------------------------- kernel
 template <int HD, int VS>
-__global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_constant__ MkArgs a) {
+__global__ void __maxnreg__(112) decode_mk_kernel(const __grid_constant__ MkArgs a) {
     extern __shared__ __align__(128) unsigned char sm[];
     __shared__ double red[kWork / 32];
     __shared__ float redf[HD / 32];
@@ -563,38 +598,36 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
         off = (off + q.T) % G;
         int it = 0;
         if (warp < kComp) {
-            // thread: row tid / 16, blocks bl and bl + 16 of the chunk (bl = tid % 16):
-            // the 8 lanes of a quarter-warp read 8 consecutive 16-byte blocks of
-            // one staged row -- no bank conflict on the dense TMA rows
-            const int row = (int)threadIdx.x >> 4, bl = (int)threadIdx.x & 15;
+            // warp w = row w of the tile, lane = block of the chunk: a warp reads
+            // one staged row (512 contiguous bytes) -- no bank conflict
+            const int row = warp, cb = lane;
             for (int t = q.t0; t < q.T; t += G) {
                 for (int c = 0; c < q.nch; ++c, ++k, ++it) {
                     const int s = (int)(k % (uint32_t)S);
                     bool ok = !*cta_abort;
                     if (ok) ok = tc::mbar_wait(full0 + 8 * s, (k / S) & 1u, a.status + 1, a.status, 43);
                     ok = __all_sync(0xffffffffu, ok);
-                    float2 o2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                    float2 o2 = make_float2(0.f, 0.f);
                     if (ok) {
                         const unsigned char* st = sm + P.ring + (size_t)s * kStage;
-                        const unsigned short* sc = reinterpret_cast<const unsigned short*>(st + kTR * kPayRow + row * kScRow);
-#pragma unroll
-                        for (int j = 0; j < 2; ++j) {
-                            const int cb = bl + 16 * j, b = c * kTC + cb;
-                            if (b < w.nb) {
-                                const int4 alo = act.lo[b], ahi = act.hi[b];
-                                const float2 dc = act.dc[b];
-                                const uint4 wv = *reinterpret_cast<const uint4*>(st + row * kPayRow + cb * 16);
-                                const int isum = block_isum(wv, alo, ahi, __float_as_int(dc.y));
-                                o2[j] = make_float2(half_bits_to_float(sc[cb]) * dc.x, (float)isum);
-                            }
+                        const int b = c * kTC + cb;
+                        if (b < w.nb) {
+                            const int4 alo = act.lo[b], ahi = act.hi[b];
+                            const float2 dc = act.dc[b];
+                            const uint4 wv = *reinterpret_cast<const uint4*>(st + row * kPayRow + cb * 16);
+                            const unsigned short sc =
+                                reinterpret_cast<const unsigned short*>(st + kTR * kPayRow + row * kScRow)[cb];
+                            const int isum = block_isum(wv, alo, ahi, __float_as_int(dc.y));
+                            // float(isum) exactly, without the int->float unit: |isum| < 2^22
+                            const float fi = __int_as_float(isum + 0x4B400000) - 12582912.0f;
+                            o2 = make_float2(half_bits_to_float(sc) * dc.x, fi);
                         }
                         __syncwarp();
                         if (lane == 0) tc::mbar_arrive(empty0 + 8 * s);
                     } else {
                         *cta_abort = 1;
                     }
-                    terms[((it & 1) * kTR + row) * kTT + bl] = o2[0];
-                    terms[((it & 1) * kTR + row) * kTT + bl + 16] = o2[1];
+                    terms[((it & 1) * kTR + row) * kTT + cb] = o2;
                     bar_named(kBarHand, kWork);  // terms of `it` complete; the chain of it-1 is done
                 }
             }
@@ -636,16 +669,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
         }
     };
 
+    NormPre np;
     for (int l = 0; l < a.n_layer; ++l) {
         const MkLayer& L = a.layers[l];
-        // ---- q|k|v (x is complete: the embedding kernel, or layer l-1's down phase)
-        if (l > 0) grid_sync(a, ++nbar, cta_abort);
-        if (!*cta_abort) prologue(a.x, L.attn_norm, a.eps, L.w[0].nb, act, red);
-        gemv(L.w[0], 0, a.qkv);
-        // ---- attention: the cached K/V of this head are requested before the barrier
+        // the cached K/V of this CTA's head (tokens of earlier steps) are
+        // requested first: they load while the q|k|v phase runs
         Attn<HD, VS> at(a, L, sm, P, cta);
         const bool attn_here = attn_cta && tid < HD && !*cta_abort;
         if (attn_here) at.prefetch();
+        // ---- q|k|v (x is complete: the embedding kernel, or layer l-1's down phase)
+        norm_fetch(np, L.attn_norm, L.w[0].nb);
+        if (l > 0) grid_sync(a, ++nbar, cta_abort);
+        if (!*cta_abort) prologue(a.x, &np, a.eps, L.w[0].nb, act, red);
+        gemv(L.w[0], 0, a.qkv);
+        // ---- attention
         grid_sync(a, ++nbar, cta_abort);
         if (attn_here) {
             if (!*cta_abort) at.run(redf, redd);
@@ -656,8 +693,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
         if (!*cta_abort) prologue(a.att, nullptr, a.eps, L.w[1].nb, act, red);
         gemv(L.w[1], 1, a.x);
         // ---- gate|up: x -> ff
+        norm_fetch(np, L.ffn_norm, L.w[2].nb);
         grid_sync(a, ++nbar, cta_abort);
-        if (!*cta_abort) prologue(a.x, L.ffn_norm, a.eps, L.w[2].nb, act, red);
+        if (!*cta_abort) prologue(a.x, &np, a.eps, L.w[2].nb, act, red);
         gemv(L.w[2], 2, a.ff);
         // ---- down: ff -> x += down rows
         grid_sync(a, ++nbar, cta_abort);
@@ -705,14 +743,15 @@ cudaError_t prepare(MkKernel k, int* smem_max) {
 }
 }  // namespace
 
-bool decode_mk_supported(int hd, int kv_type, int max_ctx, int max_pages, uint64_t max_nb, int* stages,
-                         std::string* why) {
+bool decode_mk_supported(int hd, int kv_type, int max_ctx, int max_pages, uint64_t max_nb, uint64_t norm_cols,
+                         int* stages, std::string* why) {
     auto no = [&](const std::string& r) {
         if (why) *why = r;
         return false;
     };
     if (kv_type != 0 && kv_type != 1) return no("KV cache type is not F32/F16");
     if (max_nb > (uint64_t)kMaxNb) return no("a weight is wider than " + std::to_string(kMaxNb * 32));
+    if (norm_cols > (uint64_t)kNormKeep * 8 * kWork) return no("n_embd above " + std::to_string(kNormKeep * 8 * kWork));
     const MkKernel k = mk_kernel(hd, kv_type);
     if (!k) return no("head_dim not 64/128/256");
     int smem_max = 0;

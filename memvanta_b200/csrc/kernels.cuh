@@ -216,8 +216,8 @@ struct MkArgs {
 };
 // Whether this shape runs on the persistent kernel; *stages = ring depth
 // that fits the device's shared memory.
-bool decode_mk_supported(int hd, int kv_type, int max_ctx, int max_pages, uint64_t max_nb, int* stages,
-                         std::string* why = nullptr);
+bool decode_mk_supported(int hd, int kv_type, int max_ctx, int max_pages, uint64_t max_nb, uint64_t norm_cols,
+                         int* stages, std::string* why = nullptr);
 cudaError_t decode_mk(const MkArgs& a, cudaStream_t s);
 
 }  // namespace mvb

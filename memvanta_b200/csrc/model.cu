@@ -899,7 +899,8 @@ void setup_persistent_decode(mv_model_s* m) {
     }
     int stages = 0;
     std::string why;
-    if (!mvb::decode_mk_supported((int)m->hd, m->kv_type, (int)m->n_ctx, (int)m->n_pages, max_nb, &stages, &why))
+    if (!mvb::decode_mk_supported((int)m->hd, m->kv_type, (int)m->n_ctx, (int)m->n_pages, max_nb, m->n_embd, &stages,
+                                  &why))
         return skip(why);
     m->mk_layers = dalloc<mvb::MkLayer>(m, m->n_layer);
     ck(cudaMemcpy(m->mk_layers, hl.data(), hl.size() * sizeof(mvb::MkLayer), cudaMemcpyHostToDevice), "layer table");

@@ -68,7 +68,7 @@ constexpr int kPayRow = kTC * 16;            // staged nibble bytes per row (one
 constexpr int kScRow = kTC * 2;              // staged scale bytes per row
 constexpr int kStage = kTR * (kPayRow + kScRow);
 constexpr int kTT = kTC + 2;                 // float2 per term row (padded)
-constexpr int kMaxNb = 512;                  // blocks of the widest input (K <= 16384)
+constexpr int kMaxNb = 384;                  // blocks of the widest input (K <= 12288)
 
 // named barriers (0 is not used once the producer has split off)
 constexpr int kBarHand = 2;  // compute warps + chain warp: terms hand-off
@@ -523,7 +523,7 @@ struct Attn {
 
 // ------------------------------------------------------------- kernel
 template <int HD, int VS>
-__global__ void __maxnreg__(112) decode_mk_kernel(const __grid_constant__ MkArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_constant__ MkArgs a) {
     extern __shared__ __align__(128) unsigned char sm[];
     __shared__ double red[kWork / 32];
     __shared__ float redf[HD / 32];

@@ -23,12 +23,13 @@
 // order, so outputs agree with the reference to ~1e-6 of their scale (the
 // tests hold it to 1e-5).  attention.cu's kernel stays the exact path.
 //
-// Memory: lane = token for the keys (one lane reads its token's head slice,
-// 16-byte loads, 32 rows in flight per warp), lane = 4 (8 for hd 256)
-// consecutive dimensions for the values (a warp reads a token's slice as one
-// coalesced row), the loads of 8 tokens issued before their FMA steps.  One
-// CTA per (sequence, head), 4 warps, a few KB of shared memory: many CTAs
-// per SM keep enough loads in flight for HBM.
+// Memory: a warp takes its tokens 32 at a time.  Keys: lane = token, the
+// token's whole head slice requested at once (16-byte loads, 32 slices in
+// flight per warp).  Values: lane = hd/32 consecutive dimensions, the 32
+// tokens' slices requested at once (each token's slice is one coalesced row
+// for the warp) before their FMA steps.  One CTA per (sequence, head), 4
+// warps, a few KB of shared memory: many CTAs per SM keep enough bytes in
+// flight for HBM.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -40,32 +41,42 @@ constexpr int kSW = 4;  // warps per (sequence, head)
 
 __device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
 
-// 8 consecutive cache elements of one token's row as floats (Q8 types: raw
-// int8 values; the scale is applied by the caller).
-template <int KVT>
-__device__ __forceinline__ void load8(const uint8_t* row, int d, float (&v)[8]) {
-    if constexpr (KVT == 0) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(row + d * 4));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(row + d * 4 + 16));
-        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-    } else if constexpr (KVT == 1) {
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(row + d * 2));
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+// DPL consecutive value elements of one token (lane's dimensions), as floats
+// (Q8 types: raw int8 values).
+template <int KVT, int DPL>
+struct VSlice {
+    static constexpr int ES = KVT == 0 ? 4 : KVT == 1 ? 2 : 1;
+    static constexpr int W = DPL * ES / 4 > 0 ? DPL * ES / 4 : 1;  // 32-bit words
+    uint32_t w[W];
+    __device__ __forceinline__ void load(const uint8_t* src) {
+        if constexpr (DPL * ES >= 16) {
 #pragma unroll
-        for (int l = 0; l < 8; ++l) v[l] = half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1))));
-    } else {
-        const uint2 w = __ldg(reinterpret_cast<const uint2*>(row + d));
-#pragma unroll
-        for (int l = 0; l < 8; ++l) v[l] = s8_to_f32(l < 4 ? w.x : w.y, l & 3);
+            for (int i = 0; i < W; i += 4) {
+                const uint4 u = __ldg(reinterpret_cast<const uint4*>(src) + i / 4);
+                w[i] = u.x, w[i + 1] = u.y, w[i + 2] = u.z, w[i + 3] = u.w;
+            }
+        } else if constexpr (DPL * ES == 8) {
+            const uint2 u = __ldg(reinterpret_cast<const uint2*>(src));
+            w[0] = u.x, w[1] = u.y;
+        } else if constexpr (DPL * ES == 4) {
+            w[0] = __ldg(reinterpret_cast<const uint32_t*>(src));
+        } else {  // 2 bytes (hd 64, int8)
+            w[0] = __ldg(reinterpret_cast<const unsigned short*>(src));
+        }
     }
-}
+    __device__ __forceinline__ float at(int j) const {
+        if constexpr (KVT == 0) return __uint_as_float(w[j]);
+        else if constexpr (KVT == 1) return half_bits_to_float((unsigned short)(w[j / 2] >> (16 * (j & 1))));
+        else return s8_to_f32(w[j / 4], j & 3);
+    }
+};
 
 template <int HD, int KVT>
 __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
     constexpr int DPL = HD / 32;                        // dimensions per lane (values)
     constexpr int ES = KVT == 0 ? 4 : KVT == 1 ? 2 : 1;  // bytes per element
+    constexpr int KW = HD * ES / 16;                    // 16-byte words of a key slice
     __shared__ float qs[HD];
-    __shared__ float ew[kSW][32 * 8];                   // e_t of the tokens a warp is on (one 256-token pass)
     __shared__ float mw[kSW];
     __shared__ double dw[kSW];
     __shared__ float ow[kSW][HD];
@@ -75,13 +86,15 @@ __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
     const size_t row_bytes = (size_t)kv_dim * ES;
     const size_t head_off = (size_t)kh * HD * ES;
     const int32_t* tbl = a.block_table + (a.one_seq ? 0 : (size_t)s) * a.max_pages;
+    const uint8_t* kp = static_cast<const uint8_t*>(a.k_pages);
+    const uint8_t* vp = static_cast<const uint8_t*>(a.v_pages);
     pdl_trigger();
     pdl_wait();
     const int ctx = a.ctx_len[s];
     for (int i = tid; i < HD; i += kSW * 32) qs[i] = a.q[(size_t)s * a.q_stride + (size_t)h * HD + i];
     __syncthreads();
     auto slot_of = [&](int t) -> size_t { return (size_t)__ldg(tbl + t / page) * page + t % page; };
-    // this warp's tokens
+    // this warp's tokens: a contiguous quarter of the context, in groups of 32
     const int per = (ctx + kSW - 1) / kSW;
     const int t0 = min(ctx, warp * per), t1 = min(ctx, t0 + per);
     float m = -INFINITY;
@@ -90,109 +103,84 @@ __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
 #pragma unroll
     for (int j = 0; j < DPL; ++j) o[j] = 0.0f;
     const float root = sqrtf((float)HD);
-    // passes of up to 256 tokens: scores (lane = token, 8 per lane), then the
-    // running max is raised and the partial sums rescaled once per pass
-    for (int p0 = t0; p0 < t1; p0 += 256) {
-        const int np = min(256, t1 - p0);
-        float sc[8];
-        float pm = -INFINITY;
+    for (int g0 = t0; g0 < t1; g0 += 32) {
+        const int n = min(32, t1 - g0);
+        // scores: lane = token, the whole key slice requested at once
+        const int t = g0 + lane;
+        const bool live = lane < n;
+        const size_t slot = live ? slot_of(t) : 0;
+        float sc = -INFINITY;
+        {
+            uint4 kw[KW];
+            const uint4* krow = reinterpret_cast<const uint4*>(kp + slot * row_bytes + head_off);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int tt = i * 32 + lane;
-            sc[i] = -INFINITY;
-            if (tt < np) {
-                const int t = p0 + tt;
-                const size_t slot = slot_of(t);
-                const uint8_t* row = static_cast<const uint8_t*>(a.k_pages) + slot * row_bytes + head_off;
-                float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-                for (int d = 0; d < HD; d += 8) {
-                    float kv[8];
-                    load8<KVT>(row, d, kv);
-                    float sc8 = 1.0f;
-                    if constexpr (KVT == 3) sc8 = __ldg(a.k_scales + slot * (kv_dim / 32) + (kh * HD + d) / 32);
+            for (int i = 0; i < KW; ++i) kw[i] = live ? __ldg(krow + i) : make_uint4(0u, 0u, 0u, 0u);
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                    for (int l = 0; l < 8; ++l)
-                        acc[l] = fmaf(qs[d + l], KVT == 3 ? kv[l] * sc8 : kv[l], acc[l]);
+            for (int d = 0; d < HD; d += 8) {
+                float kv[8];
+                if constexpr (KVT == 0) {
+                    const uint4 u0 = kw[d / 4], u1 = kw[d / 4 + 1];
+                    kv[0] = __uint_as_float(u0.x), kv[1] = __uint_as_float(u0.y), kv[2] = __uint_as_float(u0.z),
+                    kv[3] = __uint_as_float(u0.w), kv[4] = __uint_as_float(u1.x), kv[5] = __uint_as_float(u1.y),
+                    kv[6] = __uint_as_float(u1.z), kv[7] = __uint_as_float(u1.w);
+                } else if constexpr (KVT == 1) {
+                    const uint4 u = kw[d / 8];
+                    const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int l = 0; l < 8; ++l) kv[l] = half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1))));
+                } else {
+                    const uint4 u = kw[d / 16];
+                    const uint32_t lo = (d & 8) ? u.z : u.x, hi = (d & 8) ? u.w : u.y;
+#pragma unroll
+                    for (int l = 0; l < 8; ++l) kv[l] = s8_to_f32(l < 4 ? lo : hi, l & 3);
                 }
-                float dot = acc[0];
+                float sc8 = 1.0f;
+                if constexpr (KVT == 3) sc8 = live ? __ldg(a.k_scales + slot * (kv_dim / 32) + (kh * HD + d) / 32) : 0.f;
 #pragma unroll
-                for (int l = 1; l < 8; ++l) dot += acc[l];
-                if constexpr (KVT == 2) dot = dot * __ldg(a.k_scales + slot);
-                sc[i] = dot / root;
-                pm = fmaxf(pm, sc[i]);
+                for (int l = 0; l < 8; ++l) acc[l] = fmaf(qs[d + l], KVT == 3 ? kv[l] * sc8 : kv[l], acc[l]);
             }
+            float dot = acc[0];
+#pragma unroll
+            for (int l = 1; l < 8; ++l) dot += acc[l];
+            if constexpr (KVT == 2) dot = dot * (live ? __ldg(a.k_scales + slot) : 0.f);
+            if (live) sc = dot / root;
         }
-        pm = warp_max(pm);
-        const float nm = fmaxf(m, pm);
-        // rescale what this warp summed so far to the new max
-        if (m != nm && m != -INFINITY) {
+        // the running max, the sums rescaled when it rises
+        const float nm = fmaxf(m, warp_max(sc));
+        if (nm != m && m != -INFINITY) {
             const float c = expf_cr(m - nm);
             den *= (double)c;
 #pragma unroll
             for (int j = 0; j < DPL; ++j) o[j] *= c;
         }
         m = nm;
-        double pden = 0.0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int tt = i * 32 + lane;
-            const float e = tt < np ? expf_cr(sc[i] - m) : 0.0f;
-            if (tt < np) ew[warp][tt] = e;
-            pden += (double)e;
-        }
-        den += warp_sum_d(pden);
-        __syncwarp();
-        // values: lane owns dimensions lane*DPL .. +DPL-1, tokens in order,
-        // the loads of 8 tokens before their FMA steps
+        float e = live ? expf_cr(sc - m) : 0.0f;
+        den += warp_sum_d((double)e);
+        // values: lane = DPL dimensions, the group's slices requested at once
         const size_t voff = head_off + (size_t)lane * DPL * ES;
-        for (int tt = 0; tt < np; tt += 8) {
-            const int n8 = min(8, np - tt);
-            float v[8][DPL];
-            float al[8];
+        VSlice<KVT, DPL> v[32];
+        float vs = 1.0f;  // this lane's token's value scale (Q8 types)
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                al[u] = 0.0f;
-#pragma unroll
-                for (int j = 0; j < DPL; ++j) v[u][j] = 0.0f;
-                if (u < n8) {
-                    const int t = p0 + tt + u;
-                    const size_t slot = slot_of(t);
-                    const uint8_t* src = static_cast<const uint8_t*>(a.v_pages) + slot * row_bytes + voff;
-                    al[u] = ew[warp][tt + u];
-                    // DPL consecutive elements: two per load (hd 64 gives lanes two)
-                    if constexpr (KVT == 0) {
-#pragma unroll
-                        for (int j = 0; j < DPL; j += 2) {
-                            const float2 f = __ldg(reinterpret_cast<const float2*>(src) + j / 2);
-                            v[u][j] = f.x, v[u][j + 1] = f.y;
-                        }
-                    } else if constexpr (KVT == 1) {
-#pragma unroll
-                        for (int j = 0; j < DPL; j += 2) {
-                            const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(src) + j / 2);
-                            v[u][j] = half_bits_to_float(w & 0xffff);
-                            v[u][j + 1] = half_bits_to_float(w >> 16);
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < DPL; j += 2) {
-                            const uint32_t w = __ldg(reinterpret_cast<const unsigned short*>(src) + j / 2);
-                            v[u][j] = s8_to_f32(w, 0);
-                            v[u][j + 1] = s8_to_f32(w, 1);
-                        }
-                        // one scale per token (Q8) or per 32-element block (Q8_0)
-                        al[u] *= KVT == 2 ? __ldg(a.v_scales + slot)
-                                          : __ldg(a.v_scales + slot * (kv_dim / 32) + (kh * HD + lane * DPL) / 32);
-                    }
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-#pragma unroll
-                for (int j = 0; j < DPL; ++j) o[j] = fmaf(al[u], v[u][j], o[j]);
+        for (int u = 0; u < 32; ++u) {
+            const size_t su = __shfl_sync(0xffffffffu, slot, u);
+            if (u < n) v[u].load(vp + su * row_bytes + voff);
         }
-        __syncwarp();
+        if constexpr (KVT == 2) vs = live ? __ldg(a.v_scales + slot) : 0.f;
+        (void)vs;
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+            if (u < n) {
+                float al = __shfl_sync(0xffffffffu, e, u);
+                if constexpr (KVT == 2) al = al * __shfl_sync(0xffffffffu, vs, u);
+                if constexpr (KVT == 3) {
+                    const size_t su = __shfl_sync(0xffffffffu, slot, u);
+                    al = al * __ldg(a.v_scales + su * (kv_dim / 32) + (kh * HD + lane * DPL) / 32);
+                }
+#pragma unroll
+                for (int j = 0; j < DPL; ++j) o[j] = fmaf(al, v[u].at(j), o[j]);
+            }
+        }
     }
     // merge the warps' states in warp order
     if (lane == 0) {

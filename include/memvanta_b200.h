@@ -287,8 +287,8 @@ MV_API int mv_model_generate_greedy(mv_model_t m, int32_t token, uint64_t n, int
 /* The model's stream (cudaStream_t) -- for event timing by the caller. */
 MV_API void* mv_model_stream(mv_model_t m);
 /* 1 when a decode step runs every layer in one persistent kernel (one GPU,
- * Q4_0 layer weights, F16/F32 KV; MV_DECODE_PERSISTENT=0 in the environment
- * at mv_model_open turns it off), 0 when it runs one kernel per operation.
+ * Q4_0 layer weights, F16/F32 KV; chosen with MV_DECODE_PERSISTENT=1 in the
+ * environment at mv_model_open), 0 when it runs one kernel per operation.
  * Both give identical outputs.  No counterpart in the reference. */
 MV_API int mv_model_decode_persistent(mv_model_t m);
 

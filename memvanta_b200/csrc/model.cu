@@ -304,7 +304,7 @@ struct mv_model_s {
     float* logits_host = nullptr;          // pinned
     cudaGraphExec_t graph_logits = nullptr, graph_nologits = nullptr;
     // one GPU: every layer of a decode step in one persistent kernel
-    // (decode_mk.cu); off with MV_DECODE_PERSISTENT=0 or where unsupported
+    // (decode_mk.cu), with MV_DECODE_PERSISTENT=1 where supported
     bool mk = false;
     int mk_stages = 0;
     mvb::MkLayer* mk_layers = nullptr;     // device [n_layer]
@@ -848,13 +848,14 @@ void ready_decode(mv_model_s* m) {
 }
 
 // One GPU, Q4_0 layer weights, F16/F32 KV: the decode layers run as one
-// persistent kernel (decode_mk.cu) unless MV_DECODE_PERSISTENT=0.  Its
+// persistent kernel (decode_mk.cu) when MV_DECODE_PERSISTENT=1.  Its
 // outputs are bit-identical to the per-kernel path.
 void setup_persistent_decode(mv_model_s* m) {
-    const char* env = std::getenv("MV_DECODE_PERSISTENT");
-    if (env && std::string(env) == "0") return;
+    // opt-in while its step is slower than the per-kernel path's;
     // MV_DECODE_PERSISTENT=1 demands it: a model it cannot serve fails to open
-    const bool forced = env && std::string(env) == "1";
+    const char* env = std::getenv("MV_DECODE_PERSISTENT");
+    if (!env || std::string(env) != "1") return;
+    const bool forced = true;
     auto skip = [&](const std::string& why) {
         if (forced) throw ModelError(MV_ERR_UNSUPPORTED, "persistent decode kernel: " + why);
     };

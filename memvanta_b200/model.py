@@ -102,7 +102,8 @@ class LlamaModel:
 
     @property
     def decode_persistent(self) -> bool:
-        """Whether a decode step runs every layer in one persistent kernel."""
+        """Whether a decode step runs every layer in one persistent kernel
+        (MV_DECODE_PERSISTENT=1 at open)."""
         return bool(load().mv_model_decode_persistent(self._m))
 
     def forward(self, token: int, compute_logits: bool = True, out: np.ndarray | None = None) -> np.ndarray:

@@ -11,23 +11,21 @@
 // softmax state, merged once at the end in a fixed order:
 //
 //   warp w, tokens [t0_w, t1_w):
-//     s_t  = dot(q, k_t) / sqrt(hd)       the reference's 8-lane FMA dot and
-//                                         left-to-right sum (bit-identical)
+//     s_t  = dot(q, k_t) / sqrt(hd)       lane partials summed in a warp tree
 //     m_w  = max s_t,  e_t = exp(s_t - m_w),  den_w = sum e_t (double)
 //     o_w[d] = sum_t e_t * v_t[d]          (fp32 FMA chain per dimension)
 //   merge:  M = max_w m_w,  c_w = exp(m_w - M)
 //     den = sum_w den_w * c_w (double),  out[d] = (sum_w o_w[d] * c_w) * float(1/den)
 //
-// Scores are exact; the weights e_t * c_w differ from the reference's
-// exp(s_t - M) by a rounding or two and the output is summed in another
-// order, so outputs agree with the reference to ~1e-6 of their scale (the
-// tests hold it to 1e-5).  attention.cu's kernel stays the exact path.
+// The dot products, the weights e_t * c_w (against the reference's
+// exp(s_t - M)) and the output sums each round in another order than the
+// reference's, so outputs agree with it to ~1e-6 of their scale (the tests
+// hold it to 1e-5); attention.cu's kernel stays the exact path.
 //
-// Memory: a warp takes its tokens 32 at a time.  Keys: lane = token, the
-// token's whole head slice requested at once (16-byte loads, 32 slices in
-// flight per warp).  Values: lane = hd/32 consecutive dimensions, the 32
-// tokens' slices requested at once (each token's slice is one coalesced row
-// for the warp) before their FMA steps.  One CTA per (sequence, head), 4
+// Memory: a warp takes its tokens 32 at a time; for keys and values alike
+// lane l holds dimensions [l*hd/32, (l+1)*hd/32) of a token, so a token's
+// head slice is one coalesced row for the warp, and the 32 tokens' slices
+// are requested at once before they are used.  One CTA per (sequence, head), 4
 // warps, a few KB of shared memory: many CTAs per SM keep enough bytes in
 // flight for HBM.
 #include "common.cuh"
@@ -75,7 +73,6 @@ template <int HD, int KVT>
 __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
     constexpr int DPL = HD / 32;                        // dimensions per lane (values)
     constexpr int ES = KVT == 0 ? 4 : KVT == 1 ? 2 : 1;  // bytes per element
-    constexpr int KW = HD * ES / 16;                    // 16-byte words of a key slice
     __shared__ float qs[HD];
     __shared__ float mw[kSW];
     __shared__ double dw[kSW];
@@ -103,48 +100,43 @@ __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
 #pragma unroll
     for (int j = 0; j < DPL; ++j) o[j] = 0.0f;
     const float root = sqrtf((float)HD);
+    float qr[DPL];  // the query elements this lane multiplies
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) qr[j] = qs[lane * DPL + j];
     for (int g0 = t0; g0 < t1; g0 += 32) {
         const int n = min(32, t1 - g0);
-        // scores: lane = token, the whole key slice requested at once
+        // scores: the warp reads one token's key slice as one coalesced row
+        // (lane = hd/32 consecutive elements), the 32 tokens' rows requested
+        // at once, then one dot per token (lane partials summed by shuffles)
         const int t = g0 + lane;
         const bool live = lane < n;
         const size_t slot = live ? slot_of(t) : 0;
+        const size_t koff = head_off + (size_t)lane * DPL * ES;
         float sc = -INFINITY;
         {
-            uint4 kw[KW];
-            const uint4* krow = reinterpret_cast<const uint4*>(kp + slot * row_bytes + head_off);
+            VSlice<KVT, DPL> kk[32];
 #pragma unroll
-            for (int i = 0; i < KW; ++i) kw[i] = live ? __ldg(krow + i) : make_uint4(0u, 0u, 0u, 0u);
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int d = 0; d < HD; d += 8) {
-                float kv[8];
-                if constexpr (KVT == 0) {
-                    const uint4 u0 = kw[d / 4], u1 = kw[d / 4 + 1];
-                    kv[0] = __uint_as_float(u0.x), kv[1] = __uint_as_float(u0.y), kv[2] = __uint_as_float(u0.z),
-                    kv[3] = __uint_as_float(u0.w), kv[4] = __uint_as_float(u1.x), kv[5] = __uint_as_float(u1.y),
-                    kv[6] = __uint_as_float(u1.z), kv[7] = __uint_as_float(u1.w);
-                } else if constexpr (KVT == 1) {
-                    const uint4 u = kw[d / 8];
-                    const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                    for (int l = 0; l < 8; ++l) kv[l] = half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1))));
-                } else {
-                    const uint4 u = kw[d / 16];
-                    const uint32_t lo = (d & 8) ? u.z : u.x, hi = (d & 8) ? u.w : u.y;
-#pragma unroll
-                    for (int l = 0; l < 8; ++l) kv[l] = s8_to_f32(l < 4 ? lo : hi, l & 3);
-                }
-                float sc8 = 1.0f;
-                if constexpr (KVT == 3) sc8 = live ? __ldg(a.k_scales + slot * (kv_dim / 32) + (kh * HD + d) / 32) : 0.f;
-#pragma unroll
-                for (int l = 0; l < 8; ++l) acc[l] = fmaf(qs[d + l], KVT == 3 ? kv[l] * sc8 : kv[l], acc[l]);
+            for (int u = 0; u < 32; ++u) {
+                const size_t su = __shfl_sync(0xffffffffu, slot, u);
+                if (u < n) kk[u].load(kp + su * row_bytes + koff);
             }
-            float dot = acc[0];
 #pragma unroll
-            for (int l = 1; l < 8; ++l) dot += acc[l];
-            if constexpr (KVT == 2) dot = dot * (live ? __ldg(a.k_scales + slot) : 0.f);
-            if (live) sc = dot / root;
+            for (int u = 0; u < 32; ++u) {
+                if (u < n) {  // warp-uniform
+                    float part = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < DPL; ++j) part = fmaf(qr[j], kk[u].at(j), part);
+                    if constexpr (KVT == 3) {
+                        const size_t su = __shfl_sync(0xffffffffu, slot, u);
+                        part *= __ldg(a.k_scales + su * (kv_dim / 32) + (kh * HD + lane * DPL) / 32);
+                    }
+                    part = warp_sum(part);
+                    if (lane == u) sc = part;
+                }
+            }
+            if constexpr (KVT == 2) sc = sc * (live ? __ldg(a.k_scales + slot) : 0.f);
+            if (live) sc = sc / root;
+            else sc = -INFINITY;
         }
         // the running max, the sums rescaled when it rises
         const float nm = fmaxf(m, warp_max(sc));
@@ -213,10 +205,10 @@ template <int HD>
 cudaError_t launch_split_hd(const AttnArgs& a, cudaStream_t s) {
     const dim3 grid((unsigned)a.n_seq, (unsigned)a.n_head);
     switch (a.kv_type) {
-        case 0: return launch_pdl(attn_split_kernel<HD, 0>, grid, dim3(kSW * 32), 0, s, a);
-        case 1: return launch_pdl(attn_split_kernel<HD, 1>, grid, dim3(kSW * 32), 0, s, a);
-        case 2: return launch_pdl(attn_split_kernel<HD, 2>, grid, dim3(kSW * 32), 0, s, a);
-        case 3: return launch_pdl(attn_split_kernel<HD, 3>, grid, dim3(kSW * 32), 0, s, a);
+        case 0: return launch_opt(false, attn_split_kernel<HD, 0>, grid, dim3(kSW * 32), 0, s, a);
+        case 1: return launch_opt(false, attn_split_kernel<HD, 1>, grid, dim3(kSW * 32), 0, s, a);
+        case 2: return launch_opt(false, attn_split_kernel<HD, 2>, grid, dim3(kSW * 32), 0, s, a);
+        case 3: return launch_opt(false, attn_split_kernel<HD, 3>, grid, dim3(kSW * 32), 0, s, a);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -548,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
 
     if (warp == kProdWarp) {
         // ------------------------------------------------------ producer
-        uint32_t k = 0;
+        uint32_t k = 0, ks = 0, kpar = 0;  // chunks issued; stage and phase parity of chunk k
         bool ok = true;
         int off = 0;
         for (int l = 0; ok && l < a.n_layer; ++l) {
@@ -559,8 +559,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
                 off = (off + q.T) % G;
                 for (int t = q.t0; ok && t < q.T; t += G) {
                     for (int c = 0; c < q.nch; ++c, ++k) {
-                        const int s = (int)(k % (uint32_t)S);
-                        ok = tc::mbar_wait(empty0 + 8 * s, ((k / S) & 1u) ^ 1u, a.status + 1, a.status, 41);
+                        const int s = (int)ks;
+                        const uint32_t par = kpar;
+                        if (++ks == (uint32_t)S) ks = 0, kpar ^= 1u;
+                        ok = tc::mbar_wait(empty0 + 8 * s, par ^ 1u, a.status + 1, a.status, 41);
                         ok = __all_sync(0xffffffffu, ok);
                         if (!ok) break;
                         // one box of nibbles (16 rows x 512 B) and one of scales (16 rows x
@@ -588,12 +590,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
                   reinterpret_cast<float2*>(reinterpret_cast<int4*>(sm + P.act) + 2 * kMaxNb)};
     float2* terms = reinterpret_cast<float2*>(sm + P.terms);
     unsigned nbar = 0;
-    uint32_t k = 0;
+    uint32_t ks = 0, kpar = 0;  // stage and phase parity of the next chunk
     int off = 0;
     const bool attn_cta = cta < a.n_head;
 
     // One GEMV phase of this CTA: its tiles, chunk by chunk.
-    auto gemv = [&](const MkGemv& w, int epi, float* y) {
+    auto gemv = [&](const MkGemv& wg, int epi, float* y) {
+        const MkGemv w = wg;  // in registers: the loops below store to global memory
         const Seq q = seq_of(w, cta, G, off);
         off = (off + q.T) % G;
         int it = 0;
@@ -602,10 +605,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
             // one staged row (512 contiguous bytes) -- no bank conflict
             const int row = warp, cb = lane;
             for (int t = q.t0; t < q.T; t += G) {
-                for (int c = 0; c < q.nch; ++c, ++k, ++it) {
-                    const int s = (int)(k % (uint32_t)S);
+                for (int c = 0; c < q.nch; ++c, ++it) {
+                    const int s = (int)ks;
+                    const uint32_t par = kpar;
+                    if (++ks == (uint32_t)S) ks = 0, kpar ^= 1u;
                     bool ok = !*cta_abort;
-                    if (ok) ok = tc::mbar_wait(full0 + 8 * s, (k / S) & 1u, a.status + 1, a.status, 43);
+                    if (ok) ok = tc::mbar_wait(full0 + 8 * s, par, a.status + 1, a.status, 43);
                     ok = __all_sync(0xffffffffu, ok);
                     float2 o2 = make_float2(0.f, 0.f);
                     if (ok) {
@@ -635,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const __grid_con
             // chain warp: lane = row of the tile
             float sum = 0.0f;
             for (int t = q.t0; t < q.T; t += G) {
-                for (int c = 0; c < q.nch; ++c, ++k, ++it) {
+                for (int c = 0; c < q.nch; ++c, ++it) {
                     bar_named(kBarHand, kWork);
                     if (lane < kTR) {
                         const float2* tr = terms + ((it & 1) * kTR + lane) * kTT;

@@ -22,12 +22,12 @@
 // reference's, so outputs agree with it to ~1e-6 of their scale (the tests
 // hold it to 1e-5); attention.cu's kernel stays the exact path.
 //
-// Memory: a warp takes its tokens 32 at a time; for keys and values alike
-// lane l holds dimensions [l*hd/32, (l+1)*hd/32) of a token, so a token's
-// head slice is one coalesced row for the warp, and the 32 tokens' slices
-// are requested at once before they are used.  One CTA per (sequence, head), 4
-// warps, a few KB of shared memory: many CTAs per SM keep enough bytes in
-// flight for HBM.
+// Memory: each warp streams its tokens through its own ring of shared-memory
+// stages (16 tokens' key and value head slices per stage, 16-byte cp.async
+// copies spread over the lanes, two stages in flight while one is used), so
+// no warp waits for another before the merge.  Scores: two lanes per token,
+// each over half of the head's dimensions; values: lane = hd/32 consecutive
+// dimensions.  One CTA per (sequence, head), 4 warps.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -39,40 +39,42 @@ constexpr int kSW = 4;  // warps per (sequence, head)
 
 __device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
 
-// DPL consecutive value elements of one token (lane's dimensions), as floats
-// (Q8 types: raw int8 values).
-template <int KVT, int DPL>
-struct VSlice {
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+constexpr int kTok = 16;  // tokens per stage
+
+// Shared-memory plan of one CTA: the query, the block-table row, and per warp
+// a ring of S stages of kTok tokens' key and value head slices (rows padded
+// by 16 bytes) plus their scales (Q8: one per token, Q8_0: hd/32 per token).
+template <int HD, int KVT>
+struct SplitPlan {
     static constexpr int ES = KVT == 0 ? 4 : KVT == 1 ? 2 : 1;
-    static constexpr int W = DPL * ES / 4 > 0 ? DPL * ES / 4 : 1;  // 32-bit words
-    uint32_t w[W];
-    __device__ __forceinline__ void load(const uint8_t* src) {
-        if constexpr (DPL * ES >= 16) {
-#pragma unroll
-            for (int i = 0; i < W; i += 4) {
-                const uint4 u = __ldg(reinterpret_cast<const uint4*>(src) + i / 4);
-                w[i] = u.x, w[i + 1] = u.y, w[i + 2] = u.z, w[i + 3] = u.w;
-            }
-        } else if constexpr (DPL * ES == 8) {
-            const uint2 u = __ldg(reinterpret_cast<const uint2*>(src));
-            w[0] = u.x, w[1] = u.y;
-        } else if constexpr (DPL * ES == 4) {
-            w[0] = __ldg(reinterpret_cast<const uint32_t*>(src));
-        } else {  // 2 bytes (hd 64, int8)
-            w[0] = __ldg(reinterpret_cast<const unsigned short*>(src));
-        }
-    }
-    __device__ __forceinline__ float at(int j) const {
-        if constexpr (KVT == 0) return __uint_as_float(w[j]);
-        else if constexpr (KVT == 1) return half_bits_to_float((unsigned short)(w[j / 2] >> (16 * (j & 1))));
-        else return s8_to_f32(w[j / 4], j & 3);
-    }
+    static constexpr int SL = HD * ES;        // bytes of one head slice
+    static constexpr int SLP = SL + 16;       // padded row
+    static constexpr int NSC = KVT == 2 ? 1 : KVT == 3 ? HD / 32 : 0;  // scales per token
+    static constexpr int S = KVT == 0 ? 2 : 3;                         // ring stages
+    static constexpr int STAGE = 2 * kTok * SLP + 2 * kTok * NSC * 4;
+    static constexpr int WARP = S * STAGE;
 };
 
 template <int HD, int KVT>
 __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
-    constexpr int DPL = HD / 32;                        // dimensions per lane (values)
-    constexpr int ES = KVT == 0 ? 4 : KVT == 1 ? 2 : 1;  // bytes per element
+    using P = SplitPlan<HD, KVT>;
+    constexpr int DPL = HD / 32;  // value dimensions per lane
+    constexpr int ES = P::ES, SL = P::SL, SLP = P::SLP, NSC = P::NSC, S = P::S;
+    extern __shared__ __align__(16) unsigned char smem[];
     __shared__ float qs[HD];
     __shared__ float mw[kSW];
     __shared__ double dw[kSW];
@@ -82,62 +84,106 @@ __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
     const int kv_dim = (int)(a.n_head_kv * HD), page = (int)a.page;
     const size_t row_bytes = (size_t)kv_dim * ES;
     const size_t head_off = (size_t)kh * HD * ES;
-    const int32_t* tbl = a.block_table + (a.one_seq ? 0 : (size_t)s) * a.max_pages;
     const uint8_t* kp = static_cast<const uint8_t*>(a.k_pages);
     const uint8_t* vp = static_cast<const uint8_t*>(a.v_pages);
-    pdl_trigger();
-    pdl_wait();
+    int* tbl = reinterpret_cast<int*>(smem + kSW * P::WARP);
+    unsigned char* ring = smem + warp * P::WARP;
     const int ctx = a.ctx_len[s];
+    const int npg = (ctx + page - 1) / page;
+    const int32_t* trow = a.block_table + (a.one_seq ? 0 : (size_t)s) * a.max_pages;
+    for (int i = tid; i < npg; i += kSW * 32) tbl[i] = trow[i];
     for (int i = tid; i < HD; i += kSW * 32) qs[i] = a.q[(size_t)s * a.q_stride + (size_t)h * HD + i];
     __syncthreads();
-    auto slot_of = [&](int t) -> size_t { return (size_t)__ldg(tbl + t / page) * page + t % page; };
-    // this warp's tokens: a contiguous quarter of the context, in groups of 32
+    auto slot_of = [&](int t) -> size_t { return (size_t)tbl[t / page] * page + t % page; };
+    // this warp's tokens: a contiguous quarter of the context, in stages of kTok
     const int per = (ctx + kSW - 1) / kSW;
     const int t0 = min(ctx, warp * per), t1 = min(ctx, t0 + per);
+    const int ng = (t1 - t0 + kTok - 1) / kTok;
+    // stage g of this warp into ring slot g % S: kTok tokens' key and value
+    // slices (16-byte copies spread over the lanes) and their scales
+    auto issue = [&](int g) {
+        if (g < ng) {
+            unsigned char* base = ring + (g % S) * P::STAGE;
+            constexpr int CPT = SL / 16;  // 16-byte chunks per slice
+            const int tb = t0 + g * kTok;
+            for (int c = lane; c < 2 * kTok * CPT; c += 32) {
+                const int kv = c / (kTok * CPT), rem = c % (kTok * CPT), u = rem / CPT, off = (rem % CPT) * 16;
+                const int t = tb + u;
+                if (t < t1)
+                    cp_async16(base + (kv * kTok + u) * SLP + off,
+                               (kv ? vp : kp) + slot_of(t) * row_bytes + head_off + off);
+            }
+            if constexpr (NSC > 0) {
+                const int u = lane & 15, kv = lane >> 4, t = tb + u;
+                if (t < t1) {
+                    const float* src = (kv ? a.v_scales : a.k_scales) +
+                                       (KVT == 2 ? slot_of(t) : slot_of(t) * (kv_dim / 32) + kh * NSC);
+                    float* dst = reinterpret_cast<float*>(base + 2 * kTok * SLP) + (kv * kTok + u) * NSC;
+#pragma unroll
+                    for (int i = 0; i < NSC; ++i) cp_async4(dst + i, src + i);
+                }
+            }
+        }
+        cp_async_commit();
+    };
     float m = -INFINITY;
     double den = 0.0;
     float o[DPL];
 #pragma unroll
     for (int j = 0; j < DPL; ++j) o[j] = 0.0f;
     const float root = sqrtf((float)HD);
-    float qr[DPL];  // the query elements this lane multiplies
+    const int u = lane & 15, half = lane >> 4;  // scores: token u of the stage, half of its dimensions
 #pragma unroll
-    for (int j = 0; j < DPL; ++j) qr[j] = qs[lane * DPL + j];
-    for (int g0 = t0; g0 < t1; g0 += 32) {
-        const int n = min(32, t1 - g0);
-        // scores: the warp reads one token's key slice as one coalesced row
-        // (lane = hd/32 consecutive elements), the 32 tokens' rows requested
-        // at once, then one dot per token (lane partials summed by shuffles)
-        const int t = g0 + lane;
-        const bool live = lane < n;
-        const size_t slot = live ? slot_of(t) : 0;
-        const size_t koff = head_off + (size_t)lane * DPL * ES;
-        float sc = -INFINITY;
+    for (int k = 0; k < S - 1; ++k) issue(k);
+    for (int g = 0; g < ng; ++g) {
+        issue(g + S - 1);        // into the slot stage g-1 used (consumed before the last __syncwarp)
+        cp_async_wait<S - 1>();  // this lane's copies of stage g have landed
+        __syncwarp();            // ... and every lane's
+        const unsigned char* base = ring + (g % S) * P::STAGE;
+        const float* ksc = reinterpret_cast<const float*>(base + 2 * kTok * SLP);
+        const float* vsc = ksc + kTok * NSC;
+        const int n = min(kTok, t1 - (t0 + g * kTok));
+        // scores: two lanes per token, each over half of the dimensions
+        float part = 0.0f;
         {
-            VSlice<KVT, DPL> kk[32];
+            const unsigned char* kr = base + u * SLP + half * (SL / 2);
+            const float* qh = qs + half * (HD / 2);
+            if constexpr (KVT == 0) {
 #pragma unroll
-            for (int u = 0; u < 32; ++u) {
-                const size_t su = __shfl_sync(0xffffffffu, slot, u);
-                if (u < n) kk[u].load(kp + su * row_bytes + koff);
-            }
+                for (int d = 0; d < HD / 2; d += 4) {
+                    const float4 k4 = *reinterpret_cast<const float4*>(kr + d * 4);
+                    part = fmaf(qh[d], k4.x, part);
+                    part = fmaf(qh[d + 1], k4.y, part);
+                    part = fmaf(qh[d + 2], k4.z, part);
+                    part = fmaf(qh[d + 3], k4.w, part);
+                }
+            } else if constexpr (KVT == 1) {
 #pragma unroll
-            for (int u = 0; u < 32; ++u) {
-                if (u < n) {  // warp-uniform
-                    float part = 0.0f;
+                for (int d = 0; d < HD / 2; d += 8) {
+                    const uint4 w = *reinterpret_cast<const uint4*>(kr + d * 2);
+                    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                    for (int j = 0; j < DPL; ++j) part = fmaf(qr[j], kk[u].at(j), part);
-                    if constexpr (KVT == 3) {
-                        const size_t su = __shfl_sync(0xffffffffu, slot, u);
-                        part *= __ldg(a.k_scales + su * (kv_dim / 32) + (kh * HD + lane * DPL) / 32);
+                    for (int l = 0; l < 8; ++l)
+                        part = fmaf(qh[d + l], half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1)))), part);
+                }
+            } else {
+#pragma unroll
+                for (int bb = 0; bb < HD / 64; ++bb) {  // the 32-element blocks of this half
+                    float bs = 0.0f;
+#pragma unroll
+                    for (int d = 0; d < 32; d += 16) {
+                        const uint4 w = *reinterpret_cast<const uint4*>(kr + bb * 32 + d);
+                        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                        for (int l = 0; l < 16; ++l) bs = fmaf(qh[bb * 32 + d + l], s8_to_f32(ws[l / 4], l & 3), bs);
                     }
-                    part = warp_sum(part);
-                    if (lane == u) sc = part;
+                    part += KVT == 3 ? bs * ksc[u * NSC + half * (HD / 64) + bb] : bs;
                 }
             }
-            if constexpr (KVT == 2) sc = sc * (live ? __ldg(a.k_scales + slot) : 0.f);
-            if (live) sc = sc / root;
-            else sc = -INFINITY;
         }
+        float dot = part + __shfl_xor_sync(0xffffffffu, part, 16);
+        if constexpr (KVT == 2) dot = dot * ksc[u];
+        const float sc = u < n ? dot / root : -INFINITY;
         // the running max, the sums rescaled when it rises
         const float nm = fmaxf(m, warp_max(sc));
         if (nm != m && m != -INFINITY) {
@@ -147,33 +193,43 @@ __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
             for (int j = 0; j < DPL; ++j) o[j] *= c;
         }
         m = nm;
-        float e = live ? expf_cr(sc - m) : 0.0f;
-        den += warp_sum_d((double)e);
-        // values: lane = DPL dimensions, the group's slices requested at once
-        const size_t voff = head_off + (size_t)lane * DPL * ES;
-        VSlice<KVT, DPL> v[32];
-        float vs = 1.0f;  // this lane's token's value scale (Q8 types)
+        const float e = u < n ? expf_cr(sc - m) : 0.0f;
+        den += warp_sum_d(half == 0 ? (double)e : 0.0);
+        // values: lane = DPL consecutive dimensions, tokens in order
+        const unsigned char* vr = base + kTok * SLP + lane * DPL * ES;
+        for (int uu = 0; uu < n; ++uu) {
+            float al = __shfl_sync(0xffffffffu, e, uu);
+            if constexpr (KVT == 2) al = al * vsc[uu];
+            if constexpr (KVT == 3) al = al * vsc[uu * NSC + lane * DPL / 32];
+            const unsigned char* vv = vr + uu * SLP;
+            float v[DPL];
+            if constexpr (KVT == 0) {
 #pragma unroll
-        for (int u = 0; u < 32; ++u) {
-            const size_t su = __shfl_sync(0xffffffffu, slot, u);
-            if (u < n) v[u].load(vp + su * row_bytes + voff);
-        }
-        if constexpr (KVT == 2) vs = live ? __ldg(a.v_scales + slot) : 0.f;
-        (void)vs;
-#pragma unroll
-        for (int u = 0; u < 32; ++u) {
-            if (u < n) {
-                float al = __shfl_sync(0xffffffffu, e, u);
-                if constexpr (KVT == 2) al = al * __shfl_sync(0xffffffffu, vs, u);
-                if constexpr (KVT == 3) {
-                    const size_t su = __shfl_sync(0xffffffffu, slot, u);
-                    al = al * __ldg(a.v_scales + su * (kv_dim / 32) + (kh * HD + lane * DPL) / 32);
+                for (int j = 0; j < DPL; j += 2) {
+                    const float2 f = *reinterpret_cast<const float2*>(vv + j * 4);
+                    v[j] = f.x, v[j + 1] = f.y;
                 }
+            } else if constexpr (KVT == 1) {
 #pragma unroll
-                for (int j = 0; j < DPL; ++j) o[j] = fmaf(al, v[u].at(j), o[j]);
+                for (int j = 0; j < DPL; j += 2) {
+                    const uint32_t w = *reinterpret_cast<const uint32_t*>(vv + j * 2);
+                    v[j] = half_bits_to_float((unsigned short)(w & 0xffff));
+                    v[j + 1] = half_bits_to_float((unsigned short)(w >> 16));
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < DPL; j += 2) {
+                    const uint32_t w = *reinterpret_cast<const unsigned short*>(vv + j);
+                    v[j] = s8_to_f32(w, 0);
+                    v[j + 1] = s8_to_f32(w, 1);
+                }
             }
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) o[j] = fmaf(al, v[j], o[j]);
         }
+        __syncwarp();  // every lane is done with this slot before it is refilled
     }
+    cp_async_wait<0>();
     // merge the warps' states in warp order
     if (lane == 0) {
         mw[warp] = m;
@@ -201,14 +257,27 @@ __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
     }
 }
 
+template <int HD, int KVT>
+size_t split_smem(const AttnArgs& a) {
+    return (size_t)kSW * SplitPlan<HD, KVT>::WARP + ((a.max_ctx + a.page - 1) / a.page) * 4;
+}
+
+template <int HD, int KVT>
+cudaError_t launch_split(const AttnArgs& a, cudaStream_t s) {
+    const size_t smem = split_smem<HD, KVT>(a);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    ensure_smem_attr(attn_split_kernel<HD, KVT>, 200 * 1024);
+    return launch_opt(false, attn_split_kernel<HD, KVT>, dim3((unsigned)a.n_seq, (unsigned)a.n_head),
+                      dim3(kSW * 32), smem, s, a);
+}
+
 template <int HD>
 cudaError_t launch_split_hd(const AttnArgs& a, cudaStream_t s) {
-    const dim3 grid((unsigned)a.n_seq, (unsigned)a.n_head);
     switch (a.kv_type) {
-        case 0: return launch_opt(false, attn_split_kernel<HD, 0>, grid, dim3(kSW * 32), 0, s, a);
-        case 1: return launch_opt(false, attn_split_kernel<HD, 1>, grid, dim3(kSW * 32), 0, s, a);
-        case 2: return launch_opt(false, attn_split_kernel<HD, 2>, grid, dim3(kSW * 32), 0, s, a);
-        case 3: return launch_opt(false, attn_split_kernel<HD, 3>, grid, dim3(kSW * 32), 0, s, a);
+        case 0: return launch_split<HD, 0>(a, s);
+        case 1: return launch_split<HD, 1>(a, s);
+        case 2: return launch_split<HD, 2>(a, s);
+        case 3: return launch_split<HD, 3>(a, s);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
     constexpr int DPL = HD / 32;  // value dimensions per lane
     constexpr int ES = P::ES, SL = P::SL, SLP = P::SLP, NSC = P::NSC, S = P::S;
     extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ float qs[HD];
+    __shared__ __align__(16) float qs[HD];
     __shared__ float mw[kSW];
     __shared__ double dw[kSW];
     __shared__ float ow[kSW][HD];
@@ -106,18 +106,22 @@ __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
             unsigned char* base = ring + (g % S) * P::STAGE;
             constexpr int CPT = SL / 16;  // 16-byte chunks per slice
             const int tb = t0 + g * kTok;
-            for (int c = lane; c < 2 * kTok * CPT; c += 32) {
+            // lane u < kTok: the cache slot of token tb + u, once per stage
+            const int tu = tb + (lane & (kTok - 1));
+            const size_t myslot = tu < t1 ? slot_of(tu) : 0;
+#pragma unroll
+            for (int i = 0; i < 2 * kTok * CPT / 32; ++i) {
+                const int c = lane + 32 * i;  // chunk: (K|V, token u, 16-byte offset)
                 const int kv = c / (kTok * CPT), rem = c % (kTok * CPT), u = rem / CPT, off = (rem % CPT) * 16;
-                const int t = tb + u;
-                if (t < t1)
-                    cp_async16(base + (kv * kTok + u) * SLP + off,
-                               (kv ? vp : kp) + slot_of(t) * row_bytes + head_off + off);
+                const size_t su = __shfl_sync(0xffffffffu, myslot, u);
+                if (tb + u < t1)
+                    cp_async16(base + (kv * kTok + u) * SLP + off, (kv ? vp : kp) + su * row_bytes + head_off + off);
             }
             if constexpr (NSC > 0) {
                 const int u = lane & 15, kv = lane >> 4, t = tb + u;
                 if (t < t1) {
                     const float* src = (kv ? a.v_scales : a.k_scales) +
-                                       (KVT == 2 ? slot_of(t) : slot_of(t) * (kv_dim / 32) + kh * NSC);
+                                       (KVT == 2 ? myslot : myslot * (kv_dim / 32) + kh * NSC);
                     float* dst = reinterpret_cast<float*>(base + 2 * kTok * SLP) + (kv * kTok + u) * NSC;
 #pragma unroll
                     for (int i = 0; i < NSC; ++i) cp_async4(dst + i, src + i);
@@ -161,10 +165,13 @@ __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {
 #pragma unroll
                 for (int d = 0; d < HD / 2; d += 8) {
                     const uint4 w = *reinterpret_cast<const uint4*>(kr + d * 2);
+                    const float4 qa = *reinterpret_cast<const float4*>(qh + d);
+                    const float4 qb = *reinterpret_cast<const float4*>(qh + d + 4);
+                    const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
                     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                     for (int l = 0; l < 8; ++l)
-                        part = fmaf(qh[d + l], half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1)))), part);
+                        part = fmaf(qv[l], half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1)))), part);
                 }
             } else {
 #pragma unroll

@@ -307,13 +307,17 @@ MV_API int mv_gemm(mv_weight_t w, const float* x, uint64_t batch, float* y, int 
     }
     // Q4_0 with Q8 activations: per-row quantisation into stream-ordered
     // scratch (scales block-major), then the tensor-core GEMM.
+    // 64 tokens and more: fp16 operands (gemm_f16.cu), else int8 (gemm_tc.cu)
     const uint64_t ldb = mvb::gemm_tc_ldb(batch);
+    const bool f16 = mvb::gemm_f16_preferred(batch);
     int8_t* q = nullptr;
     float* d = nullptr;
-    CK(cudaMallocAsync(reinterpret_cast<void**>(&q), batch * w->cols, s));
+    CK(cudaMallocAsync(reinterpret_cast<void**>(&q), batch * w->cols * (f16 ? 2 : 1), s));
     cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&d), 2 * (w->cols / 32) * ldb * sizeof(float), s);
-    if (e == cudaSuccess) e = mvb::quantize_q8_rows_t(x, batch, w->cols, q, d, ldb, s);
-    if (e == cudaSuccess) e = mvb::gemm_q4_q8_tc(*w, q, d, ldb, batch, y, s);
+    uint16_t* qh = f16 ? reinterpret_cast<uint16_t*>(q) : nullptr;
+    if (e == cudaSuccess) e = mvb::quantize_q8_rows_t(x, batch, w->cols, q, d, ldb, s, qh);
+    if (e == cudaSuccess)
+        e = f16 ? mvb::gemm_q4_q8_f16(*w, qh, d, ldb, batch, y, s) : mvb::gemm_q4_q8_tc(*w, q, d, ldb, batch, y, s);
     cudaFreeAsync(q, s);
     if (d) cudaFreeAsync(d, s);
     if (e != cudaSuccess) return cuda_fail(e, "gemm_q4_q8_tc");

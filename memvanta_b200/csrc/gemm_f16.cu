@@ -1,0 +1,447 @@
+// gemm_f16.cu -- batched Q4_0 x Q8-activation matmul (prefill) on the
+// 5th-generation tensor cores with fp16 operands, for batches of 64 tokens
+// and more.
+//
+// Numerics are the reference's MEMVANTA_FORCE_Q8_ACT=1 prefill
+// (tensor_matmul_batch_v06, src/gguf_kernels.cpp:265-266): per (token t,
+// row r) the sequential chain over the 32-element blocks b
+//     sum = fma(fp16(d_w[r,b]) * d_a[t,b], float(isum[r,t,b]), sum)
+// with isum = sum_k (nib_k - 8) * q_k (dot_q4_q8, :189).  The block dots come
+// from tcgen05.mma kind::f16 with fp32 accumulation: A = nib - 8 and B = q
+// are small integers, exact in fp16, every product and partial sum is an
+// integer below 2^16, so the accumulator holds float(isum) exactly whatever
+// the order of the tensor core's additions.  Each block gets a TMEM slot of
+// its own (two K = 16 MMAs), so the epilogue reads every block's dot apart and
+// runs the chain in block order: one packed multiply and one packed FMA per
+// two (row, token) pairs and block -- no int->float step, no constant to
+// subtract, no slot to reset between uses.
+//
+// Per pipeline stage of kG = 2 blocks of a 128-row x NT-token tile:
+//   raw  smem [128][32 B]       the Q4_0 nibble bytes (TMA, no swizzle)
+//   A    smem [128][128 B]      the weights as fp16 (nib - 8), K-major,
+//                               128-byte swizzle -- written by 4 converter
+//                               warps (thread = row) from raw
+//   B    smem [NT][128 B]       the fp16 activations (TMA, 128-byte swizzle)
+//   D    TMEM 128 lanes x NT    one slot per block, 512 / NT slots in a ring
+// Epilogue data per 16 blocks: the rows' fp16 weight scales (TMA, 32-byte
+// swizzle) and the tokens' fp32 activation scales (TMA, block-major).
+//
+// Warps: 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-5 converters,
+// then NT/32 epilogue warps per TMEM lane quadrant (32 tokens each).  Every
+// wait is bounded (tc.cuh): a wait that runs out raises the CTA's abort flag,
+// records a site in the status word, and every role drains and returns.
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "tc.cuh"
+
+namespace mvb {
+
+__device__ int g_f16_status = 0;  // site of an expired bounded wait (0: none)
+
+// Adds this kernel's status to *status (first site wins) and clears it;
+// tc_status (gemm_tc.cu) reports both tensor-core GEMMs through it.
+cudaError_t f16_status_take(int* status) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_f16_status, sizeof(int));
+    if (e == cudaSuccess && v != 0) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_f16_status, &zero, sizeof(int));
+        if (!*status) *status = v;
+    }
+    return e;
+}
+
+namespace {
+
+constexpr int kM = 128;        // weight rows per tile = TMEM lanes
+constexpr int kG = 2;          // blocks per stage: K = 64 fp16 = one 128-byte swizzle row
+constexpr int kEB = 16;        // blocks per epilogue-data slot
+constexpr int kES = 2;         // epilogue-data slots
+constexpr int kConv0 = 2;      // first converter warp
+constexpr int kConvWarps = 4;
+constexpr int kEpi0 = kConv0 + kConvWarps;
+
+template <int NT>
+struct Cfg {
+    static constexpr int kEpiWarps = 4 * (NT / 32);
+    static constexpr int kThreads = (kEpi0 + kEpiWarps) * 32;
+    static constexpr int kA = kM * kG * 64;   // 16 KB
+    static constexpr int kB = NT * kG * 64;   // NT x 128 B
+    static constexpr int kRaw = kM * kG * 16; // 4 KB
+    static constexpr int kStage = kA + kB + kRaw;
+    static constexpr int kS = 4;
+    static constexpr int kDw = kM * kEB * 2;  // [128][16] fp16
+    static constexpr int kDa = kEB * NT * 4;  // [16][NT] fp32
+    static constexpr int kEpi = kDw + kDa;
+    static constexpr int kSlots = 512 / NT;   // TMEM D slots
+    static constexpr int kEpiOff = kS * kStage;
+    static constexpr int kBarOff = kEpiOff + kES * kEpi;
+    static constexpr int kBars = 3 * kS + 2 * kSlots + 2 * kES + 1;
+    static constexpr int kSmem = kBarOff + kBars * 8 + 16 + 1024;
+    static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kStage % 1024 == 0 && kEpi % 1024 == 0, "alignment");
+    static_assert(kSmem <= 227 * 1024, "shared memory");
+    static_assert(kSlots >= 2 * kG, "two stages of D slots");
+};
+
+struct F16Args {
+    float* y;  // row r of token t at y[t * ldy + r]
+    int rows, nb, batch, n_ttiles, n_tiles, accumulate, ldy;
+};
+
+// Instruction descriptor of kind::f16: f16 x f16 -> f32, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4)                      // D format: f32
+           | (0u << 7) | (0u << 10)       // A, B: f16
+           | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (=|+=) A[smem] * B[smem]^T, kind::f16, issued by one thread.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+    return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+
+// Two nibbles of each of the bytes 2p, 2p+1 of w (p = 0, 1) as fp16 (nib - 8)
+// pairs: (0x6400 | nib) is 1024 + nib in fp16, minus 1032 exactly.
+__device__ __forceinline__ uint32_t nib_pair(uint32_t w, uint32_t sel, int shift) {
+    const uint32_t t = __byte_perm(w, 0u, sel);  // bytes 2p, 2p+1 in the low bytes of each half
+    const uint32_t h = ((t >> shift) & 0x000F000Fu) | 0x64006400u;
+    const __half2 v = __hsub2(*reinterpret_cast<const __half2*>(&h), __halves2half2(__ushort_as_half(0x6408),
+                                                                                     __ushort_as_half(0x6408)));
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+template <int NT>
+__global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
+    gemm_f16_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                    const __grid_constant__ CUtensorMap dmap, const __grid_constant__ CUtensorMap smap,
+                    const F16Args a) {
+    using C = Cfg<NT>;
+    constexpr int TT = 32;  // tokens per epilogue warp
+    extern __shared__ unsigned char smem_dyn[];
+    const uint32_t s0 = tc::smem_u32(smem_dyn);
+    const uint32_t pad = ((s0 + 1023u) & ~1023u) - s0;
+    unsigned char* const sm = smem_dyn + pad;
+    const uint32_t sbase = s0 + pad;
+    const uint32_t bars = sbase + C::kBarOff;
+    const uint32_t full0 = bars;                      // TMA bytes of a stage landed
+    const uint32_t aready0 = full0 + 8u * C::kS;      // converters wrote the stage's A
+    const uint32_t empty0 = aready0 + 8u * C::kS;     // the stage's MMAs completed
+    const uint32_t tfull0 = empty0 + 8u * C::kS;      // a D slot's MMAs completed
+    const uint32_t tempty0 = tfull0 + 8u * C::kSlots; // a D slot read by every epilogue warp
+    const uint32_t efull0 = tempty0 + 8u * C::kSlots;
+    const uint32_t eempty0 = efull0 + 8u * kES;
+    const uint32_t done_bar = eempty0 + 8u * kES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kBarOff + C::kBars * 8);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + C::kBarOff + C::kBars * 8 + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int quad = warp & 3;
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kS; ++s) {
+            tc::mbar_init(full0 + 8 * s, 1);
+            tc::mbar_init(aready0 + 8 * s, kConvWarps);
+            tc::mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int j = 0; j < C::kSlots; ++j) {
+            tc::mbar_init(tfull0 + 8 * j, 1);
+            tc::mbar_init(tempty0 + 8 * j, C::kEpiWarps);
+        }
+        for (int e = 0; e < kES; ++e) {
+            tc::mbar_init(efull0 + 8 * e, 1);
+            tc::mbar_init(eempty0 + 8 * e, C::kEpiWarps);
+        }
+        tc::mbar_init(done_bar, 1);
+        *abort_flag = 0;
+        tc::mbar_fence_init();
+        tc::tma_prefetch_map(&wmap);
+        tc::tma_prefetch_map(&xmap);
+        tc::tma_prefetch_map(&dmap);
+        tc::tma_prefetch_map(&smap);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tc::smem_u32(tmem_slot), 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // the set-up above overlaps the previous kernel; activations, scales and
+    // y are touched only after it completed
+    pdl_wait();
+
+    if (warp == 0) {
+        // ---------------------------------------------------- TMA producer
+        if (lane == 0) {
+            uint32_t k = 0, j = 0;  // stages, epilogue-data groups issued
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+                const int row0 = (tile / a.n_ttiles) * kM, t0 = (tile % a.n_ttiles) * NT;
+                for (int b0 = 0; b0 < a.nb; b0 += kG) {
+                    if (b0 % kEB == 0) {
+                        const int e = j % kES;
+                        if (!tc::mbar_wait(eempty0 + 8 * e, ((j / kES) & 1u) ^ 1u, abort_flag, &g_f16_status, 21)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t ed = sbase + C::kEpiOff + e * C::kEpi;
+                        tc::mbar_expect_tx(efull0 + 8 * e, C::kEpi);
+                        tc::tma_load_2d(ed, &smap, b0, row0, efull0 + 8 * e);
+                        tc::tma_load_2d(ed + C::kDw, &dmap, t0, b0, efull0 + 8 * e);
+                        ++j;
+                    }
+                    const int s = k % C::kS;
+                    if (!tc::mbar_wait(empty0 + 8 * s, ((k / C::kS) & 1u) ^ 1u, abort_flag, &g_f16_status, 22)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t st = sbase + s * C::kStage;
+                    tc::mbar_expect_tx(full0 + 8 * s, C::kB + C::kRaw);
+                    tc::tma_load_2d(st + C::kA, &xmap, b0 * 32, t0, full0 + 8 * s);
+                    tc::tma_load_2d(st + C::kA + C::kB, &wmap, b0 * 16, row0, full0 + 8 * s);
+                    ++k;
+                }
+            }
+            // drain: the latest load of every slot has landed before the CTA exits
+            for (uint32_t i = k > (uint32_t)C::kS ? k - C::kS : 0; i < k; ++i)
+                tc::mbar_wait(full0 + 8 * (i % C::kS), (i / C::kS) & 1u, abort_flag, &g_f16_status, 23, false);
+            for (uint32_t i = j > (uint32_t)kES ? j - kES : 0; i < j; ++i)
+                tc::mbar_wait(efull0 + 8 * (i % kES), (i / kES) & 1u, abort_flag, &g_f16_status, 24, false);
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(kM, NT);
+            uint32_t k = 0, blk = 0;  // stages, blocks issued
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+                for (int b0 = 0; ok && b0 < a.nb; b0 += kG, ++k) {
+                    const int s = k % C::kS;
+                    if (!tc::mbar_wait(aready0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_f16_status, 25)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t st = sbase + s * C::kStage;
+                    const uint64_t ad = tc::sdesc_kmajor_sw128(st), bd = tc::sdesc_kmajor_sw128(st + C::kA);
+                    const int nblk = a.nb - b0 < kG ? a.nb - b0 : kG;
+                    for (int g = 0; g < nblk; ++g, ++blk) {
+                        const int slot = blk % C::kSlots;
+                        if (!tc::mbar_wait(tempty0 + 8 * slot, ((blk / C::kSlots) & 1u) ^ 1u, abort_flag,
+                                           &g_f16_status, 26)) {
+                            ok = false;
+                            break;
+                        }
+                        tc::tc_fence_after();
+                        // block g: K slices 2g, 2g+1 of 16 fp16 = 32 bytes each (+2 in the address field)
+                        const uint32_t d = tmem + slot * NT;
+                        mma_f16(d, ad + 2 * (2 * g), bd + 2 * (2 * g), idesc, 0u);
+                        mma_f16(d, ad + 2 * (2 * g + 1), bd + 2 * (2 * g + 1), idesc, 1u);
+                        tc::mma_commit(tfull0 + 8 * slot);
+                    }
+                    if (!ok) break;
+                    tc::mma_commit(empty0 + 8 * s);
+                }
+            }
+            // every MMA issued has completed before TMEM is released
+            tc::mma_commit(done_bar);
+            tc::mbar_wait(done_bar, 0, abort_flag, &g_f16_status, 27, false);
+        }
+    } else if (warp < kEpi0) {
+        // ------------------------------------------------------ converters
+        const int r = quad * 32 + lane;  // row of the tile
+        uint32_t k = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+            for (int b0 = 0; b0 < a.nb; b0 += kG, ++k) {
+                const int s = k % C::kS;
+                const bool got = tc::mbar_wait(full0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_f16_status, 28);
+                if (!__all_sync(0xffffffffu, got)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char* st = sm + s * C::kStage;
+                const uint4* raw = reinterpret_cast<const uint4*>(st + C::kA + C::kB + r * 32);
+                unsigned char* arow = st + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+                for (int g = 0; g < kG; ++g) {
+                    // GGUF order: byte i holds element i (low nibble) and 16 + i (high)
+                    const uint4 w = raw[g];
+                    const uint4 c[4] = {
+                        make_uint4(nib_pair(w.x, 0x4140u, 0), nib_pair(w.x, 0x4342u, 0), nib_pair(w.y, 0x4140u, 0),
+                                   nib_pair(w.y, 0x4342u, 0)),
+                        make_uint4(nib_pair(w.z, 0x4140u, 0), nib_pair(w.z, 0x4342u, 0), nib_pair(w.w, 0x4140u, 0),
+                                   nib_pair(w.w, 0x4342u, 0)),
+                        make_uint4(nib_pair(w.x, 0x4140u, 4), nib_pair(w.x, 0x4342u, 4), nib_pair(w.y, 0x4140u, 4),
+                                   nib_pair(w.y, 0x4342u, 4)),
+                        make_uint4(nib_pair(w.z, 0x4140u, 4), nib_pair(w.z, 0x4342u, 4), nib_pair(w.w, 0x4140u, 4),
+                                   nib_pair(w.w, 0x4342u, 4))};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int chunk = 4 * g + q;  // 128-byte swizzle: chunk j of row r at j ^ (r & 7)
+                        *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = c[q];
+                    }
+                }
+                tc::fence_proxy_async_smem();  // generic-proxy writes -> the tensor core's reads
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(aready0 + 8 * s);
+            }
+        }
+    } else {
+        // -------------------------------------------------------- epilogue
+        const int slice = (warp - kEpi0) >> 2;  // tokens slice*32 .. +31 of a tile
+        const int rr = quad * 32 + lane;        // row of the tile = TMEM lane
+        const int dsw = (rr >> 2) & 1;          // 32-byte swizzle phase of this row's weight scales
+        const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + slice * TT;
+        uint32_t blk = 0, j = 0;  // blocks, epilogue-data groups consumed
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+            const int r = (tile / a.n_ttiles) * kM + rr;
+            const int tb = (tile % a.n_ttiles) * NT + slice * TT;
+            uint64_t acc[TT / 2];  // token pairs, (+0, +0) first
+#pragma unroll
+            for (int t = 0; t < TT / 2; ++t) acc[t] = 0ull;
+            for (int b16 = 0; ok && b16 < a.nb; b16 += kEB) {
+                const int e = j % kES;
+                if (!__all_sync(0xffffffffu,
+                                tc::mbar_wait(efull0 + 8 * e, (j / kES) & 1u, abort_flag, &g_f16_status, 29))) {
+                    ok = false;
+                    break;
+                }
+                const unsigned char* ed = sm + C::kEpiOff + e * C::kEpi;
+                const uint4 w0 = *reinterpret_cast<const uint4*>(ed + rr * 32 + ((0 ^ dsw) << 4));
+                const uint4 w1 = *reinterpret_cast<const uint4*>(ed + rr * 32 + ((1 ^ dsw) << 4));
+                const uint32_t dwp[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                const float* da = reinterpret_cast<const float*>(ed + C::kDw);  // [16][NT]
+                const int neb = a.nb - b16 < kEB ? a.nb - b16 : kEB;
+                for (int eb = 0; eb < neb; ++eb, ++blk) {
+                    const int slot = blk % C::kSlots;
+                    // warp-uniform outcome: the TMEM load below is .sync.aligned
+                    if (!__all_sync(0xffffffffu, tc::mbar_wait(tfull0 + 8 * slot, (blk / C::kSlots) & 1u, abort_flag,
+                                                               &g_f16_status, 30))) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    uint32_t v[TT];
+                    tc::tmem_ld32(tl + slot * NT, v);
+                    tc::tmem_wait_ld();
+                    tc::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(tempty0 + 8 * slot);  // the slot is free for the MMAs
+                    const uint32_t word = dwp[eb >> 1];
+                    const float dw = half_bits_to_float((unsigned short)((eb & 1) ? word >> 16 : word));
+                    const uint64_t dw2 = pack2(dw, dw);
+                    const ulonglong2* d4p = reinterpret_cast<const ulonglong2*>(da + eb * NT + slice * TT);
+#pragma unroll
+                    for (int t4 = 0; t4 < TT / 4; ++t4) {
+                        const ulonglong2 d4 = d4p[t4];
+                        const uint64_t v0 = (uint64_t)v[4 * t4] | ((uint64_t)v[4 * t4 + 1] << 32);
+                        const uint64_t v1 = (uint64_t)v[4 * t4 + 2] | ((uint64_t)v[4 * t4 + 3] << 32);
+                        // fma(fp16(d_w) * d_a, float(isum), sum): the product rounded first
+                        acc[2 * t4] = tc::f2_fma(tc::f2_mul(dw2, d4.x), v0, acc[2 * t4]);
+                        acc[2 * t4 + 1] = tc::f2_fma(tc::f2_mul(dw2, d4.y), v1, acc[2 * t4 + 1]);
+                    }
+                }
+                if (!ok) break;
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(eempty0 + 8 * e);
+                ++j;
+            }
+            if (!ok) break;
+            if (r < a.rows) {
+#pragma unroll
+                for (int t = 0; t < TT; ++t) {
+                    if (tb + t < a.batch) {
+                        const float val = __uint_as_float((uint32_t)(acc[t / 2] >> (32 * (t & 1))));
+                        float* p = a.y + (size_t)(tb + t) * a.ldy + r;
+                        *p = a.accumulate ? *p + val : val;
+                    }
+                }
+            }
+        }
+    }
+
+    // teardown: every role is out of its loop, copies and MMAs have drained
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
+template <int NT>
+cudaError_t launch_f16(const mv_weight_s& w, const uint16_t* qh, const float* dT, uint64_t ldb, uint64_t batch,
+                       float* y, uint64_t ldy, cudaStream_t s, bool accumulate) {
+    using C = Cfg<NT>;
+    const tc::EncodeFn enc = tc::encode_fn();
+    if (!enc) {
+        set_last_error("cuTensorMapEncodeTiled is unavailable in this driver");
+        return cudaErrorNotSupported;
+    }
+    CUtensorMap wmap, xmap, dmap, smap;
+    // payload plane [rows][nb*16 B] -> raw [128][32 B]
+    const cuuint64_t wdims[2] = {w.nb * 16, w.rows}, wstr[1] = {w.nb * 16};
+    const cuuint32_t wbox[2] = {(cuuint32_t)(kG * 16), (cuuint32_t)kM};
+    // fp16 activations [batch][K] -> B [NT][128 B], 128-byte swizzle
+    const cuuint64_t xdims[2] = {w.nb * 32, batch}, xstr[1] = {w.nb * 32 * 2};
+    const cuuint32_t xbox[2] = {(cuuint32_t)(kG * 32), (cuuint32_t)NT};
+    // activation scales [nb][ldb] fp32 -> [16][NT]
+    const cuuint64_t ddims[2] = {ldb, w.nb}, dstr[1] = {ldb * 4};
+    const cuuint32_t dbox[2] = {(cuuint32_t)NT, (cuuint32_t)kEB};
+    // weight scales [rows][dstride] fp16 -> [128][16], 32-byte swizzle
+    const cuuint64_t sdims[2] = {w.dstride, w.rows}, sstr[1] = {w.dstride * 2};
+    const cuuint32_t sbox[2] = {(cuuint32_t)kEB, (cuuint32_t)kM};
+    if (!tc::encode(enc, &wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w.qs, wdims, wstr, wbox, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !tc::encode(enc, &xmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(qh), xdims, xstr, xbox,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !tc::encode(enc, &dmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(dT), ddims, dstr, dbox,
+                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !tc::encode(enc, &smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, w.d, sdims, sstr, sbox, CU_TENSOR_MAP_SWIZZLE_32B)) {
+        set_last_error("cuTensorMapEncodeTiled rejected a tensor map of the fp16 tensor-core GEMM");
+        return cudaErrorInvalidValue;
+    }
+    const int n_ttiles = (int)((batch + NT - 1) / NT);
+    const int n_tiles = (int)((w.rows + kM - 1) / kM) * n_ttiles;
+    const F16Args args{y, (int)w.rows, (int)w.nb, (int)batch, n_ttiles, n_tiles, accumulate ? 1 : 0, (int)ldy};
+    ensure_smem_attr(gemm_f16_kernel<NT>, C::kSmem);
+    const int grid = n_tiles < num_sms() ? n_tiles : num_sms();
+    return launch_pdl(gemm_f16_kernel<NT>, dim3(grid), dim3(C::kThreads), C::kSmem, s, wmap, xmap, dmap, smap, args);
+}
+
+}  // namespace
+
+bool gemm_f16_preferred(uint64_t batch) {
+    static const bool off = [] {
+        const char* e = std::getenv("MV_GEMM_F16");
+        return e && std::string(e) == "0";
+    }();
+    return batch >= 64 && !off;
+}
+
+cudaError_t gemm_q4_q8_f16(const mv_weight_s& w, const uint16_t* qh, const float* dT, uint64_t ldb, uint64_t batch,
+                           float* y, cudaStream_t s, bool accumulate) {
+    if (!batch) return cudaSuccess;
+    if (w.type != 2 || ldb < gemm_tc_ldb(batch) || ldb % 4 || w.rows >= (1ull << 31) || batch >= (1ull << 31))
+        return cudaErrorInvalidValue;
+    return launch_f16<64>(w, qh, dT, ldb, batch, y, w.rows, s, accumulate);
+}
+
+}  // namespace mvb

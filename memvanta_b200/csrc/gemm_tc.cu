@@ -86,6 +86,7 @@ cudaError_t tc_status(cudaStream_t s, int* status) {
         e = cudaMemcpyToSymbol(g_tc_status, &zero, sizeof(int));
     }
     *status = v;
+    if (e == cudaSuccess) e = f16_status_take(status);
     return e;
 }
 

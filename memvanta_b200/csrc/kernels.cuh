@@ -23,15 +23,16 @@ cudaError_t quantize_q8_rows(const float* x, uint64_t rows, uint64_t cols, int8_
 // for the tensor-core GEMM: scales block-major, dT[b * ldb + row], then at
 // dT + nb * ldb the GEMM's per-block constants; 2 * nb * ldb floats in all,
 // rows..ldb-1 zero-filled (ldb >= rows)
+// (qh set: the values as fp16 into qh[rows][cols] instead of int8 into q)
 cudaError_t quantize_q8_rows_t(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* dT, uint64_t ldb,
-                               cudaStream_t s);
+                               cudaStream_t s, uint16_t* qh = nullptr);
 // the same on rmsnorm(x) * w (the reference's rmsnorm), without materialising it
 cudaError_t rmsnorm_quantize_q8_rows_t(const float* x, const float* w, uint64_t rows, uint64_t cols, float eps,
-                                       int8_t* q, float* dT, uint64_t ldb, cudaStream_t s);
+                                       int8_t* q, float* dT, uint64_t ldb, cudaStream_t s, uint16_t* qh = nullptr);
 // the same on ff = silu(g) * u of a gate|up output with interleaved (g, u)
 // rows: gu is [rows][2 * cols], the quantised ff [rows][cols]
 cudaError_t silu_quantize_q8_rows_t(const float* gu, uint64_t rows, uint64_t cols, int8_t* q, float* dT, uint64_t ldb,
-                                    cudaStream_t s);
+                                    cudaStream_t s, uint16_t* qh = nullptr);
 
 // ---- gemv_q4.cu : decode GEMV over Q4_0 with Q8 activations (integer path)
 enum class Q4Pro : int {
@@ -91,6 +92,15 @@ cudaError_t gemm_q4_q8_tc(const mv_weight_s& w, const int8_t* q, const float* dT
                           float* y, cudaStream_t s, bool accumulate = false);
 // synchronise s; *status = site code of an expired bounded wait (0 = none), cleared
 cudaError_t tc_status(cudaStream_t s, int* status);
+// ---- gemm_f16.cu : the same matmul on fp16 tensor-core operands (kind::f16),
+// for batches of 64 tokens and more: qh [batch][cols] fp16 activations
+// (quantize_q8_rows_t & co. with qh), dT the block-major scales (ldb as above)
+cudaError_t gemm_q4_q8_f16(const mv_weight_s& w, const uint16_t* qh, const float* dT, uint64_t ldb, uint64_t batch,
+                           float* y, cudaStream_t s, bool accumulate = false);
+cudaError_t f16_status_take(int* status);
+// whether a Q8-activation matmul of `batch` tokens takes gemm_q4_q8_f16
+// (64 tokens and more; MV_GEMM_F16=0 keeps the int8 kernel everywhere)
+bool gemm_f16_preferred(uint64_t batch);
 
 // ---- ops.cu
 cudaError_t rmsnorm_rows(const float* x, const float* w, uint64_t rows, uint64_t n, float eps, float* out,

@@ -569,7 +569,7 @@ void ensure_prefill(mv_model_s* m, uint64_t B) {
         m->FF_l = dalloc<float>(m, B * m->Fl);
         m->PROJ_l = dalloc<float>(m, B * m->Dl);
     }
-    m->XQ = dalloc<int8_t>(m, B * K);
+    m->XQ = dalloc<int8_t>(m, B * K * 2);  // int8, or fp16 for the fp16 tensor-core GEMM
     m->XD = dalloc<float>(m, 2 * mvb::gemm_tc_ldb(B) * K / 32);  // block-major scales + constants
     if (!tp) {
         auto& a = m->pf_alt;
@@ -580,7 +580,7 @@ void ensure_prefill(mv_model_s* m, uint64_t B) {
         a.GU = dalloc<float>(m, B * 2 * m->Fl);
         a.FF = dalloc<float>(m, B * F);
         a.PROJ = dalloc<float>(m, B * D);
-        a.XQ = dalloc<int8_t>(m, B * K);
+        a.XQ = dalloc<int8_t>(m, B * K * 2);
         a.XD = dalloc<float>(m, 2 * mvb::gemm_tc_ldb(B) * K / 32);
         if (!a.stream) ck(cudaStreamCreateWithFlags(&a.stream, cudaStreamNonBlocking), "cudaStreamCreate(prefill)");
         if (!m->pf_join) ck(cudaEventCreateWithFlags(&m->pf_join, cudaEventDisableTiming), "cudaEventCreate(prefill)");
@@ -1183,11 +1183,17 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     ck(mvb::read_rows(*m->tok_embd, tok, B, m->X, s), "embed");
     // Q8 activations when B >= 2 and the weight is Q4_0 (FORCE_Q8 path);
     // fp32 activations otherwise, as tensor_matmul_batch_v06 dispatches.
+    // 64 tokens and more: fp16 activations and the fp16 tensor-core GEMM
+    uint16_t* XH = mvb::gemm_f16_preferred(B) ? reinterpret_cast<uint16_t*>(m->XQ) : nullptr;
+    auto gemm = [&](mv_weight_s* w, uint64_t ldb, float* out, bool accumulate) {
+        if (XH) ck(mvb::gemm_q4_q8_f16(*w, XH, m->XD, ldb, B, out, s, accumulate), "gemm (fp16)");
+        else ck(mvb::gemm_q4_q8_tc(*w, m->XQ, m->XD, ldb, B, out, s, accumulate), "gemm");
+    };
     auto project = [&](mv_weight_s* w, const float* in, uint64_t K, float* out, bool accumulate) {
         if (B >= 2 && w->type == 2) {
             const uint64_t ldb = mvb::gemm_tc_ldb(B);
-            ck(mvb::quantize_q8_rows_t(in, B, K, m->XQ, m->XD, ldb, s), "quantize");
-            ck(mvb::gemm_q4_q8_tc(*w, m->XQ, m->XD, ldb, B, out, s, accumulate), "gemm");
+            ck(mvb::quantize_q8_rows_t(in, B, K, m->XQ, m->XD, ldb, s, XH), "quantize");
+            gemm(w, ldb, out, accumulate);
         } else if (accumulate) {
             ck(mvb::matmul_f32act(*w, in, B, m->PROJ, s), "matmul");
             ck(mvb::add_inplace(out, m->PROJ, B * w->rows, s), "add");
@@ -1200,8 +1206,9 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     auto project_normed = [&](mv_weight_s* w, const float* norm_w, float* out) {
         if (B >= 2 && w->type == 2) {
             const uint64_t ldb = mvb::gemm_tc_ldb(B);
-            ck(mvb::rmsnorm_quantize_q8_rows_t(m->X, norm_w, B, D, m->eps, m->XQ, m->XD, ldb, s), "rmsnorm+quantize");
-            ck(mvb::gemm_q4_q8_tc(*w, m->XQ, m->XD, ldb, B, out, s, false), "gemm");
+            ck(mvb::rmsnorm_quantize_q8_rows_t(m->X, norm_w, B, D, m->eps, m->XQ, m->XD, ldb, s, XH),
+               "rmsnorm+quantize");
+            gemm(w, ldb, out, false);
         } else {
             ck(mvb::rmsnorm_rows(m->X, norm_w, B, D, m->eps, m->N, s), "rmsnorm");
             project(w, m->N, D, out, false);
@@ -1224,7 +1231,7 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
         aa.one_seq = 1;
         // single GPU, tensor-core o projection: the attention kernel also
         // writes the o GEMM's Q8 input (no separate quantisation launch)
-        const bool fuse_o = !tp && B >= 2 && L.o->type == 2;
+        const bool fuse_o = !tp && B >= 2 && L.o->type == 2 && !XH;
         if (fuse_o) {
             aa.xq = m->XQ;
             aa.xdT = m->XD;
@@ -1244,8 +1251,8 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
         if (!tp && B >= 2 && L.down->type == 2) {
             // SiLU gate fused into the down GEMM's Q8 quantisation
             const uint64_t ldb = mvb::gemm_tc_ldb(B);
-            ck(mvb::silu_quantize_q8_rows_t(m->GU, B, F, m->XQ, m->XD, ldb, s), "silu+quantize");
-            ck(mvb::gemm_q4_q8_tc(*L.down, m->XQ, m->XD, ldb, B, m->X, s, true), "gemm");
+            ck(mvb::silu_quantize_q8_rows_t(m->GU, B, F, m->XQ, m->XD, ldb, s, XH), "silu+quantize");
+            gemm(L.down, ldb, m->X, true);
             continue;
         }
         float* ff = tp ? m->FF_l : m->FF;

@@ -180,8 +180,10 @@ __global__ void quantize_q8_kernel(const float* __restrict__ x, uint64_t nblocks
 // exact constants c[b * ldb + row] = 1.5 * 2^23 + 8 * sum(q of the block) that
 // turn the GEMM's biased unsigned-nibble dot back into the reference's int32
 // block dot (gemm_tc.cu).  Rows rows..ldb-1 of both are zero.
+// qh set: the values go out as fp16 (exact: |q| <= 127) to qh instead of
+// int8 to q, for the fp16 tensor-core GEMM (gemm_f16.cu).
 __global__ void quantize_q8_t_kernel(const float* __restrict__ x, uint64_t rows, uint64_t nb, int8_t* __restrict__ q,
-                                     float* __restrict__ dT, uint64_t ldb) {
+                                     float* __restrict__ dT, uint64_t ldb, uint16_t* __restrict__ qh) {
     const int lane = threadIdx.x & 31;
     const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
     const uint64_t first = blockIdx.x * (uint64_t)(blockDim.x / 32) + threadIdx.x / 32;
@@ -191,7 +193,8 @@ __global__ void quantize_q8_t_kernel(const float* __restrict__ x, uint64_t rows,
     for (uint64_t b = first; b < rows * nb; b += warps) {
         float dd;
         const int v = quant_q8_lane(__ldcg(x + b * 32 + lane), dd);  // L2: x may come from other GPUs
-        q[b * 32 + lane] = (int8_t)v;
+        if (qh) qh[b * 32 + lane] = __half_as_ushort(__int2half_rn(v));
+        else q[b * 32 + lane] = (int8_t)v;
         const int sum = warp_sum_i(v);
         if (lane == 0) {
             const uint64_t at = (b % nb) * ldb + b / nb;
@@ -212,7 +215,8 @@ __global__ void quantize_q8_t_kernel(const float* __restrict__ x, uint64_t rows,
 // projection's input without materialising ff.  ff is evaluated exactly as
 // silu_pairs_kernel evaluates it, (g / (1 + expf(-g))) * u.
 __global__ void silu_quantize_q8_t_kernel(const float* __restrict__ gu, uint64_t rows, uint64_t nb,
-                                          int8_t* __restrict__ q, float* __restrict__ dT, uint64_t ldb) {
+                                          int8_t* __restrict__ q, float* __restrict__ dT, uint64_t ldb,
+                                          uint16_t* __restrict__ qh) {
     const int lane = threadIdx.x & 31;
     const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
     const uint64_t first = blockIdx.x * (uint64_t)(blockDim.x / 32) + threadIdx.x / 32;
@@ -224,7 +228,8 @@ __global__ void silu_quantize_q8_t_kernel(const float* __restrict__ gu, uint64_t
         const float ff = (p.x / (1.0f + expf(-p.x))) * p.y;
         float dd;
         const int v = quant_q8_lane(ff, dd);
-        q[b * 32 + lane] = (int8_t)v;
+        if (qh) qh[b * 32 + lane] = __half_as_ushort(__int2half_rn(v));
+        else q[b * 32 + lane] = (int8_t)v;
         const int sum = warp_sum_i(v);
         if (lane == 0) {
             const uint64_t at = (b % nb) * ldb + b / nb;
@@ -247,7 +252,7 @@ __global__ void silu_quantize_q8_t_kernel(const float* __restrict__ gu, uint64_t
 // block is 8 consecutive lanes and its max / sum are 3 shuffle steps.
 __global__ void rmsnorm_quantize_t_kernel(const float* __restrict__ x, const float* __restrict__ w, int n, float eps,
                                           uint64_t rows, int8_t* __restrict__ q, float* __restrict__ dT,
-                                          uint64_t ldb) {
+                                          uint64_t ldb, uint16_t* __restrict__ qh) {
     __shared__ double red[32];
     const uint64_t row = blockIdx.x;
     const int nc = n / 4, nb = n / 32;
@@ -298,9 +303,17 @@ __global__ void rmsnorm_quantize_t_kernel(const float* __restrict__ x, const flo
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
         sum += __shfl_xor_sync(0xffffffffu, sum, 4);
         if (live) {
-            reinterpret_cast<uint32_t*>(q + row * n)[c] =
-                (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8) | ((uint32_t)(q2 & 0xFF) << 16) |
-                ((uint32_t)(q3 & 0xFF) << 24);
+            if (qh) {
+                const uint32_t h01 = (uint32_t)__half_as_ushort(__int2half_rn(q0)) |
+                                     ((uint32_t)__half_as_ushort(__int2half_rn(q1)) << 16);
+                const uint32_t h23 = (uint32_t)__half_as_ushort(__int2half_rn(q2)) |
+                                     ((uint32_t)__half_as_ushort(__int2half_rn(q3)) << 16);
+                reinterpret_cast<uint2*>(qh + row * n)[c] = make_uint2(h01, h23);
+            } else {
+                reinterpret_cast<uint32_t*>(q + row * n)[c] =
+                    (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8) | ((uint32_t)(q2 & 0xFF) << 16) |
+                    ((uint32_t)(q3 & 0xFF) << 24);
+            }
             if ((c & 7) == 0) {
                 const uint64_t at = (uint64_t)(c / 8) * ldb + row;
                 dT[at] = d;
@@ -319,33 +332,33 @@ __global__ void rmsnorm_quantize_t_kernel(const float* __restrict__ x, const flo
 }
 
 cudaError_t rmsnorm_quantize_q8_rows_t(const float* x, const float* w, uint64_t rows, uint64_t cols, float eps,
-                                       int8_t* q, float* dT, uint64_t ldb, cudaStream_t s) {
+                                       int8_t* q, float* dT, uint64_t ldb, cudaStream_t s, uint16_t* qh) {
     if (!rows) return cudaSuccess;
     if (cols % 32 || ldb < rows) return cudaErrorInvalidValue;
     const uint64_t nc = cols / 4;
     const unsigned threads = (unsigned)(nc >= 1024 ? 1024 : (nc + 31) / 32 * 32);
     return launch_pdl(rmsnorm_quantize_t_kernel, dim3((unsigned)rows), dim3(threads), 0, s, x, w, (int)cols, eps, rows,
-                      q, dT, ldb);
+                      q, dT, ldb, qh);
 }
 
 cudaError_t quantize_q8_rows_t(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* dT, uint64_t ldb,
-                               cudaStream_t s) {
+                               cudaStream_t s, uint16_t* qh) {
     const uint64_t nblocks = rows * (cols / 32);
     if (!nblocks || ldb < rows) return nblocks ? cudaErrorInvalidValue : cudaSuccess;
     const uint64_t ctas = (nblocks + 7) / 8;
     const uint64_t cap = (uint64_t)num_sms() * 8;
     return launch_pdl(quantize_q8_t_kernel, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(256), 0, s, x, rows,
-                      cols / 32, q, dT, ldb);
+                      cols / 32, q, dT, ldb, qh);
 }
 
 cudaError_t silu_quantize_q8_rows_t(const float* gu, uint64_t rows, uint64_t cols, int8_t* q, float* dT, uint64_t ldb,
-                                    cudaStream_t s) {
+                                    cudaStream_t s, uint16_t* qh) {
     const uint64_t nblocks = rows * (cols / 32);
     if (!nblocks || ldb < rows || cols % 32) return nblocks ? cudaErrorInvalidValue : cudaSuccess;
     const uint64_t ctas = (nblocks + 7) / 8;
     const uint64_t cap = (uint64_t)num_sms() * 8;
     return launch_pdl(silu_quantize_q8_t_kernel, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(256), 0, s, gu, rows,
-                      cols / 32, q, dT, ldb);
+                      cols / 32, q, dT, ldb, qh);
 }
 
 cudaError_t quantize_q8_rows(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* d, cudaStream_t s) {

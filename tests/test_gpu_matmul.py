@@ -206,11 +206,13 @@ def test_tc_gemm_tile_widths_bit_exact(cuda, oracle, tile, cols):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
-def test_tc_gemm_edge_values(cuda, oracle):
+@pytest.mark.parametrize("batch", [20, 80])
+def test_tc_gemm_edge_values(cuda, oracle, batch):
     """Extreme blocks: nibbles all 0 or all 15, activations of one sign at the
-    Q8 clamp, zero rows/tokens, a negative fp16 scale -- bit-exact."""
+    Q8 clamp, zero rows/tokens, a negative fp16 scale -- bit-exact, on the int8
+    tensor-core GEMM (20 tokens) and the fp16 one (80 tokens)."""
     rng = np.random.default_rng(77)
-    rows, cols, batch = 136, 256, 20
+    rows, cols = 136, 256
     w = gguf.gen_q4_0(rows, cols, rng).reshape(rows, cols // 32, 18).copy()
     w[0, :, 2:] = 0x00                       # every nibble 0  -> q - 8 = -8
     w[1, :, 2:] = 0xFF                       # every nibble 15 -> q - 8 = 7

@@ -26,7 +26,7 @@
 // Epilogue data per 16 blocks: the rows' fp16 weight scales (TMA, 32-byte
 // swizzle) and the tokens' fp32 activation scales (TMA, block-major).
 //
-// Warps: 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-5 converters,
+// Warps: 0 TMA producer, 1-2 MMA issuers (1 also owns TMEM), 3-6 converters,
 // then NT/32 epilogue warps per TMEM lane quadrant (32 tokens each).  Every
 // wait is bounded (tc.cuh): a wait that runs out raises the CTA's abort flag,
 // records a site in the status word, and every role drains and returns.
@@ -62,7 +62,8 @@ constexpr int kM = 128;        // weight rows per tile = TMEM lanes
 constexpr int kG = 2;          // blocks per stage: K = 64 fp16 = one 128-byte swizzle row
 constexpr int kEB = 16;        // blocks per epilogue-data slot
 constexpr int kES = 2;         // epilogue-data slots
-constexpr int kConv0 = 2;      // first converter warp
+constexpr int kMmaWarps = 2;   // warps 1, 2: MMA issuers, stages alternating
+constexpr int kConv0 = 1 + kMmaWarps;  // first converter warp
 constexpr int kConvWarps = 4;
 constexpr int kEpi0 = kConv0 + kConvWarps;
 
@@ -78,14 +79,15 @@ struct Cfg {
     static constexpr int kDw = kM * kEB * 2;  // [128][16] fp16
     static constexpr int kDa = kEB * NT * 4;  // [16][NT] fp32
     static constexpr int kEpi = kDw + kDa;
-    static constexpr int kSlots = 512 / NT;   // TMEM D slots
+    static constexpr int kSlots = 512 / NT;   // TMEM D slots, one block each
+    static constexpr int kPairs = kSlots / 2; // a stage's two blocks use a pair of slots
     static constexpr int kEpiOff = kS * kStage;
     static constexpr int kBarOff = kEpiOff + kES * kEpi;
-    static constexpr int kBars = 3 * kS + 2 * kSlots + 2 * kES + 1;
+    static constexpr int kBars = 3 * kS + 2 * kPairs + 2 * kES + 1;
     static constexpr int kSmem = kBarOff + kBars * 8 + 16 + 1024;
     static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kStage % 1024 == 0 && kEpi % 1024 == 0, "alignment");
     static_assert(kSmem <= 227 * 1024, "shared memory");
-    static_assert(kSlots >= 2 * kG, "two stages of D slots");
+    static_assert(kG == 2 && kPairs >= 2, "two stages of D slot pairs");
 };
 
 struct F16Args {
@@ -141,9 +143,9 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     const uint32_t full0 = bars;                      // TMA bytes of a stage landed
     const uint32_t aready0 = full0 + 8u * C::kS;      // converters wrote the stage's A
     const uint32_t empty0 = aready0 + 8u * C::kS;     // the stage's MMAs completed
-    const uint32_t tfull0 = empty0 + 8u * C::kS;      // a D slot's MMAs completed
-    const uint32_t tempty0 = tfull0 + 8u * C::kSlots; // a D slot read by every epilogue warp
-    const uint32_t efull0 = tempty0 + 8u * C::kSlots;
+    const uint32_t tfull0 = empty0 + 8u * C::kS;      // a D slot pair's MMAs completed
+    const uint32_t tempty0 = tfull0 + 8u * C::kPairs; // a D slot pair read by every epilogue warp
+    const uint32_t efull0 = tempty0 + 8u * C::kPairs;
     const uint32_t eempty0 = efull0 + 8u * kES;
     const uint32_t done_bar = eempty0 + 8u * kES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kBarOff + C::kBars * 8);
@@ -158,7 +160,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
             tc::mbar_init(aready0 + 8 * s, kConvWarps);
             tc::mbar_init(empty0 + 8 * s, 1);
         }
-        for (int j = 0; j < C::kSlots; ++j) {
+        for (int j = 0; j < C::kPairs; ++j) {
             tc::mbar_init(tfull0 + 8 * j, 1);
             tc::mbar_init(tempty0 + 8 * j, C::kEpiWarps);
         }
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
             tc::mbar_init(efull0 + 8 * e, 1);
             tc::mbar_init(eempty0 + 8 * e, C::kEpiWarps);
         }
-        tc::mbar_init(done_bar, 1);
+        tc::mbar_init(done_bar, kMmaWarps);
         *abort_flag = 0;
         tc::mbar_fence_init();
         tc::tma_prefetch_map(&wmap);
@@ -224,37 +226,36 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
             for (uint32_t i = j > (uint32_t)kES ? j - kES : 0; i < j; ++i)
                 tc::mbar_wait(efull0 + 8 * (i % kES), (i / kES) & 1u, abort_flag, &g_f16_status, 24, false);
         }
-    } else if (warp == 1) {
-        // ---------------------------------------------------- MMA issuer
+    } else if (warp <= kMmaWarps) {
+        // --------------------------------------------------- MMA issuers
+        // (an issuing thread spends tens of cycles per MMA, commit and
+        // wait: two threads take the stages in turn)
+        const uint32_t mine = warp - 1;
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16(kM, NT);
-            uint32_t k = 0, blk = 0;  // stages, blocks issued
+            uint32_t k = 0;  // stages
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
-                for (int b0 = 0; ok && b0 < a.nb; b0 += kG, ++k) {
-                    const int s = k % C::kS;
-                    if (!tc::mbar_wait(aready0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_f16_status, 25)) {
+                for (int b0 = 0; b0 < a.nb; b0 += kG, ++k) {
+                    if (k % kMmaWarps != mine) continue;
+                    const int s = k % C::kS, pr = k % C::kPairs;
+                    if (!tc::mbar_wait(aready0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_f16_status, 25) ||
+                        !tc::mbar_wait(tempty0 + 8 * pr, ((k / C::kPairs) & 1u) ^ 1u, abort_flag, &g_f16_status,
+                                       26)) {
                         ok = false;
                         break;
                     }
+                    tc::tc_fence_after();
                     const uint32_t st = sbase + s * C::kStage;
                     const uint64_t ad = tc::sdesc_kmajor_sw128(st), bd = tc::sdesc_kmajor_sw128(st + C::kA);
                     const int nblk = a.nb - b0 < kG ? a.nb - b0 : kG;
-                    for (int g = 0; g < nblk; ++g, ++blk) {
-                        const int slot = blk % C::kSlots;
-                        if (!tc::mbar_wait(tempty0 + 8 * slot, ((blk / C::kSlots) & 1u) ^ 1u, abort_flag,
-                                           &g_f16_status, 26)) {
-                            ok = false;
-                            break;
-                        }
-                        tc::tc_fence_after();
+                    for (int g = 0; g < nblk; ++g) {
                         // block g: K slices 2g, 2g+1 of 16 fp16 = 32 bytes each (+2 in the address field)
-                        const uint32_t d = tmem + slot * NT;
+                        const uint32_t d = tmem + (2 * pr + g) * NT;
                         mma_f16(d, ad + 2 * (2 * g), bd + 2 * (2 * g), idesc, 0u);
                         mma_f16(d, ad + 2 * (2 * g + 1), bd + 2 * (2 * g + 1), idesc, 1u);
-                        tc::mma_commit(tfull0 + 8 * slot);
                     }
-                    if (!ok) break;
+                    tc::mma_commit(tfull0 + 8 * pr);
                     tc::mma_commit(empty0 + 8 * s);
                 }
             }
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
         const int rr = quad * 32 + lane;        // row of the tile = TMEM lane
         const int dsw = (rr >> 2) & 1;          // 32-byte swizzle phase of this row's weight scales
         const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + slice * TT;
-        uint32_t blk = 0, j = 0;  // blocks, epilogue-data groups consumed
+        uint32_t ke = 0, j = 0;  // stages, epilogue-data groups consumed
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
             const int r = (tile / a.n_ttiles) * kM + rr;
@@ -329,33 +330,44 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                 const uint32_t dwp[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
                 const float* da = reinterpret_cast<const float*>(ed + C::kDw);  // [16][NT]
                 const int neb = a.nb - b16 < kEB ? a.nb - b16 : kEB;
-                for (int eb = 0; eb < neb; ++eb, ++blk) {
-                    const int slot = blk % C::kSlots;
-                    // warp-uniform outcome: the TMEM load below is .sync.aligned
-                    if (!__all_sync(0xffffffffu, tc::mbar_wait(tfull0 + 8 * slot, (blk / C::kSlots) & 1u, abort_flag,
+                // a stage's two blocks per TMEM round trip: both slots loaded, one wait
+                for (int eb = 0; eb < neb; eb += 2, ++ke) {
+                    const int nl = neb - eb < 2 ? neb - eb : 2;  // warp-uniform
+                    const uint32_t pr = ke % C::kPairs;
+                    uint32_t v[2][TT];
+                    // warp-uniform outcome: the TMEM loads below are .sync.aligned
+                    if (!__all_sync(0xffffffffu, tc::mbar_wait(tfull0 + 8 * pr, (ke / C::kPairs) & 1u, abort_flag,
                                                                &g_f16_status, 30))) {
                         ok = false;
                         break;
                     }
                     tc::tc_fence_after();
-                    uint32_t v[TT];
-                    tc::tmem_ld32(tl + slot * NT, v);
+#pragma unroll
+                    for (int i = 0; i < 2; ++i)
+                        if (i < nl) tc::tmem_ld32(tl + (2 * pr + i) * NT, v[i]);
+                    if (!ok) break;
                     tc::tmem_wait_ld();
                     tc::tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(tempty0 + 8 * slot);  // the slot is free for the MMAs
-                    const uint32_t word = dwp[eb >> 1];
-                    const float dw = half_bits_to_float((unsigned short)((eb & 1) ? word >> 16 : word));
-                    const uint64_t dw2 = pack2(dw, dw);
-                    const ulonglong2* d4p = reinterpret_cast<const ulonglong2*>(da + eb * NT + slice * TT);
+                    if (lane == 0) tc::mbar_arrive(tempty0 + 8 * pr);  // the pair is free for the MMAs
 #pragma unroll
-                    for (int t4 = 0; t4 < TT / 4; ++t4) {
-                        const ulonglong2 d4 = d4p[t4];
-                        const uint64_t v0 = (uint64_t)v[4 * t4] | ((uint64_t)v[4 * t4 + 1] << 32);
-                        const uint64_t v1 = (uint64_t)v[4 * t4 + 2] | ((uint64_t)v[4 * t4 + 3] << 32);
-                        // fma(fp16(d_w) * d_a, float(isum), sum): the product rounded first
-                        acc[2 * t4] = tc::f2_fma(tc::f2_mul(dw2, d4.x), v0, acc[2 * t4]);
-                        acc[2 * t4 + 1] = tc::f2_fma(tc::f2_mul(dw2, d4.y), v1, acc[2 * t4 + 1]);
+                    for (int i = 0; i < 2; ++i) {
+                        if (i < nl) {
+                            const int b = eb + i;
+                            const uint32_t word = dwp[b >> 1];
+                            const float dw = half_bits_to_float((unsigned short)((b & 1) ? word >> 16 : word));
+                            const uint64_t dw2 = pack2(dw, dw);
+                            const ulonglong2* d4p = reinterpret_cast<const ulonglong2*>(da + b * NT + slice * TT);
+#pragma unroll
+                            for (int t4 = 0; t4 < TT / 4; ++t4) {
+                                const ulonglong2 d4 = d4p[t4];
+                                const uint64_t v0 = (uint64_t)v[i][4 * t4] | ((uint64_t)v[i][4 * t4 + 1] << 32);
+                                const uint64_t v1 = (uint64_t)v[i][4 * t4 + 2] | ((uint64_t)v[i][4 * t4 + 3] << 32);
+                                // fma(fp16(d_w) * d_a, float(isum), sum): the product rounded first
+                                acc[2 * t4] = tc::f2_fma(tc::f2_mul(dw2, d4.x), v0, acc[2 * t4]);
+                                acc[2 * t4 + 1] = tc::f2_fma(tc::f2_mul(dw2, d4.y), v1, acc[2 * t4 + 1]);
+                            }
+                        }
                     }
                 }
                 if (!ok) break;

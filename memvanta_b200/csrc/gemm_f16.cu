@@ -18,10 +18,12 @@
 //
 // Per pipeline stage of kG = 2 blocks of a 128-row x NT-token tile:
 //   raw  smem [128][32 B]       the Q4_0 nibble bytes (TMA, no swizzle)
+//   B    smem [NT][128 B]       the fp16 activations (TMA, 128-byte swizzle)
 //   A    smem [128][128 B]      the weights as fp16 (nib - 8), K-major,
 //                               128-byte swizzle -- written by 4 converter
-//                               warps (thread = row) from raw
-//   B    smem [NT][128 B]       the fp16 activations (TMA, 128-byte swizzle)
+//                               warps (thread = row) from raw into a ring of
+//                               its own, so the TMA ring (raw + B, 8 stages)
+//                               is not held while A waits for the MMAs
 //   D    TMEM 128 lanes x NT    one slot per block, 512 / NT slots in a ring
 // Epilogue data per 16 blocks: the rows' fp16 weight scales (TMA, 32-byte
 // swizzle) and the tokens' fp32 activation scales (TMA, block-major).
@@ -71,19 +73,21 @@ template <int NT>
 struct Cfg {
     static constexpr int kEpiWarps = 4 * (NT / 32);
     static constexpr int kThreads = (kEpi0 + kEpiWarps) * 32;
-    static constexpr int kA = kM * kG * 64;   // 16 KB
+    static constexpr int kA = kM * kG * 64;   // 16 KB: one A slot
+    static constexpr int kSA = 3;             // A slots (converters -> MMAs)
     static constexpr int kB = NT * kG * 64;   // NT x 128 B
     static constexpr int kRaw = kM * kG * 16; // 4 KB
-    static constexpr int kStage = kA + kB + kRaw;
-    static constexpr int kS = 4;
+    static constexpr int kStage = kB + kRaw;  // one TMA stage
+    static constexpr int kS = 8;              // TMA stages: deep enough to cover the load latency
     static constexpr int kDw = kM * kEB * 2;  // [128][16] fp16
     static constexpr int kDa = kEB * NT * 4;  // [16][NT] fp32
     static constexpr int kEpi = kDw + kDa;
     static constexpr int kSlots = 512 / NT;   // TMEM D slots, one block each
     static constexpr int kPairs = kSlots / 2; // a stage's two blocks use a pair of slots
-    static constexpr int kEpiOff = kS * kStage;
+    static constexpr int kStageOff = kSA * kA;
+    static constexpr int kEpiOff = kStageOff + kS * kStage;
     static constexpr int kBarOff = kEpiOff + kES * kEpi;
-    static constexpr int kBars = 3 * kS + 2 * kPairs + 2 * kES + 1;
+    static constexpr int kBars = 2 * kS + 2 * kSA + 2 * kPairs + 2 * kES + 1;
     static constexpr int kSmem = kBarOff + kBars * 8 + 16 + 1024;
     static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kStage % 1024 == 0 && kEpi % 1024 == 0, "alignment");
     static_assert(kSmem <= 227 * 1024, "shared memory");
@@ -141,9 +145,10 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     const uint32_t sbase = s0 + pad;
     const uint32_t bars = sbase + C::kBarOff;
     const uint32_t full0 = bars;                      // TMA bytes of a stage landed
-    const uint32_t aready0 = full0 + 8u * C::kS;      // converters wrote the stage's A
-    const uint32_t empty0 = aready0 + 8u * C::kS;     // the stage's MMAs completed
-    const uint32_t tfull0 = empty0 + 8u * C::kS;      // a D slot pair's MMAs completed
+    const uint32_t empty0 = full0 + 8u * C::kS;       // a stage's raw bytes converted and its B read by the MMAs
+    const uint32_t aready0 = empty0 + 8u * C::kS;     // converters wrote an A slot
+    const uint32_t aempty0 = aready0 + 8u * C::kSA;   // the MMAs reading an A slot completed
+    const uint32_t tfull0 = aempty0 + 8u * C::kSA;    // a D slot pair's MMAs completed
     const uint32_t tempty0 = tfull0 + 8u * C::kPairs; // a D slot pair read by every epilogue warp
     const uint32_t efull0 = tempty0 + 8u * C::kPairs;
     const uint32_t eempty0 = efull0 + 8u * kES;
@@ -157,8 +162,11 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kS; ++s) {
             tc::mbar_init(full0 + 8 * s, 1);
-            tc::mbar_init(aready0 + 8 * s, kConvWarps);
-            tc::mbar_init(empty0 + 8 * s, 1);
+            tc::mbar_init(empty0 + 8 * s, kConvWarps + 1);  // the converters + the MMAs' commit
+        }
+        for (int i = 0; i < C::kSA; ++i) {
+            tc::mbar_init(aready0 + 8 * i, kConvWarps);
+            tc::mbar_init(aempty0 + 8 * i, 1);
         }
         for (int j = 0; j < C::kPairs; ++j) {
             tc::mbar_init(tfull0 + 8 * j, 1);
@@ -213,10 +221,10 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                         ok = false;
                         break;
                     }
-                    const uint32_t st = sbase + s * C::kStage;
+                    const uint32_t st = sbase + C::kStageOff + s * C::kStage;
                     tc::mbar_expect_tx(full0 + 8 * s, C::kB + C::kRaw);
-                    tc::tma_load_2d(st + C::kA, &xmap, b0 * 32, t0, full0 + 8 * s);
-                    tc::tma_load_2d(st + C::kA + C::kB, &wmap, b0 * 16, row0, full0 + 8 * s);
+                    tc::tma_load_2d(st, &xmap, b0 * 32, t0, full0 + 8 * s);
+                    tc::tma_load_2d(st + C::kB, &wmap, b0 * 16, row0, full0 + 8 * s);
                     ++k;
                 }
             }
@@ -238,16 +246,16 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
             for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
                 for (int b0 = 0; b0 < a.nb; b0 += kG, ++k) {
                     if (k % kMmaWarps != mine) continue;
-                    const int s = k % C::kS, pr = k % C::kPairs;
-                    if (!tc::mbar_wait(aready0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_f16_status, 25) ||
+                    const int s = k % C::kS, ai = k % C::kSA, pr = k % C::kPairs;
+                    if (!tc::mbar_wait(aready0 + 8 * ai, (k / C::kSA) & 1u, abort_flag, &g_f16_status, 25) ||
                         !tc::mbar_wait(tempty0 + 8 * pr, ((k / C::kPairs) & 1u) ^ 1u, abort_flag, &g_f16_status,
                                        26)) {
                         ok = false;
                         break;
                     }
                     tc::tc_fence_after();
-                    const uint32_t st = sbase + s * C::kStage;
-                    const uint64_t ad = tc::sdesc_kmajor_sw128(st), bd = tc::sdesc_kmajor_sw128(st + C::kA);
+                    const uint64_t ad = tc::sdesc_kmajor_sw128(sbase + ai * C::kA);
+                    const uint64_t bd = tc::sdesc_kmajor_sw128(sbase + C::kStageOff + s * C::kStage);
                     const int nblk = a.nb - b0 < kG ? a.nb - b0 : kG;
                     for (int g = 0; g < nblk; ++g) {
                         // block g: K slices 2g, 2g+1 of 16 fp16 = 32 bytes each (+2 in the address field)
@@ -257,6 +265,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                     }
                     tc::mma_commit(tfull0 + 8 * pr);
                     tc::mma_commit(empty0 + 8 * s);
+                    tc::mma_commit(aempty0 + 8 * ai);
                 }
             }
             // every MMA issued has completed before TMEM is released
@@ -270,15 +279,16 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
             for (int b0 = 0; b0 < a.nb; b0 += kG, ++k) {
-                const int s = k % C::kS;
-                const bool got = tc::mbar_wait(full0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_f16_status, 28);
+                const int s = k % C::kS, ai = k % C::kSA;
+                const bool got =
+                    tc::mbar_wait(full0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_f16_status, 28) &&
+                    tc::mbar_wait(aempty0 + 8 * ai, ((k / C::kSA) & 1u) ^ 1u, abort_flag, &g_f16_status, 31);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
                 }
-                unsigned char* st = sm + s * C::kStage;
-                const uint4* raw = reinterpret_cast<const uint4*>(st + C::kA + C::kB + r * 32);
-                unsigned char* arow = st + (r >> 3) * 1024 + (r & 7) * 128;
+                const uint4* raw = reinterpret_cast<const uint4*>(sm + C::kStageOff + s * C::kStage + C::kB + r * 32);
+                unsigned char* arow = sm + ai * C::kA + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
                 for (int g = 0; g < kG; ++g) {
                     // GGUF order: byte i holds element i (low nibble) and 16 + i (high)
@@ -300,7 +310,10 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                 }
                 tc::fence_proxy_async_smem();  // generic-proxy writes -> the tensor core's reads
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(aready0 + 8 * s);
+                if (lane == 0) {
+                    tc::mbar_arrive(aready0 + 8 * ai);
+                    tc::mbar_arrive(empty0 + 8 * s);  // the raw bytes are consumed
+                }
             }
         }
     } else {

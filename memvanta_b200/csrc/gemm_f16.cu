@@ -78,7 +78,8 @@ struct Cfg {
     static constexpr int kB = NT * kG * 64;   // NT x 128 B
     static constexpr int kRaw = kM * kG * 16; // 4 KB
     static constexpr int kStage = kB + kRaw;  // one TMA stage
-    static constexpr int kS = 8;              // TMA stages: deep enough to cover the load latency
+    static constexpr int kS = NT > 64 ? 6 : 8;  // TMA stages: deep enough to cover the load latency
+    static constexpr int kR = 16;             // stage-completion barriers (one MMA commit per stage)
     static constexpr int kDw = kM * kEB * 2;  // [128][16] fp16
     static constexpr int kDa = kEB * NT * 4;  // [16][NT] fp32
     static constexpr int kEpi = kDw + kDa;
@@ -87,11 +88,12 @@ struct Cfg {
     static constexpr int kStageOff = kSA * kA;
     static constexpr int kEpiOff = kStageOff + kS * kStage;
     static constexpr int kBarOff = kEpiOff + kES * kEpi;
-    static constexpr int kBars = 2 * kS + 2 * kSA + 2 * kPairs + 2 * kES + 1;
+    static constexpr int kBars = kS + kSA + kR + kPairs + 2 * kES + 1;
     static constexpr int kSmem = kBarOff + kBars * 8 + 16 + 1024;
     static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kStage % 1024 == 0 && kEpi % 1024 == 0, "alignment");
     static_assert(kSmem <= 227 * 1024, "shared memory");
     static_assert(kG == 2 && kPairs >= 2, "two stages of D slot pairs");
+    static_assert(kR > kS && kR > kSA && kR > kPairs, "a stage's completion is awaited before its barrier recurs");
 };
 
 struct F16Args {
@@ -137,7 +139,8 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                     const __grid_constant__ CUtensorMap dmap, const __grid_constant__ CUtensorMap smap,
                     const F16Args a) {
     using C = Cfg<NT>;
-    constexpr int TT = 32;  // tokens per epilogue warp
+    constexpr int TT = 32;              // tokens per epilogue warp
+    constexpr int LB = NT > 64 ? 1 : 2; // TMEM slots per load round trip
     extern __shared__ unsigned char smem_dyn[];
     const uint32_t s0 = tc::smem_u32(smem_dyn);
     const uint32_t pad = ((s0 + 1023u) & ~1023u) - s0;
@@ -145,11 +148,11 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     const uint32_t sbase = s0 + pad;
     const uint32_t bars = sbase + C::kBarOff;
     const uint32_t full0 = bars;                      // TMA bytes of a stage landed
-    const uint32_t empty0 = full0 + 8u * C::kS;       // a stage's raw bytes converted and its B read by the MMAs
-    const uint32_t aready0 = empty0 + 8u * C::kS;     // converters wrote an A slot
-    const uint32_t aempty0 = aready0 + 8u * C::kSA;   // the MMAs reading an A slot completed
-    const uint32_t tfull0 = aempty0 + 8u * C::kSA;    // a D slot pair's MMAs completed
-    const uint32_t tempty0 = tfull0 + 8u * C::kPairs; // a D slot pair read by every epilogue warp
+    const uint32_t aready0 = full0 + 8u * C::kS;      // converters wrote an A slot
+    // stage k's MMAs completed (one commit): its TMA slot, its A slot and its
+    // D slot pair -- whose dots the epilogue then reads -- are all released
+    const uint32_t done0 = aready0 + 8u * C::kSA;
+    const uint32_t tempty0 = done0 + 8u * C::kR;      // a D slot pair read by every epilogue warp
     const uint32_t efull0 = tempty0 + 8u * C::kPairs;
     const uint32_t eempty0 = efull0 + 8u * kES;
     const uint32_t done_bar = eempty0 + 8u * kES;
@@ -162,16 +165,10 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kS; ++s) {
             tc::mbar_init(full0 + 8 * s, 1);
-            tc::mbar_init(empty0 + 8 * s, kConvWarps + 1);  // the converters + the MMAs' commit
         }
-        for (int i = 0; i < C::kSA; ++i) {
-            tc::mbar_init(aready0 + 8 * i, kConvWarps);
-            tc::mbar_init(aempty0 + 8 * i, 1);
-        }
-        for (int j = 0; j < C::kPairs; ++j) {
-            tc::mbar_init(tfull0 + 8 * j, 1);
-            tc::mbar_init(tempty0 + 8 * j, C::kEpiWarps);
-        }
+        for (int i = 0; i < C::kSA; ++i) tc::mbar_init(aready0 + 8 * i, kConvWarps);
+        for (int i = 0; i < C::kR; ++i) tc::mbar_init(done0 + 8 * i, 1);
+        for (int j = 0; j < C::kPairs; ++j) tc::mbar_init(tempty0 + 8 * j, C::kEpiWarps);
         for (int e = 0; e < kES; ++e) {
             tc::mbar_init(efull0 + 8 * e, 1);
             tc::mbar_init(eempty0 + 8 * e, C::kEpiWarps);
@@ -217,9 +214,14 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                         ++j;
                     }
                     const int s = k % C::kS;
-                    if (!tc::mbar_wait(empty0 + 8 * s, ((k / C::kS) & 1u) ^ 1u, abort_flag, &g_f16_status, 22)) {
-                        ok = false;
-                        break;
+                    // the slot's previous stage, k - kS, was converted and multiplied
+                    if (k >= (uint32_t)C::kS) {
+                        const uint32_t pk = k - C::kS;
+                        if (!tc::mbar_wait(done0 + 8 * (pk % C::kR), (pk / C::kR) & 1u, abort_flag, &g_f16_status,
+                                           22)) {
+                            ok = false;
+                            break;
+                        }
                     }
                     const uint32_t st = sbase + C::kStageOff + s * C::kStage;
                     tc::mbar_expect_tx(full0 + 8 * s, C::kB + C::kRaw);
@@ -246,7 +248,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
             for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
                 for (int b0 = 0; b0 < a.nb; b0 += kG, ++k) {
                     if (k % kMmaWarps != mine) continue;
-                    const int s = k % C::kS, ai = k % C::kSA, pr = k % C::kPairs;
+                    const int ai = k % C::kSA, pr = k % C::kPairs, s = k % C::kS;
                     if (!tc::mbar_wait(aready0 + 8 * ai, (k / C::kSA) & 1u, abort_flag, &g_f16_status, 25) ||
                         !tc::mbar_wait(tempty0 + 8 * pr, ((k / C::kPairs) & 1u) ^ 1u, abort_flag, &g_f16_status,
                                        26)) {
@@ -263,9 +265,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                         mma_f16(d, ad + 2 * (2 * g), bd + 2 * (2 * g), idesc, 0u);
                         mma_f16(d, ad + 2 * (2 * g + 1), bd + 2 * (2 * g + 1), idesc, 1u);
                     }
-                    tc::mma_commit(tfull0 + 8 * pr);
-                    tc::mma_commit(empty0 + 8 * s);
-                    tc::mma_commit(aempty0 + 8 * ai);
+                    tc::mma_commit(done0 + 8 * (k % C::kR));
                 }
             }
             // every MMA issued has completed before TMEM is released
@@ -280,9 +280,12 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
         for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
             for (int b0 = 0; b0 < a.nb; b0 += kG, ++k) {
                 const int s = k % C::kS, ai = k % C::kSA;
+                // the A slot's previous stage, k - kSA, was multiplied
+                const uint32_t pk = k - C::kSA;
                 const bool got =
                     tc::mbar_wait(full0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_f16_status, 28) &&
-                    tc::mbar_wait(aempty0 + 8 * ai, ((k / C::kSA) & 1u) ^ 1u, abort_flag, &g_f16_status, 31);
+                    (k < (uint32_t)C::kSA ||
+                     tc::mbar_wait(done0 + 8 * (pk % C::kR), (pk / C::kR) & 1u, abort_flag, &g_f16_status, 31));
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
@@ -310,10 +313,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                 }
                 tc::fence_proxy_async_smem();  // generic-proxy writes -> the tensor core's reads
                 __syncwarp();
-                if (lane == 0) {
-                    tc::mbar_arrive(aready0 + 8 * ai);
-                    tc::mbar_arrive(empty0 + 8 * s);  // the raw bytes are consumed
-                }
+                if (lane == 0) tc::mbar_arrive(aready0 + 8 * ai);
             }
         }
     } else {
@@ -347,38 +347,45 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                 for (int eb = 0; eb < neb; eb += 2, ++ke) {
                     const int nl = neb - eb < 2 ? neb - eb : 2;  // warp-uniform
                     const uint32_t pr = ke % C::kPairs;
-                    uint32_t v[2][TT];
+                    uint32_t v[LB][TT];
                     // warp-uniform outcome: the TMEM loads below are .sync.aligned
-                    if (!__all_sync(0xffffffffu, tc::mbar_wait(tfull0 + 8 * pr, (ke / C::kPairs) & 1u, abort_flag,
+                    if (!__all_sync(0xffffffffu, tc::mbar_wait(done0 + 8 * (ke % C::kR), (ke / C::kR) & 1u, abort_flag,
                                                                &g_f16_status, 30))) {
                         ok = false;
                         break;
                     }
                     tc::tc_fence_after();
+                    // LB slots per TMEM round trip (registers allow two at 64 tokens)
 #pragma unroll
-                    for (int i = 0; i < 2; ++i)
-                        if (i < nl) tc::tmem_ld32(tl + (2 * pr + i) * NT, v[i]);
-                    if (!ok) break;
-                    tc::tmem_wait_ld();
-                    tc::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(tempty0 + 8 * pr);  // the pair is free for the MMAs
+                    for (int i0 = 0; i0 < 2; i0 += LB) {
+                        if (i0 >= nl) break;
 #pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        if (i < nl) {
-                            const int b = eb + i;
-                            const uint32_t word = dwp[b >> 1];
-                            const float dw = half_bits_to_float((unsigned short)((b & 1) ? word >> 16 : word));
-                            const uint64_t dw2 = pack2(dw, dw);
-                            const ulonglong2* d4p = reinterpret_cast<const ulonglong2*>(da + b * NT + slice * TT);
+                        for (int i = 0; i < LB; ++i)
+                            if (i0 + i < nl) tc::tmem_ld32(tl + (2 * pr + i0 + i) * NT, v[i]);
+                        tc::tmem_wait_ld();
+                        if (i0 + LB >= nl) {  // the pair's last loads: the slots are free for the MMAs
+                            tc::tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) tc::mbar_arrive(tempty0 + 8 * pr);
+                        }
 #pragma unroll
-                            for (int t4 = 0; t4 < TT / 4; ++t4) {
-                                const ulonglong2 d4 = d4p[t4];
-                                const uint64_t v0 = (uint64_t)v[i][4 * t4] | ((uint64_t)v[i][4 * t4 + 1] << 32);
-                                const uint64_t v1 = (uint64_t)v[i][4 * t4 + 2] | ((uint64_t)v[i][4 * t4 + 3] << 32);
-                                // fma(fp16(d_w) * d_a, float(isum), sum): the product rounded first
-                                acc[2 * t4] = tc::f2_fma(tc::f2_mul(dw2, d4.x), v0, acc[2 * t4]);
-                                acc[2 * t4 + 1] = tc::f2_fma(tc::f2_mul(dw2, d4.y), v1, acc[2 * t4 + 1]);
+                        for (int i = 0; i < LB; ++i) {
+                            if (i0 + i < nl) {
+                                const int b = eb + i0 + i;
+                                const uint32_t word = dwp[b >> 1];
+                                const float dw = half_bits_to_float((unsigned short)((b & 1) ? word >> 16 : word));
+                                const uint64_t dw2 = pack2(dw, dw);
+                                const ulonglong2* d4p = reinterpret_cast<const ulonglong2*>(da + b * NT + slice * TT);
+#pragma unroll
+                                for (int t4 = 0; t4 < TT / 4; ++t4) {
+                                    const ulonglong2 d4 = d4p[t4];
+                                    const uint64_t v0 = (uint64_t)v[i][4 * t4] | ((uint64_t)v[i][4 * t4 + 1] << 32);
+                                    const uint64_t v1 =
+                                        (uint64_t)v[i][4 * t4 + 2] | ((uint64_t)v[i][4 * t4 + 3] << 32);
+                                    // fma(fp16(d_w) * d_a, float(isum), sum): the product rounded first
+                                    acc[2 * t4] = tc::f2_fma(tc::f2_mul(dw2, d4.x), v0, acc[2 * t4]);
+                                    acc[2 * t4 + 1] = tc::f2_fma(tc::f2_mul(dw2, d4.y), v1, acc[2 * t4 + 1]);
+                                }
                             }
                         }
                     }
@@ -466,6 +473,9 @@ cudaError_t gemm_q4_q8_f16(const mv_weight_s& w, const uint16_t* qh, const float
     if (!batch) return cudaSuccess;
     if (w.type != 2 || ldb < gemm_tc_ldb(batch) || ldb % 4 || w.rows >= (1ull << 31) || batch >= (1ull << 31))
         return cudaErrorInvalidValue;
+    // 128-token tiles halve the per-token share of the MMA issue and the
+    // pipeline's synchronisation; below 128 tokens, 64-token tiles
+    if (batch >= 128) return launch_f16<128>(w, qh, dT, ldb, batch, y, w.rows, s, accumulate);
     return launch_f16<64>(w, qh, dT, ldb, batch, y, w.rows, s, accumulate);
 }
 

@@ -60,6 +60,7 @@ extern "C" {
 
 typedef struct mv_weight_s* mv_weight_t;
 typedef struct mv_model_s* mv_model_t;
+typedef struct mv_seqs_s* mv_seqs_t;
 
 /* ------------------------------------------------------------ runtime */
 
@@ -77,6 +78,14 @@ MV_API int mv_binary_arch(int* out);
  * since the last check -- its outputs are then invalid.  Host-pointer calls
  * and the model check this themselves.  No counterpart in the reference. */
 MV_API int mv_stream_status(void* stream);
+/* Test hook for the bounded waits (no counterpart in the reference): the
+ * next fp16 tensor-core GEMM launch (mv_gemm, MV_ACT_Q8, batch >= 64) leaves
+ * out the MMA commit of its pipeline stage `skip_commit_stage` (-1: none) and
+ * bounds each of its mbarrier waits by wait_limit_us (0: the default 2 s).
+ * A wait then runs out; the kernel drains its copies and MMAs, frees its
+ * tensor memory and returns, and mv_stream_status reports MV_ERR_TIMEOUT.
+ * Applies to one launch; later launches are unaffected. */
+MV_API int mv_test_gemm_stall(int skip_commit_stage, uint64_t wait_limit_us);
 
 /* ------------------------------------------------------------ weights */
 
@@ -274,7 +283,12 @@ MV_API int mv_model_reset(mv_model_t m);                       /* LlamaModel::re
 MV_API uint64_t mv_model_position(mv_model_t m);               /* LlamaModel::position     */
 MV_API uint64_t mv_model_kv_bytes(mv_model_t m);               /* kv_bytes_allocated       */
 /* Decode one token; logits_host (vocab floats) may be NULL when
- * compute_logits is 0.  LlamaModel::forward, src/llama_model.cpp:253-259. */
+ * compute_logits is 0.  LlamaModel::forward, src/llama_model.cpp:253-259.
+ * The decode attention keeps the reference's order bit for bit; with
+ * MV_ATTN_SPLIT=1 in the environment at mv_model_open it is split over the
+ * context instead (partial softmax states merged in a fixed order, ~1e-6
+ * from the reference order per step -- enough for later Q8 activation
+ * roundings to move the logits past 2e-2 over tens of steps). */
 MV_API int mv_model_forward(mv_model_t m, int32_t token, int compute_logits, float* logits_host);
 /* Prefill in chunks of `batch` tokens with Q8 activations (the reference's
  * MEMVANTA_FORCE_Q8_ACT=1 numerics).  LlamaModel::prefill, :260. */
@@ -291,6 +305,28 @@ MV_API void* mv_model_stream(mv_model_t m);
  * environment at mv_model_open), 0 when it runs one kernel per operation.
  * Both give identical outputs.  No counterpart in the reference. */
 MV_API int mv_model_decode_persistent(mv_model_t m);
+
+/* ------------------------------------- several sequences, one batch */
+
+/* A set of n_seq sequences of up to ctx tokens each (ctx <= the model's
+ * context) decoded together with model m's weights (one GPU).  Each sequence
+ * has its own paged KV cache; the set's block table maps sequence i's pages
+ * into one pool per layer (the layout of mv_paged_attn_decode).  The
+ * reference decodes one sequence per LlamaModel; a row of a batched step is
+ * that sequence's LlamaModel::forward (src/llama_model.cpp:253-257). */
+MV_API int mv_model_seqs_open(mv_model_t m, uint64_t n_seq, uint64_t ctx, mv_seqs_t* out);
+MV_API int mv_model_seqs_free(mv_seqs_t s);
+/* mv_model_prefill for sequence `seq` of the set, from its position. */
+MV_API int mv_model_seqs_prefill(mv_seqs_t s, uint64_t seq, const int32_t* tokens_host, uint64_t n, uint64_t batch,
+                                 int compute_logits, float* logits_host);
+MV_API int mv_model_seqs_position(mv_seqs_t s, uint64_t seq, uint64_t* pos);
+MV_API int mv_model_seqs_reset(mv_seqs_t s, uint64_t seq);
+/* One decode step of every sequence of the set: tokens_host[n_seq], one per
+ * sequence at its own position; logits_host receives [n_seq][vocab] (may be
+ * NULL).  The projections run as one batch of n_seq rows (the weights are
+ * read once for all sequences) with the per-row arithmetic of mv_model_forward,
+ * the attention through the set's block table. */
+MV_API int mv_model_forward_batch(mv_model_t m, mv_seqs_t s, const int32_t* tokens_host, float* logits_host);
 
 /* ---------------------------------------------- tensor parallel model */
 

@@ -22,12 +22,13 @@ import numpy as np
 
 from . import _lib
 from ._lib import (F32, F16, Q4_0, Q8_0, Q6_K, ACT_F32, ACT_Q8, KV_F32, KV_F16, KV_Q8, KV_Q8_0,  # noqa: F401
-                   MemVantaError, check, load)
+                   MV_ERR_TIMEOUT, MemVantaError, check, load)
 
 __all__ = [
     "init", "Weight", "tensor_matvec", "tensor_matmul_batch", "tensor_matmul_batch_v06", "tensor_read_row_f32",
     "gemv", "gemm", "quantize_q8", "q4_0_block_dots", "read_rows", "rmsnorm", "rope", "silu_mul", "add_inplace",
     "fp32_to_fp16", "kv_row_bytes", "kv_row_scales", "kv_append", "paged_attn_decode", "paged_attn_prefill", "LlamaModel",
+    "SequenceSet",
     "MemVantaError",
 ]
 
@@ -147,6 +148,12 @@ def stream_status(stream=None) -> None:
     """Synchronise the stream; raise MV_ERR_TIMEOUT if a tensor-core kernel
     gave up a bounded device-side wait since the last check."""
     check(load().mv_stream_status(_stream(stream)))
+
+
+def test_gemm_stall(skip_commit_stage: int, wait_limit_us: int = 0) -> None:
+    """Test hook: the next fp16 tensor-core GEMM launch leaves out one MMA
+    commit and bounds its waits by wait_limit_us (mv_test_gemm_stall)."""
+    check(load().mv_test_gemm_stall(skip_commit_stage, wait_limit_us))
 
 
 def quantize_q8(x, stream=None):
@@ -316,4 +323,4 @@ def paged_attn_prefill(kv_type, q, n_head, n_head_kv, head_dim, k_pages, v_pages
     return out
 
 
-from .model import LlamaModel  # noqa: E402
+from .model import LlamaModel, SequenceSet  # noqa: E402

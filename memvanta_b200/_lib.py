@@ -32,6 +32,7 @@ SIGNATURES = {
     "mv_version": (_i, []),
     "mv_binary_arch": (_i, [C.POINTER(_i)]),
     "mv_stream_status": (_i, [_p]),
+    "mv_test_gemm_stall": (_i, [_i, _u64]),
     "mv_weight_upload": (_i, [_p, _u64, _i, _u64, _u64, _p, C.POINTER(_p)]),
     "mv_weight_from_device": (_i, [_p, _u64, _i, _u64, _u64, _p, C.POINTER(_p)]),
     "mv_weight_free": (_i, [_p]),
@@ -72,6 +73,12 @@ SIGNATURES = {
     "mv_model_generate_greedy": (_i, [_p, C.c_int32, _u64, _p]),
     "mv_model_stream": (_p, [_p]),
     "mv_model_decode_persistent": (_i, [_p]),
+    "mv_model_seqs_open": (_i, [_p, _u64, _u64, C.POINTER(_p)]),
+    "mv_model_seqs_free": (_i, [_p]),
+    "mv_model_seqs_prefill": (_i, [_p, _u64, _p, _u64, _u64, _i, _p]),
+    "mv_model_seqs_position": (_i, [_p, _u64, C.POINTER(_u64)]),
+    "mv_model_seqs_reset": (_i, [_p, _u64]),
+    "mv_model_forward_batch": (_i, [_p, _p, _p, _p]),
     "mv_int_quantize_q8_0": (_i, [_p, _u64, _p, _p]),
     "mv_int_quantize_q4_0": (_i, [_p, _u64, _p, _p]),
     "mv_int_matvec_q4_q8": (_i, [_p, _p, _p, _u64, _u64, _p]),

@@ -332,6 +332,12 @@ MV_API int mv_stream_status(void* stream) {
     return MV_OK;
 }
 
+MV_API int mv_test_gemm_stall(int skip_commit_stage, uint64_t wait_limit_us) {
+    if (skip_commit_stage < -1 || wait_limit_us > 10000000ull) return fail(MV_ERR_INVALID, "bad test stall");
+    mvb::gemm_f16_test_stall(skip_commit_stage, wait_limit_us * 1000ull);
+    return MV_OK;
+}
+
 MV_API int mv_quantize_q8(const float* x, uint64_t rows, uint64_t cols, int8_t* q, float* d, void* stream) {
     if (cols % 32) return fail(MV_ERR_INVALID, "Q8 activation quantization requires cols multiple of 32");
     if (rows && (!x || !q || !d)) return fail(MV_ERR_INVALID, "null pointer");

@@ -35,6 +35,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdlib>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -99,6 +100,8 @@ struct Cfg {
 struct F16Args {
     float* y;  // row r of token t at y[t * ldy + r]
     int rows, nb, batch, n_ttiles, n_tiles, accumulate, ldy;
+    uint64_t wait_ns;  // bound of every mbarrier wait
+    int skip_commit;   // test hook: the stage whose MMA commit is left out (-1: none)
 };
 
 // Instruction descriptor of kind::f16: f16 x f16 -> f32, both K-major, M x N.
@@ -203,7 +206,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                 for (int b0 = 0; b0 < a.nb; b0 += kG) {
                     if (b0 % kEB == 0) {
                         const int e = j % kES;
-                        if (!tc::mbar_wait(eempty0 + 8 * e, ((j / kES) & 1u) ^ 1u, abort_flag, &g_f16_status, 21)) {
+                        if (!tc::mbar_wait(eempty0 + 8 * e, ((j / kES) & 1u) ^ 1u, abort_flag, &g_f16_status, 21, true, a.wait_ns)) {
                             ok = false;
                             break;
                         }
@@ -218,7 +221,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                     if (k >= (uint32_t)C::kS) {
                         const uint32_t pk = k - C::kS;
                         if (!tc::mbar_wait(done0 + 8 * (pk % C::kR), (pk / C::kR) & 1u, abort_flag, &g_f16_status,
-                                           22)) {
+                                           22, true, a.wait_ns)) {
                             ok = false;
                             break;
                         }
@@ -232,9 +235,9 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
             }
             // drain: the latest load of every slot has landed before the CTA exits
             for (uint32_t i = k > (uint32_t)C::kS ? k - C::kS : 0; i < k; ++i)
-                tc::mbar_wait(full0 + 8 * (i % C::kS), (i / C::kS) & 1u, abort_flag, &g_f16_status, 23, false);
+                tc::mbar_wait(full0 + 8 * (i % C::kS), (i / C::kS) & 1u, abort_flag, &g_f16_status, 23, false, a.wait_ns);
             for (uint32_t i = j > (uint32_t)kES ? j - kES : 0; i < j; ++i)
-                tc::mbar_wait(efull0 + 8 * (i % kES), (i / kES) & 1u, abort_flag, &g_f16_status, 24, false);
+                tc::mbar_wait(efull0 + 8 * (i % kES), (i / kES) & 1u, abort_flag, &g_f16_status, 24, false, a.wait_ns);
         }
     } else if (warp <= kMmaWarps) {
         // --------------------------------------------------- MMA issuers
@@ -249,9 +252,9 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                 for (int b0 = 0; b0 < a.nb; b0 += kG, ++k) {
                     if (k % kMmaWarps != mine) continue;
                     const int ai = k % C::kSA, pr = k % C::kPairs, s = k % C::kS;
-                    if (!tc::mbar_wait(aready0 + 8 * ai, (k / C::kSA) & 1u, abort_flag, &g_f16_status, 25) ||
+                    if (!tc::mbar_wait(aready0 + 8 * ai, (k / C::kSA) & 1u, abort_flag, &g_f16_status, 25, true, a.wait_ns) ||
                         !tc::mbar_wait(tempty0 + 8 * pr, ((k / C::kPairs) & 1u) ^ 1u, abort_flag, &g_f16_status,
-                                       26)) {
+                                       26, true, a.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -265,12 +268,12 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                         mma_f16(d, ad + 2 * (2 * g), bd + 2 * (2 * g), idesc, 0u);
                         mma_f16(d, ad + 2 * (2 * g + 1), bd + 2 * (2 * g + 1), idesc, 1u);
                     }
-                    tc::mma_commit(done0 + 8 * (k % C::kR));
+                    if ((int)k != a.skip_commit) tc::mma_commit(done0 + 8 * (k % C::kR));
                 }
             }
             // every MMA issued has completed before TMEM is released
             tc::mma_commit(done_bar);
-            tc::mbar_wait(done_bar, 0, abort_flag, &g_f16_status, 27, false);
+            tc::mbar_wait(done_bar, 0, abort_flag, &g_f16_status, 27, false, a.wait_ns);
         }
     } else if (warp < kEpi0) {
         // ------------------------------------------------------ converters
@@ -283,9 +286,9 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                 // the A slot's previous stage, k - kSA, was multiplied
                 const uint32_t pk = k - C::kSA;
                 const bool got =
-                    tc::mbar_wait(full0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_f16_status, 28) &&
+                    tc::mbar_wait(full0 + 8 * s, (k / C::kS) & 1u, abort_flag, &g_f16_status, 28, true, a.wait_ns) &&
                     (k < (uint32_t)C::kSA ||
-                     tc::mbar_wait(done0 + 8 * (pk % C::kR), (pk / C::kR) & 1u, abort_flag, &g_f16_status, 31));
+                     tc::mbar_wait(done0 + 8 * (pk % C::kR), (pk / C::kR) & 1u, abort_flag, &g_f16_status, 31, true, a.wait_ns));
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
@@ -333,7 +336,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
             for (int b16 = 0; ok && b16 < a.nb; b16 += kEB) {
                 const int e = j % kES;
                 if (!__all_sync(0xffffffffu,
-                                tc::mbar_wait(efull0 + 8 * e, (j / kES) & 1u, abort_flag, &g_f16_status, 29))) {
+                                tc::mbar_wait(efull0 + 8 * e, (j / kES) & 1u, abort_flag, &g_f16_status, 29, true, a.wait_ns))) {
                     ok = false;
                     break;
                 }
@@ -350,7 +353,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                     uint32_t v[LB][TT];
                     // warp-uniform outcome: the TMEM loads below are .sync.aligned
                     if (!__all_sync(0xffffffffu, tc::mbar_wait(done0 + 8 * (ke % C::kR), (ke / C::kR) & 1u, abort_flag,
-                                                               &g_f16_status, 30))) {
+                                                               &g_f16_status, 30, true, a.wait_ns))) {
                         ok = false;
                         break;
                     }
@@ -419,6 +422,23 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     }
 }
 
+// Test hook (gemm_f16_test_stall): one launch with a shorter wait bound and
+// one MMA commit left out, so that its waits run out and it returns with a
+// status instead of its results.
+struct TestStall {
+    uint64_t wait_ns = tc::kWaitLimitNs;
+    int skip_commit = -1;
+};
+std::mutex g_stall_mu;
+TestStall g_stall;
+
+TestStall take_test_stall() {
+    std::lock_guard<std::mutex> lock(g_stall_mu);
+    const TestStall t = g_stall;
+    g_stall = TestStall{};
+    return t;
+}
+
 template <int NT>
 cudaError_t launch_f16(const mv_weight_s& w, const uint16_t* qh, const float* dT, uint64_t ldb, uint64_t batch,
                        float* y, uint64_t ldy, cudaStream_t s, bool accumulate) {
@@ -452,13 +472,21 @@ cudaError_t launch_f16(const mv_weight_s& w, const uint16_t* qh, const float* dT
     }
     const int n_ttiles = (int)((batch + NT - 1) / NT);
     const int n_tiles = (int)((w.rows + kM - 1) / kM) * n_ttiles;
-    const F16Args args{y, (int)w.rows, (int)w.nb, (int)batch, n_ttiles, n_tiles, accumulate ? 1 : 0, (int)ldy};
+    const TestStall ts = take_test_stall();
+    const F16Args args{y,        (int)w.rows,         (int)w.nb, (int)batch, n_ttiles, n_tiles, accumulate ? 1 : 0,
+                       (int)ldy, ts.wait_ns,          ts.skip_commit};
     ensure_smem_attr(gemm_f16_kernel<NT>, C::kSmem);
     const int grid = n_tiles < num_sms() ? n_tiles : num_sms();
     return launch_pdl(gemm_f16_kernel<NT>, dim3(grid), dim3(C::kThreads), C::kSmem, s, wmap, xmap, dmap, smap, args);
 }
 
 }  // namespace
+
+void gemm_f16_test_stall(int skip_commit, uint64_t wait_ns) {
+    std::lock_guard<std::mutex> lock(g_stall_mu);
+    g_stall.skip_commit = skip_commit;
+    g_stall.wait_ns = wait_ns ? wait_ns : tc::kWaitLimitNs;
+}
 
 bool gemm_f16_preferred(uint64_t batch) {
     static const bool off = [] {

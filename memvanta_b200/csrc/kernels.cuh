@@ -101,6 +101,9 @@ cudaError_t f16_status_take(int* status);
 // whether a Q8-activation matmul of `batch` tokens takes gemm_q4_q8_f16
 // (64 tokens and more; MV_GEMM_F16=0 keeps the int8 kernel everywhere)
 bool gemm_f16_preferred(uint64_t batch);
+// Test hook: the next fp16 GEMM launch leaves out the MMA commit of stage
+// skip_commit (-1: none) and bounds its waits by wait_ns (0: the default).
+void gemm_f16_test_stall(int skip_commit, uint64_t wait_ns);
 
 // ---- ops.cu
 cudaError_t rmsnorm_rows(const float* x, const float* w, uint64_t rows, uint64_t n, float eps, float* out,
@@ -188,6 +191,16 @@ cudaError_t tp_scatter_ll(const TpCtx& tp, const float* src, uint64_t n, uint64_
 
 uint64_t attn_fused_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type);
 cudaError_t attn_decode_fused(const AttnFusedArgs& a, cudaStream_t s);
+// The same step with the attention split over the context (attn_split.cu):
+// a cluster of CTAs per head, partial softmax states merged in a fixed order
+// (outputs within ~1e-6 of the exact kernel; cache rows identical).
+// attn_fused_split_smem_bytes is 0 for an unsupported kv type / head size.
+uint64_t attn_fused_split_smem_bytes(uint64_t hd, uint64_t max_pages, int kv_type);
+// The same step in the reference's order over a cluster of CTAs per head
+// (attn_cluster.cu); attn_cluster_smem_bytes is 0 when unsupported.
+uint64_t attn_cluster_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type);
+cudaError_t attn_decode_cluster(const AttnFusedArgs& a, cudaStream_t s);
+cudaError_t attn_decode_fused_split(const AttnFusedArgs& a, cudaStream_t s);
 
 // ---- decode_mk.cu : every layer of one decode step as one persistent
 // (cooperative) kernel, one CTA per SM; one GPU, Q4_0 layer weights, F32/F16 KV

@@ -51,7 +51,7 @@ namespace mvb {
 // receives pos+1 for the attention that follows.
 __global__ void rope_append_heads_kernel(float* __restrict__ qkv, int ld, int n_head, int n_head_kv, int hd,
                                          const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                         const int32_t* __restrict__ pos, int kv_type, const int32_t* __restrict__ table,
+                                         const int32_t* __restrict__ pos, int kv_type, const int32_t* __restrict__ table, int table_ld,
                                          int page, uint8_t* __restrict__ k_pages, uint8_t* __restrict__ v_pages,
                                          float* __restrict__ k_scales, float* __restrict__ v_scales,
                                          int32_t* __restrict__ ctx_out) {
@@ -74,7 +74,7 @@ __global__ void rope_append_heads_kernel(float* __restrict__ qkv, int ld, int n_
         __syncthreads();
         const bool is_v = unit >= n_head + n_head_kv;
         const int head = unit - n_head - (is_v ? n_head_kv : 0);
-        const size_t slot = (size_t)table[p / page] * page + p % page;
+        const size_t slot = (size_t)table[(size_t)r * table_ld + p / page] * page + p % page;
         uint8_t* pages = is_v ? v_pages : k_pages;
         const size_t base = slot * KV + (size_t)head * hd;
         if (kv_type == 0) {
@@ -104,7 +104,7 @@ __global__ void rope_append_heads_kernel(float* __restrict__ qkv, int ld, int n_
 // ctx_out (optional) receives pos+1 for the attention that follows.
 __global__ void rope_append_row_kernel(float* __restrict__ qkv, int ld, int n_head, int n_head_kv, int hd,
                                    const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                   const int32_t* __restrict__ pos, int kv_type, const int32_t* __restrict__ table,
+                                   const int32_t* __restrict__ pos, int kv_type, const int32_t* __restrict__ table, int table_ld,
                                    int page, uint8_t* __restrict__ k_pages, uint8_t* __restrict__ v_pages,
                                    float* __restrict__ k_scales, float* __restrict__ v_scales,
                                    int32_t* __restrict__ ctx_out) {
@@ -123,7 +123,7 @@ __global__ void rope_append_row_kernel(float* __restrict__ qkv, int ld, int n_he
         b[j + half] = __fmaf_rn(x0, s, __fmul_rn(x1, c));
     }
     __syncthreads();
-    const size_t slot = (size_t)table[p / page] * page + p % page;
+    const size_t slot = (size_t)table[(size_t)r * table_ld + p / page] * page + p % page;
     for (int which = 0; which < 2; ++which) {
         const float* src = row + D + which * KV;
         uint8_t* pages = which ? v_pages : k_pages;
@@ -296,6 +296,9 @@ struct mv_model_s {
     float* rope_sin = nullptr;
     int32_t* table = nullptr;              // [max_q][n_pages] identity rows
     uint64_t table_rows = 0;
+    // set while a prefill fills one sequence of a sequence set (mv_seqs_s):
+    // the layers with that sequence's cache pages
+    const std::vector<mvb::Layer>* kv_layers = nullptr;
 
     // decode state (device)
     float *x = nullptr, *qkv = nullptr, *att = nullptr, *ff = nullptr, *gu = nullptr, *nrm = nullptr;
@@ -303,6 +306,15 @@ struct mv_model_s {
     int32_t *token_dev = nullptr, *pos_dev = nullptr, *ctx_dev = nullptr, *history = nullptr;
     float* logits_host = nullptr;          // pinned
     cudaGraphExec_t graph_logits = nullptr, graph_nologits = nullptr;
+    // decode attention in the reference's order (attention.cu), or split
+    // over the context (attn_split.cu) with MV_ATTN_SPLIT=1: ~1e-6 from the
+    // reference order per step, which later Q8 activation roundings amplify
+    // past the end-to-end logits bar, so it is not the default
+    bool attn_split = false;
+    // F16/F32 reference-order decode attention over a cluster of CTAs per
+    // head (attn_cluster.cu) where its staging fits; MV_ATTN_CLUSTER=0 keeps
+    // the one-CTA-per-head kernel (attention.cu)
+    bool attn_cluster = false;
     // one GPU: every layer of a decode step in one persistent kernel
     // (decode_mk.cu), with MV_DECODE_PERSISTENT=1 where supported
     bool mk = false;
@@ -635,14 +647,17 @@ void project_decode(mv_model_s* m, mv_weight_s* w, const float* x, const float* 
 // plain = true: a full-order launch, for a launch right after an event wait
 // (the attention after it, a PDL launch, relies on this kernel's completion
 // implying the event's).
+// table: block-table rows of `table_ld` pages, row r for qkv row r (table_ld 0:
+// every row is a token of the one sequence whose pages row 0 lists).
 void rope_append(mv_model_s* m, const mvb::Layer& L, float* qkv, uint64_t rows, const int32_t* pos, int32_t* ctx_out,
-                 bool plain = false) {
+                 bool plain = false, const int32_t* table = nullptr, int table_ld = 0) {
+    if (!table) table = m->table;
     const uint64_t QKVW = m->qkvw;  // this rank's heads
     cudaError_t e;
     if (m->kv_type == MV_KV_Q8) {
         e = mvb::launch_opt(!plain, mvb::rope_append_row_kernel, dim3((unsigned)rows), dim3(256), 0, m->stream, qkv,
                             (int)QKVW, (int)m->nh, (int)m->nkv, (int)m->hd, (const float*)m->rope_cos,
-                            (const float*)m->rope_sin, pos, m->kv_type, (const int32_t*)m->table, (int)m->page,
+                            (const float*)m->rope_sin, pos, m->kv_type, table, table_ld, (int)m->page,
                             L.k_pages, L.v_pages, L.k_scales, L.v_scales, ctx_out);
     } else {
         const int threads = m->kv_type == MV_KV_Q8_0 ? (int)std::max<uint64_t>(64, m->hd) : (int)(m->hd / 2);
@@ -650,7 +665,7 @@ void rope_append(mv_model_s* m, const mvb::Layer& L, float* qkv, uint64_t rows, 
                             dim3((unsigned)rows, (unsigned)(m->nh + 2 * m->nkv)), dim3(threads), 0,
                             m->stream, qkv, (int)QKVW, (int)m->nh, (int)m->nkv, (int)m->hd,
                             (const float*)m->rope_cos, (const float*)m->rope_sin, pos, m->kv_type,
-                            (const int32_t*)m->table, (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales,
+                            table, table_ld, (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales,
                             ctx_out);
     }
     ck(e, "rope_append");
@@ -745,11 +760,15 @@ void launch_decode(mv_model_s* m, bool with_logits) {
                 fa.head_off = (int)(r * m->nh);
                 fa.out_point = pt_att(l);
             }
-            ck(mvb::attn_decode_fused(fa, s), "attention (fused)");
+            ck(m->attn_split     ? mvb::attn_decode_fused_split(fa, s)
+               : m->attn_cluster ? mvb::attn_decode_cluster(fa, s)
+                                 : mvb::attn_decode_fused(fa, s),
+               "attention (fused)");
         } else {
             rope_append(m, L, m->qkv, 1, m->pos_dev, m->ctx_dev);
             float* out = tp ? m->ATT_l : m->att;
-            ck(mvb::paged_attn_decode(attn_args(m, L, m->qkv, m->qkvw, 1, m->ctx_dev, m->n_ctx, out), s), "attention");
+            const mvb::AttnArgs aa = attn_args(m, L, m->qkv, m->qkvw, 1, m->ctx_dev, m->n_ctx, out);
+            ck(m->attn_split ? mvb::paged_attn_decode_split(aa, s) : mvb::paged_attn_decode(aa, s), "attention");
             if (tp) ck(mvb::tp_scatter_ll(m->tp, out, m->Dl, m->off_att, r * m->Dl, pt_att(l), s), "scatter");
         }
         if (tp) {
@@ -812,7 +831,7 @@ void set_decode_inputs(mv_model_s* m, int32_t token) {
 // Stages the token ids, positions and context lengths of a whole prefill
 // call with one copy each.  The caller has synchronised the stream, so the
 // pinned staging buffer is free to overwrite.
-void stage_prefill_inputs(mv_model_s* m, const int32_t* tokens, uint64_t n) {
+void stage_prefill_inputs(mv_model_s* m, const int32_t* tokens, uint64_t n, const uint64_t* row_pos = nullptr) {
     if (n > m->in_cap) {
         m->pf_tok = dalloc<int32_t>(m, n);
         m->pf_pos = dalloc<int32_t>(m, n);
@@ -823,9 +842,10 @@ void stage_prefill_inputs(mv_model_s* m, const int32_t* tokens, uint64_t n) {
         m->in_cap = n;
     }
     for (uint64_t i = 0; i < n; ++i) {
+        const uint64_t p = row_pos ? row_pos[i] : m->pos + i;  // row_pos: one decode row per sequence
         m->pf_host[i] = tokens[i];
-        m->pf_host[n + i] = (int32_t)(m->pos + i);
-        m->pf_host[2 * n + i] = (int32_t)(m->pos + i + 1);
+        m->pf_host[n + i] = (int32_t)p;
+        m->pf_host[2 * n + i] = (int32_t)(p + 1);
     }
     ck(cudaMemcpyAsync(m->pf_tok, m->pf_host, n * 4, cudaMemcpyHostToDevice, m->stream), "tokens H2D");
     ck(cudaMemcpyAsync(m->pf_pos, m->pf_host + n, n * 4, cudaMemcpyHostToDevice, m->stream), "pos H2D");
@@ -849,7 +869,8 @@ void ready_decode(mv_model_s* m) {
 
 // One GPU, Q4_0 layer weights, F16/F32 KV: the decode layers run as one
 // persistent kernel (decode_mk.cu) when MV_DECODE_PERSISTENT=1.  Its
-// outputs are bit-identical to the per-kernel path.
+// outputs are bit-identical to the per-kernel path (reference-order
+// attention).
 void setup_persistent_decode(mv_model_s* m) {
     // opt-in while its step is slower than the per-kernel path's;
     // MV_DECODE_PERSISTENT=1 demands it: a model it cannot serve fails to open
@@ -1074,6 +1095,16 @@ void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, in
     m->history = dalloc<int32_t>(m, m->n_ctx + 1);
     ck(cudaMallocHost(reinterpret_cast<void**>(&m->logits_host), m->vocab * sizeof(float)), "cudaMallocHost");
     ensure_prefill(m, 1);  // identity block table
+    {
+        const char* env = std::getenv("MV_ATTN_SPLIT");
+        m->attn_split = env && std::string(env) == "1";
+        const bool fused = m->kv_type == MV_KV_F32 || m->kv_type == MV_KV_F16;
+        const uint64_t need = fused ? mvb::attn_fused_split_smem_bytes(m->hd, m->n_pages, m->kv_type) : 0;
+        if (fused && (need == 0 || need > 200 * 1024)) m->attn_split = false;
+        const char* cenv = std::getenv("MV_ATTN_CLUSTER");
+        const uint64_t cneed = fused ? mvb::attn_cluster_smem_bytes(m->hd, m->n_ctx, m->n_pages, m->kv_type) : 0;
+        m->attn_cluster = cneed && cneed <= 110 * 1024 && !(cenv && std::string(cenv) == "0");
+    }
     if (world == 1) setup_persistent_decode(m);
     if (world == 1) ready_decode(m);  // tensor parallel: once the peers are connected
 }
@@ -1171,8 +1202,22 @@ struct AltSet {
 // Tokens one merged prefill batch holds at most (single GPU).
 constexpr uint64_t kMergedPrefill = 512;
 
-// One chunk of B tokens; `off` indexes the call's staged inputs.
-void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
+// One decode step of every sequence of a set (mv_seqs_s): row i of the batch
+// is sequence i's token at its own position, reading its own cache pages
+// through row i of the set's block table.
+struct SeqStep {
+    const std::vector<mvb::Layer>* layers;  // the set's caches (weights shared)
+    const int32_t* table;                   // device [n_seq][pages]
+    uint64_t pages, max_ctx;
+    float* logits;                          // device [n_seq][vocab]
+};
+
+// One chunk of B tokens; `off` indexes the call's staged inputs.  With `st`,
+// the B rows are one decode token of each of B sequences instead (the
+// reference's LlamaModel::forward per sequence): Q8 activations for every
+// Q4_0 projection as tensor_matvec uses them, the decode attention over each
+// row's own pages, and logits for every row.
+void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last, const SeqStep* st = nullptr) {
     cudaStream_t s = m->stream;
     const uint64_t D = m->n_embd, F = m->n_ff;
     const bool tp = m->tp_world > 1;
@@ -1180,6 +1225,8 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     const int32_t* tok = m->pf_tok + off;
     const int32_t* pos = m->pf_pos + off;
     const int32_t* ctx = m->pf_ctx + off;
+    // Q8 (tensor-core) projections: a chunk of 2+ tokens, or decode rows
+    const bool q8 = B >= 2 || st;
     ck(mvb::read_rows(*m->tok_embd, tok, B, m->X, s), "embed");
     // Q8 activations when B >= 2 and the weight is Q4_0 (FORCE_Q8 path);
     // fp32 activations otherwise, as tensor_matmul_batch_v06 dispatches.
@@ -1190,7 +1237,7 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
         else ck(mvb::gemm_q4_q8_tc(*w, m->XQ, m->XD, ldb, B, out, s, accumulate), "gemm");
     };
     auto project = [&](mv_weight_s* w, const float* in, uint64_t K, float* out, bool accumulate) {
-        if (B >= 2 && w->type == 2) {
+        if (q8 && w->type == 2) {
             const uint64_t ldb = mvb::gemm_tc_ldb(B);
             ck(mvb::quantize_q8_rows_t(in, B, K, m->XQ, m->XD, ldb, s, XH), "quantize");
             gemm(w, ldb, out, accumulate);
@@ -1204,7 +1251,7 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
     // rmsnorm(X) as the input of a projection: fused into the quantisation on
     // the tensor-core path, materialised otherwise
     auto project_normed = [&](mv_weight_s* w, const float* norm_w, float* out) {
-        if (B >= 2 && w->type == 2) {
+        if (q8 && w->type == 2) {
             const uint64_t ldb = mvb::gemm_tc_ldb(B);
             ck(mvb::rmsnorm_quantize_q8_rows_t(m->X, norm_w, B, D, m->eps, m->XQ, m->XD, ldb, s, XH),
                "rmsnorm+quantize");
@@ -1221,23 +1268,32 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
         ck(mvb::tp_scatter(m->tp, src, B, w, w, dst_off, dst_ld, col, add, point, point & 3, s), "scatter");
         ck(mvb::tp_wait(m->tp, point, s), "tp wait");
     };
+    const std::vector<mvb::Layer>& layers = st ? *st->layers : m->kv_layers ? *m->kv_layers : m->layers;
     for (uint64_t l = 0; l < m->n_layer; ++l) {
-        auto& L = m->layers[l];
+        const auto& L = layers[l];
         project_normed(L.qkv, L.attn_norm, m->QKV);
         if (m->pf_wait) ck(cudaStreamWaitEvent(s, (*m->pf_wait)[l], 0), "wait (previous chunk's KV)");
-        rope_append(m, L, m->QKV, B, pos, nullptr, m->pf_wait != nullptr);
+        rope_append(m, L, m->QKV, B, pos, nullptr, m->pf_wait != nullptr, st ? st->table : nullptr,
+                    st ? (int)st->pages : 0);
         if (m->pf_rec) ck(cudaEventRecord((*m->pf_rec)[l], s), "record (this chunk's KV)");
-        mvb::AttnArgs aa = attn_args(m, L, m->QKV, m->qkvw, B, ctx, start + B, tp ? m->ATT_l : m->ATT);
-        aa.one_seq = 1;
+        mvb::AttnArgs aa = attn_args(m, L, m->QKV, m->qkvw, B, ctx, st ? st->max_ctx : start + B,
+                                     tp ? m->ATT_l : m->ATT);
         // single GPU, tensor-core o projection: the attention kernel also
         // writes the o GEMM's Q8 input (no separate quantisation launch)
-        const bool fuse_o = !tp && B >= 2 && L.o->type == 2 && !XH;
-        if (fuse_o) {
-            aa.xq = m->XQ;
-            aa.xdT = m->XD;
-            aa.xq_ldb = mvb::gemm_tc_ldb(B);
+        const bool fuse_o = !tp && !st && B >= 2 && L.o->type == 2 && !XH;
+        if (st) {
+            aa.block_table = st->table;
+            aa.max_pages = st->pages;
+            ck(m->attn_split ? mvb::paged_attn_decode_split(aa, s) : mvb::paged_attn_decode(aa, s), "attention");
+        } else {
+            aa.one_seq = 1;
+            if (fuse_o) {
+                aa.xq = m->XQ;
+                aa.xdT = m->XD;
+                aa.xq_ldb = mvb::gemm_tc_ldb(B);
+            }
+            ck(mvb::paged_attn_prefill(aa, s), "attention");
         }
-        ck(mvb::paged_attn_prefill(aa, s), "attention");
         if (tp) {
             exchange(m->ATT_l, m->Dl, m->off_ATT, D, m->tp_rank * m->Dl, false, pt_att(l));
             project(L.o, m->ATT, D, m->PROJ_l, false);
@@ -1248,7 +1304,7 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
             project(L.o, m->ATT, D, m->X, true);
         }
         project_normed(L.gu, L.ffn_norm, m->GU);
-        if (!tp && B >= 2 && L.down->type == 2) {
+        if (!tp && q8 && L.down->type == 2) {
             // SiLU gate fused into the down GEMM's Q8 quantisation
             const uint64_t ldb = mvb::gemm_tc_ldb(B);
             ck(mvb::silu_quantize_q8_rows_t(m->GU, B, F, m->XQ, m->XD, ldb, s, XH), "silu+quantize");
@@ -1265,6 +1321,10 @@ void prefill_chunk(mv_model_s* m, uint64_t off, uint64_t B, bool logits_last) {
         } else {
             project(L.down, m->FF, F, m->X, true);
         }
+    }
+    if (st) {  // every row's logits: rmsnorm and the output projection over the batch
+        project_normed(m->output, m->output_norm, st->logits);
+        return;
     }
     m->pos += B;
     if (logits_last) {
@@ -1444,11 +1504,13 @@ MV_API int mv_model_forward(mv_model_t m, int32_t token, int compute_logits, flo
     return rc ? model_fail(rc) : MV_OK;
 }
 
-MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uint64_t batch, int compute_logits,
-                            float* logits_host) {
-    if (!m) return MV_ERR_INVALID;
-    if (n == 0) return MV_OK;
-    int rc = guarded([&] {
+}  // extern "C"
+
+namespace {
+
+void prefill_impl(mv_model_t m, const int32_t* tokens, uint64_t n, uint64_t batch, int compute_logits,
+                  float* logits_host) {
+    {
         if (!tokens) throw ModelError(MV_ERR_INVALID, "null tokens");
         if (m->pos + n > m->n_ctx) throw ModelError(MV_ERR_INVALID, "context exhausted");
         for (uint64_t i = 0; i < n; ++i)
@@ -1516,7 +1578,18 @@ MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uin
         ck(mvb::tc_status(m->stream, &status), "status");
         if (status)
             throw ModelError(MV_ERR_TIMEOUT, "prefill GEMM gave up a bounded wait (site " + std::to_string(status) + ")");
-    });
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+MV_API int mv_model_prefill(mv_model_t m, const int32_t* tokens, uint64_t n, uint64_t batch, int compute_logits,
+                            float* logits_host) {
+    if (!m) return MV_ERR_INVALID;
+    if (n == 0) return MV_OK;
+    int rc = guarded([&] { prefill_impl(m, tokens, n, batch, compute_logits, logits_host); });
     return rc ? model_fail(rc) : MV_OK;
 }
 
@@ -1537,6 +1610,174 @@ MV_API int mv_model_generate_greedy(mv_model_t m, int32_t token, uint64_t n, int
         m->pos += n;
         check_tp_status(m);
     });
+    return rc ? model_fail(rc) : MV_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------- sequence sets
+// Several sequences decoded together against one model's weights: each has
+// its own paged KV cache (a run of pages of one pool per layer, placed in
+// the pool in reverse sequence order so the block table is not the
+// identity), filled by its own prefill, and every mv_model_forward_batch
+// call advances all of them by one token as one batch -- the weights are
+// read once per step for all sequences.  Row i of the step is sequence i's
+// LlamaModel::forward (src/llama_model.cpp:253-257): the same per-token
+// arithmetic as a single-sequence decode (Q8 activations and the per-row FMA
+// chain for Q4_0, fp32 activations otherwise), the attention over its own
+// pages through the block table (config 4's layout).
+struct mv_seqs_s {
+    mv_model_s* m = nullptr;
+    uint64_t n_seq = 0, ctx = 0, pages = 0;       // pages per sequence
+    std::vector<uint64_t> slot;                   // pool run of each sequence
+    std::vector<std::vector<mvb::Layer>> views;   // [seq]: layers with that sequence's pages
+    std::vector<mvb::Layer> pool;                 // layers with the pool's base
+    std::vector<void*> allocs;
+    int32_t* table = nullptr;                     // device [n_seq][pages]
+    float* logits = nullptr;                      // device [n_seq][vocab]
+    float* logits_host = nullptr;                 // pinned
+    std::vector<uint64_t> pos;
+    ~mv_seqs_s() {
+        for (void* p : allocs) cudaFree(p);  // (synchronises with the device's work)
+        if (logits_host) cudaFreeHost(logits_host);
+    }
+    template <class T>
+    T* alloc(uint64_t count) {
+        void* p = nullptr;
+        ck(cudaMalloc(&p, count * sizeof(T) + 16), "cudaMalloc(sequence set)");
+        allocs.push_back(p);
+        return static_cast<T*>(p);
+    }
+};
+
+namespace {
+
+void seqs_open(mv_model_s* m, mv_seqs_s* S, uint64_t n_seq, uint64_t ctx) {
+    if (m->tp_world != 1) throw ModelError(MV_ERR_UNSUPPORTED, "sequence sets run on one GPU");
+    if (n_seq == 0 || n_seq > 4096) throw ModelError(MV_ERR_INVALID, "sequence count must be 1..4096");
+    if (ctx == 0 || ctx > m->n_ctx) throw ModelError(MV_ERR_INVALID, "sequence context must be 1..the model's");
+    S->m = m;
+    S->n_seq = n_seq;
+    S->ctx = ctx;
+    S->pages = (ctx + m->page - 1) / m->page;
+    S->pos.assign(n_seq, 0);
+    S->slot.resize(n_seq);
+    for (uint64_t i = 0; i < n_seq; ++i) S->slot[i] = n_seq - 1 - i;
+    const uint64_t rows = n_seq * S->pages * m->page;
+    const uint64_t rb = mvb::kv_row_bytes(m->kv_type, m->kvd), ns = mvb::kv_row_scales(m->kv_type, m->kvd);
+    S->pool = m->layers;
+    for (auto& L : S->pool) {
+        L.k_pages = S->alloc<uint8_t>(rows * rb);
+        L.v_pages = S->alloc<uint8_t>(rows * rb);
+        L.k_scales = ns ? S->alloc<float>(rows * ns) : nullptr;
+        L.v_scales = ns ? S->alloc<float>(rows * ns) : nullptr;
+    }
+    S->views.assign(n_seq, S->pool);
+    std::vector<int32_t> t(n_seq * S->pages);
+    for (uint64_t i = 0; i < n_seq; ++i) {
+        const uint64_t first = S->slot[i] * S->pages;  // first page of the sequence's run
+        for (auto& L : S->views[i]) {
+            L.k_pages += first * m->page * rb;
+            L.v_pages += first * m->page * rb;
+            if (ns) {
+                L.k_scales += first * m->page * ns;
+                L.v_scales += first * m->page * ns;
+            }
+        }
+        for (uint64_t j = 0; j < S->pages; ++j) t[i * S->pages + j] = (int32_t)(first + j);
+    }
+    S->table = S->alloc<int32_t>(t.size());
+    ck(cudaMemcpy(S->table, t.data(), t.size() * 4, cudaMemcpyHostToDevice), "block table upload");
+    S->logits = S->alloc<float>(n_seq * m->vocab);
+    ck(cudaMallocHost(reinterpret_cast<void**>(&S->logits_host), n_seq * m->vocab * sizeof(float)),
+       "cudaMallocHost(sequence set)");
+}
+
+void seqs_forward(mv_model_s* m, mv_seqs_s* S, const int32_t* tokens, float* logits_host) {
+    if (!tokens) throw ModelError(MV_ERR_INVALID, "null tokens");
+    const uint64_t n = S->n_seq;
+    for (uint64_t i = 0; i < n; ++i) {
+        if (tokens[i] < 0 || (uint64_t)tokens[i] >= m->vocab) throw ModelError(MV_ERR_INVALID, "token id out of range");
+        if (S->pos[i] >= S->ctx) throw ModelError(MV_ERR_INVALID, "context exhausted (sequence " + std::to_string(i) + ")");
+    }
+    ck(cudaStreamSynchronize(m->stream), "sync");
+    ensure_prefill(m, n);
+    stage_prefill_inputs(m, tokens, n, S->pos.data());
+    const SeqStep st{&S->pool, S->table, S->pages, S->ctx, S->logits};
+    prefill_chunk(m, 0, n, false, &st);
+    ck(cudaMemcpyAsync(S->logits_host, S->logits, n * m->vocab * 4, cudaMemcpyDeviceToHost, m->stream),
+       "logits D2H");
+    ck(cudaStreamSynchronize(m->stream), "sync");
+    int status = 0;
+    ck(mvb::tc_status(m->stream, &status), "status");
+    if (status)
+        throw ModelError(MV_ERR_TIMEOUT, "batched decode GEMM gave up a bounded wait (site " + std::to_string(status) + ")");
+    for (auto& p : S->pos) ++p;
+    if (logits_host) std::memcpy(logits_host, S->logits_host, n * m->vocab * 4);
+}
+
+}  // namespace
+
+extern "C" {
+
+MV_API int mv_model_seqs_open(mv_model_t m, uint64_t n_seq, uint64_t ctx, mv_seqs_t* out) {
+    if (!m || !out) return MV_ERR_INVALID;
+    *out = nullptr;
+    auto* S = new mv_seqs_s();
+    int rc = guarded([&] { seqs_open(m, S, n_seq, ctx); });
+    if (rc) {
+        delete S;
+        return model_fail(rc);
+    }
+    *out = S;
+    return MV_OK;
+}
+
+MV_API int mv_model_seqs_free(mv_seqs_t s) {
+    delete s;
+    return MV_OK;
+}
+
+MV_API int mv_model_seqs_prefill(mv_seqs_t s, uint64_t seq, const int32_t* tokens, uint64_t n, uint64_t batch,
+                                 int compute_logits, float* logits_host) {
+    if (!s || seq >= s->n_seq) return MV_ERR_INVALID;
+    if (n == 0) return MV_OK;
+    mv_model_s* m = s->m;
+    int rc = guarded([&] {
+        if (s->pos[seq] + n > s->ctx) throw ModelError(MV_ERR_INVALID, "context exhausted");
+        // the model's prefill, pointed at this sequence's pages and position
+        const uint64_t saved = m->pos;
+        m->pos = s->pos[seq];
+        m->kv_layers = &s->views[seq];
+        try {
+            prefill_impl(m, tokens, n, batch, compute_logits, logits_host);
+        } catch (...) {
+            m->kv_layers = nullptr;
+            m->pos = saved;
+            throw;
+        }
+        s->pos[seq] = m->pos;
+        m->kv_layers = nullptr;
+        m->pos = saved;
+    });
+    return rc ? model_fail(rc) : MV_OK;
+}
+
+MV_API int mv_model_seqs_position(mv_seqs_t s, uint64_t seq, uint64_t* pos) {
+    if (!s || !pos || seq >= s->n_seq) return MV_ERR_INVALID;
+    *pos = s->pos[seq];
+    return MV_OK;
+}
+
+MV_API int mv_model_seqs_reset(mv_seqs_t s, uint64_t seq) {
+    if (!s || seq >= s->n_seq) return MV_ERR_INVALID;
+    s->pos[seq] = 0;
+    return MV_OK;
+}
+
+MV_API int mv_model_forward_batch(mv_model_t m, mv_seqs_t s, const int32_t* tokens, float* logits_host) {
+    if (!m || !s || s->m != m) return MV_ERR_INVALID;
+    int rc = guarded([&] { seqs_forward(m, s, tokens, logits_host); });
     return rc ? model_fail(rc) : MV_OK;
 }
 

@@ -89,7 +89,7 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 // site wins).  honor_abort = false keeps waiting after an abort (used to drain
 // copies in flight).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
-                                          int site, bool honor_abort = true) {
+                                          int site, bool honor_abort = true, uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
@@ -98,7 +98,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
         if (mbar_try(bar, parity)) return true;
         if ((i & 7u) == 0) {
             if (honor_abort && *abort_flag) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+            if (globaltimer() - t0 > limit_ns) {
                 *abort_flag = 1;
                 atomicCAS(status, 0, site);
                 return false;

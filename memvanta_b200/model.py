@@ -144,6 +144,11 @@ class LlamaModel:
                 break
         return out
 
+    def open_sequences(self, n_seq: int, ctx: int) -> "SequenceSet":
+        """A set of n_seq sequences (own KV caches, one block table) decoded
+        together with this model's weights (mv_model_seqs_open)."""
+        return SequenceSet(self, n_seq, ctx)
+
     def close(self, barrier: bool = True) -> None:
         """Frees the model.  Tensor parallel: every rank's block is mapped by
         the others, so the ranks first wait for one another."""
@@ -161,5 +166,56 @@ class LlamaModel:
     def __del__(self):
         try:
             self.close(barrier=False)
+        except Exception:
+            pass
+
+
+class SequenceSet:
+    """Several sequences decoded as one batch (mv_model_forward_batch): each
+    has its own paged KV cache and position; ``forward(tokens)`` advances every
+    sequence by one token and returns [n_seq, vocab] logits."""
+
+    def __init__(self, model: LlamaModel, n_seq: int, ctx: int):
+        self._s = None
+        self.model, self.n_seq = model, int(n_seq)
+        h = C.c_void_p()
+        check(load().mv_model_seqs_open(model._m, self.n_seq, int(ctx), C.byref(h)))
+        self._s = h
+        self._logits = np.empty((self.n_seq, model.vocab), np.float32)
+
+    def prefill(self, seq: int, tokens, batch_size: int = 64, compute_logits_last: bool = True) -> np.ndarray:
+        """LlamaModel.prefill for one sequence of the set; its last logits."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty(self.model.vocab, np.float32)
+        check(load().mv_model_seqs_prefill(self._s, int(seq), t.ctypes.data_as(C.c_void_p), t.size, batch_size,
+                                           int(compute_logits_last),
+                                           out.ctypes.data_as(C.c_void_p) if compute_logits_last else None))
+        return out
+
+    def forward(self, tokens) -> np.ndarray:
+        """One decode token of every sequence; [n_seq, vocab] host logits."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        if t.size != self.n_seq:
+            raise ValueError(f"need {self.n_seq} tokens, got {t.size}")
+        check(load().mv_model_forward_batch(self.model._m, self._s, t.ctypes.data_as(C.c_void_p),
+                                            self._logits.ctypes.data_as(C.c_void_p)))
+        return self._logits
+
+    def position(self, seq: int) -> int:
+        p = C.c_uint64()
+        check(load().mv_model_seqs_position(self._s, int(seq), C.byref(p)))
+        return p.value
+
+    def reset(self, seq: int) -> None:
+        check(load().mv_model_seqs_reset(self._s, int(seq)))
+
+    def close(self) -> None:
+        if self._s:
+            load().mv_model_seqs_free(self._s)
+            self._s = None
+
+    def __del__(self):
+        try:
+            self.close()
         except Exception:
             pass

@@ -240,6 +240,31 @@ def test_stream_status_clean(cuda):
     mv.stream_status()
 
 
+@pytest.mark.parametrize("stage", [0, 5])
+def test_tc_gemm_wait_runs_out_then_next_call_is_clean(cuda, oracle, stage):
+    """A bounded wait that runs out, made on purpose through the test hook:
+    the fp16 tensor-core GEMM leaves out one stage's MMA commit, so the
+    epilogue, converters and producer stop getting that stage; with a 20 ms
+    bound one of their waits gives up, every role drains and returns, and
+    mv_stream_status reports MV_ERR_TIMEOUT (no fault, the context stays
+    usable).  The next launch, without the hook, is bit-exact again."""
+    rng = np.random.default_rng(900 + stage)
+    rows, cols, batch = 1024, 2048, 96
+    w = gguf.gen_q4_0(rows, cols, rng)
+    X = rng.standard_normal((batch, cols)).astype(np.float32)
+    W = upload(w, gguf.Q4_0, rows, cols)
+    mv.stream_status()
+    mv.test_gemm_stall(stage, 20000)
+    run_gemm(W, X, cuda, mv.ACT_Q8)
+    with pytest.raises(mv.MemVantaError) as e:
+        mv.stream_status()
+    assert e.value.code == mv.MV_ERR_TIMEOUT
+    got = run_gemm(W, X, cuda, mv.ACT_Q8)
+    mv.stream_status()
+    want = oracle.matmul_batch_v06(gguf.Q4_0, w, rows, cols, X, force_q8=True)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_config2_q8_0_and_q6_k(cuda, oracle):
     """Config 2: Q8_0 4096x4096 and a Q6_K 32000x4096 head, batch 1 and 32."""
     rng = np.random.default_rng(2)

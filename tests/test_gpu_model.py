@@ -8,6 +8,7 @@ no switch (tensor_matvec always quantises Q4_0 activations).
 from __future__ import annotations
 
 import hashlib
+import dataclasses
 import os
 import tempfile
 
@@ -113,6 +114,7 @@ def test_persistent_decode_matches_per_kernel_path(cuda, tmp, kv_type, monkeypat
     rng = np.random.default_rng(11)
     prompt = rng.integers(0, MID.vocab, size=70).astype(np.int32)
     monkeypatch.setenv("MV_DECODE_PERSISTENT", "1")  # fails to open if it cannot run
+    monkeypatch.delenv("MV_ATTN_SPLIT", raising=False)
     a = mv.LlamaModel(path, ctx_override=256, kv_page_tokens=16, kv_type=kv_type)
     monkeypatch.setenv("MV_DECODE_PERSISTENT", "0")
     b = mv.LlamaModel(path, ctx_override=256, kv_page_tokens=16, kv_type=kv_type)
@@ -133,6 +135,159 @@ def test_persistent_decode_matches_per_kernel_path(cuda, tmp, kv_type, monkeypat
     finally:
         a.close()
         b.close()
+
+
+@pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_F32])
+def test_cluster_attention_matches_one_cta_per_head(cuda, tmp, kv_type, monkeypatch):
+    """The reference-order decode attention over a cluster of CTAs per head
+    (the default for F16/F32 caches) against the one-CTA-per-head kernel
+    (MV_ATTN_CLUSTER=0): the same scores, weights and per-dimension chains,
+    so the logits are identical at every step while the context grows from
+    1 token (every CTA but the last without cached tokens) past 200."""
+    path = os.path.join(tmp, "mid.gguf")
+    if not os.path.exists(path):
+        gguf.write_random_llama(path, MID, seed=5)
+    monkeypatch.delenv("MV_ATTN_SPLIT", raising=False)
+    monkeypatch.delenv("MV_ATTN_CLUSTER", raising=False)
+    a = mv.LlamaModel(path, ctx_override=512, kv_page_tokens=16, kv_type=kv_type)
+    monkeypatch.setenv("MV_ATTN_CLUSTER", "0")
+    b = mv.LlamaModel(path, ctx_override=512, kv_page_tokens=16, kv_type=kv_type)
+    try:
+        cur = 7
+        for i in range(210):
+            la, lb = a.forward(cur).copy(), b.forward(cur).copy()
+            assert np.array_equal(la, lb), (i, float(np.max(np.abs(la - lb))))
+            cur = int(np.argmax(la))
+    finally:
+        a.close()
+        b.close()
+
+
+@pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_F32, mv.KV_Q8_0])
+def test_split_attention_decode_close_to_exact(cuda, tmp, kv_type, monkeypatch):
+    """Decode attention split over the context (MV_ATTN_SPLIT=1; the fused
+    RoPE + append + attention kernel for F16/F32, the multi-sequence split
+    kernel after the append for Q8_0) against the default reference-order
+    kernels on the same token stream, with a context that spans several
+    16-token stages of every warp: the prefill is the same code (identical
+    logits), the first decode step agrees within the end-to-end logits bar
+    (2e-2) and the next ones within 1% of the logits' scale, with the same
+    greedy tokens.  (The ~1e-6 attention differences flip Q8 activation
+    roundings in later layers and steps, so the logits drift past 2e-2 within
+    a few steps: the reason the split is not the default.)"""
+    path = os.path.join(tmp, "mid.gguf")
+    if not os.path.exists(path):
+        gguf.write_random_llama(path, MID, seed=5)
+    prompt = np.random.default_rng(3).integers(0, MID.vocab, size=150).astype(np.int32)
+    monkeypatch.delenv("MV_ATTN_SPLIT", raising=False)
+    a = mv.LlamaModel(path, ctx_override=512, kv_page_tokens=16, kv_type=kv_type)
+    monkeypatch.setenv("MV_ATTN_SPLIT", "1")
+    b = mv.LlamaModel(path, ctx_override=512, kv_page_tokens=16, kv_type=kv_type)
+    try:
+        la, lb = a.prefill(prompt, 32).copy(), b.prefill(prompt, 32).copy()
+        assert np.array_equal(la, lb)
+        cur = int(np.argmax(la))
+        for i in range(6):
+            la, lb = a.forward(cur).copy(), b.forward(cur).copy()
+            d = float(np.max(np.abs(la - lb)))
+            assert d <= (LOGIT_TOL if i == 0 else 1e-2 * float(np.max(np.abs(la)))), (i, d)
+            assert int(np.argmax(lb)) == int(np.argmax(la))
+            cur = int(np.argmax(la))
+        assert a.position() == b.position() == 156
+    finally:
+        a.close()
+        b.close()
+
+
+MID_Q4_HEAD = dataclasses.replace(MID, output_type=gguf.Q4_0)
+
+
+@pytest.mark.parametrize("kv_type,head", [(mv.KV_F16, "q4_0"), (mv.KV_F32, "q4_0"), (mv.KV_Q8, "q4_0"),
+                                          (mv.KV_Q8_0, "q4_0"), (mv.KV_F16, "q6_k")])
+def test_forward_batch_matches_single_sequences(cuda, tmp, kv_type, head, monkeypatch):
+    """Several sequences with ragged contexts (prompts of 1 to 150 tokens)
+    decoded as one batch (mv_model_forward_batch, the set's block table)
+    against each sequence decoded alone by the same model (mv_model_forward):
+    the prefill into the set is bit-identical, and so is every step's logits
+    (the batched Q8 GEMM keeps the decode GEMV's per-row chain, the paged
+    attention the reference's order), hence the greedy tokens.  With the
+    Q6_K head (whose single-row and batched kernels sum in different fp32
+    orders; the reference sums in double) the logits agree to 1e-6 of their
+    scale and the tokens are identical."""
+    if head == "q4_0":
+        path = os.path.join(tmp, "mid_q4head.gguf")
+        if not os.path.exists(path):
+            gguf.write_random_llama(path, MID_Q4_HEAD, seed=5)
+    else:
+        path = os.path.join(tmp, "mid.gguf")
+        if not os.path.exists(path):
+            gguf.write_random_llama(path, MID, seed=5)
+    monkeypatch.delenv("MV_ATTN_SPLIT", raising=False)
+    m = mv.LlamaModel(path, ctx_override=512, kv_page_tokens=16, kv_type=kv_type)
+    rng = np.random.default_rng(21)
+    lens = [1, 17, 40, 64, 100, 150]
+    prompts = [rng.integers(0, MID.vocab, size=n).astype(np.int32) for n in lens]
+    steps = 12
+    try:
+        ref = []
+        for p in prompts:
+            m.reset()
+            pl = m.prefill(p, 32).copy()
+            toks, logs = [int(np.argmax(pl))], []
+            for _ in range(steps):
+                lg = m.forward(toks[-1]).copy()
+                logs.append(lg)
+                toks.append(int(np.argmax(lg)))
+            ref.append((pl, logs, toks))
+        S = m.open_sequences(len(prompts), 256)
+        try:
+            for i, p in enumerate(prompts):
+                assert np.array_equal(S.prefill(i, p, 32), ref[i][0]), i
+                assert S.position(i) == len(p)
+            cur = [r[2][0] for r in ref]
+            worst = 0.0
+            for k in range(steps):
+                lg = S.forward(cur).copy()
+                for i in range(len(prompts)):
+                    d = float(np.max(np.abs(lg[i] - ref[i][1][k])))
+                    worst = max(worst, d)
+                    if head == "q4_0":
+                        assert np.array_equal(lg[i], ref[i][1][k]), (k, i, d)
+                    else:
+                        assert d <= 1e-6 * float(np.max(np.abs(ref[i][1][k]))), (k, i, d)
+                cur = [int(np.argmax(lg[i])) for i in range(len(prompts))]
+                assert cur == [r[2][k + 1] for r in ref], k
+            assert [S.position(i) for i in range(len(prompts))] == [n + steps for n in lens]
+        finally:
+            S.close()
+    finally:
+        m.close()
+
+
+def test_sequence_set_errors(cuda, tmp):
+    path = os.path.join(tmp, "mid.gguf")
+    if not os.path.exists(path):
+        gguf.write_random_llama(path, MID, seed=5)
+    m = mv.LlamaModel(path, ctx_override=128, kv_page_tokens=16)
+    try:
+        with pytest.raises(mv.MemVantaError):
+            m.open_sequences(2, 4096)  # above the model's context
+        S = m.open_sequences(2, 32)
+        with pytest.raises(ValueError):
+            S.forward([1])
+        with pytest.raises(mv.MemVantaError):
+            S.forward([1, MID.vocab])  # token out of range
+        S.prefill(0, np.arange(30, dtype=np.int32), 16)
+        S.forward([1, 2])
+        S.forward([3, 4])
+        with pytest.raises(mv.MemVantaError):
+            S.forward([5, 6])  # sequence 0 is at its context
+        S.reset(0)
+        assert S.position(0) == 0 and S.position(1) == 2
+        S.forward([5, 6])
+        S.close()
+    finally:
+        m.close()
 
 
 @pytest.mark.parametrize("n,batch", [(70, 16), (22, 7), (33, 32), (1, 8), (150, 64)])

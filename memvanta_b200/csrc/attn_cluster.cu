@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(kCT) attn_decode_cluster_kernel(AttnFusedArgs 
     __shared__ float mx[kCC];
     __shared__ double dn[kCC];
     __shared__ float snew;
+    __shared__ float qv[32];  // xq: the 32 outputs of one Q8 block (its first CTA)
     cg::cluster_group cl = cg::this_cluster();
     const int r = (int)cl.block_rank(), h = blockIdx.x / kCC;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -276,8 +277,8 @@ __global__ void __launch_bounds__(kCT) attn_decode_cluster_kernel(AttnFusedArgs 
     cluster_wait();
 
     // 4. this CTA's output dimensions: one chain per dimension over t = 0..p
+    float out = 0.0f;
     if (tid < DPC) {
-        float out = 0.0f;
         auto v_at = [&](int t) -> float {
             const unsigned char* vr = vs + (size_t)t * P.vcol;
             if constexpr (KVT == 1) return half_bits_to_float(reinterpret_cast<const uint16_t*>(vr)[tid]);
@@ -300,6 +301,34 @@ __global__ void __launch_bounds__(kCT) attn_decode_cluster_kernel(AttnFusedArgs 
         if constexpr (TP) ll_put_all(a.tp, a.out_shared, (uint64_t)(a.head_off + h) * HD + d, out,
                                      tp_uepoch(a.tp, a.out_point));
         else a.out[(size_t)h * HD + d] = out;
+    }
+    // 5. one GPU, xq: the o projection's input quantised here (as the GEMV's
+    // own prologue would: d = max|v|/127, q = clamp(round(v/d))), the 32
+    // outputs of a block gathered in the first of its CTAs
+    if constexpr (!TP) {
+        if (a.xq) {
+            constexpr int CPB = 32 / DPC;  // CTAs per Q8 block
+            if (tid < DPC) cl.map_shared_rank(qv, r - r % CPB)[(r % CPB) * DPC + tid] = out;
+            cluster_arrive();
+            cluster_wait();
+            if (r % CPB == 0 && warp == 0) {
+                const float v = qv[lane];
+                const float mxa = warp_max(fabsf(v));
+                const float d = mxa > 0.0f ? mxa / 127.0f : 1.0f;
+                const float id = 1.0f / d;
+                const int q = (int)fminf(fmaxf(roundf(v * id), -127.0f), 127.0f);
+                const int qsum = warp_sum_i(q);
+                uint32_t word = (uint32_t)(q & 0xff);
+#pragma unroll
+                for (int k = 1; k < 4; ++k) word |= (uint32_t)(__shfl_down_sync(0xffffffffu, q, k) & 0xff) << (8 * k);
+                const int b = (h * HD + r * DPC) / 32, nbo = (int)(a.n_head * HD / 32);
+                uint8_t* base = static_cast<uint8_t*>(a.xq);
+                if ((lane & 3) == 0)
+                    *reinterpret_cast<uint32_t*>(base + (size_t)(lane < 16 ? b : nbo + b) * 16 + (lane & 15)) = word;
+                if (lane == 0)
+                    reinterpret_cast<float2*>(base + (size_t)nbo * 32)[b] = make_float2(d, __int_as_float(8 * qsum));
+            }
+        }
     }
 }
 

@@ -501,10 +501,23 @@ cudaError_t gemm_q4_q8_f16(const mv_weight_s& w, const uint16_t* qh, const float
     if (!batch) return cudaSuccess;
     if (w.type != 2 || ldb < gemm_tc_ldb(batch) || ldb % 4 || w.rows >= (1ull << 31) || batch >= (1ull << 31))
         return cudaErrorInvalidValue;
-    // 128-token tiles halve the per-token share of the MMA issue and the
-    // pipeline's synchronisation; below 128 tokens, 64-token tiles
-    if (batch >= 128) return launch_f16<128>(w, qh, dT, ldb, batch, y, w.rows, s, accumulate);
-    return launch_f16<64>(w, qh, dT, ldb, batch, y, w.rows, s, accumulate);
+    // Token-tile width: a tile's time is a fixed part (the converters expand
+    // the weight tile whatever its width, the MMA issue and the hand-offs)
+    // plus a part per token (measured at K = 4096: ~19.5 us + 0.42 us per
+    // token); tiles run in waves of one per SM.  Wide tiles share the fixed
+    // part among more tokens, narrow ones give narrow weights (o, down: 32
+    // row tiles) enough tiles to fill the SMs.
+    const uint64_t row_tiles = (w.rows + kM - 1) / kM, sms = (uint64_t)num_sms();
+    int best = 128;
+    double best_t = 1e30;
+    for (int nt : {128, 64, 32}) {
+        const uint64_t tiles = row_tiles * ((batch + nt - 1) / nt);
+        const double t = (double)((tiles + sms - 1) / sms) * (19.5 + 0.42 * nt);
+        if (t < best_t * 0.999) best_t = t, best = nt;
+    }
+    if (best == 128) return launch_f16<128>(w, qh, dT, ldb, batch, y, w.rows, s, accumulate);
+    if (best == 64) return launch_f16<64>(w, qh, dT, ldb, batch, y, w.rows, s, accumulate);
+    return launch_f16<32>(w, qh, dT, ldb, batch, y, w.rows, s, accumulate);
 }
 
 }  // namespace mvb

@@ -512,7 +512,7 @@ __device__ __forceinline__ uint32_t pair_bytes(int nb, int rank) {
 // Thread 0, first thing in the kernel: the two receive barriers, armed for
 // what the partner will send; then every CTA of the cluster has started and
 // sees them initialised (relaxed arrive: nothing else is published yet).
-__device__ __forceinline__ void pair_setup(PairX& px, int nb, bool rms) {
+__device__ __forceinline__ void pair_setup(PairX& px, int nb, bool rms, bool exchange = true) {
     if (threadIdx.x == 0) {
         const uint32_t b = tc::smem_u32(px.bar);
         px.abort = 0;
@@ -520,7 +520,7 @@ __device__ __forceinline__ void pair_setup(PairX& px, int nb, bool rms) {
         tc::mbar_init(b + 8, 1);
         tc::mbar_fence_init();
         if (rms) tc::mbar_expect_tx(b, 8);
-        tc::mbar_expect_tx(b + 8, pair_bytes(nb, (int)cluster_rank() ^ 1));
+        if (exchange) tc::mbar_expect_tx(b + 8, pair_bytes(nb, (int)cluster_rank() ^ 1));
     }
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
@@ -696,12 +696,21 @@ struct TileIssuer {
 };
 
 // (tile, chunk) of this CTA's items in order, advanced one item at a time.
+// A CTA takes groups of `sup` consecutive tiles (g = blockIdx.x, then
+// + gridDim.x): sup = 4 puts the 64 rows of one 32-output SiLU block in one
+// CTA, in order.
 struct TileCursor {
-    int t, c;
+    int t, c, sub, g, sup;
+    __device__ __forceinline__ TileCursor(int sup_) : t((int)blockIdx.x * sup_), c(0), sub(0), g((int)blockIdx.x),
+                                                      sup(sup_) {}
     __device__ __forceinline__ void next(int nchunk) {
         if (++c == nchunk) {
             c = 0;
-            t += gridDim.x;
+            if (++sub == sup) {
+                sub = 0;
+                g += gridDim.x;
+            }
+            t = g * sup + sub;
         }
     }
 };
@@ -715,17 +724,21 @@ __global__ void __launch_bounds__(kTThreads, 3) gemv_q4_tile_kernel(const uint4*
                                                                     const float* __restrict__ norm_w, float eps,
                                                                     int pro, int epi, float* __restrict__ y,
                                                                     const TpCtx tp, int x_point, uint64_t y_shared,
-                                                                    int y_row_off, int y_point, int res_point) {
+                                                                    int y_row_off, int y_point, int res_point,
+                                                                    void* __restrict__ yq) {
     __shared__ PairX px;
-    const bool rms = pro == (int)Q4Pro::RmsNorm;
-    pair_setup(px, nb, rms);
+    __shared__ float qbuf[32];  // yq: the SiLU outputs of one Q8 block
+    const bool rms = pro == (int)Q4Pro::RmsNorm, pre = pro == (int)Q4Pro::PreQuant;
+    pair_setup(px, nb, rms, !pre);
     const TileSmem sm = tile_smem(nb);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int tiles = (rows + kTR - 1) / kTR, nchunk = (nb + kTC - 1) / kTC;
-    const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    // yq: groups of 4 tiles (the host checks tiles % 4 == 0)
+    const int sup = yq ? 4 : 1, groups = tiles / sup;
+    const int my_tiles = blockIdx.x < groups ? ((groups - 1 - blockIdx.x) / gridDim.x + 1) * sup : 0;
     const int items = my_tiles * nchunk;
     const TileIssuer issue{qs, dsc, rows, nb, dstride, tid};
-    TileCursor nx{(int)blockIdx.x, 0};  // next item to stage
+    TileCursor nx(sup);  // next item to stage
     // weights are immutable: the first kTS-1 chunks are requested before
     // waiting on the previous kernel
     pdl_trigger();
@@ -743,10 +756,19 @@ __global__ void __launch_bounds__(kTThreads, 3) gemv_q4_tile_kernel(const uint4*
     norm_preload_slice(np, norm_w, rms, nb);
     pdl_wait();
     const Act a{sm.lo, sm.hi, sm.dc, nullptr};
-    if constexpr (LL)
+    if (pre) {
+        // the previous kernel quantised x already: copy its blocks as they are
+        const int4* src = static_cast<const int4*>(x);
+        int4* dst = sm.lo;
+        const int n16 = (int)(q8_act_bytes((uint64_t)nb * 32) / 16);
+        for (int i = tid; i < n16; i += (int)blockDim.x) dst[i] = src[i];
+        __syncthreads();
+    } else if constexpr (LL) {
         prologue_cluster(XLL{tp, static_cast<const uint2*>(x), tp_uepoch(tp, x_point), 100 + x_point}, np, norm_w,
                          eps, rms, nb, a, px);
-    else prologue_cluster(XFloat{static_cast<const float4*>(x)}, np, norm_w, eps, rms, nb, a, px);
+    } else {
+        prologue_cluster(XFloat{static_cast<const float4*>(x)}, np, norm_w, eps, rms, nb, a, px);
+    }
 
     if (warp < kTComp) {
         // compute warps: lane & 15 = row, warp and lane >> 4 pick 2 blocks
@@ -789,7 +811,7 @@ __global__ void __launch_bounds__(kTThreads, 3) gemv_q4_tile_kernel(const uint4*
         const YOut<LL> yo{y, tp, y_shared, y_row_off, rep ? tp_uepoch(tp, y_point) : 0u,
                           rep ? tp_uepoch(tp, res_point) : 0u, rep};
         float sum = 0.0f;
-        TileCursor cur{(int)blockIdx.x, 0};
+        TileCursor cur(sup);
         for (int it = 0; it < items; ++it) {
             bar_named(2, kTThreads);
             const int t = cur.t, c = cur.c;
@@ -812,8 +834,35 @@ __global__ void __launch_bounds__(kTThreads, 3) gemv_q4_tile_kernel(const uint4*
                 const int r = t * kTR + lane;
                 if (epi == (int)Q4Epi::SiluGate) {
                     const float u = __shfl_down_sync(0xffffffffu, sum, 1);
-                    if (lane < kTR && (lane & 1) == 0 && r + 1 < rows)
-                        yo.put(r / 2, (sum / (1.0f + expf_cr(-sum))) * u);
+                    const float g = (sum / (1.0f + expf_cr(-sum))) * u;
+                    if (lane < kTR && (lane & 1) == 0 && r + 1 < rows) yo.put(r / 2, g);
+                    if (yq) {
+                        // 8 outputs per tile; after the 4th tile of the group the
+                        // warp quantises their 32-element block as quant_group does
+                        if (lane < kTR && (lane & 1) == 0) qbuf[(t & 3) * 8 + lane / 2] = g;
+                        if ((t & 3) == 3) {
+                            __syncwarp();
+                            const float v = qbuf[lane];
+                            const float m = warp_max(fabsf(v));
+                            const float d = m > 0.0f ? m / 127.0f : 1.0f;
+                            const float id = 1.0f / d;
+                            const int q = (int)fminf(fmaxf(roundf(v * id), -127.0f), 127.0f);
+                            const int qsum = warp_sum_i(q);
+                            uint32_t word = (uint32_t)(q & 0xff);
+#pragma unroll
+                            for (int k = 1; k < 4; ++k)
+                                word |= (uint32_t)(__shfl_down_sync(0xffffffffu, q, k) & 0xff) << (8 * k);
+                            const int b = t >> 2, nbo = rows / 64;
+                            uint8_t* base = static_cast<uint8_t*>(yq);
+                            if ((lane & 3) == 0)
+                                *reinterpret_cast<uint32_t*>(base + (size_t)(lane < 16 ? b : nbo + b) * 16 +
+                                                             (lane & 15)) = word;
+                            if (lane == 0)
+                                reinterpret_cast<float2*>(base + (size_t)nbo * 32)[b] =
+                                    make_float2(d, __int_as_float(8 * qsum));
+                            __syncwarp();
+                        }
+                    }
                 } else if (lane < kTR && r < rows) {
                     yo.put(r, epi == (int)Q4Epi::AddTo ? yo.local(r) + sum : sum);
                 }
@@ -892,24 +941,36 @@ cudaError_t launch_tile(const GemvQ4Args& g, cudaStream_t s) {
         }
     }
     const uint64_t tiles = (w.rows + kTR - 1) / kTR;
+    const uint64_t units = g.yq ? tiles / 4 : tiles;  // yq: CTAs take groups of 4 tiles
     uint64_t cap = (uint64_t)clusters * kCl;
     const uint64_t keep = ((uint64_t)g.reserve + kCl - 1) / kCl * kCl;
     if (keep && cap > 2 * keep) cap -= keep;
-    const uint64_t grid = ((tiles < cap ? tiles : cap) + kCl - 1) / kCl * kCl;
+    const uint64_t grid = ((units < cap ? units : cap) + kCl - 1) / kCl * kCl;
     const void* x = LL ? g.x_ll : static_cast<const void*>(g.x);
     return launch_pdl_cluster(gemv_q4_tile_kernel<LL>, dim3((unsigned)grid), dim3(kTThreads), smem, s, kCl,
                               reinterpret_cast<const uint4*>(w.qs), (const unsigned short*)w.d, (int)w.rows,
                               (int)w.nb, (int)w.dstride, x, g.norm_w, g.eps, (int)g.pro, (int)g.epi, g.y,
-                              g.tp ? *g.tp : TpCtx{}, g.x_point, g.y_shared, g.y_row_off, g.y_point, g.res_point);
+                              g.tp ? *g.tp : TpCtx{}, g.x_point, g.y_shared, g.y_row_off, g.y_point, g.res_point,
+                              g.yq);
 }
 
 }  // namespace
+
+bool gemv_q4_prequant_ok(const mv_weight_s& w) {
+    return w.type == 2 && w.cols % 32 == 0 && tile_smem_bytes(w.nb) <= 110 * 1024;
+}
 
 cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s) {
     // x and norm_w are read as float4: the width must keep 8-element groups
     if (a.w->cols % 32) return cudaErrorInvalidValue;
     const bool tp = a.tp && a.tp->world > 1;
     if ((!a.y && !a.x_ll) || (a.x_ll && !tp) || (!a.x_ll && !a.x)) return cudaErrorInvalidValue;
+    // quantised input / output: one GPU, the row-tile kernel, whole SiLU blocks
+    if (a.pro == Q4Pro::PreQuant || a.yq) {
+        if (tp || !gemv_q4_prequant_ok(*a.w)) return cudaErrorInvalidValue;
+        if (a.yq && (a.epi != Q4Epi::SiluGate || a.w->rows % 64)) return cudaErrorInvalidValue;
+        return launch_tile<false>(a, s);
+    }
     if (tile_smem_bytes(a.w->nb) <= 110 * 1024) return a.x_ll ? launch_tile<true>(a, s) : launch_tile<false>(a, s);
     // Four rows per warp where the matrix has rows to spare (the chain cost
     // is shared by more rows), two otherwise so every SM has warps in flight.

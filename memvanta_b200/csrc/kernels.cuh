@@ -36,9 +36,18 @@ cudaError_t silu_quantize_q8_rows_t(const float* gu, uint64_t rows, uint64_t col
 
 // ---- gemv_q4.cu : decode GEMV over Q4_0 with Q8 activations (integer path)
 enum class Q4Pro : int {
-    Plain = 0,    // activations = x
-    RmsNorm = 1,  // activations = rmsnorm(x) * norm_w (the reference's rmsnorm)
+    Plain = 0,     // activations = x
+    RmsNorm = 1,   // activations = rmsnorm(x) * norm_w (the reference's rmsnorm)
+    PreQuant = 2,  // x points to activations already quantised (q8_act_bytes layout)
 };
+// Quantised activations of K elements as the decode GEMV keeps them in shared
+// memory, also written by the kernel before it so that the GEMV only copies
+// them: per 32-element block b, int8 q[0..15] at 16*b, q[16..31] at
+// 16*(nb + b), and (d, bits of float 8*sum q) as float2 at 32*nb + 8*b.
+__host__ __device__ inline uint64_t q8_act_bytes(uint64_t K) {
+    const uint64_t nb = K / 32;
+    return nb * 32 + (nb + 1) / 2 * 16;
+}
 enum class Q4Epi : int {
     Store = 0,     // y[r] = acc
     AddTo = 1,     // y[r] += acc          (residual stream)
@@ -69,7 +78,12 @@ struct GemvQ4Args {
     // CTA slots the launch leaves free for the kernel after it (the decode
     // attention after the q|k|v GEMV starts on them while this one runs)
     int reserve = 0;
+    // SiluGate, one GPU: also write the outputs' Q8 blocks (q8_act_bytes
+    // layout) for the next GEMV's PreQuant input
+    void* yq = nullptr;
 };
+// Whether a one-GPU GEMV of this weight takes PreQuant input / writes yq.
+bool gemv_q4_prequant_ok(const mv_weight_s& w);
 cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s);
 cudaError_t q4_block_dots(const mv_weight_s& w, const float* x, int32_t* isum, cudaStream_t s);
 
@@ -174,6 +188,9 @@ struct AttnFusedArgs {
     uint64_t out_shared = 0;
     int head_off = 0;
     int out_point = 0;
+    // one GPU: also write the output's Q8 blocks (q8_act_bytes layout) for
+    // the o projection's PreQuant input (attn_decode_cluster only)
+    void* xq = nullptr;
 };
 // ---- tp.cu (tensor parallel, protocol in tp.cuh)
 cudaError_t tp_wait(const TpCtx& tp, int point, cudaStream_t s);

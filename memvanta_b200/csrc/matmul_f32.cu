@@ -17,10 +17,11 @@ constexpr uint32_t kLoNib = 0x0F0F0F0Fu;
 // activations; Q6_K/F16 accumulate in fp32 instead of the reference's double
 // (the 5e-3 / 1e-3 tolerances hold with margin).
 //
-// Mapping: one warp per row, lane l owns elements [128*s + 4l, +4) of every
-// 128-wide step s, so a lane reads one 32-bit payload word (4 elements) and
-// one float4 of each token's activations; the token tile (T tokens x K
-// floats) sits in shared memory and every float4 read is bank-conflict-free.
+// Mapping (1 to 7 tokens): one warp per row, lane l owns elements
+// [128*s + 4l, +4) of every 128-wide step s, so a lane reads one 32-bit
+// payload word (4 elements) and one float4 of each token's activations; the
+// token tile (T tokens x K floats) sits in shared memory and every float4
+// read is bank-conflict-free.
 // =====================================================================
 
 constexpr int kFWarps = 8;
@@ -118,9 +119,119 @@ static cudaError_t launch_f32act(const mv_weight_s& w, const float* x, uint64_t 
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------
+// Batches of 8 tokens and more: a register-tiled kernel.  A CTA of 128
+// threads owns ROWS (64 or 32) rows x 32 tokens; K advances in chunks of 64
+// elements, dequantised (deq4, the same per-element values) into a row-major
+// shared tile next to the chunk's activations, so each weight element is
+// loaded and dequantised once per 32 tokens instead of once per token.  A
+// thread owns rows tid%16 + 16i (i < ROWS/16) and tokens 4*(tid/16) + j
+// (j < 4) and reads float4 runs of 4 k from both tiles (the 16 rows a warp
+// reads are consecutive: no bank conflicts); the next chunk's weights and
+// activations are loaded into registers while the current chunk is
+// multiplied.  Each output is one fp32 FMA chain over k in order.
+constexpr int kTTok = 32, kTK = 64, kTThreads = 128;
+constexpr int kTPad = kTK + 4;  // floats per tile row (16-byte aligned, rows 4 banks apart)
+
+template <int TYPE, int ROWS>
+__global__ void __launch_bounds__(kTThreads) matmul_f32act_tiled_kernel(mv_weight_s w, const float* __restrict__ x,
+                                                                        int batch, float* __restrict__ y) {
+    constexpr int RT = ROWS / 16;                       // rows per thread
+    constexpr int WG = ROWS * kTK / 4 / kTThreads;      // weight groups of 4 a thread stages
+    constexpr int XG = kTTok * kTK / 4 / kTThreads;     // activation float4 a thread stages
+    __shared__ __align__(16) float ws[ROWS][kTPad];
+    __shared__ __align__(16) float xs[kTTok][kTPad];
+    const int K = (int)w.cols, rows = (int)w.rows, tid = threadIdx.x;
+    const int r0 = blockIdx.x * ROWS, t0 = blockIdx.y * kTTok;
+    const int tr = tid & 15, tt = (tid >> 4) * 4;
+    float wv[WG][4], xv[XG][4];
+    auto load = [&](int k0) {
+#pragma unroll
+        for (int i = 0; i < WG; ++i) {
+            const int g = tid + i * kTThreads, row = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
+            const int r = r0 + row, e0 = k0 + kk;
+            if (r < rows && e0 < K) deq4<TYPE>(w, (uint64_t)r, (uint64_t)e0, wv[i]);
+            else wv[i][0] = wv[i][1] = wv[i][2] = wv[i][3] = 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < XG; ++i) {
+            const int g = tid + i * kTThreads, tok = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
+            const int t = t0 + tok, e0 = k0 + kk;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t < batch && e0 < K) v = *reinterpret_cast<const float4*>(x + (size_t)t * K + e0);
+            xv[i][0] = v.x, xv[i][1] = v.y, xv[i][2] = v.z, xv[i][3] = v.w;
+        }
+    };
+    auto store = [&]() {
+#pragma unroll
+        for (int i = 0; i < WG; ++i) {
+            const int g = tid + i * kTThreads, row = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
+            *reinterpret_cast<float4*>(&ws[row][kk]) = make_float4(wv[i][0], wv[i][1], wv[i][2], wv[i][3]);
+        }
+#pragma unroll
+        for (int i = 0; i < XG; ++i) {
+            const int g = tid + i * kTThreads, tok = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
+            *reinterpret_cast<float4*>(&xs[tok][kk]) = make_float4(xv[i][0], xv[i][1], xv[i][2], xv[i][3]);
+        }
+    };
+    float acc[RT][4];
+#pragma unroll
+    for (int i = 0; i < RT; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    load(0);
+    for (int k0 = 0; k0 < K; k0 += kTK) {
+        __syncthreads();  // the previous chunk's tiles are no longer read
+        store();
+        __syncthreads();
+        if (k0 + kTK < K) load(k0 + kTK);  // in flight during this chunk's FMAs
+#pragma unroll 4
+        for (int k = 0; k < kTK; k += 4) {
+            float4 a[RT], b[4];
+#pragma unroll
+            for (int i = 0; i < RT; ++i) a[i] = *reinterpret_cast<const float4*>(&ws[tr + 16 * i][k]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(&xs[tt + j][k]);
+#pragma unroll
+            for (int i = 0; i < RT; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    acc[i][j] = fmaf(a[i].x, b[j].x, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].y, b[j].y, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].z, b[j].z, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].w, b[j].w, acc[i][j]);
+                }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int t = t0 + tt + j;
+        if (t >= batch) continue;
+#pragma unroll
+        for (int i = 0; i < RT; ++i) {
+            const int r = r0 + tr + 16 * i;
+            if (r < rows) y[(size_t)t * rows + r] = acc[i][j];
+        }
+    }
+}
+
+template <int TYPE>
+static cudaError_t launch_f32act_tiled(const mv_weight_s& w, const float* x, uint64_t batch, float* y,
+                                       cudaStream_t s) {
+    // 32-row tiles where 64-row tiles would leave SMs without two CTAs
+    const uint64_t ttiles = (batch + kTTok - 1) / kTTok;
+    const bool narrow = (w.rows + 63) / 64 * ttiles < 2 * (uint64_t)num_sms();
+    const unsigned rows_per = narrow ? 32 : 64;
+    const dim3 grid((unsigned)((w.rows + rows_per - 1) / rows_per), (unsigned)ttiles);
+    if (narrow) matmul_f32act_tiled_kernel<TYPE, 32><<<grid, kTThreads, 0, s>>>(w, x, (int)batch, y);
+    else matmul_f32act_tiled_kernel<TYPE, 64><<<grid, kTThreads, 0, s>>>(w, x, (int)batch, y);
+    return cudaGetLastError();
+}
+
 template <int TYPE>
 static cudaError_t dispatch_t(const mv_weight_s& w, const float* x, uint64_t batch, float* y, cudaStream_t s) {
     const uint64_t budget = 200 * 1024 / 4;  // floats of activation tile that fit in shared memory
+    if (batch >= 8) return launch_f32act_tiled<TYPE>(w, x, batch, y, s);
     if (batch == 1) return launch_f32act<TYPE, 1>(w, x, batch, y, s);
     if (batch == 2 || 4 * w.cols > budget) {
         if (2 * w.cols > budget) return launch_f32act<TYPE, 1>(w, x, batch, y, s);

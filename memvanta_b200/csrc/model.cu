@@ -315,6 +315,11 @@ struct mv_model_s {
     // head (attn_cluster.cu) where its staging fits; MV_ATTN_CLUSTER=0 keeps
     // the one-CTA-per-head kernel (attention.cu)
     bool attn_cluster = false;
+    // one GPU, MV_DECODE_PREQUANT: the o and down GEMVs take their inputs
+    // already quantised by the kernels before them (the cluster attention,
+    // the gate|up GEMV) in these buffers (q8_act_bytes layout); else nullptr
+    uint8_t* attq = nullptr;
+    uint8_t* ffq = nullptr;
     // one GPU: every layer of a decode step in one persistent kernel
     // (decode_mk.cu), with MV_DECODE_PERSISTENT=1 where supported
     bool mk = false;
@@ -616,12 +621,19 @@ void ensure_prefill(mv_model_s* m, uint64_t B) {
 
 // x_out = W x_in for one weight of any type, with the decode path's fused
 // prologue/epilogue where the weight is Q4_0.
+// xq: the input already quantised (Q4_0 weights only); yq: SiluGate also
+// writes its outputs quantised.
 void project_decode(mv_model_s* m, mv_weight_s* w, const float* x, const float* norm_w, float* y, mvb::Q4Epi epi,
-                    int reserve = 0) {
+                    int reserve = 0, void* yq = nullptr, const void* xq = nullptr) {
     cudaStream_t s = m->stream;
     if (w->type == 2) {
         mvb::GemvQ4Args a{w, x, norm_w, m->eps, y, norm_w ? mvb::Q4Pro::RmsNorm : mvb::Q4Pro::Plain, epi};
+        if (xq) {
+            a.x = static_cast<const float*>(xq);
+            a.pro = mvb::Q4Pro::PreQuant;
+        }
         a.reserve = reserve;
+        a.yq = yq;
         ck(mvb::gemv_q4(a, s), "gemv_q4");
         return;
     }
@@ -760,6 +772,7 @@ void launch_decode(mv_model_s* m, bool with_logits) {
                 fa.head_off = (int)(r * m->nh);
                 fa.out_point = pt_att(l);
             }
+            fa.xq = m->attq;  // set only with the cluster kernel on one GPU
             ck(m->attn_split     ? mvb::attn_decode_fused_split(fa, s)
                : m->attn_cluster ? mvb::attn_decode_cluster(fa, s)
                                  : mvb::attn_decode_fused(fa, s),
@@ -779,9 +792,9 @@ void launch_decode(mv_model_s* m, bool with_logits) {
             gemv_tp(m, L.down, m->off_ff, pt_gu(l), nullptr, mvb::Q4Epi::AddTo, nullptr, m->off_x, r * m->Dl,
                     pt_down(l), pt_o(l));
         } else {
-            project_decode(m, L.o, m->att, nullptr, m->x, mvb::Q4Epi::AddTo);
-            project_decode(m, L.gu, m->x, L.ffn_norm, m->ff, mvb::Q4Epi::SiluGate);
-            project_decode(m, L.down, m->ff, nullptr, m->x, mvb::Q4Epi::AddTo);
+            project_decode(m, L.o, m->att, nullptr, m->x, mvb::Q4Epi::AddTo, 0, nullptr, m->attq);
+            project_decode(m, L.gu, m->x, L.ffn_norm, m->ff, mvb::Q4Epi::SiluGate, 0, m->ffq);
+            project_decode(m, L.down, m->ff, nullptr, m->x, mvb::Q4Epi::AddTo, 0, nullptr, m->ffq);
         }
     }
     // every rank's down rows, as floats, before the head (and before the next
@@ -1104,6 +1117,20 @@ void load_model(mv_model_s* m, const char* path, uint64_t ctx, uint64_t page, in
         const char* cenv = std::getenv("MV_ATTN_CLUSTER");
         const uint64_t cneed = fused ? mvb::attn_cluster_smem_bytes(m->hd, m->n_ctx, m->n_pages, m->kv_type) : 0;
         m->attn_cluster = cneed && cneed <= 110 * 1024 && !(cenv && std::string(cenv) == "0");
+        // quantised hand-offs, opt-in: MV_DECODE_PREQUANT=1 (both), o, ff.  Measured
+        // slower on the 7B step (683 tok/s without, 679 o only, 671 ff only, 661
+        // both): the cluster barrier the attention adds and the 4-tile groups the
+        // gate|up GEMV needs cost more than the copied prologue saves
+        const char* qenv = std::getenv("MV_DECODE_PREQUANT");
+        const std::string qv = qenv ? qenv : "0";
+        const bool pq = world == 1 && qv != "0";
+        bool o_ok = pq && qv != "ff" && fused && m->attn_cluster && !m->attn_split, f_ok = pq && qv != "o";
+        for (const auto& L : m->layers) {
+            o_ok = o_ok && mvb::gemv_q4_prequant_ok(*L.o);
+            f_ok = f_ok && mvb::gemv_q4_prequant_ok(*L.gu) && mvb::gemv_q4_prequant_ok(*L.down) && L.gu->rows % 64 == 0;
+        }
+        if (o_ok) m->attq = dalloc<uint8_t>(m, mvb::q8_act_bytes(m->n_embd));
+        if (f_ok) m->ffq = dalloc<uint8_t>(m, mvb::q8_act_bytes(m->n_ff));
     }
     if (world == 1) setup_persistent_decode(m);
     if (world == 1) ready_decode(m);  // tensor parallel: once the peers are connected

@@ -206,6 +206,26 @@ def test_tc_gemm_tile_widths_bit_exact(cuda, oracle, tile, cols):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("tile", ["nt128", "nt64", "nt32"])
+def test_f16_gemm_tile_widths_bit_exact(cuda, oracle, tile):
+    """Every token-tile width of the fp16 tensor-core GEMM (64 tokens and
+    more), bit-exact against the FORCE_Q8 chain: the launcher's wave model
+    takes 128-token tiles when one tile per SM already fills the machine
+    (148 row tiles, 128 tokens), 64 at 64 tokens, and 32 for a narrow weight
+    (3 row tiles at 100 tokens, ragged rows and tokens)."""
+    sms = _sms()
+    rows, batch, cols = {"nt128": (128 * sms - 37, 128, 512), "nt64": (128 * sms - 5, 64, 512),
+                         "nt32": (300, 100, 1056)}[tile]
+    rng = np.random.default_rng(rows + batch)
+    w = gguf.gen_q4_0(rows, cols, rng)
+    X = rng.standard_normal((batch, cols)).astype(np.float32)
+    W = upload(w, gguf.Q4_0, rows, cols)
+    got = run_gemm(W, X, cuda, mv.ACT_Q8)
+    mv.stream_status()
+    want = oracle.matmul_batch_v06(gguf.Q4_0, w, rows, cols, X, force_q8=True)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 @pytest.mark.parametrize("batch", [20, 80])
 def test_tc_gemm_edge_values(cuda, oracle, batch):
     """Extreme blocks: nibbles all 0 or all 15, activations of one sign at the

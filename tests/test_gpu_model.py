@@ -164,6 +164,36 @@ def test_cluster_attention_matches_one_cta_per_head(cuda, tmp, kv_type, monkeypa
 
 
 @pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_F32, mv.KV_Q8_0])
+def test_prequantised_handoffs_match_gemv_prologues(cuda, tmp, kv_type, monkeypatch):
+    """One GPU, MV_DECODE_PREQUANT=1: the attention writes the o projection's
+    Q8 input and the gate|up GEMV the down projection's, instead of each GEMV
+    quantising its fp32 input itself (the default): the same quantiser, so
+    the logits are identical at every step (the Q8_0 cache runs the
+    attention without a quantised output, so only down's input moves)."""
+    path = os.path.join(tmp, "mid.gguf")
+    if not os.path.exists(path):
+        gguf.write_random_llama(path, MID, seed=5)
+    monkeypatch.delenv("MV_ATTN_SPLIT", raising=False)
+    monkeypatch.setenv("MV_DECODE_PREQUANT", "1")
+    a = mv.LlamaModel(path, ctx_override=512, kv_page_tokens=16, kv_type=kv_type)
+    monkeypatch.delenv("MV_DECODE_PREQUANT")
+    b = mv.LlamaModel(path, ctx_override=512, kv_page_tokens=16, kv_type=kv_type)
+    try:
+        prompt = np.random.default_rng(9).integers(0, MID.vocab, size=40).astype(np.int32)
+        assert np.array_equal(a.prefill(prompt, 16), b.prefill(prompt, 16))
+        cur = 11
+        for i in range(120):
+            la, lb = a.forward(cur).copy(), b.forward(cur).copy()
+            assert np.array_equal(la, lb), (i, float(np.max(np.abs(la - lb))))
+            cur = int(np.argmax(la))
+        t0 = int(np.argmax(la))
+        assert list(a.generate_greedy(t0, 16)) == list(b.generate_greedy(t0, 16))
+    finally:
+        a.close()
+        b.close()
+
+
+@pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_F32, mv.KV_Q8_0])
 def test_split_attention_decode_close_to_exact(cuda, tmp, kv_type, monkeypatch):
     """Decode attention split over the context (MV_ATTN_SPLIT=1; the fused
     RoPE + append + attention kernel for F16/F32, the multi-sequence split
@@ -212,7 +242,7 @@ def test_forward_batch_matches_single_sequences(cuda, tmp, kv_type, head, monkey
     (the batched Q8 GEMM keeps the decode GEMV's per-row chain, the paged
     attention the reference's order), hence the greedy tokens.  With the
     Q6_K head (whose single-row and batched kernels sum in different fp32
-    orders; the reference sums in double) the logits agree to 1e-6 of their
+    orders; the reference sums in double) the logits agree to 1e-5 of their
     scale and the tokens are identical."""
     if head == "q4_0":
         path = os.path.join(tmp, "mid_q4head.gguf")
@@ -254,7 +284,7 @@ def test_forward_batch_matches_single_sequences(cuda, tmp, kv_type, head, monkey
                     if head == "q4_0":
                         assert np.array_equal(lg[i], ref[i][1][k]), (k, i, d)
                     else:
-                        assert d <= 1e-6 * float(np.max(np.abs(ref[i][1][k]))), (k, i, d)
+                        assert d <= 1e-5 * float(np.max(np.abs(ref[i][1][k]))), (k, i, d)
                 cur = [int(np.argmax(lg[i])) for i in range(len(prompts))]
                 assert cur == [r[2][k + 1] for r in ref], k
             assert [S.position(i) for i in range(len(prompts))] == [n + steps for n in lens]

@@ -24,8 +24,10 @@
 //
 // Memory: each warp streams its tokens through its own ring of shared-memory
 // stages (16 tokens' key and value head slices per stage, 16-byte cp.async
-// copies spread over the lanes, two stages in flight while one is used), so
-// no warp waits for another before the merge.  Scores: two lanes per token,
+// copies spread over the lanes, one stage in flight while one is used), so
+// no warp waits for another before the merge.  Two stages keep a CTA at
+// ~70 KB (F16, hd 128): three CTAs share an SM, which measured faster than
+// deeper rings at two CTAs per SM (config 4 F16: 96.5 against 121.8 us).  Scores: two lanes per token,
 // each over half of the head's dimensions; values: lane = hd/32 consecutive
 // dimensions.  One CTA per (sequence, head), 4 warps.
 #include <cooperative_groups.h>
@@ -246,7 +248,7 @@ struct WarpSoftmax {
 };
 
 template <int HD, int KVT>
-using SplitPlanOf = SplitPlan<HD, KVT, KVT == 0 ? 2 : 3>;
+using SplitPlanOf = SplitPlan<HD, KVT, 2>;  // two stages: three CTAs fit an SM
 
 template <int HD, int KVT>
 __global__ void __launch_bounds__(kSW * 32) attn_split_kernel(AttnArgs a) {

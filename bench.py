@@ -340,7 +340,7 @@ def run_llama7b_ours(args, world, rank, local):
     t_load = time.perf_counter()
     if world > 1:  # one model over all ranks (tensor parallel, exact)
         m = mv.LlamaModel.tensor_parallel(path, device=local, ctx_override=L7_CTX, kv_page_tokens=16,
-                                          kv_type=mv.KV_F16, prefill_batch=L7_BATCH)
+                                          kv_type=mv.KV_F16, prefill_batch=L7_PP)  # room for merged batches
     else:
         m = mv.LlamaModel(path, ctx_override=L7_CTX, kv_page_tokens=16, kv_type=mv.KV_F16)
     load_s = time.perf_counter() - t_load  # GGUF parse + upload pipeline (+ peer connect at N > 1)

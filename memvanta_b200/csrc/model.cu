@@ -1226,7 +1226,7 @@ struct AltSet {
     }
 };
 
-// Tokens one merged prefill batch holds at most (single GPU).
+// Tokens one merged prefill batch holds at most.
 constexpr uint64_t kMergedPrefill = 512;
 
 // One decode step of every sequence of a set (mv_seqs_s): row i of the batch
@@ -1550,14 +1550,16 @@ void prefill_impl(mv_model_t m, const int32_t* tokens, uint64_t n, uint64_t batc
         // GEMM chains, the chunk's K/V appended before its causal attention --
         // except that a 1-token chunk takes the fp32-activation path
         // (tensor_matmul_batch_v06 routes batch < 2 to tensor_matmul_batch).
-        // So on one GPU the chunks of 2 or more tokens run together as one
-        // batch of up to kMergedPrefill tokens (every weight read once per
-        // layer, not once per chunk); a last chunk of 1 token (n % batch == 1)
-        // runs on its own.  Outputs are identical to chunk-by-chunk execution.
+        // So the chunks of 2 or more tokens run together as one batch of up to
+        // kMergedPrefill tokens (every weight read once per layer, not once per
+        // chunk; tensor parallel: up to the prefill rows the shared buffers
+        // hold); a last chunk of 1 token (n % batch == 1) runs on its own.
+        // Outputs are identical to chunk-by-chunk execution.
         const char* env = std::getenv("MV_PREFILL_MERGE");
-        const bool merge = m->tp_world == 1 && B0 >= 2 && !(env && std::string(env) == "0");
+        const uint64_t cap = m->tp_world > 1 ? std::min<uint64_t>(kMergedPrefill, m->tp_bmax) : kMergedPrefill;
+        const bool merge = B0 >= 2 && (m->tp_world == 1 || cap > B0) && !(env && std::string(env) == "0");
         const uint64_t tail1 = (B0 >= 2 && n % B0 == 1) ? 1 : 0;
-        const uint64_t B = merge ? std::min<uint64_t>(std::max(B0, kMergedPrefill), n - tail1 ? n - tail1 : 1) : B0;
+        const uint64_t B = merge ? std::min<uint64_t>(std::max(B0, cap), n - tail1 ? n - tail1 : 1) : B0;
         ck(cudaStreamSynchronize(m->stream), "sync");
         ensure_prefill(m, std::min(B, n));
         stage_prefill_inputs(m, tokens, n);

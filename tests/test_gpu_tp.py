@@ -46,7 +46,7 @@ def _free_port() -> int:
 def _plan(m, kv_type):
     """The calls every arm makes, in order; returns the results."""
     out = {}
-    out["prefill"] = m.prefill(PROMPT, batch_size=32).copy()  # chunks 32, 32, 11 (tensor cores)
+    out["prefill"] = m.prefill(PROMPT, batch_size=32).copy()  # chunks 32, 32, 11 merged into one batch of 75
     cur = int(np.argmax(out["prefill"]))
     dec = []
     for _ in range(N_DECODE):
@@ -83,7 +83,7 @@ def _rank(rank, world, port, path, kv_type, outdir, mode):
 
         dist.init_process_group("gloo", rank=rank, world_size=world)
         m = mv.LlamaModel.tensor_parallel(path, device=rank, ctx_override=256, kv_page_tokens=16, kv_type=kv_type,
-                                          prefill_batch=32)
+                                          prefill_batch=128)  # the 75-token prompt merges into one fp16-GEMM batch
         if mode == "parity":
             np.savez(os.path.join(outdir, f"rank{rank}.npz"), **_plan(m, kv_type))
         else:  # failure: rank 1 skips one step; rank 0's step must give up, not hang

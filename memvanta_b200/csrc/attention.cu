@@ -118,13 +118,14 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Tokens per K tile: one per thread, at most 128, and two tiles of padded
-// rows within 128 KB.
+// Tokens per K tile: one per thread, at most 64, and two tiles of padded
+// rows within 128 KB (64-token tiles keep a CTA near 38 KB for hd 128 F16,
+// five per SM: these kernels are latency-bound, resident warps count).
 __host__ __device__ inline int attn_ktile(uint64_t hd, int kv_type) {
     const uint64_t esize = kv_type == 0 ? 4 : kv_type == 1 ? 2 : 1;
     uint64_t kt = 65536 / (hd * esize + 16);
     if (kt > hd) kt = hd;
-    if (kt > 128) kt = 128;
+    if (kt > 64) kt = 64;
     return (int)(kt / 32 * 32);
 }
 
@@ -965,8 +966,14 @@ cudaError_t launch_group_hd(const AttnArgs& a, size_t smem, cudaStream_t s) {
 cudaError_t paged_attn_prefill(const AttnArgs& a, cudaStream_t s) {
     if (!a.n_seq) return cudaSuccess;
     if (a.n_head % a.n_head_kv) return cudaErrorInvalidValue;
-    // groups of 4 when that still gives every SM a CTA, else pairs
-    const int qg = (a.n_seq + 3) / 4 * a.n_head >= (uint64_t)num_sms() ? 4 : a.n_seq >= 2 ? 2 : 1;
+    // groups of 8 when that still gives every SM two CTAs (merged prefill
+    // batches: twice the reuse of every staged K/V tile, eight independent
+    // chains per thread), of 4 when it gives every SM a CTA, else pairs
+    const uint64_t sms = (uint64_t)num_sms();
+    const int qg = (a.n_seq + 7) / 8 * a.n_head >= 2 * sms ? 8
+                   : (a.n_seq + 3) / 4 * a.n_head >= sms   ? 4
+                   : a.n_seq >= 2                          ? 2
+                                                           : 1;
     const size_t smem = qg > 1 ? attn_group_plan(a.hd, a.max_ctx ? a.max_ctx : 1, a.max_pages, a.kv_type, qg).total : 0;
     if (qg == 1 || smem > 200 * 1024) {
         cudaError_t e = paged_attn_decode(a, s);
@@ -974,7 +981,8 @@ cudaError_t paged_attn_prefill(const AttnArgs& a, cudaStream_t s) {
         return e;
     }
     if (a.xq && a.xq_ldb < a.n_seq) return cudaErrorInvalidValue;
-    return qg == 4 ? launch_group_hd<4>(a, smem, s) : launch_group_hd<2>(a, smem, s);
+    return qg == 8 ? launch_group_hd<8>(a, smem, s) : qg == 4 ? launch_group_hd<4>(a, smem, s)
+                                                     : launch_group_hd<2>(a, smem, s);
 }
 
 }  // namespace mvb

@@ -46,32 +46,35 @@ namespace mvb {
 // RoPE (half-split, the reference's GCC roundings: fma(x0,c,-(x1*s)) and
 // fma(x0,s,x1*c)) on the q and k parts of each qkv row, and the k and v parts
 // into the paged cache (F32 copy / F16 with the reference rounding / Q8_0 per
-// 32-element block).  Grid (rows, n_head + 2*n_head_kv): one CTA per q head
-// (rotate), k head (rotate + store) and v head (store).  ctx_out (optional)
-// receives pos+1 for the attention that follows.
+// 32-element block).  Grid (rows, ceil((n_head + 2*n_head_kv) / upc)): each
+// CTA takes upc units -- a q head (rotate), k head (rotate + store) or v head
+// (store).  ctx_out (optional) receives pos+1 for the attention that follows.
 __global__ void rope_append_heads_kernel(float* __restrict__ qkv, int ld, int n_head, int n_head_kv, int hd,
                                          const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                          const int32_t* __restrict__ pos, int kv_type, const int32_t* __restrict__ table, int table_ld,
                                          int page, uint8_t* __restrict__ k_pages, uint8_t* __restrict__ v_pages,
                                          float* __restrict__ k_scales, float* __restrict__ v_scales,
-                                         int32_t* __restrict__ ctx_out) {
-    const int r = blockIdx.x, unit = blockIdx.y, half = hd / 2, KV = n_head_kv * hd;
+                                         int32_t* __restrict__ ctx_out, int upc) {
+    // upc units per CTA, blockDim.x / upc threads each
+    const int T = (int)blockDim.x / upc, sub = (int)threadIdx.x / T, tt = (int)threadIdx.x % T;
+    const int r = blockIdx.x, unit = (int)blockIdx.y * upc + sub, half = hd / 2, KV = n_head_kv * hd;
+    const bool valid = unit < n_head + 2 * n_head_kv;
     pdl_trigger();
     pdl_wait();
     float* row = qkv + (size_t)r * ld;
     const int p = pos[r];
     float* b = row + (size_t)unit * hd;  // q heads, then k heads, then v heads
-    if (unit < n_head + n_head_kv) {
+    if (valid && unit < n_head + n_head_kv) {
         const float* co = cos_t + (size_t)p * half;
         const float* si = sin_t + (size_t)p * half;
-        for (int j = threadIdx.x; j < half; j += blockDim.x) {
+        for (int j = tt; j < half; j += T) {
             const float x0 = b[j], x1 = b[j + half], c = co[j], s = si[j];
             b[j] = __fmaf_rn(x0, c, -__fmul_rn(x1, s));
             b[j + half] = __fmaf_rn(x0, s, __fmul_rn(x1, c));
         }
     }
-    if (unit >= n_head) {
-        __syncthreads();
+    __syncthreads();
+    if (valid && unit >= n_head) {
         const bool is_v = unit >= n_head + n_head_kv;
         const int head = unit - n_head - (is_v ? n_head_kv : 0);
         const size_t slot = (size_t)table[(size_t)r * table_ld + p / page] * page + p % page;
@@ -79,22 +82,22 @@ __global__ void rope_append_heads_kernel(float* __restrict__ qkv, int ld, int n_
         const size_t base = slot * KV + (size_t)head * hd;
         if (kv_type == 0) {
             float* dst = reinterpret_cast<float*>(pages) + base;
-            for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = b[i];
+            for (int i = tt; i < hd; i += T) dst[i] = b[i];
         } else if (kv_type == 1) {
             uint16_t* dst = reinterpret_cast<uint16_t*>(pages) + base;
-            for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = f32_to_f16_ref(b[i]);
-        } else {  // Q8_0: warp per 32-element block
+            for (int i = tt; i < hd; i += T) dst[i] = f32_to_f16_ref(b[i]);
+        } else {  // Q8_0: warp per 32-element block (T is a multiple of 32)
             float* scales = is_v ? v_scales : k_scales;
             int8_t* dst = reinterpret_cast<int8_t*>(pages) + base;
-            const int lane = threadIdx.x & 31;
-            for (int blk = threadIdx.x >> 5; blk < hd / 32; blk += blockDim.x >> 5) {
+            const int lane = tt & 31;
+            for (int blk = tt >> 5; blk < hd / 32; blk += T >> 5) {
                 float dd;
                 dst[blk * 32 + lane] = (int8_t)quant_q8_lane(b[blk * 32 + lane], dd);
                 if (lane == 0) scales[slot * (KV / 32) + (size_t)head * (hd / 32) + blk] = dd;
             }
         }
     }
-    if (ctx_out && unit == 0 && threadIdx.x == 0) ctx_out[r] = p + 1;
+    if (ctx_out && unit == 0 && tt == 0) ctx_out[r] = p + 1;
 }
 
 // The MV_KV_Q8 cache keeps one scale per token over all kv_dim elements, so
@@ -672,13 +675,15 @@ void rope_append(mv_model_s* m, const mvb::Layer& L, float* qkv, uint64_t rows, 
                             (const float*)m->rope_sin, pos, m->kv_type, table, table_ld, (int)m->page,
                             L.k_pages, L.v_pages, L.k_scales, L.v_scales, ctx_out);
     } else {
-        const int threads = m->kv_type == MV_KV_Q8_0 ? (int)std::max<uint64_t>(64, m->hd) : (int)(m->hd / 2);
+        // four heads per CTA: a prefill batch has rows x (heads + 2 kv heads) units
+        const int T = m->kv_type == MV_KV_Q8_0 ? (int)std::max<uint64_t>(64, m->hd) : (int)(m->hd / 2);
+        const int upc = 4, units = (int)(m->nh + 2 * m->nkv);
         e = mvb::launch_opt(!plain, mvb::rope_append_heads_kernel,
-                            dim3((unsigned)rows, (unsigned)(m->nh + 2 * m->nkv)), dim3(threads), 0,
+                            dim3((unsigned)rows, (unsigned)((units + upc - 1) / upc)), dim3(T * upc), 0,
                             m->stream, qkv, (int)QKVW, (int)m->nh, (int)m->nkv, (int)m->hd,
                             (const float*)m->rope_cos, (const float*)m->rope_sin, pos, m->kv_type,
                             table, table_ld, (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales,
-                            ctx_out);
+                            ctx_out, upc);
     }
     ck(e, "rope_append");
 }

@@ -190,7 +190,7 @@ def test_config4_ragged_paged_attention(cuda, oracle, kv_type):
 
 @pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_Q8, mv.KV_Q8_0, mv.KV_F32])
 @pytest.mark.parametrize("n_q,n_head,n_head_kv,hd", [(32, 32, 32, 128), (30, 32, 8, 128), (64, 32, 4, 64),
-                                                     (16, 16, 2, 256)])
+                                                     (16, 16, 2, 256), (83, 32, 8, 128)])
 def test_prefill_attention_groups(cuda, oracle, kv_type, n_q, n_head, n_head_kv, hd):
     """A prefill chunk: n_q causal query rows of one sequence (row i sees
     start + i + 1 tokens) over scattered 16-token pages.  The grouped kernel

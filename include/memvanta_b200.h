@@ -339,7 +339,8 @@ MV_API int mv_model_forward_batch(mv_model_t m, mv_seqs_t s, const int32_t* toke
  * each kernel stores its slice into every rank's copy over peer memory.
  * Needs Q4_0 layer weights, heads / kv heads / n_embd / n_ff / vocab divisible
  * by world, and a KV type other than MV_KV_Q8.  prefill_batch bounds the
- * `batch` of mv_model_prefill (0 -> 64).  Protocol:
+ * `batch` of mv_model_prefill (0 -> 64) and the batches a call's chunks
+ * merge into (up to 512 tokens).  Protocol:
  *   mv_model_open_tp on every rank; mv_model_tp_handle on every rank; gather
  *   the world handles (MV_TP_HANDLE_BYTES each, rank order) on every rank by
  *   any host channel; mv_model_tp_connect on every rank at the same time.

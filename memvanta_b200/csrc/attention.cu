@@ -616,7 +616,9 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
             if (s0 + i < (int)a.n_seq) {  // warp-uniform
                 float dd;
                 const int v = quant_q8_lane(out[i], dd);
-                a.xq[(size_t)(s0 + i) * D + (size_t)h * HD + tid] = (int8_t)v;
+                const size_t at = (size_t)(s0 + i) * D + (size_t)h * HD + tid;
+                if (a.xq_f16) reinterpret_cast<uint16_t*>(a.xq)[at] = __half_as_ushort(__int2half_rn(v));
+                else a.xq[at] = (int8_t)v;
                 const int sum = warp_sum_i(v);
                 if (lane == 0) {
                     a.xdT[blk * ldb + s0 + i] = dd;
@@ -977,7 +979,9 @@ cudaError_t paged_attn_prefill(const AttnArgs& a, cudaStream_t s) {
     const size_t smem = qg > 1 ? attn_group_plan(a.hd, a.max_ctx ? a.max_ctx : 1, a.max_pages, a.kv_type, qg).total : 0;
     if (qg == 1 || smem > 200 * 1024) {
         cudaError_t e = paged_attn_decode(a, s);
-        if (e == cudaSuccess && a.xq) e = quantize_q8_rows_t(a.out, a.n_seq, a.n_head * a.hd, a.xq, a.xdT, a.xq_ldb, s);
+        if (e == cudaSuccess && a.xq)
+            e = quantize_q8_rows_t(a.out, a.n_seq, a.n_head * a.hd, a.xq, a.xdT, a.xq_ldb, s,
+                                   a.xq_f16 ? reinterpret_cast<uint16_t*>(a.xq) : nullptr);
         return e;
     }
     if (a.xq && a.xq_ldb < a.n_seq) return cudaErrorInvalidValue;

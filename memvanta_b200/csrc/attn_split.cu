@@ -1,5 +1,7 @@
-// attn_split.cu -- one-query paged attention for many sequences (BASELINE
-// config 4: ragged contexts, scattered pages) split over the context.
+// attn_split.cu -- one-query paged attention split over the context: for
+// many sequences (ragged contexts, scattered pages;
+// attn_split_kernel) and, opt-in, for the model's decode step with RoPE and
+// the KV append fused in (attn_fused_split_kernel, MV_ATTN_SPLIT=1).
 //
 // The reference's decode loop (src/llama_model.cpp:256 over
 // PagedKVCache::dot_key / add_value, :23-55) walks one head's tokens in

@@ -156,6 +156,7 @@ struct AttnArgs {
     int8_t* xq = nullptr;
     float* xdT = nullptr;
     uint64_t xq_ldb = 0;
+    bool xq_f16 = false;  // xq holds fp16 values of the Q8 integers (the fp16 GEMM's input)
 };
 uint64_t attn_smem_bytes(uint64_t hd, uint64_t max_ctx, uint64_t max_pages, int kv_type);
 cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s);

@@ -121,7 +121,7 @@ static cudaError_t launch_f32act(const mv_weight_s& w, const float* x, uint64_t 
 
 // ---------------------------------------------------------------------
 // Batches of 8 tokens and more: a register-tiled kernel.  A CTA of 128
-// threads owns ROWS (64 or 32) rows x 32 tokens; K advances in chunks of 64
+// threads owns ROWS (64, 32 or 16) rows x 32 tokens; K advances in chunks of 64
 // elements, dequantised (deq4, the same per-element values) into a row-major
 // shared tile next to the chunk's activations, so each weight element is
 // loaded and dequantised once per 32 tokens instead of once per token.  A
@@ -218,13 +218,14 @@ __global__ void __launch_bounds__(kTThreads) matmul_f32act_tiled_kernel(mv_weigh
 template <int TYPE>
 static cudaError_t launch_f32act_tiled(const mv_weight_s& w, const float* x, uint64_t batch, float* y,
                                        cudaStream_t s) {
-    // 32-row tiles where 64-row tiles would leave SMs without two CTAs
-    const uint64_t ttiles = (batch + kTTok - 1) / kTTok;
-    const bool narrow = (w.rows + 63) / 64 * ttiles < 2 * (uint64_t)num_sms();
-    const unsigned rows_per = narrow ? 32 : 64;
+    // narrower row tiles where wider ones would leave SMs without two CTAs
+    // (the kernel is latency-bound: resident warps hide the chunk loads)
+    const uint64_t ttiles = (batch + kTTok - 1) / kTTok, want = 2 * (uint64_t)num_sms();
+    const unsigned rows_per = (w.rows + 63) / 64 * ttiles >= want ? 64 : (w.rows + 31) / 32 * ttiles >= want ? 32 : 16;
     const dim3 grid((unsigned)((w.rows + rows_per - 1) / rows_per), (unsigned)ttiles);
-    if (narrow) matmul_f32act_tiled_kernel<TYPE, 32><<<grid, kTThreads, 0, s>>>(w, x, (int)batch, y);
-    else matmul_f32act_tiled_kernel<TYPE, 64><<<grid, kTThreads, 0, s>>>(w, x, (int)batch, y);
+    if (rows_per == 64) matmul_f32act_tiled_kernel<TYPE, 64><<<grid, kTThreads, 0, s>>>(w, x, (int)batch, y);
+    else if (rows_per == 32) matmul_f32act_tiled_kernel<TYPE, 32><<<grid, kTThreads, 0, s>>>(w, x, (int)batch, y);
+    else matmul_f32act_tiled_kernel<TYPE, 16><<<grid, kTThreads, 0, s>>>(w, x, (int)batch, y);
     return cudaGetLastError();
 }
 

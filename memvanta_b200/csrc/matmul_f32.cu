@@ -120,42 +120,52 @@ static cudaError_t launch_f32act(const mv_weight_s& w, const float* x, uint64_t 
 }
 
 // ---------------------------------------------------------------------
-// Batches of 8 tokens and more: a register-tiled kernel.  A CTA of 128
-// threads owns ROWS (64, 32 or 16) rows x 32 tokens; K advances in chunks of 64
-// elements, dequantised (deq4, the same per-element values) into a row-major
-// shared tile next to the chunk's activations, so each weight element is
-// loaded and dequantised once per 32 tokens instead of once per token.  A
-// thread owns rows tid%16 + 16i (i < ROWS/16) and tokens 4*(tid/16) + j
-// (j < 4) and reads float4 runs of 4 k from both tiles (the 16 rows a warp
-// reads are consecutive: no bank conflicts); the next chunk's weights and
-// activations are loaded into registers while the current chunk is
-// multiplied.  Each output is one fp32 FMA chain over k in order.
+// Batches of 8 tokens and more: a register-tiled kernel.  A CTA owns ROWS
+// (64, 32 or 16) rows x 32 tokens and runs KS groups of 128 threads; group g
+// takes the K chunks g, g + KS, ... (64 elements each), dequantised (deq4,
+// the same per-element values) into the group's row-major shared tile next
+// to the chunk's activations, so each weight element is loaded and
+// dequantised once per 32 tokens instead of once per token.  A thread owns
+// rows lt%16 + 16i (i < ROWS/16) and tokens 4*(lt/16) + j (j < 4) and reads
+// float4 runs of 4 k from both tiles (the 16 rows a warp reads are
+// consecutive: no bank conflicts); the group's next chunk is loaded into
+// registers while the current one is multiplied.  The kernel is
+// latency-bound on those loads, so the K groups are there for resident
+// warps.  Each output is one fp32 FMA chain per group over its chunks in
+// order, the groups' partial sums then added in group order.
 constexpr int kTTok = 32, kTK = 64, kTThreads = 128;
 constexpr int kTPad = kTK + 4;  // floats per tile row (16-byte aligned, rows 4 banks apart)
 
-template <int TYPE, int ROWS>
-__global__ void __launch_bounds__(kTThreads) matmul_f32act_tiled_kernel(mv_weight_s w, const float* __restrict__ x,
-                                                                        int batch, float* __restrict__ y) {
+__host__ __device__ constexpr size_t tiled_smem(int rows, int ks) {
+    return (size_t)ks * (rows + kTTok) * kTPad * sizeof(float);
+}
+
+template <int TYPE, int ROWS, int KS>
+__global__ void __launch_bounds__(kTThreads * KS) matmul_f32act_tiled_kernel(mv_weight_s w,
+                                                                             const float* __restrict__ x, int batch,
+                                                                             float* __restrict__ y) {
     constexpr int RT = ROWS / 16;                       // rows per thread
     constexpr int WG = ROWS * kTK / 4 / kTThreads;      // weight groups of 4 a thread stages
     constexpr int XG = kTTok * kTK / 4 / kTThreads;     // activation float4 a thread stages
-    __shared__ __align__(16) float ws[ROWS][kTPad];
-    __shared__ __align__(16) float xs[kTTok][kTPad];
-    const int K = (int)w.cols, rows = (int)w.rows, tid = threadIdx.x;
+    extern __shared__ __align__(16) float tsm[];
+    const int K = (int)w.cols, rows = (int)w.rows;
+    const int grp = (int)threadIdx.x / kTThreads, lt = (int)threadIdx.x % kTThreads;
+    float(*ws)[kTPad] = reinterpret_cast<float(*)[kTPad]>(tsm + (size_t)grp * (ROWS + kTTok) * kTPad);
+    float(*xs)[kTPad] = ws + ROWS;
     const int r0 = blockIdx.x * ROWS, t0 = blockIdx.y * kTTok;
-    const int tr = tid & 15, tt = (tid >> 4) * 4;
+    const int tr = lt & 15, tt = (lt >> 4) * 4;
     float wv[WG][4], xv[XG][4];
     auto load = [&](int k0) {
 #pragma unroll
         for (int i = 0; i < WG; ++i) {
-            const int g = tid + i * kTThreads, row = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
+            const int g = lt + i * kTThreads, row = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
             const int r = r0 + row, e0 = k0 + kk;
             if (r < rows && e0 < K) deq4<TYPE>(w, (uint64_t)r, (uint64_t)e0, wv[i]);
             else wv[i][0] = wv[i][1] = wv[i][2] = wv[i][3] = 0.0f;
         }
 #pragma unroll
         for (int i = 0; i < XG; ++i) {
-            const int g = tid + i * kTThreads, tok = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
+            const int g = lt + i * kTThreads, tok = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
             const int t = t0 + tok, e0 = k0 + kk;
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
             if (t < batch && e0 < K) v = *reinterpret_cast<const float4*>(x + (size_t)t * K + e0);
@@ -165,12 +175,12 @@ __global__ void __launch_bounds__(kTThreads) matmul_f32act_tiled_kernel(mv_weigh
     auto store = [&]() {
 #pragma unroll
         for (int i = 0; i < WG; ++i) {
-            const int g = tid + i * kTThreads, row = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
+            const int g = lt + i * kTThreads, row = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
             *reinterpret_cast<float4*>(&ws[row][kk]) = make_float4(wv[i][0], wv[i][1], wv[i][2], wv[i][3]);
         }
 #pragma unroll
         for (int i = 0; i < XG; ++i) {
-            const int g = tid + i * kTThreads, tok = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
+            const int g = lt + i * kTThreads, tok = g / (kTK / 4), kk = (g % (kTK / 4)) * 4;
             *reinterpret_cast<float4*>(&xs[tok][kk]) = make_float4(xv[i][0], xv[i][1], xv[i][2], xv[i][3]);
         }
     };
@@ -179,12 +189,14 @@ __global__ void __launch_bounds__(kTThreads) matmul_f32act_tiled_kernel(mv_weigh
     for (int i = 0; i < RT; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-    load(0);
-    for (int k0 = 0; k0 < K; k0 += kTK) {
+    // every group runs the same number of rounds (a chunk past K loads zeros)
+    const int rounds = ((K + kTK - 1) / kTK + KS - 1) / KS;
+    load(grp * kTK);
+    for (int rd = 0; rd < rounds; ++rd) {
         __syncthreads();  // the previous chunk's tiles are no longer read
         store();
         __syncthreads();
-        if (k0 + kTK < K) load(k0 + kTK);  // in flight during this chunk's FMAs
+        if (rd + 1 < rounds) load((grp + (rd + 1) * KS) * kTK);  // in flight during this chunk's FMAs
 #pragma unroll 4
         for (int k = 0; k < kTK; k += 4) {
             float4 a[RT], b[4];
@@ -203,6 +215,24 @@ __global__ void __launch_bounds__(kTThreads) matmul_f32act_tiled_kernel(mv_weigh
                 }
         }
     }
+    if constexpr (KS > 1) {
+        // groups 1.. hand their partial sums to group 0 (the tiles are free now)
+        __syncthreads();
+        float* part = tsm + (size_t)lt * (KS - 1) * RT * 4;
+        if (grp > 0)
+#pragma unroll
+            for (int i = 0; i < RT; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) part[((grp - 1) * RT + i) * 4 + j] = acc[i][j];
+        __syncthreads();
+        if (grp > 0) return;
+#pragma unroll
+        for (int g = 0; g < KS - 1; ++g)
+#pragma unroll
+            for (int i = 0; i < RT; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] += part[(g * RT + i) * 4 + j];
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int t = t0 + tt + j;
@@ -215,18 +245,25 @@ __global__ void __launch_bounds__(kTThreads) matmul_f32act_tiled_kernel(mv_weigh
     }
 }
 
+template <int TYPE, int ROWS, int KS>
+static cudaError_t launch_tiled(const mv_weight_s& w, const float* x, uint64_t batch, float* y, cudaStream_t s,
+                                uint64_t ttiles) {
+    const size_t smem = tiled_smem(ROWS, KS);
+    ensure_smem_attr(matmul_f32act_tiled_kernel<TYPE, ROWS, KS>, (int)smem);
+    const dim3 grid((unsigned)((w.rows + ROWS - 1) / ROWS), (unsigned)ttiles);
+    matmul_f32act_tiled_kernel<TYPE, ROWS, KS><<<grid, kTThreads * KS, smem, s>>>(w, x, (int)batch, y);
+    return cudaGetLastError();
+}
+
 template <int TYPE>
 static cudaError_t launch_f32act_tiled(const mv_weight_s& w, const float* x, uint64_t batch, float* y,
                                        cudaStream_t s) {
-    // narrower row tiles where wider ones would leave SMs without two CTAs
-    // (the kernel is latency-bound: resident warps hide the chunk loads)
+    // narrower row tiles, and more K groups, where wider ones would leave SMs
+    // without two CTAs (resident warps hide the chunk loads)
     const uint64_t ttiles = (batch + kTTok - 1) / kTTok, want = 2 * (uint64_t)num_sms();
-    const unsigned rows_per = (w.rows + 63) / 64 * ttiles >= want ? 64 : (w.rows + 31) / 32 * ttiles >= want ? 32 : 16;
-    const dim3 grid((unsigned)((w.rows + rows_per - 1) / rows_per), (unsigned)ttiles);
-    if (rows_per == 64) matmul_f32act_tiled_kernel<TYPE, 64><<<grid, kTThreads, 0, s>>>(w, x, (int)batch, y);
-    else if (rows_per == 32) matmul_f32act_tiled_kernel<TYPE, 32><<<grid, kTThreads, 0, s>>>(w, x, (int)batch, y);
-    else matmul_f32act_tiled_kernel<TYPE, 16><<<grid, kTThreads, 0, s>>>(w, x, (int)batch, y);
-    return cudaGetLastError();
+    if ((w.rows + 63) / 64 * ttiles >= want) return launch_tiled<TYPE, 64, 2>(w, x, batch, y, s, ttiles);
+    if ((w.rows + 31) / 32 * ttiles >= want) return launch_tiled<TYPE, 32, 2>(w, x, batch, y, s, ttiles);
+    return launch_tiled<TYPE, 16, 4>(w, x, batch, y, s, ttiles);
 }
 
 template <int TYPE>

@@ -319,6 +319,9 @@ def test_error_paths(cuda):
     w = gguf.gen_q4_0(4, 64, rng)
     with pytest.raises(mv.MemVantaError, match="UNSUPPORTED"):
         mv.Weight.upload(w, 3, 4, 64)                  # Q4_1: the reference cannot matvec it either
+    for kq, bb in ((12, 144), (13, 176)):             # Q4_K / Q5_K: sized by the loader, no kernel
+        with pytest.raises(mv.MemVantaError, match="UNSUPPORTED"):  # (src/gguf_kernels.cpp:251 throws too)
+            mv.Weight.upload(np.zeros(4 * bb, np.uint8), kq, 4, 256)
     with pytest.raises(mv.MemVantaError, match="INVALID"):
         mv.Weight.upload(w[:-1], gguf.Q4_0, 4, 64)     # nbytes mismatch
     with pytest.raises(mv.MemVantaError, match="not block aligned"):

@@ -413,7 +413,8 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
     __syncthreads();
     auto slot_of = [&](int t) -> size_t { return (size_t)tbl[t / page] * page + t % page; };
 
-    // 1. scores: thread t of a K tile owns one token for all QG queries
+    // 1. scores: a K tile's rows are copied by thread t (token t of the tile) and
+    // scored by a pair of lanes, for all QG queries
     {
         const int krow = slice + 16;
         const int KT = attn_ktile(HD, kvt);
@@ -429,54 +430,67 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
         const int ntile = (cmax + KT - 1) / KT;
         issue_k(0, 0);
         for (int tile = 0; tile < ntile; ++tile) {
+            cp_async_wait<0>();  // this thread's copies of the tile have landed
+            __syncthreads();     // ... every thread's; and tile-1's rows are no longer read
             if (tile + 1 < ntile) issue_k(tile + 1, (tile + 1) & 1);
             else cp_async_commit();
-            cp_async_wait<1>();
-            const int t = tile * KT + tid;
-            if (tid < KT && t < cmax) {
-                const uint8_t* row = ring + ((size_t)(tile & 1) * KT + tid) * krow;
-                float acc[QG][8];
+            // a pair of lanes per token: the even lane accumulates the reference's
+            // lanes 0..3 (elements d..d+3 of every 8), the odd lane lanes 4..7;
+            // the odd lane's four sums then join the even lane's in lane order
+            const int half = lane & 1;
+            for (int tk = warp * 16 + (lane >> 1); tk < KT; tk += (HD / 32) * 16) {  // warp-uniform trips
+                const int t = tile * KT + tk;
+                const bool valid = t < cmax;
+                const uint8_t* row = ring + ((size_t)(tile & 1) * KT + tk) * krow;
+                float acc[QG][4];
 #pragma unroll
                 for (int i = 0; i < QG; ++i)
 #pragma unroll
-                    for (int l = 0; l < 8; ++l) acc[i][l] = 0.f;
-                const size_t slot = kvt >= 2 ? slot_of(t) : 0;
+                    for (int l = 0; l < 4; ++l) acc[i][l] = 0.f;
+                const size_t slot = kvt >= 2 && valid ? slot_of(t) : 0;
+                if (valid) {
 #pragma unroll 2
-                for (int d = 0; d < HD; d += 8) {
-                    float kf[8];
-                    if (kvt == 1) {
-                        const uint4 w = *reinterpret_cast<const uint4*>(row + d * 2);
-                        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+                    for (int d = 0; d < HD; d += 8) {
+                        const int e = d + 4 * half;  // this lane's four elements of the group
+                        float kf[4];
+                        if (kvt == 1) {
+                            const uint2 w = *reinterpret_cast<const uint2*>(row + e * 2);
+                            kf[0] = half_bits_to_float((unsigned short)(w.x & 0xffff));
+                            kf[1] = half_bits_to_float((unsigned short)(w.x >> 16));
+                            kf[2] = half_bits_to_float((unsigned short)(w.y & 0xffff));
+                            kf[3] = half_bits_to_float((unsigned short)(w.y >> 16));
+                        } else if (kvt == 0) {
+                            const float4 u = *reinterpret_cast<const float4*>(row + e * 4);
+                            kf[0] = u.x, kf[1] = u.y, kf[2] = u.z, kf[3] = u.w;
+                        } else {
+                            const uint32_t w = *reinterpret_cast<const uint32_t*>(row + e);
+                            const float sc8 = kvt == 3 ? a.k_scales[slot * (kv_dim / 32) + (kh * HD + d) / 32] : 1.0f;
 #pragma unroll
-                        for (int l = 0; l < 8; ++l)
-                            kf[l] = half_bits_to_float((unsigned short)(ws[l / 2] >> (16 * (l & 1))));
-                    } else if (kvt == 0) {
-                        const float4 u = *reinterpret_cast<const float4*>(row + d * 4);
-                        const float4 v = *reinterpret_cast<const float4*>(row + d * 4 + 16);
-                        kf[0] = u.x, kf[1] = u.y, kf[2] = u.z, kf[3] = u.w;
-                        kf[4] = v.x, kf[5] = v.y, kf[6] = v.z, kf[7] = v.w;
-                    } else {
-                        const uint2 w = *reinterpret_cast<const uint2*>(row + d);
-                        const float sc8 = kvt == 3 ? a.k_scales[slot * (kv_dim / 32) + (kh * HD + d) / 32] : 1.0f;
+                            for (int l = 0; l < 4; ++l) kf[l] = s8_to_f32(w, l) * sc8;
+                        }
 #pragma unroll
-                        for (int l = 0; l < 8; ++l) kf[l] = s8_to_f32(l < 4 ? w.x : w.y, l & 3) * sc8;
-                    }
-#pragma unroll
-                    for (int i = 0; i < QG; ++i) {
-                        const float4 qa = *reinterpret_cast<const float4*>(qs + i * HD + d);
-                        const float4 qb = *reinterpret_cast<const float4*>(qs + i * HD + d + 4);
-                        const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-                        for (int l = 0; l < 8; ++l) acc[i][l] = fmaf(qv[l], kf[l], acc[i][l]);
+                        for (int i = 0; i < QG; ++i) {
+                            const float4 qv = *reinterpret_cast<const float4*>(qs + i * HD + e);
+                            acc[i][0] = fmaf(qv.x, kf[0], acc[i][0]);
+                            acc[i][1] = fmaf(qv.y, kf[1], acc[i][1]);
+                            acc[i][2] = fmaf(qv.z, kf[2], acc[i][2]);
+                            acc[i][3] = fmaf(qv.w, kf[3], acc[i][3]);
+                        }
                     }
                 }
-                const float ksc = kvt == 2 ? a.k_scales[slot] : 1.0f;
+                const float ksc = kvt == 2 && valid ? a.k_scales[slot] : 1.0f;
 #pragma unroll
                 for (int i = 0; i < QG; ++i) {
-                    if (t < cq[i]) {
-                        float dot = acc[i][0];
+                    float hi[4];
 #pragma unroll
-                        for (int l = 1; l < 8; ++l) dot += acc[i][l];
+                    for (int l = 0; l < 4; ++l) hi[l] = __shfl_xor_sync(0xffffffffu, acc[i][l], 1);
+                    if (valid && half == 0 && t < cq[i]) {
+                        float dot = acc[i][0];
+                        dot += acc[i][1];
+                        dot += acc[i][2];
+                        dot += acc[i][3];
+#pragma unroll
+                        for (int l = 0; l < 4; ++l) dot += hi[l];
                         if (kvt == 2) dot = dot * ksc;
                         sc[i * mctx + t] = dot / sqrtf((float)HD);
                     }
@@ -972,6 +986,7 @@ cudaError_t paged_attn_prefill(const AttnArgs& a, cudaStream_t s) {
     // batches: twice the reuse of every staged K/V tile, eight independent
     // chains per thread), of 4 when it gives every SM a CTA, else pairs
     const uint64_t sms = (uint64_t)num_sms();
+    // (pp512, 7B: groups of 8 12,640 tok/s against 12,350 with groups of 4)
     const int qg = (a.n_seq + 7) / 8 * a.n_head >= 2 * sms ? 8
                    : (a.n_seq + 3) / 4 * a.n_head >= sms   ? 4
                    : a.n_seq >= 2                          ? 2

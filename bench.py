@@ -608,11 +608,11 @@ def main_micro(args):
         return
     if args.workload == "prefill":
         # pp512 alone: `steps` prefills of the 512-token prompt in batches of
-        # 32 after one warm-up prefill of the first batch
+        # 32 after one warm-up prefill of the same prompt
         m = mv.LlamaModel(ensure_llama7b(), ctx_override=L7_CTX, kv_page_tokens=16, kv_type=mv.KV_F16)
         ms = torch.cuda.ExternalStream(m.stream)
         prompt = fixed_tokens(L7_PP)
-        m.prefill(prompt[:L7_BATCH], L7_BATCH, True)
+        m.prefill(prompt, L7_BATCH, True)  # warm-up: the 512-token batch's buffers and kernels
         total = 0.0
         for _ in range(args.steps):
             m.reset()

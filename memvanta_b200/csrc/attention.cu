@@ -591,6 +591,22 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
         // go out before the chain steps (each query's steps stay in token order)
         const int nall = max(0, min(n, cmin - tile * kVTile));
         int tt = 0;
+        if (kvt < 2 && (mctx & 3) == 0) {  // weights as float4 runs (16-byte aligned rows)
+            for (; tt + 8 <= nall; tt += 8) {
+                float v[8], vs;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) vload(tt + j, v[j], vs);
+#pragma unroll
+                for (int i = 0; i < QG; ++i) {
+                    const float* al = sc + i * mctx + tile * kVTile + tt;
+                    const float4 a0 = *reinterpret_cast<const float4*>(al);
+                    const float4 a1 = *reinterpret_cast<const float4*>(al + 4);
+                    const float aj[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) out[i] = fmaf(aj[j], v[j], out[i]);
+                }
+            }
+        }
         for (; tt + 8 <= nall; tt += 8) {
             float v[8], vs[8], al[QG][8];
 #pragma unroll

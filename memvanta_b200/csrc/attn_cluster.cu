@@ -12,10 +12,11 @@
 //   * CTA r scores its contiguous share of the cached tokens 0..p-1 (one
 //     thread per token, the K rows in its shared memory); the last CTA also
 //     rotates and scores this token p;
-//   * the cluster combines the per-CTA maxima and double denominators
-//     through distributed shared memory (every CTA adds them in rank order,
-//     so all hold the same m and den), and every CTA broadcasts its tokens'
-//     weights e_t * float(1/den) into every CTA's weight array;
+//   * the cluster combines the per-CTA maxima through distributed shared
+//     memory, then in one more exchange every CTA broadcasts its tokens'
+//     exponentials e_t into every CTA's weight array and its double
+//     denominator into every CTA (each adds them in rank order, so all hold
+//     the same den and form alpha_t = e_t * float(1/den) themselves);
 //   * CTA r then runs the chains of dimensions [r*hd/kCC, (r+1)*hd/kCC) over
 //     all tokens in order, from the V columns of those dimensions, which it
 //     staged for every token.
@@ -236,17 +237,19 @@ __global__ void __launch_bounds__(kCT) attn_decode_cluster_kernel(AttnFusedArgs 
 #pragma unroll
     for (int q = 1; q < kCC; ++q) M = fmaxf(M, mx[q]);
 
-    // 2. exponentials and the double denominator, combined in rank order
+    // 2. exponentials into every CTA's weight array and the double denominator
+    //    into every CTA (one exchange); every CTA then adds the denominators in
+    //    rank order and forms alpha_t = e_t * float(1/den) itself
     double den = 0.0;
     for (int i = tid; i < nt; i += kCT) {
         const float e = expf_cr(sc[i] - M);
-        sc[i] = e;
         den += (double)e;
+        for (int q = 0; q < kCC; ++q) cl.map_shared_rank(wt, q)[t0 + i] = e;
     }
-    float enew = 0.0f;
     if (last && tid == kCT - 1) {
-        enew = expf_cr(snew - M);
+        const float enew = expf_cr(snew - M);
         den += (double)enew;
+        for (int q = 0; q < kCC; ++q) cl.map_shared_rank(wt, q)[p] = enew;
     }
     den = warp_sum_d(den);
     if (lane == 0) redd[warp] = den;
@@ -264,18 +267,6 @@ __global__ void __launch_bounds__(kCT) attn_decode_cluster_kernel(AttnFusedArgs 
     for (int q = 0; q < kCC; ++q) tot += dn[q];
     const float inv = (float)(1.0 / tot);
 
-    // 3. every token's weight into every CTA
-    for (int i = tid; i < nt; i += kCT) {
-        const float al = sc[i] * inv;
-        for (int q = 0; q < kCC; ++q) cl.map_shared_rank(wt, q)[t0 + i] = al;
-    }
-    if (last && tid == kCT - 1) {
-        const float al = enew * inv;
-        for (int q = 0; q < kCC; ++q) cl.map_shared_rank(wt, q)[p] = al;
-    }
-    cluster_arrive();
-    cluster_wait();
-
     // 4. this CTA's output dimensions: one chain per dimension over t = 0..p
     float out = 0.0f;
     if (tid < DPC) {
@@ -289,14 +280,14 @@ __global__ void __launch_bounds__(kCT) attn_decode_cluster_kernel(AttnFusedArgs 
             float v[8], al[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                al[j] = wt[t + j];
+                al[j] = wt[t + j] * inv;
                 v[j] = v_at(t + j);
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j) out = fmaf(al[j], v[j], out);
         }
-        for (; t < p; ++t) out = fmaf(wt[t], v_at(t), out);
-        out = fmaf(wt[p], vnew[tid], out);
+        for (; t < p; ++t) out = fmaf(wt[t] * inv, v_at(t), out);
+        out = fmaf(wt[p] * inv, vnew[tid], out);
         const int d = r * DPC + tid;
         if constexpr (TP) ll_put_all(a.tp, a.out_shared, (uint64_t)(a.head_off + h) * HD + d, out,
                                      tp_uepoch(a.tp, a.out_point));

@@ -73,10 +73,12 @@ MV_API int mv_version(void);
  * as cudaFuncGetAttributes' binaryVersion (100 = sm_100).  No counterpart in
  * the reference; lets a caller or a test check the build at run time. */
 MV_API int mv_binary_arch(int* out);
-/* Synchronises `stream` and reports MV_ERR_TIMEOUT if a tensor-core kernel
- * (mv_gemm with MV_ACT_Q8, model prefill) gave up a bounded device-side wait
- * since the last check -- its outputs are then invalid.  Host-pointer calls
- * and the model check this themselves.  No counterpart in the reference. */
+/* Synchronises `stream` and reports MV_ERR_TIMEOUT if a kernel with bounded
+ * device-side waits (the tensor-core GEMMs of mv_gemm with MV_ACT_Q8 and of
+ * the model's prefill, the decode GEMV's and the cluster attention's
+ * exchanges between CTAs) gave up a wait since the last check -- its outputs
+ * are then invalid.  Host-pointer calls and the model's prefill check this
+ * themselves.  No counterpart in the reference. */
 MV_API int mv_stream_status(void* stream);
 /* Test hook for the bounded waits (no counterpart in the reference): the
  * next fp16 tensor-core GEMM launch (mv_gemm, MV_ACT_Q8, batch >= 64) leaves

@@ -13,7 +13,9 @@
 //     thread per token, the K rows in its shared memory); the last CTA also
 //     rotates and scores this token p;
 //   * the cluster combines the per-CTA maxima through distributed shared
-//     memory, then in one more exchange every CTA broadcasts its tokens'
+//     memory (st.async stores that complete bytes on the receiving CTA's
+//     mbarrier: no cluster-wide fence), then in one more exchange every CTA
+//     broadcasts its tokens'
 //     exponentials e_t into every CTA's weight array and its double
 //     denominator into every CTA (each adds them in rank order, so all hold
 //     the same den and form alpha_t = e_t * float(1/den) themselves);
@@ -33,11 +35,26 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tc.cuh"
 #include "tp.cuh"
 
 namespace mvb {
 
 namespace cg = cooperative_groups;
+
+__device__ int g_attn_status = 0;  // site of a cluster-attention wait that ran out (0: none)
+
+// Adds this file's status to *status (first site wins) and clears it.
+cudaError_t attn_status_take(int* status) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_attn_status, sizeof(int));
+    if (e == cudaSuccess && v) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_attn_status, &zero, sizeof(int));
+        if (!*status) *status = v;
+    }
+    return e;
+}
 
 namespace {
 
@@ -52,6 +69,24 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Remote 4- / 8-byte stores into a peer CTA's shared memory that complete
+// bytes on the peer's mbarrier (no fence, no cluster barrier on the data path).
+__device__ __forceinline__ uint32_t mapa_u32(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_async_b32(uint32_t raddr, uint32_t v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr), "r"(v),
+                 "r"(rbar)
+                 : "memory");
+}
+__device__ __forceinline__ void st_async_b64(uint32_t raddr, uint64_t v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b64 [%0], %1, [%2];" ::"r"(raddr), "l"(v),
+                 "r"(rbar)
+                 : "memory");
+}
 
 __device__ __forceinline__ void cluster_arrive() {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
@@ -92,6 +127,8 @@ __global__ void __launch_bounds__(kCT) attn_decode_cluster_kernel(AttnFusedArgs 
     __shared__ double dn[kCC];
     __shared__ float snew;
     __shared__ float qv[32];  // xq: the 32 outputs of one Q8 block (its first CTA)
+    __shared__ __align__(8) uint64_t xbar[2];  // [0]: the maxima landed, [1]: exponentials + denominators
+    __shared__ int xabort;
     cg::cluster_group cl = cg::this_cluster();
     const int r = (int)cl.block_rank(), h = blockIdx.x / kCC;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -107,11 +144,22 @@ __global__ void __launch_bounds__(kCT) attn_decode_cluster_kernel(AttnFusedArgs 
     const uint8_t* kp = static_cast<const uint8_t*>(a.k_pages);
     const uint8_t* vp = static_cast<const uint8_t*>(a.v_pages);
     const size_t row_bytes = (size_t)kv_dim * ES, head_off = (size_t)kh * HD * ES;
-    // every CTA of the cluster has started before any writes another's memory
+    const uint32_t xb0 = tc::smem_u32(&xbar[0]), xb1 = xb0 + 8;
+    const int p = a.pos[0];  // this token; tokens 0..p-1 are cached
+    if (tid == 0) {
+        // the exchanges' receive barriers, armed for what every CTA will send
+        xabort = 0;
+        tc::mbar_init(xb0, 1);
+        tc::mbar_init(xb1, 1);
+        tc::mbar_fence_init();
+        tc::mbar_expect_tx(xb0, kCC * 4);
+        tc::mbar_expect_tx(xb1, (uint32_t)(p + 1) * 4 + kCC * 8);
+    }
+    // every CTA of the cluster has started (and armed its barriers) before
+    // any writes another's memory
     cluster_arrive();
 
     pdl_trigger();
-    const int p = a.pos[0];  // this token; tokens 0..p-1 are cached
     const int npg = (p + page) / page;
     for (int i = tid; i < npg; i += kCT) tbl[i] = a.block_table[i];
     __syncthreads();
@@ -229,10 +277,10 @@ __global__ void __launch_bounds__(kCT) attn_decode_cluster_kernel(AttnFusedArgs 
         float cm = red[0];
 #pragma unroll
         for (int w = 1; w < kCT / 32; ++w) cm = fmaxf(cm, red[w]);
-        for (int q = 0; q < kCC; ++q) cl.map_shared_rank(mx, q)[r] = cm;  // into every CTA
+        const uint32_t dst = tc::smem_u32(&mx[r]);
+        for (int q = 0; q < kCC; ++q) st_async_b32(mapa_u32(dst, q), __float_as_uint(cm), mapa_u32(xb0, q));
     }
-    cluster_arrive();
-    cluster_wait();
+    tc::mbar_wait(xb0, 0, &xabort, &g_attn_status, 51);  // every CTA's maximum has landed
     float M = mx[0];
 #pragma unroll
     for (int q = 1; q < kCC; ++q) M = fmaxf(M, mx[q]);
@@ -241,15 +289,17 @@ __global__ void __launch_bounds__(kCT) attn_decode_cluster_kernel(AttnFusedArgs 
     //    into every CTA (one exchange); every CTA then adds the denominators in
     //    rank order and forms alpha_t = e_t * float(1/den) itself
     double den = 0.0;
+    const uint32_t wt0 = tc::smem_u32(wt);
     for (int i = tid; i < nt; i += kCT) {
         const float e = expf_cr(sc[i] - M);
         den += (double)e;
-        for (int q = 0; q < kCC; ++q) cl.map_shared_rank(wt, q)[t0 + i] = e;
+        for (int q = 0; q < kCC; ++q)
+            st_async_b32(mapa_u32(wt0 + (uint32_t)(t0 + i) * 4, q), __float_as_uint(e), mapa_u32(xb1, q));
     }
     if (last && tid == kCT - 1) {
         const float enew = expf_cr(snew - M);
         den += (double)enew;
-        for (int q = 0; q < kCC; ++q) cl.map_shared_rank(wt, q)[p] = enew;
+        for (int q = 0; q < kCC; ++q) st_async_b32(mapa_u32(wt0 + (uint32_t)p * 4, q), __float_as_uint(enew), mapa_u32(xb1, q));
     }
     den = warp_sum_d(den);
     if (lane == 0) redd[warp] = den;
@@ -258,10 +308,11 @@ __global__ void __launch_bounds__(kCT) attn_decode_cluster_kernel(AttnFusedArgs 
         double cd = 0.0;
 #pragma unroll
         for (int w = 0; w < kCT / 32; ++w) cd += redd[w];
-        for (int q = 0; q < kCC; ++q) cl.map_shared_rank(dn, q)[r] = cd;
+        const uint32_t dst = tc::smem_u32(&dn[r]);
+        for (int q = 0; q < kCC; ++q)
+            st_async_b64(mapa_u32(dst, q), (uint64_t)__double_as_longlong(cd), mapa_u32(xb1, q));
     }
-    cluster_arrive();
-    cluster_wait();
+    tc::mbar_wait(xb1, 0, &xabort, &g_attn_status, 52);  // every exponential and denominator has landed
     double tot = 0.0;
 #pragma unroll
     for (int q = 0; q < kCC; ++q) tot += dn[q];

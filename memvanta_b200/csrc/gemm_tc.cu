@@ -87,6 +87,8 @@ cudaError_t tc_status(cudaStream_t s, int* status) {
     }
     *status = v;
     if (e == cudaSuccess) e = f16_status_take(status);
+    if (e == cudaSuccess) e = gemv_status_take(status);
+    if (e == cudaSuccess) e = attn_status_take(status);
     return e;
 }
 

@@ -979,6 +979,19 @@ cudaError_t gemv_q4(const GemvQ4Args& a, cudaStream_t s) {
     return r4 ? launch<4, false, 2>(a, s) : launch<2, false, 2>(a, s);
 }
 
+// Adds the GEMV's status (a pair exchange whose bounded wait ran out) to
+// *status (first site wins) and clears it.
+cudaError_t gemv_status_take(int* status) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_gemv_status, sizeof(int));
+    if (e == cudaSuccess && v) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_gemv_status, &zero, sizeof(int));
+        if (!*status) *status = v;
+    }
+    return e;
+}
+
 cudaError_t q4_block_dots(const mv_weight_s& w, const float* x, int32_t* isum, cudaStream_t s) {
     ensure_smem_attr(q4_block_dots_kernel, 200 * 1024);
     const uint64_t total = w.rows * w.nb;

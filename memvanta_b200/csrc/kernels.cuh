@@ -112,6 +112,10 @@ cudaError_t tc_status(cudaStream_t s, int* status);
 cudaError_t gemm_q4_q8_f16(const mv_weight_s& w, const uint16_t* qh, const float* dT, uint64_t ldb, uint64_t batch,
                            float* y, cudaStream_t s, bool accumulate = false);
 cudaError_t f16_status_take(int* status);
+// The same for the decode GEMV's pair exchange and the cluster attention's
+// exchanges (bounded waits on their receive barriers).
+cudaError_t gemv_status_take(int* status);
+cudaError_t attn_status_take(int* status);
 // whether a Q8-activation matmul of `batch` tokens takes gemm_q4_q8_f16
 // (64 tokens and more; MV_GEMM_F16=0 keeps the int8 kernel everywhere)
 bool gemm_f16_preferred(uint64_t batch);

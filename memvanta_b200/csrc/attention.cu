@@ -121,7 +121,7 @@ __device__ __forceinline__ void cp_async_wait() {
 // Tokens per K tile: one per thread, at most 64, and two tiles of padded
 // rows within 128 KB (64-token tiles keep a CTA near 38 KB for hd 128 F16,
 // five per SM: these kernels are latency-bound, resident warps count).
-__host__ __device__ inline int attn_ktile(uint64_t hd, int kv_type) {
+__host__ __device__ constexpr int attn_ktile(uint64_t hd, int kv_type) {
     const uint64_t esize = kv_type == 0 ? 4 : kv_type == 1 ? 2 : 1;
     uint64_t kt = 65536 / (hd * esize + 16);
     if (kt > hd) kt = hd;
@@ -369,30 +369,97 @@ __host__ __device__ inline AttnGroupSmem attn_group_plan(uint64_t hd, uint64_t m
     return p;
 }
 
-template <int HD, int QG>
+// Page of token t by a multiply: t / page = umulhi(t, ceil(2^32 / page)) is
+// exact while t * page < 2^32 (paged_attn_prefill checks max_ctx * page).
+struct PageDiv {
+    uint32_t page, mul;
+    __device__ explicit PageDiv(uint64_t p) : page((uint32_t)p), mul((uint32_t)((0x100000000ull + p - 1) / p)) {}
+    __device__ __forceinline__ uint32_t index(uint32_t t) const { return page == 1 ? t : __umulhi(t, mul); }
+};
+
+// Two fp32 values in one 64-bit register pair (element 0 in the low half) and
+// fma.rn.f32x2: two IEEE round-to-nearest FMAs, each bit-identical to fmaf.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// The QG weights of one token (token-major rows, 8-byte aligned for QG = 2,
+// 16-byte aligned from QG = 4) as QG/2 pairs of queries (2p, 2p+1).
+template <int QG>
+__device__ __forceinline__ void ld_pairs(const float* p, uint64_t (&w)[QG / 2]) {
+    if constexpr (QG == 2) {
+        w[0] = *reinterpret_cast<const uint64_t*>(p);
+    } else {
+#pragma unroll
+        for (int k = 0; k < QG / 4; ++k) {
+            const ulonglong2 u = reinterpret_cast<const ulonglong2*>(p)[k];
+            w[2 * k] = u.x;
+            w[2 * k + 1] = u.y;
+        }
+    }
+}
+template <int QG>
+__device__ __forceinline__ void ld_row(const float* p, float (&w)[QG]) {
+#pragma unroll
+    for (int k = 0; k < QG / 2; ++k) {
+        const float2 u = reinterpret_cast<const float2*>(p)[k];
+        w[2 * k] = u.x;
+        w[2 * k + 1] = u.y;
+    }
+}
+template <int QG>
+__device__ __forceinline__ void st_row(float* p, const float (&w)[QG]) {
+    if constexpr (QG == 2) {
+        *reinterpret_cast<float2*>(p) = make_float2(w[0], w[1]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < QG / 4; ++k)
+            reinterpret_cast<float4*>(p)[k] = make_float4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+    }
+}
+
+template <int HD, int QG, int KVT>
 __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ float redf[QG][HD / 32];
     __shared__ double redd[QG][HD / 32];
-    const int s0 = blockIdx.x * QG, h = blockIdx.y, tid = threadIdx.x;
+    constexpr int kEs = KVT == 0 ? 4 : KVT == 1 ? 2 : 1;
+    constexpr int kSlice = HD * kEs;  // bytes of one head's K or V row
+    constexpr int kKT = attn_ktile(HD, KVT);
+    // blockIdx.x is the query head; blockIdx.y counts groups from the last, so
+    // the groups with the longest causal context are dispatched first
+    const int grp = (int)(gridDim.y - 1 - blockIdx.y);
+    const int s0 = grp * QG, h = blockIdx.x, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int G = (int)(a.n_head / a.n_head_kv), kh = h / G;
     const int kv_dim = (int)(a.n_head_kv * HD);
-    const int kvt = a.kv_type;
-    const int esize = kvt == 0 ? 4 : kvt == 1 ? 2 : 1;
-    const int page = (int)a.page;
-    const int mctx = (int)a.max_ctx;
-    const AttnGroupSmem P = attn_group_plan(HD, a.max_ctx, a.max_pages, kvt, QG);
+    const PageDiv pdiv(a.page);
+    const AttnGroupSmem P = attn_group_plan(HD, a.max_ctx, a.max_pages, KVT, QG);
     float* qs = reinterpret_cast<float*>(smem + P.q);  // [QG][HD]
     int* tbl = reinterpret_cast<int*>(smem + P.table);
-    float* sc = reinterpret_cast<float*>(smem + P.sc);  // [QG][max_ctx]
+    float* sc = reinterpret_cast<float*>(smem + P.sc);  // [max_ctx][QG]: token-major
     float* vsc = reinterpret_cast<float*>(smem + P.vsc);
     uint8_t* ring = smem + P.ring;
     const uint8_t* kp = static_cast<const uint8_t*>(a.k_pages);
     const uint8_t* vp = static_cast<const uint8_t*>(a.v_pages);
-    const size_t row_bytes = (size_t)kv_dim * esize;
-    const size_t head_off = (size_t)kh * HD * esize;
-    const int slice = HD * esize;
+    const size_t row_bytes = (size_t)kv_dim * kEs;
+    const size_t head_off = (size_t)kh * kSlice;
 
     pdl_trigger();
     pdl_wait();
@@ -404,30 +471,33 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
         cmax = max(cmax, cq[i]);
         cmin = min(cmin, cq[i]);
     }
-    const int npg = (cmax + page - 1) / page;
+    const int npg = (int)pdiv.index((uint32_t)cmax + pdiv.page - 1);
     const size_t trow = a.one_seq ? 0 : (size_t)s0;
     for (int i = tid; i < npg; i += HD) tbl[i] = a.block_table[trow * a.max_pages + i];
 #pragma unroll
     for (int i = 0; i < QG; ++i)
         qs[i * HD + tid] = cq[i] > 0 ? a.q[(size_t)(s0 + i) * a.q_stride + (size_t)h * HD + tid] : 0.0f;
     __syncthreads();
-    auto slot_of = [&](int t) -> size_t { return (size_t)tbl[t / page] * page + t % page; };
+    auto slot_of = [&](int t) -> size_t {
+        const uint32_t pi = pdiv.index((uint32_t)t);
+        return (size_t)tbl[pi] * pdiv.page + ((uint32_t)t - pi * pdiv.page);
+    };
 
-    // 1. scores: a K tile's rows are copied by thread t (token t of the tile) and
-    // scored by a pair of lanes, for all QG queries
+    // 1. raw dot products of every query with tokens 0..cmax-1: a K tile's rows
+    // are copied by thread t (token t of the tile) and scored by a pair of lanes
     {
-        const int krow = slice + 16;
-        const int KT = attn_ktile(HD, kvt);
+        constexpr int kRow = kSlice + 16;
         auto issue_k = [&](int tile, int buf) {
-            const int t = tile * KT + tid;
-            if (tid < KT && t < cmax) {
+            const int t = tile * kKT + tid;
+            if (tid < kKT && t < cmax) {
                 const uint8_t* src = kp + slot_of(t) * row_bytes + head_off;
-                uint8_t* dst = ring + ((size_t)buf * KT + tid) * krow;
-                for (int c = 0; c < slice; c += 16) cp_async16(dst + c, src + c);
+                uint8_t* dst = ring + ((size_t)buf * kKT + tid) * kRow;
+#pragma unroll
+                for (int c = 0; c < kSlice; c += 16) cp_async16(dst + c, src + c);
             }
             cp_async_commit();
         };
-        const int ntile = (cmax + KT - 1) / KT;
+        const int ntile = (cmax + kKT - 1) / kKT;
         issue_k(0, 0);
         for (int tile = 0; tile < ntile; ++tile) {
             cp_async_wait<0>();  // this thread's copies of the tile have landed
@@ -435,73 +505,74 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
             if (tile + 1 < ntile) issue_k(tile + 1, (tile + 1) & 1);
             else cp_async_commit();
             // a pair of lanes per token: the even lane accumulates the reference's
-            // lanes 0..3 (elements d..d+3 of every 8), the odd lane lanes 4..7;
-            // the odd lane's four sums then join the even lane's in lane order
+            // lanes 0..3 (elements d..d+3 of every 8), the odd lane lanes 4..7,
+            // as two packed pairs (lanes 0,1 and 2,3); the odd lane's four sums
+            // then join the even lane's in lane order
             const int half = lane & 1;
-            for (int tk = warp * 16 + (lane >> 1); tk < KT; tk += (HD / 32) * 16) {  // warp-uniform trips
-                const int t = tile * KT + tk;
+            for (int tk = warp * 16 + (lane >> 1); tk < kKT; tk += (HD / 32) * 16) {  // warp-uniform trips
+                const int t = tile * kKT + tk;
                 const bool valid = t < cmax;
-                const uint8_t* row = ring + ((size_t)(tile & 1) * KT + tk) * krow;
-                float acc[QG][4];
+                const uint8_t* row = ring + ((size_t)(tile & 1) * kKT + tk) * kRow + 4 * half * kEs;
+                const float* qh = qs + 4 * half;
+                uint64_t acc[QG][2];
 #pragma unroll
-                for (int i = 0; i < QG; ++i)
-#pragma unroll
-                    for (int l = 0; l < 4; ++l) acc[i][l] = 0.f;
-                const size_t slot = kvt >= 2 && valid ? slot_of(t) : 0;
+                for (int i = 0; i < QG; ++i) acc[i][0] = acc[i][1] = 0ull;  // +0.0f, +0.0f
+                const size_t slot = KVT >= 2 && valid ? slot_of(t) : 0;
                 if (valid) {
-#pragma unroll 2
-                    for (int d = 0; d < HD; d += 8) {
-                        const int e = d + 4 * half;  // this lane's four elements of the group
-                        float kf[4];
-                        if (kvt == 1) {
-                            const uint2 w = *reinterpret_cast<const uint2*>(row + e * 2);
-                            kf[0] = half_bits_to_float((unsigned short)(w.x & 0xffff));
-                            kf[1] = half_bits_to_float((unsigned short)(w.x >> 16));
-                            kf[2] = half_bits_to_float((unsigned short)(w.y & 0xffff));
-                            kf[3] = half_bits_to_float((unsigned short)(w.y >> 16));
-                        } else if (kvt == 0) {
-                            const float4 u = *reinterpret_cast<const float4*>(row + e * 4);
-                            kf[0] = u.x, kf[1] = u.y, kf[2] = u.z, kf[3] = u.w;
-                        } else {
-                            const uint32_t w = *reinterpret_cast<const uint32_t*>(row + e);
-                            const float sc8 = kvt == 3 ? a.k_scales[slot * (kv_dim / 32) + (kh * HD + d) / 32] : 1.0f;
 #pragma unroll
-                            for (int l = 0; l < 4; ++l) kf[l] = s8_to_f32(w, l) * sc8;
+                    for (int d = 0; d < HD; d += 8) {
+                        uint64_t k01, k23;
+                        if constexpr (KVT == 1) {
+                            const uint2 w = *reinterpret_cast<const uint2*>(row + d * 2);
+                            k01 = f2_pack(half_bits_to_float((unsigned short)(w.x & 0xffff)),
+                                          half_bits_to_float((unsigned short)(w.x >> 16)));
+                            k23 = f2_pack(half_bits_to_float((unsigned short)(w.y & 0xffff)),
+                                          half_bits_to_float((unsigned short)(w.y >> 16)));
+                        } else if constexpr (KVT == 0) {
+                            const ulonglong2 u = *reinterpret_cast<const ulonglong2*>(row + d * 4);
+                            k01 = u.x, k23 = u.y;
+                        } else {
+                            const uint32_t w = *reinterpret_cast<const uint32_t*>(row + d);
+                            const float sc8 = KVT == 3 ? a.k_scales[slot * (kv_dim / 32) + (kh * HD + d) / 32] : 1.0f;
+                            k01 = f2_pack(s8_to_f32(w, 0) * sc8, s8_to_f32(w, 1) * sc8);
+                            k23 = f2_pack(s8_to_f32(w, 2) * sc8, s8_to_f32(w, 3) * sc8);
                         }
 #pragma unroll
                         for (int i = 0; i < QG; ++i) {
-                            const float4 qv = *reinterpret_cast<const float4*>(qs + i * HD + e);
-                            acc[i][0] = fmaf(qv.x, kf[0], acc[i][0]);
-                            acc[i][1] = fmaf(qv.y, kf[1], acc[i][1]);
-                            acc[i][2] = fmaf(qv.z, kf[2], acc[i][2]);
-                            acc[i][3] = fmaf(qv.w, kf[3], acc[i][3]);
+                            const ulonglong2 qv = *reinterpret_cast<const ulonglong2*>(qh + i * HD + d);
+                            acc[i][0] = f2_fma(qv.x, k01, acc[i][0]);
+                            acc[i][1] = f2_fma(qv.y, k23, acc[i][1]);
                         }
                     }
                 }
-                const float ksc = kvt == 2 && valid ? a.k_scales[slot] : 1.0f;
+                const float ksc = KVT == 2 && valid ? a.k_scales[slot] : 1.0f;
+                float dots[QG];
 #pragma unroll
                 for (int i = 0; i < QG; ++i) {
-                    float hi[4];
-#pragma unroll
-                    for (int l = 0; l < 4; ++l) hi[l] = __shfl_xor_sync(0xffffffffu, acc[i][l], 1);
-                    if (valid && half == 0 && t < cq[i]) {
-                        float dot = acc[i][0];
-                        dot += acc[i][1];
-                        dot += acc[i][2];
-                        dot += acc[i][3];
-#pragma unroll
-                        for (int l = 0; l < 4; ++l) dot += hi[l];
-                        if (kvt == 2) dot = dot * ksc;
-                        sc[i * mctx + t] = dot / sqrtf((float)HD);
-                    }
+                    const float2 a01 = f2_unpack(acc[i][0]), a23 = f2_unpack(acc[i][1]);
+                    const float hi0 = __shfl_xor_sync(0xffffffffu, a01.x, 1);
+                    const float hi1 = __shfl_xor_sync(0xffffffffu, a01.y, 1);
+                    const float hi2 = __shfl_xor_sync(0xffffffffu, a23.x, 1);
+                    const float hi3 = __shfl_xor_sync(0xffffffffu, a23.y, 1);
+                    float dot = a01.x;
+                    dot += a01.y;
+                    dot += a23.x;
+                    dot += a23.y;
+                    dot += hi0;
+                    dot += hi1;
+                    dot += hi2;
+                    dot += hi3;
+                    if (KVT == 2) dot = dot * ksc;
+                    dots[i] = dot;  // divided by sqrt(hd) in the max pass below
                 }
+                if (valid && half == 0) st_row<QG>(sc + (size_t)t * QG, dots);
             }
         }
         cp_async_wait<0>();
     }
-    if (kvt == 2) {
+    if constexpr (KVT == 2) {
         for (int t = tid; t < cmax; t += HD) vsc[t] = a.v_scales[slot_of(t)];
-    } else if (kvt == 3) {
+    } else if constexpr (KVT == 3) {
         for (int i = tid; i < cmax * (HD / 32); i += HD) {
             const int t = i / (HD / 32), b = i % (HD / 32);
             vsc[i] = a.v_scales[slot_of(t) * (kv_dim / 32) + kh * (HD / 32) + b];
@@ -509,132 +580,160 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
     }
     __syncthreads();  // every K tile is consumed: the ring is free for V
 
-    // 2. per query: max, exp, double denominator, alpha_t = e_t * float(1/den)
+    // 2. per query: s_t = dot_t / sqrt(hd), max, exp, double denominator,
+    // alpha_t = e_t * float(1/den); thread tid visits tokens tid, tid + hd, ...
+    // for every query (each query's own sums in that order, as the one-query
+    // kernel's)
     float m[QG];
 #pragma unroll
+    for (int i = 0; i < QG; ++i) m[i] = -INFINITY;
+    for (int t = tid; t < cmax; t += HD) {
+        float w[QG];
+        ld_row<QG>(sc + (size_t)t * QG, w);
+#pragma unroll
+        for (int i = 0; i < QG; ++i) {
+            w[i] = w[i] / sqrtf((float)HD);
+            if (t < cq[i]) m[i] = fmaxf(m[i], w[i]);
+        }
+        st_row<QG>(sc + (size_t)t * QG, w);
+    }
+#pragma unroll
     for (int i = 0; i < QG; ++i) {
-        float v = -INFINITY;
-        for (int t = tid; t < cq[i]; t += HD) v = fmaxf(v, sc[i * mctx + t]);
-        v = warp_max(v);
+        const float v = warp_max(m[i]);
         if (lane == 0) redf[i][warp] = v;
     }
     __syncthreads();
+    double den[QG];
 #pragma unroll
     for (int i = 0; i < QG; ++i) {
         m[i] = redf[i][0];
 #pragma unroll
         for (int w = 1; w < HD / 32; ++w) m[i] = fmaxf(m[i], redf[i][w]);
-        double den = 0.0;
-        for (int t = tid; t < cq[i]; t += HD) {
-            const float e = expf_cr(sc[i * mctx + t] - m[i]);
-            sc[i * mctx + t] = e;
-            den += (double)e;
-        }
-        den = warp_sum_d(den);
-        if (lane == 0) redd[i][warp] = den;
+        den[i] = 0.0;
     }
-    __syncthreads();
+    for (int t = tid; t < cmax; t += HD) {
+        float w[QG];
+        ld_row<QG>(sc + (size_t)t * QG, w);
+#pragma unroll
+        for (int i = 0; i < QG; ++i) {
+            if (t < cq[i]) {
+                w[i] = expf_cr(w[i] - m[i]);
+                den[i] += (double)w[i];
+            }
+        }
+        st_row<QG>(sc + (size_t)t * QG, w);
+    }
 #pragma unroll
     for (int i = 0; i < QG; ++i) {
-        double den = 0.0;
+        const double d = warp_sum_d(den[i]);
+        if (lane == 0) redd[i][warp] = d;
+    }
+    __syncthreads();
+    float inv[QG];
 #pragma unroll
-        for (int w = 0; w < HD / 32; ++w) den += redd[i][w];
-        const float inv = (float)(1.0 / den);
-        for (int t = tid; t < cq[i]; t += HD) sc[i * mctx + t] = sc[i * mctx + t] * inv;
+    for (int i = 0; i < QG; ++i) {
+        double d = 0.0;
+#pragma unroll
+        for (int w = 0; w < HD / 32; ++w) d += redd[i][w];
+        inv[i] = (float)(1.0 / d);
+    }
+    for (int t = tid; t < cmax; t += HD) {
+        float w[QG];
+        ld_row<QG>(sc + (size_t)t * QG, w);
+#pragma unroll
+        for (int i = 0; i < QG; ++i) w[i] = w[i] * inv[i];
+        st_row<QG>(sc + (size_t)t * QG, w);
     }
 
-    // 3. thread d: out_q,d = fma(alpha_q,t, v_t[d], out_q,d) over t < ctx_q in order
-    const int chunks = kVTile * slice / 16;
+    // 3. thread d: out_q,d = fma(alpha_q,t, v_t[d], out_q,d) over t < ctx_q in
+    // order, queries (2p, 2p+1) in one packed FMA
+    constexpr int kChunks = kVTile * kSlice / 16;
     const int ntile = (cmax + kVTile - 1) / kVTile;
     auto issue_v = [&](int tile) {
         if (tile < ntile) {
-            uint8_t* dst = ring + (size_t)(tile % kVStages) * kVTile * slice;
-            for (int c = tid; c < chunks; c += HD) {
-                const int tt = c / (slice / 16), off = (c % (slice / 16)) * 16;
+            uint8_t* dst = ring + (size_t)(tile % kVStages) * kVTile * kSlice;
+#pragma unroll
+            for (int c0 = 0; c0 < kChunks; c0 += HD) {
+                const int c = c0 + tid;
+                const int tt = c / (kSlice / 16), off = (c % (kSlice / 16)) * 16;
                 const int t = tile * kVTile + tt;
-                if (t < cmax) cp_async16(dst + tt * slice + off, vp + slot_of(t) * row_bytes + head_off + off);
+                if ((kChunks % HD == 0 || c < kChunks) && t < cmax)
+                    cp_async16(dst + tt * kSlice + off, vp + slot_of(t) * row_bytes + head_off + off);
             }
         }
         cp_async_commit();
     };
-    for (int k = 0; k < kVStages - 1; ++k) issue_v(k);
-    float out[QG];
 #pragma unroll
-    for (int i = 0; i < QG; ++i) out[i] = 0.0f;
+    for (int k = 0; k < kVStages - 1; ++k) issue_v(k);
+    uint64_t out[QG / 2];
+#pragma unroll
+    for (int p = 0; p < QG / 2; ++p) out[p] = 0ull;
     for (int tile = 0; tile < ntile; ++tile) {
         cp_async_wait<kVStages - 2>();
         __syncthreads();  // the tile (and, first time round, every alpha) is visible
-        const uint8_t* vt = ring + (size_t)(tile % kVStages) * kVTile * slice;
+        const uint8_t* vt = ring + (size_t)(tile % kVStages) * kVTile * kSlice;
         const int n = min(kVTile, cmax - tile * kVTile);
         auto vload = [&](int tt, float& v, float& vs) {
             const int t = tile * kVTile + tt;
             vs = 1.0f;
-            if (kvt == 1) v = half_bits_to_float(reinterpret_cast<const uint16_t*>(vt + tt * slice)[tid]);
-            else if (kvt == 0) v = reinterpret_cast<const float*>(vt + tt * slice)[tid];
+            if constexpr (KVT == 1) v = half_bits_to_float(reinterpret_cast<const uint16_t*>(vt + tt * kSlice)[tid]);
+            else if constexpr (KVT == 0) v = reinterpret_cast<const float*>(vt + tt * kSlice)[tid];
             else {
-                v = (float)reinterpret_cast<const int8_t*>(vt + tt * slice)[tid];
-                vs = kvt == 2 ? vsc[t] : vsc[t * (HD / 32) + tid / 32];
-            }
-        };
-        auto vstep = [&](int tt, float v, float vs) {
-            const int t = tile * kVTile + tt;
-#pragma unroll
-            for (int i = 0; i < QG; ++i) {
-                if (t < cq[i]) {
-                    float al = sc[i * mctx + t];
-                    if (kvt >= 2) al = al * vs;
-                    out[i] = fmaf(al, v, out[i]);
-                }
+                v = (float)reinterpret_cast<const int8_t*>(vt + tt * kSlice)[tid];
+                vs = KVT == 2 ? vsc[t] : vsc[t * (HD / 32) + tid / 32];
             }
         };
         // tokens every query of the group sees, 8 at a time: all their loads
         // go out before the chain steps (each query's steps stay in token order)
         const int nall = max(0, min(n, cmin - tile * kVTile));
+        const float* wt = sc + (size_t)tile * kVTile * QG;
         int tt = 0;
-        if (kvt < 2 && (mctx & 3) == 0) {  // weights as float4 runs (16-byte aligned rows)
-            for (; tt + 8 <= nall; tt += 8) {
-                float v[8], vs;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) vload(tt + j, v[j], vs);
-#pragma unroll
-                for (int i = 0; i < QG; ++i) {
-                    const float* al = sc + i * mctx + tile * kVTile + tt;
-                    const float4 a0 = *reinterpret_cast<const float4*>(al);
-                    const float4 a1 = *reinterpret_cast<const float4*>(al + 4);
-                    const float aj[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) out[i] = fmaf(aj[j], v[j], out[i]);
-                }
-            }
-        }
         for (; tt + 8 <= nall; tt += 8) {
-            float v[8], vs[8], al[QG][8];
+            float v[8], vs[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) vload(tt + j, v[j], vs[j]);
 #pragma unroll
-            for (int i = 0; i < QG; ++i)
+            for (int j = 0; j < 8; ++j) {
+                uint64_t w[QG / 2];
+                ld_pairs<QG>(wt + (tt + j) * QG, w);
+                const uint64_t vv = f2_pack(v[j], v[j]);
+                if constexpr (KVT >= 2) {
+                    const uint64_t ss = f2_pack(vs[j], vs[j]);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    al[i][j] = sc[i * mctx + tile * kVTile + tt + j];
-                    if (kvt >= 2) al[i][j] = al[i][j] * vs[j];
+                    for (int p = 0; p < QG / 2; ++p) w[p] = f2_mul(w[p], ss);
                 }
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-#pragma unroll
-                for (int i = 0; i < QG; ++i) out[i] = fmaf(al[i][j], v[j], out[i]);
+                for (int p = 0; p < QG / 2; ++p) out[p] = f2_fma(w[p], vv, out[p]);
+            }
         }
         for (; tt < n; ++tt) {
             float v, vs;
             vload(tt, v, vs);
-            vstep(tt, v, vs);
+            const int t = tile * kVTile + tt;
+            float w[QG];
+            ld_row<QG>(wt + tt * QG, w);
+#pragma unroll
+            for (int p = 0; p < QG / 2; ++p) {
+                float2 o = f2_unpack(out[p]);
+                if (t < cq[2 * p]) o.x = fmaf(KVT >= 2 ? w[2 * p] * vs : w[2 * p], v, o.x);
+                if (t < cq[2 * p + 1]) o.y = fmaf(KVT >= 2 ? w[2 * p + 1] * vs : w[2 * p + 1], v, o.y);
+                out[p] = f2_pack(o.x, o.y);
+            }
         }
         __syncthreads();
         issue_v(tile + kVStages - 1);
     }
     cp_async_wait<0>();
+    float res[QG];
+#pragma unroll
+    for (int p = 0; p < QG / 2; ++p) {
+        const float2 o = f2_unpack(out[p]);
+        res[2 * p] = o.x;
+        res[2 * p + 1] = o.y;
+    }
 #pragma unroll
     for (int i = 0; i < QG; ++i)
-        if (s0 + i < (int)a.n_seq) a.out[((size_t)(s0 + i) * a.n_head + h) * HD + tid] = out[i];
+        if (s0 + i < (int)a.n_seq) a.out[((size_t)(s0 + i) * a.n_head + h) * HD + tid] = res[i];
     if (a.xq) {
         // the o projection's Q8 input, as quantize_q8_t_kernel lays it out:
         // warp w holds 32-element block (h*HD + 32w)/32 of every query row
@@ -645,7 +744,7 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
         for (int i = 0; i < QG; ++i) {
             if (s0 + i < (int)a.n_seq) {  // warp-uniform
                 float dd;
-                const int v = quant_q8_lane(out[i], dd);
+                const int v = quant_q8_lane(res[i], dd);
                 const size_t at = (size_t)(s0 + i) * D + (size_t)h * HD + tid;
                 if (a.xq_f16) reinterpret_cast<uint16_t*>(a.xq)[at] = __half_as_ushort(__int2half_rn(v));
                 else a.xq[at] = (int8_t)v;
@@ -656,7 +755,7 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
                 }
             }
         }
-        if (blockIdx.x == 0) {  // token rows n_seq..ldb-1 of this block: zero
+        if (grp == 0) {  // token rows n_seq..ldb-1 of this block: zero
             for (uint64_t r = a.n_seq + lane; r < ldb; r += 32) {
                 a.xdT[blk * ldb + r] = 0.0f;
                 cT[blk * ldb + r] = 0.0f;
@@ -978,18 +1077,28 @@ cudaError_t paged_attn_decode(const AttnArgs& a, cudaStream_t s) {
 }
 
 namespace {
-template <int HD, int QG>
+template <int HD, int QG, int KVT>
 cudaError_t launch_group(const AttnArgs& a, size_t smem, cudaStream_t s) {
-    dim3 grid((unsigned)((a.n_seq + QG - 1) / QG), (unsigned)a.n_head);
-    ensure_smem_attr(attn_group_kernel<HD, QG>, 200 * 1024);
-    return launch_pdl(attn_group_kernel<HD, QG>, grid, dim3(HD), smem, s, a);
+    dim3 grid((unsigned)a.n_head, (unsigned)((a.n_seq + QG - 1) / QG));
+    ensure_smem_attr(attn_group_kernel<HD, QG, KVT>, 200 * 1024);
+    return launch_pdl(attn_group_kernel<HD, QG, KVT>, grid, dim3(HD), smem, s, a);
+}
+template <int HD, int QG>
+cudaError_t launch_group_kv(const AttnArgs& a, size_t smem, cudaStream_t s) {
+    switch (a.kv_type) {
+        case 0: return launch_group<HD, QG, 0>(a, smem, s);
+        case 1: return launch_group<HD, QG, 1>(a, smem, s);
+        case 2: return launch_group<HD, QG, 2>(a, smem, s);
+        case 3: return launch_group<HD, QG, 3>(a, smem, s);
+        default: return cudaErrorInvalidValue;
+    }
 }
 template <int QG>
 cudaError_t launch_group_hd(const AttnArgs& a, size_t smem, cudaStream_t s) {
     switch (a.hd) {
-        case 64: return launch_group<64, QG>(a, smem, s);
-        case 128: return launch_group<128, QG>(a, smem, s);
-        case 256: return launch_group<256, QG>(a, smem, s);
+        case 64: return launch_group_kv<64, QG>(a, smem, s);
+        case 128: return launch_group_kv<128, QG>(a, smem, s);
+        case 256: return launch_group_kv<256, QG>(a, smem, s);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -1008,7 +1117,10 @@ cudaError_t paged_attn_prefill(const AttnArgs& a, cudaStream_t s) {
                    : a.n_seq >= 2                          ? 2
                                                            : 1;
     const size_t smem = qg > 1 ? attn_group_plan(a.hd, a.max_ctx ? a.max_ctx : 1, a.max_pages, a.kv_type, qg).total : 0;
-    if (qg == 1 || smem > 200 * 1024) {
+    // the group kernel finds a token's page by a 32-bit multiply (exact while
+    // (max_ctx + page) * page < 2^32) and numbers its groups in grid.y
+    const bool fits = (a.max_ctx + a.page) * a.page < (1ull << 32) && (a.n_seq + qg - 1) / qg <= 65535;
+    if (qg == 1 || smem > 200 * 1024 || !fits) {
         cudaError_t e = paged_attn_decode(a, s);
         if (e == cudaSuccess && a.xq)
             e = quantize_q8_rows_t(a.out, a.n_seq, a.n_head * a.hd, a.xq, a.xdT, a.xq_ldb, s,

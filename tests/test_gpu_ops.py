@@ -189,15 +189,17 @@ def test_config4_ragged_paged_attention(cuda, oracle, kv_type):
 
 
 @pytest.mark.parametrize("kv_type", [mv.KV_F16, mv.KV_Q8, mv.KV_Q8_0, mv.KV_F32])
-@pytest.mark.parametrize("n_q,n_head,n_head_kv,hd", [(32, 32, 32, 128), (30, 32, 8, 128), (64, 32, 4, 64),
-                                                     (16, 16, 2, 256), (83, 32, 8, 128)])
-def test_prefill_attention_groups(cuda, oracle, kv_type, n_q, n_head, n_head_kv, hd):
+@pytest.mark.parametrize("n_q,n_head,n_head_kv,hd,page", [(32, 32, 32, 128, 16), (30, 32, 8, 128, 1),
+                                                          (64, 32, 4, 64, 16), (16, 16, 2, 256, 16),
+                                                          (83, 32, 8, 128, 13)])
+def test_prefill_attention_groups(cuda, oracle, kv_type, n_q, n_head, n_head_kv, hd, page):
     """A prefill chunk: n_q causal query rows of one sequence (row i sees
-    start + i + 1 tokens) over scattered 16-token pages.  The grouped kernel
-    (query rows sharing each staged K/V tile) must equal the one-query kernel
-    bit for bit, and the oracle's reference loop within 1e-4."""
+    start + i + 1 tokens) over scattered pages (16 tokens, one token, and 13
+    tokens: the kernel's page lookup by multiply).  The grouped kernel (query
+    rows sharing each staged K/V tile) must equal the one-query kernel bit for
+    bit, and the oracle's reference loop within 1e-4."""
     rng = np.random.default_rng(50 + kv_type + n_q + hd)
-    page, start = 16, 437
+    start = 437
     kv_dim = n_head_kv * hd
     n_ctx = start + n_q
     max_pages = (n_ctx + page - 1) // page

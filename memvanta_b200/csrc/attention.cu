@@ -348,6 +348,9 @@ __global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
 // by warp, alpha_t = e_t * float(1/den), the same per-dimension FMA chain over
 // its own tokens in order -- so the outputs are identical to it bit for bit.
 // Query q of the group sees tokens t < ctx_len[s0 + q] (causal prefill).
+// One K tile and three V stages (45 KB for hd 128, F16, 8 queries over 512
+// tokens: five CTAs per SM, four with a double-buffered K tile)
+constexpr int kGroupVStages = 3;
 struct AttnGroupSmem {
     uint64_t q, table, sc, vsc, ring, total;
 };
@@ -356,8 +359,8 @@ __host__ __device__ inline AttnGroupSmem attn_group_plan(uint64_t hd, uint64_t m
     auto up = [](uint64_t n) { return (n + 15) / 16 * 16; };
     const uint64_t esize = kv_type == 0 ? 4 : kv_type == 1 ? 2 : 1;
     const uint64_t krow = hd * esize + 16;
-    const uint64_t kring = 2 * (uint64_t)attn_ktile(hd, kv_type) * krow;
-    const uint64_t vring = (uint64_t)kVStages * kVTile * hd * esize;
+    const uint64_t kring = (uint64_t)attn_ktile(hd, kv_type) * krow;  // one K tile
+    const uint64_t vring = (uint64_t)kGroupVStages * kVTile * hd * esize;
     const uint64_t nsc = kv_type == 2 ? 1 : kv_type == 3 ? hd / 32 : 0;
     AttnGroupSmem p;
     p.q = 0;
@@ -437,8 +440,6 @@ __device__ __forceinline__ void st_row(float* p, const float (&w)[QG]) {
 template <int HD, int QG, int KVT>
 __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ float redf[QG][HD / 32];
-    __shared__ double redd[QG][HD / 32];
     constexpr int kEs = KVT == 0 ? 4 : KVT == 1 ? 2 : 1;
     constexpr int kSlice = HD * kEs;  // bytes of one head's K or V row
     constexpr int kKT = attn_ktile(HD, KVT);
@@ -456,6 +457,10 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
     float* sc = reinterpret_cast<float*>(smem + P.sc);  // [max_ctx][QG]: token-major
     float* vsc = reinterpret_cast<float*>(smem + P.vsc);
     uint8_t* ring = smem + P.ring;
+    // the softmax's cross-warp reductions live in the ring while no K or V
+    // tile is staged (between the last K tile and the first V copy)
+    auto redd = reinterpret_cast<double(*)[HD / 32]>(ring);
+    auto redf = reinterpret_cast<float(*)[HD / 32]>(ring + QG * (HD / 32) * sizeof(double));
     const uint8_t* kp = static_cast<const uint8_t*>(a.k_pages);
     const uint8_t* vp = static_cast<const uint8_t*>(a.v_pages);
     const size_t row_bytes = (size_t)kv_dim * kEs;
@@ -498,12 +503,11 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
             cp_async_commit();
         };
         const int ntile = (cmax + kKT - 1) / kKT;
-        issue_k(0, 0);
         for (int tile = 0; tile < ntile; ++tile) {
+            if (tile) __syncthreads();  // tile-1's rows are no longer read
+            issue_k(tile, 0);
             cp_async_wait<0>();  // this thread's copies of the tile have landed
-            __syncthreads();     // ... every thread's; and tile-1's rows are no longer read
-            if (tile + 1 < ntile) issue_k(tile + 1, (tile + 1) & 1);
-            else cp_async_commit();
+            __syncthreads();     // ... every thread's
             // a pair of lanes per token: the even lane accumulates the reference's
             // lanes 0..3 (elements d..d+3 of every 8), the odd lane lanes 4..7,
             // as two packed pairs (lanes 0,1 and 2,3); the odd lane's four sums
@@ -512,7 +516,7 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
             for (int tk = warp * 16 + (lane >> 1); tk < kKT; tk += (HD / 32) * 16) {  // warp-uniform trips
                 const int t = tile * kKT + tk;
                 const bool valid = t < cmax;
-                const uint8_t* row = ring + ((size_t)(tile & 1) * kKT + tk) * kRow + 4 * half * kEs;
+                const uint8_t* row = ring + (size_t)tk * kRow + 4 * half * kEs;
                 const float* qh = qs + 4 * half;
                 uint64_t acc[QG][2];
 #pragma unroll
@@ -644,6 +648,7 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
         for (int i = 0; i < QG; ++i) w[i] = w[i] * inv[i];
         st_row<QG>(sc + (size_t)t * QG, w);
     }
+    __syncthreads();  // redd is read: the ring takes V tiles
 
     // 3. thread d: out_q,d = fma(alpha_q,t, v_t[d], out_q,d) over t < ctx_q in
     // order, queries (2p, 2p+1) in one packed FMA
@@ -651,7 +656,7 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
     const int ntile = (cmax + kVTile - 1) / kVTile;
     auto issue_v = [&](int tile) {
         if (tile < ntile) {
-            uint8_t* dst = ring + (size_t)(tile % kVStages) * kVTile * kSlice;
+            uint8_t* dst = ring + (size_t)(tile % kGroupVStages) * kVTile * kSlice;
 #pragma unroll
             for (int c0 = 0; c0 < kChunks; c0 += HD) {
                 const int c = c0 + tid;
@@ -664,14 +669,14 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
         cp_async_commit();
     };
 #pragma unroll
-    for (int k = 0; k < kVStages - 1; ++k) issue_v(k);
+    for (int k = 0; k < kGroupVStages - 1; ++k) issue_v(k);
     uint64_t out[QG / 2];
 #pragma unroll
     for (int p = 0; p < QG / 2; ++p) out[p] = 0ull;
     for (int tile = 0; tile < ntile; ++tile) {
-        cp_async_wait<kVStages - 2>();
+        cp_async_wait<kGroupVStages - 2>();
         __syncthreads();  // the tile (and, first time round, every alpha) is visible
-        const uint8_t* vt = ring + (size_t)(tile % kVStages) * kVTile * kSlice;
+        const uint8_t* vt = ring + (size_t)(tile % kGroupVStages) * kVTile * kSlice;
         const int n = min(kVTile, cmax - tile * kVTile);
         auto vload = [&](int tt, float& v, float& vs) {
             const int t = tile * kVTile + tt;
@@ -721,7 +726,7 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
             }
         }
         __syncthreads();
-        issue_v(tile + kVStages - 1);
+        issue_v(tile + kGroupVStages - 1);
     }
     cp_async_wait<0>();
     float res[QG];

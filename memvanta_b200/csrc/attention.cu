@@ -348,11 +348,11 @@ __global__ void __launch_bounds__(HD) attn_exact_kernel(AttnArgs a) {
 // by warp, alpha_t = e_t * float(1/den), the same per-dimension FMA chain over
 // its own tokens in order -- so the outputs are identical to it bit for bit.
 // Query q of the group sees tokens t < ctx_len[s0 + q] (causal prefill).
-// One K tile and three V stages (45 KB for hd 128, F16, 8 queries over 512
-// tokens: five CTAs per SM, four with a double-buffered K tile)
-constexpr int kGroupVStages = 3;
+// One K tile and two V stages, the block table read through L1 (37,888 bytes
+// for hd 128, F16, 8 queries over 512 tokens: six CTAs per SM)
+constexpr int kGroupVStages = 2;
 struct AttnGroupSmem {
-    uint64_t q, table, sc, vsc, ring, total;
+    uint64_t q, sc, vsc, ring, total;
 };
 __host__ __device__ inline AttnGroupSmem attn_group_plan(uint64_t hd, uint64_t max_ctx, uint64_t max_pages,
                                                          int kv_type, int qg) {
@@ -364,8 +364,7 @@ __host__ __device__ inline AttnGroupSmem attn_group_plan(uint64_t hd, uint64_t m
     const uint64_t nsc = kv_type == 2 ? 1 : kv_type == 3 ? hd / 32 : 0;
     AttnGroupSmem p;
     p.q = 0;
-    p.table = up((uint64_t)qg * hd * 4);
-    p.sc = p.table + up(max_pages * 4);
+    p.sc = up((uint64_t)qg * hd * 4);
     p.vsc = p.sc + up((uint64_t)qg * max_ctx * 4);
     p.ring = p.vsc + up(max_ctx * nsc * 4);
     p.total = p.ring + (kring > vring ? kring : vring);
@@ -453,7 +452,6 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
     const PageDiv pdiv(a.page);
     const AttnGroupSmem P = attn_group_plan(HD, a.max_ctx, a.max_pages, KVT, QG);
     float* qs = reinterpret_cast<float*>(smem + P.q);  // [QG][HD]
-    int* tbl = reinterpret_cast<int*>(smem + P.table);
     float* sc = reinterpret_cast<float*>(smem + P.sc);  // [max_ctx][QG]: token-major
     float* vsc = reinterpret_cast<float*>(smem + P.vsc);
     uint8_t* ring = smem + P.ring;
@@ -476,16 +474,14 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
         cmax = max(cmax, cq[i]);
         cmin = min(cmin, cq[i]);
     }
-    const int npg = (int)pdiv.index((uint32_t)cmax + pdiv.page - 1);
-    const size_t trow = a.one_seq ? 0 : (size_t)s0;
-    for (int i = tid; i < npg; i += HD) tbl[i] = a.block_table[trow * a.max_pages + i];
+    const int32_t* tbl = a.block_table + (a.one_seq ? 0 : (size_t)s0) * a.max_pages;
 #pragma unroll
     for (int i = 0; i < QG; ++i)
         qs[i * HD + tid] = cq[i] > 0 ? a.q[(size_t)(s0 + i) * a.q_stride + (size_t)h * HD + tid] : 0.0f;
     __syncthreads();
     auto slot_of = [&](int t) -> size_t {
         const uint32_t pi = pdiv.index((uint32_t)t);
-        return (size_t)tbl[pi] * pdiv.page + ((uint32_t)t - pi * pdiv.page);
+        return (size_t)__ldg(tbl + pi) * pdiv.page + ((uint32_t)t - pi * pdiv.page);
     };
 
     // 1. raw dot products of every query with tokens 0..cmax-1: a K tile's rows
@@ -668,14 +664,14 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
         }
         cp_async_commit();
     };
-#pragma unroll
-    for (int k = 0; k < kGroupVStages - 1; ++k) issue_v(k);
+    issue_v(0);
     uint64_t out[QG / 2];
 #pragma unroll
     for (int p = 0; p < QG / 2; ++p) out[p] = 0ull;
     for (int tile = 0; tile < ntile; ++tile) {
-        cp_async_wait<kGroupVStages - 2>();
-        __syncthreads();  // the tile (and, first time round, every alpha) is visible
+        cp_async_wait<0>();
+        __syncthreads();    // the tile (and, first time round, every alpha) is visible, and
+        issue_v(tile + 1);  // the other stage (tile - 1) is read by no one: it takes tile + 1
         const uint8_t* vt = ring + (size_t)(tile % kGroupVStages) * kVTile * kSlice;
         const int n = min(kVTile, cmax - tile * kVTile);
         auto vload = [&](int tt, float& v, float& vs) {
@@ -725,8 +721,6 @@ __global__ void __launch_bounds__(HD) attn_group_kernel(AttnArgs a) {
                 out[p] = f2_pack(o.x, o.y);
             }
         }
-        __syncthreads();
-        issue_v(tile + kGroupVStages - 1);
     }
     cp_async_wait<0>();
     float res[QG];

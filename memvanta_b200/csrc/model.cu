@@ -49,24 +49,74 @@ namespace mvb {
 // 32-element block).  Grid (rows, ceil((n_head + 2*n_head_kv) / upc)): each
 // CTA takes upc units -- a q head (rotate), k head (rotate + store) or v head
 // (store).  ctx_out (optional) receives pos+1 for the attention that follows.
+constexpr int kRopeUnits = 6;  // units a thread holds at once in the F32/F16 path
 __global__ void rope_append_heads_kernel(float* __restrict__ qkv, int ld, int n_head, int n_head_kv, int hd,
                                          const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                          const int32_t* __restrict__ pos, int kv_type, const int32_t* __restrict__ table, int table_ld,
                                          int page, uint8_t* __restrict__ k_pages, uint8_t* __restrict__ v_pages,
                                          float* __restrict__ k_scales, float* __restrict__ v_scales,
                                          int32_t* __restrict__ ctx_out, int upc) {
-    // upc units per CTA, blockDim.x / upc threads each
-    const int T = (int)blockDim.x / upc, sub = (int)threadIdx.x / T, tt = (int)threadIdx.x % T;
-    const int r = blockIdx.x, unit = (int)blockIdx.y * upc + sub, half = hd / 2, KV = n_head_kv * hd;
-    const bool valid = unit < n_head + 2 * n_head_kv;
+    // upc units per CTA, taken four at a time (blockDim.x / 4 threads each): a
+    // prefill batch gives each CTA many heads, so the chain position ->
+    // cos/sin -> block table is waited for once per many heads
+    const int nsub = 4, T = (int)blockDim.x / nsub, sub = (int)threadIdx.x / T, tt = (int)threadIdx.x % T;
+    const int units = n_head + 2 * n_head_kv;
+    const int r = blockIdx.x, u0 = (int)blockIdx.y * upc, uend = min(u0 + upc, units), half = hd / 2,
+              KV = n_head_kv * hd;
     pdl_trigger();
     pdl_wait();
     float* row = qkv + (size_t)r * ld;
     const int p = pos[r];
-    float* b = row + (size_t)unit * hd;  // q heads, then k heads, then v heads
-    if (valid && unit < n_head + n_head_kv) {
-        const float* co = cos_t + (size_t)p * half;
-        const float* si = sin_t + (size_t)p * half;
+    const float* co = cos_t + (size_t)p * half;
+    const float* si = sin_t + (size_t)p * half;
+    if (kv_type <= 1 && T == half && upc <= kRopeUnits * nsub) {
+        // F32 / F16 pages: thread tt holds the pair (tt, tt + half) of each of
+        // its units -- all loads first, then the rotation (q and k heads,
+        // written back) and the append (k and v heads) from registers
+        const int nrot = n_head + n_head_kv;
+        const size_t slot = uend > n_head ? (size_t)table[(size_t)r * table_ld + p / page] * page + p % page : 0;
+        const float c = co[tt], s = si[tt];
+        float x0[kRopeUnits], x1[kRopeUnits];
+#pragma unroll
+        for (int k = 0; k < kRopeUnits; ++k) {
+            const int unit = u0 + sub + k * nsub;
+            if (unit < uend) {
+                x0[k] = row[(size_t)unit * hd + tt];
+                x1[k] = row[(size_t)unit * hd + tt + half];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kRopeUnits; ++k) {
+            const int unit = u0 + sub + k * nsub;
+            if (unit >= uend) continue;
+            float y0 = x0[k], y1 = x1[k];
+            if (unit < nrot) {
+                y0 = __fmaf_rn(x0[k], c, -__fmul_rn(x1[k], s));
+                y1 = __fmaf_rn(x0[k], s, __fmul_rn(x1[k], c));
+                row[(size_t)unit * hd + tt] = y0;
+                row[(size_t)unit * hd + tt + half] = y1;
+            }
+            if (unit >= n_head) {
+                const bool is_v = unit >= nrot;
+                const int head = unit - n_head - (is_v ? n_head_kv : 0);
+                const size_t base = slot * KV + (size_t)head * hd;
+                if (kv_type == 0) {
+                    float* dst = reinterpret_cast<float*>(is_v ? v_pages : k_pages) + base;
+                    dst[tt] = y0;
+                    dst[tt + half] = y1;
+                } else {
+                    uint16_t* dst = reinterpret_cast<uint16_t*>(is_v ? v_pages : k_pages) + base;
+                    dst[tt] = f32_to_f16_ref(y0);
+                    dst[tt + half] = f32_to_f16_ref(y1);
+                }
+            }
+        }
+        if (ctx_out && blockIdx.y == 0 && threadIdx.x == 0) ctx_out[r] = p + 1;
+        return;
+    }
+#pragma unroll 2
+    for (int unit = u0 + sub; unit < min(uend, n_head + n_head_kv); unit += nsub) {  // q heads, then k heads
+        float* b = row + (size_t)unit * hd;
         for (int j = tt; j < half; j += T) {
             const float x0 = b[j], x1 = b[j + half], c = co[j], s = si[j];
             b[j] = __fmaf_rn(x0, c, -__fmul_rn(x1, s));
@@ -74,30 +124,33 @@ __global__ void rope_append_heads_kernel(float* __restrict__ qkv, int ld, int n_
         }
     }
     __syncthreads();
-    if (valid && unit >= n_head) {
-        const bool is_v = unit >= n_head + n_head_kv;
-        const int head = unit - n_head - (is_v ? n_head_kv : 0);
+    if (uend > n_head) {
         const size_t slot = (size_t)table[(size_t)r * table_ld + p / page] * page + p % page;
-        uint8_t* pages = is_v ? v_pages : k_pages;
-        const size_t base = slot * KV + (size_t)head * hd;
-        if (kv_type == 0) {
-            float* dst = reinterpret_cast<float*>(pages) + base;
-            for (int i = tt; i < hd; i += T) dst[i] = b[i];
-        } else if (kv_type == 1) {
-            uint16_t* dst = reinterpret_cast<uint16_t*>(pages) + base;
-            for (int i = tt; i < hd; i += T) dst[i] = f32_to_f16_ref(b[i]);
-        } else {  // Q8_0: warp per 32-element block (T is a multiple of 32)
-            float* scales = is_v ? v_scales : k_scales;
-            int8_t* dst = reinterpret_cast<int8_t*>(pages) + base;
-            const int lane = tt & 31;
-            for (int blk = tt >> 5; blk < hd / 32; blk += T >> 5) {
-                float dd;
-                dst[blk * 32 + lane] = (int8_t)quant_q8_lane(b[blk * 32 + lane], dd);
-                if (lane == 0) scales[slot * (KV / 32) + (size_t)head * (hd / 32) + blk] = dd;
+        for (int unit = max(u0, n_head) + sub; unit < uend; unit += nsub) {  // k heads, then v heads
+            const float* b = row + (size_t)unit * hd;
+            const bool is_v = unit >= n_head + n_head_kv;
+            const int head = unit - n_head - (is_v ? n_head_kv : 0);
+            uint8_t* pages = is_v ? v_pages : k_pages;
+            const size_t base = slot * KV + (size_t)head * hd;
+            if (kv_type == 0) {
+                float* dst = reinterpret_cast<float*>(pages) + base;
+                for (int i = tt; i < hd; i += T) dst[i] = b[i];
+            } else if (kv_type == 1) {
+                uint16_t* dst = reinterpret_cast<uint16_t*>(pages) + base;
+                for (int i = tt; i < hd; i += T) dst[i] = f32_to_f16_ref(b[i]);
+            } else {  // Q8_0: warp per 32-element block (T is a multiple of 32)
+                float* scales = is_v ? v_scales : k_scales;
+                int8_t* dst = reinterpret_cast<int8_t*>(pages) + base;
+                const int lane = tt & 31;
+                for (int blk = tt >> 5; blk < hd / 32; blk += T >> 5) {
+                    float dd;
+                    dst[blk * 32 + lane] = (int8_t)quant_q8_lane(b[blk * 32 + lane], dd);
+                    if (lane == 0) scales[slot * (KV / 32) + (size_t)head * (hd / 32) + blk] = dd;
+                }
             }
         }
     }
-    if (ctx_out && unit == 0 && tt == 0) ctx_out[r] = p + 1;
+    if (ctx_out && blockIdx.y == 0 && threadIdx.x == 0) ctx_out[r] = p + 1;
 }
 
 // The MV_KV_Q8 cache keeps one scale per token over all kv_dim elements, so
@@ -675,11 +728,12 @@ void rope_append(mv_model_s* m, const mvb::Layer& L, float* qkv, uint64_t rows, 
                             (const float*)m->rope_sin, pos, m->kv_type, table, table_ld, (int)m->page,
                             L.k_pages, L.v_pages, L.k_scales, L.v_scales, ctx_out);
     } else {
-        // four heads per CTA: a prefill batch has rows x (heads + 2 kv heads) units
+        // four heads at a time per CTA; a prefill batch (rows x (heads + 2 kv
+        // heads) units) gives each CTA 24 of them in turn, a decode step 4
         const int T = m->kv_type == MV_KV_Q8_0 ? (int)std::max<uint64_t>(64, m->hd) : (int)(m->hd / 2);
-        const int upc = 4, units = (int)(m->nh + 2 * m->nkv);
+        const int upc = rows >= 64 ? 24 : 4, units = (int)(m->nh + 2 * m->nkv);
         e = mvb::launch_opt(!plain, mvb::rope_append_heads_kernel,
-                            dim3((unsigned)rows, (unsigned)((units + upc - 1) / upc)), dim3(T * upc), 0,
+                            dim3((unsigned)rows, (unsigned)((units + upc - 1) / upc)), dim3(T * 4), 0,
                             m->stream, qkv, (int)QKVW, (int)m->nh, (int)m->nkv, (int)m->hd,
                             (const float*)m->rope_cos, (const float*)m->rope_sin, pos, m->kv_type,
                             table, table_ld, (int)m->page, L.k_pages, L.v_pages, L.k_scales, L.v_scales,

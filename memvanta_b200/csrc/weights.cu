@@ -182,6 +182,23 @@ __global__ void quantize_q8_kernel(const float* __restrict__ x, uint64_t nblocks
 // block dot (gemm_tc.cu).  Rows rows..ldb-1 of both are zero.
 // qh set: the values go out as fp16 (exact: |q| <= 127) to qh instead of
 // int8 to q, for the fp16 tensor-core GEMM (gemm_f16.cu).
+// Position (row, block) of block b = row * nb + block, advanced by a fixed
+// stride of blocks without a division per step.
+constexpr int kUnroll = 4;  // blocks per warp and trip in the quantisers below
+struct BlockPos {
+    uint64_t row, blk, drow, dblk, nb;
+    __device__ BlockPos(uint64_t b, uint64_t stride, uint64_t n)
+        : row(b / n), blk(b % n), drow(stride / n), dblk(stride % n), nb(n) {}
+    __device__ __forceinline__ void step() {
+        blk += dblk;
+        row += drow;
+        if (blk >= nb) {
+            blk -= nb;
+            ++row;
+        }
+    }
+};
+
 __global__ void quantize_q8_t_kernel(const float* __restrict__ x, uint64_t rows, uint64_t nb, int8_t* __restrict__ q,
                                      float* __restrict__ dT, uint64_t ldb, uint16_t* __restrict__ qh) {
     const int lane = threadIdx.x & 31;
@@ -190,16 +207,33 @@ __global__ void quantize_q8_t_kernel(const float* __restrict__ x, uint64_t rows,
     float* cT = dT + nb * ldb;
     pdl_trigger();
     pdl_wait();
-    for (uint64_t b = first; b < rows * nb; b += warps) {
-        float dd;
-        const int v = quant_q8_lane(__ldcg(x + b * 32 + lane), dd);  // L2: x may come from other GPUs
-        if (qh) qh[b * 32 + lane] = __half_as_ushort(__int2half_rn(v));
-        else q[b * 32 + lane] = (int8_t)v;
-        const int sum = warp_sum_i(v);
-        if (lane == 0) {
-            const uint64_t at = (b % nb) * ldb + b / nb;
-            dT[at] = dd;
-            cT[at] = 12582912.0f + (float)(8 * sum);
+    // kUnroll blocks per warp and trip, all loads issued before the first
+    // block is quantised (bytes in flight bound this kernel)
+    const uint64_t nbt = rows * nb;
+    BlockPos bp(first, warps, nb);
+    for (uint64_t b0 = first; b0 < nbt; b0 += kUnroll * warps) {
+        float xv[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint64_t b = b0 + u * warps;
+            xv[u] = b < nbt ? __ldcg(x + b * 32 + lane) : 0.0f;  // L2: x may come from other GPUs
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint64_t b = b0 + u * warps;
+            if (b < nbt) {  // warp-uniform
+                float dd;
+                const int v = quant_q8_lane(xv[u], dd);
+                if (qh) qh[b * 32 + lane] = __half_as_ushort(__int2half_rn(v));
+                else q[b * 32 + lane] = (int8_t)v;
+                const int sum = warp_sum_i(v);
+                if (lane == 0) {
+                    const uint64_t at = bp.blk * ldb + bp.row;
+                    dT[at] = dd;
+                    cT[at] = 12582912.0f + (float)(8 * sum);
+                }
+            }
+            bp.step();
         }
     }
     const uint64_t padw = ldb - rows, padn = nb * padw;
@@ -223,18 +257,32 @@ __global__ void silu_quantize_q8_t_kernel(const float* __restrict__ gu, uint64_t
     float* cT = dT + nb * ldb;
     pdl_trigger();
     pdl_wait();
-    for (uint64_t b = first; b < rows * nb; b += warps) {
-        const float2 p = reinterpret_cast<const float2*>(gu)[b * 32 + lane];  // (g, u) of element b*32+lane
-        const float ff = (p.x / (1.0f + expf(-p.x))) * p.y;
-        float dd;
-        const int v = quant_q8_lane(ff, dd);
-        if (qh) qh[b * 32 + lane] = __half_as_ushort(__int2half_rn(v));
-        else q[b * 32 + lane] = (int8_t)v;
-        const int sum = warp_sum_i(v);
-        if (lane == 0) {
-            const uint64_t at = (b % nb) * ldb + b / nb;
-            dT[at] = dd;
-            cT[at] = 12582912.0f + (float)(8 * sum);
+    const uint64_t nbt = rows * nb;
+    BlockPos bp(first, warps, nb);
+    for (uint64_t b0 = first; b0 < nbt; b0 += kUnroll * warps) {
+        float2 gp[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint64_t b = b0 + u * warps;  // (g, u) of element b*32+lane
+            gp[u] = b < nbt ? reinterpret_cast<const float2*>(gu)[b * 32 + lane] : make_float2(0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint64_t b = b0 + u * warps;
+            if (b < nbt) {  // warp-uniform
+                const float ff = (gp[u].x / (1.0f + expf(-gp[u].x))) * gp[u].y;
+                float dd;
+                const int v = quant_q8_lane(ff, dd);
+                if (qh) qh[b * 32 + lane] = __half_as_ushort(__int2half_rn(v));
+                else q[b * 32 + lane] = (int8_t)v;
+                const int sum = warp_sum_i(v);
+                if (lane == 0) {
+                    const uint64_t at = bp.blk * ldb + bp.row;
+                    dT[at] = dd;
+                    cT[at] = 12582912.0f + (float)(8 * sum);
+                }
+            }
+            bp.step();
         }
     }
     const uint64_t padw = ldb - rows, padn = nb * padw;

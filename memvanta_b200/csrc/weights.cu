@@ -251,34 +251,66 @@ __global__ void quantize_q8_t_kernel(const float* __restrict__ x, uint64_t rows,
 __global__ void silu_quantize_q8_t_kernel(const float* __restrict__ gu, uint64_t rows, uint64_t nb,
                                           int8_t* __restrict__ q, float* __restrict__ dT, uint64_t ldb,
                                           uint16_t* __restrict__ qh) {
-    const int lane = threadIdx.x & 31;
+    // 8 lanes per 32-element block, 4 consecutive elements each (two float4 of
+    // (g, u) pairs): a warp takes 4 blocks per step and kUnroll steps' loads at
+    // once; a block's max and sum are 3 shuffle steps within its 8 lanes
+    const int lane = threadIdx.x & 31, sub = lane >> 3, l8 = lane & 7;
     const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
     const uint64_t first = blockIdx.x * (uint64_t)(blockDim.x / 32) + threadIdx.x / 32;
     float* cT = dT + nb * ldb;
     pdl_trigger();
     pdl_wait();
-    const uint64_t nbt = rows * nb;
-    BlockPos bp(first, warps, nb);
-    for (uint64_t b0 = first; b0 < nbt; b0 += kUnroll * warps) {
-        float2 gp[kUnroll];
+    const uint64_t nbt = rows * nb, ngroups = (nbt + 3) / 4;
+    BlockPos bp(4 * first + sub, 4 * warps, nb);
+    for (uint64_t g0 = first; g0 < ngroups; g0 += kUnroll * warps) {
+        float4 pa[kUnroll], pb[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            const uint64_t b = b0 + u * warps;  // (g, u) of element b*32+lane
-            gp[u] = b < nbt ? reinterpret_cast<const float2*>(gu)[b * 32 + lane] : make_float2(0.0f, 0.0f);
+            const uint64_t b = 4 * (g0 + u * warps) + sub;
+            if (b < nbt) {
+                const float4* src = reinterpret_cast<const float4*>(gu) + b * 16 + l8 * 2;
+                pa[u] = src[0];
+                pb[u] = src[1];
+            } else {
+                pa[u] = pb[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            const uint64_t b = b0 + u * warps;
-            if (b < nbt) {  // warp-uniform
-                const float ff = (gp[u].x / (1.0f + expf(-gp[u].x))) * gp[u].y;
-                float dd;
-                const int v = quant_q8_lane(ff, dd);
-                if (qh) qh[b * 32 + lane] = __half_as_ushort(__int2half_rn(v));
-                else q[b * 32 + lane] = (int8_t)v;
-                const int sum = warp_sum_i(v);
-                if (lane == 0) {
+            const uint64_t b = 4 * (g0 + u * warps) + sub;  // the same for the block's 8 lanes
+            const float f0 = (pa[u].x / (1.0f + expf(-pa[u].x))) * pa[u].y;
+            const float f1 = (pa[u].z / (1.0f + expf(-pa[u].z))) * pa[u].w;
+            const float f2 = (pb[u].x / (1.0f + expf(-pb[u].x))) * pb[u].y;
+            const float f3 = (pb[u].z / (1.0f + expf(-pb[u].z))) * pb[u].w;
+            float mx = fmaxf(fmaxf(fabsf(f0), fabsf(f1)), fmaxf(fabsf(f2), fabsf(f3)));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            const float d = mx > 0.0f ? mx / 127.0f : 1.0f;
+            const float id = 1.0f / d;
+            const int q0 = (int)fminf(fmaxf(roundf(f0 * id), -127.0f), 127.0f);
+            const int q1 = (int)fminf(fmaxf(roundf(f1 * id), -127.0f), 127.0f);
+            const int q2 = (int)fminf(fmaxf(roundf(f2 * id), -127.0f), 127.0f);
+            const int q3 = (int)fminf(fmaxf(roundf(f3 * id), -127.0f), 127.0f);
+            int sum = q0 + q1 + q2 + q3;
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            if (b < nbt) {
+                if (qh) {
+                    const uint32_t h01 = (uint32_t)__half_as_ushort(__int2half_rn(q0)) |
+                                         ((uint32_t)__half_as_ushort(__int2half_rn(q1)) << 16);
+                    const uint32_t h23 = (uint32_t)__half_as_ushort(__int2half_rn(q2)) |
+                                         ((uint32_t)__half_as_ushort(__int2half_rn(q3)) << 16);
+                    reinterpret_cast<uint2*>(qh)[b * 8 + l8] = make_uint2(h01, h23);
+                } else {
+                    reinterpret_cast<uint32_t*>(q)[b * 8 + l8] =
+                        (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8) | ((uint32_t)(q2 & 0xFF) << 16) |
+                        ((uint32_t)(q3 & 0xFF) << 24);
+                }
+                if (l8 == 0) {
                     const uint64_t at = bp.blk * ldb + bp.row;
-                    dT[at] = dd;
+                    dT[at] = d;
                     cT[at] = 12582912.0f + (float)(8 * sum);
                 }
             }
@@ -403,7 +435,7 @@ cudaError_t silu_quantize_q8_rows_t(const float* gu, uint64_t rows, uint64_t col
                                     cudaStream_t s, uint16_t* qh) {
     const uint64_t nblocks = rows * (cols / 32);
     if (!nblocks || ldb < rows || cols % 32) return nblocks ? cudaErrorInvalidValue : cudaSuccess;
-    const uint64_t ctas = (nblocks + 7) / 8;
+    const uint64_t ctas = (nblocks + 31) / 32;  // 8 warps of 4 blocks
     const uint64_t cap = (uint64_t)num_sms() * 8;
     return launch_pdl(silu_quantize_q8_t_kernel, dim3((unsigned)(ctas < cap ? ctas : cap)), dim3(256), 0, s, gu, rows,
                       cols / 32, q, dT, ldb, qh);

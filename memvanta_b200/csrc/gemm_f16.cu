@@ -341,16 +341,18 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                     break;
                 }
                 const unsigned char* ed = sm + C::kEpiOff + e * C::kEpi;
-                const uint4 w0 = *reinterpret_cast<const uint4*>(ed + rr * 32 + ((0 ^ dsw) << 4));
-                const uint4 w1 = *reinterpret_cast<const uint4*>(ed + rr * 32 + ((1 ^ dsw) << 4));
-                const uint32_t dwp[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                // this row's 16 fp16 weight scales: blocks 8c..8c+7 in 16-byte chunk c ^ dsw
+                const unsigned char* dwrow = ed + rr * 32;
                 const float* da = reinterpret_cast<const float*>(ed + C::kDw);  // [16][NT]
                 const int neb = a.nb - b16 < kEB ? a.nb - b16 : kEB;
-                // a stage's two blocks per TMEM round trip: both slots loaded, one wait
-                for (int eb = 0; eb < neb; eb += 2, ++ke) {
+                // the group's pairs unrolled; a stage's two blocks per TMEM round trip
+                // (LB = 2: both slots loaded, one wait) or, at 128 tokens, each
+                // block in two 16-column halves (registers: no spills)
+#pragma unroll
+                for (int eb = 0; eb < kEB; eb += 2, ++ke) {
+                    if (eb >= neb) break;                        // warp-uniform
                     const int nl = neb - eb < 2 ? neb - eb : 2;  // warp-uniform
                     const uint32_t pr = ke % C::kPairs;
-                    uint32_t v[LB][TT];
                     // warp-uniform outcome: the TMEM loads below are .sync.aligned
                     if (!__all_sync(0xffffffffu, tc::mbar_wait(done0 + 8 * (ke % C::kR), (ke / C::kR) & 1u, abort_flag,
                                                                &g_f16_status, 30, true, a.wait_ns))) {
@@ -358,37 +360,50 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
                         break;
                     }
                     tc::tc_fence_after();
-                    // LB slots per TMEM round trip (registers allow two at 64 tokens)
+                    // the pair's two weight scales (blocks eb, eb + 1)
+                    const uint32_t word =
+                        *reinterpret_cast<const uint32_t*>(dwrow + (((eb >> 3) ^ dsw) << 4) + (eb & 7) * 2);
+                    // the products of block b with its TMEM values w (tokens 4*t4.. of this warp's slice)
+                    auto step = [&](int b, int t4, const uint32_t* w) {
+                        const float dw = half_bits_to_float((unsigned short)((b & 1) ? word >> 16 : word));
+                        const uint64_t dw2 = pack2(dw, dw);
+                        const ulonglong2 d4 = reinterpret_cast<const ulonglong2*>(da + b * NT + slice * TT)[t4];
+                        const uint64_t v0 = (uint64_t)w[0] | ((uint64_t)w[1] << 32);
+                        const uint64_t v1 = (uint64_t)w[2] | ((uint64_t)w[3] << 32);
+                        // fma(fp16(d_w) * d_a, float(isum), sum): the product rounded first
+                        acc[2 * t4] = tc::f2_fma(tc::f2_mul(dw2, d4.x), v0, acc[2 * t4]);
+                        acc[2 * t4 + 1] = tc::f2_fma(tc::f2_mul(dw2, d4.y), v1, acc[2 * t4 + 1]);
+                    };
+                    auto release = [&]() {  // the pair's last loads: the slots are free for the MMAs
+                        tc::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(tempty0 + 8 * pr);
+                    };
+                    if constexpr (LB == 2) {
+                        uint32_t v[2][TT];
 #pragma unroll
-                    for (int i0 = 0; i0 < 2; i0 += LB) {
-                        if (i0 >= nl) break;
-#pragma unroll
-                        for (int i = 0; i < LB; ++i)
-                            if (i0 + i < nl) tc::tmem_ld32(tl + (2 * pr + i0 + i) * NT, v[i]);
+                        for (int i = 0; i < 2; ++i)
+                            if (i < nl) tc::tmem_ld32(tl + (2 * pr + i) * NT, v[i]);
                         tc::tmem_wait_ld();
-                        if (i0 + LB >= nl) {  // the pair's last loads: the slots are free for the MMAs
-                            tc::tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) tc::mbar_arrive(tempty0 + 8 * pr);
-                        }
+                        release();
 #pragma unroll
-                        for (int i = 0; i < LB; ++i) {
-                            if (i0 + i < nl) {
-                                const int b = eb + i0 + i;
-                                const uint32_t word = dwp[b >> 1];
-                                const float dw = half_bits_to_float((unsigned short)((b & 1) ? word >> 16 : word));
-                                const uint64_t dw2 = pack2(dw, dw);
-                                const ulonglong2* d4p = reinterpret_cast<const ulonglong2*>(da + b * NT + slice * TT);
+                        for (int i = 0; i < 2; ++i)
+                            if (i < nl) {
 #pragma unroll
-                                for (int t4 = 0; t4 < TT / 4; ++t4) {
-                                    const ulonglong2 d4 = d4p[t4];
-                                    const uint64_t v0 = (uint64_t)v[i][4 * t4] | ((uint64_t)v[i][4 * t4 + 1] << 32);
-                                    const uint64_t v1 =
-                                        (uint64_t)v[i][4 * t4 + 2] | ((uint64_t)v[i][4 * t4 + 3] << 32);
-                                    // fma(fp16(d_w) * d_a, float(isum), sum): the product rounded first
-                                    acc[2 * t4] = tc::f2_fma(tc::f2_mul(dw2, d4.x), v0, acc[2 * t4]);
-                                    acc[2 * t4 + 1] = tc::f2_fma(tc::f2_mul(dw2, d4.y), v1, acc[2 * t4 + 1]);
-                                }
+                                for (int t4 = 0; t4 < TT / 4; ++t4) step(eb + i, t4, &v[i][4 * t4]);
+                            }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            if (i >= nl) break;
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                uint32_t v[TT / 2];
+                                tc::tmem_ld16(tl + (2 * pr + i) * NT + h * (TT / 2), v);
+                                tc::tmem_wait_ld();
+                                if (i == nl - 1 && h == 1) release();
+#pragma unroll
+                                for (int t4 = 0; t4 < TT / 8; ++t4) step(eb + i, h * (TT / 8) + t4, &v[4 * t4]);
                             }
                         }
                     }

@@ -523,7 +523,9 @@ cudaError_t gemm_q4_q8_f16(const mv_weight_s& w, const uint16_t* qh, const float
     // part among more tokens, narrow ones give narrow weights (o, down: 32
     // row tiles) enough tiles to fill the SMs.  (Checked at 512 tokens on the
     // four 7B shapes: 128-token tiles 213 / 81 / 344 / 205 us against 267 / 95 /
-    // 449 / 248 with 64 and 393 / 153 / 666 / 401 with 32.)
+    // 449 / 248 with 64 and 393 / 153 / 666 / 401 with 32; with the epilogue
+    // free of spills the 128-token tiles take 179 / 76 / 294 / 170 us, about
+    // 61 us per tile at K = 4096, so the model's choices for these shapes stand.)
     const uint64_t row_tiles = (w.rows + kM - 1) / kM, sms = (uint64_t)num_sms();
     int best = 128;
     double best_t = 1e30;
